@@ -1,0 +1,117 @@
+// common.cuh — device helpers shared by the ds_cuda kernels (sm_100a).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define DS_WARP 32
+#define DS_FULL 0xffffffffu
+
+namespace ds {
+
+// BF16 weights widen exactly to F32 by a 16-bit shift (the reference does
+// the same, ds_kernels_avx.c:49-51).
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Schraudolph fast exp exactly as the compiled reference evaluates it
+// (ds_kernels.h:296-302, product-add fused by gcc into one FMA): the FMA is
+// rounded to nearest, then truncated to uint32 and reinterpreted.
+__device__ __forceinline__ float fast_expf(float x) {
+    if (x < -88.0f) return 0.0f;
+    if (x > 88.0f) return 1e38f;
+    return __uint_as_float(__float2uint_rz(__fmaf_rn(12102203.0f, x, 1064866805.0f)));
+}
+
+// F32 -> BF16 -> F32 with the reference's round-half-up on the magnitude
+// (ds_kernels.c:2464-2492).
+__device__ __forceinline__ float bf16_roundtrip(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x8000u) & 0xffff0000u);
+}
+
+// SwiGLU of the reference's non-Apple build (ds_kernels.c:1770-1773).
+__device__ __forceinline__ float swiglu(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, fast_expf(-g))), u);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(DS_FULL, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(DS_FULL, v, o));
+    return v;
+}
+
+// 16-byte streaming load that bypasses L1 (weights are read once per step).
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint2 ldg_stream8(const void *p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                 : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+
+// Eight BF16 weights (one 16-byte chunk) times eight F32 activations.
+__device__ __forceinline__ float dot8_bf16(uint4 w, const float4 &xa, const float4 &xb, float acc) {
+    acc = __fmaf_rn(bf16_lo(w.x), xa.x, acc);
+    acc = __fmaf_rn(bf16_hi(w.x), xa.y, acc);
+    acc = __fmaf_rn(bf16_lo(w.y), xa.z, acc);
+    acc = __fmaf_rn(bf16_hi(w.y), xa.w, acc);
+    acc = __fmaf_rn(bf16_lo(w.z), xb.x, acc);
+    acc = __fmaf_rn(bf16_hi(w.z), xb.y, acc);
+    acc = __fmaf_rn(bf16_lo(w.w), xb.z, acc);
+    acc = __fmaf_rn(bf16_hi(w.w), xb.w, acc);
+    return acc;
+}
+
+// Unsigned byte b (0..255) of a word as an exact F32: 0x4B0000bb is
+// 2^23 + b, and subtracting 2^23 is exact. Two full-rate ops, no I2F.
+__device__ __forceinline__ float ubyte_f(uint32_t w, int b) {
+    uint32_t v = __byte_perm(w, 0x4B000000u, 0x7440 + b);  // bytes: [b,4,4,7]
+    return __fsub_rn(__uint_as_float(v), 8388608.0f);
+}
+
+// Programmatic dependent launch (PDL). wait: block until the predecessor
+// grid has completed and its memory is visible. launch_dependents: allow the
+// next grid in the stream to begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Bulk L2 prefetch of [p, p+bytes): p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
+// Prefetch an arbitrary byte range in chunks (addresses rounded to 16 B).
+__device__ __forceinline__ void prefetch_range(const void *p, size_t bytes) {
+    uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes + 15) & ~uintptr_t(15);
+    while (a < e) {
+        uintptr_t rem = e - a;
+        uint32_t n = rem < (uintptr_t(1) << 20) ? (uint32_t)rem : (1u << 20);
+        prefetch_l2(reinterpret_cast<const void *>(a), n);
+        a += n;
+    }
+}
+
+// Order-preserving map of an F32 to uint32 (larger float -> larger uint).
+__device__ __forceinline__ uint32_t f32_ordered(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float f32_from_ordered(uint32_t u) {
+    return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+// Argmax key: larger value wins; on equal values the LOWER index wins
+// (the reference's strict '>' scan, ds_kernels_avx.c:223-226).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+    return ((unsigned long long)f32_ordered(v) << 32) | (unsigned long long)(0xffffffffu - idx);
+}
+
+}  // namespace ds

@@ -1,0 +1,169 @@
+// kernels_moe.cuh — batch-1 decode kernels for the MoE layer and LM head.
+//
+// All of these are HBM-bound matvecs: one warp streams whole weight rows with
+// 16-byte non-allocating loads, keeps its slice of the activation vector in
+// registers, accumulates in F32 with FMA and reduces with shuffles. Weights
+// are BF16 widened exactly (u16 << 16) or per-row asymmetric INT8 dequantised
+// in registers, as in the reference CPU path.
+#pragma once
+#include "common.cuh"
+
+namespace ds {
+
+// One weight matrix: BF16 rows, or INT8 rows (stored q - 128) with per-row
+// F32 scale and offset (ds_quantize.h:30-37).
+struct WMat {
+    const void *w;
+    const float *scale;
+    const float *off;
+};
+
+// Arguments of the decode MoE chain for one token.
+//  explicit mode  (d_idx == nullptr): gu[k], dn[k], wt[k] name the top_k experts
+//  routed mode    (d_idx != nullptr): expert e = d_idx[k] is at
+//                 gu_base + e*gu_stride (elements; rows for scale/off: e*2*inter)
+struct MoeArgs {
+    int hidden, inter, sh_inter, top_k;
+    int int8, simulate, has_shared;
+    int out_mode;            // 0: out = moe; 1: out += moe; 2: out = resid + moe
+    WMat gu[8], dn[8];
+    float wt[8];
+    WMat gu_base, dn_base;
+    long long gu_stride, dn_stride;  // elements between experts
+    const int *d_idx;
+    const float *d_wt;
+    WMat sh_gu, sh_dn;
+    const float *x;          // [hidden]
+    float *h;                // scratch [top_k*inter + sh_inter]
+    float *out;              // [hidden]
+    const float *resid;      // [hidden] for out_mode 2
+};
+
+__device__ __forceinline__ WMat expert_mat(const MoeArgs &a, int k, bool gate_up) {
+    if (a.d_idx == nullptr) return gate_up ? a.gu[k] : a.dn[k];
+    int e = a.d_idx[k];
+    const WMat &b = gate_up ? a.gu_base : a.dn_base;
+    long long st = gate_up ? a.gu_stride : a.dn_stride;
+    long long rows = gate_up ? 2LL * a.inter : a.hidden;
+    WMat m;
+    m.w = a.int8 ? (const void *)((const int8_t *)b.w + st * e)
+                 : (const void *)((const uint16_t *)b.w + st * e);
+    m.scale = b.scale ? b.scale + rows * e : nullptr;
+    m.off = b.off ? b.off + rows * e : nullptr;
+    return m;
+}
+__device__ __forceinline__ float expert_wt(const MoeArgs &a, int k) {
+    return a.d_idx == nullptr ? a.wt[k] : a.d_wt[k];
+}
+
+// ---------------------------------------------------------------------------
+// Register-resident activation slices. Lane `l` owns chunks l, l+32, ... of
+// the input; a BF16 chunk is 8 columns (16 B), an INT8 chunk is 16 columns.
+// ---------------------------------------------------------------------------
+template <int CPL>
+struct XRegBF16 {
+    float4 v[CPL][2];
+    __device__ __forceinline__ void load(const float *x, int n, int lane) {
+        const int nch = n >> 3;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            int ch = lane + 32 * c;
+            if (ch < nch) {
+                v[c][0] = *reinterpret_cast<const float4 *>(x + 8 * ch);
+                v[c][1] = *reinterpret_cast<const float4 *>(x + 8 * ch + 4);
+            } else {
+                v[c][0] = make_float4(0.f, 0.f, 0.f, 0.f);
+                v[c][1] = v[c][0];
+            }
+        }
+    }
+};
+
+// Dot of one BF16 row (n columns) with the register slice; lane partial only.
+template <int CPL>
+__device__ __forceinline__ float row_dot_bf16(const uint16_t *row, int n, const XRegBF16<CPL> &x, int lane) {
+    const int nch = n >> 3;
+    uint4 w[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        int ch = lane + 32 * c;
+        w[c] = ch < nch ? ldg_stream(row + 8 * ch) : make_uint4(0, 0, 0, 0);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; c++) acc = dot8_bf16(w[c], x.v[c][0], x.v[c][1], acc);
+    return acc;
+}
+
+// Two rows at once (twice the bytes in flight per lane).
+template <int CPL>
+__device__ __forceinline__ void row_dot2_bf16(const uint16_t *r0, const uint16_t *r1, int n,
+                                              const XRegBF16<CPL> &x, int lane, float &s0, float &s1) {
+    const int nch = n >> 3;
+    uint4 w0[CPL], w1[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        int ch = lane + 32 * c;
+        bool ok = ch < nch;
+        w0[c] = ok ? ldg_stream(r0 + 8 * ch) : make_uint4(0, 0, 0, 0);
+        w1[c] = ok ? ldg_stream(r1 + 8 * ch) : make_uint4(0, 0, 0, 0);
+    }
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        a0 = dot8_bf16(w0[c], x.v[c][0], x.v[c][1], a0);
+        a1 = dot8_bf16(w1[c], x.v[c][0], x.v[c][1], a1);
+    }
+    s0 = a0;
+    s1 = a1;
+}
+
+template <int CPL>
+struct XRegI8 {
+    float4 v[CPL][4];
+    __device__ __forceinline__ void load(const float *x, int n, int lane) {
+        const int nch = n >> 4;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            int ch = lane + 32 * c;
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                v[c][q] = ch < nch ? *reinterpret_cast<const float4 *>(x + 16 * ch + 4 * q)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+};
+
+__device__ __forceinline__ float dot4_u8(uint32_t w, const float4 &x, float acc) {
+    // stored int8 q - 128 == unsigned byte (q + 128) ^ 0x80 ... the stored
+    // byte s = q_u - 128 (two's complement), so q_u = s ^ 0x80.
+    uint32_t u = w ^ 0x80808080u;
+    acc = __fmaf_rn(ubyte_f(u, 0), x.x, acc);
+    acc = __fmaf_rn(ubyte_f(u, 1), x.y, acc);
+    acc = __fmaf_rn(ubyte_f(u, 2), x.z, acc);
+    acc = __fmaf_rn(ubyte_f(u, 3), x.w, acc);
+    return acc;
+}
+
+// Lane partial of sum_c (q_c + 128) * x_c over one INT8 row.
+template <int CPL>
+__device__ __forceinline__ float row_dot_i8(const int8_t *row, int n, const XRegI8<CPL> &x, int lane) {
+    const int nch = n >> 4;
+    uint4 w[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        int ch = lane + 32 * c;
+        w[c] = ch < nch ? ldg_stream(row + 16 * ch) : make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        acc = dot4_u8(w[c].x, x.v[c][0], acc);
+        acc = dot4_u8(w[c].y, x.v[c][1], acc);
+        acc = dot4_u8(w[c].z, x.v[c][2], acc);
+        acc = dot4_u8(w[c].w, x.v[c][3], acc);
+    }
+    return acc;
+}
+
+}  // namespace ds

@@ -1,0 +1,193 @@
+/*
+ * ds_cuda.h — C ABI of the B200 (sm_100a) implementation of ds-ocr's
+ * MoE-decoder hot path. It fills the slot the reference's Metal offload
+ * (ds_metal.h) occupies and adds CUDA entry points with the signatures of
+ * the ds_kernels / ds_quantize functions the hot path calls.
+ *
+ * Conventions
+ *  - Plain C types only: pointers, sizes, ints. No CUDA or torch types.
+ *  - Every call returns an int status: >= 0 success (token ids are >= 0),
+ *    negative = error (DS_CUDA_E*). ds_cuda_last_error() describes the last
+ *    failure of a context. Nothing fails silently (unlike the reference's
+ *    void Metal calls, ds_metal.m:263,318,439).
+ *  - Host-pointer calls are synchronous, like the Metal ones
+ *    (waitUntilCompleted, ds_metal.m:425-427): inputs are copied to the
+ *    device, outputs copied back before return.
+ *  - Weights are copied to HBM once and looked up by HOST pointer, interior
+ *    pointers included (the Metal context wraps host buffers and translates
+ *    pointers into the expert block, ds_metal.m:56-86). A weight not
+ *    registered beforehand is registered on first use with the size the call
+ *    implies (the Metal get_wbuf wraps on demand the same way).
+ *  - "_dev" entry points take DEVICE pointers and a stream (cudaStream_t
+ *    passed as void*, NULL = the context's stream) and only enqueue work.
+ *  - One context per device; a context is not thread-safe (the Metal one
+ *    is not either: shared scratch per context).
+ *  - Shape limits: hidden dimensions a multiple of 16 and <= 2048, expert
+ *    intermediate a multiple of 16, top_k <= 6 with shared experts (<= 8
+ *    without), <= 256 routed experts. DS_CUDA_EINVAL otherwise.
+ *
+ * This library has no CPU fallback: without a usable CUDA device
+ * ds_cuda_init returns NULL and ds_cuda_is_available returns 0.
+ */
+#ifndef DS_CUDA_H
+#define DS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DS_CUDA_OK 0
+#define DS_CUDA_EINVAL (-1)     /* bad argument or unsupported shape */
+#define DS_CUDA_ENOTREG (-2)    /* pointer not inside a registered weight */
+#define DS_CUDA_ECUDA (-3)      /* CUDA runtime / launch error */
+#define DS_CUDA_ENOMEM (-4)     /* device allocation failed */
+#define DS_CUDA_ESTATE (-5)     /* call not valid in the current state */
+#define DS_CUDA_ENCCL (-6)      /* NCCL error */
+#define DS_CUDA_ETIMEOUT (-7)   /* a bounded device-side wait gave up */
+
+typedef struct ds_cuda_ctx ds_cuda_ctx_t;
+
+/* Same memory layout as the reference's ds_int4_block_t
+ * (ds_quantize.h:30-37): per-row asymmetric INT8, stored q - 128. */
+typedef struct {
+    int8_t *qweight; /* [out_dim, in_dim] row-major */
+    float *scale;    /* [out_dim] */
+    float *offset;   /* [out_dim] (row minimum) */
+    int out_dim;
+    int in_dim;
+    size_t bytes;
+} ds_cuda_int8_block_t;
+
+/* ---------------------------------------------------------------------
+ * Lifecycle — ds_metal_init / ds_metal_free / ds_metal_is_available
+ * (ds_metal.h:37-46).
+ * --------------------------------------------------------------------- */
+ds_cuda_ctx_t *ds_cuda_init(int device);
+void ds_cuda_free(ds_cuda_ctx_t *ctx);
+int ds_cuda_is_available(const ds_cuda_ctx_t *ctx);
+const char *ds_cuda_last_error(const ds_cuda_ctx_t *ctx);
+/* The context's CUDA stream (cudaStream_t) as an opaque pointer. */
+void *ds_cuda_stream(ds_cuda_ctx_t *ctx);
+int ds_cuda_synchronize(ds_cuda_ctx_t *ctx);
+
+/* Numerics switches of the reference:
+ *  simulate_bf16 — ds_bf16_simulate_python (ds_ocr.c:27, main.c:106): BF16
+ *                  round-trip of expert intermediates (ds_kernels.c:333-356).
+ *  renorm_topk   — divide the top-k router weights by their sum. The
+ *                  reference code does NOT (ds_moe_decoder.c:157-183); default 0. */
+int ds_cuda_set_numerics(ds_cuda_ctx_t *ctx, int simulate_bf16, int renorm_topk);
+
+/* ---------------------------------------------------------------------
+ * Weight registration — ds_metal_register_bf16 / _f32 /
+ * _register_expert_block (ds_metal.h:52-66). The host range is copied to
+ * HBM once; later calls passing any pointer inside it use the device copy.
+ * --------------------------------------------------------------------- */
+int ds_cuda_register_bf16(ds_cuda_ctx_t *ctx, const uint16_t *data, size_t n);
+int ds_cuda_register_f32(ds_cuda_ctx_t *ctx, const float *data, size_t n);
+int ds_cuda_register_expert_block(ds_cuda_ctx_t *ctx, const void *block_ptr, size_t block_bytes);
+/* Registers the three arrays of an INT8 block (the --int4 path,
+ * ds_quantize.h:30-37; quantised by ds_int4_quantize_bf16 on the host). */
+int ds_cuda_register_int8_block(ds_cuda_ctx_t *ctx, const ds_cuda_int8_block_t *block);
+/* Device address of a registered host pointer (NULL if unregistered). */
+const void *ds_cuda_device_ptr(ds_cuda_ctx_t *ctx, const void *host_ptr);
+/* Bytes of HBM held by registered weights. */
+size_t ds_cuda_registered_bytes(const ds_cuda_ctx_t *ctx);
+
+/* ---------------------------------------------------------------------
+ * Decode MoE — ds_metal_moe_experts / ds_metal_shared_experts
+ * (ds_metal.h:96-128). moe_experts WRITES output = sum_k w_k expert_k(x);
+ * shared_experts ADDS its result into output.
+ * --------------------------------------------------------------------- */
+int ds_cuda_moe_experts(ds_cuda_ctx_t *ctx, const float *x, const uint16_t **gate_up_ptrs,
+                        const uint16_t **down_ptrs, const float *top_weights, int top_k,
+                        int hidden, int inter, float *output);
+int ds_cuda_shared_experts(ds_cuda_ctx_t *ctx, const float *x, const uint16_t *gate_up_bf16,
+                           const uint16_t *down_bf16, int hidden, int shared_inter, float *output);
+
+/* ds_expert_forward_fused (ds_kernels.h:209-214) and
+ * ds_expert_forward_fused_int4 (ds_quantize.h:69-75) without the caller
+ * scratch buffers (scratch lives in the context). */
+int ds_cuda_expert_forward_fused(ds_cuda_ctx_t *ctx, float *out, const float *x,
+                                 const uint16_t *gate_up_fused_bf16, const uint16_t *down_bf16,
+                                 int hidden, int intermediate);
+int ds_cuda_expert_forward_fused_int4(ds_cuda_ctx_t *ctx, float *out, const float *x,
+                                      const ds_cuda_int8_block_t *gate_up_int4,
+                                      const ds_cuda_int8_block_t *down_int4, int hidden,
+                                      int intermediate);
+
+/* Whole moe_forward (ds_moe_decoder.c:131-333) for one token: router
+ * matvec, softmax + top-k, routed experts, combine, shared experts.
+ *   router_bf16   [n_experts x hidden]
+ *   expert_block  [n_experts x (2*inter x hidden)] then shared [(2*shared_inter) x hidden]
+ *                 (the contiguous block of ds_ocr.c:696-768)
+ *   down_bf16     [n_experts x (hidden x inter)] contiguous
+ *   shared_down   [hidden x shared_inter]
+ * top_idx / top_w (optional, may be NULL) receive the routing decision. */
+int ds_cuda_moe_layer(ds_cuda_ctx_t *ctx, const float *x, float *out, const uint16_t *router_bf16,
+                      const uint16_t *expert_block, const uint16_t *down_bf16,
+                      const uint16_t *shared_down_bf16, int hidden, int inter, int shared_inter,
+                      int n_experts, int top_k, int *top_idx, float *top_w);
+/* Same with INT8 experts: per-expert blocks laid out contiguously
+ * (gu: [E][2I x H] q, [E][2I] scale/offset; dn: [E][H x I], [E][H]). */
+int ds_cuda_moe_layer_int8(ds_cuda_ctx_t *ctx, const float *x, float *out, const uint16_t *router_bf16,
+                           const int8_t *gu_q, const float *gu_scale, const float *gu_off,
+                           const int8_t *dn_q, const float *dn_scale, const float *dn_off,
+                           const int8_t *sgu_q, const float *sgu_scale, const float *sgu_off,
+                           const int8_t *sdn_q, const float *sdn_scale, const float *sdn_off,
+                           int hidden, int inter, int shared_inter, int n_experts, int top_k,
+                           int *top_idx, float *top_w);
+
+/* ---------------------------------------------------------------------
+ * LM head — ds_metal_lm_head_argmax (ds_metal.h:146-150) and
+ * ds_argmax_matvec_bf16 (ds_kernels.h:239-240). Returns the token id
+ * (lowest id wins ties) or a negative error. *logit (optional) receives its
+ * logit.
+ * --------------------------------------------------------------------- */
+int ds_cuda_lm_head_argmax(ds_cuda_ctx_t *ctx, const float *x, const uint16_t *W_bf16, int hidden,
+                           int vocab);
+int ds_cuda_argmax_matvec_bf16(ds_cuda_ctx_t *ctx, const float *x, const uint16_t *W_bf16, int in_dim,
+                               int out_dim, float *logit);
+/* B independent inputs x[B x in_dim] (the reference loops; here one pass). */
+int ds_cuda_argmax_matvec_bf16_batch(ds_cuda_ctx_t *ctx, const float *x, const uint16_t *W_bf16,
+                                     int in_dim, int out_dim, int batch, int *tokens, float *logits);
+
+/* ds_metal_matvec_bf16 (ds_metal.h:168-174): y = W x (+ bias). */
+int ds_cuda_matvec_bf16(ds_cuda_ctx_t *ctx, float *y, const float *x, const uint16_t *W_bf16,
+                        const float *bias, int in_dim, int out_dim);
+
+/* ---------------------------------------------------------------------
+ * INT8 quantisation on the device, bit-identical to ds_int4_quantize_bf16
+ * (ds_quantize.c:49-81). W is host BF16 [out_dim x in_dim]; q/scale/offset
+ * receive the host result.
+ * --------------------------------------------------------------------- */
+int ds_cuda_int8_quantize_bf16(ds_cuda_ctx_t *ctx, const uint16_t *W_bf16, int out_dim, int in_dim,
+                               int8_t *qweight, float *scale, float *offset);
+
+/* ---------------------------------------------------------------------
+ * Device-pointer entry points (enqueue only).
+ * --------------------------------------------------------------------- */
+int ds_cuda_argmax_matvec_bf16_dev(ds_cuda_ctx_t *ctx, const float *d_x, const uint16_t *d_W,
+                                   int in_dim, int out_dim, int *d_token, float *d_logit, void *stream);
+int ds_cuda_moe_layer_dev(ds_cuda_ctx_t *ctx, const float *d_x, float *d_out,
+                          const uint16_t *d_router, const uint16_t *d_expert_block,
+                          const uint16_t *d_down, const uint16_t *d_shared_down, int hidden, int inter,
+                          int shared_inter, int n_experts, int top_k, int *d_top_idx, float *d_top_w,
+                          void *stream);
+
+/* ---------------------------------------------------------------------
+ * Host-side synthetic data (seeded, counter-based: value i of a stream
+ * depends only on (seed, i)); used to build the benchmark workloads.
+ * normal_bf16: RNE-rounded N(mean, std); normal_f32: F32 N(mean, std);
+ * normal_f32_bf16exact: F32 values that are exactly BF16-representable.
+ * --------------------------------------------------------------------- */
+void ds_synth_normal_bf16(uint16_t *out, size_t n, uint64_t seed, float mean, float stddev);
+void ds_synth_normal_f32(float *out, size_t n, uint64_t seed, float mean, float stddev);
+void ds_synth_normal_f32_bf16exact(float *out, size_t n, uint64_t seed, float mean, float stddev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DS_CUDA_H */

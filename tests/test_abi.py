@@ -1,0 +1,48 @@
+"""The C-ABI library loads and exports every symbol include/ds_cuda.h
+declares; host-side logic that needs no GPU."""
+import ctypes
+
+import numpy as np
+
+from conftest import HAS_GPU
+from ds_ocr_b200 import _lib, synth
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _lib.declared_symbols()
+    assert len(declared) >= 25
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+    # and the Python binding covers exactly the declared set
+    assert sorted(_lib.SIGNATURES) == declared
+
+
+def test_init_without_gpu_returns_null():
+    lib = _lib.load()
+    if HAS_GPU:
+        return
+    assert not lib.ds_cuda_init(0)
+    assert lib.ds_cuda_is_available(None) == 0
+    assert b"no context" in lib.ds_cuda_last_error(None)
+
+
+def test_invalid_context_calls_fail_loudly():
+    lib = _lib.load()
+    x = np.zeros(1280, np.float32)
+    assert lib.ds_cuda_lm_head_argmax(None, x.ctypes.data, x.ctypes.data, 1280, 10) < 0
+    assert lib.ds_cuda_moe_experts(None, None, None, None, None, 0, 1280, 896, None) < 0
+    assert lib.ds_cuda_set_numerics(None, 0, 0) < 0
+
+
+def test_synth_is_counter_based():
+    a = synth.normal_bf16(100000, 42)
+    b = synth.normal_bf16(100000, 42)
+    c = np.empty(100000, np.uint16)
+    synth.fill_bf16(c[:50000], 42)
+    assert np.array_equal(a, b) and np.array_equal(a[:50000], c[:50000])
+    f = synth.bf16_to_f32(synth.normal_bf16(1 << 20, 7))
+    assert abs(f.mean()) < 1e-4 and abs(f.std() - 0.02) < 2e-4
+    e = np.empty(1000, np.float32)
+    synth.fill_f32_bf16exact(e, 3)
+    assert np.all((e.view(np.uint32) & 0xFFFF) == 0)

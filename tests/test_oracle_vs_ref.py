@@ -1,0 +1,139 @@
+"""Pins the CPU oracle (oracle/ds_oracle.c) to the reference itself, compiled
+unmodified from its own sources into oracle/_ref/libdsref.so."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import rel_l2
+from ds_ocr_b200 import synth
+
+pytestmark = pytest.mark.ref
+
+
+def test_fast_expf_bit_exact(orc):
+    r = O.ref()
+    xs = np.concatenate([np.linspace(-100, 100, 20001, dtype=np.float32),
+                         synth.normal_f32(20000, 1, std=8.0)])
+    a = np.array([orc.orc_fast_expf(float(x)) for x in xs], np.float32)
+    b = np.array([r.ref_fast_expf(float(x)) for x in xs], np.float32)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_matvec_and_argmax(orc):
+    r = O.ref()
+    r.ref_set_threads(4)
+    W = synth.normal_bf16((3001, 1280), 5)
+    for s in range(4):
+        x = synth.normal_f32(1280, 100 + s)
+        y1 = np.empty(3001, np.float32)
+        y2 = np.empty(3001, np.float32)
+        orc.orc_matvec_bf16(y1.ctypes.data, x.ctypes.data, W.ctypes.data, 1280, 3001)
+        r.ref_matvec(y2.ctypes.data, x.ctypes.data, W.ctypes.data, 1280, 3001)
+        assert rel_l2(y1, y2) < 1e-6
+        v1 = np.empty(1, np.float32)
+        v2 = np.empty(1, np.float32)
+        t1 = orc.orc_argmax_bf16(x.ctypes.data, W.ctypes.data, 1280, 3001, v1.ctypes.data)
+        t2 = r.ref_argmax(x.ctypes.data, W.ctypes.data, 1280, 3001, v2.ctypes.data)
+        top2 = np.sort(y2)[-2:]
+        if top2[1] - top2[0] > 1e-4:
+            assert t1 == t2
+
+
+def test_argmax_ties_lowest_index(orc):
+    r = O.ref()
+    W = synth.normal_bf16((64, 128), 9)
+    W[40] = W[7]
+    W[63] = W[7]
+    x = synth.bf16_to_f32(W[7]).copy()  # row 7 (and its copies) maximise x.W
+    assert r.ref_argmax(x.ctypes.data, W.ctypes.data, 128, 64, None) == 7
+    assert orc.orc_argmax_bf16(x.ctypes.data, W.ctypes.data, 128, 64, None) == 7
+
+
+def test_int8_quantize_bit_exact(orc):
+    r = O.ref()
+    for shape, seed in (((1792, 1280), 3), ((1280, 896), 4), ((17, 48), 5)):
+        W = synth.normal_bf16(shape, seed)
+        qa, sa, oa = np.empty(W.size, np.int8), np.empty(shape[0], np.float32), np.empty(shape[0], np.float32)
+        qb, sb, ob = np.empty_like(qa), np.empty_like(sa), np.empty_like(oa)
+        orc.orc_int8_quantize(W.ctypes.data, shape[0], shape[1], qa.ctypes.data, sa.ctypes.data, oa.ctypes.data)
+        r.ref_quantize(W.ctypes.data, shape[0], shape[1], qb.ctypes.data, sb.ctypes.data, ob.ctypes.data)
+        assert np.array_equal(qa, qb) and np.array_equal(sa, sb) and np.array_equal(oa, ob)
+    # constant row: scale clamps to 1e-10
+    W = np.full((2, 32), 0x3f80, np.uint16)
+    orc.orc_int8_quantize(W.ctypes.data, 2, 32, qa.ctypes.data, sa.ctypes.data, oa.ctypes.data)
+    r.ref_quantize(W.ctypes.data, 2, 32, qb.ctypes.data, sb.ctypes.data, ob.ctypes.data)
+    assert np.array_equal(qa[:64], qb[:64]) and sa[0] == sb[0] == np.float32(1e-10)
+
+
+def test_int8_matvec_bit_exact(orc):
+    r = O.ref()
+    r.ref_set_threads(1)
+    W = synth.normal_bf16((300, 1280), 8)
+    q, s, o = np.empty(W.size, np.int8), np.empty(300, np.float32), np.empty(300, np.float32)
+    r.ref_quantize(W.ctypes.data, 300, 1280, q.ctypes.data, s.ctypes.data, o.ctypes.data)
+    x = synth.normal_f32(1280, 12)
+    y1, y2 = np.empty(300, np.float32), np.empty(300, np.float32)
+    orc.orc_int8_matvec(y1.ctypes.data, x.ctypes.data, q.ctypes.data, s.ctypes.data, o.ctypes.data, 300, 1280)
+    r.ref_int8_matvec(y2.ctypes.data, x.ctypes.data, q.ctypes.data, s.ctypes.data, o.ctypes.data, 300, 1280)
+    assert rel_l2(y1, y2) < 1e-6
+
+
+@pytest.fixture(scope="module")
+def small_model():
+    return synth.Model(n_layers=2, vocab=4096)
+
+
+@pytest.mark.parametrize("simulate", [0, 1])
+def test_moe_forward(small_model, simulate):
+    r = O.ref()
+    r.ref_set_simulate(simulate)
+    try:
+        R = O.RefDecoder(small_model, kv_max=64, threads=4)
+        D = O.OracleDecoder(small_model, kv_max=64, simulate=simulate)
+        for s in range(6):
+            x = synth.normal_f32(1280, 50 + s)
+            ro = R.moe_forward(1, x)
+            oo, idx, w = D.moe_forward(1, x)
+            # with BF16 truncation a ~1e-7 difference can flip one rounding
+            # (2^-8 relative on that element): the north-star 1e-3 bar applies
+            assert rel_l2(oo, ro) < (1e-5 if simulate == 0 else 1e-3)
+    finally:
+        r.ref_set_simulate(0)
+
+
+def test_decoder_steps(small_model):
+    R = O.RefDecoder(small_model, kv_max=128, threads=4)
+    D = O.OracleDecoder(small_model, kv_max=128)
+    ks, vs = synth.kv_prefix(small_model.d, 50)
+    R.load_kv(ks, vs)
+    D.load_kv(ks, vs)
+    e = small_model.embed(11)
+    for _ in range(4):
+        rt, rx, rl = R.step(e)
+        ot, ox, ol = D.step(e)
+        assert rt == ot
+        assert rel_l2(ox, rx) < 1e-4
+        e = small_model.embed(rt)
+
+
+def test_int8_moe_and_prefill(small_model):
+    R = O.RefDecoder(small_model, kv_max=64, threads=4)
+    D = O.OracleDecoder(small_model, kv_max=64)
+    x = synth.normal_f32(1280, 77)
+    bf = R.moe_forward(1, x)
+    R.quantize()
+    ro = R.moe_forward(1, x)
+    oo, _, _ = D.moe_forward(1, x, use_int8=True)
+    assert rel_l2(oo, ro) < 1e-5
+    assert rel_l2(ro, bf) < 0.05  # INT8 vs BF16 (reference's own quantisation error)
+    small_model.layers[1].moe.int8 = None
+    xp = synth.normal_f32((48, 1280), 78)
+    lg = synth.normal_f32((48, 64), 79)
+    for logits in (lg, None):
+        xr, xo = xp.copy(), xp.copy()
+        i1, w1 = R.prefill_moe(1, xr, logits)
+        i2, w2 = D.prefill_moe(1, xo, logits)
+        assert np.array_equal(i1, i2)
+        assert rel_l2(xo - xp, xr - xp) < 1e-5

@@ -268,51 +268,204 @@ def ref_moe_time(wl, threads, budget_s):
     return n / t_total, n
 
 
+# ---------------------------------------------------------------------------
+# Decode (config 3), the headline workload
+# ---------------------------------------------------------------------------
+DEC_WEIGHT_BYTES = 1148318720        # per token: attention + dense L0 + 11 MoE + LM head + norms
+KV_BYTES_PER_KEY = 61440             # 12 layers x (K + V) x 1280 x BF16
+PREFIX = 662
+
+
+def decode_bytes(first_pos, n_steps):
+    keys = sum(first_pos + s + 1 for s in range(n_steps))
+    return DEC_WEIGHT_BYTES * n_steps + KV_BYTES_PER_KEY * keys
+
+
+def decode_config(kv_max):
+    return {"workload": "config3_decode_b1", "model": "DeepSeek3B-MoE decoder (12 layers, random init)",
+            "global_batch": 1, "streams_per_gpu": 1, "kv_prefix": PREFIX, "kv_max": kv_max,
+            "hidden": 1280, "experts": 64, "top_k": 6, "vocab": 129280,
+            "l2": "each step streams 1.2 GB of weights (> 126 MB L2)"}
+
+
+def build_decode_model():
+    from ds_ocr_b200 import synth
+    model = synth.Model()
+    ks, vs = synth.kv_prefix(model.d, PREFIX)
+    return model, ks, vs
+
+
+def run_ours_decode(args, rank, world, pg, model, ks, vs):
+    import torch
+    from ds_ocr_b200 import cuda
+    from ds_ocr_b200.decoder import Decoder
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = cuda.Context(local if world > 1 else 0)
+    kv_max = 1024
+    dec = Decoder(model, ctx, kv_max=kv_max)
+    dec.load_kv(ks, vs)
+    st = torch.cuda.ExternalStream(ctx.stream)
+    e0 = model.embed(1)
+    # warm-up (graph capture happens here), then reset to the prefix
+    dec.generate(args.warmup, first_embed=e0)
+    dec.set_len(PREFIX)
+    dec.forward(e0)
+    first = PREFIX + 1
+    ctx.synchronize()
+    barrier(pg)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(st)
+        dec.generate_dev(args.steps)
+        ev1.record(st)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, pg)
+    value = world * args.steps / (ms_max / 1e3)
+    step_bytes = decode_bytes(first, args.steps)
+    launches = dec.launches_per_step
+
+    # e2e: the public host-pointer API, one call per token: H2D of the
+    # token's embedding, D2H of the token (+ its logit), host picks the next
+    # embedding (the reference's decode loop, ds_ocr.c:2157-2282)
+    n_e2e = args.steps
+    dec.set_len(PREFIX)
+    e = e0
+    ctx.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    for _ in range(n_e2e):
+        tok = dec.forward(e)
+        e = model.embed(tok)
+    t1.record(st)
+    t1.synchronize()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1), pg)
+    e2e = world * n_e2e / (e2e_ms / 1e3)
+
+    # dominant-kernel roofline: the LM-head argmax kernel of the graph,
+    # launched alone on the same stream (same kernel, same grid)
+    lib = ctx.lib
+    d_lm = ctx.device_ptr(model.lm_head)
+    X = torch.randn(64, 1280, device="cuda")
+    tok_t = torch.zeros(64, dtype=torch.int32, device="cuda")
+    val_t = torch.zeros(64, device="cuda")
+    torch.cuda.synchronize()
+    for i in range(5):
+        lib.ds_cuda_argmax_matvec_bf16_dev(ctx.h, X[i].data_ptr(), d_lm, 1280, 129280, tok_t[i].data_ptr(),
+                                           val_t[i].data_ptr(), None)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nk = 50
+    k0.record(st)
+    for i in range(nk):
+        lib.ds_cuda_argmax_matvec_bf16_dev(ctx.h, X[i % 64].data_ptr(), d_lm, 1280, 129280,
+                                           tok_t[i % 64].data_ptr(), val_t[i % 64].data_ptr(), None)
+    k1.record(st)
+    k1.synchronize()
+    lm_us = k0.elapsed_time(k1) / nk * 1e3
+    pk = peaks()
+    lm_ach = LM_BYTES / (lm_us * 1e-6) / 1e9
+    step_ach = step_bytes / (ms_max / 1e3) / 1e9
+    res = {
+        "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
+        "metric": "decode tokens/s (greedy, batch 1 per GPU, 12-layer DeepSeek3B-MoE, 662-token KV prefix)",
+        "unit": "tokens/s", "dtype": "bf16 weights + bf16 KV, f32 math",
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 1280 * 4, "d2h_bytes_per_step": 8},
+        "gpu_launches": launches * args.steps, "config": decode_config(kv_max),
+        "roofline": {"bound": "hbm", "achieved": lm_ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": lm_ach / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "argmax_bf16_kernel (LM head 129280x1280, 330,956,800 B/launch)",
+                     "kernel_us": lm_us, "peak_source": pk["source"]},
+        "step_roofline": {"bound": "hbm", "achieved": step_ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                          "frac": step_ach / pk["hbm_gbs"], "frac_of_8tbs": step_ach / 8000.0,
+                          "bytes_per_token": step_bytes / args.steps},
+    }
+    dec.close()
+    ctx.close()
+    return res
+
+
+def ref_decode_time(model, ks, vs, threads, budget_s, max_steps):
+    """The reference's own ds_decoder_forward (compiled unmodified) on the
+    same weights and KV prefix, `threads` host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    R = O.RefDecoder(model, kv_max=1024, threads=threads)
+    R.load_kv(ks, vs)
+    e = model.embed(1)
+    tok, _, _ = R.step(e)           # warm (page-in, thread pool)
+    e = model.embed(tok)
+    n, t_total = 0, 0.0
+    while t_total < budget_s and n < max_steps:
+        t = time.perf_counter()
+        tok, _, _ = R.step(e)
+        t_total += time.perf_counter() - t
+        e = model.embed(tok)
+        n += 1
+    R.close()
+    return n / t_total, n
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=224)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="moe_layer", choices=["moe_layer"])
-    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of reference CPU work to time")
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer"])
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local, pg = dist_setup(args.gpus)
+    T = cpu_threads()
+    common = {"higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+              "data": "synthetic (seeded random-init weights of the DeepSeek3B-MoE shapes; BF16 N(0,1) KV prefix)"}
 
     if args.impl == "reference":
         if rank != 0:
             return
-        wl = MoeLayerWorkload()
-        T = cpu_threads()
-        v, n = ref_moe_time(wl, T, max(args.cpu_budget, 1.0))
-        line = {"impl": "reference", "metric": wl.metric, "value": v, "unit": wl.unit, "n_gpus": 0,
-                "steps": n, "warmup": 1, "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "bf16 weights, f32 math", "data": "synthetic",
-                "config": wl.config(),
-                "cpu_baseline": {"value": v, "unit": wl.unit, "cores": T, "kind": "reference",
-                                 "sample": f"{n} single-token moe_forward calls over 11 layers"},
-                "e2e": {"value": v, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if args.workload == "decode":
+            model, ks, vs = build_decode_model()
+            v, n = ref_decode_time(model, ks, vs, T, max(args.cpu_budget, 1.0), max_steps=args.steps)
+            metric = "decode tokens/s (greedy, batch 1 per GPU, 12-layer DeepSeek3B-MoE, 662-token KV prefix)"
+            cfg, sample = decode_config(1024), f"{n} greedy ds_decoder_forward steps from position 663"
+        else:
+            wl = MoeLayerWorkload()
+            v, n = ref_moe_time(wl, T, max(args.cpu_budget, 1.0))
+            metric, cfg, sample = wl.metric, wl.config(), f"{n} single-token moe_forward calls over 11 layers"
+        line = {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": 0, "steps": n,
+                "warmup": 1, "ms_per_step": 1e3 / v, "dtype": "bf16 weights, f32 math", "config": cfg,
+                "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": T, "kind": "reference", "sample": sample},
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        line.update(common)
         print(json.dumps(line))
         return
 
-    res = run_ours_moe(args, rank, world, pg)
+    if args.workload == "decode":
+        model, ks, vs = build_decode_model()
+        res = run_ours_decode(args, rank, world, pg, model, ks, vs)
+    else:
+        res = run_ours_moe(args, rank, world, pg)
     if rank != 0:
         return
     line = {"metric": res["metric"], "value": res["value"], "unit": res["unit"], "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": res["dtype"],
-            "data": "synthetic (seeded random-init weights of the DeepSeek3B-MoE shapes)",
-            "config": res["config"], "e2e": res["e2e"], "roofline": res["roofline"],
-            "clocks": res["clocks"], "gpu_launches": res["gpu_launches"]}
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "dtype": res["dtype"],
+            "config": res["config"], "e2e": res["e2e"], "roofline": res["roofline"], "clocks": res["clocks"],
+            "gpu_launches": res["gpu_launches"]}
+    if "step_roofline" in res:
+        line["step_roofline"] = res["step_roofline"]
+    line.update(common)
     if not args.no_cpu_baseline:
         try:
-            wl = MoeLayerWorkload()
-            T = cpu_threads()
-            v, n = ref_moe_time(wl, T, args.cpu_budget)
+            if args.workload == "decode":
+                v, n = ref_decode_time(model, ks, vs, T, args.cpu_budget, max_steps=64)
+                sample = f"{n} greedy ds_decoder_forward steps from position 663"
+            else:
+                wl = MoeLayerWorkload()
+                v, n = ref_moe_time(wl, T, args.cpu_budget)
+                sample = f"{n} single-token moe_forward calls over 11 layers"
             line["cpu_baseline"] = {"value": v, "unit": res["unit"], "cores": T, "kind": "reference",
-                                    "sample": f"{n} single-token moe_forward calls over 11 layers"}
+                                    "sample": sample}
         except Exception as e:  # reported, never silently substituted
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     print(json.dumps(line))

@@ -26,6 +26,7 @@ SIGNATURES = {
     "ds_cuda_register_f32": (c_int, [P, P, c_size_t]),
     "ds_cuda_register_expert_block": (c_int, [P, P, c_size_t]),
     "ds_cuda_register_int8_block": (c_int, [P, P]),
+    "ds_cuda_unregister": (c_int, [P, P]),
     "ds_cuda_device_ptr": (c_void_p, [P, P]),
     "ds_cuda_registered_bytes": (c_size_t, [P]),
     "ds_cuda_moe_experts": (c_int, [P, P, P, P, P, c_int, c_int, c_int, P]),
@@ -41,6 +42,15 @@ SIGNATURES = {
     "ds_cuda_int8_quantize_bf16": (c_int, [P, P, c_int, c_int, P, P, P]),
     "ds_cuda_argmax_matvec_bf16_dev": (c_int, [P, P, P, c_int, c_int, P, P, P]),
     "ds_cuda_moe_layer_dev": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P]),
+    "ds_cuda_decoder_create": (c_int, [P, P, P, P, P]),
+    "ds_cuda_decoder_destroy": (c_int, [P, c_int]),
+    "ds_cuda_decoder_load_kv": (c_int, [P, c_int, c_int, c_int, c_int, P, P]),
+    "ds_cuda_decoder_set_len": (c_int, [P, c_int, c_int]),
+    "ds_cuda_decoder_get_len": (c_int, [P, c_int]),
+    "ds_cuda_decoder_forward": (c_int, [P, c_int, P, P, P]),
+    "ds_cuda_decoder_generate": (c_int, [P, c_int, P, c_int, P]),
+    "ds_cuda_decoder_generate_dev": (c_int, [P, c_int, c_int, P]),
+    "ds_cuda_decoder_launches_per_step": (c_int, [P, c_int]),
     "ds_synth_normal_bf16": (None, [P, c_size_t, c_uint64, c_float, c_float]),
     "ds_synth_normal_f32": (None, [P, c_size_t, c_uint64, c_float, c_float]),
     "ds_synth_normal_f32_bf16exact": (None, [P, c_size_t, c_uint64, c_float, c_float]),

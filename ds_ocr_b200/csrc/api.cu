@@ -222,6 +222,18 @@ extern "C" int ds_cuda_register_int8_block(ds_cuda_ctx_t *c, const ds_cuda_int8_
     CK(ctx_register(c, b->scale, (size_t)b->out_dim * sizeof(float)));
     return ctx_register(c, b->offset, (size_t)b->out_dim * sizeof(float));
 }
+extern "C" int ds_cuda_unregister(ds_cuda_ctx_t *c, const void *p) {
+    if (!c || !p) return DS_CUDA_EINVAL;
+    auto it = c->regs.find(reinterpret_cast<uintptr_t>(p));
+    if (it == c->regs.end()) return ctx_fail(c, DS_CUDA_ENOTREG, "unregister: %p is not a registration base", p);
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    cudaFree(it->second.dev);
+    c->reg_bytes -= it->second.bytes;
+    c->regs.erase(it);
+    return DS_CUDA_OK;
+}
+
 extern "C" const void *ds_cuda_device_ptr(ds_cuda_ctx_t *c, const void *p) {
     return c ? ctx_lookup(c, p, 1, false) : nullptr;
 }

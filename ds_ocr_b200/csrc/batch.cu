@@ -14,4 +14,3 @@ int batch_argmax_enqueue(ds_cuda_ctx *c, const float *d_x, const uint16_t *d_W, 
     return DS_CUDA_OK;
 }
 
-void ctx_release_models(ds_cuda_ctx *c) { (void)c; }

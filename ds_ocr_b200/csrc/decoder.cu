@@ -1,0 +1,507 @@
+// decoder.cu — batch-1 greedy decode of the DeepSeek3B-MoE decoder on one
+// GPU: weights and KV cache resident in HBM, one decode step = one CUDA graph
+// of kernels chained with programmatic dependent launch (each kernel's
+// prologue overlaps its predecessor's tail), replayed once per token.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "ctx.h"
+#include "kernels_decode.cuh"
+
+using namespace ds;
+
+struct DecLayer {
+    const uint16_t *wq, *wk, *wv, *wo;
+    const float *in_norm, *post_norm;
+    bool dense;
+    const uint16_t *dgate, *dup, *ddown;
+    const uint16_t *router, *block, *down, *sdown;
+    WMat gu, dn, sgu, sdn;  // INT8
+};
+
+struct DecoderModel {
+    ds_cuda_decoder_config_t cfg;
+    std::vector<DecLayer> layers;
+    const float *final_norm = nullptr;
+    const uint16_t *lm_head = nullptr;
+    // device state
+    float *xa = nullptr, *xb = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *xfinal = nullptr;
+    float *scores = nullptr, *wt = nullptr, *val = nullptr;
+    int *idx = nullptr, *pos = nullptr, *tok = nullptr, *tok_log = nullptr;
+    unsigned *tickets = nullptr;
+    unsigned long long *slot = nullptr;
+    uint16_t *kv = nullptr;  // 4 planes: k_hi, k_lo, v_hi, v_lo, each [L][heads][kv_max][hd]
+    float *cos_t = nullptr, *sin_t = nullptr;
+    std::vector<int> lo_start;  // per layer: rows below are exact BF16
+    int host_len = 0;
+    cudaGraphExec_t graph = nullptr, graph_final = nullptr;
+    bool pdl = true;
+    int launches = 0;
+    std::vector<void *> allocs;
+
+    size_t plane_elems() const {
+        return (size_t)cfg.n_layers * cfg.n_heads * cfg.kv_max * cfg.head_dim;
+    }
+    uint16_t *plane(int p, int l) const {
+        return kv + p * plane_elems() + (size_t)l * cfg.n_heads * cfg.kv_max * cfg.head_dim;
+    }
+};
+
+static void drop_graphs(DecoderModel *m) {
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->graph_final) cudaGraphExecDestroy(m->graph_final);
+    m->graph = m->graph_final = nullptr;
+}
+
+static void free_model(DecoderModel *m) {
+    drop_graphs(m);
+    for (void *p : m->allocs) cudaFree(p);
+    delete m;
+}
+
+void ctx_release_models(ds_cuda_ctx *c) {
+    for (auto &kv : c->models) free_model(kv.second);
+    c->models.clear();
+}
+
+static DecoderModel *get_model(ds_cuda_ctx *c, int id) {
+    auto it = c->models.find(id);
+    return it == c->models.end() ? nullptr : it->second;
+}
+
+template <typename T>
+static int dalloc(ds_cuda_ctx *c, DecoderModel *m, T **p, size_t elems) {
+    void *d = nullptr;
+    if (cudaMalloc(&d, elems * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return ctx_fail(c, DS_CUDA_ENOMEM, "decoder: cudaMalloc(%zu) failed", elems * sizeof(T));
+    }
+    cudaMemset(d, 0, elems * sizeof(T));
+    m->allocs.push_back(d);
+    *p = (T *)d;
+    return DS_CUDA_OK;
+}
+
+#define CK(expr)                 \
+    do {                         \
+        int _rc = (expr);        \
+        if (_rc < 0) return _rc; \
+    } while (0)
+#define CKL(expr, what)                                             \
+    do {                                                            \
+        cudaError_t _e = (expr);                                    \
+        if (_e != cudaSuccess) return ctx_cuda(c, _e, what);        \
+    } while (0)
+
+// All kernels of one decode step, in dependency order.
+static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool with_final) {
+    const auto &g = m->cfg;
+    const int H = g.hidden, NH = g.n_heads, HD = g.head_dim;
+    const bool pdl = m->pdl;
+    int launches = 0;
+    for (int l = 0; l < g.n_layers; l++) {
+        const DecLayer &L = m->layers[l];
+        QkvArgs qa = {};
+        qa.x = m->xa;
+        qa.norm_w = L.in_norm;
+        qa.eps = g.rms_eps;
+        qa.hidden = H;
+        qa.w[0] = L.wq;
+        qa.w[1] = L.wk;
+        qa.w[2] = L.wv;
+        qa.cos_t = m->cos_t;
+        qa.sin_t = m->sin_t;
+        qa.d_pos = m->pos;
+        qa.q_out = m->q;
+        qa.k_hi = m->plane(0, l);
+        qa.k_lo = m->plane(1, l);
+        qa.v_hi = m->plane(2, l);
+        qa.v_lo = m->plane(3, l);
+        qa.kv_max = g.kv_max;
+        qa.n_heads = NH;
+        qa.head_dim = HD;
+        CKL(launch_qkv_rope(qa, st, pdl), "qkv launch");
+        AttnArgs aa = {};
+        aa.q = m->q;
+        aa.k_hi = qa.k_hi;
+        aa.k_lo = qa.k_lo;
+        aa.v_hi = qa.v_hi;
+        aa.v_lo = qa.v_lo;
+        aa.kv_max = g.kv_max;
+        aa.n_heads = NH;
+        aa.d_pos = m->pos;
+        aa.lo_start = m->lo_start[l];
+        aa.scale = 1.0f / sqrtf((float)HD);
+        aa.out = m->attn;
+        CKL(launch_attn_decode(aa, st, pdl), "attention launch");
+        MvArgs oa = {};
+        oa.W = L.wo;
+        oa.x = m->attn;
+        oa.resid = m->xa;
+        oa.y = m->xb;
+        oa.rows = H;
+        oa.n = NH * HD;
+        CKL(launch_matvec_res(oa, st, pdl), "o-proj launch");
+        launches += 3;
+        if (L.dense) {
+            MoeArgs da = {};
+            da.hidden = H;
+            da.sh_inter = g.dense_inter;
+            da.has_shared = 1;
+            da.dense = 1;
+            da.norm_w = L.post_norm;
+            da.eps = g.rms_eps;
+            da.sh_gu.w = L.dgate;
+            da.sh_up.w = L.dup;
+            da.x = m->xb;
+            da.h = m->h;
+            CKL(launch_moe_gate_up(da, st, pdl), "dense gate_up launch");
+            MvArgs dd = {};
+            dd.W = L.ddown;
+            dd.x = m->h;
+            dd.resid = m->xb;
+            dd.y = m->xa;
+            dd.rows = H;
+            dd.n = g.dense_inter;
+            CKL(launch_matvec_res(dd, st, pdl), "dense down launch");
+            launches += 2;
+        } else {
+            MoeArgs a = {};
+            a.hidden = H;
+            a.inter = g.moe_inter;
+            a.sh_inter = g.n_shared * g.moe_inter;
+            a.top_k = g.top_k;
+            a.simulate = c->simulate;
+            a.has_shared = a.sh_inter > 0;
+            a.norm_w = L.post_norm;
+            a.eps = g.rms_eps;
+            a.int8 = g.use_int8;
+            size_t fused = (size_t)2 * g.moe_inter * H;
+            if (g.use_int8) {
+                a.gu_base = L.gu;
+                a.dn_base = L.dn;
+                a.sh_gu = L.sgu;
+                a.sh_dn = L.sdn;
+            } else {
+                a.gu_base.w = L.block;
+                a.dn_base.w = L.down;
+                a.sh_gu.w = L.block + (size_t)g.n_experts * fused;
+                a.sh_dn.w = L.sdown;
+            }
+            a.gu_stride = (long long)fused;
+            a.dn_stride = (long long)H * g.moe_inter;
+            a.x = m->xb;
+            a.h = m->h;
+            a.out = m->xa;
+            a.resid = m->xb;
+            a.out_mode = 2;
+            CKL(launch_router(L.router, m->xb, g.n_experts, H, m->scores, m->tickets + 1, g.top_k, c->renorm, m->idx,
+                              m->wt, st, pdl, L.post_norm, g.rms_eps),
+                "router launch");
+            a.d_idx = m->idx;
+            a.d_wt = m->wt;
+            CKL(launch_moe_gate_up(a, st, pdl), "moe gate_up launch");
+            CKL(launch_moe_down(a, st, pdl), "moe down launch");
+            launches += 3;
+        }
+    }
+    if (with_final) {
+        // the final RMS-normed hidden state, for callers that ask for it
+        // (the LM-head kernel normalises on load and does not store it)
+        CKL(launch_rmsnorm(m->xa, m->final_norm, m->xfinal, H, g.rms_eps, st, pdl), "final norm launch");
+        launches += 1;
+    }
+    CKL(launch_argmax_bf16(m->lm_head, m->xa, g.vocab, H, m->slot, m->tickets + 0, m->tok, m->val, st, pdl,
+                           m->final_norm, g.rms_eps),
+        "lm head launch");
+    CKL(launch_decode_advance(m->lm_head, H, m->tok, m->pos, m->tok_log, m->xa, st, pdl), "advance launch");
+    launches += 2;
+    m->launches = launches;
+    return DS_CUDA_OK;
+}
+
+static int capture(ds_cuda_ctx *c, DecoderModel *m, bool with_final, cudaGraphExec_t *out) {
+    cudaStream_t st = c->stream;
+    for (int attempt = 0; attempt < 2; attempt++) {
+        cudaGraph_t graph = nullptr;
+        CKL(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
+        int rc = enqueue_step(c, m, st, with_final);
+        cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (rc < 0) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (e == cudaSuccess) e = cudaGraphInstantiate(out, graph, 0);
+        if (graph) cudaGraphDestroy(graph);
+        if (e == cudaSuccess) return DS_CUDA_OK;
+        cudaGetLastError();
+        if (!m->pdl) return ctx_cuda(c, e, "graph capture");
+        m->pdl = false;  // retry without programmatic edges
+    }
+    return ctx_fail(c, DS_CUDA_ECUDA, "graph capture failed");
+}
+
+static int ensure_graph(ds_cuda_ctx *c, DecoderModel *m, bool with_final) {
+    cudaGraphExec_t *g = with_final ? &m->graph_final : &m->graph;
+    if (*g) return DS_CUDA_OK;
+    return capture(c, m, with_final, g);
+}
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+#define LOOK(ptr, bytes) ctx_lookup(c, (ptr), (bytes), true)
+
+extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
+                                      const ds_cuda_layer_weights_t *lw, const float *final_norm,
+                                      const uint16_t *lm_head) {
+    if (!c || !cfg || !lw || !final_norm || !lm_head) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_create: null argument");
+    const auto &g = *cfg;
+    if (g.head_dim != 128 || g.hidden % 16 || g.hidden > 2048 || g.n_heads * g.head_dim > 2048 ||
+        g.kv_max <= 0 || g.kv_max > 4096 || g.n_layers <= 0 || g.moe_inter % 16 || g.top_k > 6 ||
+        g.n_experts > 256 || g.dense_inter % 8 || g.dense_inter > 8192 || g.vocab <= 0)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_create: unsupported configuration");
+    cudaSetDevice(c->device);
+    DecoderModel *m = new DecoderModel();
+    m->cfg = g;
+    const size_t H = g.hidden, QD = (size_t)g.n_heads * g.head_dim, I = g.moe_inter, S = (size_t)g.n_shared * I;
+    const size_t E = g.n_experts;
+    int rc = DS_CUDA_OK;
+    for (int l = 0; l < g.n_layers && rc == DS_CUDA_OK; l++) {
+        const ds_cuda_layer_weights_t &w = lw[l];
+        DecLayer L = {};
+        L.wq = (const uint16_t *)LOOK(w.wq, QD * H * 2);
+        L.wk = (const uint16_t *)LOOK(w.wk, QD * H * 2);
+        L.wv = (const uint16_t *)LOOK(w.wv, QD * H * 2);
+        L.wo = (const uint16_t *)LOOK(w.wo, H * QD * 2);
+        L.in_norm = (const float *)LOOK(w.input_norm, H * 4);
+        L.post_norm = (const float *)LOOK(w.post_attn_norm, H * 4);
+        L.dense = l < g.first_dense;
+        bool ok = L.wq && L.wk && L.wv && L.wo && L.in_norm && L.post_norm;
+        if (L.dense) {
+            size_t D = g.dense_inter;
+            L.dgate = (const uint16_t *)LOOK(w.dense_gate, D * H * 2);
+            L.dup = (const uint16_t *)LOOK(w.dense_up, D * H * 2);
+            L.ddown = (const uint16_t *)LOOK(w.dense_down, H * D * 2);
+            ok = ok && L.dgate && L.dup && L.ddown;
+        } else {
+            L.router = (const uint16_t *)LOOK(w.router, E * H * 2);
+            ok = ok && L.router;
+            if (g.use_int8) {
+                L.gu = WMat{LOOK(w.gu_q, E * 2 * I * H), (const float *)LOOK(w.gu_scale, E * 2 * I * 4),
+                            (const float *)LOOK(w.gu_off, E * 2 * I * 4)};
+                L.dn = WMat{LOOK(w.dn_q, E * H * I), (const float *)LOOK(w.dn_scale, E * H * 4),
+                            (const float *)LOOK(w.dn_off, E * H * 4)};
+                L.sgu = WMat{LOOK(w.sgu_q, 2 * S * H), (const float *)LOOK(w.sgu_scale, 2 * S * 4),
+                             (const float *)LOOK(w.sgu_off, 2 * S * 4)};
+                L.sdn = WMat{LOOK(w.sdn_q, H * S), (const float *)LOOK(w.sdn_scale, H * 4),
+                             (const float *)LOOK(w.sdn_off, H * 4)};
+                ok = ok && L.gu.w && L.gu.scale && L.gu.off && L.dn.w && L.dn.scale && L.dn.off && L.sgu.w &&
+                     L.sgu.scale && L.sgu.off && L.sdn.w && L.sdn.scale && L.sdn.off;
+            } else {
+                L.block = (const uint16_t *)LOOK(w.expert_block, (E * 2 * I * H + 2 * S * H) * 2);
+                L.down = (const uint16_t *)LOOK(w.down, E * H * I * 2);
+                L.sdown = (const uint16_t *)LOOK(w.shared_down, H * S * 2);
+                ok = ok && L.block && L.down && L.sdown;
+            }
+        }
+        if (!ok) rc = ctx_fail(c, DS_CUDA_ENOTREG, "decoder_create: layer %d weights missing or not registrable", l);
+        m->layers.push_back(L);
+    }
+    if (rc == DS_CUDA_OK) {
+        m->final_norm = (const float *)LOOK(final_norm, H * 4);
+        m->lm_head = (const uint16_t *)LOOK(lm_head, (size_t)g.vocab * H * 2);
+        if (!m->final_norm || !m->lm_head) rc = ctx_fail(c, DS_CUDA_ENOTREG, "decoder_create: head weights");
+    }
+    size_t hcap = std::max((size_t)g.top_k * I + S, (size_t)g.dense_inter);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->xa, H);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->xb, H);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->xfinal, H);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->q, QD);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->attn, QD);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->h, hcap);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->scores, 256);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->wt, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->val, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->idx, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->pos, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tok, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tok_log, (size_t)g.kv_max + 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tickets, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->slot, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->kv, 4 * m->plane_elems());
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->cos_t, (size_t)g.kv_max * g.head_dim);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->sin_t, (size_t)g.kv_max * g.head_dim);
+    if (rc == DS_CUDA_OK) {
+        // RoPE cos/sin cache exactly as ds_compute_rope_neox (ds_kernels.c:2399-2424)
+        // over positions 0..kv_max-1 (ds_ocr.c:934-941), in host float math.
+        std::vector<float> cs((size_t)g.kv_max * g.head_dim), sn(cs.size());
+        int half = g.head_dim / 2;
+        for (int s = 0; s < g.kv_max; s++) {
+            float p = (float)s;
+            for (int d = 0; d < half; d++) {
+                float freq = 1.0f / powf(g.rope_theta, (float)(2 * d) / (float)g.head_dim);
+                float ang = p * freq;
+                float cv = cosf(ang), sv = sinf(ang);
+                cs[(size_t)s * g.head_dim + d] = cv;
+                cs[(size_t)s * g.head_dim + d + half] = cv;
+                sn[(size_t)s * g.head_dim + d] = sv;
+                sn[(size_t)s * g.head_dim + d + half] = sv;
+            }
+        }
+        cudaMemcpy(m->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+        m->lo_start.assign(g.n_layers, 0);
+    }
+    if (rc != DS_CUDA_OK) {
+        free_model(m);
+        return rc;
+    }
+    int id = c->next_model++;
+    c->models[id] = m;
+    return id;
+}
+
+extern "C" int ds_cuda_decoder_destroy(ds_cuda_ctx_t *c, int id) {
+    if (!c) return DS_CUDA_EINVAL;
+    DecoderModel *m = get_model(c, id);
+    if (!m) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_destroy: unknown model %d", id);
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    c->models.erase(id);
+    free_model(m);
+    return DS_CUDA_OK;
+}
+
+static inline uint16_t f2bf_rne(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+extern "C" int ds_cuda_decoder_load_kv(ds_cuda_ctx_t *c, int id, int layer, int pos0, int n, const float *k,
+                                       const float *v) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || !k || !v || layer < 0 || layer >= m->cfg.n_layers || pos0 < 0 || n <= 0 || pos0 + n > m->cfg.kv_max)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_load_kv: bad argument");
+    cudaSetDevice(c->device);
+    const int NH = m->cfg.n_heads, HD = m->cfg.head_dim;
+    std::vector<uint16_t> hi((size_t)n * HD), lo((size_t)n * HD);
+    bool exact = true;
+    for (int which = 0; which < 2; which++) {
+        const float *src = which == 0 ? k : v;
+        for (int h = 0; h < NH; h++) {
+            for (int i = 0; i < n; i++)
+                for (int d = 0; d < HD; d++) {
+                    float f = src[(size_t)i * NH * HD + (size_t)h * HD + d];
+                    uint16_t a = f2bf_rne(f);
+                    uint32_t au = (uint32_t)a << 16;
+                    float af;
+                    memcpy(&af, &au, 4);
+                    uint16_t b = f2bf_rne(f - af);
+                    hi[(size_t)i * HD + d] = a;
+                    lo[(size_t)i * HD + d] = b;
+                    if (b != 0) exact = false;
+                }
+            size_t off = ((size_t)h * m->cfg.kv_max + pos0) * HD;
+            CKL(cudaMemcpy(m->plane(which * 2, layer) + off, hi.data(), hi.size() * 2, cudaMemcpyHostToDevice), "kv copy");
+            CKL(cudaMemcpy(m->plane(which * 2 + 1, layer) + off, lo.data(), lo.size() * 2, cudaMemcpyHostToDevice), "kv copy");
+        }
+    }
+    // the lo plane may be skipped below lo_start only while every row there is exact
+    int &ls = m->lo_start[layer];
+    int new_ls = ls;
+    if (exact && pos0 <= ls) new_ls = std::max(ls, pos0 + n);
+    if (!exact && pos0 < ls) new_ls = pos0;
+    if (new_ls != ls) {
+        ls = new_ls;
+        drop_graphs(m);  // lo_start is baked into the captured graph
+    }
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_decoder_set_len(ds_cuda_ctx_t *c, int id, int len) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || len < 0 || len >= m->cfg.kv_max) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_len: bad argument");
+    cudaSetDevice(c->device);
+    // rows at or beyond len will be rewritten by decode steps with F32 values
+    for (int l = 0; l < m->cfg.n_layers; l++)
+        if (m->lo_start[l] > len) {
+            m->lo_start[l] = len;
+            drop_graphs(m);
+        }
+    CKL(cudaMemcpyAsync(m->pos, &len, sizeof(int), cudaMemcpyHostToDevice, c->stream), "set len");
+    CKL(cudaStreamSynchronize(c->stream), "set len");
+    m->host_len = len;
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_decoder_get_len(ds_cuda_ctx_t *c, int id) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_get_len: unknown model");
+    return m->host_len;
+}
+
+extern "C" int ds_cuda_decoder_forward(ds_cuda_ctx_t *c, int id, const float *embed, float *final_x, float *logit) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || !embed) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_forward: bad argument");
+    if (m->host_len + 1 > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_forward: KV cache full");
+    cudaSetDevice(c->device);
+    const int H = m->cfg.hidden;
+    CK(ensure_graph(c, m, final_x != nullptr));
+    CK(ctx_pinned(c, (size_t)H * 8 + 64));
+    memcpy(c->pin, embed, (size_t)H * 4);
+    CKL(cudaMemcpyAsync(m->xa, c->pin, (size_t)H * 4, cudaMemcpyHostToDevice, c->stream), "embed copy");
+    CKL(cudaGraphLaunch(final_x ? m->graph_final : m->graph, c->stream), "graph launch");
+    char *pb = (char *)c->pin;
+    CKL(cudaMemcpyAsync(pb, m->tok, 4, cudaMemcpyDeviceToHost, c->stream), "token copy");
+    CKL(cudaMemcpyAsync(pb + 4, m->val, 4, cudaMemcpyDeviceToHost, c->stream), "logit copy");
+    if (final_x) CKL(cudaMemcpyAsync(pb + 64, m->xfinal, (size_t)H * 4, cudaMemcpyDeviceToHost, c->stream), "x copy");
+    CKL(cudaStreamSynchronize(c->stream), "decoder_forward");
+    int tok;
+    memcpy(&tok, pb, 4);
+    if (logit) memcpy(logit, pb + 4, 4);
+    if (final_x) memcpy(final_x, pb + 64, (size_t)H * 4);
+    m->host_len++;
+    return tok;
+}
+
+extern "C" int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *c, int id, int n_steps, void *stream) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || n_steps < 0) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_generate_dev: bad argument");
+    if (m->host_len + n_steps > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_generate: KV cache full");
+    cudaSetDevice(c->device);
+    CK(ensure_graph(c, m, false));
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    for (int s = 0; s < n_steps; s++) CKL(cudaGraphLaunch(m->graph, st), "graph launch");
+    m->host_len += n_steps;
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_decoder_generate(ds_cuda_ctx_t *c, int id, const float *first_embed, int n_steps,
+                                        int *tokens) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || n_steps <= 0 || !tokens) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_generate: bad argument");
+    cudaSetDevice(c->device);
+    const int H = m->cfg.hidden;
+    int start = m->host_len;
+    if (first_embed) {
+        CK(ctx_pinned(c, (size_t)H * 4));
+        memcpy(c->pin, first_embed, (size_t)H * 4);
+        CKL(cudaMemcpyAsync(m->xa, c->pin, (size_t)H * 4, cudaMemcpyHostToDevice, c->stream), "embed copy");
+    }
+    CK(ds_cuda_decoder_generate_dev(c, id, n_steps, nullptr));
+    CKL(cudaMemcpyAsync(tokens, m->tok_log + start, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, c->stream),
+        "token copy");
+    CKL(cudaStreamSynchronize(c->stream), "decoder_generate");
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *c, int id) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m) return ctx_fail(c, DS_CUDA_EINVAL, "unknown model");
+    if (!m->launches) CK(ensure_graph(c, m, false));
+    return m->launches;
+}

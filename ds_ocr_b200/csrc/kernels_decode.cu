@@ -1,0 +1,478 @@
+// kernels_decode.cu — the rest of the batch-1 greedy decode step
+// (ds_decoder_forward, ds_moe_decoder.c:911-1264): input RMSNorm + QKV +
+// RoPE + KV append, decode attention, O-projection + residual, long-K matvec
+// for the dense FFN down projection, and the step advance (next embedding,
+// position, token log).
+#include <cooperative_groups.h>
+
+#include "kernels_decode.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace ds {
+
+// F32 -> BF16 with round-to-nearest-even, as raw bits.
+__device__ __forceinline__ uint16_t bf16_rne_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+// Split v into hi + lo BF16 halves (v ~= hi + lo to ~2^-17 relative): the KV
+// cache stores K and V as two BF16 planes; the lo plane is only read for
+// positions that are not exactly BF16 (lo_start onwards).
+__device__ __forceinline__ void split_bf16(float v, uint16_t &hi, uint16_t &lo) {
+    hi = bf16_rne_bits(v);
+    lo = bf16_rne_bits(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
+}
+
+// ---------------------------------------------------------------------------
+// Input RMSNorm + QKV + RoPE + KV append (decoder_layer_forward,
+// ds_moe_decoder.c:358-393). Work item t is the row pair (d, d + hd/2) of one
+// head of Q, K or V, so RoPE's split-half rotation (ds_apply_rope_neox,
+// ds_kernels.c:2426-2458) happens in registers:
+//   out[d]      = x1 cos[d]      - x2 sin[d]
+//   out[d+half] = x1 sin[d+half] + x2 cos[d+half]
+// K and V are written to row `pos` of this layer's cache, layout
+// [head][kv_max][head_dim], as hi/lo BF16 planes.
+// ---------------------------------------------------------------------------
+
+template <int CPL>
+__global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
+    pdl_wait();
+    pdl_launch();
+    const int lane = threadIdx.x & 31;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    const int n = a.hidden;
+    const float inv = block_rms_inv(a.x, n, a.eps);
+    XRegBF16<CPL> xr;
+    xr.load_norm(a.x, a.norm_w, inv, n, lane);
+    const int half = a.head_dim >> 1;
+    const int per_mat = a.n_heads * half;
+    const int pos = *a.d_pos;
+    for (int t = gw; t < 3 * per_mat; t += nw) {
+        int m = t / per_mat;
+        int r = t - m * per_mat;
+        int h = r / half;
+        int d = r - h * half;
+        int row0 = h * a.head_dim + d;
+        const uint16_t *W = m == 0 ? a.w[0] : (m == 1 ? a.w[1] : a.w[2]);
+        float s0, s1;
+        row_dot2_bf16<CPL>(W + (size_t)row0 * n, W + (size_t)(row0 + half) * n, n, xr, lane, s0, s1);
+        s0 = warp_sum(s0);
+        s1 = warp_sum(s1);
+        if (lane == 0) {
+            float o0 = s0, o1 = s1;
+            if (m < 2) {
+                const float *cs = a.cos_t + (size_t)pos * a.head_dim;
+                const float *sn = a.sin_t + (size_t)pos * a.head_dim;
+                o0 = __fsub_rn(__fmul_rn(s0, cs[d]), __fmul_rn(s1, sn[d]));
+                o1 = __fadd_rn(__fmul_rn(s0, sn[d + half]), __fmul_rn(s1, cs[d + half]));
+            }
+            if (m == 0) {
+                a.q_out[row0] = o0;
+                a.q_out[row0 + half] = o1;
+            } else {
+                size_t idx = ((size_t)h * a.kv_max + pos) * a.head_dim + d;
+                uint16_t *hi = m == 1 ? a.k_hi : a.v_hi;
+                uint16_t *lo = m == 1 ? a.k_lo : a.v_lo;
+                uint16_t h0, l0, h1, l1;
+                split_bf16(o0, h0, l0);
+                split_bf16(o1, h1, l1);
+                hi[idx] = h0;
+                lo[idx] = l0;
+                hi[idx + half] = h1;
+                lo[idx + half] = l1;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention for one token, all heads (ds_causal_attention_aligned MHA
+// fast path, ds_kernels.c:2181-2249 / :2124-2159).
+//
+// The reference runs, per head, a sequential online softmax with fast exp:
+//   s_j > m : c = fexp(m - s_j); sum = sum*c + 1;  o = o*c + v_j;  m = s_j
+//   else    : a = fexp(s_j - m); sum += a;          o += a*v_j
+//   o *= 1/sum
+// fexp(a)fexp(b) != fexp(a+b), so a plain flash-style merge would differ.
+// Unrolled, key j contributes w_j v_j with
+//   w_j = a_j * prod_{t>j, s_t new max} c_t,   a_j = 1 at a new max,
+// and sum = sum_j w_j. This kernel evaluates exactly that: a cluster of CL
+// CTAs per head splits the keys; each CTA scores its chunk (q.k * scale),
+// the cluster exchanges scores through distributed shared memory, every CTA
+// runs the exclusive prefix-max and the suffix product of correction factors
+// over all keys, forms w_j for its chunk and accumulates w_j v_j; rank 0 sums
+// the CL partial outputs (DSMEM) and scales by 1/sum.
+// head_dim must be 128 (8 lanes x 16 elements per key row).
+// ---------------------------------------------------------------------------
+
+constexpr int ATT_CL = 8;
+constexpr int ATT_MAXK = 4096;
+constexpr int ATT_HD = 128;
+
+__device__ __forceinline__ void load_row16(const uint16_t *hi, const uint16_t *lo, bool use_lo, float f[16]) {
+    uint4 h0 = ldg_stream(hi), h1 = ldg_stream(hi + 8);
+    uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        f[2 * i] = bf16_lo(hw[i]);
+        f[2 * i + 1] = bf16_hi(hw[i]);
+    }
+    if (use_lo) {
+        uint4 l0 = ldg_stream(lo), l1 = ldg_stream(lo + 8);
+        uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            f[2 * i] = __fadd_rn(f[2 * i], bf16_lo(lw[i]));
+            f[2 * i + 1] = __fadd_rn(f[2 * i + 1], bf16_hi(lw[i]));
+        }
+    }
+}
+
+// Block-wide exclusive scan of one value per thread (blockDim == 256) with an
+// associative op; reverse = scan from the last thread down. Warp 0 scans:
+// lane l owns 8 consecutive logical slots, then a shuffle scan of lane totals.
+template <typename Op>
+__device__ __forceinline__ float block_excl_scan(float v, float ident, Op op, bool reverse, float *buf) {
+    const int t = threadIdx.x;
+    const int lt = reverse ? 255 - t : t;
+    buf[lt] = v;
+    __syncthreads();
+    if (t < 32) {
+        float loc[8], acc = ident;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            loc[i] = acc;
+            acc = op(acc, buf[t * 8 + i]);
+        }
+        float inc = acc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            float y = __shfl_up_sync(DS_FULL, inc, o);
+            if (t >= o) inc = op(y, inc);
+        }
+        float excl = __shfl_up_sync(DS_FULL, inc, 1);
+        if (t == 0) excl = ident;
+#pragma unroll
+        for (int i = 0; i < 8; i++) buf[t * 8 + i] = op(excl, loc[i]);
+    }
+    __syncthreads();
+    float r = buf[lt];
+    __syncthreads();
+    return r;
+}
+
+// Block sum of one value per thread (blockDim == 256) in a fixed order.
+__device__ __forceinline__ float block_sum256(float v, float *buf) {
+    buf[threadIdx.x] = v;
+    __syncthreads();
+    float r = 0.f;
+    if (threadIdx.x < 32) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) s = __fadd_rn(s, buf[threadIdx.x * 8 + i]);
+        r = warp_sum(s);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) buf[0] = r;
+    __syncthreads();
+    r = buf[0];
+    __syncthreads();
+    return r;
+}
+
+__global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
+    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ float sc_own[ATT_MAXK / ATT_CL];
+    __shared__ float wts[ATT_MAXK];
+    __shared__ __align__(16) float corr[ATT_MAXK];  // reused as the [32][128] PV reduction buffer
+    __shared__ float opart[ATT_HD];
+    __shared__ float tmp[256];
+    __shared__ float s_sum;
+    float(*red)[ATT_HD] = reinterpret_cast<float(*)[ATT_HD]>(corr);
+
+    const int crank = (int)cluster.block_rank();
+    const int h = blockIdx.x / ATT_CL;
+    const int tid = threadIdx.x;
+    const int g = tid >> 3, li = tid & 7;
+
+    pdl_wait();
+    pdl_launch();
+    const int n = *a.d_pos + 1;
+    const int per = (n + ATT_CL - 1) / ATT_CL;
+    const int j0 = min(n, crank * per), j1 = min(n, j0 + per);
+    const size_t hoff = (size_t)h * a.kv_max * ATT_HD;
+    const uint16_t *khi = a.k_hi + hoff, *klo = a.k_lo + hoff, *vhi = a.v_hi + hoff, *vlo = a.v_lo + hoff;
+    if (tid == 0 && j1 > j0) {
+        prefetch_range(vhi + (size_t)j0 * ATT_HD, (size_t)(j1 - j0) * ATT_HD * 2);
+        int ls = max(j0, a.lo_start);
+        if (ls < j1) prefetch_range(vlo + (size_t)ls * ATT_HD, (size_t)(j1 - ls) * ATT_HD * 2);
+    }
+    float qf[16];
+    {
+        const float4 *qp = reinterpret_cast<const float4 *>(a.q + h * ATT_HD + li * 16);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float4 v = qp[i];
+            qf[4 * i] = v.x; qf[4 * i + 1] = v.y; qf[4 * i + 2] = v.z; qf[4 * i + 3] = v.w;
+        }
+    }
+    // 1. scores of this CTA's keys: 8 lanes per key, 32 keys per pass
+    for (int jb = j0; jb < j1; jb += 32) {
+        int j = jb + g;
+        float s = 0.f;
+        if (j < j1) {
+            float kf[16];
+            load_row16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16, j >= a.lo_start, kf);
+#pragma unroll
+            for (int i = 0; i < 16; i++) s = __fmaf_rn(qf[i], kf[i], s);
+        }
+        s += __shfl_xor_sync(DS_FULL, s, 1);
+        s += __shfl_xor_sync(DS_FULL, s, 2);
+        s += __shfl_xor_sync(DS_FULL, s, 4);
+        if (li == 0 && j < j1) sc_own[j - j0] = __fmul_rn(s, a.scale);
+    }
+    cluster.sync();
+    // 2. gather every key's score of this head
+    for (int j = tid; j < n; j += blockDim.x) {
+        int owner = j / per;
+        const float *src = cluster.map_shared_rank(sc_own, owner);
+        wts[j] = src[j - owner * per];
+    }
+    __syncthreads();
+    // 3. exclusive prefix max -> per-key factor a_j and correction c_j
+    const int seg = (n + blockDim.x - 1) / blockDim.x;
+    const int s0 = min(n, tid * seg), s1 = min(n, s0 + seg);
+    float lm = -1e30f;
+    for (int j = s0; j < s1; j++) lm = fmaxf(lm, wts[j]);
+    float m = block_excl_scan(lm, -1e30f, [](float x, float y) { return fmaxf(x, y); }, false, tmp);
+    for (int j = s0; j < s1; j++) {
+        float s = wts[j];
+        if (s > m) {
+            corr[j] = fast_expf(__fsub_rn(m, s));
+            wts[j] = 1.0f;
+            m = s;
+        } else {
+            corr[j] = 1.0f;
+            wts[j] = fast_expf(__fsub_rn(s, m));
+        }
+    }
+    // 4. suffix product of corrections -> w_j = a_j * prod_{t>j} c_t; sum
+    float lp = 1.0f;
+    for (int j = s1 - 1; j >= s0; j--) lp = __fmul_rn(lp, corr[j]);
+    float P = block_excl_scan(lp, 1.0f, [](float x, float y) { return __fmul_rn(x, y); }, true, tmp);
+    float lsum = 0.f;
+    for (int j = s1 - 1; j >= s0; j--) {
+        float w = __fmul_rn(wts[j], P);
+        wts[j] = w;
+        P = __fmul_rn(P, corr[j]);
+    }
+    for (int j = s0; j < s1; j++) lsum = __fadd_rn(lsum, wts[j]);
+    float S_all = block_sum256(lsum, tmp);  // includes the barrier before corr is reused
+    if (tid == 0) s_sum = S_all;
+    // 5. this chunk's sum_j w_j v_j
+    float acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc[i] = 0.f;
+    for (int jb = j0; jb < j1; jb += 32) {
+        int j = jb + g;
+        if (j < j1) {
+            float vf[16];
+            load_row16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16, j >= a.lo_start, vf);
+            float w = wts[j];
+#pragma unroll
+            for (int i = 0; i < 16; i++) acc[i] = __fmaf_rn(w, vf[i], acc[i]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i++) red[g][li * 16 + i] = acc[i];
+    __syncthreads();
+    if (tid < ATT_HD) {
+        float o = 0.f;
+        for (int k = 0; k < 32; k++) o = __fadd_rn(o, red[k][tid]);
+        opart[tid] = o;
+    }
+    cluster.sync();
+    // 6. rank 0 combines the cluster's partial outputs
+    if (crank == 0 && tid < ATT_HD) {
+        float o = 0.f;
+        for (int r = 0; r < ATT_CL; r++) o = __fadd_rn(o, cluster.map_shared_rank(opart, r)[tid]);
+        float S = s_sum;
+        a.out[h * ATT_HD + tid] = S > 0.f ? __fmul_rn(o, __fdiv_rn(1.0f, S)) : o;
+    }
+    cluster.sync();
+}
+
+// ---------------------------------------------------------------------------
+// Generic row matvec with optional input RMSNorm, bias and residual:
+//   y = [resid +] W . norm(x) [+ bias]      (n <= 2048)
+// O-projection + residual: ds_linear_nobias_bf16 + ds_residual_rms_norm's add
+// (ds_moe_decoder.c:447-453).
+// ---------------------------------------------------------------------------
+
+template <int CPL>
+__global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
+    pdl_wait();
+    pdl_launch();
+    const int lane = threadIdx.x & 31;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    const float inv = a.norm_w ? block_rms_inv(a.x, a.n, a.eps) : 1.f;
+    XRegBF16<CPL> xr;
+    xr.load_norm(a.x, a.norm_w, inv, a.n, lane);
+    for (int r = 2 * gw; r < a.rows; r += 2 * nw) {
+        float s0, s1 = 0.f;
+        if (r + 1 < a.rows) row_dot2_bf16<CPL>(a.W + (size_t)r * a.n, a.W + (size_t)(r + 1) * a.n, a.n, xr, lane, s0, s1);
+        else s0 = row_dot_bf16<CPL>(a.W + (size_t)r * a.n, a.n, xr, lane);
+        s0 = warp_sum(s0);
+        s1 = warp_sum(s1);
+        if (lane == 0) {
+#pragma unroll
+            for (int k = 0; k < 2; k++) {
+                int rr = r + k;
+                if (rr >= a.rows) break;
+                float v = k ? s1 : s0;
+                if (a.bias) v = __fadd_rn(v, a.bias[rr]);
+                if (a.resid) v = __fadd_rn(a.resid[rr], v);
+                a.y[rr] = v;
+            }
+        }
+    }
+}
+
+// Long-K matvec (n up to 8192, x staged in shared memory): the dense FFN down
+// projection [1280 x 6848] with the residual add (ds_moe_decoder.c:101, :468).
+__global__ void __launch_bounds__(128) matvec_long_kernel(MvArgs a) {
+    extern __shared__ float xs[];
+    pdl_wait();
+    pdl_launch();
+    for (int i = threadIdx.x; i < a.n; i += blockDim.x) xs[i] = a.x[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= a.rows) return;
+    const uint16_t *wr = a.W + (size_t)row * a.n;
+    const int nch = a.n >> 3;
+    float acc = 0.f;
+    constexpr int U = 8;
+    for (int c0 = lane; c0 < nch; c0 += 32 * U) {
+        uint4 w[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            int ch = c0 + 32 * u;
+            w[u] = ch < nch ? ldg_stream(wr + 8 * ch) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            int ch = c0 + 32 * u;
+            if (ch < nch) {
+                const float4 *xp = reinterpret_cast<const float4 *>(xs + 8 * ch);
+                acc = dot8_bf16(w[u], xp[0], xp[1], acc);
+            }
+        }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        float v = acc;
+        if (a.bias) v = __fadd_rn(v, a.bias[row]);
+        if (a.resid) v = __fadd_rn(a.resid[row], v);
+        a.y[row] = v;
+    }
+}
+
+// out = RMSNorm(x; w) for one vector (ds_rms_norm, ds_kernels.c:1387-1471).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *w, float *out, int n, float eps) {
+    pdl_wait();
+    pdl_launch();
+    const float inv = block_rms_inv(x, n, eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], w[i]), inv);
+}
+
+// Step advance for greedy decode: next input = BF16 embedding row of the
+// token just produced, widened to F32 (ds_ocr.c:2272-2279); token logged at
+// its position; position advanced (ds_moe_decoder.c:997).
+__global__ void decode_advance_kernel(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,
+                                      float *x_out) {
+    pdl_wait();
+    pdl_launch();
+    int tok = *d_tok;
+    const int pos = *d_pos;
+    // an all-NaN logit row leaves no winner (token -1): embed row 0, log -1
+    const uint16_t *row = E + (size_t)(tok < 0 ? 0 : tok) * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) x_out[i] = __uint_as_float((uint32_t)row[i] << 16);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        tok_log[pos] = tok;
+        *d_pos = pos + 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+static int sms() {
+    static int n = 0;
+    if (!n) {
+        int dev;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    }
+    return n;
+}
+
+#define DS_CPL_SWITCH2(n, CHUNK, BODY)                \
+    do {                                              \
+        int _c = ((n) / (CHUNK) + 31) / 32;           \
+        if (_c <= 2) { constexpr int CPL = 2; BODY; } \
+        else if (_c <= 4) { constexpr int CPL = 4; BODY; } \
+        else if (_c <= 5) { constexpr int CPL = 5; BODY; } \
+        else if (_c <= 8) { constexpr int CPL = 8; BODY; } \
+        else return cudaErrorInvalidValue;            \
+    } while (0)
+
+cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl) {
+    if (a.hidden % 8 || a.hidden > 2048 || a.head_dim % 2) return cudaErrorInvalidValue;
+    int tasks = 3 * a.n_heads * (a.head_dim / 2);
+    int grid = min((tasks + 7) / 8, sms() * 8);
+    QkvArgs aa = a;
+    void *args[] = {&aa};
+    DS_CPL_SWITCH2(a.hidden, 8, return launch_ex((const void *)qkv_rope_kernel<CPL>, grid, 256, 0, st, pdl, args));
+}
+
+cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl) {
+    if (a.kv_max > ATT_MAXK) return cudaErrorInvalidValue;
+    AttnArgs aa = a;
+    void *args[] = {&aa};
+    // cluster dims are compiled into the kernel (__cluster_dims__)
+    return launch_ex((const void *)attn_decode_kernel, a.n_heads * ATT_CL, 256, 0, st, pdl, args);
+}
+
+cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl) {
+    MvArgs aa = a;
+    void *args[] = {&aa};
+    if (a.n % 8) return cudaErrorInvalidValue;
+    if (a.n <= 2048) {
+        int grid = min(((a.rows + 1) / 2 + 7) / 8, sms() * 8);
+        DS_CPL_SWITCH2(a.n, 8, return launch_ex((const void *)matvec_res_kernel<CPL>, grid, 256, 0, st, pdl, args));
+    }
+    if (a.n > 8192 || a.norm_w) return cudaErrorInvalidValue;  // x stays within the 48 KB default smem
+    int grid = (a.rows + 3) / 4;
+    return launch_ex((const void *)matvec_long_kernel, grid, 128, (size_t)a.n * 4, st, pdl, args);
+}
+
+cudaError_t launch_decode_advance(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,
+                                  float *x_out, cudaStream_t st, bool pdl) {
+    void *args[] = {&E, &hidden, &d_tok, &d_pos, &tok_log, &x_out};
+    return launch_ex((const void *)decode_advance_kernel, 1, 256, 0, st, pdl, args);
+}
+
+}  // namespace ds
+
+namespace ds {
+cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int n, float eps, cudaStream_t st, bool pdl) {
+    void *args[] = {&x, &w, &out, &n, &eps};
+    return launch_ex((const void *)rmsnorm_kernel, 1, 256, 0, st, pdl, args);
+}
+}  // namespace ds

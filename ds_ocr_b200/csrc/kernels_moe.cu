@@ -17,14 +17,16 @@ template <int CPL>
 __global__ void __launch_bounds__(256) argmax_bf16_kernel(const uint16_t *__restrict__ W,
                                                           const float *__restrict__ x, int rows, int n,
                                                           unsigned long long *slot, unsigned *ticket,
-                                                          int *tok_out, float *val_out) {
+                                                          int *tok_out, float *val_out, const float *norm_w,
+                                                          float eps) {
     pdl_wait();
     pdl_launch();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
+    const float inv = norm_w ? block_rms_inv(x, n, eps) : 1.f;
     XRegBF16<CPL> xr;
-    xr.load(x, n, lane);
+    xr.load_norm(x, norm_w, inv, n, lane);
     float best = -INFINITY;
     int bi = 0x7fffffff;
     for (int r = 2 * gw; r < rows; r += 2 * nw) {
@@ -117,14 +119,16 @@ __device__ void router_select(const float *scores, int E, int top_k, int renorm,
 template <int CPL>
 __global__ void __launch_bounds__(256) router_kernel(const uint16_t *__restrict__ Wr, const float *__restrict__ x,
                                                      int E, int n, float *scores, unsigned *ticket, int top_k,
-                                                     int renorm, int *d_idx, float *d_wt) {
+                                                     int renorm, int *d_idx, float *d_wt, const float *norm_w,
+                                                     float eps) {
     pdl_wait();
     pdl_launch();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
+    const float inv = norm_w ? block_rms_inv(x, n, eps) : 1.f;
     XRegBF16<CPL> xr;
-    xr.load(x, n, lane);
+    xr.load_norm(x, norm_w, inv, n, lane);
     for (int r = gw; r < E; r += nw) {
         float s = warp_sum(row_dot_bf16<CPL>(Wr + (size_t)r * n, n, xr, lane));
         if (lane == 0) scores[r] = s;
@@ -167,36 +171,38 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
     const int nr = a.top_k * a.inter;
     const int total = nr + (a.has_shared ? a.sh_inter : 0);
     const int n = a.hidden;
+    const float inv = a.norm_w ? block_rms_inv(a.x, n, a.eps) : 1.f;
+    const bool sim = a.simulate && !a.dense;  // the dense FFN path never truncates (ds_moe_decoder.c:75-105)
     if constexpr (!I8) {
         XRegBF16<CPL> xr;
-        xr.load(a.x, n, lane);
+        xr.load_norm(a.x, a.norm_w, inv, n, lane);
         for (int p = gw; p < total; p += nw) {
-            const uint16_t *w;
-            int i, half;
+            const uint16_t *w, *wu;
+            int i;
             if (p < nr) {
                 int k = p / a.inter;
                 i = p - k * a.inter;
-                half = a.inter;
                 w = (const uint16_t *)expert_mat(a, k, true).w;
+                wu = w + (size_t)a.inter * n;
             } else {
                 i = p - nr;
-                half = a.sh_inter;
                 w = (const uint16_t *)a.sh_gu.w;
+                wu = a.sh_up.w ? (const uint16_t *)a.sh_up.w : w + (size_t)a.sh_inter * n;
             }
             float g, u;
-            row_dot2_bf16<CPL>(w + (size_t)i * n, w + (size_t)(i + half) * n, n, xr, lane, g, u);
+            row_dot2_bf16<CPL>(w + (size_t)i * n, wu + (size_t)i * n, n, xr, lane, g, u);
             g = warp_sum(g);
             u = warp_sum(u);
             if (lane == 0) {
-                if (a.simulate) { g = bf16_roundtrip(g); u = bf16_roundtrip(u); }
+                if (sim) { g = bf16_roundtrip(g); u = bf16_roundtrip(u); }
                 float hv = swiglu(g, u);
-                if (a.simulate) hv = bf16_roundtrip(hv);
+                if (sim) hv = bf16_roundtrip(hv);
                 a.h[p] = hv;
             }
         }
     } else {
         XRegI8<CPL> xr;
-        xr.load(a.x, n, lane);
+        xr.load_norm(a.x, a.norm_w, inv, n, lane);
         float xs = 0.f;
 #pragma unroll
         for (int c = 0; c < CPL; c++)
@@ -435,19 +441,21 @@ cudaError_t launch_ex(const void *func, dim3 grid, dim3 block, size_t smem, cuda
     } while (0)
 
 cudaError_t launch_argmax_bf16(const uint16_t *W, const float *x, int rows, int n, unsigned long long *slot,
-                               unsigned *ticket, int *tok, float *val, cudaStream_t st, bool pdl) {
+                               unsigned *ticket, int *tok, float *val, cudaStream_t st, bool pdl,
+                               const float *norm_w, float eps) {
     if (n % 8 || n > 2048) return cudaErrorInvalidValue;
     int warps_needed = (rows + 1) / 2;
     int grid = min((warps_needed + 7) / 8, sm_count() * 8);
-    void *args[] = {&W, &x, &rows, &n, &slot, &ticket, &tok, &val};
+    void *args[] = {&W, &x, &rows, &n, &slot, &ticket, &tok, &val, &norm_w, &eps};
     DS_CPL_SWITCH(n, 8, return launch_ex((const void *)argmax_bf16_kernel<CPL>, grid, 256, 0, st, pdl, args));
 }
 
 cudaError_t launch_router(const uint16_t *Wr, const float *x, int E, int n, float *scores, unsigned *ticket,
-                          int top_k, int renorm, int *d_idx, float *d_wt, cudaStream_t st, bool pdl) {
+                          int top_k, int renorm, int *d_idx, float *d_wt, cudaStream_t st, bool pdl,
+                          const float *norm_w, float eps) {
     if (n % 8 || n > 2048 || E > 256 || top_k > 8) return cudaErrorInvalidValue;
     int grid = (E + 7) / 8;
-    void *args[] = {&Wr, &x, &E, &n, &scores, &ticket, &top_k, &renorm, &d_idx, &d_wt};
+    void *args[] = {&Wr, &x, &E, &n, &scores, &ticket, &top_k, &renorm, &d_idx, &d_wt, &norm_w, &eps};
     DS_CPL_SWITCH(n, 8, return launch_ex((const void *)router_kernel<CPL>, grid, 256, 0, st, pdl, args));
 }
 

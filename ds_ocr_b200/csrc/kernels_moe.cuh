@@ -25,6 +25,10 @@ struct WMat {
 struct MoeArgs {
     int hidden, inter, sh_inter, top_k;
     int int8, simulate, has_shared;
+    int dense;               // dense FFN: sh_gu = gate [S x H], sh_up = up [S x H]; no truncation
+    const float *norm_w;     // if set, x is RMS-normalised on load with these weights
+    float eps;
+    WMat sh_up;
     int out_mode;            // 0: out = moe; 1: out += moe; 2: out = resid + moe
     WMat gu[8], dn[8];
     float wt[8];
@@ -60,9 +64,54 @@ __device__ __forceinline__ float expert_wt(const MoeArgs &a, int k) {
 // Register-resident activation slices. Lane `l` owns chunks l, l+32, ... of
 // the input; a BF16 chunk is 8 columns (16 B), an INT8 chunk is 16 columns.
 // ---------------------------------------------------------------------------
+// RMS inverse of src[0..n) for the whole block: 1/sqrtf(sum(x^2)/n + eps)
+// (ds_rms_norm, ds_kernels.c:1387-1440). Fixed reduction order, so every CTA
+// of a grid computes the identical value. All threads must call it.
+__device__ __forceinline__ float block_rms_inv(const float *src, int n, float eps) {
+    __shared__ float red[33];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = __fmaf_rn(src[i], src[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t = __fadd_rn(t, red[w]);
+        red[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)n), eps)));
+    }
+    __syncthreads();
+    float inv = red[32];
+    __syncthreads();
+    return inv;
+}
+
+// (x * w) * inv, the reference's operation order (ds_kernels.c:1443-1449).
+__device__ __forceinline__ float4 norm4(float4 x, float4 w, float inv) {
+    return make_float4(__fmul_rn(__fmul_rn(x.x, w.x), inv), __fmul_rn(__fmul_rn(x.y, w.y), inv),
+                       __fmul_rn(__fmul_rn(x.z, w.z), inv), __fmul_rn(__fmul_rn(x.w, w.w), inv));
+}
+
 template <int CPL>
 struct XRegBF16 {
     float4 v[CPL][2];
+    // load with optional RMS normalisation (w == nullptr: plain load)
+    __device__ __forceinline__ void load_norm(const float *x, const float *w, float inv, int n, int lane) {
+        if (!w) { load(x, n, lane); return; }
+        const int nch = n >> 3;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            int ch = lane + 32 * c;
+            if (ch < nch) {
+                v[c][0] = norm4(*reinterpret_cast<const float4 *>(x + 8 * ch),
+                                *reinterpret_cast<const float4 *>(w + 8 * ch), inv);
+                v[c][1] = norm4(*reinterpret_cast<const float4 *>(x + 8 * ch + 4),
+                                *reinterpret_cast<const float4 *>(w + 8 * ch + 4), inv);
+            } else {
+                v[c][0] = make_float4(0.f, 0.f, 0.f, 0.f);
+                v[c][1] = v[c][0];
+            }
+        }
+    }
     __device__ __forceinline__ void load(const float *x, int n, int lane) {
         const int nch = n >> 3;
 #pragma unroll
@@ -121,6 +170,19 @@ __device__ __forceinline__ void row_dot2_bf16(const uint16_t *r0, const uint16_t
 template <int CPL>
 struct XRegI8 {
     float4 v[CPL][4];
+    __device__ __forceinline__ void load_norm(const float *x, const float *w, float inv, int n, int lane) {
+        if (!w) { load(x, n, lane); return; }
+        const int nch = n >> 4;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            int ch = lane + 32 * c;
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                v[c][q] = ch < nch ? norm4(*reinterpret_cast<const float4 *>(x + 16 * ch + 4 * q),
+                                           *reinterpret_cast<const float4 *>(w + 16 * ch + 4 * q), inv)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     __device__ __forceinline__ void load(const float *x, int n, int lane) {
         const int nch = n >> 4;
 #pragma unroll

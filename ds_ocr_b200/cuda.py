@@ -77,6 +77,18 @@ class Context:
             rc = self.lib.ds_cuda_register_expert_block(self.h, _a(arr), arr.nbytes)
         return self.check(rc, "register")
 
+    def unregister(self, arr):
+        rc = self.check(self.lib.ds_cuda_unregister(self.h, _a(arr)), "unregister")
+        self._keep = [a for a in self._keep if a is not arr]
+        return rc
+
+    def _pin(self, *arrs):
+        """Weights passed by pointer are registered on first use and keyed by
+        host address: keep them alive so the address cannot be reused."""
+        for a in arrs:
+            if a is not None and not any(a is k for k in self._keep[-64:]):
+                self._keep.append(a)
+
     def device_ptr(self, arr):
         return self.lib.ds_cuda_device_ptr(self.h, _a(arr))
 
@@ -87,6 +99,7 @@ class Context:
     # -- Metal-shaped MoE calls -------------------------------------------
     def moe_experts(self, x, gate_ups, downs, weights, hidden, inter):
         k = len(gate_ups)
+        self._pin(*gate_ups, *downs)
         gp = (ctypes.c_void_p * max(k, 1))(*[_a(g) for g in gate_ups])
         dp = (ctypes.c_void_p * max(k, 1))(*[_a(d) for d in downs])
         w = _f32(weights)
@@ -96,12 +109,14 @@ class Context:
         return out
 
     def shared_experts(self, x, gate_up, down, hidden, shared_inter, output):
+        self._pin(gate_up, down)
         x = _f32(x)
         self.check(self.lib.ds_cuda_shared_experts(self.h, _a(x), _a(gate_up), _a(down), hidden, shared_inter,
                                                    _a(output)), "shared_experts")
         return output
 
     def expert_forward_fused(self, x, gate_up, down, hidden, inter):
+        self._pin(gate_up, down)
         x = _f32(x)
         out = np.empty(hidden, np.float32)
         self.check(self.lib.ds_cuda_expert_forward_fused(self.h, _a(out), _a(x), _a(gate_up), _a(down), hidden,
@@ -118,6 +133,7 @@ class Context:
 
     def moe_layer(self, x, mw, return_routing=False):
         d = mw.d
+        self._pin(mw.router, mw.block, mw.down, mw.shared_down)
         x = _f32(x)
         out = np.empty(d.hidden, np.float32)
         idx = np.empty(d.top_k, np.int32)
@@ -129,6 +145,8 @@ class Context:
 
     def moe_layer_int8(self, x, mw, return_routing=False):
         d, q = mw.d, mw.int8
+        self._pin(mw.router, *[getattr(q, n) for n in ("gu_q", "gu_s", "gu_o", "dn_q", "dn_s", "dn_o", "sgu_q",
+                                                        "sgu_s", "sgu_o", "sdn_q", "sdn_s", "sdn_o")])
         x = _f32(x)
         out = np.empty(d.hidden, np.float32)
         idx = np.empty(d.top_k, np.int32)
@@ -141,16 +159,19 @@ class Context:
 
     # -- LM head -----------------------------------------------------------
     def argmax_matvec_bf16(self, x, W, in_dim, out_dim):
+        self._pin(W)
         x = _f32(x)
         lg = np.empty(1, np.float32)
         tok = self.check(self.lib.ds_cuda_argmax_matvec_bf16(self.h, _a(x), _a(W), in_dim, out_dim, _a(lg)), "argmax")
         return tok, float(lg[0])
 
     def lm_head_argmax(self, x, W, hidden, vocab):
+        self._pin(W)
         x = _f32(x)
         return self.check(self.lib.ds_cuda_lm_head_argmax(self.h, _a(x), _a(W), hidden, vocab), "lm_head_argmax")
 
     def argmax_batch(self, X, W, in_dim, out_dim):
+        self._pin(W)
         X = _f32(X)
         B = X.shape[0]
         tok = np.empty(B, np.int32)
@@ -160,6 +181,7 @@ class Context:
         return tok, lg
 
     def matvec_bf16(self, x, W, in_dim, out_dim, bias=None):
+        self._pin(W, bias)
         x = _f32(x)
         y = np.empty(out_dim, np.float32)
         self.check(self.lib.ds_cuda_matvec_bf16(self.h, _a(y), _a(x), _a(W), _a(bias), in_dim, out_dim), "matvec")

@@ -1,0 +1,140 @@
+"""Greedy decode of the DeepSeek3B-MoE decoder through the ds_cuda C ABI.
+
+`Decoder` mirrors the reference's decode entry point ds_decoder_forward
+(ds_moe_decoder.c:911): forward(embed) runs one step and returns the greedy
+token, advancing the KV cache. generate(n) runs n steps on the device
+without host round trips (each step's token embedding feeds the next).
+"""
+import ctypes
+
+import numpy as np
+
+from . import synth
+from ._lib import DsCudaError, load
+from .cuda import Context, _a
+
+
+class DecoderConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "n_heads", "head_dim", "dense_inter", "moe_inter",
+                                            "n_experts", "n_shared", "top_k", "vocab", "first_dense")] + \
+               [("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("kv_max", ctypes.c_int),
+                ("use_int8", ctypes.c_int)]
+
+
+_LW_FIELDS = ("wq", "wk", "wv", "wo", "input_norm", "post_attn_norm", "dense_gate", "dense_up", "dense_down",
+              "router", "expert_block", "down", "shared_down", "gu_q", "gu_scale", "gu_off", "dn_q", "dn_scale",
+              "dn_off", "sgu_q", "sgu_scale", "sgu_off", "sdn_q", "sdn_scale", "sdn_off")
+
+
+class LayerWeightsC(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in _LW_FIELDS]
+
+
+def layer_struct(lw):
+    s = LayerWeightsC()
+    s.wq, s.wk, s.wv, s.wo = _a(lw.wq), _a(lw.wk), _a(lw.wv), _a(lw.wo)
+    s.input_norm, s.post_attn_norm = _a(lw.input_norm), _a(lw.post_norm)
+    s.dense_gate, s.dense_up, s.dense_down = _a(lw.dense_gate), _a(lw.dense_up), _a(lw.dense_down)
+    m = lw.moe
+    if m is not None:
+        s.router, s.expert_block, s.down, s.shared_down = _a(m.router), _a(m.block), _a(m.down), _a(m.shared_down)
+        q = m.int8
+        if q is not None:
+            s.gu_q, s.gu_scale, s.gu_off = _a(q.gu_q), _a(q.gu_s), _a(q.gu_o)
+            s.dn_q, s.dn_scale, s.dn_off = _a(q.dn_q), _a(q.dn_s), _a(q.dn_o)
+            s.sgu_q, s.sgu_scale, s.sgu_off = _a(q.sgu_q), _a(q.sgu_s), _a(q.sgu_o)
+            s.sdn_q, s.sdn_scale, s.sdn_off = _a(q.sdn_q), _a(q.sdn_s), _a(q.sdn_o)
+    return s
+
+
+def quantize_int8(model, ctx=None):
+    """The --int4 switch: per-row INT8 copies of every MoE layer's experts,
+    quantised on the GPU (bit-identical to ds_int4_quantize_bf16)."""
+    own = ctx is None
+    ctx = ctx or Context(0)
+    d = model.d
+    H, I, S, E = d.hidden, d.moe_inter, d.shared_inter, d.n_experts
+    for lw in model.layers:
+        m = lw.moe
+        if m is None:
+            continue
+        q = synth.Int8Moe(d)
+        for e in range(E):
+            a, b, c = ctx.int8_quantize_bf16(m.expert_gate_up(e), 2 * I, H)
+            q.gu_q[e * 2 * I * H:(e + 1) * 2 * I * H], q.gu_s[e * 2 * I:(e + 1) * 2 * I], q.gu_o[e * 2 * I:(e + 1) * 2 * I] = a, b, c
+            a, b, c = ctx.int8_quantize_bf16(m.expert_down(e), H, I)
+            q.dn_q[e * H * I:(e + 1) * H * I], q.dn_s[e * H:(e + 1) * H], q.dn_o[e * H:(e + 1) * H] = a, b, c
+        q.sgu_q[:], q.sgu_s[:], q.sgu_o[:] = ctx.int8_quantize_bf16(m.shared_gate_up(), 2 * S, H)
+        q.sdn_q[:], q.sdn_s[:], q.sdn_o[:] = ctx.int8_quantize_bf16(m.shared_down, H, S)
+        m.int8 = q
+    if own:
+        ctx.close()
+    return model
+
+
+class Decoder:
+    def __init__(self, model, ctx=None, kv_max=1024, use_int8=False):
+        self.ctx = ctx or Context(0)
+        self.lib = self.ctx.lib
+        self.model = model
+        d = model.d
+        self.cfg = DecoderConfig(d.hidden, d.n_layers, d.n_heads, d.head_dim, d.dense_inter, d.moe_inter,
+                                 d.n_experts, d.n_shared, d.top_k, d.vocab, d.first_dense, synth.RMS_EPS,
+                                 synth.ROPE_THETA, kv_max, int(use_int8))
+        self._layers = (LayerWeightsC * d.n_layers)(*[layer_struct(lw) for lw in model.layers])
+        self.ctx._pin(*[getattr(lw, n) for lw in model.layers for n in ("wq", "wk", "wv", "wo", "input_norm",
+                                                                        "post_norm", "dense_gate", "dense_up",
+                                                                        "dense_down")])
+        for lw in model.layers:
+            if lw.moe is not None:
+                m = lw.moe
+                self.ctx._pin(m.router, m.block, m.down, m.shared_down)
+                if m.int8 is not None:
+                    self.ctx._pin(*m.int8.__dict__.values())
+        self.ctx._pin(model.final_norm, model.lm_head)
+        self.id = self.ctx.check(self.lib.ds_cuda_decoder_create(self.ctx.h, ctypes.byref(self.cfg), self._layers,
+                                                                 _a(model.final_norm), _a(model.lm_head)),
+                                 "decoder_create")
+
+    def load_kv(self, ks, vs, pos0=0):
+        for l, (k, v) in enumerate(zip(ks, vs)):
+            k = np.ascontiguousarray(k, np.float32)
+            v = np.ascontiguousarray(v, np.float32)
+            self.ctx.check(self.lib.ds_cuda_decoder_load_kv(self.ctx.h, self.id, l, pos0, k.shape[0], _a(k), _a(v)),
+                           "decoder_load_kv")
+        self.set_len(pos0 + ks[0].shape[0])
+
+    def set_len(self, n):
+        self.ctx.check(self.lib.ds_cuda_decoder_set_len(self.ctx.h, self.id, n), "decoder_set_len")
+
+    @property
+    def length(self):
+        return self.ctx.check(self.lib.ds_cuda_decoder_get_len(self.ctx.h, self.id), "decoder_get_len")
+
+    def forward(self, embed, want_x=False):
+        embed = np.ascontiguousarray(embed, np.float32)
+        fx = np.empty(self.model.d.hidden, np.float32) if want_x else None
+        lg = np.empty(1, np.float32)
+        tok = self.ctx.check(self.lib.ds_cuda_decoder_forward(self.ctx.h, self.id, _a(embed), _a(fx), _a(lg)),
+                             "decoder_forward")
+        return (tok, fx, float(lg[0])) if want_x else tok
+
+    def generate(self, n_steps, first_embed=None):
+        toks = np.empty(n_steps, np.int32)
+        fe = None if first_embed is None else np.ascontiguousarray(first_embed, np.float32)
+        self.ctx.check(self.lib.ds_cuda_decoder_generate(self.ctx.h, self.id, _a(fe), n_steps, _a(toks)),
+                       "decoder_generate")
+        return toks
+
+    def generate_dev(self, n_steps, stream=None):
+        self.ctx.check(self.lib.ds_cuda_decoder_generate_dev(self.ctx.h, self.id, n_steps, stream),
+                       "decoder_generate_dev")
+
+    @property
+    def launches_per_step(self):
+        return self.ctx.check(self.lib.ds_cuda_decoder_launches_per_step(self.ctx.h, self.id), "launches")
+
+    def close(self):
+        if self.id and self.ctx.h:
+            self.lib.ds_cuda_decoder_destroy(self.ctx.h, self.id)
+            self.id = 0

@@ -91,6 +91,11 @@ int ds_cuda_register_expert_block(ds_cuda_ctx_t *ctx, const void *block_ptr, siz
 /* Registers the three arrays of an INT8 block (the --int4 path,
  * ds_quantize.h:30-37; quantised by ds_int4_quantize_bf16 on the host). */
 int ds_cuda_register_int8_block(ds_cuda_ctx_t *ctx, const ds_cuda_int8_block_t *block);
+/* Drops the registration whose host range starts at host_ptr and frees its
+ * HBM copy. Registrations are keyed by host address, so a caller that frees
+ * or reuses a registered host buffer must unregister it first (the
+ * reference's weights are mmap'd for the context's lifetime and never are). */
+int ds_cuda_unregister(ds_cuda_ctx_t *ctx, const void *host_ptr);
 /* Device address of a registered host pointer (NULL if unregistered). */
 const void *ds_cuda_device_ptr(ds_cuda_ctx_t *ctx, const void *host_ptr);
 /* Bytes of HBM held by registered weights. */
@@ -176,6 +181,70 @@ int ds_cuda_moe_layer_dev(ds_cuda_ctx_t *ctx, const float *d_x, float *d_out,
                           const uint16_t *d_down, const uint16_t *d_shared_down, int hidden, int inter,
                           int shared_inter, int n_experts, int top_k, int *d_top_idx, float *d_top_w,
                           void *stream);
+
+/* ---------------------------------------------------------------------
+ * Decoder — the single-token greedy decode step of ds_decoder_forward
+ * (ds_moe_decoder.c:911-1264, decoder_layer_forward :339-474) on the GPU,
+ * with the KV cache resident in HBM. One call = input RMSNorm, QKV, RoPE,
+ * KV append, attention, O-proj + residual, post-attention RMSNorm, dense
+ * FFN (layer < first_dense) or MoE, residual, for every layer; final
+ * RMSNorm; argmax LM head. The step is one CUDA graph of ~85 kernels
+ * chained with programmatic dependent launch.
+ * --------------------------------------------------------------------- */
+typedef struct {
+    int hidden, n_layers, n_heads, head_dim; /* head_dim must be 128 */
+    int dense_inter, moe_inter, n_experts, n_shared, top_k, vocab, first_dense;
+    float rms_eps, rope_theta;
+    int kv_max;   /* KV capacity in tokens (the reference allocates 4096, ds_ocr.c:861) */
+    int use_int8; /* 1: MoE layers use the INT8 blocks (the --int4 path) */
+} ds_cuda_decoder_config_t;
+
+/* The fields of the reference's ds_dec_layer_t (ds_ocr.h:282-342) the
+ * decode step reads. Host pointers; copied to HBM at create. */
+typedef struct {
+    const uint16_t *wq, *wk, *wv, *wo;        /* [heads*head_dim x hidden], wo [hidden x heads*head_dim] */
+    const float *input_norm, *post_attn_norm; /* [hidden] */
+    const uint16_t *dense_gate, *dense_up;    /* dense layers: [dense_inter x hidden] */
+    const uint16_t *dense_down;               /* [hidden x dense_inter] */
+    const uint16_t *router;                   /* MoE layers: [n_experts x hidden] */
+    const uint16_t *expert_block;             /* [E x 2I x H] + shared [2S x H] (ds_ocr.c:696-768) */
+    const uint16_t *down;                     /* [E x H x I] */
+    const uint16_t *shared_down;              /* [H x S] */
+    /* INT8 copies (use_int8), contiguous per kind as in ds_cuda_moe_layer_int8 */
+    const int8_t *gu_q; const float *gu_scale, *gu_off;
+    const int8_t *dn_q; const float *dn_scale, *dn_off;
+    const int8_t *sgu_q; const float *sgu_scale, *sgu_off;
+    const int8_t *sdn_q; const float *sdn_scale, *sdn_off;
+} ds_cuda_layer_weights_t;
+
+/* Returns a model handle > 0. lm_head is [vocab x hidden] BF16, also used
+ * as the token embedding table (tied, as in the reference's V2 config). */
+int ds_cuda_decoder_create(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
+                           const ds_cuda_layer_weights_t *layers, const float *final_norm,
+                           const uint16_t *lm_head);
+int ds_cuda_decoder_destroy(ds_cuda_ctx_t *ctx, int model);
+/* Writes KV rows [pos0, pos0+n) of one layer from F32 [n x heads*head_dim]
+ * arrays (the reference's F32 cache rows, ds_moe_decoder.c:45-53). */
+int ds_cuda_decoder_load_kv(ds_cuda_ctx_t *ctx, int model, int layer, int pos0, int n, const float *k,
+                            const float *v);
+/* kv_cache_len: the position the next token is written at. */
+int ds_cuda_decoder_set_len(ds_cuda_ctx_t *ctx, int model, int kv_len);
+int ds_cuda_decoder_get_len(ds_cuda_ctx_t *ctx, int model);
+/* ds_decoder_forward: one step on input_embed [hidden]; returns the greedy
+ * token. final_x (optional) receives the final RMS-normed hidden state,
+ * logit (optional) the winning logit. Advances kv_cache_len by one. */
+int ds_cuda_decoder_forward(ds_cuda_ctx_t *ctx, int model, const float *input_embed, float *final_x,
+                            float *logit);
+/* n_steps greedy steps without host round trips: step 0 consumes
+ * first_embed (NULL: the embedding of the previous step's token), each
+ * next step the embedding row of the previous token. tokens[n_steps]. */
+int ds_cuda_decoder_generate(ds_cuda_ctx_t *ctx, int model, const float *first_embed, int n_steps,
+                             int *tokens);
+/* Enqueue n_steps greedy steps on `stream` from the device-resident state
+ * (no host copies; for timing). */
+int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *ctx, int model, int n_steps, void *stream);
+/* Kernel launches one decode step issues. */
+int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *ctx, int model);
 
 /* ---------------------------------------------------------------------
  * Host-side synthetic data (seeded, counter-based: value i of a stream

@@ -1,0 +1,115 @@
+"""Parity of the full CUDA decode step (through the C ABI) with the CPU
+oracle: greedy tokens bit-exact where the top logit gap exceeds 1e-4, final
+hidden state within 1e-3 relative L2; small and full-size (12-layer)
+models, BF16 and INT8 experts, host-driven and device-looped decoding."""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import rel_l2
+from ds_ocr_b200 import synth
+from ds_ocr_b200.decoder import Decoder, quantize_int8
+
+pytestmark = pytest.mark.gpu
+
+
+def logit_gap(orc, model, fx):
+    y = np.empty(model.d.vocab, np.float32)
+    orc.orc_matvec_bf16(y.ctypes.data, fx.ctypes.data, model.lm_head.ctypes.data, model.d.hidden, model.d.vocab)
+    t = np.sort(y)[-2:]
+    return t[1] - t[0]
+
+
+def run_pair(cuda_ctx, orc, model, n_prefix, n_steps, kv_max=1024, use_int8=False, tol=1e-3):
+    dec = Decoder(model, cuda_ctx, kv_max=kv_max, use_int8=use_int8)
+    ora = O.OracleDecoder(model, kv_max=kv_max)
+    ks, vs = synth.kv_prefix(model.d, n_prefix)
+    dec.load_kv(ks, vs)
+    ora.load_kv(ks, vs)
+    e = model.embed(7)
+    compared = 0
+    try:
+        for s in range(n_steps):
+            tok, fx, lg = dec.forward(e, want_x=True)
+            otok, ofx, olg = ora.step(e, use_int8=use_int8)
+            assert rel_l2(fx, ofx) < tol, f"step {s}"
+            if logit_gap(orc, model, ofx) > 1e-4:
+                assert tok == otok, f"step {s}"
+                compared += 1
+            e = model.embed(otok)  # follow the oracle's path
+        assert dec.length == n_prefix + n_steps
+    finally:
+        dec.close()
+    return compared
+
+
+@pytest.fixture(scope="module")
+def small_model():
+    return synth.Model(n_layers=3, vocab=8192)
+
+
+def test_decoder_small(cuda_ctx, orc, small_model):
+    assert run_pair(cuda_ctx, orc, small_model, n_prefix=37, n_steps=6, kv_max=256) >= 4
+
+
+def test_decoder_empty_prefix(cuda_ctx, orc, small_model):
+    # first token of a sequence: attention over a single key
+    assert run_pair(cuda_ctx, orc, small_model, n_prefix=0, n_steps=3, kv_max=64) >= 0
+
+
+def test_decoder_long_context(cuda_ctx, orc, small_model):
+    # near the per-CTA key capacity of the cluster attention
+    run_pair(cuda_ctx, orc, small_model, n_prefix=3000, n_steps=2, kv_max=4096)
+
+
+def test_decoder_simulate_bf16(cuda_ctx, orc, small_model):
+    cuda_ctx.set_numerics(simulate_bf16=1)
+    try:
+        dec = Decoder(small_model, cuda_ctx, kv_max=128)
+        ora = O.OracleDecoder(small_model, kv_max=128, simulate=1)
+        ks, vs = synth.kv_prefix(small_model.d, 20)
+        dec.load_kv(ks, vs)
+        ora.load_kv(ks, vs)
+        e = small_model.embed(3)
+        tok, fx, _ = dec.forward(e, want_x=True)
+        otok, ofx, _ = ora.step(e)
+        assert rel_l2(fx, ofx) < 5e-3
+        dec.close()
+    finally:
+        cuda_ctx.set_numerics(0, 0)
+
+
+def test_generate_matches_stepwise(cuda_ctx, small_model):
+    dec = Decoder(small_model, cuda_ctx, kv_max=256)
+    ks, vs = synth.kv_prefix(small_model.d, 30)
+    dec.load_kv(ks, vs)
+    e = small_model.embed(5)
+    toks = dec.generate(8, first_embed=e)
+    dec.load_kv(ks, vs)
+    seq = []
+    for _ in range(8):
+        t = dec.forward(e)
+        seq.append(t)
+        e = small_model.embed(t)
+    dec.close()
+    assert list(toks) == seq
+
+
+def test_decoder_int8(cuda_ctx, orc, small_model):
+    quantize_int8(small_model, cuda_ctx)
+    try:
+        run_pair(cuda_ctx, orc, small_model, n_prefix=25, n_steps=3, kv_max=128, use_int8=True)
+    finally:
+        for lw in small_model.layers:
+            if lw.moe is not None:
+                lw.moe.int8 = None
+
+
+@pytest.fixture(scope="module")
+def full_model():
+    return synth.Model()  # 12 layers, vocab 129280: the benchmark model
+
+
+def test_decoder_full_size(cuda_ctx, orc, full_model):
+    # the benchmark configuration: 662-token BF16 KV prefix
+    assert run_pair(cuda_ctx, orc, full_model, n_prefix=662, n_steps=3, kv_max=1024) >= 2

@@ -112,22 +112,35 @@ constexpr int ATT_CL = 8;
 constexpr int ATT_MAXK = 4096;
 constexpr int ATT_HD = 128;
 
-__device__ __forceinline__ void load_row16(const uint16_t *hi, const uint16_t *lo, bool use_lo, float f[16]) {
-    uint4 h0 = ldg_stream(hi), h1 = ldg_stream(hi + 8);
-    uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+constexpr int ATT_KPG = 4;  // keys per 8-lane group per load batch
+
+// 16 consecutive head-dim elements of one KV row: hi plane and (optional) lo plane.
+struct Row16 {
+    uint4 h0, h1, l0, l1;
+};
+
+__device__ __forceinline__ Row16 load_raw16(const uint16_t *hi, const uint16_t *lo, bool use_lo) {
+    Row16 r;
+    r.h0 = ldg_stream(hi);
+    r.h1 = ldg_stream(hi + 8);
+    if (use_lo) {
+        r.l0 = ldg_stream(lo);
+        r.l1 = ldg_stream(lo + 8);
+    } else {
+        r.l0 = make_uint4(0, 0, 0, 0);
+        r.l1 = r.l0;
+    }
+    return r;
+}
+
+// hi + lo widened to F32 (lo is zero for exact-BF16 rows, and x + 0 == x).
+__device__ __forceinline__ void raw_to_f32(const Row16 &r, float f[16]) {
+    uint32_t hw[8] = {r.h0.x, r.h0.y, r.h0.z, r.h0.w, r.h1.x, r.h1.y, r.h1.z, r.h1.w};
+    uint32_t lw[8] = {r.l0.x, r.l0.y, r.l0.z, r.l0.w, r.l1.x, r.l1.y, r.l1.z, r.l1.w};
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        f[2 * i] = bf16_lo(hw[i]);
-        f[2 * i + 1] = bf16_hi(hw[i]);
-    }
-    if (use_lo) {
-        uint4 l0 = ldg_stream(lo), l1 = ldg_stream(lo + 8);
-        uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            f[2 * i] = __fadd_rn(f[2 * i], bf16_lo(lw[i]));
-            f[2 * i + 1] = __fadd_rn(f[2 * i + 1], bf16_hi(lw[i]));
-        }
+        f[2 * i] = __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i]));
+        f[2 * i + 1] = __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i]));
     }
 }
 
@@ -219,20 +232,41 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
             qf[4 * i] = v.x; qf[4 * i + 1] = v.y; qf[4 * i + 2] = v.z; qf[4 * i + 3] = v.w;
         }
     }
-    // 1. scores of this CTA's keys: 8 lanes per key, 32 keys per pass
-    for (int jb = j0; jb < j1; jb += 32) {
-        int j = jb + g;
-        float s = 0.f;
-        if (j < j1) {
+    // 1. scores of this CTA's keys: 8 lanes per key, ATT_KPG keys per lane
+    //    group per block (all their K loads in flight together); the first
+    //    block's V rows are loaded alongside and kept in registers for step 5
+    Row16 vraw[ATT_KPG];
+    for (int jb = j0, blk = 0; jb < j1; jb += 32 * ATT_KPG, blk++) {
+        Row16 kraw[ATT_KPG];
+#pragma unroll
+        for (int r = 0; r < ATT_KPG; r++) {
+            int j = jb + g + 32 * r;
+            kraw[r] = j < j1 ? load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16,
+                                          j >= a.lo_start)
+                             : Row16{};
+        }
+        if (blk == 0) {
+#pragma unroll
+            for (int r = 0; r < ATT_KPG; r++) {
+                int j = jb + g + 32 * r;
+                vraw[r] = j < j1 ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
+                                              j >= a.lo_start)
+                                 : Row16{};
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < ATT_KPG; r++) {
+            int j = jb + g + 32 * r;
             float kf[16];
-            load_row16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16, j >= a.lo_start, kf);
+            raw_to_f32(kraw[r], kf);
+            float s = 0.f;
 #pragma unroll
             for (int i = 0; i < 16; i++) s = __fmaf_rn(qf[i], kf[i], s);
+            s += __shfl_xor_sync(DS_FULL, s, 1);
+            s += __shfl_xor_sync(DS_FULL, s, 2);
+            s += __shfl_xor_sync(DS_FULL, s, 4);
+            if (li == 0 && j < j1) sc_own[j - j0] = __fmul_rn(s, a.scale);
         }
-        s += __shfl_xor_sync(DS_FULL, s, 1);
-        s += __shfl_xor_sync(DS_FULL, s, 2);
-        s += __shfl_xor_sync(DS_FULL, s, 4);
-        if (li == 0 && j < j1) sc_own[j - j0] = __fmul_rn(s, a.scale);
     }
     cluster.sync();
     // 2. gather every key's score of this head
@@ -276,14 +310,26 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
     float acc[16];
 #pragma unroll
     for (int i = 0; i < 16; i++) acc[i] = 0.f;
-    for (int jb = j0; jb < j1; jb += 32) {
-        int j = jb + g;
-        if (j < j1) {
-            float vf[16];
-            load_row16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16, j >= a.lo_start, vf);
-            float w = wts[j];
+    for (int jb = j0, blk = 0; jb < j1; jb += 32 * ATT_KPG, blk++) {
+        Row16 vr[ATT_KPG];
 #pragma unroll
-            for (int i = 0; i < 16; i++) acc[i] = __fmaf_rn(w, vf[i], acc[i]);
+        for (int r = 0; r < ATT_KPG; r++) {
+            int j = jb + g + 32 * r;
+            if (blk == 0) vr[r] = vraw[r];
+            else vr[r] = j < j1 ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
+                                             j >= a.lo_start)
+                                : Row16{};
+        }
+#pragma unroll
+        for (int r = 0; r < ATT_KPG; r++) {
+            int j = jb + g + 32 * r;
+            if (j < j1) {
+                float vf[16];
+                raw_to_f32(vr[r], vf);
+                float w = wts[j];
+#pragma unroll
+                for (int i = 0; i < 16; i++) acc[i] = __fmaf_rn(w, vf[i], acc[i]);
+            }
         }
     }
 #pragma unroll

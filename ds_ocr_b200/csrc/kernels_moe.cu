@@ -77,13 +77,11 @@ __device__ void router_select(const float *scores, int E, int top_k, int renorm,
     mx = warp_max(mx);
     for (int e = lane; e < E; e += 32) p[e] = fast_expf(__fsub_rn(scores[e], mx));
     __syncwarp();
-    float inv = 0.f;
-    if (lane == 0) {
-        float sum = 0.f;
-        for (int e = 0; e < E; e++) sum = __fadd_rn(sum, p[e]);
-        inv = __fdiv_rn(1.0f, sum);
-    }
-    inv = __shfl_sync(DS_FULL, inv, 0);
+    // sum of exponentials: per-lane partials, then a fixed shuffle tree (the
+    // reference sums sequentially; the difference is a few ulp of the sum)
+    float part = 0.f;
+    for (int e = lane; e < E; e += 32) part = __fadd_rn(part, p[e]);
+    const float inv = __fdiv_rn(1.0f, warp_sum(part));
     for (int e = lane; e < E; e += 32) p[e] = __fmul_rn(p[e], inv);
     __syncwarp();
     unsigned long long taken[4] = {0, 0, 0, 0};  // E <= 256

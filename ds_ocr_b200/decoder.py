@@ -97,6 +97,9 @@ class Decoder:
                                  "decoder_create")
 
     def load_kv(self, ks, vs, pos0=0):
+        if ks[0].shape[0] == 0:
+            self.set_len(pos0)
+            return
         for l, (k, v) in enumerate(zip(ks, vs)):
             k = np.ascontiguousarray(k, np.float32)
             v = np.ascontiguousarray(v, np.float32)

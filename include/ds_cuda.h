@@ -182,6 +182,27 @@ int ds_cuda_moe_layer_dev(ds_cuda_ctx_t *ctx, const float *d_x, float *d_out,
                           int shared_inter, int n_experts, int top_k, int *d_top_idx, float *d_top_w,
                           void *stream);
 
+/* ds_cuda_moe_experts_noalloc — no counterpart in the reference.
+ * The routed-expert chain of ds_cuda_moe_experts (output = sum_k
+ * top_weights[k] * expert_k(x), no shared expert) for callers that cannot
+ * allocate device memory at the point of the call, e.g. a plugin handed
+ * device buffers by its host framework, or a process whose device memory is
+ * fixed after start-up. It creates no context and allocates nothing: x,
+ * the weights and output are DEVICE pointers the caller owns (gate-up and
+ * down are host arrays of top_k device pointers; top_weights is a host
+ * array), and the SwiGLU activations live in a static 64 KB device array
+ * the library holds on every GPU that loads it until the process exits.
+ * Limits: top_k <= 8, hidden and inter multiples of 8 and <= 2048,
+ * top_k * inter <= 16384; larger sizes return DS_CUDA_EINVAL with a message
+ * on stderr. Work is enqueued on `stream` (NULL = the legacy default stream)
+ * of the current device. The first call on a device looks up the array's
+ * device address; make that first call before any stream capture. All
+ * calls share the one array, so calls that overlap on the GPU (different
+ * streams, or different host threads) race; serialise them. */
+int ds_cuda_moe_experts_noalloc(const float *d_x, const uint16_t *const *d_gate_up,
+                                const uint16_t *const *d_down, const float *top_weights, int top_k,
+                                int hidden, int inter, float *d_output, void *stream);
+
 /* ---------------------------------------------------------------------
  * Decoder — the single-token greedy decode step of ds_decoder_forward
  * (ds_moe_decoder.c:911-1264, decoder_layer_forward :339-474) on the GPU,

@@ -13,6 +13,10 @@ cudaError_t launch_ex(const void *func, dim3 grid, dim3 block, size_t smem, cuda
 cudaError_t launch_argmax_bf16(const uint16_t *W, const float *x, int rows, int n, unsigned long long *slot,
                                unsigned *ticket, int *tok, float *val, cudaStream_t st, bool pdl,
                                const float *norm_w = nullptr, float eps = 0.f);
+bool st_stages_ok(int n);
+cudaError_t launch_argmax_tma(const uint16_t *W, const float *x, int rows, int n, unsigned long long *slot,
+                              unsigned *ticket, int *tok, float *val, cudaStream_t st, bool pdl, const float *norm_w,
+                              float eps, unsigned *err);
 cudaError_t launch_router(const uint16_t *Wr, const float *x, int E, int n, float *scores, unsigned *ticket,
                           int top_k, int renorm, int *d_idx, float *d_wt, cudaStream_t st, bool pdl,
                           const float *norm_w = nullptr, float eps = 0.f);

@@ -302,7 +302,7 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     ctx = cuda.Context(local if world > 1 else 0)
     kv_max = 1024
-    dec = Decoder(model, ctx, kv_max=kv_max)
+    dec = Decoder(model, ctx, kv_max=kv_max, engine=args.engine)
     dec.load_kv(ks, vs)
     st = torch.cuda.ExternalStream(ctx.stream)
     e0 = model.embed(1)
@@ -370,7 +370,9 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
         "metric": "decode tokens/s (greedy, batch 1 per GPU, 12-layer DeepSeek3B-MoE, 662-token KV prefix)",
         "unit": "tokens/s", "dtype": "bf16 weights + bf16 KV, f32 math",
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 1280 * 4, "d2h_bytes_per_step": 8},
-        "gpu_launches": launches * args.steps, "config": decode_config(kv_max),
+        # persistent engine: the timed region is ONE kernel launch for all steps
+        "gpu_launches": launches * args.steps if launches else 1,
+        "config": dict(decode_config(kv_max), engine=["persistent kernel", "kernel graph"][args.engine]),
         "roofline": {"bound": "hbm", "achieved": lm_ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": lm_ach / pk["hbm_gbs"], "traffic": None,
                      "kernel": "argmax_bf16_kernel (LM head 129280x1280, 330,956,800 B/launch)",
@@ -412,6 +414,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer"])
+    ap.add_argument("--engine", type=int, default=0, choices=[0, 1],
+                    help="decode engine: 0 persistent kernel, 1 CUDA graph of per-phase kernels")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -134,6 +134,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     if (err) atomicExch(err, 1u);
     return false;
 }
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Global -> shared bulk copy completing on `bar` (dst, src 16-byte aligned,
 // bytes a multiple of 16).
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

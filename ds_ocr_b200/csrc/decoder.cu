@@ -8,6 +8,7 @@
 
 #include "ctx.h"
 #include "kernels_decode.cuh"
+#include "mega.h"
 
 using namespace ds;
 
@@ -36,6 +37,15 @@ struct DecoderModel {
     std::vector<int> lo_start;  // per layer: rows below are exact BF16
     int host_len = 0;
     cudaGraphExec_t graph = nullptr, graph_final = nullptr;
+    // persistent-kernel engine (mega.cu)
+    bool mega = false;
+    bool mega_dirty = true;     // parameter block must be re-uploaded
+    bool xa_staged = false;     // the host staged the next step's input embedding in xa
+    int mega_grid = 0;
+    MegaParams *mega_dp = nullptr;
+    MegaLayer *mega_dl = nullptr;
+    float *att_sc = nullptr, *att_part = nullptr, *att_sum = nullptr;
+    unsigned *bar = nullptr;
     bool pdl = true;
     int launches = 0;
     std::vector<void *> allocs;
@@ -49,6 +59,7 @@ struct DecoderModel {
 };
 
 static void drop_graphs(DecoderModel *m) {
+    m->mega_dirty = true;
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->graph_final) cudaGraphExecDestroy(m->graph_final);
     m->graph = m->graph_final = nullptr;
@@ -249,6 +260,105 @@ static int ensure_graph(ds_cuda_ctx *c, DecoderModel *m, bool with_final) {
 }
 
 // ---------------------------------------------------------------------------
+// Persistent-kernel engine: parameter block upload and launch
+// ---------------------------------------------------------------------------
+static MegaParams mega_params(ds_cuda_ctx *c, DecoderModel *m) {
+    const auto &g = m->cfg;
+    MegaParams p = {};
+    p.H = g.hidden;
+    p.NH = g.n_heads;
+    p.HD = g.head_dim;
+    p.D = g.dense_inter;
+    p.I = g.moe_inter;
+    p.E = g.n_experts;
+    p.S = g.n_shared * g.moe_inter;
+    p.K = g.top_k;
+    p.V = g.vocab;
+    p.L = g.n_layers;
+    p.kv_max = g.kv_max;
+    p.eps = g.rms_eps;
+    p.scale = 1.0f / sqrtf((float)g.head_dim);
+    p.simulate = c->simulate;
+    p.renorm = c->renorm;
+    p.layers = m->mega_dl;
+    p.final_norm = m->final_norm;
+    p.lm_head = m->lm_head;
+    p.cos_t = m->cos_t;
+    p.sin_t = m->sin_t;
+    p.xa = m->xa;
+    p.xb = m->xb;
+    p.q = m->q;
+    p.att_sc = m->att_sc;
+    p.att_part = m->att_part;
+    p.att_sum = m->att_sum;
+    p.h = m->h;
+    p.rscore = m->scores;
+    p.slot = m->slot;
+    p.bar = m->bar;
+    p.pos = m->pos;
+    p.tok = m->tok;
+    p.tok_log = m->tok_log;
+    p.val = m->val;
+    return p;
+}
+
+// Enqueues n_steps greedy steps as one persistent-kernel launch.
+static int mega_run(ds_cuda_ctx *c, DecoderModel *m, int n_steps, bool first_from_token, float *final_x,
+                    cudaStream_t st) {
+    if (m->mega_dirty) {
+        std::vector<MegaLayer> hl(m->cfg.n_layers);
+        for (int l = 0; l < m->cfg.n_layers; l++) {
+            const DecLayer &L = m->layers[l];
+            MegaLayer &d = hl[l];
+            d.wq = L.wq;
+            d.wk = L.wk;
+            d.wv = L.wv;
+            d.wo = L.wo;
+            d.in_norm = L.in_norm;
+            d.post_norm = L.post_norm;
+            d.dense = L.dense;
+            d.dgate = L.dgate;
+            d.dup = L.dup;
+            d.ddown = L.ddown;
+            d.router = L.router;
+            d.block = L.block;
+            d.down = L.down;
+            d.sdown = L.sdown;
+            d.k_hi = m->plane(0, l);
+            d.k_lo = m->plane(1, l);
+            d.v_hi = m->plane(2, l);
+            d.v_lo = m->plane(3, l);
+            d.lo_start = m->lo_start[l];
+        }
+        CKL(cudaMemcpyAsync(m->mega_dl, hl.data(), hl.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice, st),
+            "mega layers upload");
+        CKL(cudaStreamSynchronize(st), "mega layers upload");
+        m->mega_dirty = false;
+    }
+    // the per-launch fields travel in a fresh parameter block each launch
+    // (stream-ordered copy from pinned staging)
+    MegaParams p = mega_params(c, m);
+    p.n_steps = n_steps;
+    p.first_from_token = first_from_token ? 1 : 0;
+    p.final_x = final_x;
+    CK(ctx_pinned(c, sizeof(MegaParams) + 64));
+    CKL(cudaStreamSynchronize(st), "mega params staging");  // the staging buffer may be in use
+    memcpy(c->pin, &p, sizeof p);
+    CKL(cudaMemcpyAsync(m->mega_dp, c->pin, sizeof p, cudaMemcpyHostToDevice, st), "mega params upload");
+    CKL(cudaMemsetAsync(m->slot, 0, 2 * sizeof(unsigned long long), st), "slot reset");
+    CKL(cudaMemsetAsync(m->bar, 0, 3 * sizeof(unsigned), st), "barrier reset");
+    CKL(launch_mega(m->mega_dp, m->mega_grid, st), "persistent decode launch");
+    return DS_CUDA_OK;
+}
+
+static int mega_check(ds_cuda_ctx *c, DecoderModel *m) {
+    unsigned e = 0;
+    CKL(cudaMemcpy(&e, m->bar + 2, sizeof e, cudaMemcpyDeviceToHost), "error flag read");
+    if (e) return ctx_fail(c, DS_CUDA_ETIMEOUT, "persistent decode: a bounded device-side wait gave up");
+    return DS_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
 #define LOOK(ptr, bytes) ctx_lookup(c, (ptr), (bytes), true)
@@ -354,6 +464,27 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
         cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
         m->lo_start.assign(g.n_layers, 0);
     }
+    if (rc == DS_CUDA_OK && g.engine == 0) {
+        // the persistent kernel is specialised for hidden = heads*head_dim =
+        // 1280 (5 x 256-column register slices) and BF16 experts
+        int G = mega_grid(c->device);
+        int S = g.n_shared * g.moe_inter;
+        bool fits = G >= g.n_heads && ((S + G - 1) / G) * 4 * g.hidden + ((g.n_experts + G - 1) / G) * 2 * g.hidden <= 92 * 1024;
+        if (g.use_int8 || g.hidden != 1280 || g.n_heads * g.head_dim != 1280 || g.top_k > 8 ||
+            g.top_k * g.moe_inter + S > 8192 || g.dense_inter > 8192 || !fits) {
+            rc = ctx_fail(c, DS_CUDA_EINVAL, "decoder_create: configuration not supported by the persistent engine "
+                                             "(use engine = 1)");
+        } else {
+            m->mega = true;
+            m->mega_grid = G;
+            rc = dalloc(c, m, &m->att_sc, (size_t)g.n_heads * g.kv_max);
+            if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->att_part, (size_t)g.n_heads * G * g.head_dim);
+            if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->att_sum, 64);
+            if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->bar, 16);
+            if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->mega_dl, (size_t)g.n_layers);
+            if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->mega_dp, 1);
+        }
+    }
     if (rc != DS_CUDA_OK) {
         free_model(m);
         return rc;
@@ -450,16 +581,21 @@ extern "C" int ds_cuda_decoder_forward(ds_cuda_ctx_t *c, int id, const float *em
     if (m->host_len + 1 > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_forward: KV cache full");
     cudaSetDevice(c->device);
     const int H = m->cfg.hidden;
-    CK(ensure_graph(c, m, final_x != nullptr));
-    CK(ctx_pinned(c, (size_t)H * 8 + 64));
+    if (!m->mega) CK(ensure_graph(c, m, final_x != nullptr));
+    CK(ctx_pinned(c, (size_t)H * 8 + 64 + sizeof(MegaParams)));
     memcpy(c->pin, embed, (size_t)H * 4);
     CKL(cudaMemcpyAsync(m->xa, c->pin, (size_t)H * 4, cudaMemcpyHostToDevice, c->stream), "embed copy");
-    CKL(cudaGraphLaunch(final_x ? m->graph_final : m->graph, c->stream), "graph launch");
+    if (m->mega) {
+        CK(mega_run(c, m, 1, false, final_x ? m->xfinal : nullptr, c->stream));
+    } else {
+        CKL(cudaGraphLaunch(final_x ? m->graph_final : m->graph, c->stream), "graph launch");
+    }
     char *pb = (char *)c->pin;
     CKL(cudaMemcpyAsync(pb, m->tok, 4, cudaMemcpyDeviceToHost, c->stream), "token copy");
     CKL(cudaMemcpyAsync(pb + 4, m->val, 4, cudaMemcpyDeviceToHost, c->stream), "logit copy");
     if (final_x) CKL(cudaMemcpyAsync(pb + 64, m->xfinal, (size_t)H * 4, cudaMemcpyDeviceToHost, c->stream), "x copy");
     CKL(cudaStreamSynchronize(c->stream), "decoder_forward");
+    if (m->mega) CK(mega_check(c, m));
     int tok;
     memcpy(&tok, pb, 4);
     if (logit) memcpy(logit, pb + 4, 4);
@@ -473,9 +609,17 @@ extern "C" int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *c, int id, int n_step
     if (!m || n_steps < 0) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_generate_dev: bad argument");
     if (m->host_len + n_steps > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_generate: KV cache full");
     cudaSetDevice(c->device);
-    CK(ensure_graph(c, m, false));
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
-    for (int s = 0; s < n_steps; s++) CKL(cudaGraphLaunch(m->graph, st), "graph launch");
+    if (n_steps == 0) return DS_CUDA_OK;
+    if (m->mega) {
+        // step 0 consumes the embedding of the last token the model produced
+        // (or the one ds_cuda_decoder_generate staged in xa)
+        CK(mega_run(c, m, n_steps, !m->xa_staged, nullptr, st));
+        m->xa_staged = false;
+    } else {
+        CK(ensure_graph(c, m, false));
+        for (int s = 0; s < n_steps; s++) CKL(cudaGraphLaunch(m->graph, st), "graph launch");
+    }
     m->host_len += n_steps;
     return DS_CUDA_OK;
 }
@@ -491,17 +635,20 @@ extern "C" int ds_cuda_decoder_generate(ds_cuda_ctx_t *c, int id, const float *f
         CK(ctx_pinned(c, (size_t)H * 4));
         memcpy(c->pin, first_embed, (size_t)H * 4);
         CKL(cudaMemcpyAsync(m->xa, c->pin, (size_t)H * 4, cudaMemcpyHostToDevice, c->stream), "embed copy");
+        m->xa_staged = true;
     }
     CK(ds_cuda_decoder_generate_dev(c, id, n_steps, nullptr));
     CKL(cudaMemcpyAsync(tokens, m->tok_log + start, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, c->stream),
         "token copy");
     CKL(cudaStreamSynchronize(c->stream), "decoder_generate");
+    if (m->mega) CK(mega_check(c, m));
     return DS_CUDA_OK;
 }
 
 extern "C" int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *c, int id) {
     DecoderModel *m = c ? get_model(c, id) : nullptr;
     if (!m) return ctx_fail(c, DS_CUDA_EINVAL, "unknown model");
+    if (m->mega) return 0;  // the persistent engine: one launch per generate call, whatever n_steps
     if (!m->launches) CK(ensure_graph(c, m, false));
     return m->launches;
 }

@@ -228,4 +228,56 @@ __device__ __forceinline__ float row_dot_i8(const int8_t *row, int n, const XReg
     return acc;
 }
 
+// ---------------------------------------------------------------------------
+// Router: scores = W_r x (ds_moe_router_bf16, ds_kernels.c:187-191), then the
+// last CTA runs the softmax over all experts with fast exp and the k strict-'>'
+// selection passes of ds_moe_decoder.c:157-183 (raw probabilities unless
+// renorm).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void router_select(const float *scores, int E, int top_k, int renorm, int *d_idx, float *d_wt) {
+    // called by warp 0 of one CTA
+    __shared__ float p[256];
+    const int lane = threadIdx.x & 31;
+    float mx = -1e30f;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, scores[e]);
+    mx = warp_max(mx);
+    for (int e = lane; e < E; e += 32) p[e] = fast_expf(__fsub_rn(scores[e], mx));
+    __syncwarp();
+    // sum of exponentials: per-lane partials, then a fixed shuffle tree (the
+    // reference sums sequentially; the difference is a few ulp of the sum)
+    float part = 0.f;
+    for (int e = lane; e < E; e += 32) part = __fadd_rn(part, p[e]);
+    const float inv = __fdiv_rn(1.0f, warp_sum(part));
+    for (int e = lane; e < E; e += 32) p[e] = __fmul_rn(p[e], inv);
+    __syncwarp();
+    unsigned long long taken[4] = {0, 0, 0, 0};  // E <= 256
+    float wsum = 0.f;
+    float wk[8];
+    int ik[8];
+    for (int k = 0; k < top_k; k++) {
+        float bv = -1e30f;
+        int bidx = 0x7fffffff;
+        for (int e = lane; e < E; e += 32) {
+            bool t = (taken[e >> 6] >> (e & 63)) & 1ull;
+            if (!t && p[e] > bv) { bv = p[e]; bidx = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(DS_FULL, bv, o);
+            int oi = __shfl_xor_sync(DS_FULL, bidx, o);
+            if (ov > bv || (ov == bv && oi < bidx)) { bv = ov; bidx = oi; }
+        }
+        taken[bidx >> 6] |= 1ull << (bidx & 63);
+        wk[k] = bv;
+        ik[k] = bidx;
+        wsum = __fadd_rn(wsum, bv);
+    }
+    if (lane == 0) {
+        for (int k = 0; k < top_k; k++) {
+            d_idx[k] = ik[k];
+            d_wt[k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
+        }
+    }
+}
+
 }  // namespace ds

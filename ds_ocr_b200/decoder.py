@@ -18,7 +18,7 @@ class DecoderConfig(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("hidden", "n_layers", "n_heads", "head_dim", "dense_inter", "moe_inter",
                                             "n_experts", "n_shared", "top_k", "vocab", "first_dense")] + \
                [("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("kv_max", ctypes.c_int),
-                ("use_int8", ctypes.c_int)]
+                ("use_int8", ctypes.c_int), ("engine", ctypes.c_int)]
 
 
 _LW_FIELDS = ("wq", "wk", "wv", "wo", "input_norm", "post_attn_norm", "dense_gate", "dense_up", "dense_down",
@@ -73,14 +73,16 @@ def quantize_int8(model, ctx=None):
 
 
 class Decoder:
-    def __init__(self, model, ctx=None, kv_max=1024, use_int8=False):
+    ENGINE_PERSISTENT, ENGINE_GRAPH = 0, 1
+
+    def __init__(self, model, ctx=None, kv_max=1024, use_int8=False, engine=0):
         self.ctx = ctx or Context(0)
         self.lib = self.ctx.lib
         self.model = model
         d = model.d
         self.cfg = DecoderConfig(d.hidden, d.n_layers, d.n_heads, d.head_dim, d.dense_inter, d.moe_inter,
                                  d.n_experts, d.n_shared, d.top_k, d.vocab, d.first_dense, synth.RMS_EPS,
-                                 synth.ROPE_THETA, kv_max, int(use_int8))
+                                 synth.ROPE_THETA, kv_max, int(use_int8), int(engine))
         self._layers = (LayerWeightsC * d.n_layers)(*[layer_struct(lw) for lw in model.layers])
         self.ctx._pin(*[getattr(lw, n) for lw in model.layers for n in ("wq", "wk", "wv", "wo", "input_norm",
                                                                         "post_norm", "dense_gate", "dense_up",

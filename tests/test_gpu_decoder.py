@@ -20,8 +20,8 @@ def logit_gap(orc, model, fx):
     return t[1] - t[0]
 
 
-def run_pair(cuda_ctx, orc, model, n_prefix, n_steps, kv_max=1024, use_int8=False, tol=1e-3):
-    dec = Decoder(model, cuda_ctx, kv_max=kv_max, use_int8=use_int8)
+def run_pair(cuda_ctx, orc, model, n_prefix, n_steps, kv_max=1024, use_int8=False, tol=1e-3, engine=0):
+    dec = Decoder(model, cuda_ctx, kv_max=kv_max, use_int8=use_int8, engine=engine)
     ora = O.OracleDecoder(model, kv_max=kv_max)
     ks, vs = synth.kv_prefix(model.d, n_prefix)
     dec.load_kv(ks, vs)
@@ -48,24 +48,31 @@ def small_model():
     return synth.Model(n_layers=3, vocab=8192)
 
 
-def test_decoder_small(cuda_ctx, orc, small_model):
-    assert run_pair(cuda_ctx, orc, small_model, n_prefix=37, n_steps=6, kv_max=256) >= 4
+ENGINES = pytest.mark.parametrize("engine", [0, 1], ids=["persistent", "graph"])
 
 
-def test_decoder_empty_prefix(cuda_ctx, orc, small_model):
+@ENGINES
+def test_decoder_small(cuda_ctx, orc, small_model, engine):
+    assert run_pair(cuda_ctx, orc, small_model, n_prefix=37, n_steps=6, kv_max=256, engine=engine) >= 4
+
+
+@ENGINES
+def test_decoder_empty_prefix(cuda_ctx, orc, small_model, engine):
     # first token of a sequence: attention over a single key
-    assert run_pair(cuda_ctx, orc, small_model, n_prefix=0, n_steps=3, kv_max=64) >= 0
+    assert run_pair(cuda_ctx, orc, small_model, n_prefix=0, n_steps=3, kv_max=64, engine=engine) >= 0
 
 
-def test_decoder_long_context(cuda_ctx, orc, small_model):
-    # near the per-CTA key capacity of the cluster attention
-    run_pair(cuda_ctx, orc, small_model, n_prefix=3000, n_steps=2, kv_max=4096)
+@ENGINES
+def test_decoder_long_context(cuda_ctx, orc, small_model, engine):
+    # long context: many keys per CTA
+    run_pair(cuda_ctx, orc, small_model, n_prefix=3000, n_steps=2, kv_max=4096, engine=engine)
 
 
-def test_decoder_simulate_bf16(cuda_ctx, orc, small_model):
+@ENGINES
+def test_decoder_simulate_bf16(cuda_ctx, orc, small_model, engine):
     cuda_ctx.set_numerics(simulate_bf16=1)
     try:
-        dec = Decoder(small_model, cuda_ctx, kv_max=128)
+        dec = Decoder(small_model, cuda_ctx, kv_max=128, engine=engine)
         ora = O.OracleDecoder(small_model, kv_max=128, simulate=1)
         ks, vs = synth.kv_prefix(small_model.d, 20)
         dec.load_kv(ks, vs)
@@ -79,8 +86,9 @@ def test_decoder_simulate_bf16(cuda_ctx, orc, small_model):
         cuda_ctx.set_numerics(0, 0)
 
 
-def test_generate_matches_stepwise(cuda_ctx, small_model):
-    dec = Decoder(small_model, cuda_ctx, kv_max=256)
+@ENGINES
+def test_generate_matches_stepwise(cuda_ctx, small_model, engine):
+    dec = Decoder(small_model, cuda_ctx, kv_max=256, engine=engine)
     ks, vs = synth.kv_prefix(small_model.d, 30)
     dec.load_kv(ks, vs)
     e = small_model.embed(5)
@@ -98,7 +106,7 @@ def test_generate_matches_stepwise(cuda_ctx, small_model):
 def test_decoder_int8(cuda_ctx, orc, small_model):
     quantize_int8(small_model, cuda_ctx)
     try:
-        run_pair(cuda_ctx, orc, small_model, n_prefix=25, n_steps=3, kv_max=128, use_int8=True)
+        run_pair(cuda_ctx, orc, small_model, n_prefix=25, n_steps=3, kv_max=128, use_int8=True, engine=1)
     finally:
         for lw in small_model.layers:
             if lw.moe is not None:
@@ -110,6 +118,20 @@ def full_model():
     return synth.Model()  # 12 layers, vocab 129280: the benchmark model
 
 
-def test_decoder_full_size(cuda_ctx, orc, full_model):
+@ENGINES
+def test_decoder_full_size(cuda_ctx, orc, full_model, engine):
     # the benchmark configuration: 662-token BF16 KV prefix
-    assert run_pair(cuda_ctx, orc, full_model, n_prefix=662, n_steps=3, kv_max=1024) >= 2
+    assert run_pair(cuda_ctx, orc, full_model, n_prefix=662, n_steps=3, kv_max=1024, engine=engine) >= 2
+
+
+def test_engines_agree_on_long_generation(cuda_ctx, full_model):
+    # 16 device-looped steps: the persistent kernel and the kernel graph
+    # produce the same greedy tokens
+    ks, vs = synth.kv_prefix(full_model.d, 662)
+    out = []
+    for engine in (0, 1):
+        dec = Decoder(full_model, cuda_ctx, kv_max=1024, engine=engine)
+        dec.load_kv(ks, vs)
+        out.append(list(dec.generate(16, first_embed=full_model.embed(9))))
+        dec.close()
+    assert out[0] == out[1]

@@ -46,6 +46,7 @@ struct DecoderModel {
     MegaLayer *mega_dl = nullptr;
     float *att_sc = nullptr, *att_part = nullptr, *att_sum = nullptr;
     unsigned *bar = nullptr;
+    long long *trace = nullptr;
     bool pdl = true;
     int launches = 0;
     std::vector<void *> allocs;
@@ -341,6 +342,14 @@ static int mega_run(ds_cuda_ctx *c, DecoderModel *m, int n_steps, bool first_fro
     p.n_steps = n_steps;
     p.first_from_token = first_from_token ? 1 : 0;
     p.final_x = final_x;
+    // phase timing trace for performance work (DS_CUDA_MEGA_TRACE=<file>)
+    static const char *trace_file = getenv("DS_CUDA_MEGA_TRACE");
+    if (trace_file) {
+        if (!m->trace) CK(dalloc(c, m, &m->trace, (size_t)2 * 4096 * 5));
+        CKL(cudaMemsetAsync(m->trace, 0, (size_t)2 * 4096 * 5 * 8, st), "trace reset");
+        p.trace = m->trace;
+        p.trace_cap = 4096;
+    }
     CK(ctx_pinned(c, sizeof(MegaParams) + 64));
     CKL(cudaStreamSynchronize(st), "mega params staging");  // the staging buffer may be in use
     memcpy(c->pin, &p, sizeof p);
@@ -354,6 +363,20 @@ static int mega_run(ds_cuda_ctx *c, DecoderModel *m, int n_steps, bool first_fro
 static int mega_check(ds_cuda_ctx *c, DecoderModel *m) {
     unsigned e = 0;
     CKL(cudaMemcpy(&e, m->bar + 2, sizeof e, cudaMemcpyDeviceToHost), "error flag read");
+    static const char *trace_file = getenv("DS_CUDA_MEGA_TRACE");
+    if (trace_file && m->trace) {
+        std::vector<long long> t((size_t)2 * 4096 * 5);
+        cudaMemcpy(t.data(), m->trace, t.size() * 8, cudaMemcpyDeviceToHost);
+        if (FILE *f = fopen(trace_file, "w")) {
+            for (int s = 0; s < 2; s++)
+                for (int i = 0; i < 4096; i++) {
+                    const long long *r = &t[((size_t)s * 4096 + i) * 5];
+                    if (!r[4]) continue;
+                    fprintf(f, "%d,%d,%lld,%lld,%lld,%lld,%lld\n", s, i, r[0], r[1], r[2], r[3], r[4]);
+                }
+            fclose(f);
+        }
+    }
     if (e) return ctx_fail(c, DS_CUDA_ETIMEOUT, "persistent decode: a bounded device-side wait gave up");
     return DS_CUDA_OK;
 }
@@ -469,7 +492,9 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
         // 1280 (5 x 256-column register slices) and BF16 experts
         int G = mega_grid(c->device);
         int S = g.n_shared * g.moe_inter;
-        bool fits = G >= g.n_heads && ((S + G - 1) / G) * 4 * g.hidden + ((g.n_experts + G - 1) / G) * 2 * g.hidden <= 92 * 1024;
+        // one gate/up pair plus the CTA's router rows must fit one 46 KB region
+        bool fits = G >= g.n_heads && 4 * g.hidden + ((g.n_experts + G - 1) / G) * 2 * g.hidden <= 46 * 1024 &&
+                    2 * g.dense_inter <= 46 * 1024 && 2 * (g.top_k * g.moe_inter + S) <= 46 * 1024;
         if (g.use_int8 || g.hidden != 1280 || g.n_heads * g.head_dim != 1280 || g.top_k > 8 ||
             g.top_k * g.moe_inter + S > 8192 || g.dense_inter > 8192 || !fits) {
             rc = ctx_fail(c, DS_CUDA_EINVAL, "decoder_create: configuration not supported by the persistent engine "

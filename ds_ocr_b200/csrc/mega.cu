@@ -32,10 +32,10 @@ namespace ds {
 
 constexpr int MK_THREADS = 512;
 constexpr int MK_WARPS = MK_THREADS / 32;
-constexpr int MK_REGION = 92 * 1024;  // bytes per weight region (two regions)
+constexpr int MK_NREG = 4;             // weight regions in the shared-memory ring
+constexpr int MK_REGION = 46 * 1024;  // bytes per weight region
 constexpr int MK_XS = 8192;           // floats of vector scratch (also attention scratch)
-constexpr int MK_SMEM = 2 * MK_REGION + MK_XS * 4;
-constexpr int MK_VREG = 2;            // V rows per 8-lane group kept in registers across a barrier
+constexpr int MK_SMEM = MK_NREG * MK_REGION + MK_XS * 4;
 
 enum Phase { PH_QKV, PH_ATTS, PH_ATTV, PH_OPROJ, PH_DGU, PH_DDOWN, PH_RSGU, PH_RGU, PH_MDOWN, PH_LMH, PH_END };
 
@@ -68,31 +68,26 @@ __device__ __forceinline__ uint16_t bf16_bits_rne(float f) {
 
 // Grid-wide barrier over co-resident CTAs, bounded: returns false (and sets
 // *err) if it does not complete within its poll budget or another CTA failed.
-__device__ bool grid_sync(unsigned *bar) {
+// bar[0] counts arrivals monotonically (never reset within a launch): the
+// n-th barrier completes when it reaches n * gridDim.x. One release-add per
+// CTA, then acquire polls; the error flag is checked only every 256 polls.
+__device__ bool grid_sync(unsigned *bar, unsigned &epoch) {
     __shared__ int ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        unsigned g = ld_acquire(bar + 1);
-        __threadfence();
+        epoch++;
+        const unsigned target = epoch * gridDim.x;
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(bar), "r"(1u) : "memory");
         int good = 0;
-        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
-            atomicExch(bar, 0u);
-            __threadfence();
-            atomicAdd(bar + 1, 1u);
-            good = 1;
-        } else {
-            for (uint32_t it = 0; it < (1u << 22); it++) {
-                if (ld_acquire(bar + 1) != g) {
-                    good = 1;
-                    break;
-                }
-                if (ld_acquire(bar + 2)) break;
-                __nanosleep(64);
+        for (uint32_t it = 0; it < (1u << 24); it++) {
+            if ((int)(ld_acquire(bar) - target) >= 0) {
+                good = 1;
+                break;
             }
-            if (!good) atomicExch(bar + 2, 1u);
+            if ((it & 255) == 255 && ld_acquire(bar + 2)) break;
         }
-        __threadfence();
-        ok = good && ld_acquire(bar + 2) == 0;
+        if (!good) atomicExch(bar + 2, 1u);
+        ok = good;
     }
     __syncthreads();
     return ok != 0;
@@ -194,10 +189,15 @@ __device__ Geo geometry(const MegaParams &p, int phase) {
         default: return g;
     }
     split_range(total, gridDim.x, blockIdx.x, g.a, g.b);
-    g.ipc = MK_REGION / item_bytes(p, phase);
-    if (phase == PH_RSGU) g.ipc = g.b - g.a;
-    int cnt = g.b - g.a;
-    g.nsub = cnt <= 0 ? 1 : (cnt + g.ipc - 1) / g.ipc;
+    // the same chunk count on every CTA (balanced by the largest share), so
+    // no CTA trails the others into the next barrier by a whole chunk; the
+    // router rows of PH_RSGU ride in its last chunk
+    const int G = gridDim.x;
+    const int cmax = (total + G - 1) / G;
+    const int extra = phase == PH_RSGU ? ((p.E + G - 1) / G) * 2 * p.H : 0;
+    const int cap = max(1, (MK_REGION - extra) / item_bytes(p, phase));
+    g.nsub = max(1, (cmax + cap - 1) / cap);
+    g.ipc = max(1, (cmax + g.nsub - 1) / g.nsub);
     return g;
 }
 
@@ -229,7 +229,7 @@ __device__ uint32_t chunk_bytes(const MegaParams &p, const Cur &c, int sub) {
     Geo g = geometry(p, c.phase);
     int ia = g.a + sub * g.ipc, ib = min(g.b, ia + g.ipc);
     uint32_t n = ib > ia ? (uint32_t)(ib - ia) * item_bytes(p, c.phase) : 0;
-    if (c.phase == PH_RSGU) {
+    if (c.phase == PH_RSGU && sub == g.nsub - 1) {
         int ea, eb;
         split_range(p.E, gridDim.x, blockIdx.x, ea, eb);
         n += (uint32_t)(eb - ea) * 2 * p.H;
@@ -246,7 +246,7 @@ __device__ void issue_chunk(const MegaParams &p, const Cur &c, int sub, uint8_t 
     mbar_expect_tx(bar, total);
     const MegaLayer &L = p.layers[c.layer];
     Geo g = geometry(p, c.phase);
-    const int ia = g.a + sub * g.ipc, ib = min(g.b, ia + g.ipc), cnt = ib - ia;
+    const int ia = g.a + sub * g.ipc, ib = min(g.b, ia + g.ipc), cnt = max(0, ib - ia);
     const uint32_t rb = 2 * p.H;  // hidden-length BF16 row
     switch (c.phase) {
         case PH_QKV: {
@@ -275,9 +275,11 @@ __device__ void issue_chunk(const MegaParams &p, const Cur &c, int sub, uint8_t 
                 bulk_g2s(dst, sgu + (size_t)ia * p.H, cnt * rb, bar);
                 bulk_g2s(dst + (size_t)cnt * rb, sgu + (size_t)(p.S + ia) * p.H, cnt * rb, bar);
             }
-            int ea, eb;
-            split_range(p.E, gridDim.x, blockIdx.x, ea, eb);
-            if (eb > ea) bulk_g2s(dst + (size_t)2 * cnt * rb, L.router + (size_t)ea * p.H, (eb - ea) * rb, bar);
+            if (sub == g.nsub - 1) {
+                int ea, eb;
+                split_range(p.E, gridDim.x, blockIdx.x, ea, eb);
+                if (eb > ea) bulk_g2s(dst + (size_t)2 * cnt * rb, L.router + (size_t)ea * p.H, (eb - ea) * rb, bar);
+            }
             break;
         }
         case PH_RGU: {
@@ -316,7 +318,7 @@ __device__ void issue_chunk(const MegaParams &p, const Cur &c, int sub, uint8_t 
 // True when chunk (n, nsub) may be loaded before the barrier that precedes
 // it: routed-expert chunks need the router result of their own layer, which
 // exists once the CTA is past that layer's router phase.
-__device__ __forceinline__ bool loadable_early(const Cur &cur, const Cur &nx) {
+__device__ __forceinline__ bool loadable_now(const Cur &cur, const Cur &nx) {
     if (nx.phase != PH_RGU && nx.phase != PH_MDOWN) return true;
     return cur.layer == nx.layer && cur.step == nx.step && (cur.phase == PH_RGU || cur.phase == PH_MDOWN);
 }
@@ -347,13 +349,48 @@ __device__ __forceinline__ float sdot_long(const uint16_t *row, const float *xs,
     return acc;
 }
 
+// One KV row slice (16 head-dim elements, hi and lo planes) of key j, or
+// zeros when j >= j1; L2-coherent loads (rows are written inside the launch).
+__device__ __forceinline__ void kv_row(const uint16_t *hi, const uint16_t *lo, int j, int j1, int lo_start, int hd,
+                                       int li, uint4 r[4]) {
+    r[0] = r[1] = r[2] = r[3] = make_uint4(0, 0, 0, 0);
+    if (j >= j1) return;
+    const size_t o = (size_t)j * hd + li * 16;
+    r[0] = ldcg16(hi + o);
+    r[1] = ldcg16(hi + o + 8);
+    if (j >= lo_start) {
+        r[2] = ldcg16(lo + o);
+        r[3] = ldcg16(lo + o + 8);
+    }
+}
+__device__ __forceinline__ float kv_dot(const uint4 r[4], const float qf[16]) {
+    uint32_t hw[8] = {r[0].x, r[0].y, r[0].z, r[0].w, r[1].x, r[1].y, r[1].z, r[1].w};
+    uint32_t lw[8] = {r[2].x, r[2].y, r[2].z, r[2].w, r[3].x, r[3].y, r[3].z, r[3].w};
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        s = __fmaf_rn(qf[2 * i], __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i])), s);
+        s = __fmaf_rn(qf[2 * i + 1], __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i])), s);
+    }
+    return s;
+}
+__device__ __forceinline__ void kv_axpy(const uint4 r[4], float w, float acc[16]) {
+    uint32_t hw[8] = {r[0].x, r[0].y, r[0].z, r[0].w, r[1].x, r[1].y, r[1].z, r[1].w};
+    uint32_t lw[8] = {r[2].x, r[2].y, r[2].z, r[2].w, r[3].x, r[3].y, r[3].z, r[3].w};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        acc[2 * i] = __fmaf_rn(w, __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i])), acc[2 * i]);
+        acc[2 * i + 1] = __fmaf_rn(w, __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i])), acc[2 * i + 1]);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaParams *__restrict__ pp) {
     extern __shared__ __align__(128) uint8_t smem[];
-    float *xs = reinterpret_cast<float *>(smem + 2 * MK_REGION);
-    __shared__ uint64_t full[2];
+    float *xs = reinterpret_cast<float *>(smem + MK_NREG * MK_REGION);
+    __shared__ uint64_t full[MK_NREG];
     __shared__ float buf[MK_THREADS + 1];
     __shared__ float ysm[8][8];
     __shared__ int sidx[8];
@@ -361,27 +398,34 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
     __shared__ float rsc[256];
     __shared__ int s_tok;
     __shared__ unsigned long long cta_best;
-    const MegaParams p = *pp;
+    const MegaParams &p = *pp;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned *err = p.bar + 2;
     constexpr int CPL = 5;  // hidden 1280 = 5 x 256 (checked on the host)
 
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int i = 0; i < MK_NREG; i++) mbar_init(&full[i], 1);
         mbar_fence_init();
     }
     __syncthreads();
 
     int pos = *p.pos;
+    unsigned epoch = 0;  // grid barriers passed
     int tok = 0;
     Cur cur = {0, 0, PH_QKV};
-    int chunk_id = 0;          // global chunk counter: region = chunk_id & 1
-    uint32_t uses = 0;  // completed waits, 2 bits: parity of region 0 and region 1
-    bool next_issued = false;  // thread 0: whether chunk_id+1 was issued
-
-    // first chunk's weights
-    if (tid == 0) issue_chunk(p, cur, 0, smem, &full[0], sidx);
+    int chunk_id = 0;    // chunk counter: chunk c computes from region c % MK_NREG
+    // optional timing trace: CTA 0 and the last CTA, 5 values per chunk
+    const int trace_sel = p.trace == nullptr ? -1 : (blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x - 1 ? 1 : -1));
+    long long t_bar0 = 0, t_bar1 = 0;
+#define MK_TRACE(slot, val)                                                                                    \
+    do {                                                                                                        \
+        if (trace_sel >= 0 && tid == 0 && chunk_id < p.trace_cap)                                               \
+            p.trace[((size_t)trace_sel * p.trace_cap + chunk_id) * 5 + (slot)] = (val);                         \
+    } while (0)
+    uint32_t uses = 0;  // one parity bit per region
+    // issue cursor (thread 0): the next chunk whose copies are not issued yet
+    Cur ic = cur;
+    int isub = 0, iid = 0;
     bool first = true;
 
     while (cur.phase != PH_END) {
@@ -389,8 +433,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
         const MegaLayer &L = p.layers[cur.layer];
         // ---- barrier that publishes the previous phase's outputs ----
         if (!first) {
-            if (!grid_sync(p.bar)) return;
+            t_bar0 = clock64();
+            if (!grid_sync(p.bar, epoch)) return;
+            t_bar1 = clock64();
         }
+        first = false;
         // new step: decode the previous step's token
         if (cur.phase == PH_QKV && cur.layer == 0 && (cur.step > 0 || p.first_from_token)) {
             if (tid == 0) {
@@ -418,35 +465,34 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
             __syncthreads();
         }
         for (int sub = 0; sub < geo.nsub; sub++, chunk_id++) {
-            const int r = chunk_id & 1;
+            const int r = chunk_id % MK_NREG;
             const uint32_t bytes = chunk_bytes(p, cur, sub);
-            // successor chunk (same phase next sub, or the next phase's first)
-            Cur nx = cur;
-            int nsub_next = sub + 1;
-            if (sub + 1 >= geo.nsub) {
-                next_phase(p, nx);
-                nsub_next = 0;
-            }
+            // keep up to MK_NREG chunks in flight: issue every chunk up to
+            // chunk_id + MK_NREG - 1 whose addresses are known by now (the
+            // region of chunk i was last used by chunk i - MK_NREG, done)
             if (tid == 0) {
-                if (first) {
-                    first = false;
-                } else if (!next_issued && bytes) {
-                    fence_proxy_async();
-                    issue_chunk(p, cur, sub, (smem + r * MK_REGION), &full[r], sidx);
-                }
-                next_issued = false;
-                if (nx.phase != PH_END && loadable_early(cur, nx) && chunk_bytes(p, nx, nsub_next)) {
-                    fence_proxy_async();
-                    issue_chunk(p, nx, nsub_next, (smem + (r ^ 1) * MK_REGION), &full[r ^ 1], sidx);
-                    next_issued = true;
+                while (iid <= chunk_id + MK_NREG - 1 && ic.phase != PH_END && loadable_now(cur, ic)) {
+                    const int ir = iid % MK_NREG;
+                    if (chunk_bytes(p, ic, isub)) {
+                        fence_proxy_async();
+                        issue_chunk(p, ic, isub, smem + ir * MK_REGION, &full[ir], sidx);
+                    }
+                    if (++isub >= geometry(p, ic.phase).nsub) {
+                        isub = 0;
+                        next_phase(p, ic);
+                    }
+                    iid++;
                 }
             }
-            first = false;
             if (bytes) {
                 if (!mbar_wait(&full[r], (uses >> r) & 1, err)) return;
                 uses ^= 1u << r;
             }
-            const uint16_t *W = reinterpret_cast<const uint16_t *>((smem + r * MK_REGION));
+            MK_TRACE(0, (long long)(cur.phase | (sub << 8) | (cur.layer << 16) | ((long long)cur.step << 24)));
+            MK_TRACE(1, sub == 0 ? t_bar0 : 0);
+            MK_TRACE(2, sub == 0 ? t_bar1 : 0);
+            MK_TRACE(3, clock64());
+            const uint16_t *W = reinterpret_cast<const uint16_t *>(smem + r * MK_REGION);
             const int ia = geo.a + sub * geo.ipc, ib = min(geo.b, ia + geo.ipc), cnt = max(0, ib - ia);
 
             switch (cur.phase) {
@@ -498,7 +544,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                 }
                 case PH_ATTS:
                 case PH_ATTV: {
-                    const int cph = gridDim.x / p.NH;
+                    const int cph = min(16, (int)gridDim.x / p.NH);  // CTAs per head (<= 16 partials)
                     const int h = blockIdx.x / cph, cc = blockIdx.x - h * cph;
                     if (h >= p.NH) break;
                     const int n = pos + 1;
@@ -510,32 +556,30 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                     const uint16_t *vhi = L.v_hi + hoff, *vlo = L.v_lo + hoff;
                     float *wts = xs, *corr = xs + MK_XS / 2;
                     if (cur.phase == PH_ATTS) {
+                        // this group's first key and q in one round trip
+                        uint4 kr[4];
+                        kv_row(khi, klo, j0 + g, j1, L.lo_start, p.HD, li, kr);
                         float qf[16];
 #pragma unroll
-                        for (int i = 0; i < 16; i++) qf[i] = __ldcg(p.q + h * p.HD + li * 16 + i);
+                        for (int i = 0; i < 4; i++) {
+                            uint4 u = ldcg16(p.q + h * p.HD + li * 16 + 4 * i);
+                            qf[4 * i] = __uint_as_float(u.x); qf[4 * i + 1] = __uint_as_float(u.y);
+                            qf[4 * i + 2] = __uint_as_float(u.z); qf[4 * i + 3] = __uint_as_float(u.w);
+                        }
                         for (int jb = j0; jb < j1; jb += MK_THREADS / 8) {
                             int j = jb + g;
-                            float s = 0.f;
-                            if (j < j1) {
-                                const size_t o = (size_t)j * p.HD + li * 16;
-                                uint4 a0 = ldcg16(khi + o), a1 = ldcg16(khi + o + 8);
-                                uint4 b0 = make_uint4(0, 0, 0, 0), b1 = b0;
-                                if (j >= L.lo_start) { b0 = ldcg16(klo + o); b1 = ldcg16(klo + o + 8); }
-                                uint32_t hw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                                uint32_t lw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-                                for (int i = 0; i < 8; i++) {
-                                    s = __fmaf_rn(qf[2 * i], __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i])), s);
-                                    s = __fmaf_rn(qf[2 * i + 1], __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i])), s);
-                                }
-                            }
+                            if (jb != j0) kv_row(khi, klo, j, j1, L.lo_start, p.HD, li, kr);
+                            float s = kv_dot(kr, qf);
                             s += __shfl_xor_sync(DS_FULL, s, 1);
                             s += __shfl_xor_sync(DS_FULL, s, 2);
                             s += __shfl_xor_sync(DS_FULL, s, 4);
                             if (li == 0 && j < j1) p.att_sc[(size_t)h * p.kv_max + j] = __fmul_rn(s, p.scale);
                         }
                     } else {
-                        // every key's score of this head -> exact unrolled weights
+                        // this group's first V row and every key's score of the head in
+                        // one round trip -> exact unrolled weights
+                        uint4 vr[4];
+                        kv_row(vhi, vlo, j0 + g, j1, L.lo_start, p.HD, li, vr);
                         for (int j = tid; j < n; j += MK_THREADS) wts[j] = __ldcg(p.att_sc + (size_t)h * p.kv_max + j);
                         __syncthreads();
                         const int seg = (n + MK_THREADS - 1) / MK_THREADS;
@@ -570,20 +614,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                         for (int i = 0; i < 16; i++) acc[i] = 0.f;
                         for (int jb = j0; jb < j1; jb += MK_THREADS / 8) {
                             int j = jb + g;
-                            if (j < j1) {
-                                const size_t o = (size_t)j * p.HD + li * 16;
-                                uint4 a0 = ldcg16(vhi + o), a1 = ldcg16(vhi + o + 8);
-                                uint4 b0 = make_uint4(0, 0, 0, 0), b1 = b0;
-                                if (j >= L.lo_start) { b0 = ldcg16(vlo + o); b1 = ldcg16(vlo + o + 8); }
-                                uint32_t hw[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                                uint32_t lw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-                                float w = wts[j];
-#pragma unroll
-                                for (int i = 0; i < 8; i++) {
-                                    acc[2 * i] = __fmaf_rn(w, __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i])), acc[2 * i]);
-                                    acc[2 * i + 1] = __fmaf_rn(w, __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i])), acc[2 * i + 1]);
-                                }
-                            }
+                            if (jb != j0) kv_row(vhi, vlo, j, j1, L.lo_start, p.HD, li, vr);
+                            if (j < j1) kv_axpy(vr, wts[j], acc);
                         }
                         // reduce the 4 groups of each warp, then the 16 warps
 #pragma unroll
@@ -607,12 +639,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                 }
                 case PH_OPROJ: {
                     // attention output = sum of the head's partials / sum of weights
-                    const int cph = gridDim.x / p.NH;
+                    const int cph = min(16, (int)gridDim.x / p.NH);  // CTAs per head (<= 16 partials)
                     for (int i = tid; i < p.NH * p.HD; i += MK_THREADS) {
                         int h = i / p.HD, d = i - h * p.HD;
-                        float o = 0.f;
-                        for (int cc = 0; cc < cph; cc++) o = __fadd_rn(o, __ldcg(p.att_part + ((size_t)h * gridDim.x + cc) * p.HD + d));
+                        // all partials of this element in one round trip, summed in order
+                        float v[16];
+#pragma unroll
+                        for (int cc = 0; cc < 16; cc++)
+                            v[cc] = cc < cph ? __ldcg(p.att_part + ((size_t)h * gridDim.x + cc) * p.HD + d) : 0.f;
                         float S = __ldcg(p.att_sum + h);
+                        float o = 0.f;
+                        for (int cc = 0; cc < cph; cc++) o = __fadd_rn(o, v[cc]);
                         xs[i] = S > 0.f ? __fmul_rn(o, __fdiv_rn(1.0f, S)) : o;
                     }
                     __syncthreads();
@@ -643,7 +680,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                             hout[ia + i] = hv;
                         }
                     }
-                    if (cur.phase == PH_RSGU) {
+                    if (cur.phase == PH_RSGU && sub == geo.nsub - 1) {
                         int ea, eb;
                         split_range(p.E, gridDim.x, blockIdx.x, ea, eb);
                         for (int e = ea + warp; e < eb; e += MK_WARPS) {
@@ -729,11 +766,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                     break;
             }
             __syncthreads();  // region r and xs are free again
+            MK_TRACE(4, clock64());
         }
         next_phase(p, cur);
     }
     // publish the last token
-    if (!grid_sync(p.bar)) return;
+    if (!grid_sync(p.bar, epoch)) return;
     if (tid == 0 && blockIdx.x == 0) {
         unsigned long long k = atomicAdd(&p.slot[(p.n_steps - 1) & 1], 0ull);
         int t = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffull));

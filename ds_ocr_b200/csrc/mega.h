@@ -34,6 +34,8 @@ struct MegaParams {
     unsigned *bar;             // [0] arrive count, [1] generation, [2] error flag
     int *pos, *tok, *tok_log;
     float *val, *final_x;      // final_x optional (last step's normed hidden state)
+    long long *trace;          // optional: CTA 0 / last CTA phase timestamps (clock64)
+    int trace_cap;
     int n_steps;
     int first_from_token;      // 1: step 0 input = embedding of *tok; 0: xa holds it
 };

@@ -176,7 +176,7 @@ __device__ __forceinline__ int item_bytes(const MegaParams &p, int phase) {
     }
 }
 
-__device__ Geo geometry(const MegaParams &p, int phase) {
+__device__ Geo compute_geometry(const MegaParams &p, int phase) {
     Geo g = {0, 0, 1, 1};
     int total = 0;
     switch (phase) {
@@ -200,6 +200,13 @@ __device__ Geo geometry(const MegaParams &p, int phase) {
     g.ipc = max(1, (cmax + g.nsub - 1) / g.nsub);
     return g;
 }
+
+// Per-CTA geometry of every phase and this CTA's router rows, computed once
+// at kernel start (the issuing thread must not redo integer divisions per
+// chunk: it sits on the critical path of its warp).
+__shared__ Geo s_geo[PH_END];
+__shared__ int s_ea, s_eb;
+__device__ __forceinline__ Geo geometry(const MegaParams &, int phase) { return s_geo[phase]; }
 
 __device__ __forceinline__ void next_phase(const MegaParams &p, Cur &c) {
     const MegaLayer &L = p.layers[c.layer];
@@ -231,7 +238,8 @@ __device__ uint32_t chunk_bytes(const MegaParams &p, const Cur &c, int sub) {
     uint32_t n = ib > ia ? (uint32_t)(ib - ia) * item_bytes(p, c.phase) : 0;
     if (c.phase == PH_RSGU && sub == g.nsub - 1) {
         int ea, eb;
-        split_range(p.E, gridDim.x, blockIdx.x, ea, eb);
+        ea = s_ea;
+        eb = s_eb;
         n += (uint32_t)(eb - ea) * 2 * p.H;
     }
     return n;
@@ -277,7 +285,8 @@ __device__ void issue_chunk(const MegaParams &p, const Cur &c, int sub, uint8_t 
             }
             if (sub == g.nsub - 1) {
                 int ea, eb;
-                split_range(p.E, gridDim.x, blockIdx.x, ea, eb);
+                ea = s_ea;
+                eb = s_eb;
                 if (eb > ea) bulk_g2s(dst + (size_t)2 * cnt * rb, L.router + (size_t)ea * p.H, (eb - ea) * rb, bar);
             }
             break;
@@ -406,7 +415,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
     if (tid == 0) {
         for (int i = 0; i < MK_NREG; i++) mbar_init(&full[i], 1);
         mbar_fence_init();
+        split_range(p.E, gridDim.x, blockIdx.x, s_ea, s_eb);
     }
+    if (tid < PH_END) s_geo[tid] = compute_geometry(p, tid);
     __syncthreads();
 
     int pos = *p.pos;
@@ -682,7 +693,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                     }
                     if (cur.phase == PH_RSGU && sub == geo.nsub - 1) {
                         int ea, eb;
-                        split_range(p.E, gridDim.x, blockIdx.x, ea, eb);
+                        ea = s_ea;
+                        eb = s_eb;
                         for (int e = ea + warp; e < eb; e += MK_WARPS) {
                             float s = warp_sum(sdot<CPL>(W + (size_t)(2 * cnt + e - ea) * p.H, p.H, xr, lane));
                             if (lane == 0) p.rscore[e] = s;

@@ -338,13 +338,20 @@ __device__ __forceinline__ bool loadable_now(const Cur &cur, const Cur &nx) {
 template <int CPL>
 __device__ __forceinline__ float sdot(const uint16_t *row, int n, const XRegBF16<CPL> &x, int lane) {
     const int nch = n >> 3;
-    float acc = 0.f;
+    uint4 w[CPL];
 #pragma unroll
     for (int c = 0; c < CPL; c++) {
         int ch = lane + 32 * c;
-        if (ch < nch) acc = dot8_bf16(*reinterpret_cast<const uint4 *>(row + 8 * ch), x.v[c][0], x.v[c][1], acc);
+        w[c] = ch < nch ? *reinterpret_cast<const uint4 *>(row + 8 * ch) : make_uint4(0, 0, 0, 0);
     }
-    return acc;
+    // two independent FMA chains (even / odd chunks) for instruction-level parallelism
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; c++) {
+        if (c & 1) a1 = dot8_bf16(w[c], x.v[c][0], x.v[c][1], a1);
+        else a0 = dot8_bf16(w[c], x.v[c][0], x.v[c][1], a0);
+    }
+    return __fadd_rn(a0, a1);
 }
 
 // Long row (n up to MK_XS) against a vector in shared memory.
@@ -508,20 +515,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
 
             switch (cur.phase) {
                 case PH_QKV: {
-                    // input: the token embedding (layer 0 of a token-fed step) or xa
-                    if (cur.layer == 0 && (cur.step > 0 || p.first_from_token)) {
-                        const uint16_t *e = p.lm_head + (size_t)tok * p.H;
-                        for (int i = tid; i < p.H; i += MK_THREADS) xs[i] = __uint_as_float((uint32_t)e[i] << 16);
-                        __syncthreads();
-                        if (sub == 0) {
+                    // input: the token embedding (layer 0 of a token-fed step) or
+                    // xa, normalised once per phase (xs persists across its chunks)
+                    if (sub == 0) {
+                        if (cur.layer == 0 && (cur.step > 0 || p.first_from_token)) {
+                            const uint16_t *e = p.lm_head + (size_t)tok * p.H;
+                            for (int i = tid; i < p.H; i += MK_THREADS) xs[i] = __uint_as_float((uint32_t)e[i] << 16);
+                            __syncthreads();
                             int xa0, xa1;
                             split_range(p.H, gridDim.x, blockIdx.x, xa0, xa1);
                             for (int i = xa0 + tid; i < xa1; i += MK_THREADS) p.xa[i] = xs[i];
+                        } else {
+                            load_vec(xs, p.xa, p.H);
                         }
-                    } else {
-                        load_vec(xs, p.xa, p.H);
+                        norm_vec(xs, L.in_norm, p.H, p.eps);
                     }
-                    norm_vec(xs, L.in_norm, p.H, p.eps);
                     XRegBF16<CPL> xr;
                     xr.load(xs, p.H, lane);
                     const int half = p.HD / 2, per = p.NH * half;
@@ -675,8 +683,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                 case PH_DGU:
                 case PH_RSGU:
                 case PH_RGU: {
-                    load_vec(xs, p.xb, p.H);
-                    norm_vec(xs, L.post_norm, p.H, p.eps);
+                    if (sub == 0) {
+                        load_vec(xs, p.xb, p.H);
+                        norm_vec(xs, L.post_norm, p.H, p.eps);
+                    }
                     XRegBF16<CPL> xr;
                     xr.load(xs, p.H, lane);
                     const bool sim = p.simulate && cur.phase != PH_DGU;

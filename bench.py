@@ -372,7 +372,7 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 1280 * 4, "d2h_bytes_per_step": 8},
         # persistent engine: the timed region is ONE kernel launch for all steps
         "gpu_launches": launches * args.steps if launches else 1,
-        "config": dict(decode_config(kv_max), engine=["persistent kernel", "kernel graph"][args.engine]),
+        "config": dict(decode_config(kv_max), engine=["kernel graph", "persistent kernel"][args.engine]),
         "roofline": {"bound": "hbm", "achieved": lm_ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": lm_ach / pk["hbm_gbs"], "traffic": None,
                      "kernel": "argmax_bf16_kernel (LM head 129280x1280, 330,956,800 B/launch)",
@@ -415,7 +415,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer"])
     ap.add_argument("--engine", type=int, default=0, choices=[0, 1],
-                    help="decode engine: 0 persistent kernel, 1 CUDA graph of per-phase kernels")
+                    help="decode engine: 0 CUDA graph of per-phase kernels, 1 persistent kernel")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -487,7 +487,7 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
         cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
         m->lo_start.assign(g.n_layers, 0);
     }
-    if (rc == DS_CUDA_OK && g.engine == 0) {
+    if (rc == DS_CUDA_OK && g.engine == 1) {
         // the persistent kernel is specialised for hidden = heads*head_dim =
         // 1280 (5 x 256-column register slices) and BF16 experts
         int G = mega_grid(c->device);
@@ -498,7 +498,7 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
         if (g.use_int8 || g.hidden != 1280 || g.n_heads * g.head_dim != 1280 || g.top_k > 8 ||
             g.top_k * g.moe_inter + S > 8192 || g.dense_inter > 8192 || !fits) {
             rc = ctx_fail(c, DS_CUDA_EINVAL, "decoder_create: configuration not supported by the persistent engine "
-                                             "(use engine = 1)");
+                                             "(use engine = 0)");
         } else {
             m->mega = true;
             m->mega_grid = G;

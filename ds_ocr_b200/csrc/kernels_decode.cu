@@ -38,27 +38,43 @@ __device__ __forceinline__ void split_bf16(float v, uint16_t &hi, uint16_t &lo) 
 
 template <int CPL>
 __global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
-    pdl_wait();
-    pdl_launch();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
     const int n = a.hidden;
+    const int half = a.head_dim >> 1;
+    const int per_mat = a.n_heads * half;
+    // task t: the rotary row pair (row0, row0 + half) of Wq, Wk or Wv
+    auto task_rows = [&](int t, const uint16_t *&p0, int &m, int &h, int &d) {
+        m = t / per_mat;
+        int r = t - m * per_mat;
+        h = r / half;
+        d = r - h * half;
+        const uint16_t *W = m == 0 ? a.w[0] : (m == 1 ? a.w[1] : a.w[2]);
+        p0 = W + (size_t)(h * a.head_dim + d) * n;
+    };
+    // the first task's weights load before the dependency wait
+    Rows2<CPL> w;
+    if (gw < 3 * per_mat) {
+        const uint16_t *p0;
+        int m, h, d;
+        task_rows(gw, p0, m, h, d);
+        w.load(p0, p0 + (size_t)half * n, n, lane);
+    }
+    pdl_wait();
+    pdl_launch();
     const float inv = block_rms_inv(a.x, n, a.eps);
     XRegBF16<CPL> xr;
     xr.load_norm(a.x, a.norm_w, inv, n, lane);
-    const int half = a.head_dim >> 1;
-    const int per_mat = a.n_heads * half;
     const int pos = *a.d_pos;
     for (int t = gw; t < 3 * per_mat; t += nw) {
-        int m = t / per_mat;
-        int r = t - m * per_mat;
-        int h = r / half;
-        int d = r - h * half;
-        int row0 = h * a.head_dim + d;
-        const uint16_t *W = m == 0 ? a.w[0] : (m == 1 ? a.w[1] : a.w[2]);
+        const uint16_t *p0;
+        int m, h, d;
+        task_rows(t, p0, m, h, d);
+        const int row0 = h * a.head_dim + d;
+        if (t != gw) w.load(p0, p0 + (size_t)half * n, n, lane);
         float s0, s1;
-        row_dot2_bf16<CPL>(W + (size_t)row0 * n, W + (size_t)(row0 + half) * n, n, xr, lane, s0, s1);
+        w.dot(xr, s0, s1);
         s0 = warp_sum(s0);
         s1 = warp_sum(s1);
         if (lane == 0) {
@@ -360,18 +376,24 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
 
 template <int CPL>
 __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
-    pdl_wait();
-    pdl_launch();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
+    // the first row pair's weights load before the dependency wait
+    Rows2<CPL> w;
+    const int r0 = 2 * gw;
+    if (r0 < a.rows)
+        w.load(a.W + (size_t)r0 * a.n, r0 + 1 < a.rows ? a.W + (size_t)(r0 + 1) * a.n : nullptr, a.n, lane);
+    pdl_wait();
+    pdl_launch();
     const float inv = a.norm_w ? block_rms_inv(a.x, a.n, a.eps) : 1.f;
     XRegBF16<CPL> xr;
     xr.load_norm(a.x, a.norm_w, inv, a.n, lane);
-    for (int r = 2 * gw; r < a.rows; r += 2 * nw) {
-        float s0, s1 = 0.f;
-        if (r + 1 < a.rows) row_dot2_bf16<CPL>(a.W + (size_t)r * a.n, a.W + (size_t)(r + 1) * a.n, a.n, xr, lane, s0, s1);
-        else s0 = row_dot_bf16<CPL>(a.W + (size_t)r * a.n, a.n, xr, lane);
+    for (int r = r0; r < a.rows; r += 2 * nw) {
+        if (r != r0)
+            w.load(a.W + (size_t)r * a.n, r + 1 < a.rows ? a.W + (size_t)(r + 1) * a.n : nullptr, a.n, lane);
+        float s0, s1;
+        w.dot(xr, s0, s1);
         s0 = warp_sum(s0);
         s1 = warp_sum(s1);
         if (lane == 0) {

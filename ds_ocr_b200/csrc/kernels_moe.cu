@@ -69,16 +69,22 @@ __global__ void __launch_bounds__(256) router_kernel(const uint16_t *__restrict_
                                                      int E, int n, float *scores, unsigned *ticket, int top_k,
                                                      int renorm, int *d_idx, float *d_wt, const float *norm_w,
                                                      float eps) {
-    pdl_wait();
-    pdl_launch();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
+    // the first router row loads before the dependency wait
+    Rows2<CPL> w;
+    if (gw < E) w.load(Wr + (size_t)gw * n, nullptr, n, lane);
+    pdl_wait();
+    pdl_launch();
     const float inv = norm_w ? block_rms_inv(x, n, eps) : 1.f;
     XRegBF16<CPL> xr;
     xr.load_norm(x, norm_w, inv, n, lane);
     for (int r = gw; r < E; r += nw) {
-        float s = warp_sum(row_dot_bf16<CPL>(Wr + (size_t)r * n, n, xr, lane));
+        if (r != gw) w.load(Wr + (size_t)r * n, nullptr, n, lane);
+        float s, s1;
+        w.dot(xr, s, s1);
+        s = warp_sum(s);
         if (lane == 0) scores[r] = s;
     }
     __shared__ bool last;
@@ -111,34 +117,53 @@ __global__ void router_select_kernel(const float *scores, int E, int top_k, int 
 // ---------------------------------------------------------------------------
 template <int CPL, bool I8>
 __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
-    pdl_wait();
-    pdl_launch();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
     const int nr = a.top_k * a.inter;
-    const int total = nr + (a.has_shared ? a.sh_inter : 0);
+    const int ns = a.has_shared ? a.sh_inter : 0;
+    const int total = nr + ns;
     const int n = a.hidden;
-    const float inv = a.norm_w ? block_rms_inv(a.x, n, a.eps) : 1.f;
     const bool sim = a.simulate && !a.dense;  // the dense FFN path never truncates (ds_moe_decoder.c:75-105)
     if constexpr (!I8) {
+        // work order: the shared expert's pairs first (their weights do not
+        // depend on the routing, so they load before the dependency wait),
+        // then the routed experts'. h keeps routed [0, nr), shared [nr, total).
+        auto shared_rows = [&](int i, const uint16_t *&w, const uint16_t *&wu) {
+            w = (const uint16_t *)a.sh_gu.w;
+            wu = a.sh_up.w ? (const uint16_t *)a.sh_up.w : w + (size_t)a.sh_inter * n;
+            w += (size_t)i * n;
+            wu += (size_t)i * n;
+        };
+        Rows2<CPL> wr;
+        if (gw < ns) {
+            const uint16_t *w, *wu;
+            shared_rows(gw, w, wu);
+            wr.load(w, wu, n, lane);
+        }
+        pdl_wait();
+        pdl_launch();
+        const float inv = a.norm_w ? block_rms_inv(a.x, n, a.eps) : 1.f;
         XRegBF16<CPL> xr;
         xr.load_norm(a.x, a.norm_w, inv, n, lane);
-        for (int p = gw; p < total; p += nw) {
-            const uint16_t *w, *wu;
-            int i;
-            if (p < nr) {
-                int k = p / a.inter;
-                i = p - k * a.inter;
-                w = (const uint16_t *)expert_mat(a, k, true).w;
-                wu = w + (size_t)a.inter * n;
+        for (int q = gw; q < total; q += nw) {
+            int p;
+            if (q < ns) {
+                p = nr + q;
+                if (q != gw) {
+                    const uint16_t *w, *wu;
+                    shared_rows(q, w, wu);
+                    wr.load(w, wu, n, lane);
+                }
             } else {
-                i = p - nr;
-                w = (const uint16_t *)a.sh_gu.w;
-                wu = a.sh_up.w ? (const uint16_t *)a.sh_up.w : w + (size_t)a.sh_inter * n;
+                p = q - ns;
+                int k = p / a.inter;
+                int i = p - k * a.inter;
+                const uint16_t *w = (const uint16_t *)expert_mat(a, k, true).w;
+                wr.load(w + (size_t)i * n, w + (size_t)(a.inter + i) * n, n, lane);
             }
             float g, u;
-            row_dot2_bf16<CPL>(w + (size_t)i * n, wu + (size_t)i * n, n, xr, lane, g, u);
+            wr.dot(xr, g, u);
             g = warp_sum(g);
             u = warp_sum(u);
             if (lane == 0) {
@@ -149,6 +174,9 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
             }
         }
     } else {
+        pdl_wait();
+        pdl_launch();
+        const float inv = a.norm_w ? block_rms_inv(a.x, n, a.eps) : 1.f;
         XRegI8<CPL> xr;
         xr.load_norm(a.x, a.norm_w, inv, n, lane);
         float xs = 0.f;
@@ -195,14 +223,31 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
 // ---------------------------------------------------------------------------
 template <int CPL, bool I8, int RB>
 __global__ void __launch_bounds__(256) moe_down_kernel(MoeArgs a) {
-    pdl_wait();
-    pdl_launch();
     __shared__ float y[RB][8];
     const int lane = threadIdx.x & 31;
     const int slot = threadIdx.x >> 5;
     const int j0 = blockIdx.x * RB;
     const int nslots = a.top_k + (a.has_shared ? 2 : 0);
     const int nr = a.top_k * a.inter;
+    // the shared expert's down rows do not depend on the routing: its two
+    // warps load them before the dependency wait
+    Rows2<CPL> pre[(RB + 1) / 2];
+    const bool sh_slot = !I8 && slot >= a.top_k && slot < nslots;
+    if constexpr (!I8) {
+        if (sh_slot) {
+            const int len = a.sh_inter >> 1, rowlen = a.sh_inter;
+            const uint16_t *w = (const uint16_t *)a.sh_dn.w + (slot - a.top_k) * len;
+#pragma unroll
+            for (int r = 0; r < RB; r += 2) {
+                int j = j0 + r;
+                if (j < a.hidden)
+                    pre[r / 2].load(w + (size_t)j * rowlen, j + 1 < a.hidden ? w + (size_t)(j + 1) * rowlen : nullptr,
+                                    len, lane);
+            }
+        }
+    }
+    pdl_wait();
+    pdl_launch();
     if (slot < nslots) {
         const float *hv;
         WMat m;
@@ -229,10 +274,11 @@ __global__ void __launch_bounds__(256) moe_down_kernel(MoeArgs a) {
             for (int r = 0; r < RB; r += 2) {
                 int j = j0 + r;
                 float s0 = 0.f, s1 = 0.f;
-                if (j + 1 < a.hidden) {
-                    row_dot2_bf16<CPL>(w + (size_t)j * rowlen, w + (size_t)(j + 1) * rowlen, len, hr, lane, s0, s1);
-                } else if (j < a.hidden) {
-                    s0 = row_dot_bf16<CPL>(w + (size_t)j * rowlen, len, hr, lane);
+                if (j < a.hidden) {
+                    if (!sh_slot)
+                        pre[r / 2].load(w + (size_t)j * rowlen,
+                                        j + 1 < a.hidden ? w + (size_t)(j + 1) * rowlen : nullptr, len, lane);
+                    pre[r / 2].dot(hr, s0, s1);
                 }
                 s0 = warp_sum(s0);
                 s1 = warp_sum(s1);

@@ -144,6 +144,35 @@ __device__ __forceinline__ float row_dot_bf16(const uint16_t *row, int n, const 
     return acc;
 }
 
+// The lane slices of two BF16 rows held in registers, so a kernel can issue
+// its weight loads before griddepcontrol.wait (weights never depend on the
+// preceding kernel) and overlap them with the predecessor's tail. r1 may be
+// null (one row; its dot is 0).
+template <int CPL>
+struct Rows2 {
+    uint4 w0[CPL], w1[CPL];
+    __device__ __forceinline__ void load(const uint16_t *r0, const uint16_t *r1, int n, int lane) {
+        const int nch = n >> 3;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            int ch = lane + 32 * c;
+            bool ok = ch < nch;
+            w0[c] = ok ? ldg_stream(r0 + 8 * ch) : make_uint4(0, 0, 0, 0);
+            w1[c] = ok && r1 ? ldg_stream(r1 + 8 * ch) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    __device__ __forceinline__ void dot(const XRegBF16<CPL> &x, float &s0, float &s1) const {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; c++) {
+            a0 = dot8_bf16(w0[c], x.v[c][0], x.v[c][1], a0);
+            a1 = dot8_bf16(w1[c], x.v[c][0], x.v[c][1], a1);
+        }
+        s0 = a0;
+        s1 = a1;
+    }
+};
+
 // Two rows at once (twice the bytes in flight per lane).
 template <int CPL>
 __device__ __forceinline__ void row_dot2_bf16(const uint16_t *r0, const uint16_t *r1, int n,

@@ -218,8 +218,9 @@ typedef struct {
     float rms_eps, rope_theta;
     int kv_max;   /* KV capacity in tokens (the reference allocates 4096, ds_ocr.c:861) */
     int use_int8; /* 1: MoE layers use the INT8 blocks (the --int4 path) */
-    int engine;   /* 0: one persistent kernel per call (default; BF16, hidden 1280);
-                     1: a CUDA graph of per-phase kernels per token (any supported shape, INT8) */
+    int engine;   /* 0: a CUDA graph of per-phase kernels per token (default; any
+                        supported shape, INT8);
+                     1: one persistent kernel per call (BF16, hidden 1280) */
 } ds_cuda_decoder_config_t;
 
 /* The fields of the reference's ds_dec_layer_t (ds_ocr.h:282-342) the
@@ -266,7 +267,7 @@ int ds_cuda_decoder_generate(ds_cuda_ctx_t *ctx, int model, const float *first_e
 /* Enqueue n_steps greedy steps on `stream` from the device-resident state
  * (no host copies; for timing). */
 int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *ctx, int model, int n_steps, void *stream);
-/* Kernel launches one decode step issues with engine 1; 0 with the
+/* Kernel launches one decode step issues with engine 0; 0 with the
  * persistent engine (one launch per forward/generate call). */
 int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *ctx, int model);
 

@@ -8,7 +8,7 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libds_cuda.so")
+LIB_PATH = os.environ.get("DS_CUDA_LIB") or os.path.join(HERE, "libds_cuda.so")
 
 c_int, c_float, c_size_t, c_void_p, c_uint64 = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_uint64
 P = c_void_p  # all pointers are passed as raw addresses
@@ -52,6 +52,9 @@ SIGNATURES = {
     "ds_cuda_decoder_generate": (c_int, [P, c_int, P, c_int, P]),
     "ds_cuda_decoder_generate_dev": (c_int, [P, c_int, c_int, P]),
     "ds_cuda_decoder_launches_per_step": (c_int, [P, c_int]),
+    "ds_cuda_prefill_moe": (c_int, [P, P, P, P, c_int, P, P, P]),
+    "ds_cuda_prefill_moe_dev": (c_int, [P, P, P, P, c_int, P, P, P, P]),
+    "ds_cuda_prefill_check": (c_int, [P]),
     "ds_synth_normal_bf16": (None, [P, c_size_t, c_uint64, c_float, c_float]),
     "ds_synth_normal_f32": (None, [P, c_size_t, c_uint64, c_float, c_float]),
     "ds_synth_normal_f32_bf16exact": (None, [P, c_size_t, c_uint64, c_float, c_float]),

@@ -147,6 +147,19 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+// F32 -> BF16 with round-to-nearest-even, as raw bits.
+__device__ __forceinline__ uint16_t bf16_rne_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+// Split v into hi + lo BF16 halves (v ~= hi + lo to ~2^-17 relative): the
+// decode KV cache stores K and V as two such planes, and the prefill GEMMs
+// take their F32 activations as two such planes.
+__device__ __forceinline__ void split_bf16(float v, uint16_t &hi, uint16_t &lo) {
+    hi = bf16_rne_bits(v);
+    lo = bf16_rne_bits(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
+}
 // Order-preserving map of an F32 to uint32 (larger float -> larger uint).
 __device__ __forceinline__ uint32_t f32_ordered(float f) {
     uint32_t u = __float_as_uint(f);

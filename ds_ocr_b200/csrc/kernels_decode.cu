@@ -11,19 +11,6 @@ namespace cg = cooperative_groups;
 
 namespace ds {
 
-// F32 -> BF16 with round-to-nearest-even, as raw bits.
-__device__ __forceinline__ uint16_t bf16_rne_bits(float f) {
-    uint32_t u = __float_as_uint(f);
-    u += 0x7fffu + ((u >> 16) & 1u);
-    return (uint16_t)(u >> 16);
-}
-// Split v into hi + lo BF16 halves (v ~= hi + lo to ~2^-17 relative): the KV
-// cache stores K and V as two BF16 planes; the lo plane is only read for
-// positions that are not exactly BF16 (lo_start onwards).
-__device__ __forceinline__ void split_bf16(float v, uint16_t &hi, uint16_t &lo) {
-    hi = bf16_rne_bits(v);
-    lo = bf16_rne_bits(__fsub_rn(v, __uint_as_float((uint32_t)hi << 16)));
-}
 
 // ---------------------------------------------------------------------------
 // Input RMSNorm + QKV + RoPE + KV append (decoder_layer_forward,

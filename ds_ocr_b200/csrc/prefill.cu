@@ -1,0 +1,759 @@
+// prefill.cu — batched MoE prefill block of ds_decoder_prefill
+// (ds_moe_decoder.c:630-809) for n tokens at once, on the 5th-generation
+// tensor cores.
+//
+// Per MoE layer the reference computes, for x [n x H] (F32):
+//   xn = RMSNorm(x)                                  (:598, ds_rms_norm)
+//   logits = xn W_r^T; softmax (fast exp); top-6     (:643-686, no renorm)
+//   shared = down_s(SwiGLU(xn Wg_s^T, xn Wu_s^T))    (:688-712, sgemm)
+//   per expert e, over its tokens (ascending e):     (:714-791)
+//     y = down_e(SwiGLU(X_e Wg_e^T, X_e Wu_e^T)); routed[s] += w * y
+//   x += routed + shared                              (:794-800)
+// with BF16 weights widened exactly to F32 and F32 GEMMs (cblas_sgemm).
+//
+// B200 design:
+//   * activations are split into two BF16 planes, hi = bf16(v) and
+//     lo = bf16(v - hi), so hi + lo carries 16 significant bits; the weights
+//     are exact in BF16. Each GEMM runs A_hi*B + A_lo*B into one F32
+//     accumulator (tcgen05.mma kind::f16, accumulator in tensor memory):
+//     twice the tensor work of a plain BF16 GEMM, F32-class accuracy.
+//   * routing groups token copies by expert into contiguous row segments
+//     (counting sort), so every expert's A operand is a plain 2-D TMA tile.
+//   * one persistent grouped-GEMM kernel per stage walks a device-built tile
+//     list (routed expert tiles and shared-expert tiles together): warp 0
+//     streams A_hi/A_lo/B tiles with TMA into a 3-stage ring, warp 1 issues
+//     the MMAs, warps 2-5 drain the accumulator (two tensor-memory buffers,
+//     so the epilogue of one tile overlaps the main loop of the next).
+//   * gate/up tiles hold 128 gate rows and the matching 128 up rows, so the
+//     SwiGLU runs in the epilogue and writes the down GEMM's split A planes.
+//   * the down GEMM writes each routed (token, slot) row; a combine kernel
+//     sums a token's 6 rows in ascending expert order (the reference's
+//     accumulation order) and adds the shared expert and the residual.
+#include <cstdio>
+#include <cstring>
+#include <vector>
+#include <cuda.h>
+#include "ctx.h"
+#include "umma.cuh"
+
+namespace ds {
+
+constexpr int PF_BM = 128;  // tile rows (tokens) = tensor-memory lanes
+constexpr int PF_BK = 64;   // K per stage: one 128-byte swizzle row of BF16
+constexpr int PF_BN = 256;  // accumulator columns per tile
+constexpr int PF_STAGES = 3;
+constexpr int PF_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;
+constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;
+constexpr int PF_STAGE_BYTES = 2 * PF_A_BYTES + PF_B_BYTES;
+constexpr int PF_SMEM = PF_STAGES * PF_STAGE_BYTES + 1024;
+constexpr int PF_MAXE = 256;
+
+struct PfTile {
+    int kind;   // 0: routed expert, 1: shared expert
+    int e;      // expert (kind 0)
+    int a_row;  // first row of the tile in the A planes
+    int rows;   // valid rows (<= 128)
+    int n0;     // first output column (gate/up: first gate row)
+};
+
+struct PfGemm {
+    CUtensorMap a_hi[2], a_lo[2], b[2];  // [kind]
+    const PfTile *tiles;
+    const int *n_tiles;
+    int k_blocks[2];
+    int b_base[2], b_group_rows[2], b_half[2];
+    uint16_t *h_hi[2], *h_lo[2];  // gate/up epilogue outputs
+    int h_ld[2];
+    float *y[2];                  // down epilogue outputs
+    const int *slot_of;           // routed: output row of each sorted position
+    int y_ld;
+    unsigned *err;
+};
+
+// ---------------------------------------------------------------------------
+// Grouped split-BF16 GEMM. MODE 0: gate/up + SwiGLU; MODE 1: down.
+// ---------------------------------------------------------------------------
+template <int MODE>
+__global__ void __launch_bounds__(PF_THREADS, 1) pf_gemm_kernel(const __grid_constant__ PfGemm p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[PF_STAGES], empty[PF_STAGES], acc_full[2], acc_empty[2], drain;
+    __shared__ uint32_t tmem_base;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = *p.n_tiles;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PF_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(&drain, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) tmem_alloc(&tmem_base, 2 * PF_BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer: A_hi, A_lo and B tiles of every k block of every tile
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const PfTile tl = p.tiles[t];
+                const int kind = tl.kind;
+                const int brow = p.b_base[kind] + tl.e * p.b_group_rows[kind] + tl.n0;
+                for (int kb = 0; kb < p.k_blocks[kind]; kb++, it++) {
+                    const int s = it % PF_STAGES, r = it / PF_STAGES;
+                    if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = smem + s * PF_STAGE_BYTES;
+                    mbar_expect_tx(&full[s], PF_STAGE_BYTES);
+                    tma_load_2d(st, &p.a_hi[kind], kb * PF_BK, tl.a_row, &full[s]);
+                    tma_load_2d(st + PF_A_BYTES, &p.a_lo[kind], kb * PF_BK, tl.a_row, &full[s]);
+                    if (MODE == 0) {
+                        tma_load_2d(st + 2 * PF_A_BYTES, &p.b[kind], kb * PF_BK, brow, &full[s]);
+                        tma_load_2d(st + 2 * PF_A_BYTES + PF_B_BYTES / 2, &p.b[kind], kb * PF_BK,
+                                    brow + p.b_half[kind], &full[s]);
+                    } else {
+                        tma_load_2d(st + 2 * PF_A_BYTES, &p.b[kind], kb * PF_BK, brow, &full[s]);
+                    }
+                }
+            }
+            // the last copies have landed before the CTA can exit (already
+            // true unless a wait above gave up)
+            for (int i = max(0, it - PF_STAGES); i < it; i++)
+                mbar_wait(&full[i % PF_STAGES], (i / PF_STAGES) & 1, p.err);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: 4 K=16 steps per stage, hi and lo against one B
+            constexpr uint32_t idesc = idesc_bf16_f32(PF_BM, PF_BN);
+            int it = 0, ti = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ti++) {
+                const int b = ti & 1, u = ti >> 1;
+                if (u > 0 && !mbar_wait(&acc_empty[b], (u - 1) & 1, p.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + b * PF_BN;
+                const int nk = p.k_blocks[p.tiles[t].kind];
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % PF_STAGES, r = it / PF_STAGES;
+                    if (!mbar_wait(&full[s], r & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t *st = smem + s * PF_STAGE_BYTES;
+                    const uint64_t ah = sw128_desc(st), al = sw128_desc(st + PF_A_BYTES);
+                    const uint64_t bd = sw128_desc(st + 2 * PF_A_BYTES);
+#pragma unroll
+                    for (int j = 0; j < PF_BK / 16; j++) {
+                        umma_bf16(d, ah + 2 * j, bd + 2 * j, idesc, (kb | j) != 0);
+                        umma_bf16(d, al + 2 * j, bd + 2 * j, idesc, 1u);
+                    }
+                    umma_commit(&empty[s]);  // frees the stage when these MMAs finish
+                }
+                if (ok) umma_commit(&acc_full[b]);
+            }
+            // every MMA has finished before tensor memory is released
+            umma_commit(&drain);
+            mbar_wait(&drain, 0, p.err);
+        }
+    } else {
+        // epilogue: warp w reads tensor-memory lanes 32*(w%4) .. +31 = tile rows
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        int ti = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ti++) {
+            const int b = ti & 1, u = ti >> 1;
+            if (!mbar_wait(&acc_full[b], u & 1, p.err)) break;
+            tc_fence_after();
+            const PfTile tl = p.tiles[t];
+            const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + b * PF_BN;
+            const bool valid = row < tl.rows;
+            if (MODE == 0) {
+                const size_t orow = (size_t)(tl.a_row + row) * p.h_ld[tl.kind] + tl.n0;
+#pragma unroll 1
+                for (int c0 = 0; c0 < PF_BN / 2; c0 += 32) {
+                    float g[32], v[32];
+                    tmem_ld32(tb + c0, g);
+                    tmem_ld32(tb + PF_BN / 2 + c0, v);
+                    if (valid) {
+                        uint32_t hw[16], lw[16];
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            uint16_t h0, l0, h1, l1;
+                            split_bf16(swiglu(g[j], v[j]), h0, l0);
+                            split_bf16(swiglu(g[j + 1], v[j + 1]), h1, l1);
+                            hw[j / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                            lw[j / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+                        }
+                        uint4 *dh = reinterpret_cast<uint4 *>(p.h_hi[tl.kind] + orow + c0);
+                        uint4 *dl = reinterpret_cast<uint4 *>(p.h_lo[tl.kind] + orow + c0);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            dh[j] = make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
+                            dl[j] = make_uint4(lw[4 * j], lw[4 * j + 1], lw[4 * j + 2], lw[4 * j + 3]);
+                        }
+                    }
+                }
+            } else {
+                int orow_i = tl.a_row + row;
+                if (tl.kind == 0 && valid) orow_i = p.slot_of[orow_i];
+                float *dst = p.y[tl.kind] + (size_t)orow_i * p.y_ld + tl.n0;
+#pragma unroll 1
+                for (int c0 = 0; c0 < PF_BN; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(tb + c0, v);
+                    if (valid) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst + c0);
+#pragma unroll
+                        for (int j = 0; j < 8; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * PF_BN);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Per-token RMSNorm (ds_rms_norm), split into BF16 planes, and routing:
+// softmax with fast exp over the logits (given, or xn W_r^T), strict-'>'
+// top-k, weights = probabilities (ds_moe_decoder.c:652-686). One warp per
+// token; H a multiple of 128, E <= 256.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) pf_norm_route_kernel(const float *__restrict__ x, const float *__restrict__ nw,
+                                                            float eps, int M, int H, const float *logits_in,
+                                                            const uint16_t *__restrict__ Wr, float *logits_buf, int E,
+                                                            int K, int renorm, uint16_t *xn_hi, uint16_t *xn_lo,
+                                                            int *idx, float *wt, int *counts) {
+    const int lane = threadIdx.x & 31;
+    const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (s >= M) return;
+    const float *xr = x + (size_t)s * H;
+    const int nv = H / 128;  // float4 per lane
+    float4 v[16];
+    float ss = 0.f;
+    for (int i = 0; i < nv; i++) {
+        v[i] = *reinterpret_cast<const float4 *>(xr + 4 * (lane + 32 * i));
+        ss = __fmaf_rn(v[i].x, v[i].x, ss);
+        ss = __fmaf_rn(v[i].y, v[i].y, ss);
+        ss = __fmaf_rn(v[i].z, v[i].z, ss);
+        ss = __fmaf_rn(v[i].w, v[i].w, ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+    for (int i = 0; i < nv; i++) {
+        const int c = 4 * (lane + 32 * i);
+        const float4 w4 = *reinterpret_cast<const float4 *>(nw + c);
+        v[i].x = __fmul_rn(__fmul_rn(v[i].x, w4.x), inv);
+        v[i].y = __fmul_rn(__fmul_rn(v[i].y, w4.y), inv);
+        v[i].z = __fmul_rn(__fmul_rn(v[i].z, w4.z), inv);
+        v[i].w = __fmul_rn(__fmul_rn(v[i].w, w4.w), inv);
+        uint16_t h[4], l[4];
+        split_bf16(v[i].x, h[0], l[0]);
+        split_bf16(v[i].y, h[1], l[1]);
+        split_bf16(v[i].z, h[2], l[2]);
+        split_bf16(v[i].w, h[3], l[3]);
+        *reinterpret_cast<uint2 *>(xn_hi + (size_t)s * H + c) =
+            make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+        *reinterpret_cast<uint2 *>(xn_lo + (size_t)s * H + c) =
+            make_uint2((uint32_t)l[0] | ((uint32_t)l[1] << 16), (uint32_t)l[2] | ((uint32_t)l[3] << 16));
+    }
+    const float *lg;
+    if (logits_in) {
+        lg = logits_in + (size_t)s * E;
+    } else {
+        // router scores in F32 from the normalised row (ds_linear_nobias_bf16)
+        float *out = logits_buf + (size_t)s * E;
+        for (int e = 0; e < E; e++) {
+            const uint16_t *wr = Wr + (size_t)e * H;
+            float acc = 0.f;
+            for (int i = 0; i < nv; i++) {
+                const uint2 w2 = *reinterpret_cast<const uint2 *>(wr + 4 * (lane + 32 * i));
+                acc = __fmaf_rn(v[i].x, __uint_as_float(w2.x << 16), acc);
+                acc = __fmaf_rn(v[i].y, __uint_as_float(w2.x & 0xffff0000u), acc);
+                acc = __fmaf_rn(v[i].z, __uint_as_float(w2.y << 16), acc);
+                acc = __fmaf_rn(v[i].w, __uint_as_float(w2.y & 0xffff0000u), acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) out[e] = acc;
+        }
+        __syncwarp();
+        lg = out;
+    }
+    // softmax + top-k: lane holds experts lane, lane+32, ...
+    const int per = (E + 31) / 32;
+    float p[8];
+    float mx = -1e30f;
+    for (int j = 0; j < per; j++) {
+        const int e = lane + 32 * j;
+        p[j] = e < E ? lg[e] : -1e30f;
+        mx = fmaxf(mx, p[j]);
+    }
+    mx = warp_max(mx);
+    float part = 0.f;
+    for (int j = 0; j < per; j++) {
+        const int e = lane + 32 * j;
+        p[j] = e < E ? fast_expf(__fsub_rn(p[j], mx)) : 0.f;
+        part = __fadd_rn(part, p[j]);
+    }
+    const float sinv = __fdiv_rn(1.0f, warp_sum(part));
+    for (int j = 0; j < per; j++) p[j] = __fmul_rn(p[j], sinv);
+    unsigned taken = 0;  // bit j: expert lane + 32j chosen
+    float wk[8];
+    int ik[8];
+    float wsum = 0.f;
+    for (int k = 0; k < K; k++) {
+        float bv = -1e30f;
+        int bi = 0x7fffffff;
+        for (int j = 0; j < per; j++) {
+            const int e = lane + 32 * j;
+            if (e < E && !((taken >> j) & 1u) && p[j] > bv) {
+                bv = p[j];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        wk[k] = bv;
+        ik[k] = bi;
+        wsum = __fadd_rn(wsum, bv);
+    }
+    if (lane == 0) {
+        for (int k = 0; k < K; k++) {
+            idx[(size_t)s * K + k] = ik[k];
+            wt[(size_t)s * K + k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
+            atomicAdd(&counts[ik[k]], 1);
+        }
+    }
+}
+
+// Segment starts of the expert-sorted rows, cursors, and the tile lists of
+// both GEMM stages (shared-expert tiles first, then routed ones). One block.
+__global__ void __launch_bounds__(256) pf_plan_kernel(int *counts, int E, int M, int I, int S, int H, int *seg,
+                                                      int *cursor, PfTile *gu_tiles, int *n_gu, PfTile *dn_tiles,
+                                                      int *n_dn) {
+    __shared__ int cnt[PF_MAXE], mt[PF_MAXE], seg_s[PF_MAXE], mto[PF_MAXE + 1];
+    const int t = threadIdx.x;
+    if (t < E) {
+        cnt[t] = counts[t];
+        mt[t] = (cnt[t] + PF_BM - 1) / PF_BM;
+    }
+    __syncthreads();
+    if (t == 0) {
+        int a = 0, b = 0;
+        for (int e = 0; e < E; e++) {
+            seg_s[e] = a;
+            mto[e] = b;
+            a += cnt[e];
+            b += mt[e];
+        }
+        mto[E] = b;
+    }
+    __syncthreads();
+    const int mts = (M + PF_BM - 1) / PF_BM;
+    const int gu_nt_r = I / 128, gu_nt_s = S / 128, dn_nt = H / PF_BN;
+    const int sh_gu = mts * gu_nt_s, sh_dn = mts * dn_nt;
+    for (int i = t; i < sh_gu; i += blockDim.x) {
+        const int m = i / gu_nt_s, n = i - m * gu_nt_s;
+        gu_tiles[i] = PfTile{1, 0, m * PF_BM, min(PF_BM, M - m * PF_BM), n * 128};
+    }
+    for (int i = t; i < sh_dn; i += blockDim.x) {
+        const int m = i / dn_nt, n = i - m * dn_nt;
+        dn_tiles[i] = PfTile{1, 0, m * PF_BM, min(PF_BM, M - m * PF_BM), n * PF_BN};
+    }
+    if (t < E) {
+        seg[t] = seg_s[t];
+        cursor[t] = 0;
+        for (int m = 0; m < mt[t]; m++) {
+            const int r0 = seg_s[t] + m * PF_BM, rows = min(PF_BM, cnt[t] - m * PF_BM);
+            for (int n = 0; n < gu_nt_r; n++)
+                gu_tiles[sh_gu + (mto[t] + m) * gu_nt_r + n] = PfTile{0, t, r0, rows, n * 128};
+            for (int n = 0; n < dn_nt; n++)
+                dn_tiles[sh_dn + (mto[t] + m) * dn_nt + n] = PfTile{0, t, r0, rows, n * PF_BN};
+        }
+        counts[t] = 0;  // ready for the next layer
+    }
+    if (t == 0) {
+        *n_gu = sh_gu + mto[E] * gu_nt_r;
+        *n_dn = sh_dn + mto[E] * dn_nt;
+    }
+}
+
+// Copies each token's split row to the segment of each of its experts.
+__global__ void __launch_bounds__(256) pf_scatter_kernel(int M, int H, int K, const int *idx, const int *seg,
+                                                         int *cursor, const uint16_t *xn_hi, const uint16_t *xn_lo,
+                                                         uint16_t *xg_hi, uint16_t *xg_lo, int *slot_of) {
+    const int lane = threadIdx.x & 31;
+    const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (s >= M) return;
+    const int nv = H / 256;  // uint4 (8 BF16) per lane
+    uint4 hi[8], lo[8];
+    for (int i = 0; i < nv; i++) {
+        hi[i] = reinterpret_cast<const uint4 *>(xn_hi + (size_t)s * H)[lane + 32 * i];
+        lo[i] = reinterpret_cast<const uint4 *>(xn_lo + (size_t)s * H)[lane + 32 * i];
+    }
+    for (int k = 0; k < K; k++) {
+        int pos = 0;
+        if (lane == 0) {
+            const int e = idx[(size_t)s * K + k];
+            pos = seg[e] + atomicAdd(&cursor[e], 1);
+            slot_of[pos] = s * K + k;
+        }
+        pos = __shfl_sync(0xffffffffu, pos, 0);
+        for (int i = 0; i < nv; i++) {
+            reinterpret_cast<uint4 *>(xg_hi + (size_t)pos * H)[lane + 32 * i] = hi[i];
+            reinterpret_cast<uint4 *>(xg_lo + (size_t)pos * H)[lane + 32 * i] = lo[i];
+        }
+    }
+}
+
+// x[s] += (sum over the token's experts in ascending order of w_k * y_k) +
+// shared[s]  (ds_moe_decoder.c:785-800).
+__global__ void __launch_bounds__(256) pf_combine_kernel(float *x, int M, int H, int K, const int *idx, const float *wt,
+                                                         const float *yr, const float *ys) {
+    const int lane = threadIdx.x & 31;
+    const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (s >= M) return;
+    int ord[8];
+    for (int k = 0; k < K; k++) ord[k] = k;
+    for (int a = 1; a < K; a++)  // insertion sort of the slots by expert
+        for (int b = a; b > 0 && idx[(size_t)s * K + ord[b]] < idx[(size_t)s * K + ord[b - 1]]; b--) {
+            int tmp = ord[b];
+            ord[b] = ord[b - 1];
+            ord[b - 1] = tmp;
+        }
+    const int nv = H / 128;
+    for (int i = 0; i < nv; i++) {
+        const int c = 4 * (lane + 32 * i);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < K; j++) {
+            const int k = ord[j];
+            const float w = wt[(size_t)s * K + k];
+            const float4 y = *reinterpret_cast<const float4 *>(yr + ((size_t)s * K + k) * H + c);
+            acc.x = __fmaf_rn(w, y.x, acc.x);
+            acc.y = __fmaf_rn(w, y.y, acc.y);
+            acc.z = __fmaf_rn(w, y.z, acc.z);
+            acc.w = __fmaf_rn(w, y.w, acc.w);
+        }
+        const float4 sh = *reinterpret_cast<const float4 *>(ys + (size_t)s * H + c);
+        float4 *xp = reinterpret_cast<float4 *>(x + (size_t)s * H + c);
+        float4 xv = *xp;
+        xv.x = __fadd_rn(xv.x, __fadd_rn(acc.x, sh.x));
+        xv.y = __fadd_rn(xv.y, __fadd_rn(acc.y, sh.y));
+        xv.z = __fadd_rn(xv.z, __fadd_rn(acc.z, sh.z));
+        xv.w = __fadd_rn(xv.w, __fadd_rn(acc.w, sh.w));
+        *xp = xv;
+    }
+}
+
+}  // namespace ds
+
+using namespace ds;
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+struct PfWork {
+    int cap_m = 0, H = 0, I = 0, S = 0, E = 0, K = 0;
+    uint16_t *xn_hi = nullptr, *xn_lo = nullptr, *xg_hi = nullptr, *xg_lo = nullptr;
+    uint16_t *hg_hi = nullptr, *hg_lo = nullptr, *hs_hi = nullptr, *hs_lo = nullptr;
+    float *yr = nullptr, *ys = nullptr, *logits = nullptr, *wt = nullptr;
+    int *idx = nullptr, *counts = nullptr, *seg = nullptr, *cursor = nullptr, *slot_of = nullptr, *nt = nullptr;
+    PfTile *gu_tiles = nullptr, *dn_tiles = nullptr;
+    unsigned *err = nullptr;  // set by a device-side wait that gave up
+    int max_gu = 0, max_dn = 0;
+};
+
+void prefill_release(ds_cuda_ctx *c) {
+    PfWork *w = (PfWork *)c->prefill;
+    if (!w) return;
+    void *ptrs[] = {w->xn_hi, w->xn_lo, w->xg_hi, w->xg_lo, w->hg_hi, w->hg_lo, w->hs_hi, w->hs_lo, w->yr,
+                    w->ys, w->logits, w->wt, w->idx, w->counts, w->seg, w->cursor, w->slot_of, w->nt,
+                    w->gu_tiles, w->dn_tiles, w->err};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    delete w;
+    c->prefill = nullptr;
+}
+
+static int pf_workspace(ds_cuda_ctx *c, int M, int H, int I, int S, int E, int K, cudaStream_t st, PfWork **out) {
+    PfWork *w = (PfWork *)c->prefill;
+    if (w && w->cap_m >= M && w->H == H && w->I == I && w->S == S && w->E == E && w->K == K) {
+        *out = w;
+        return DS_CUDA_OK;
+    }
+    prefill_release(c);
+    w = new PfWork();
+    c->prefill = w;
+    w->cap_m = M;
+    w->H = H, w->I = I, w->S = S, w->E = E, w->K = K;
+    const size_t P = (size_t)M * K;
+    const int mts = (M + PF_BM - 1) / PF_BM;
+    // routed tiles: sum_e ceil(n_e / 128) <= P / 128 + E
+    const size_t mt_r = P / PF_BM + E;
+    w->max_gu = (int)(mts * (S / 128) + mt_r * (I / 128));
+    w->max_dn = (int)(mts * (H / PF_BN) + mt_r * (H / PF_BN));
+    // A planes get one tile of slack rows so a tile never starts past the end
+    const size_t PR = P + PF_BM;
+    struct A {
+        void **p;
+        size_t bytes;
+    } allocs[] = {
+        {(void **)&w->xn_hi, (size_t)(M + PF_BM) * H * 2}, {(void **)&w->xn_lo, (size_t)(M + PF_BM) * H * 2},
+        {(void **)&w->xg_hi, PR * H * 2},                  {(void **)&w->xg_lo, PR * H * 2},
+        {(void **)&w->hg_hi, PR * I * 2},                  {(void **)&w->hg_lo, PR * I * 2},
+        {(void **)&w->hs_hi, (size_t)(M + PF_BM) * S * 2}, {(void **)&w->hs_lo, (size_t)(M + PF_BM) * S * 2},
+        {(void **)&w->yr, P * H * 4},                      {(void **)&w->ys, (size_t)M * H * 4},
+        {(void **)&w->logits, (size_t)M * E * 4},          {(void **)&w->wt, P * 4},
+        {(void **)&w->idx, P * 4},                         {(void **)&w->counts, (size_t)E * 4},
+        {(void **)&w->seg, (size_t)E * 4},                 {(void **)&w->cursor, (size_t)E * 4},
+        {(void **)&w->slot_of, PR * 4},                    {(void **)&w->nt, 2 * 4},
+        {(void **)&w->gu_tiles, (size_t)w->max_gu * sizeof(PfTile)},
+        {(void **)&w->dn_tiles, (size_t)w->max_dn * sizeof(PfTile)},
+        {(void **)&w->err, 4},
+    };
+    for (auto &a : allocs) {
+        cudaError_t e = cudaMalloc(a.p, a.bytes);
+        if (e != cudaSuccess) {
+            prefill_release(c);
+            return ctx_cuda(c, e, "prefill workspace");
+        }
+    }
+    // stream-ordered with the kernels (the context's stream does not
+    // synchronise with the legacy default stream)
+    cudaMemsetAsync(w->counts, 0, (size_t)E * 4, st);
+    cudaMemsetAsync(w->err, 0, 4, st);
+    // padding rows of the A planes stay zero (TMA reads them for partial tiles)
+    cudaMemsetAsync(w->xn_hi, 0, (size_t)(M + PF_BM) * H * 2, st);
+    cudaMemsetAsync(w->xn_lo, 0, (size_t)(M + PF_BM) * H * 2, st);
+    cudaMemsetAsync(w->hs_hi, 0, (size_t)(M + PF_BM) * S * 2, st);
+    cudaMemsetAsync(w->hs_lo, 0, (size_t)(M + PF_BM) * S * 2, st);
+    *out = w;
+    return DS_CUDA_OK;
+}
+
+// cuTensorMapEncodeTiled, looked up through the runtime so the library does
+// not link the driver library directly (it loads where no driver exists).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// BF16 row-major [rows x cols] as a 2-D tensor map with 64 x box_rows boxes,
+// 128-byte swizzle (the UMMA K-major canonical layout).
+static bool pf_map(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)PF_BK, box_rows};
+    cuuint32_t es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+                                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// One MoE prefill layer on device buffers. d_x [M x H] is updated in place.
+int prefill_moe_enqueue(ds_cuda_ctx *c, int H, int I, int S, int E, int K, float eps, const float *d_norm,
+                        const uint16_t *d_router, const uint16_t *d_block, const uint16_t *d_down,
+                        const uint16_t *d_sdown, float *d_x, int M, const float *d_logits, int *d_idx_out,
+                        float *d_w_out, cudaStream_t st) {
+    if (M <= 0) return DS_CUDA_OK;
+    if (H % 256 || I % 128 || S % 128 || E <= 0 || E > PF_MAXE || K <= 0 || K > 8 || K > E || H > 2048)
+        return ctx_fail(c, DS_CUDA_EINVAL, "prefill_moe: unsupported shape (H %% 256, I %% 128, S %% 128, "
+                                           "E <= 256, top_k <= 8, H <= 2048 required)");
+    if (!d_logits && !d_router) return ctx_fail(c, DS_CUDA_EINVAL, "prefill_moe: no router weights and no logits");
+    PfWork *w;
+    int rc = pf_workspace(c, M, H, I, S, E, K, st, &w);
+    if (rc < 0) return rc;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(pf_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+        cudaFuncSetAttribute(pf_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+        attr = true;
+    }
+    const size_t P = (size_t)M * K;
+    const int wblocks = (M + 7) / 8;
+    pf_norm_route_kernel<<<wblocks, 256, 0, st>>>(d_x, d_norm, eps, M, H, d_logits, d_router, w->logits, E, K,
+                                                  c->renorm, w->xn_hi, w->xn_lo, w->idx, w->wt, w->counts);
+    pf_plan_kernel<<<1, 256, 0, st>>>(w->counts, E, M, I, S, H, w->seg, w->cursor, w->gu_tiles, w->nt,
+                                      w->dn_tiles, w->nt + 1);
+    pf_scatter_kernel<<<wblocks, 256, 0, st>>>(M, H, K, w->idx, w->seg, w->cursor, w->xn_hi, w->xn_lo, w->xg_hi,
+                                               w->xg_lo, w->slot_of);
+    const int grid = c->sm_count;
+    // gate/up (+SwiGLU): routed A = expert-sorted rows, shared A = all rows;
+    // B = the expert block [E*2I + 2S rows x H] for both
+    PfGemm g;
+    memset(&g, 0, sizeof g);
+    const uint64_t brows = (uint64_t)E * 2 * I + 2 * (uint64_t)S;
+    bool ok = pf_map(&g.a_hi[0], w->xg_hi, H, P + PF_BM, PF_BM) && pf_map(&g.a_lo[0], w->xg_lo, H, P + PF_BM, PF_BM) &&
+              pf_map(&g.a_hi[1], w->xn_hi, H, M + PF_BM, PF_BM) && pf_map(&g.a_lo[1], w->xn_lo, H, M + PF_BM, PF_BM) &&
+              pf_map(&g.b[0], d_block, H, brows, 128) && pf_map(&g.b[1], d_block, H, brows, 128);
+    if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill_moe: tensor map encoding failed");
+    g.tiles = w->gu_tiles;
+    g.n_tiles = w->nt;
+    g.k_blocks[0] = g.k_blocks[1] = H / PF_BK;
+    g.b_base[0] = 0;
+    g.b_group_rows[0] = 2 * I;
+    g.b_half[0] = I;
+    g.b_base[1] = E * 2 * I;
+    g.b_group_rows[1] = 0;
+    g.b_half[1] = S;
+    g.h_hi[0] = w->hg_hi;
+    g.h_lo[0] = w->hg_lo;
+    g.h_ld[0] = I;
+    g.h_hi[1] = w->hs_hi;
+    g.h_lo[1] = w->hs_lo;
+    g.h_ld[1] = S;
+    g.err = w->err;
+    pf_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, st>>>(g);
+    // down: routed A = SwiGLU rows [P x I], shared A = [M x S]
+    PfGemm d;
+    memset(&d, 0, sizeof d);
+    ok = pf_map(&d.a_hi[0], w->hg_hi, I, P + PF_BM, PF_BM) && pf_map(&d.a_lo[0], w->hg_lo, I, P + PF_BM, PF_BM) &&
+         pf_map(&d.a_hi[1], w->hs_hi, S, M + PF_BM, PF_BM) && pf_map(&d.a_lo[1], w->hs_lo, S, M + PF_BM, PF_BM) &&
+         pf_map(&d.b[0], d_down, I, (uint64_t)E * H, PF_BN) && pf_map(&d.b[1], d_sdown, S, H, PF_BN);
+    if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill_moe: tensor map encoding failed");
+    d.tiles = w->dn_tiles;
+    d.n_tiles = w->nt + 1;
+    d.k_blocks[0] = I / PF_BK;
+    d.k_blocks[1] = S / PF_BK;
+    d.b_base[0] = 0;
+    d.b_group_rows[0] = H;
+    d.b_base[1] = 0;
+    d.b_group_rows[1] = 0;
+    d.y[0] = w->yr;
+    d.y[1] = w->ys;
+    d.slot_of = w->slot_of;
+    d.y_ld = H;
+    d.err = w->err;
+    pf_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, st>>>(d);
+    pf_combine_kernel<<<wblocks, 256, 0, st>>>(d_x, M, H, K, w->idx, w->wt, w->yr, w->ys);
+    if (d_idx_out) cudaMemcpyAsync(d_idx_out, w->idx, P * 4, cudaMemcpyDeviceToDevice, st);
+    if (d_w_out) cudaMemcpyAsync(d_w_out, w->wt, P * 4, cudaMemcpyDeviceToDevice, st);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return ctx_cuda(c, e, "prefill_moe launch");
+    return DS_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+static int pf_layer_ptrs(ds_cuda_ctx *c, const ds_cuda_decoder_config_t *g, const ds_cuda_layer_weights_t *L,
+                         bool need_router, const float **norm, const uint16_t **router, const uint16_t **block,
+                         const uint16_t **down, const uint16_t **sdown) {
+    const size_t H = g->hidden, I = g->moe_inter, S = (size_t)g->n_shared * g->moe_inter, E = g->n_experts;
+    *norm = (const float *)ctx_lookup(c, L->post_attn_norm, H * 4, true);
+    *router = need_router ? (const uint16_t *)ctx_lookup(c, L->router, E * H * 2, true) : nullptr;
+    *block = (const uint16_t *)ctx_lookup(c, L->expert_block, (E * 2 * I + 2 * S) * H * 2, true);
+    *down = (const uint16_t *)ctx_lookup(c, L->down, E * H * I * 2, true);
+    *sdown = (const uint16_t *)ctx_lookup(c, L->shared_down, H * S * 2, true);
+    if (!*norm || (need_router && !*router) || !*block || !*down || !*sdown)
+        return ctx_fail(c, DS_CUDA_EINVAL, "prefill_moe: a weight array is missing or could not be registered");
+    return DS_CUDA_OK;
+}
+
+static int pf_check(ds_cuda_ctx *c) {
+    PfWork *w = (PfWork *)c->prefill;
+    if (!w) return DS_CUDA_OK;
+    unsigned e = 0;
+    cudaError_t ce = cudaMemcpy(&e, w->err, 4, cudaMemcpyDeviceToHost);
+    if (ce != cudaSuccess) return ctx_cuda(c, ce, "prefill error flag");
+    if (e) {
+        cudaMemsetAsync(w->err, 0, 4, c->stream);
+        return ctx_fail(c, DS_CUDA_ETIMEOUT, "prefill_moe: a bounded device-side wait gave up");
+    }
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_prefill_moe_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
+                                       const ds_cuda_layer_weights_t *layer, float *d_x, int n_tokens,
+                                       const float *d_logits, int *d_top_idx, float *d_top_w, void *stream) {
+    if (!c || !c->ok || !cfg || !layer || (!d_x && n_tokens > 0) || n_tokens < 0) return DS_CUDA_EINVAL;
+    cudaSetDevice(c->device);
+    const float *norm;
+    const uint16_t *router, *block, *down, *sdown;
+    int rc = pf_layer_ptrs(c, cfg, layer, d_logits == nullptr, &norm, &router, &block, &down, &sdown);
+    if (rc < 0) return rc;
+    return prefill_moe_enqueue(c, cfg->hidden, cfg->moe_inter, cfg->n_shared * cfg->moe_inter, cfg->n_experts,
+                               cfg->top_k, cfg->rms_eps, norm, router, block, down, sdown, d_x, n_tokens, d_logits,
+                               d_top_idx, d_top_w, stream ? (cudaStream_t)stream : c->stream);
+}
+
+extern "C" int ds_cuda_prefill_moe(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
+                                   const ds_cuda_layer_weights_t *layer, float *x, int n_tokens, const float *logits,
+                                   int *top_idx, float *top_w) {
+    if (!c || !c->ok || !cfg || !layer || (!x && n_tokens > 0) || n_tokens < 0) return DS_CUDA_EINVAL;
+    if (n_tokens == 0) return DS_CUDA_OK;
+    cudaSetDevice(c->device);
+    const size_t M = n_tokens, H = cfg->hidden, E = cfg->n_experts, K = cfg->top_k;
+    float *dx = nullptr, *dl = nullptr, *dw = nullptr;
+    int *di = nullptr;
+    cudaStream_t st = c->stream;
+    int rc = DS_CUDA_OK;
+    cudaError_t e = cudaMalloc(&dx, M * H * 4);
+    if (e == cudaSuccess && logits) e = cudaMalloc(&dl, M * E * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&di, M * K * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&dw, M * K * 4);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dx, x, M * H * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && logits) e = cudaMemcpyAsync(dl, logits, M * E * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) rc = ctx_cuda(c, e, "prefill_moe staging");
+    if (rc == DS_CUDA_OK) rc = ds_cuda_prefill_moe_dev(c, cfg, layer, dx, n_tokens, dl, di, dw, st);
+    if (rc == DS_CUDA_OK) {
+        e = cudaMemcpyAsync(x, dx, M * H * 4, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess && top_idx) e = cudaMemcpyAsync(top_idx, di, M * K * 4, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess && top_w) e = cudaMemcpyAsync(top_w, dw, M * K * 4, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        rc = e == cudaSuccess ? pf_check(c) : ctx_cuda(c, e, "prefill_moe");
+    }
+    cudaFree(dx);
+    cudaFree(dl);
+    cudaFree(di);
+    cudaFree(dw);
+    return rc;
+}
+
+extern "C" int ds_cuda_prefill_check(ds_cuda_ctx_t *c) {
+    if (!c || !c->ok) return DS_CUDA_EINVAL;
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return ctx_cuda(c, e, "prefill_check");
+    return pf_check(c);
+}

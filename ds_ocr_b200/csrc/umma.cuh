@@ -1,0 +1,94 @@
+// umma.cuh — sm_100a tensor-core building blocks: tiled TMA loads, the
+// tcgen05 MMA (kind::f16, BF16 operands, F32 accumulator in tensor memory),
+// tensor-memory allocation and loads, and the shared-memory / instruction
+// descriptors those take. Bit layouts follow the PTX ISA descriptions of the
+// tcgen05 matrix and instruction descriptors (the same layouts CUTLASS's
+// cute/arch/mma_sm100_desc.hpp documents).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include "common.cuh"
+
+namespace ds {
+
+// 2-D tiled TMA load (no multicast) of box {x .. x+bx, y .. y+by} into
+// shared memory, completing on `bar`. x * element size must be a multiple
+// of 16 bytes (callers pass x as a multiple of 64 BF16 elements).
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major BF16 tile stored in the
+// 128-byte-swizzled canonical layout (rows of 64 elements = 128 B, 8-row
+// atoms of 1024 B, atoms stacked along M/N). Fields: start address >> 4
+// (bits 0-13), leading byte offset >> 4 (16-29; 1 for swizzled K-major),
+// stride byte offset >> 4 (32-45; 1024 B between 8-row atoms), version 1
+// (46-47), base offset 0 (tiles are 1024-byte aligned), layout type 2 =
+// 128-byte swizzle (61-63).
+__device__ __forceinline__ uint64_t sw128_desc(const void *smem_tile) {
+    const uint64_t start = (smem_u32(smem_tile) >> 4) & 0x3fffu;
+    return start | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor for kind::f16 with BF16 A and B (both K-major) and
+// an F32 accumulator: c_format = 1 (bits 4-5), a_format = b_format = 1
+// (bits 7-9, 10-12), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, one CTA, issued by a single thread.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05 operation this thread issued so
+// far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Tensor-memory allocation (whole warp): writes the base address to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(dst)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+// (The load and its wait are one asm statement so no use of the outputs can
+// be scheduled before the wait.)
+// 32 consecutive F32 columns of this thread's tensor-memory lane (warp w of
+// a warpgroup reads lanes 32*(w%4) .. +31; taddr carries the lane in bits
+// 16-31 and the column in bits 0-15).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr) : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace ds

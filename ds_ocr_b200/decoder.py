@@ -73,7 +73,7 @@ def quantize_int8(model, ctx=None):
 
 
 class Decoder:
-    ENGINE_PERSISTENT, ENGINE_GRAPH = 0, 1
+    ENGINE_GRAPH, ENGINE_PERSISTENT = 0, 1
 
     def __init__(self, model, ctx=None, kv_max=1024, use_int8=False, engine=0):
         self.ctx = ctx or Context(0)

@@ -272,6 +272,35 @@ int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *ctx, int model, int n_steps, voi
 int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *ctx, int model);
 
 /* ---------------------------------------------------------------------
+ * Batched MoE prefill — the MoE block of ds_decoder_prefill for n tokens
+ * (ds_moe_decoder.c:630-809): per token RMSNorm(post_attn_norm), router
+ * softmax/top-k (fast exp, strict '>', weights = probabilities unless the
+ * renorm numerics flag is set), shared expert and routed experts grouped by
+ * expert, then x += routed + shared. The reference runs F32 sgemm on
+ * widened BF16 weights; here the GEMMs run on the tensor cores with the
+ * activations split into two BF16 planes (F32-class accuracy).
+ * Shapes: hidden % 256 == 0, moe_inter and n_shared*moe_inter % 128 == 0,
+ * n_experts <= 256, top_k <= 8.
+ * Weights are the layer's host pointers (registered on first use, as
+ * elsewhere in this ABI); router may be NULL when logits are given.
+ * logits [n_tokens x n_experts] (optional) replace xn W_r^T (the scores
+ * before the softmax). top_idx / top_w [n_tokens x top_k] (optional)
+ * receive the routing.
+ * --------------------------------------------------------------------- */
+int ds_cuda_prefill_moe(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
+                        const ds_cuda_layer_weights_t *layer, float *x, int n_tokens, const float *logits,
+                        int *top_idx, float *top_w);
+/* Same on device buffers, enqueued on `stream` (NULL: the context's stream);
+ * no synchronisation. A device-side wait that gave up is reported by the
+ * next ds_cuda_prefill_check. */
+int ds_cuda_prefill_moe_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
+                            const ds_cuda_layer_weights_t *layer, float *d_x, int n_tokens, const float *d_logits,
+                            int *d_top_idx, float *d_top_w, void *stream);
+/* Synchronises the context's stream and reports DS_CUDA_ETIMEOUT if a
+ * prefill kernel's bounded wait gave up since the last check. */
+int ds_cuda_prefill_check(ds_cuda_ctx_t *ctx);
+
+/* ---------------------------------------------------------------------
  * Host-side synthetic data (seeded, counter-based: value i of a stream
  * depends only on (seed, i)); used to build the benchmark workloads.
  * normal_bf16: RNE-rounded N(mean, std); normal_f32: F32 N(mean, std);

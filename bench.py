@@ -1,7 +1,7 @@
 """Benchmark of the ds-ocr MoE-decoder hot path on B200.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                [--workload decode|moe_layer|lm_head]
+                [--workload decode|moe_layer|prefill] [--engine 0|1]
 
 Prints ONE JSON line (rank 0). Under torchrun (N > 1) every rank runs its own
 independent replica of the workload (weak scaling: decode streams / tokens
@@ -12,7 +12,8 @@ Workloads (synthetic random-init weights):
             batch 1, 662-token BF16 KV prefix        (headline)
   moe_layer config 0: one MoE layer, one token; steps rotate over 11 layers'
             weights (5.0 GB) so no step finds its experts in L2
-  lm_head   config 1: argmax LM head 129280 x 1280, batch 1
+  prefill   config 4: batched MoE prefill, 3328 tokens through the 11 MoE
+            layers (router logits overridden, skewed routing)
 --impl reference times the reference's own CPU code (compiled unmodified
 into oracle/_ref/libdsref.so) on the same workload, on this host's cores.
 """
@@ -407,13 +408,155 @@ def ref_decode_time(model, ks, vs, threads, budget_s, max_steps):
     return n / t_total, n
 
 
+# ---------------------------------------------------------------------------
+# Batched MoE prefill (config 4)
+# ---------------------------------------------------------------------------
+PF_TOKENS = 3328
+PF_LAYERS = 11
+PF_FLOPS_LAYER = PF_TOKENS * (6 * 6881280 + 13762560)        # routed + shared, per MoE layer
+PF_FLOPS_GU_LAYER = PF_TOKENS * (6 * 2 * 1792 * 1280 + 2 * 3584 * 1280)
+
+
+def prefill_inputs(d):
+    """x [3328 x 1280] N(0,1) (seed 5); per layer l = 1..11 the router logits
+    N(0,1) (seed 600+l) plus a per-expert bias N(0,0.5) (seed 700+l), which
+    replace xn W_r^T and give the skewed routing of config 4."""
+    from ds_ocr_b200 import synth
+    x = synth.normal_f32((PF_TOKENS, d.hidden), 5)
+    logits = []
+    for l in range(1, PF_LAYERS + 1):
+        lg = synth.normal_f32((PF_TOKENS, d.n_experts), 600 + l)
+        lg += 0.5 * synth.normal_f32(d.n_experts, 700 + l)[None, :]
+        logits.append(lg)
+    return x, logits
+
+
+def prefill_config():
+    return {"workload": "config4_prefill_moe", "model": "DeepSeek3B-MoE MoE layers 1-11 (random init)",
+            "tokens": PF_TOKENS, "layers": PF_LAYERS, "hidden": 1280, "experts": 64, "top_k": 6,
+            "routing": "logits N(0,1) + per-expert bias N(0,0.5) (attention not included)",
+            "gemm": "tcgen05 split-BF16 activations x BF16 weights, F32 accumulate",
+            "l2": "each step streams 5.0 GB of expert weights and 0.5 GB of activations (> 126 MB L2)"}
+
+
+def run_ours_prefill(args, rank, world, pg, model):
+    import torch
+    from ds_ocr_b200 import cuda
+    from ds_ocr_b200.prefill import Prefill
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = cuda.Context(local if world > 1 else 0)
+    d = model.d
+    pf = Prefill(d, ctx)
+    x, logits = prefill_inputs(d)
+    layers = model.layers[1:1 + PF_LAYERS]
+    st = torch.cuda.ExternalStream(ctx.stream)
+    with torch.cuda.stream(st):
+        dx0 = torch.from_numpy(x).cuda()
+        dx = dx0.clone()
+        dlg = [torch.from_numpy(l).cuda() for l in logits]
+    st.synchronize()
+
+    def step():
+        with torch.cuda.stream(st):
+            dx.copy_(dx0)
+        for lw, lg in zip(layers, dlg):
+            pf.moe_layer_dev(lw, dx.data_ptr(), PF_TOKENS, lg.data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    pf.check()
+    barrier(pg)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(st)
+        for _ in range(args.steps):
+            step()
+        ev1.record(st)
+        ev1.synchronize()
+    pf.check()
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), pg)
+    value = world * PF_TOKENS * args.steps / (ms_max / 1e3)
+
+    # per-stage device times (one extra, untimed pass): the gate/up GEMM is
+    # the dominant kernel
+    pf.timing(True)
+    stages = np.zeros(6)
+    with torch.cuda.stream(st):
+        dx.copy_(dx0)
+    for lw, lg in zip(layers, dlg):
+        pf.moe_layer_dev(lw, dx.data_ptr(), PF_TOKENS, lg.data_ptr())
+        stages += pf.stage_ms()
+    pf.timing(False)
+    stages /= len(layers)
+
+    # e2e: the host-pointer API per layer (x and logits copied in, x and the
+    # routing copied out, as a host caller of ds_cuda_prefill_moe does)
+    n_e2e = max(1, min(args.steps, 3))
+    xs = x.copy()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.synchronize()
+    t0.record(st)
+    for _ in range(n_e2e):
+        xs[:] = x
+        for lw, lg in zip(layers, logits):
+            pf.moe_layer(lw, xs, lg)
+    t1.record(st)
+    t1.synchronize()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1), pg)
+    e2e = world * PF_TOKENS * n_e2e / (e2e_ms / 1e3)
+    pk = peaks()
+    peak_t = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    gu_ach = PF_FLOPS_GU_LAYER / (stages[3] / 1e3) / 1e12
+    step_ach = PF_FLOPS_LAYER * PF_LAYERS * args.steps / (ms_max / 1e3) / 1e12
+    res = {
+        "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
+        "metric": "MoE prefill tokens/s (3328 tokens x 11 MoE layers, 64 experts top-6 + 2 shared)",
+        "unit": "tokens/s", "dtype": "bf16 weights, f32 activations as two bf16 planes, f32 accumulate",
+        "e2e": {"value": e2e, "unit": "tokens/s",
+                "h2d_bytes_per_step": PF_LAYERS * PF_TOKENS * (d.hidden + d.n_experts) * 4,
+                "d2h_bytes_per_step": PF_LAYERS * PF_TOKENS * (d.hidden + 2 * d.top_k) * 4},
+        "gpu_launches": 6 * PF_LAYERS * args.steps, "config": prefill_config(),
+        "roofline": {"bound": "tensor", "achieved": gu_ach, "peak": peak_t, "unit": "TFLOP/s",
+                     "frac": gu_ach / peak_t, "traffic": None,
+                     "kernel": "pf_gemm_kernel<0> (gate/up + SwiGLU), 122.1 GFLOP algorithmic per layer; "
+                               "the split-BF16 A operand doubles the tensor work (not counted)",
+                     "kernel_us": stages[3] * 1e3, "peak_source": pk["source"] + " (sustained bf16)"},
+        "step_roofline": {"bound": "tensor", "achieved": step_ach, "peak": peak_t, "unit": "TFLOP/s",
+                          "frac": step_ach / peak_t, "flops_per_step": PF_FLOPS_LAYER * PF_LAYERS,
+                          "stage_us": dict(zip(["norm_route", "plan", "scatter", "gemm_gate_up", "gemm_down",
+                                                "combine"], [round(float(s) * 1e3, 1) for s in stages]))},
+    }
+    ctx.close()
+    return res
+
+
+def ref_prefill_time(model, threads, budget_s):
+    """The reference's prefill MoE block (its own kernels and OpenBLAS sgemm,
+    compiled unmodified) on the config-4 inputs, one layer per call, until
+    about budget_s seconds have passed. Returns (tokens/s through 11 layers,
+    layers run)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    x, logits = prefill_inputs(model.d)
+    R = O.RefDecoder(model, kv_max=8, threads=threads)
+    n, t_total = 0, 0.0
+    xs = x.copy()
+    while t_total < budget_s and n < PF_LAYERS:
+        t = time.perf_counter()
+        R.prefill_moe(1 + n, xs, logits[n])
+        t_total += time.perf_counter() - t
+        n += 1
+    R.close()
+    return PF_TOKENS * n / (t_total * PF_LAYERS), n
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=224)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer", "prefill"])
     ap.add_argument("--engine", type=int, default=0, choices=[0, 1],
                     help="decode engine: 0 CUDA graph of per-phase kernels, 1 persistent kernel")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
@@ -433,6 +576,11 @@ def main():
             v, n = ref_decode_time(model, ks, vs, T, max(args.cpu_budget, 1.0), max_steps=args.steps)
             metric = "decode tokens/s (greedy, batch 1 per GPU, 12-layer DeepSeek3B-MoE, 662-token KV prefix)"
             cfg, sample = decode_config(1024), f"{n} greedy ds_decoder_forward steps from position 663"
+        elif args.workload == "prefill":
+            from ds_ocr_b200 import synth
+            v, n = ref_prefill_time(synth.Model(), T, max(args.cpu_budget, 1.0))
+            metric = "MoE prefill tokens/s (3328 tokens x 11 MoE layers, 64 experts top-6 + 2 shared)"
+            cfg, sample = prefill_config(), f"{n} of 11 MoE layers of the prefill block at 3328 tokens"
         else:
             wl = MoeLayerWorkload()
             v, n = ref_moe_time(wl, T, max(args.cpu_budget, 1.0))
@@ -448,6 +596,10 @@ def main():
     if args.workload == "decode":
         model, ks, vs = build_decode_model()
         res = run_ours_decode(args, rank, world, pg, model, ks, vs)
+    elif args.workload == "prefill":
+        from ds_ocr_b200 import synth
+        model = synth.Model()
+        res = run_ours_prefill(args, rank, world, pg, model)
     else:
         res = run_ours_moe(args, rank, world, pg)
     if rank != 0:
@@ -464,6 +616,9 @@ def main():
             if args.workload == "decode":
                 v, n = ref_decode_time(model, ks, vs, T, args.cpu_budget, max_steps=64)
                 sample = f"{n} greedy ds_decoder_forward steps from position 663"
+            elif args.workload == "prefill":
+                v, n = ref_prefill_time(model, T, args.cpu_budget)
+                sample = f"{n} of 11 MoE layers of the prefill block at 3328 tokens"
             else:
                 wl = MoeLayerWorkload()
                 v, n = ref_moe_time(wl, T, args.cpu_budget)

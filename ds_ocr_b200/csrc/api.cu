@@ -167,6 +167,8 @@ extern "C" void ds_cuda_free(ds_cuda_ctx_t *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     ctx_release_models(c);
     prefill_release(c);
+    for (auto &e : c->prefill_ev)
+        if (e) cudaEventDestroy(e);
     for (auto &kv : c->regs) cudaFree(kv.second.dev);
     void *bufs[] = {c->d_tickets, c->d_slots, c->d_tok, c->d_val, c->d_scores, c->d_idx, c->d_wt,
                     c->d_x, c->d_out, c->d_h, c->d_tmp};

@@ -39,8 +39,10 @@ struct ds_cuda_ctx {
     // pinned staging
     void *pin = nullptr;
     size_t pin_cap = 0;
-    // batched-prefill workspace (prefill.cu)
+    // batched-prefill workspace (prefill.cu) and optional per-stage timing
     void *prefill = nullptr;
+    bool prefill_timing = false;
+    cudaEvent_t prefill_ev[7] = {};
     // decoder models owned by this context
     std::map<int, DecoderModel *> models;
     int next_model = 1;

@@ -612,10 +612,17 @@ int prefill_moe_enqueue(ds_cuda_ctx *c, int H, int I, int S, int E, int K, float
     }
     const size_t P = (size_t)M * K;
     const int wblocks = (M + 7) / 8;
+    // optional stage timing: events between the six launches
+    auto mark = [&](int i) {
+        if (c->prefill_timing) cudaEventRecord(c->prefill_ev[i], st);
+    };
+    mark(0);
     pf_norm_route_kernel<<<wblocks, 256, 0, st>>>(d_x, d_norm, eps, M, H, d_logits, d_router, w->logits, E, K,
                                                   c->renorm, w->xn_hi, w->xn_lo, w->idx, w->wt, w->counts);
+    mark(1);
     pf_plan_kernel<<<1, 256, 0, st>>>(w->counts, E, M, I, S, H, w->seg, w->cursor, w->gu_tiles, w->nt,
                                       w->dn_tiles, w->nt + 1);
+    mark(2);
     pf_scatter_kernel<<<wblocks, 256, 0, st>>>(M, H, K, w->idx, w->seg, w->cursor, w->xn_hi, w->xn_lo, w->xg_hi,
                                                w->xg_lo, w->slot_of);
     const int grid = c->sm_count;
@@ -644,7 +651,9 @@ int prefill_moe_enqueue(ds_cuda_ctx *c, int H, int I, int S, int E, int K, float
     g.h_lo[1] = w->hs_lo;
     g.h_ld[1] = S;
     g.err = w->err;
+    mark(3);
     pf_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, st>>>(g);
+    mark(4);
     // down: routed A = SwiGLU rows [P x I], shared A = [M x S]
     PfGemm d;
     memset(&d, 0, sizeof d);
@@ -666,7 +675,9 @@ int prefill_moe_enqueue(ds_cuda_ctx *c, int H, int I, int S, int E, int K, float
     d.y_ld = H;
     d.err = w->err;
     pf_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, st>>>(d);
+    mark(5);
     pf_combine_kernel<<<wblocks, 256, 0, st>>>(d_x, M, H, K, w->idx, w->wt, w->yr, w->ys);
+    mark(6);
     if (d_idx_out) cudaMemcpyAsync(d_idx_out, w->idx, P * 4, cudaMemcpyDeviceToDevice, st);
     if (d_w_out) cudaMemcpyAsync(d_w_out, w->wt, P * 4, cudaMemcpyDeviceToDevice, st);
     cudaError_t e = cudaGetLastError();
@@ -756,4 +767,25 @@ extern "C" int ds_cuda_prefill_check(ds_cuda_ctx_t *c) {
     cudaError_t e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) return ctx_cuda(c, e, "prefill_check");
     return pf_check(c);
+}
+
+// Per-stage device times of prefill calls: enable, then read the last call's
+// six stage durations (norm+route, plan, scatter, gate/up GEMM, down GEMM,
+// combine) in milliseconds.
+extern "C" int ds_cuda_prefill_timing(ds_cuda_ctx_t *c, int enable) {
+    if (!c || !c->ok) return DS_CUDA_EINVAL;
+    cudaSetDevice(c->device);
+    if (enable && !c->prefill_ev[0])
+        for (auto &e : c->prefill_ev)
+            if (cudaEventCreate(&e) != cudaSuccess) return ctx_fail(c, DS_CUDA_ECUDA, "prefill_timing: events");
+    c->prefill_timing = enable != 0;
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_prefill_stage_ms(ds_cuda_ctx_t *c, float *ms6) {
+    if (!c || !c->ok || !ms6 || !c->prefill_ev[0]) return DS_CUDA_EINVAL;
+    cudaError_t e = cudaEventSynchronize(c->prefill_ev[6]);
+    for (int i = 0; i < 6 && e == cudaSuccess; i++) e = cudaEventElapsedTime(&ms6[i], c->prefill_ev[i], c->prefill_ev[i + 1]);
+    if (e != cudaSuccess) return ctx_cuda(c, e, "prefill_stage_ms");
+    return DS_CUDA_OK;
 }

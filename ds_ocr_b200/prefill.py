@@ -52,6 +52,16 @@ class Prefill:
         self.ctx.check(self.lib.ds_cuda_prefill_moe_dev(self.ctx.h, ctypes.byref(self.cfg), self._layer(lw), d_x, n,
                                                         d_logits, d_idx, d_w, stream), "prefill_moe_dev")
 
+    def timing(self, enable=True):
+        self.ctx.check(self.lib.ds_cuda_prefill_timing(self.ctx.h, int(enable)), "prefill_timing")
+
+    def stage_ms(self):
+        """The last call's stage times (ms): norm+route, plan, scatter,
+        gate/up GEMM, down GEMM, combine."""
+        out = np.zeros(6, np.float32)
+        self.ctx.check(self.lib.ds_cuda_prefill_stage_ms(self.ctx.h, _a(out)), "prefill_stage_ms")
+        return out
+
     def check(self):
         """Synchronise and raise if a prefill kernel's bounded wait gave up."""
         self.ctx.check(self.lib.ds_cuda_prefill_check(self.ctx.h), "prefill_check")

@@ -299,6 +299,12 @@ int ds_cuda_prefill_moe_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *
 /* Synchronises the context's stream and reports DS_CUDA_ETIMEOUT if a
  * prefill kernel's bounded wait gave up since the last check. */
 int ds_cuda_prefill_check(ds_cuda_ctx_t *ctx);
+/* Stage timing (no counterpart in the reference): while enabled, prefill
+ * calls record CUDA events between their six kernels; stage_ms returns the
+ * last call's durations (norm+route, plan, scatter, gate/up GEMM, down GEMM,
+ * combine) in ms[6]. */
+int ds_cuda_prefill_timing(ds_cuda_ctx_t *ctx, int enable);
+int ds_cuda_prefill_stage_ms(ds_cuda_ctx_t *ctx, float *ms);
 
 /* ---------------------------------------------------------------------
  * Host-side synthetic data (seeded, counter-based: value i of a stream

@@ -449,21 +449,40 @@ def run_ours_prefill(args, rank, world, pg, model):
     pf = Prefill(d, ctx)
     x, logits = prefill_inputs(d)
     layers = model.layers[1:1 + PF_LAYERS]
-    st = torch.cuda.ExternalStream(ctx.stream)
-    with torch.cuda.stream(st):
-        dx0 = torch.from_numpy(x).cuda()
-        dx = dx0.clone()
-        dlg = [torch.from_numpy(l).cuda() for l in logits]
+    ep = None
+    a, b = 0, PF_TOKENS
+    if world > 1:
+        # expert-parallel: this rank's token slice, experts [rank*E/G, ...)
+        from ds_ocr_b200.ep import CudaStages, ExpertParallelPrefill, token_range
+        stages = CudaStages(d, ctx)
+        ep = ExpertParallelPrefill(d, stages, pg, rank, world, stages.device)
+        a, b = token_range(PF_TOKENS, rank, world)
+        st = stages.stream
+    else:
+        st = torch.cuda.Stream()
+    # every kernel, copy and collective of a step runs on stream st (the C
+    # ABI takes its handle per call)
+    sp = st.cuda_stream
+    torch.cuda.set_stream(st)
+    dx0 = torch.from_numpy(x[a:b].copy()).cuda()
+    dx = dx0.clone()
+    dlg = [torch.from_numpy(l[a:b].copy()).cuda() for l in logits]
     st.synchronize()
 
+    def run_layers(xbuf, lgs):
+        for lw, lg in zip(layers, lgs):
+            if ep is None:
+                pf.moe_layer_dev(lw, xbuf.data_ptr(), PF_TOKENS, lg.data_ptr(), stream=sp)
+            else:
+                ep.moe_layer(lw, xbuf, lg)
+
     def step():
-        with torch.cuda.stream(st):
-            dx.copy_(dx0)
-        for lw, lg in zip(layers, dlg):
-            pf.moe_layer_dev(lw, dx.data_ptr(), PF_TOKENS, lg.data_ptr())
+        dx.copy_(dx0)
+        run_layers(dx, dlg)
 
     for _ in range(args.warmup):
         step()
+    st.synchronize()
     pf.check()
     barrier(pg)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -475,47 +494,73 @@ def run_ours_prefill(args, rank, world, pg, model):
         ev1.synchronize()
     pf.check()
     ms_max = max_over_ranks(ev0.elapsed_time(ev1), pg)
-    value = world * PF_TOKENS * args.steps / (ms_max / 1e3)
+    # one GPU: 3328 tokens per step; expert-parallel: the same 3328 tokens
+    # split over the ranks (strong scaling)
+    value = PF_TOKENS * args.steps / (ms_max / 1e3)
 
     # per-stage device times (one extra, untimed pass): the gate/up GEMM is
     # the dominant kernel
     pf.timing(True)
     stages = np.zeros(6)
-    with torch.cuda.stream(st):
-        dx.copy_(dx0)
+    dx.copy_(dx0)
     for lw, lg in zip(layers, dlg):
-        pf.moe_layer_dev(lw, dx.data_ptr(), PF_TOKENS, lg.data_ptr())
+        if ep is None:
+            pf.moe_layer_dev(lw, dx.data_ptr(), PF_TOKENS, lg.data_ptr(), stream=sp)
+        else:
+            ep.moe_layer(lw, dx, lg)
         stages += pf.stage_ms()
     pf.timing(False)
     stages /= len(layers)
 
-    # e2e: the host-pointer API per layer (x and logits copied in, x and the
-    # routing copied out, as a host caller of ds_cuda_prefill_moe does)
+    # e2e through the public API with host buffers: one GPU, the host-pointer
+    # ds_cuda_prefill_moe per layer (x and logits in, x and routing out);
+    # expert-parallel, the rank's x slice and logits copied in from pinned
+    # host memory before the layers and x copied out after them
     n_e2e = max(1, min(args.steps, 3))
-    xs = x.copy()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ctx.synchronize()
-    t0.record(st)
-    for _ in range(n_e2e):
-        xs[:] = x
-        for lw, lg in zip(layers, logits):
-            pf.moe_layer(lw, xs, lg)
-    t1.record(st)
+    st.synchronize()
+    barrier(pg)
+    if ep is None:
+        xs = x.copy()
+        t0.record(st)
+        for _ in range(n_e2e):
+            xs[:] = x
+            for lw, lg in zip(layers, logits):
+                pf.moe_layer(lw, xs, lg)
+        t1.record(st)
+        h2d = PF_LAYERS * PF_TOKENS * (d.hidden + d.n_experts) * 4
+        d2h = PF_LAYERS * PF_TOKENS * (d.hidden + 2 * d.top_k) * 4
+    else:
+        hx = torch.from_numpy(x[a:b].copy()).pin_memory()
+        hl = [torch.from_numpy(l[a:b].copy()).pin_memory() for l in logits]
+        out = torch.empty_like(hx).pin_memory()
+        t0.record(st)
+        for _ in range(n_e2e):
+            dx.copy_(hx, non_blocking=True)
+            for dl, hlg in zip(dlg, hl):
+                dl.copy_(hlg, non_blocking=True)
+            run_layers(dx, dlg)
+            out.copy_(dx, non_blocking=True)
+        t1.record(st)
+        h2d = (b - a) * (d.hidden + PF_LAYERS * d.n_experts) * 4
+        d2h = (b - a) * d.hidden * 4
     t1.synchronize()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1), pg)
-    e2e = world * PF_TOKENS * n_e2e / (e2e_ms / 1e3)
+    e2e = PF_TOKENS * n_e2e / (e2e_ms / 1e3)
     pk = peaks()
     peak_t = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
-    gu_ach = PF_FLOPS_GU_LAYER / (stages[3] / 1e3) / 1e12
-    step_ach = PF_FLOPS_LAYER * PF_LAYERS * args.steps / (ms_max / 1e3) / 1e12
+    # expert-parallel: rank 0's GEMM does about 1/G of the layer's work
+    gu_ach = PF_FLOPS_GU_LAYER / world / (stages[3] / 1e3) / 1e12
+    step_ach = PF_FLOPS_LAYER * PF_LAYERS * args.steps / (ms_max / 1e3) / 1e12 / world
     res = {
         "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
         "metric": "MoE prefill tokens/s (3328 tokens x 11 MoE layers, 64 experts top-6 + 2 shared)",
         "unit": "tokens/s", "dtype": "bf16 weights, f32 activations as two bf16 planes, f32 accumulate",
-        "e2e": {"value": e2e, "unit": "tokens/s",
-                "h2d_bytes_per_step": PF_LAYERS * PF_TOKENS * (d.hidden + d.n_experts) * 4,
-                "d2h_bytes_per_step": PF_LAYERS * PF_TOKENS * (d.hidden + 2 * d.top_k) * 4},
-        "gpu_launches": 6 * PF_LAYERS * args.steps, "config": prefill_config(),
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": 6 * PF_LAYERS * args.steps,
+        "config": dict(prefill_config(), parallelism=f"ep{world}" if world > 1 else "single GPU",
+                       tokens_per_rank=b - a),
+        "scaling": "strong" if world > 1 else "weak",
         "roofline": {"bound": "tensor", "achieved": gu_ach, "peak": peak_t, "unit": "TFLOP/s",
                      "frac": gu_ach / peak_t, "traffic": None,
                      "kernel": "pf_gemm_kernel<0> (gate/up + SwiGLU), 122.1 GFLOP algorithmic per layer; "
@@ -526,6 +571,11 @@ def run_ours_prefill(args, rank, world, pg, model):
                           "stage_us": dict(zip(["norm_route", "plan", "scatter", "gemm_gate_up", "gemm_down",
                                                 "combine"], [round(float(s) * 1e3, 1) for s in stages]))},
     }
+    # torch tensors used on the context's stream go before the stream does
+    del dx, dx0, dlg, ep
+    import gc
+    gc.collect()
+    torch.cuda.synchronize()
     ctx.close()
     return res
 
@@ -590,7 +640,7 @@ def main():
                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": T, "kind": "reference", "sample": sample},
                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         line.update(common)
-        print(json.dumps(line))
+        print(json.dumps(line), flush=True)
         return
 
     if args.workload == "decode":
@@ -611,7 +661,9 @@ def main():
     if "step_roofline" in res:
         line["step_roofline"] = res["step_roofline"]
     line.update(common)
-    if not args.no_cpu_baseline:
+    if "scaling" in res:
+        line["scaling"] = res["scaling"]
+    if not args.no_cpu_baseline and world == 1:
         try:
             if args.workload == "decode":
                 v, n = ref_decode_time(model, ks, vs, T, args.cpu_budget, max_steps=64)
@@ -627,8 +679,12 @@ def main():
                                     "sample": sample}
         except Exception as e:  # reported, never silently substituted
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    print(json.dumps(line))
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
     main()
+    if os.environ.get("WORLD_SIZE", "1") != "1":
+        import torch.distributed as _dist
+        if _dist.is_initialized():
+            _dist.destroy_process_group()

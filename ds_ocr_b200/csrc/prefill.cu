@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(256) pf_norm_route_kernel(const float *__restr
                                                             float eps, int M, int H, const float *logits_in,
                                                             const uint16_t *__restrict__ Wr, float *logits_buf, int E,
                                                             int K, int renorm, uint16_t *xn_hi, uint16_t *xn_lo,
-                                                            int *idx, float *wt, int *counts) {
+                                                            int *idx, float *wt) {
     const int lane = threadIdx.x & 31;
     const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (s >= M) return;
@@ -349,14 +349,13 @@ __global__ void __launch_bounds__(256) pf_norm_route_kernel(const float *__restr
         for (int k = 0; k < K; k++) {
             idx[(size_t)s * K + k] = ik[k];
             wt[(size_t)s * K + k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
-            atomicAdd(&counts[ik[k]], 1);
         }
     }
 }
 
 // Segment starts of the expert-sorted rows, cursors, and the tile lists of
 // both GEMM stages (shared-expert tiles first, then routed ones). One block.
-__global__ void __launch_bounds__(256) pf_plan_kernel(int *counts, int E, int M, int I, int S, int H, int *seg,
+__global__ void __launch_bounds__(256) pf_plan_kernel(int *counts, int E, int M_sh, int I, int S, int H, int *seg,
                                                       int *cursor, PfTile *gu_tiles, int *n_gu, PfTile *dn_tiles,
                                                       int *n_dn) {
     __shared__ int cnt[PF_MAXE], mt[PF_MAXE], seg_s[PF_MAXE], mto[PF_MAXE + 1];
@@ -377,16 +376,16 @@ __global__ void __launch_bounds__(256) pf_plan_kernel(int *counts, int E, int M,
         mto[E] = b;
     }
     __syncthreads();
-    const int mts = (M + PF_BM - 1) / PF_BM;
+    const int mts = (M_sh + PF_BM - 1) / PF_BM;
     const int gu_nt_r = I / 128, gu_nt_s = S / 128, dn_nt = H / PF_BN;
     const int sh_gu = mts * gu_nt_s, sh_dn = mts * dn_nt;
     for (int i = t; i < sh_gu; i += blockDim.x) {
         const int m = i / gu_nt_s, n = i - m * gu_nt_s;
-        gu_tiles[i] = PfTile{1, 0, m * PF_BM, min(PF_BM, M - m * PF_BM), n * 128};
+        gu_tiles[i] = PfTile{1, 0, m * PF_BM, min(PF_BM, M_sh - m * PF_BM), n * 128};
     }
     for (int i = t; i < sh_dn; i += blockDim.x) {
         const int m = i / dn_nt, n = i - m * dn_nt;
-        dn_tiles[i] = PfTile{1, 0, m * PF_BM, min(PF_BM, M - m * PF_BM), n * PF_BN};
+        dn_tiles[i] = PfTile{1, 0, m * PF_BM, min(PF_BM, M_sh - m * PF_BM), n * PF_BN};
     }
     if (t < E) {
         seg[t] = seg_s[t];
@@ -406,31 +405,45 @@ __global__ void __launch_bounds__(256) pf_plan_kernel(int *counts, int E, int M,
     }
 }
 
-// Copies each token's split row to the segment of each of its experts.
-__global__ void __launch_bounds__(256) pf_scatter_kernel(int M, int H, int K, const int *idx, const int *seg,
-                                                         int *cursor, const uint16_t *xn_hi, const uint16_t *xn_lo,
+// Tokens per expert over the (row, expert) pairs (block histogram first).
+__global__ void __launch_bounds__(256) pf_count_kernel(int P, const int *__restrict__ pair_expert, int E, int *counts) {
+    __shared__ int h[PF_MAXE];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+    __syncthreads();
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < P; p += gridDim.x * blockDim.x) {
+        const int e = pair_expert[p];
+        if ((unsigned)e < (unsigned)E) atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+        if (h[e]) atomicAdd(&counts[e], h[e]);
+}
+
+// Copies the split row of each (row, expert) pair to the next free slot of
+// the expert's segment; slot_of[slot] = pair. pair_row == null: row = p / K.
+__global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int K, const int *pair_row,
+                                                         const int *pair_expert, int E, const int *seg, int *cursor,
+                                                         const uint16_t *rows_hi, const uint16_t *rows_lo,
                                                          uint16_t *xg_hi, uint16_t *xg_lo, int *slot_of) {
     const int lane = threadIdx.x & 31;
-    const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (s >= M) return;
-    const int nv = H / 256;  // uint4 (8 BF16) per lane
-    uint4 hi[8], lo[8];
-    for (int i = 0; i < nv; i++) {
-        hi[i] = reinterpret_cast<const uint4 *>(xn_hi + (size_t)s * H)[lane + 32 * i];
-        lo[i] = reinterpret_cast<const uint4 *>(xn_lo + (size_t)s * H)[lane + 32 * i];
+    const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (p >= P) return;
+    const int e = pair_expert[p];
+    if ((unsigned)e >= (unsigned)E) return;
+    const int r = pair_row ? pair_row[p] : p / K;
+    int pos = 0;
+    if (lane == 0) {
+        pos = seg[e] + atomicAdd(&cursor[e], 1);
+        slot_of[pos] = p;
     }
-    for (int k = 0; k < K; k++) {
-        int pos = 0;
-        if (lane == 0) {
-            const int e = idx[(size_t)s * K + k];
-            pos = seg[e] + atomicAdd(&cursor[e], 1);
-            slot_of[pos] = s * K + k;
-        }
-        pos = __shfl_sync(0xffffffffu, pos, 0);
-        for (int i = 0; i < nv; i++) {
-            reinterpret_cast<uint4 *>(xg_hi + (size_t)pos * H)[lane + 32 * i] = hi[i];
-            reinterpret_cast<uint4 *>(xg_lo + (size_t)pos * H)[lane + 32 * i] = lo[i];
-        }
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    const uint4 *sh = reinterpret_cast<const uint4 *>(rows_hi + (size_t)r * H);
+    const uint4 *sl = reinterpret_cast<const uint4 *>(rows_lo + (size_t)r * H);
+    uint4 *dh = reinterpret_cast<uint4 *>(xg_hi + (size_t)pos * H);
+    uint4 *dl = reinterpret_cast<uint4 *>(xg_lo + (size_t)pos * H);
+    for (int i = lane; i < H / 8; i += 32) {
+        dh[i] = sh[i];
+        dl[i] = sl[i];
     }
 }
 
@@ -481,83 +494,59 @@ using namespace ds;
 // Host side
 // ---------------------------------------------------------------------------
 struct PfWork {
-    int cap_m = 0, H = 0, I = 0, S = 0, E = 0, K = 0;
+    // grown on demand; caps in bytes
     uint16_t *xn_hi = nullptr, *xn_lo = nullptr, *xg_hi = nullptr, *xg_lo = nullptr;
     uint16_t *hg_hi = nullptr, *hg_lo = nullptr, *hs_hi = nullptr, *hs_lo = nullptr;
     float *yr = nullptr, *ys = nullptr, *logits = nullptr, *wt = nullptr;
-    int *idx = nullptr, *counts = nullptr, *seg = nullptr, *cursor = nullptr, *slot_of = nullptr, *nt = nullptr;
+    int *idx = nullptr, *slot_of = nullptr;
     PfTile *gu_tiles = nullptr, *dn_tiles = nullptr;
+    size_t c_xn_hi = 0, c_xn_lo = 0, c_xg_hi = 0, c_xg_lo = 0, c_hg_hi = 0, c_hg_lo = 0, c_hs_hi = 0, c_hs_lo = 0;
+    size_t c_yr = 0, c_ys = 0, c_logits = 0, c_wt = 0, c_idx = 0, c_slot = 0, c_gu = 0, c_dn = 0;
+    // fixed
+    int *counts = nullptr, *seg = nullptr, *cursor = nullptr, *nt = nullptr;
     unsigned *err = nullptr;  // set by a device-side wait that gave up
-    int max_gu = 0, max_dn = 0;
 };
 
 void prefill_release(ds_cuda_ctx *c) {
     PfWork *w = (PfWork *)c->prefill;
     if (!w) return;
     void *ptrs[] = {w->xn_hi, w->xn_lo, w->xg_hi, w->xg_lo, w->hg_hi, w->hg_lo, w->hs_hi, w->hs_lo, w->yr,
-                    w->ys, w->logits, w->wt, w->idx, w->counts, w->seg, w->cursor, w->slot_of, w->nt,
-                    w->gu_tiles, w->dn_tiles, w->err};
+                    w->ys, w->logits, w->wt, w->idx, w->slot_of, w->gu_tiles, w->dn_tiles, w->counts, w->seg,
+                    w->cursor, w->nt, w->err};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete w;
     c->prefill = nullptr;
 }
 
-static int pf_workspace(ds_cuda_ctx *c, int M, int H, int I, int S, int E, int K, cudaStream_t st, PfWork **out) {
+static int pf_work(ds_cuda_ctx *c, cudaStream_t st, PfWork **out) {
     PfWork *w = (PfWork *)c->prefill;
-    if (w && w->cap_m >= M && w->H == H && w->I == I && w->S == S && w->E == E && w->K == K) {
-        *out = w;
-        return DS_CUDA_OK;
-    }
-    prefill_release(c);
-    w = new PfWork();
-    c->prefill = w;
-    w->cap_m = M;
-    w->H = H, w->I = I, w->S = S, w->E = E, w->K = K;
-    const size_t P = (size_t)M * K;
-    const int mts = (M + PF_BM - 1) / PF_BM;
-    // routed tiles: sum_e ceil(n_e / 128) <= P / 128 + E
-    const size_t mt_r = P / PF_BM + E;
-    w->max_gu = (int)(mts * (S / 128) + mt_r * (I / 128));
-    w->max_dn = (int)(mts * (H / PF_BN) + mt_r * (H / PF_BN));
-    // A planes get one tile of slack rows so a tile never starts past the end
-    const size_t PR = P + PF_BM;
-    struct A {
-        void **p;
-        size_t bytes;
-    } allocs[] = {
-        {(void **)&w->xn_hi, (size_t)(M + PF_BM) * H * 2}, {(void **)&w->xn_lo, (size_t)(M + PF_BM) * H * 2},
-        {(void **)&w->xg_hi, PR * H * 2},                  {(void **)&w->xg_lo, PR * H * 2},
-        {(void **)&w->hg_hi, PR * I * 2},                  {(void **)&w->hg_lo, PR * I * 2},
-        {(void **)&w->hs_hi, (size_t)(M + PF_BM) * S * 2}, {(void **)&w->hs_lo, (size_t)(M + PF_BM) * S * 2},
-        {(void **)&w->yr, P * H * 4},                      {(void **)&w->ys, (size_t)M * H * 4},
-        {(void **)&w->logits, (size_t)M * E * 4},          {(void **)&w->wt, P * 4},
-        {(void **)&w->idx, P * 4},                         {(void **)&w->counts, (size_t)E * 4},
-        {(void **)&w->seg, (size_t)E * 4},                 {(void **)&w->cursor, (size_t)E * 4},
-        {(void **)&w->slot_of, PR * 4},                    {(void **)&w->nt, 2 * 4},
-        {(void **)&w->gu_tiles, (size_t)w->max_gu * sizeof(PfTile)},
-        {(void **)&w->dn_tiles, (size_t)w->max_dn * sizeof(PfTile)},
-        {(void **)&w->err, 4},
-    };
-    for (auto &a : allocs) {
-        cudaError_t e = cudaMalloc(a.p, a.bytes);
+    if (!w) {
+        w = new PfWork();
+        c->prefill = w;
+        cudaError_t e = cudaMalloc(&w->counts, PF_MAXE * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&w->seg, PF_MAXE * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&w->cursor, PF_MAXE * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&w->nt, 2 * 4);
+        if (e == cudaSuccess) e = cudaMalloc(&w->err, 4);
+        // stream-ordered with the kernels (the context's stream does not
+        // synchronise with the legacy default stream)
+        if (e == cudaSuccess) e = cudaMemsetAsync(w->counts, 0, PF_MAXE * 4, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(w->err, 0, 4, st);
         if (e != cudaSuccess) {
             prefill_release(c);
             return ctx_cuda(c, e, "prefill workspace");
         }
     }
-    // stream-ordered with the kernels (the context's stream does not
-    // synchronise with the legacy default stream)
-    cudaMemsetAsync(w->counts, 0, (size_t)E * 4, st);
-    cudaMemsetAsync(w->err, 0, 4, st);
-    // padding rows of the A planes stay zero (TMA reads them for partial tiles)
-    cudaMemsetAsync(w->xn_hi, 0, (size_t)(M + PF_BM) * H * 2, st);
-    cudaMemsetAsync(w->xn_lo, 0, (size_t)(M + PF_BM) * H * 2, st);
-    cudaMemsetAsync(w->hs_hi, 0, (size_t)(M + PF_BM) * S * 2, st);
-    cudaMemsetAsync(w->hs_lo, 0, (size_t)(M + PF_BM) * S * 2, st);
     *out = w;
     return DS_CUDA_OK;
 }
+
+#define PF_GROW(ptr, cap, bytes)                                                          \
+    do {                                                                                  \
+        int _rc = ctx_grow(c, (void **)&(ptr), &(cap), (bytes));                          \
+        if (_rc < 0) return _rc;                                                          \
+    } while (0)
 
 // cuTensorMapEncodeTiled, looked up through the runtime so the library does
 // not link the driver library directly (it loads where no driver exists).
@@ -577,32 +566,64 @@ static EncodeTiledFn encode_tiled() {
 }
 
 // BF16 row-major [rows x cols] as a 2-D tensor map with 64 x box_rows boxes,
-// 128-byte swizzle (the UMMA K-major canonical layout).
+// 128-byte swizzle (the UMMA K-major canonical layout). Rows past `rows`
+// read as zeros (partial tiles).
 static bool pf_map(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
     EncodeTiledFn enc = encode_tiled();
-    if (!enc) return false;
-    cuuint64_t dims[2] = {cols, rows};
+    if (!enc || !base) return false;
+    cuuint64_t dims[2] = {cols, rows < 1 ? 1 : rows};
     cuuint64_t strides[1] = {cols * 2};
     cuuint32_t box[2] = {(cuuint32_t)PF_BK, box_rows};
     cuuint32_t es[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
-                                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// One MoE prefill layer on device buffers. d_x [M x H] is updated in place.
-int prefill_moe_enqueue(ds_cuda_ctx *c, int H, int I, int S, int E, int K, float eps, const float *d_norm,
-                        const uint16_t *d_router, const uint16_t *d_block, const uint16_t *d_down,
-                        const uint16_t *d_sdown, float *d_x, int M, const float *d_logits, int *d_idx_out,
-                        float *d_w_out, cudaStream_t st) {
+struct PfShape {
+    int H, I, S, E, K;
+    float eps;
+};
+
+static int pf_shape_ok(ds_cuda_ctx *c, const PfShape &g) {
+    if (g.H % 256 || g.H > 2048 || g.I % 128 || g.I <= 0 || g.S % 128 || g.E <= 0 || g.E > PF_MAXE || g.K <= 0 ||
+        g.K > 8 || g.K > g.E)
+        return ctx_fail(c, DS_CUDA_EINVAL, "prefill: unsupported shape (hidden %% 256 and <= 2048, inter and shared "
+                                           "inter %% 128, n_experts <= 256, top_k <= 8 required)");
+    return DS_CUDA_OK;
+}
+
+static void mark(ds_cuda_ctx *c, int i, cudaStream_t st) {
+    if (c->prefill_timing) cudaEventRecord(c->prefill_ev[i], st);
+}
+
+// Stage 1: RMSNorm, BF16 split planes and routing of M tokens.
+static int pf_route(ds_cuda_ctx *c, const PfShape &g, const float *d_norm, const uint16_t *d_router,
+                    const float *d_x, int M, const float *d_logits, uint16_t *xn_hi, uint16_t *xn_lo, int *idx,
+                    float *wt, cudaStream_t st) {
     if (M <= 0) return DS_CUDA_OK;
-    if (H % 256 || I % 128 || S % 128 || E <= 0 || E > PF_MAXE || K <= 0 || K > 8 || K > E || H > 2048)
-        return ctx_fail(c, DS_CUDA_EINVAL, "prefill_moe: unsupported shape (H %% 256, I %% 128, S %% 128, "
-                                           "E <= 256, top_k <= 8, H <= 2048 required)");
-    if (!d_logits && !d_router) return ctx_fail(c, DS_CUDA_EINVAL, "prefill_moe: no router weights and no logits");
+    if (!d_logits && !d_router) return ctx_fail(c, DS_CUDA_EINVAL, "prefill: no router weights and no logits");
     PfWork *w;
-    int rc = pf_workspace(c, M, H, I, S, E, K, st, &w);
+    int rc = pf_work(c, st, &w);
+    if (rc < 0) return rc;
+    if (!d_logits) PF_GROW(w->logits, w->c_logits, (size_t)M * g.E * 4);
+    mark(c, 0, st);
+    pf_norm_route_kernel<<<(M + 7) / 8, 256, 0, st>>>(d_x, d_norm, g.eps, M, g.H, d_logits, d_router, w->logits,
+                                                      g.E, g.K, c->renorm, xn_hi, xn_lo, idx, wt);
+    return DS_CUDA_OK;
+}
+
+// Stage 2: the grouped GEMMs. Routed: pair p = (row pair_row[p] (or p / K),
+// expert pair_expert[p]) of rows_hi/lo [n_rows x H] -> y[p] [H]. Shared:
+// sh_hi/lo [n_sh x H] -> ys [n_sh x H]. Either part may be empty.
+static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block, const uint16_t *d_down,
+                      const uint16_t *d_sdown, const uint16_t *rows_hi, const uint16_t *rows_lo, const int *pair_row,
+                      const int *pair_expert, int P, float *y, const uint16_t *sh_hi, const uint16_t *sh_lo, int n_sh,
+                      float *ys, cudaStream_t st) {
+    if (P <= 0 && n_sh <= 0) return DS_CUDA_OK;
+    const int H = g.H, I = g.I, S = g.S, E = g.E;
+    PfWork *w;
+    int rc = pf_work(c, st, &w);
     if (rc < 0) return rc;
     static bool attr = false;
     if (!attr) {
@@ -610,74 +631,108 @@ int prefill_moe_enqueue(ds_cuda_ctx *c, int H, int I, int S, int E, int K, float
         cudaFuncSetAttribute(pf_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
         attr = true;
     }
-    const size_t P = (size_t)M * K;
-    const int wblocks = (M + 7) / 8;
-    // optional stage timing: events between the six launches
-    auto mark = [&](int i) {
-        if (c->prefill_timing) cudaEventRecord(c->prefill_ev[i], st);
-    };
-    mark(0);
-    pf_norm_route_kernel<<<wblocks, 256, 0, st>>>(d_x, d_norm, eps, M, H, d_logits, d_router, w->logits, E, K,
-                                                  c->renorm, w->xn_hi, w->xn_lo, w->idx, w->wt, w->counts);
-    mark(1);
-    pf_plan_kernel<<<1, 256, 0, st>>>(w->counts, E, M, I, S, H, w->seg, w->cursor, w->gu_tiles, w->nt,
-                                      w->dn_tiles, w->nt + 1);
-    mark(2);
-    pf_scatter_kernel<<<wblocks, 256, 0, st>>>(M, H, K, w->idx, w->seg, w->cursor, w->xn_hi, w->xn_lo, w->xg_hi,
-                                               w->xg_lo, w->slot_of);
+    const size_t Pz = P > 0 ? P : 0, Sz = n_sh > 0 ? n_sh : 0;
+    const size_t mt_r = Pz / PF_BM + E, mts = (Sz + PF_BM - 1) / PF_BM;
+    PF_GROW(w->xg_hi, w->c_xg_hi, Pz * H * 2 + 16);
+    PF_GROW(w->xg_lo, w->c_xg_lo, Pz * H * 2 + 16);
+    PF_GROW(w->hg_hi, w->c_hg_hi, Pz * I * 2 + 16);
+    PF_GROW(w->hg_lo, w->c_hg_lo, Pz * I * 2 + 16);
+    PF_GROW(w->hs_hi, w->c_hs_hi, Sz * S * 2 + 16);
+    PF_GROW(w->hs_lo, w->c_hs_lo, Sz * S * 2 + 16);
+    PF_GROW(w->slot_of, w->c_slot, Pz * 4 + 16);
+    PF_GROW(w->gu_tiles, w->c_gu, (mts * (S / 128) + mt_r * (I / 128)) * sizeof(PfTile));
+    PF_GROW(w->dn_tiles, w->c_dn, (mts + mt_r) * (H / PF_BN) * sizeof(PfTile));
     const int grid = c->sm_count;
-    // gate/up (+SwiGLU): routed A = expert-sorted rows, shared A = all rows;
+    mark(c, 1, st);
+    if (P > 0) pf_count_kernel<<<min((P + 255) / 256, grid), 256, 0, st>>>(P, pair_expert, E, w->counts);
+    pf_plan_kernel<<<1, 256, 0, st>>>(w->counts, E, n_sh > 0 ? n_sh : 0, I, S, H, w->seg, w->cursor, w->gu_tiles,
+                                      w->nt, w->dn_tiles, w->nt + 1);
+    mark(c, 2, st);
+    if (P > 0)
+        pf_scatter_kernel<<<(P + 7) / 8, 256, 0, st>>>(P, H, g.K, pair_row, pair_expert, E, w->seg, w->cursor,
+                                                       rows_hi, rows_lo, w->xg_hi, w->xg_lo, w->slot_of);
+    // gate/up (+SwiGLU): routed A = expert-sorted rows, shared A = sh planes;
     // B = the expert block [E*2I + 2S rows x H] for both
-    PfGemm g;
-    memset(&g, 0, sizeof g);
+    PfGemm gu;
+    memset(&gu, 0, sizeof gu);
     const uint64_t brows = (uint64_t)E * 2 * I + 2 * (uint64_t)S;
-    bool ok = pf_map(&g.a_hi[0], w->xg_hi, H, P + PF_BM, PF_BM) && pf_map(&g.a_lo[0], w->xg_lo, H, P + PF_BM, PF_BM) &&
-              pf_map(&g.a_hi[1], w->xn_hi, H, M + PF_BM, PF_BM) && pf_map(&g.a_lo[1], w->xn_lo, H, M + PF_BM, PF_BM) &&
-              pf_map(&g.b[0], d_block, H, brows, 128) && pf_map(&g.b[1], d_block, H, brows, 128);
-    if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill_moe: tensor map encoding failed");
-    g.tiles = w->gu_tiles;
-    g.n_tiles = w->nt;
-    g.k_blocks[0] = g.k_blocks[1] = H / PF_BK;
-    g.b_base[0] = 0;
-    g.b_group_rows[0] = 2 * I;
-    g.b_half[0] = I;
-    g.b_base[1] = E * 2 * I;
-    g.b_group_rows[1] = 0;
-    g.b_half[1] = S;
-    g.h_hi[0] = w->hg_hi;
-    g.h_lo[0] = w->hg_lo;
-    g.h_ld[0] = I;
-    g.h_hi[1] = w->hs_hi;
-    g.h_lo[1] = w->hs_lo;
-    g.h_ld[1] = S;
-    g.err = w->err;
-    mark(3);
-    pf_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, st>>>(g);
-    mark(4);
-    // down: routed A = SwiGLU rows [P x I], shared A = [M x S]
-    PfGemm d;
-    memset(&d, 0, sizeof d);
-    ok = pf_map(&d.a_hi[0], w->hg_hi, I, P + PF_BM, PF_BM) && pf_map(&d.a_lo[0], w->hg_lo, I, P + PF_BM, PF_BM) &&
-         pf_map(&d.a_hi[1], w->hs_hi, S, M + PF_BM, PF_BM) && pf_map(&d.a_lo[1], w->hs_lo, S, M + PF_BM, PF_BM) &&
-         pf_map(&d.b[0], d_down, I, (uint64_t)E * H, PF_BN) && pf_map(&d.b[1], d_sdown, S, H, PF_BN);
-    if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill_moe: tensor map encoding failed");
-    d.tiles = w->dn_tiles;
-    d.n_tiles = w->nt + 1;
-    d.k_blocks[0] = I / PF_BK;
-    d.k_blocks[1] = S / PF_BK;
-    d.b_base[0] = 0;
-    d.b_group_rows[0] = H;
-    d.b_base[1] = 0;
-    d.b_group_rows[1] = 0;
-    d.y[0] = w->yr;
-    d.y[1] = w->ys;
-    d.slot_of = w->slot_of;
-    d.y_ld = H;
-    d.err = w->err;
-    pf_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, st>>>(d);
-    mark(5);
-    pf_combine_kernel<<<wblocks, 256, 0, st>>>(d_x, M, H, K, w->idx, w->wt, w->yr, w->ys);
-    mark(6);
+    const uint16_t *shh = n_sh > 0 ? sh_hi : w->xg_hi, *shl = n_sh > 0 ? sh_lo : w->xg_lo;
+    bool ok = pf_map(&gu.a_hi[0], w->xg_hi, H, Pz, PF_BM) && pf_map(&gu.a_lo[0], w->xg_lo, H, Pz, PF_BM) &&
+              pf_map(&gu.a_hi[1], shh, H, Sz, PF_BM) && pf_map(&gu.a_lo[1], shl, H, Sz, PF_BM) &&
+              pf_map(&gu.b[0], d_block, H, brows, 128) && pf_map(&gu.b[1], d_block, H, brows, 128);
+    if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill: tensor map encoding failed");
+    gu.tiles = w->gu_tiles;
+    gu.n_tiles = w->nt;
+    gu.k_blocks[0] = gu.k_blocks[1] = H / PF_BK;
+    gu.b_base[0] = 0;
+    gu.b_group_rows[0] = 2 * I;
+    gu.b_half[0] = I;
+    gu.b_base[1] = E * 2 * I;
+    gu.b_half[1] = S;
+    gu.h_hi[0] = w->hg_hi;
+    gu.h_lo[0] = w->hg_lo;
+    gu.h_ld[0] = I;
+    gu.h_hi[1] = w->hs_hi;
+    gu.h_lo[1] = w->hs_lo;
+    gu.h_ld[1] = S;
+    gu.err = w->err;
+    mark(c, 3, st);
+    pf_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, st>>>(gu);
+    mark(c, 4, st);
+    // down: routed A = SwiGLU rows [P x I], shared A = [n_sh x S]
+    PfGemm dn;
+    memset(&dn, 0, sizeof dn);
+    ok = pf_map(&dn.a_hi[0], w->hg_hi, I, Pz, PF_BM) && pf_map(&dn.a_lo[0], w->hg_lo, I, Pz, PF_BM) &&
+         pf_map(&dn.a_hi[1], w->hs_hi, S, Sz, PF_BM) && pf_map(&dn.a_lo[1], w->hs_lo, S, Sz, PF_BM) &&
+         pf_map(&dn.b[0], d_down, I, (uint64_t)E * H, PF_BN) && pf_map(&dn.b[1], d_sdown, S, H, PF_BN);
+    if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill: tensor map encoding failed");
+    dn.tiles = w->dn_tiles;
+    dn.n_tiles = w->nt + 1;
+    dn.k_blocks[0] = I / PF_BK;
+    dn.k_blocks[1] = S / PF_BK;
+    dn.b_group_rows[0] = H;
+    dn.y[0] = y;
+    dn.y[1] = ys;
+    dn.slot_of = w->slot_of;
+    dn.y_ld = H;
+    dn.err = w->err;
+    pf_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, st>>>(dn);
+    mark(c, 5, st);
+    return DS_CUDA_OK;
+}
+
+// Stage 3: x += (sum in ascending expert order of w_k y_k) + ys.
+static int pf_combine(ds_cuda_ctx *c, const PfShape &g, float *d_x, int M, const int *idx, const float *wt,
+                      const float *y, const float *ys, cudaStream_t st) {
+    if (M <= 0) return DS_CUDA_OK;
+    pf_combine_kernel<<<(M + 7) / 8, 256, 0, st>>>(d_x, M, g.H, g.K, idx, wt, y, ys);
+    mark(c, 6, st);
+    return DS_CUDA_OK;
+}
+
+// One MoE prefill layer on device buffers. d_x [M x H] is updated in place.
+int prefill_moe_enqueue(ds_cuda_ctx *c, const PfShape &g, const float *d_norm, const uint16_t *d_router,
+                        const uint16_t *d_block, const uint16_t *d_down, const uint16_t *d_sdown, float *d_x, int M,
+                        const float *d_logits, int *d_idx_out, float *d_w_out, cudaStream_t st) {
+    if (M <= 0) return DS_CUDA_OK;
+    int rc = pf_shape_ok(c, g);
+    if (rc < 0) return rc;
+    PfWork *w;
+    rc = pf_work(c, st, &w);
+    if (rc < 0) return rc;
+    const size_t P = (size_t)M * g.K;
+    PF_GROW(w->xn_hi, w->c_xn_hi, (size_t)M * g.H * 2);
+    PF_GROW(w->xn_lo, w->c_xn_lo, (size_t)M * g.H * 2);
+    PF_GROW(w->idx, w->c_idx, P * 4);
+    PF_GROW(w->wt, w->c_wt, P * 4);
+    PF_GROW(w->yr, w->c_yr, P * g.H * 4);
+    PF_GROW(w->ys, w->c_ys, (size_t)M * g.H * 4);
+    if ((rc = pf_route(c, g, d_norm, d_router, d_x, M, d_logits, w->xn_hi, w->xn_lo, w->idx, w->wt, st)) < 0) return rc;
+    // pairs (token s, slot k) = index s*K + k; its expert is idx[s*K + k]
+    if ((rc = pf_experts(c, g, d_block, d_down, d_sdown, w->xn_hi, w->xn_lo, nullptr, w->idx, (int)P, w->yr,
+                         w->xn_hi, w->xn_lo, M, w->ys, st)) < 0)
+        return rc;
+    if ((rc = pf_combine(c, g, d_x, M, w->idx, w->wt, w->yr, w->ys, st)) < 0) return rc;
     if (d_idx_out) cudaMemcpyAsync(d_idx_out, w->idx, P * 4, cudaMemcpyDeviceToDevice, st);
     if (d_w_out) cudaMemcpyAsync(d_w_out, w->wt, P * 4, cudaMemcpyDeviceToDevice, st);
     cudaError_t e = cudaGetLastError();
@@ -688,17 +743,23 @@ int prefill_moe_enqueue(ds_cuda_ctx *c, int H, int I, int S, int E, int K, float
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
+static PfShape pf_shape(const ds_cuda_decoder_config_t *cfg) {
+    return PfShape{cfg->hidden, cfg->moe_inter, cfg->n_shared * cfg->moe_inter, cfg->n_experts, cfg->top_k,
+                   cfg->rms_eps};
+}
+
 static int pf_layer_ptrs(ds_cuda_ctx *c, const ds_cuda_decoder_config_t *g, const ds_cuda_layer_weights_t *L,
                          bool need_router, const float **norm, const uint16_t **router, const uint16_t **block,
                          const uint16_t **down, const uint16_t **sdown) {
     const size_t H = g->hidden, I = g->moe_inter, S = (size_t)g->n_shared * g->moe_inter, E = g->n_experts;
-    *norm = (const float *)ctx_lookup(c, L->post_attn_norm, H * 4, true);
-    *router = need_router ? (const uint16_t *)ctx_lookup(c, L->router, E * H * 2, true) : nullptr;
-    *block = (const uint16_t *)ctx_lookup(c, L->expert_block, (E * 2 * I + 2 * S) * H * 2, true);
-    *down = (const uint16_t *)ctx_lookup(c, L->down, E * H * I * 2, true);
-    *sdown = (const uint16_t *)ctx_lookup(c, L->shared_down, H * S * 2, true);
-    if (!*norm || (need_router && !*router) || !*block || !*down || !*sdown)
-        return ctx_fail(c, DS_CUDA_EINVAL, "prefill_moe: a weight array is missing or could not be registered");
+    if (norm) *norm = (const float *)ctx_lookup(c, L->post_attn_norm, H * 4, true);
+    if (router) *router = need_router ? (const uint16_t *)ctx_lookup(c, L->router, E * H * 2, true) : nullptr;
+    if (block) *block = (const uint16_t *)ctx_lookup(c, L->expert_block, (E * 2 * I + 2 * S) * H * 2, true);
+    if (down) *down = (const uint16_t *)ctx_lookup(c, L->down, E * H * I * 2, true);
+    if (sdown) *sdown = (const uint16_t *)ctx_lookup(c, L->shared_down, H * S * 2, true);
+    if ((norm && !*norm) || (router && need_router && !*router) || (block && !*block) || (down && !*down) ||
+        (sdown && !*sdown))
+        return ctx_fail(c, DS_CUDA_EINVAL, "prefill: a weight array is missing or could not be registered");
     return DS_CUDA_OK;
 }
 
@@ -710,10 +771,12 @@ static int pf_check(ds_cuda_ctx *c) {
     if (ce != cudaSuccess) return ctx_cuda(c, ce, "prefill error flag");
     if (e) {
         cudaMemsetAsync(w->err, 0, 4, c->stream);
-        return ctx_fail(c, DS_CUDA_ETIMEOUT, "prefill_moe: a bounded device-side wait gave up");
+        return ctx_fail(c, DS_CUDA_ETIMEOUT, "prefill: a bounded device-side wait gave up");
     }
     return DS_CUDA_OK;
 }
+
+static cudaStream_t pf_stream(ds_cuda_ctx *c, void *s) { return s ? (cudaStream_t)s : c->stream; }
 
 extern "C" int ds_cuda_prefill_moe_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
                                        const ds_cuda_layer_weights_t *layer, float *d_x, int n_tokens,
@@ -724,9 +787,8 @@ extern "C" int ds_cuda_prefill_moe_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_c
     const uint16_t *router, *block, *down, *sdown;
     int rc = pf_layer_ptrs(c, cfg, layer, d_logits == nullptr, &norm, &router, &block, &down, &sdown);
     if (rc < 0) return rc;
-    return prefill_moe_enqueue(c, cfg->hidden, cfg->moe_inter, cfg->n_shared * cfg->moe_inter, cfg->n_experts,
-                               cfg->top_k, cfg->rms_eps, norm, router, block, down, sdown, d_x, n_tokens, d_logits,
-                               d_top_idx, d_top_w, stream ? (cudaStream_t)stream : c->stream);
+    return prefill_moe_enqueue(c, pf_shape(cfg), norm, router, block, down, sdown, d_x, n_tokens, d_logits,
+                               d_top_idx, d_top_w, pf_stream(c, stream));
 }
 
 extern "C" int ds_cuda_prefill_moe(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
@@ -760,6 +822,61 @@ extern "C" int ds_cuda_prefill_moe(ds_cuda_ctx_t *c, const ds_cuda_decoder_confi
     cudaFree(di);
     cudaFree(dw);
     return rc;
+}
+
+// The three stages on caller buffers, for expert-parallel prefill (the
+// caller moves rows between devices in between).
+extern "C" int ds_cuda_prefill_route_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
+                                         const ds_cuda_layer_weights_t *layer, const float *d_x, int n_tokens,
+                                         const float *d_logits, uint16_t *d_xn_hi, uint16_t *d_xn_lo, int *d_top_idx,
+                                         float *d_top_w, void *stream) {
+    if (!c || !c->ok || !cfg || !layer || n_tokens < 0 ||
+        (n_tokens > 0 && (!d_x || !d_xn_hi || !d_xn_lo || !d_top_idx || !d_top_w)))
+        return DS_CUDA_EINVAL;
+    cudaSetDevice(c->device);
+    PfShape g = pf_shape(cfg);
+    int rc = pf_shape_ok(c, g);
+    if (rc < 0) return rc;
+    const float *norm;
+    const uint16_t *router;
+    rc = pf_layer_ptrs(c, cfg, layer, d_logits == nullptr, &norm, &router, nullptr, nullptr, nullptr);
+    if (rc < 0) return rc;
+    return pf_route(c, g, norm, router, d_x, n_tokens, d_logits, d_xn_hi, d_xn_lo, d_top_idx, d_top_w,
+                    pf_stream(c, stream));
+}
+
+extern "C" int ds_cuda_prefill_experts_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
+                                           const ds_cuda_layer_weights_t *layer, const uint16_t *d_rows_hi,
+                                           const uint16_t *d_rows_lo, int n_rows, const int *d_pair_row,
+                                           const int *d_pair_expert, int n_pairs, float *d_y,
+                                           const uint16_t *d_sh_hi, const uint16_t *d_sh_lo, int n_shared_rows,
+                                           float *d_ys, void *stream) {
+    if (!c || !c->ok || !cfg || !layer || n_rows < 0 || n_pairs < 0 || n_shared_rows < 0 ||
+        (n_pairs > 0 && (!d_rows_hi || !d_rows_lo || !d_pair_expert || !d_y)) ||
+        (n_pairs > 0 && !d_pair_row && n_rows * cfg->top_k < n_pairs) ||
+        (n_shared_rows > 0 && (!d_sh_hi || !d_sh_lo || !d_ys)))
+        return DS_CUDA_EINVAL;
+    cudaSetDevice(c->device);
+    PfShape g = pf_shape(cfg);
+    int rc = pf_shape_ok(c, g);
+    if (rc < 0) return rc;
+    const uint16_t *block, *down, *sdown;
+    rc = pf_layer_ptrs(c, cfg, layer, false, nullptr, nullptr, &block, &down, &sdown);
+    if (rc < 0) return rc;
+    return pf_experts(c, g, block, down, sdown, d_rows_hi, d_rows_lo, d_pair_row, d_pair_expert, n_pairs, d_y,
+                      d_sh_hi, d_sh_lo, n_shared_rows, d_ys, pf_stream(c, stream));
+}
+
+extern "C" int ds_cuda_prefill_combine_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg, float *d_x,
+                                           int n_tokens, const int *d_top_idx, const float *d_top_w,
+                                           const float *d_y, const float *d_ys, void *stream) {
+    if (!c || !c->ok || !cfg || n_tokens < 0 || (n_tokens > 0 && (!d_x || !d_top_idx || !d_top_w || !d_y || !d_ys)))
+        return DS_CUDA_EINVAL;
+    cudaSetDevice(c->device);
+    PfShape g = pf_shape(cfg);
+    int rc = pf_shape_ok(c, g);
+    if (rc < 0) return rc;
+    return pf_combine(c, g, d_x, n_tokens, d_top_idx, d_top_w, d_y, d_ys, pf_stream(c, stream));
 }
 
 extern "C" int ds_cuda_prefill_check(ds_cuda_ctx_t *c) {

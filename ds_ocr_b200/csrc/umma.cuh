@@ -11,7 +11,7 @@
 
 namespace ds {
 
-// 2-D tiled TMA load (no multicast) of box {x .. x+bx, y .. y+by} into
+// 2-D tiled TMA load, this CTA only, of box {x .. x+bx, y .. y+by} into
 // shared memory, completing on `bar`. x * element size must be a multiple
 // of 16 bytes (callers pass x as a multiple of 64 BF16 elements).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {

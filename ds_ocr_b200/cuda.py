@@ -34,6 +34,7 @@ class Int8Block(ctypes.Structure):
 class Context:
     def __init__(self, device=0):
         self.lib = load()
+        self.device = device
         self.h = self.lib.ds_cuda_init(device)
         if not self.h:
             raise DsCudaError("ds_cuda_init failed: no usable sm_100 CUDA device")

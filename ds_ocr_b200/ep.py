@@ -1,0 +1,182 @@
+"""Expert-parallel batched MoE prefill over the GPUs of one box.
+
+The reference runs the prefill MoE block (ds_moe_decoder.c:630-809) on one
+host. Here G ranks (one process per GPU, torch.distributed over NCCL) split
+the work:
+  * tokens are split evenly by index: rank r owns rows [r*n/G, (r+1)*n/G);
+  * experts are split into contiguous blocks: rank r runs experts
+    [r*E/G, (r+1)*E/G); the shared expert is replicated and runs on each
+    rank's own tokens.
+Per layer:
+  1. route      (local): RMSNorm into two BF16 planes, softmax/top-k;
+  2. dispatch   (all-to-all): each token's split row goes once to every rank
+                that owns one of its experts, with the list of those experts;
+  3. experts    (local): the grouped tensor-core GEMMs over the received
+                (row, expert) pairs, plus the shared expert on local rows;
+  4. return     (all-to-all): one output row per (token, expert) back to the
+                token's rank, in the order it asked for them;
+  5. combine    (local): x += sum over the token's experts in ascending
+                order of w * y, plus shared, the same arithmetic as one GPU,
+                so the result is bit-identical to the single-GPU path.
+Counts travel first (all-to-all of G integers) so every rank knows its
+receive sizes. The stage kernels come from `stages` (CudaStages below for
+the product; the CPU tests pass a numpy stand-in with the same interface).
+"""
+import ctypes
+
+from . import synth
+from .decoder import DecoderConfig, layer_struct
+
+
+class CudaStages:
+    """The three prefill stages of the C ABI on torch device tensors."""
+
+    def __init__(self, d, ctx):
+        import torch
+        self.torch = torch
+        self.ctx = ctx
+        self.lib = ctx.lib
+        self.d = d
+        self.cfg = DecoderConfig(d.hidden, d.n_layers, d.n_heads, d.head_dim, d.dense_inter, d.moe_inter,
+                                 d.n_experts, d.n_shared, d.top_k, d.vocab, d.first_dense, synth.RMS_EPS,
+                                 synth.ROPE_THETA, 0, 0, 0)
+        self._structs = {}
+        self.device = torch.device("cuda", ctx.device)
+        # a torch-owned stream: the stage kernels, the bookkeeping tensor ops
+        # and the collectives all run in its order
+        self.stream = torch.cuda.Stream(self.device)
+
+    def _st(self):
+        return self.stream.cuda_stream
+
+    def _layer(self, lw):
+        s = self._structs.get(id(lw))
+        if s is None:
+            m = lw.moe
+            self.ctx._pin(lw.post_norm, m.router, m.block, m.down, m.shared_down)
+            s = self._structs[id(lw)] = (lw, layer_struct(lw))
+        return ctypes.byref(s[1])
+
+    @staticmethod
+    def _p(t):
+        return None if t is None or t.numel() == 0 else t.data_ptr()
+
+    def route(self, lw, x, logits):
+        torch = self.torch
+        n, H, K = x.shape[0], self.d.hidden, self.d.top_k
+        hi = torch.empty((n, H), dtype=torch.int16, device=self.device)
+        lo = torch.empty((n, H), dtype=torch.int16, device=self.device)
+        idx = torch.empty((n, K), dtype=torch.int32, device=self.device)
+        w = torch.empty((n, K), dtype=torch.float32, device=self.device)
+        self.ctx.check(self.lib.ds_cuda_prefill_route_dev(self.ctx.h, ctypes.byref(self.cfg), self._layer(lw),
+                                                          self._p(x), n, self._p(logits), self._p(hi), self._p(lo),
+                                                          self._p(idx), self._p(w), self._st()), "prefill_route")
+        return hi, lo, idx, w
+
+    def experts(self, lw, rows_hi, rows_lo, pair_row, pair_expert, sh_hi, sh_lo):
+        torch = self.torch
+        H = self.d.hidden
+        P, S = pair_row.shape[0], sh_hi.shape[0]
+        y = torch.empty((P, H), dtype=torch.float32, device=self.device)
+        ys = torch.empty((S, H), dtype=torch.float32, device=self.device)
+        self.ctx.check(self.lib.ds_cuda_prefill_experts_dev(
+            self.ctx.h, ctypes.byref(self.cfg), self._layer(lw), self._p(rows_hi), self._p(rows_lo),
+            rows_hi.shape[0], self._p(pair_row), self._p(pair_expert), P, self._p(y), self._p(sh_hi),
+            self._p(sh_lo), S, self._p(ys), self._st()), "prefill_experts")
+        return y, ys
+
+    def combine(self, x, idx, w, y, ys):
+        self.ctx.check(self.lib.ds_cuda_prefill_combine_dev(self.ctx.h, ctypes.byref(self.cfg), self._p(x),
+                                                            x.shape[0], self._p(idx), self._p(w), self._p(y),
+                                                            self._p(ys), self._st()), "prefill_combine")
+
+    def check(self):
+        self.stream.synchronize()
+        self.ctx.check(self.lib.ds_cuda_prefill_check(self.ctx.h), "prefill_check")
+
+
+def token_range(n, rank, world):
+    return n * rank // world, n * (rank + 1) // world
+
+
+class ExpertParallelPrefill:
+    """One rank of the expert-parallel prefill. `dist` is torch.distributed
+    with an initialised process group; `stages` runs the kernels."""
+
+    def __init__(self, d, stages, dist, rank, world, device):
+        import torch
+        self.torch = torch
+        self.d = d
+        self.st = stages
+        self.dist = dist
+        self.rank, self.world = rank, world
+        self.device = device
+        if d.n_experts % world:
+            raise ValueError(f"{d.n_experts} experts do not split over {world} ranks")
+        self.e_per = d.n_experts // world
+
+    def _a2a(self, send, send_counts, recv_counts):
+        """all-to-all(v) along dim 0 (counts are host lists of rows)."""
+        torch = self.torch
+        out = torch.empty((sum(recv_counts),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
+        self.dist.all_to_all_single(out, send.contiguous(), recv_counts, send_counts)
+        return out
+
+    def _counts(self, counts):
+        torch = self.torch
+        c = torch.tensor(counts, dtype=torch.int64, device=self.device)
+        r = torch.empty_like(c)
+        self.dist.all_to_all_single(r, c)
+        return r.tolist()
+
+    def moe_layer(self, lw, x, logits):
+        """x [n_local x H] F32 (this rank's tokens, updated in place);
+        logits [n_local x E] or None. Returns (idx, w) of the local tokens.
+        Runs on the stages' stream (made current here); callers order their
+        own work on x against it."""
+        s = getattr(self.st, "stream", None)
+        if s is None:
+            return self._moe_layer(lw, x, logits)
+        with self.torch.cuda.stream(s):
+            return self._moe_layer(lw, x, logits)
+
+    def _moe_layer(self, lw, x, logits):
+        torch = self.torch
+        G, K = self.world, self.d.top_k
+        n = x.shape[0]
+        hi, lo, idx, w = self.st.route(lw, x, logits)
+        # --- dispatch: one row per (token, destination rank), in rank order,
+        # tokens ascending; with it the K expert ids served there (-1 else)
+        dest = (idx // self.e_per).long()                                # [n, K]
+        ranks = torch.arange(G, device=self.device)
+        hit = dest[:, None, :] == ranks[None, :, None]                   # [n, G, K]
+        need = hit.any(dim=2)                                            # [n, G]
+        send_tok = torch.nonzero(need.t(), as_tuple=False)               # (g, s) sorted by g then s
+        g_of, s_of = send_tok[:, 0], send_tok[:, 1]
+        send_counts = torch.bincount(g_of, minlength=G).tolist()
+        meta = torch.where(hit[s_of, g_of], idx[s_of], torch.full_like(idx[s_of], -1))   # [n_send, K]
+        recv_counts = self._counts(send_counts)
+        # the BF16 planes travel as int32 pairs (a pure reinterpretation)
+        r_hi = self._a2a(hi[s_of].view(torch.int32), send_counts, recv_counts).view(hi.dtype)
+        r_lo = self._a2a(lo[s_of].view(torch.int32), send_counts, recv_counts).view(lo.dtype)
+        r_meta = self._a2a(meta, send_counts, recv_counts)
+        # --- local experts over the received (row, expert) pairs
+        valid = r_meta >= 0
+        pr = torch.nonzero(valid, as_tuple=False)                        # (row, k) row-major
+        pair_row = pr[:, 0].to(torch.int32).contiguous()
+        pair_expert = r_meta[valid].to(torch.int32).contiguous()
+        y, ys = self.st.experts(lw, r_hi, r_lo, pair_row, pair_expert, hi, lo)
+        # --- return one row per pair to the token's rank, in request order
+        rows_from = torch.repeat_interleave(torch.arange(G, device=self.device),
+                                            torch.tensor(recv_counts, device=self.device))
+        back_send = torch.bincount(rows_from[pair_row.long()], minlength=G).tolist() if pair_row.numel() else [0] * G
+        back_recv = [int(v) for v in hit.sum(dim=(0, 2)).tolist()]
+        y_back = self._a2a(y, back_send, back_recv)
+        # request order on this rank: g ascending, sent tokens ascending, k ascending
+        sel = hit[s_of, g_of]                                            # [n_send, K]
+        slot = (s_of[:, None] * K + torch.arange(K, device=self.device)[None, :])[sel]
+        yr = torch.zeros((n * K, self.d.hidden), dtype=torch.float32, device=self.device)
+        if slot.numel():
+            yr.index_copy_(0, slot, y_back)
+        self.st.combine(x, idx, w, yr, ys)
+        return idx, w

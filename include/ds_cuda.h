@@ -296,6 +296,31 @@ int ds_cuda_prefill_moe(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
 int ds_cuda_prefill_moe_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
                             const ds_cuda_layer_weights_t *layer, float *d_x, int n_tokens, const float *d_logits,
                             int *d_top_idx, float *d_top_w, void *stream);
+/* The three stages of ds_cuda_prefill_moe_dev on caller buffers, for
+ * expert-parallel prefill, where the caller moves rows between devices
+ * between the stages (no counterpart in the reference, which runs on one
+ * host):
+ *  route:   RMSNorm of d_x [n x H] into two BF16 planes d_xn_hi/lo [n x H]
+ *           (v = hi + lo), and the routing d_top_idx / d_top_w [n x top_k].
+ *  experts: for each pair p = (row d_pair_row[p] of d_rows_hi/lo [n_rows x H],
+ *           expert d_pair_expert[p]) the routed expert's output
+ *           d_y[p] [H]; pairs whose expert is outside [0, n_experts) are
+ *           skipped. d_pair_row NULL means row = p / top_k. Also the shared
+ *           expert of d_sh_hi/lo [n_shared_rows x H] into d_ys.
+ *  combine: d_x[s] += sum over k, in ascending expert order, of
+ *           w[s,k] * d_y[s*top_k + k], plus d_ys[s] (ds_moe_decoder.c:785-800). */
+int ds_cuda_prefill_route_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
+                              const ds_cuda_layer_weights_t *layer, const float *d_x, int n_tokens,
+                              const float *d_logits, uint16_t *d_xn_hi, uint16_t *d_xn_lo, int *d_top_idx,
+                              float *d_top_w, void *stream);
+int ds_cuda_prefill_experts_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
+                                const ds_cuda_layer_weights_t *layer, const uint16_t *d_rows_hi,
+                                const uint16_t *d_rows_lo, int n_rows, const int *d_pair_row,
+                                const int *d_pair_expert, int n_pairs, float *d_y, const uint16_t *d_sh_hi,
+                                const uint16_t *d_sh_lo, int n_shared_rows, float *d_ys, void *stream);
+int ds_cuda_prefill_combine_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg, float *d_x,
+                                int n_tokens, const int *d_top_idx, const float *d_top_w, const float *d_y,
+                                const float *d_ys, void *stream);
 /* Synchronises the context's stream and reports DS_CUDA_ETIMEOUT if a
  * prefill kernel's bounded wait gave up since the last check. */
 int ds_cuda_prefill_check(ds_cuda_ctx_t *ctx);

@@ -56,8 +56,10 @@ SIGNATURES = {
     "ds_cuda_prefill_moe_dev": (c_int, [P, P, P, P, c_int, P, P, P, P]),
     "ds_cuda_prefill_check": (c_int, [P]),
     "ds_cuda_prefill_route_dev": (c_int, [P, P, P, P, c_int, P, P, P, P, P, P]),
-    "ds_cuda_prefill_experts_dev": (c_int, [P, P, P, P, P, c_int, P, P, c_int, P, P, P, c_int, P, P]),
-    "ds_cuda_prefill_combine_dev": (c_int, [P, P, P, c_int, P, P, P, P, P]),
+    "ds_cuda_prefill_experts_dev": (c_int, [P, P, P, P, P, c_int, c_int, P, P, c_int, P, P, P, c_int, P, P]),
+    "ds_cuda_prefill_combine_dev": (c_int, [P, P, P, c_int, P, P, P, P, P, P]),
+    "ds_cuda_ep_dispatch_dev": (c_int, [P, c_int, c_int, c_int, c_int, P, P, P, c_int, P, P, P, P, P]),
+    "ds_cuda_ep_pairs_dev": (c_int, [P, c_int, c_int, c_int, P, P, c_int, P, P, P, P]),
     "ds_cuda_prefill_timing": (c_int, [P, c_int]),
     "ds_cuda_prefill_stage_ms": (c_int, [P, P]),
     "ds_synth_normal_bf16": (None, [P, c_size_t, c_uint64, c_float, c_float]),

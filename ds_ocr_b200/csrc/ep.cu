@@ -1,0 +1,204 @@
+// ep.cu — device-side bookkeeping of expert-parallel prefill: which split
+// rows go to which rank (dispatch), which (row, expert) pairs a rank received,
+// and where each returned expert output lands (the combine index).
+//
+// Ranks own contiguous expert blocks of experts_per_rank experts. A token is
+// sent once to every rank owning one of its top-k experts, in the order
+// (destination rank ascending, token ascending); with the row go the k expert
+// ids served there (-1 for the others). Expert outputs come back one row per
+// (token, k) pair in the order (rank ascending, token ascending, k
+// ascending); inv[s*K + k] is that pair's row in the returned stream, so the
+// combine reads them without a scatter.
+//
+// These are planning kernels over a few thousand tokens: one CTA, block-wide
+// scans in chunks of 1024.
+#include "ctx.h"
+
+namespace ds {
+
+constexpr int EP_THREADS = 1024;
+constexpr int EP_META = 8;  // int32 slots after the two BF16 planes of a payload row
+
+// exclusive block scan of one int per thread; returns the block total
+__device__ int ep_scan(int v, int &excl) {
+    __shared__ int warp_tot[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int t = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        warp_tot[lane] = t;  // inclusive
+    }
+    __syncthreads();
+    const int before = warp ? warp_tot[warp - 1] : 0;
+    excl = before + x - v;
+    const int total = warp_tot[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return total;
+}
+
+// Plans the dispatch of n tokens and writes each sent row's expert list into
+// the payload (row pitch `ld` int16 elements; the meta sits at int16 offset
+// 2*H). counts[0..G) = rows per destination, counts[G..2G) = pairs per
+// destination. send_tok[i] = token of send row i.
+__global__ void __launch_bounds__(EP_THREADS) ep_dispatch_plan_kernel(int n, int K, int G, int e_per,
+                                                                      const int *__restrict__ idx, int H, int ld,
+                                                                      uint16_t *payload, int *send_tok, int *counts,
+                                                                      int *inv) {
+    int row_base = 0, pair_base = 0;
+    for (int g = 0; g < G; g++) {
+        int rows_g = 0, pairs_g = 0;
+        for (int c0 = 0; c0 < n; c0 += EP_THREADS) {
+            const int s = c0 + threadIdx.x;
+            int cnt = 0;
+            if (s < n)
+                for (int k = 0; k < K; k++) cnt += idx[s * K + k] / e_per == g;
+            int r_ex, p_ex;
+            const int r_tot = ep_scan(cnt > 0, r_ex);
+            const int p_tot = ep_scan(cnt, p_ex);
+            if (s < n && cnt > 0) {
+                const int row = row_base + rows_g + r_ex;
+                send_tok[row] = s;
+                int *meta = reinterpret_cast<int *>(payload + (size_t)row * ld + 2 * H);
+                int j = 0;
+                for (int k = 0; k < K; k++) {
+                    const int e = idx[s * K + k];
+                    const bool mine = e / e_per == g;
+                    meta[k] = mine ? e : -1;
+                    if (mine) inv[s * K + k] = pair_base + pairs_g + p_ex + j++;
+                }
+                for (int k = K; k < EP_META; k++) meta[k] = -1;
+            }
+            rows_g += r_tot;
+            pairs_g += p_tot;
+        }
+        if (threadIdx.x == 0) {
+            counts[g] = rows_g;
+            counts[G + g] = pairs_g;
+        }
+        row_base += rows_g;
+        pair_base += pairs_g;
+    }
+}
+
+// Copies each send row's two BF16 planes into the payload (one warp per row).
+__global__ void __launch_bounds__(256) ep_pack_rows_kernel(int rows, int H, int ld, const int *__restrict__ send_tok,
+                                                           const uint16_t *__restrict__ xn_hi,
+                                                           const uint16_t *__restrict__ xn_lo, uint16_t *payload,
+                                                           const int *counts, int G) {
+    const int lane = threadIdx.x & 31;
+    const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int total = 0;
+    for (int g = 0; g < G; g++) total += counts[g];
+    if (i >= rows || i >= total) return;
+    const int s = send_tok[i];
+    const uint4 *sh = reinterpret_cast<const uint4 *>(xn_hi + (size_t)s * H);
+    const uint4 *sl = reinterpret_cast<const uint4 *>(xn_lo + (size_t)s * H);
+    uint4 *d = reinterpret_cast<uint4 *>(payload + (size_t)i * ld);
+    for (int j = lane; j < H / 8; j += 32) {
+        d[j] = sh[j];
+        d[H / 8 + j] = sl[j];
+    }
+}
+
+struct EpCounts {
+    int c[8];
+};
+
+// Compact (row, expert) pairs of R received payload rows, row-major; out[g]
+// = pairs whose row came from rank g (rows arrive grouped by source rank,
+// recv.c[g] rows each), out[G] = total.
+__global__ void __launch_bounds__(EP_THREADS) ep_pairs_kernel(int R, int K, int G, EpCounts recv,
+                                                              const uint16_t *__restrict__ payload, int H, int ld,
+                                                              int *pair_row, int *pair_expert, int *out) {
+    int base = 0;
+    __shared__ int per_src[8];
+    if (threadIdx.x < 8) per_src[threadIdx.x] = 0;
+    __syncthreads();
+    for (int c0 = 0; c0 < R; c0 += EP_THREADS) {
+        const int r = c0 + threadIdx.x;
+        int cnt = 0;
+        const int *meta = nullptr;
+        if (r < R) {
+            meta = reinterpret_cast<const int *>(payload + (size_t)r * ld + 2 * H);
+            for (int k = 0; k < K; k++) cnt += meta[k] >= 0;
+        }
+        int ex;
+        const int tot = ep_scan(cnt, ex);
+        if (r < R) {
+            int j = base + ex;
+            for (int k = 0; k < K; k++)
+                if (meta[k] >= 0) {
+                    pair_row[j] = r;
+                    pair_expert[j] = meta[k];
+                    j++;
+                }
+            // source rank of row r
+            int g = 0, acc = recv.c[0];
+            while (g + 1 < G && r >= acc) acc += recv.c[++g];
+            if (cnt) atomicAdd(&per_src[g], cnt);
+        }
+        base += tot;
+    }
+    __syncthreads();
+    if (threadIdx.x < G) out[threadIdx.x] = per_src[threadIdx.x];
+    if (threadIdx.x == 0) out[G] = base;
+}
+
+}  // namespace ds
+
+using namespace ds;
+
+extern "C" int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *c, int n_tokens, int top_k, int n_ranks,
+                                       int experts_per_rank, const int *d_top_idx, const uint16_t *d_xn_hi,
+                                       const uint16_t *d_xn_lo, int hidden, uint16_t *d_payload, int *d_send_tok,
+                                       int *d_counts, int *d_inv, void *stream) {
+    if (!c || !c->ok || n_tokens < 0 || top_k <= 0 || top_k > EP_META || n_ranks <= 0 || n_ranks > 8 ||
+        experts_per_rank <= 0 || hidden % 8 ||
+        (n_tokens > 0 && (!d_top_idx || !d_xn_hi || !d_xn_lo || !d_payload || !d_send_tok || !d_inv)) || !d_counts)
+        return DS_CUDA_EINVAL;
+    cudaSetDevice(c->device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    const int ld = 2 * hidden + 2 * EP_META;
+    ep_dispatch_plan_kernel<<<1, EP_THREADS, 0, st>>>(n_tokens, top_k, n_ranks, experts_per_rank, d_top_idx, hidden,
+                                                      ld, d_payload, d_send_tok, d_counts, d_inv);
+    // rows <= n * min(top_k, n_ranks)
+    const int max_rows = n_tokens * (top_k < n_ranks ? top_k : n_ranks);
+    if (max_rows > 0)
+        ep_pack_rows_kernel<<<(max_rows + 7) / 8, 256, 0, st>>>(max_rows, hidden, ld, d_send_tok, d_xn_hi, d_xn_lo,
+                                                               d_payload, d_counts, n_ranks);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DS_CUDA_OK : ctx_cuda(c, e, "ep_dispatch");
+}
+
+extern "C" int ds_cuda_ep_pairs_dev(ds_cuda_ctx_t *c, int n_rows, int top_k, int n_ranks, const int *recv_counts,
+                                    const uint16_t *d_payload, int hidden, int *d_pair_row, int *d_pair_expert,
+                                    int *d_counts, void *stream) {
+    if (!c || !c->ok || n_rows < 0 || top_k <= 0 || top_k > EP_META || n_ranks <= 0 || n_ranks > 8 ||
+        !recv_counts || !d_counts || (n_rows > 0 && (!d_payload || !d_pair_row || !d_pair_expert)))
+        return DS_CUDA_EINVAL;
+    cudaSetDevice(c->device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    EpCounts rc = {};
+    int sum = 0;
+    for (int g = 0; g < n_ranks; g++) {
+        rc.c[g] = recv_counts[g];
+        sum += recv_counts[g];
+    }
+    if (sum != n_rows) return ctx_fail(c, DS_CUDA_EINVAL, "ep_pairs: receive counts do not add up to n_rows");
+    ep_pairs_kernel<<<1, EP_THREADS, 0, st>>>(n_rows, top_k, n_ranks, rc, d_payload, hidden, 2 * hidden + 2 * EP_META,
+                                              d_pair_row, d_pair_expert, d_counts);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? DS_CUDA_OK : ctx_cuda(c, e, "ep_pairs");
+}

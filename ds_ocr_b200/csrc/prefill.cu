@@ -421,7 +421,8 @@ __global__ void __launch_bounds__(256) pf_count_kernel(int P, const int *__restr
 
 // Copies the split row of each (row, expert) pair to the next free slot of
 // the expert's segment; slot_of[slot] = pair. pair_row == null: row = p / K.
-__global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int K, const int *pair_row,
+// Source rows are ld elements apart (ld % 8 == 0).
+__global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int ld, int K, const int *pair_row,
                                                          const int *pair_expert, int E, const int *seg, int *cursor,
                                                          const uint16_t *rows_hi, const uint16_t *rows_lo,
                                                          uint16_t *xg_hi, uint16_t *xg_lo, int *slot_of) {
@@ -437,8 +438,8 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int K, co
         slot_of[pos] = p;
     }
     pos = __shfl_sync(0xffffffffu, pos, 0);
-    const uint4 *sh = reinterpret_cast<const uint4 *>(rows_hi + (size_t)r * H);
-    const uint4 *sl = reinterpret_cast<const uint4 *>(rows_lo + (size_t)r * H);
+    const uint4 *sh = reinterpret_cast<const uint4 *>(rows_hi + (size_t)r * ld);
+    const uint4 *sl = reinterpret_cast<const uint4 *>(rows_lo + (size_t)r * ld);
     uint4 *dh = reinterpret_cast<uint4 *>(xg_hi + (size_t)pos * H);
     uint4 *dl = reinterpret_cast<uint4 *>(xg_lo + (size_t)pos * H);
     for (int i = lane; i < H / 8; i += 32) {
@@ -448,9 +449,10 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int K, co
 }
 
 // x[s] += (sum over the token's experts in ascending order of w_k * y_k) +
-// shared[s]  (ds_moe_decoder.c:785-800).
+// shared[s]  (ds_moe_decoder.c:785-800). y_k is row s*K + k of yr, or row
+// yrow[s*K + k] when given.
 __global__ void __launch_bounds__(256) pf_combine_kernel(float *x, int M, int H, int K, const int *idx, const float *wt,
-                                                         const float *yr, const float *ys) {
+                                                         const float *yr, const int *yrow, const float *ys) {
     const int lane = threadIdx.x & 31;
     const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (s >= M) return;
@@ -469,7 +471,8 @@ __global__ void __launch_bounds__(256) pf_combine_kernel(float *x, int M, int H,
         for (int j = 0; j < K; j++) {
             const int k = ord[j];
             const float w = wt[(size_t)s * K + k];
-            const float4 y = *reinterpret_cast<const float4 *>(yr + ((size_t)s * K + k) * H + c);
+            const size_t row = yrow ? (size_t)yrow[(size_t)s * K + k] : (size_t)s * K + k;
+            const float4 y = *reinterpret_cast<const float4 *>(yr + row * H + c);
             acc.x = __fmaf_rn(w, y.x, acc.x);
             acc.y = __fmaf_rn(w, y.y, acc.y);
             acc.z = __fmaf_rn(w, y.z, acc.z);
@@ -617,7 +620,8 @@ static int pf_route(ds_cuda_ctx *c, const PfShape &g, const float *d_norm, const
 // expert pair_expert[p]) of rows_hi/lo [n_rows x H] -> y[p] [H]. Shared:
 // sh_hi/lo [n_sh x H] -> ys [n_sh x H]. Either part may be empty.
 static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block, const uint16_t *d_down,
-                      const uint16_t *d_sdown, const uint16_t *rows_hi, const uint16_t *rows_lo, const int *pair_row,
+                      const uint16_t *d_sdown, const uint16_t *rows_hi, const uint16_t *rows_lo, int rows_ld,
+                      const int *pair_row,
                       const int *pair_expert, int P, float *y, const uint16_t *sh_hi, const uint16_t *sh_lo, int n_sh,
                       float *ys, cudaStream_t st) {
     if (P <= 0 && n_sh <= 0) return DS_CUDA_OK;
@@ -649,7 +653,7 @@ static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block,
                                       w->nt, w->dn_tiles, w->nt + 1);
     mark(c, 2, st);
     if (P > 0)
-        pf_scatter_kernel<<<(P + 7) / 8, 256, 0, st>>>(P, H, g.K, pair_row, pair_expert, E, w->seg, w->cursor,
+        pf_scatter_kernel<<<(P + 7) / 8, 256, 0, st>>>(P, H, rows_ld, g.K, pair_row, pair_expert, E, w->seg, w->cursor,
                                                        rows_hi, rows_lo, w->xg_hi, w->xg_lo, w->slot_of);
     // gate/up (+SwiGLU): routed A = expert-sorted rows, shared A = sh planes;
     // B = the expert block [E*2I + 2S rows x H] for both
@@ -703,9 +707,9 @@ static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block,
 
 // Stage 3: x += (sum in ascending expert order of w_k y_k) + ys.
 static int pf_combine(ds_cuda_ctx *c, const PfShape &g, float *d_x, int M, const int *idx, const float *wt,
-                      const float *y, const float *ys, cudaStream_t st) {
+                      const float *y, const int *yrow, const float *ys, cudaStream_t st) {
     if (M <= 0) return DS_CUDA_OK;
-    pf_combine_kernel<<<(M + 7) / 8, 256, 0, st>>>(d_x, M, g.H, g.K, idx, wt, y, ys);
+    pf_combine_kernel<<<(M + 7) / 8, 256, 0, st>>>(d_x, M, g.H, g.K, idx, wt, y, yrow, ys);
     mark(c, 6, st);
     return DS_CUDA_OK;
 }
@@ -729,10 +733,10 @@ int prefill_moe_enqueue(ds_cuda_ctx *c, const PfShape &g, const float *d_norm, c
     PF_GROW(w->ys, w->c_ys, (size_t)M * g.H * 4);
     if ((rc = pf_route(c, g, d_norm, d_router, d_x, M, d_logits, w->xn_hi, w->xn_lo, w->idx, w->wt, st)) < 0) return rc;
     // pairs (token s, slot k) = index s*K + k; its expert is idx[s*K + k]
-    if ((rc = pf_experts(c, g, d_block, d_down, d_sdown, w->xn_hi, w->xn_lo, nullptr, w->idx, (int)P, w->yr,
+    if ((rc = pf_experts(c, g, d_block, d_down, d_sdown, w->xn_hi, w->xn_lo, g.H, nullptr, w->idx, (int)P, w->yr,
                          w->xn_hi, w->xn_lo, M, w->ys, st)) < 0)
         return rc;
-    if ((rc = pf_combine(c, g, d_x, M, w->idx, w->wt, w->yr, w->ys, st)) < 0) return rc;
+    if ((rc = pf_combine(c, g, d_x, M, w->idx, w->wt, w->yr, nullptr, w->ys, st)) < 0) return rc;
     if (d_idx_out) cudaMemcpyAsync(d_idx_out, w->idx, P * 4, cudaMemcpyDeviceToDevice, st);
     if (d_w_out) cudaMemcpyAsync(d_w_out, w->wt, P * 4, cudaMemcpyDeviceToDevice, st);
     cudaError_t e = cudaGetLastError();
@@ -847,13 +851,13 @@ extern "C" int ds_cuda_prefill_route_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder
 
 extern "C" int ds_cuda_prefill_experts_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg,
                                            const ds_cuda_layer_weights_t *layer, const uint16_t *d_rows_hi,
-                                           const uint16_t *d_rows_lo, int n_rows, const int *d_pair_row,
+                                           const uint16_t *d_rows_lo, int rows_ld, int n_rows, const int *d_pair_row,
                                            const int *d_pair_expert, int n_pairs, float *d_y,
                                            const uint16_t *d_sh_hi, const uint16_t *d_sh_lo, int n_shared_rows,
                                            float *d_ys, void *stream) {
     if (!c || !c->ok || !cfg || !layer || n_rows < 0 || n_pairs < 0 || n_shared_rows < 0 ||
         (n_pairs > 0 && (!d_rows_hi || !d_rows_lo || !d_pair_expert || !d_y)) ||
-        (n_pairs > 0 && !d_pair_row && n_rows * cfg->top_k < n_pairs) ||
+        (n_pairs > 0 && !d_pair_row && n_rows * cfg->top_k < n_pairs) || rows_ld < cfg->hidden || rows_ld % 8 ||
         (n_shared_rows > 0 && (!d_sh_hi || !d_sh_lo || !d_ys)))
         return DS_CUDA_EINVAL;
     cudaSetDevice(c->device);
@@ -863,20 +867,20 @@ extern "C" int ds_cuda_prefill_experts_dev(ds_cuda_ctx_t *c, const ds_cuda_decod
     const uint16_t *block, *down, *sdown;
     rc = pf_layer_ptrs(c, cfg, layer, false, nullptr, nullptr, &block, &down, &sdown);
     if (rc < 0) return rc;
-    return pf_experts(c, g, block, down, sdown, d_rows_hi, d_rows_lo, d_pair_row, d_pair_expert, n_pairs, d_y,
+    return pf_experts(c, g, block, down, sdown, d_rows_hi, d_rows_lo, rows_ld, d_pair_row, d_pair_expert, n_pairs, d_y,
                       d_sh_hi, d_sh_lo, n_shared_rows, d_ys, pf_stream(c, stream));
 }
 
 extern "C" int ds_cuda_prefill_combine_dev(ds_cuda_ctx_t *c, const ds_cuda_decoder_config_t *cfg, float *d_x,
                                            int n_tokens, const int *d_top_idx, const float *d_top_w,
-                                           const float *d_y, const float *d_ys, void *stream) {
+                                           const float *d_y, const int *d_y_row, const float *d_ys, void *stream) {
     if (!c || !c->ok || !cfg || n_tokens < 0 || (n_tokens > 0 && (!d_x || !d_top_idx || !d_top_w || !d_y || !d_ys)))
         return DS_CUDA_EINVAL;
     cudaSetDevice(c->device);
     PfShape g = pf_shape(cfg);
     int rc = pf_shape_ok(c, g);
     if (rc < 0) return rc;
-    return pf_combine(c, g, d_x, n_tokens, d_top_idx, d_top_w, d_y, d_ys, pf_stream(c, stream));
+    return pf_combine(c, g, d_x, n_tokens, d_top_idx, d_top_w, d_y, d_y_row, d_ys, pf_stream(c, stream));
 }
 
 extern "C" int ds_cuda_prefill_check(ds_cuda_ctx_t *c) {

@@ -73,22 +73,55 @@ class CudaStages:
                                                           self._p(idx), self._p(w), self._st()), "prefill_route")
         return hi, lo, idx, w
 
-    def experts(self, lw, rows_hi, rows_lo, pair_row, pair_expert, sh_hi, sh_lo):
+    def dispatch(self, idx, hi, lo, n_ranks, e_per):
+        """Pack this rank's rows for the other ranks. Returns (payload
+        [rows x (2H + 16)] int16, send_tok, counts [2G] on the host: rows
+        then pairs per destination, inv [n*K])."""
+        torch = self.torch
+        n, K, H = idx.shape[0], self.d.top_k, self.d.hidden
+        cap = max(1, n * min(K, n_ranks))
+        payload = torch.empty((cap, 2 * H + 16), dtype=torch.int16, device=self.device)
+        send_tok = torch.empty(cap, dtype=torch.int32, device=self.device)
+        counts = torch.empty(2 * n_ranks, dtype=torch.int32, device=self.device)
+        inv = torch.empty(max(1, n * K), dtype=torch.int32, device=self.device)
+        self.ctx.check(self.lib.ds_cuda_ep_dispatch_dev(self.ctx.h, n, K, n_ranks, e_per, self._p(idx), self._p(hi),
+                                                        self._p(lo), H, payload.data_ptr(), send_tok.data_ptr(),
+                                                        counts.data_ptr(), inv.data_ptr(), self._st()),
+                       "ep_dispatch")
+        return payload, counts.tolist(), inv
+
+    def pairs(self, payload, recv_counts):
+        """(row, expert) pairs of the received payload rows; returns
+        (pair_row, pair_expert, pairs per source rank on the host)."""
+        torch = self.torch
+        R, K, G = payload.shape[0], self.d.top_k, len(recv_counts)
+        pr = torch.empty(max(1, R * K), dtype=torch.int32, device=self.device)
+        pe = torch.empty(max(1, R * K), dtype=torch.int32, device=self.device)
+        out = torch.empty(G + 1, dtype=torch.int32, device=self.device)
+        rc = (ctypes.c_int * G)(*recv_counts)
+        self.ctx.check(self.lib.ds_cuda_ep_pairs_dev(self.ctx.h, R, K, G, rc, self._p(payload), self.d.hidden,
+                                                     pr.data_ptr(), pe.data_ptr(), out.data_ptr(), self._st()),
+                       "ep_pairs")
+        o = out.tolist()
+        return pr[:o[G]], pe[:o[G]], o[:G]
+
+    def experts(self, lw, rows_hi, rows_lo, rows_ld, pair_row, pair_expert, sh_hi, sh_lo):
         torch = self.torch
         H = self.d.hidden
         P, S = pair_row.shape[0], sh_hi.shape[0]
         y = torch.empty((P, H), dtype=torch.float32, device=self.device)
         ys = torch.empty((S, H), dtype=torch.float32, device=self.device)
         self.ctx.check(self.lib.ds_cuda_prefill_experts_dev(
-            self.ctx.h, ctypes.byref(self.cfg), self._layer(lw), self._p(rows_hi), self._p(rows_lo),
+            self.ctx.h, ctypes.byref(self.cfg), self._layer(lw), self._p(rows_hi), self._p(rows_lo), rows_ld,
             rows_hi.shape[0], self._p(pair_row), self._p(pair_expert), P, self._p(y), self._p(sh_hi),
             self._p(sh_lo), S, self._p(ys), self._st()), "prefill_experts")
         return y, ys
 
-    def combine(self, x, idx, w, y, ys):
+    def combine(self, x, idx, w, y, y_row, ys):
         self.ctx.check(self.lib.ds_cuda_prefill_combine_dev(self.ctx.h, ctypes.byref(self.cfg), self._p(x),
                                                             x.shape[0], self._p(idx), self._p(w), self._p(y),
-                                                            self._p(ys), self._st()), "prefill_combine")
+                                                            self._p(y_row), self._p(ys), self._st()),
+                       "prefill_combine")
 
     def check(self):
         self.stream.synchronize()
@@ -142,41 +175,19 @@ class ExpertParallelPrefill:
 
     def _moe_layer(self, lw, x, logits):
         torch = self.torch
-        G, K = self.world, self.d.top_k
-        n = x.shape[0]
+        G, H = self.world, self.d.hidden
         hi, lo, idx, w = self.st.route(lw, x, logits)
-        # --- dispatch: one row per (token, destination rank), in rank order,
-        # tokens ascending; with it the K expert ids served there (-1 else)
-        dest = (idx // self.e_per).long()                                # [n, K]
-        ranks = torch.arange(G, device=self.device)
-        hit = dest[:, None, :] == ranks[None, :, None]                   # [n, G, K]
-        need = hit.any(dim=2)                                            # [n, G]
-        send_tok = torch.nonzero(need.t(), as_tuple=False)               # (g, s) sorted by g then s
-        g_of, s_of = send_tok[:, 0], send_tok[:, 1]
-        send_counts = torch.bincount(g_of, minlength=G).tolist()
-        meta = torch.where(hit[s_of, g_of], idx[s_of], torch.full_like(idx[s_of], -1))   # [n_send, K]
-        recv_counts = self._counts(send_counts)
-        # the BF16 planes travel as int32 pairs (a pure reinterpretation)
-        r_hi = self._a2a(hi[s_of].view(torch.int32), send_counts, recv_counts).view(hi.dtype)
-        r_lo = self._a2a(lo[s_of].view(torch.int32), send_counts, recv_counts).view(lo.dtype)
-        r_meta = self._a2a(meta, send_counts, recv_counts)
-        # --- local experts over the received (row, expert) pairs
-        valid = r_meta >= 0
-        pr = torch.nonzero(valid, as_tuple=False)                        # (row, k) row-major
-        pair_row = pr[:, 0].to(torch.int32).contiguous()
-        pair_expert = r_meta[valid].to(torch.int32).contiguous()
-        y, ys = self.st.experts(lw, r_hi, r_lo, pair_row, pair_expert, hi, lo)
-        # --- return one row per pair to the token's rank, in request order
-        rows_from = torch.repeat_interleave(torch.arange(G, device=self.device),
-                                            torch.tensor(recv_counts, device=self.device))
-        back_send = torch.bincount(rows_from[pair_row.long()], minlength=G).tolist() if pair_row.numel() else [0] * G
-        back_recv = [int(v) for v in hit.sum(dim=(0, 2)).tolist()]
+        # dispatch: one payload row per (token, owning rank)
+        payload, counts, inv = self.st.dispatch(idx, hi, lo, G, self.e_per)
+        send_rows, back_recv = counts[:G], counts[G:]
+        recv_rows = self._counts(send_rows)
+        width = payload.shape[1] // 2  # payload rows travel as int32
+        r_payload = self._a2a(payload[:sum(send_rows)].view(torch.int32), send_rows, recv_rows)
+        r_payload = r_payload.view(torch.int16).reshape(-1, 2 * width)
+        # local experts over the received pairs; the shared expert on local rows
+        pair_row, pair_expert, back_send = self.st.pairs(r_payload, recv_rows)
+        y, ys = self.st.experts(lw, r_payload, r_payload[:, H:], 2 * width, pair_row, pair_expert, hi, lo)
+        # outputs return in request order; inv locates each (token, k)
         y_back = self._a2a(y, back_send, back_recv)
-        # request order on this rank: g ascending, sent tokens ascending, k ascending
-        sel = hit[s_of, g_of]                                            # [n_send, K]
-        slot = (s_of[:, None] * K + torch.arange(K, device=self.device)[None, :])[sel]
-        yr = torch.zeros((n * K, self.d.hidden), dtype=torch.float32, device=self.device)
-        if slot.numel():
-            yr.index_copy_(0, slot, y_back)
-        self.st.combine(x, idx, w, yr, ys)
+        self.st.combine(x, idx, w, y_back, inv, ys)
         return idx, w

@@ -302,25 +302,48 @@ int ds_cuda_prefill_moe_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *
  * host):
  *  route:   RMSNorm of d_x [n x H] into two BF16 planes d_xn_hi/lo [n x H]
  *           (v = hi + lo), and the routing d_top_idx / d_top_w [n x top_k].
- *  experts: for each pair p = (row d_pair_row[p] of d_rows_hi/lo [n_rows x H],
- *           expert d_pair_expert[p]) the routed expert's output
- *           d_y[p] [H]; pairs whose expert is outside [0, n_experts) are
- *           skipped. d_pair_row NULL means row = p / top_k. Also the shared
- *           expert of d_sh_hi/lo [n_shared_rows x H] into d_ys.
+ *  experts: for each pair p = (row d_pair_row[p] of d_rows_hi/lo, rows
+ *           rows_ld elements apart (a multiple of 8), expert d_pair_expert[p])
+ *           the routed expert's output d_y[p] [H]; pairs whose expert is
+ *           outside [0, n_experts) are skipped. d_pair_row NULL means
+ *           row = p / top_k. Also the shared expert of d_sh_hi/lo
+ *           [n_shared_rows x H] into d_ys.
  *  combine: d_x[s] += sum over k, in ascending expert order, of
- *           w[s,k] * d_y[s*top_k + k], plus d_ys[s] (ds_moe_decoder.c:785-800). */
+ *           w[s,k] * y_k, plus d_ys[s] (ds_moe_decoder.c:785-800), where y_k
+ *           is row s*top_k + k of d_y, or row d_y_row[s*top_k + k] if given. */
 int ds_cuda_prefill_route_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
                               const ds_cuda_layer_weights_t *layer, const float *d_x, int n_tokens,
                               const float *d_logits, uint16_t *d_xn_hi, uint16_t *d_xn_lo, int *d_top_idx,
                               float *d_top_w, void *stream);
 int ds_cuda_prefill_experts_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
                                 const ds_cuda_layer_weights_t *layer, const uint16_t *d_rows_hi,
-                                const uint16_t *d_rows_lo, int n_rows, const int *d_pair_row,
+                                const uint16_t *d_rows_lo, int rows_ld, int n_rows, const int *d_pair_row,
                                 const int *d_pair_expert, int n_pairs, float *d_y, const uint16_t *d_sh_hi,
                                 const uint16_t *d_sh_lo, int n_shared_rows, float *d_ys, void *stream);
 int ds_cuda_prefill_combine_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg, float *d_x,
                                 int n_tokens, const int *d_top_idx, const float *d_top_w, const float *d_y,
-                                const float *d_ys, void *stream);
+                                const int *d_y_row, const float *d_ys, void *stream);
+/* Expert-parallel bookkeeping (no counterpart in the reference). Ranks own
+ * contiguous blocks of experts_per_rank experts (n_ranks <= 8, top_k <= 8).
+ * A payload row is [hi plane H | lo plane H | 8 int32 expert ids] as
+ * uint16_t, row pitch 2*H + 16.
+ *  dispatch: plans sending each token once to every rank owning one of its
+ *            experts (rank ascending, token ascending) and packs those rows
+ *            into d_payload (capacity n_tokens * min(top_k, n_ranks) rows);
+ *            d_send_tok[i] = token of row i; d_counts[0..G) rows and
+ *            d_counts[G..2G) (token, expert) pairs per destination rank;
+ *            d_inv[s*top_k + k] = row of that pair's output in the stream
+ *            that comes back (rank, token, k ascending).
+ *  pairs:    for n_rows received payload rows (recv_counts [n_ranks], a HOST
+ *            array, rows per source rank in rank order) the compact
+ *            row-major (row, expert) pairs; d_counts[0..G) pairs per source
+ *            rank, d_counts[G] all pairs. */
+int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *ctx, int n_tokens, int top_k, int n_ranks, int experts_per_rank,
+                            const int *d_top_idx, const uint16_t *d_xn_hi, const uint16_t *d_xn_lo, int hidden,
+                            uint16_t *d_payload, int *d_send_tok, int *d_counts, int *d_inv, void *stream);
+int ds_cuda_ep_pairs_dev(ds_cuda_ctx_t *ctx, int n_rows, int top_k, int n_ranks, const int *recv_counts,
+                         const uint16_t *d_payload, int hidden, int *d_pair_row, int *d_pair_expert, int *d_counts,
+                         void *stream);
 /* Synchronises the context's stream and reports DS_CUDA_ETIMEOUT if a
  * prefill kernel's bounded wait gave up since the last check. */
 int ds_cuda_prefill_check(ds_cuda_ctx_t *ctx);

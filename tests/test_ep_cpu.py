@@ -33,20 +33,53 @@ class StandInStages:
     def _val(hi, lo):
         return hi.view(torch.bfloat16).float() + lo.view(torch.bfloat16).float()
 
-    def experts(self, lw, rows_hi, rows_lo, pair_row, pair_expert, sh_hi, sh_lo):
-        v = self._val(rows_hi, rows_lo)[pair_row.long()]
+    def dispatch(self, idx, hi, lo, G, e_per):
+        n = idx.shape[0]
+        dest = idx.long() // e_per
+        rows, tok, meta, inv = [], [], [], torch.zeros(n * K, dtype=torch.int32)
+        counts, pairs = [0] * G, [0] * G
+        base = 0
+        for g in range(G):
+            for s_ in range(n):
+                ks = [k for k in range(K) if dest[s_, k] == g]
+                if not ks:
+                    continue
+                counts[g] += 1
+                m = [int(idx[s_, k]) if k in ks else -1 for k in range(K)] + [-1] * (8 - K)
+                rows.append(torch.cat([hi[s_], lo[s_], torch.tensor(m, dtype=torch.int32).view(torch.int16)]))
+                for k in ks:
+                    inv[s_ * K + k] = base
+                    base += 1
+                    pairs[g] += 1
+        payload = torch.stack(rows) if rows else torch.zeros((1, 2 * H + 16), dtype=torch.int16)
+        return payload, counts + pairs, inv
+
+    def pairs(self, payload, recv_counts):
+        R = payload.shape[0]
+        meta = payload[:, 2 * H:].contiguous().view(torch.int32)[:, :K] if R else torch.zeros((0, K), dtype=torch.int32)
+        src = torch.repeat_interleave(torch.arange(len(recv_counts)), torch.tensor(recv_counts))
+        valid = meta >= 0
+        pr = torch.nonzero(valid)[:, 0].to(torch.int32)
+        pe = meta[valid].to(torch.int32)
+        per = torch.bincount(src[pr.long()], minlength=len(recv_counts)).tolist() if pr.numel() else [0] * len(recv_counts)
+        return pr, pe, per
+
+    def experts(self, lw, rows_hi, rows_lo, rows_ld, pair_row, pair_expert, sh_hi, sh_lo):
+        v = self._val(rows_hi[:, :H].contiguous(), rows_lo[:, :H].contiguous())[pair_row.long()]
         e = pair_expert.float()[:, None]
         y = torch.tanh(v * (e + 1.0) + 0.1 * e)
         ys = 0.5 * self._val(sh_hi, sh_lo)
         return y, ys
 
-    def combine(self, x, idx, w, y, ys):
+    def combine(self, x, idx, w, y, y_row, ys):
         n = x.shape[0]
         order = torch.argsort(idx, dim=1, stable=True)
         acc = torch.zeros_like(x)
         for j in range(K):
             k = order[:, j]
             rows = torch.arange(n) * K + k
+            if y_row is not None:
+                rows = y_row[rows].long()
             acc = acc + w[torch.arange(n), k][:, None] * y[rows]
         x += acc + ys
 

@@ -89,3 +89,71 @@ def test_ep_two_gpus_bit_identical_to_one():
     idx = np.concatenate([got[0][1], got[1][1]])
     assert np.array_equal(idx, idx_ref)
     assert np.array_equal(out, ref)
+
+
+class _SelfDist:
+    @staticmethod
+    def all_to_all_single(out, inp, out_splits=None, in_splits=None):
+        out.copy_(inp)
+
+
+def test_ep_one_rank_path_matches_prefill(cuda_ctx):
+    # the expert-parallel code path (dispatch, pairs, payload rows, combine
+    # through the return index) at one rank equals the fused single-GPU call
+    import torch
+    from ds_ocr_b200 import synth
+    from ds_ocr_b200.ep import CudaStages, ExpertParallelPrefill
+    from ds_ocr_b200.prefill import Prefill
+    model = synth.Model(n_layers=2, vocab=256)
+    x, lg = _inputs(model.d)
+    ref = x.copy()
+    idx_ref, w_ref = Prefill(model.d, cuda_ctx).moe_layer(model.layers[1], ref, lg)
+    st = CudaStages(model.d, cuda_ctx)
+    ep = ExpertParallelPrefill(model.d, st, _SelfDist, 0, 1, st.device)
+    with torch.cuda.stream(st.stream):
+        tx = torch.from_numpy(x).to(st.device)
+        tl = torch.from_numpy(lg).to(st.device)
+    idx, w = ep.moe_layer(model.layers[1], tx, tl)
+    st.check()
+    assert np.array_equal(idx.cpu().numpy(), idx_ref)
+    assert np.array_equal(tx.cpu().numpy(), ref)
+
+
+def test_dispatch_and_pairs_kernels(cuda_ctx):
+    # the bookkeeping kernels against the CPU stand-in's reading of the same
+    # contract, for 4 ranks of 16 experts
+    import torch
+    from test_ep_cpu import StandInStages
+    from ds_ocr_b200 import synth
+    from ds_ocr_b200.ep import CudaStages
+    model = synth.Model(n_layers=2, vocab=256)
+    st = CudaStages(model.d, cuda_ctx)
+    n, K, H, G = 300, model.d.top_k, model.d.hidden, 4
+    rng = np.random.default_rng(3)
+    idx = np.stack([rng.choice(64, K, replace=False) for _ in range(n)]).astype(np.int32)
+    idx[:20] = np.arange(K)  # all on rank 0
+    hi = rng.integers(-30000, 30000, (n, H)).astype(np.int16)
+    lo = rng.integers(-30000, 30000, (n, H)).astype(np.int16)
+    with torch.cuda.stream(st.stream):
+        t_idx, t_hi, t_lo = (torch.from_numpy(a).to(st.device) for a in (idx, hi, lo))
+        payload, counts, inv = st.dispatch(t_idx, t_hi, t_lo, G, 64 // G)
+    ref = StandInStages()
+    import test_ep_cpu as T
+    saved = T.K, T.H
+    T.K, T.H = K, H  # the stand-in reads the shapes from its module
+    try:
+        r_payload, r_counts, r_inv = ref.dispatch(torch.from_numpy(idx), torch.from_numpy(hi), torch.from_numpy(lo),
+                                                  G, 64 // G)
+        recv = [0, 0, 0, 0]
+        rows = sum(r_counts[:G])
+        recv = [rows // 4, rows // 4, rows // 4, rows - 3 * (rows // 4)]
+        rpr, rpe, rper = ref.pairs(r_payload, recv)
+    finally:
+        T.K, T.H = saved
+    assert counts == r_counts
+    rows = sum(counts[:G])
+    assert torch.equal(payload[:rows].cpu(), r_payload)
+    assert torch.equal(inv[:n * K].cpu(), r_inv)
+    # the payload as if received from 4 ranks with these row counts
+    pr, pe, per = st.pairs(payload[:rows], recv)
+    assert torch.equal(pr.cpu(), rpr) and torch.equal(pe.cpu(), rpe) and per == rper

@@ -41,6 +41,7 @@ SIGNATURES = {
     "ds_cuda_matvec_bf16": (c_int, [P, P, P, P, P, c_int, c_int]),
     "ds_cuda_int8_quantize_bf16": (c_int, [P, P, c_int, c_int, P, P, P]),
     "ds_cuda_argmax_matvec_bf16_dev": (c_int, [P, P, P, c_int, c_int, P, P, P]),
+    "ds_cuda_argmax_matvec_bf16_batch_dev": (c_int, [P, P, P, c_int, c_int, c_int, P, P, P]),
     "ds_cuda_moe_layer_dev": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P]),
     "ds_cuda_moe_experts_noalloc": (c_int, [P, P, P, P, c_int, c_int, c_int, P, P]),
     "ds_cuda_decoder_create": (c_int, [P, P, P, P, P]),

@@ -171,7 +171,7 @@ extern "C" void ds_cuda_free(ds_cuda_ctx_t *c) {
         if (e) cudaEventDestroy(e);
     for (auto &kv : c->regs) cudaFree(kv.second.dev);
     void *bufs[] = {c->d_tickets, c->d_slots, c->d_tok, c->d_val, c->d_scores, c->d_idx, c->d_wt,
-                    c->d_x, c->d_out, c->d_h, c->d_tmp};
+                    c->d_x, c->d_out, c->d_h, c->d_tmp, c->d_lt_planes, c->d_lt_err};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (c->pin) cudaFreeHost(c->pin);
@@ -545,6 +545,15 @@ extern "C" int ds_cuda_argmax_matvec_bf16_batch(ds_cuda_ctx_t *c, const float *x
     CK(d2h_sync(c, tokens, c->d_tok, (size_t)batch * sizeof(int)));
     if (logits) CK(d2h_sync(c, logits, c->d_val, (size_t)batch * sizeof(float)));
     return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_argmax_matvec_bf16_batch_dev(ds_cuda_ctx_t *c, const float *d_x, const uint16_t *d_W,
+                                                    int in_dim, int out_dim, int batch, int *d_tokens,
+                                                    float *d_logits, void *stream) {
+    if (!c || !d_x || !d_W || !d_tokens || !d_logits || batch <= 0 || batch > 512)
+        return ctx_fail(c, DS_CUDA_EINVAL, "argmax_batch_dev: bad argument");
+    cudaSetDevice(c->device);
+    return batch_argmax_enqueue(c, d_x, d_W, in_dim, out_dim, batch, d_tokens, d_logits, pick_stream(c, stream));
 }
 
 extern "C" int ds_cuda_matvec_bf16(ds_cuda_ctx_t *c, float *y, const float *x, const uint16_t *W, const float *bias,

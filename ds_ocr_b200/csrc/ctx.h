@@ -36,6 +36,10 @@ struct ds_cuda_ctx {
     size_t x_cap = 0, out_cap = 0, h_cap = 0;
     void *d_tmp = nullptr;
     size_t tmp_cap = 0;
+    // tensor-core batched LM head: split input planes, error flag
+    void *d_lt_planes = nullptr;
+    size_t lt_planes_cap = 0;
+    void *d_lt_err = nullptr;
     // pinned staging
     void *pin = nullptr;
     size_t pin_cap = 0;
@@ -58,5 +62,7 @@ void ctx_release_models(ds_cuda_ctx *c);
 void prefill_release(ds_cuda_ctx *c);
 int moe_layer_enqueue(ds_cuda_ctx *c, ds::MoeArgs &a, const uint16_t *d_router, int n_experts, int *d_idx,
                       float *d_wt, cudaStream_t st, bool pdl);
+int lmhead_tc_enqueue(ds_cuda_ctx *c, const float *d_x, const uint16_t *d_W, int in_dim, int out_dim, int batch,
+                      int *d_tok, float *d_val, cudaStream_t st);
 int batch_argmax_enqueue(ds_cuda_ctx *c, const float *d_x, const uint16_t *d_W, int in_dim, int out_dim, int batch,
                          int *d_tok, float *d_val, cudaStream_t st);

@@ -35,6 +35,7 @@
 #include <cuda.h>
 #include "ctx.h"
 #include "umma.cuh"
+#include "tmap.h"
 
 namespace ds {
 
@@ -551,38 +552,6 @@ static int pf_work(ds_cuda_ctx *c, cudaStream_t st, PfWork **out) {
         if (_rc < 0) return _rc;                                                          \
     } while (0)
 
-// cuTensorMapEncodeTiled, looked up through the runtime so the library does
-// not link the driver library directly (it loads where no driver exists).
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-static EncodeTiledFn encode_tiled() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-    }
-    return fn;
-}
-
-// BF16 row-major [rows x cols] as a 2-D tensor map with 64 x box_rows boxes,
-// 128-byte swizzle (the UMMA K-major canonical layout). Rows past `rows`
-// read as zeros (partial tiles).
-static bool pf_map(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
-    EncodeTiledFn enc = encode_tiled();
-    if (!enc || !base) return false;
-    cuuint64_t dims[2] = {cols, rows < 1 ? 1 : rows};
-    cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {(cuuint32_t)PF_BK, box_rows};
-    cuuint32_t es[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 struct PfShape {
     int H, I, S, E, K;
     float eps;
@@ -661,9 +630,9 @@ static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block,
     memset(&gu, 0, sizeof gu);
     const uint64_t brows = (uint64_t)E * 2 * I + 2 * (uint64_t)S;
     const uint16_t *shh = n_sh > 0 ? sh_hi : w->xg_hi, *shl = n_sh > 0 ? sh_lo : w->xg_lo;
-    bool ok = pf_map(&gu.a_hi[0], w->xg_hi, H, Pz, PF_BM) && pf_map(&gu.a_lo[0], w->xg_lo, H, Pz, PF_BM) &&
-              pf_map(&gu.a_hi[1], shh, H, Sz, PF_BM) && pf_map(&gu.a_lo[1], shl, H, Sz, PF_BM) &&
-              pf_map(&gu.b[0], d_block, H, brows, 128) && pf_map(&gu.b[1], d_block, H, brows, 128);
+    bool ok = tmap_bf16(&gu.a_hi[0], w->xg_hi, H, Pz, PF_BM) && tmap_bf16(&gu.a_lo[0], w->xg_lo, H, Pz, PF_BM) &&
+              tmap_bf16(&gu.a_hi[1], shh, H, Sz, PF_BM) && tmap_bf16(&gu.a_lo[1], shl, H, Sz, PF_BM) &&
+              tmap_bf16(&gu.b[0], d_block, H, brows, 128) && tmap_bf16(&gu.b[1], d_block, H, brows, 128);
     if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill: tensor map encoding failed");
     gu.tiles = w->gu_tiles;
     gu.n_tiles = w->nt;
@@ -686,9 +655,9 @@ static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block,
     // down: routed A = SwiGLU rows [P x I], shared A = [n_sh x S]
     PfGemm dn;
     memset(&dn, 0, sizeof dn);
-    ok = pf_map(&dn.a_hi[0], w->hg_hi, I, Pz, PF_BM) && pf_map(&dn.a_lo[0], w->hg_lo, I, Pz, PF_BM) &&
-         pf_map(&dn.a_hi[1], w->hs_hi, S, Sz, PF_BM) && pf_map(&dn.a_lo[1], w->hs_lo, S, Sz, PF_BM) &&
-         pf_map(&dn.b[0], d_down, I, (uint64_t)E * H, PF_BN) && pf_map(&dn.b[1], d_sdown, S, H, PF_BN);
+    ok = tmap_bf16(&dn.a_hi[0], w->hg_hi, I, Pz, PF_BM) && tmap_bf16(&dn.a_lo[0], w->hg_lo, I, Pz, PF_BM) &&
+         tmap_bf16(&dn.a_hi[1], w->hs_hi, S, Sz, PF_BM) && tmap_bf16(&dn.a_lo[1], w->hs_lo, S, Sz, PF_BM) &&
+         tmap_bf16(&dn.b[0], d_down, I, (uint64_t)E * H, PF_BN) && tmap_bf16(&dn.b[1], d_sdown, S, H, PF_BN);
     if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill: tensor map encoding failed");
     dn.tiles = w->dn_tiles;
     dn.n_tiles = w->nt + 1;

@@ -155,9 +155,15 @@ int ds_cuda_lm_head_argmax(ds_cuda_ctx_t *ctx, const float *x, const uint16_t *W
                            int vocab);
 int ds_cuda_argmax_matvec_bf16(ds_cuda_ctx_t *ctx, const float *x, const uint16_t *W_bf16, int in_dim,
                                int out_dim, float *logit);
-/* B independent inputs x[B x in_dim] (the reference loops; here one pass). */
+/* B independent inputs x[B x in_dim] (the reference loops). B = 2..64 with
+ * in_dim % 64 == 0 is one tensor-core pass over W (the inputs split into two
+ * BF16 planes, F32 accumulation); other shapes run one matvec per input. */
 int ds_cuda_argmax_matvec_bf16_batch(ds_cuda_ctx_t *ctx, const float *x, const uint16_t *W_bf16,
                                      int in_dim, int out_dim, int batch, int *tokens, float *logits);
+/* Same on device buffers (W registered, d_W its device copy), enqueued on
+ * `stream` (NULL: the context's stream). */
+int ds_cuda_argmax_matvec_bf16_batch_dev(ds_cuda_ctx_t *ctx, const float *d_x, const uint16_t *d_W, int in_dim,
+                                         int out_dim, int batch, int *d_tokens, float *d_logits, void *stream);
 
 /* ds_metal_matvec_bf16 (ds_metal.h:168-174): y = W x (+ bias). */
 int ds_cuda_matvec_bf16(ds_cuda_ctx_t *ctx, float *y, const float *x, const uint16_t *W_bf16,

@@ -14,6 +14,7 @@ Workloads (synthetic random-init weights):
             weights (5.0 GB) so no step finds its experts in L2
   prefill   config 4: batched MoE prefill, 3328 tokens through the 11 MoE
             layers (router logits overridden, skewed routing)
+  lm_head   config 1: argmax LM head 129280 x 1280 at batch 64 (and batch 1)
 --impl reference times the reference's own CPU code (compiled unmodified
 into oracle/_ref/libdsref.so) on the same workload, on this host's cores.
 """
@@ -409,6 +410,118 @@ def ref_decode_time(model, ks, vs, threads, budget_s, max_steps):
 
 
 # ---------------------------------------------------------------------------
+# Argmax LM head (config 1), batch 64 and batch 1
+# ---------------------------------------------------------------------------
+LM_BATCH = 64
+
+
+def lm_inputs():
+    from ds_ocr_b200 import synth
+    W = synth.normal_bf16((129280, 1280), 300)
+    X = synth.normal_f32((LM_BATCH, 1280), 2)
+    return W, X
+
+
+def lm_config():
+    return {"workload": "config1_lm_head_b64", "vocab": 129280, "hidden": 1280, "batch": LM_BATCH,
+            "kernel": "tcgen05 argmax (split-BF16 inputs, one pass over W)",
+            "l2": "each call streams 331 MB of weights (> 126 MB L2)"}
+
+
+def run_ours_lmhead(args, rank, world, pg):
+    import torch
+    from ds_ocr_b200 import cuda
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = cuda.Context(local if world > 1 else 0)
+    lib = ctx.lib
+    W, X = lm_inputs()
+    ctx.register(W)
+    dW = ctx.device_ptr(W)
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    dX = torch.from_numpy(X).cuda()
+    tok = torch.zeros(LM_BATCH, dtype=torch.int32, device="cuda")
+    val = torch.zeros(LM_BATCH, device="cuda")
+    sp = st.cuda_stream
+
+    def call(B):
+        if B == 1:
+            rc = lib.ds_cuda_argmax_matvec_bf16_dev(ctx.h, dX.data_ptr(), dW, 1280, 129280, tok.data_ptr(),
+                                                    val.data_ptr(), sp)
+        else:
+            rc = lib.ds_cuda_argmax_matvec_bf16_batch_dev(ctx.h, dX.data_ptr(), dW, 1280, 129280, B, tok.data_ptr(),
+                                                          val.data_ptr(), sp)
+        assert rc == 0, lib.ds_cuda_last_error(ctx.h)
+
+    def timed(B, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(n):
+            call(B)
+        e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    for _ in range(args.warmup):
+        call(LM_BATCH)
+        call(1)
+    st.synchronize()
+    barrier(pg)
+    with ClockSampler(local) as clk:
+        ms = timed(LM_BATCH, args.steps)
+    ms_max = max_over_ranks(ms, pg)
+    value = world * LM_BATCH * args.steps / (ms_max / 1e3)
+    ms1 = timed(1, args.steps)
+    # e2e: host inputs in, tokens and logits out, through the host API
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(3, args.steps // 4)
+    t0.record(st)
+    for _ in range(n_e2e):
+        ctx.argmax_batch(X, W, 1280, 129280)
+    t1.record(st)
+    t1.synchronize()
+    e2e = world * LM_BATCH * n_e2e / (max_over_ranks(t0.elapsed_time(t1), pg) / 1e3)
+    pk = peaks()
+    us = ms_max / args.steps * 1e3
+    ach = LM_BYTES / (us * 1e-6) / 1e9
+    res = {
+        "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
+        "metric": "argmax LM head tokens/s (batch 64, vocab 129280 x 1280 BF16)", "unit": "tokens/s",
+        "dtype": "bf16 weights, f32 inputs as two bf16 planes, f32 accumulate",
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": LM_BATCH * 1280 * 4,
+                "d2h_bytes_per_step": LM_BATCH * 8},
+        "gpu_launches": 2 * args.steps, "config": lm_config(),
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": ach / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "lt_argmax_kernel (330,956,800 B per call)", "kernel_us": us,
+                     "peak_source": pk["source"]},
+        "batch1": {"us_per_call": ms1 / args.steps * 1e3, "tokens_per_s": args.steps / (ms1 / 1e3),
+                   "kernel": "argmax_tma_kernel"},
+    }
+    del dX, tok, val
+    torch.cuda.synchronize()
+    ctx.close()
+    return res
+
+
+def ref_lmhead_time(threads, budget_s):
+    """The reference's ds_argmax_matvec_bf16 (compiled unmodified), one call
+    per input as the reference does, on `threads` host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    W, X = lm_inputs()
+    r = O.ref()
+    r.ref_set_threads(threads)
+    n, t_total = 0, 0.0
+    while t_total < budget_s and n < 4 * LM_BATCH:
+        t = time.perf_counter()
+        r.ref_argmax(X[n % LM_BATCH].ctypes.data, W.ctypes.data, 1280, 129280, None)
+        t_total += time.perf_counter() - t
+        n += 1
+    return n / t_total, n
+
+
+# ---------------------------------------------------------------------------
 # Batched MoE prefill (config 4)
 # ---------------------------------------------------------------------------
 PF_TOKENS = 3328
@@ -431,9 +544,10 @@ def prefill_inputs(d):
     return x, logits
 
 
-def prefill_config():
-    return {"workload": "config4_prefill_moe", "model": "DeepSeek3B-MoE MoE layers 1-11 (random init)",
-            "tokens": PF_TOKENS, "layers": PF_LAYERS, "hidden": 1280, "experts": 64, "top_k": 6,
+def prefill_config(n_layers=PF_LAYERS):
+    return {"workload": "config4_prefill_moe" if n_layers == PF_LAYERS else f"prefill_moe_{n_layers}_layers",
+            "model": "DeepSeek3B-MoE MoE layers 1-11 (random init)",
+            "tokens": PF_TOKENS, "layers": n_layers, "hidden": 1280, "experts": 64, "top_k": 6,
             "routing": "logits N(0,1) + per-expert bias N(0,0.5) (attention not included)",
             "gemm": "tcgen05 split-BF16 activations x BF16 weights, F32 accumulate",
             "l2": "each step streams 5.0 GB of expert weights and 0.5 GB of activations (> 126 MB L2)"}
@@ -448,7 +562,9 @@ def run_ours_prefill(args, rank, world, pg, model):
     d = model.d
     pf = Prefill(d, ctx)
     x, logits = prefill_inputs(d)
-    layers = model.layers[1:1 + PF_LAYERS]
+    n_layers = args.prefill_layers
+    layers = model.layers[1:1 + n_layers]
+    logits = logits[:n_layers]
     ep = None
     a, b = 0, PF_TOKENS
     if world > 1:
@@ -528,8 +644,8 @@ def run_ours_prefill(args, rank, world, pg, model):
             for lw, lg in zip(layers, logits):
                 pf.moe_layer(lw, xs, lg)
         t1.record(st)
-        h2d = PF_LAYERS * PF_TOKENS * (d.hidden + d.n_experts) * 4
-        d2h = PF_LAYERS * PF_TOKENS * (d.hidden + 2 * d.top_k) * 4
+        h2d = n_layers * PF_TOKENS * (d.hidden + d.n_experts) * 4
+        d2h = n_layers * PF_TOKENS * (d.hidden + 2 * d.top_k) * 4
     else:
         hx = torch.from_numpy(x[a:b].copy()).pin_memory()
         hl = [torch.from_numpy(l[a:b].copy()).pin_memory() for l in logits]
@@ -542,7 +658,7 @@ def run_ours_prefill(args, rank, world, pg, model):
             run_layers(dx, dlg)
             out.copy_(dx, non_blocking=True)
         t1.record(st)
-        h2d = (b - a) * (d.hidden + PF_LAYERS * d.n_experts) * 4
+        h2d = (b - a) * (d.hidden + n_layers * d.n_experts) * 4
         d2h = (b - a) * d.hidden * 4
     t1.synchronize()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1), pg)
@@ -551,14 +667,14 @@ def run_ours_prefill(args, rank, world, pg, model):
     peak_t = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
     # expert-parallel: rank 0's GEMM does about 1/G of the layer's work
     gu_ach = PF_FLOPS_GU_LAYER / world / (stages[3] / 1e3) / 1e12
-    step_ach = PF_FLOPS_LAYER * PF_LAYERS * args.steps / (ms_max / 1e3) / 1e12 / world
+    step_ach = PF_FLOPS_LAYER * n_layers * args.steps / (ms_max / 1e3) / 1e12 / world
     res = {
         "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
         "metric": "MoE prefill tokens/s (3328 tokens x 11 MoE layers, 64 experts top-6 + 2 shared)",
         "unit": "tokens/s", "dtype": "bf16 weights, f32 activations as two bf16 planes, f32 accumulate",
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": 6 * PF_LAYERS * args.steps,
-        "config": dict(prefill_config(), parallelism=f"ep{world}" if world > 1 else "single GPU",
+        "gpu_launches": 6 * n_layers * args.steps,
+        "config": dict(prefill_config(n_layers), parallelism=f"ep{world}" if world > 1 else "single GPU",
                        tokens_per_rank=b - a),
         "scaling": "strong" if world > 1 else "weak",
         "roofline": {"bound": "tensor", "achieved": gu_ach, "peak": peak_t, "unit": "TFLOP/s",
@@ -567,7 +683,7 @@ def run_ours_prefill(args, rank, world, pg, model):
                                "the split-BF16 A operand doubles the tensor work (not counted)",
                      "kernel_us": stages[3] * 1e3, "peak_source": pk["source"] + " (sustained bf16)"},
         "step_roofline": {"bound": "tensor", "achieved": step_ach, "peak": peak_t, "unit": "TFLOP/s",
-                          "frac": step_ach / peak_t, "flops_per_step": PF_FLOPS_LAYER * PF_LAYERS,
+                          "frac": step_ach / peak_t, "flops_per_step": PF_FLOPS_LAYER * n_layers,
                           "stage_us": dict(zip(["norm_route", "plan", "scatter", "gemm_gate_up", "gemm_down",
                                                 "combine"], [round(float(s) * 1e3, 1) for s in stages]))},
     }
@@ -606,10 +722,12 @@ def main():
     ap.add_argument("--steps", type=int, default=224)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer", "prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer", "prefill", "lm_head"])
     ap.add_argument("--engine", type=int, default=0, choices=[0, 1],
                     help="decode engine: 0 CUDA graph of per-phase kernels, 1 persistent kernel")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
+    ap.add_argument("--prefill-layers", type=int, default=PF_LAYERS,
+                    help="prefill: MoE layers per step (11 = config 4; fewer only for small profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -626,6 +744,10 @@ def main():
             v, n = ref_decode_time(model, ks, vs, T, max(args.cpu_budget, 1.0), max_steps=args.steps)
             metric = "decode tokens/s (greedy, batch 1 per GPU, 12-layer DeepSeek3B-MoE, 662-token KV prefix)"
             cfg, sample = decode_config(1024), f"{n} greedy ds_decoder_forward steps from position 663"
+        elif args.workload == "lm_head":
+            v, n = ref_lmhead_time(T, max(args.cpu_budget, 1.0))
+            metric = "argmax LM head tokens/s (batch 64, vocab 129280 x 1280 BF16)"
+            cfg, sample = lm_config(), f"{n} ds_argmax_matvec_bf16 calls (one per input)"
         elif args.workload == "prefill":
             from ds_ocr_b200 import synth
             v, n = ref_prefill_time(synth.Model(), T, max(args.cpu_budget, 1.0))
@@ -650,6 +772,8 @@ def main():
         from ds_ocr_b200 import synth
         model = synth.Model()
         res = run_ours_prefill(args, rank, world, pg, model)
+    elif args.workload == "lm_head":
+        res = run_ours_lmhead(args, rank, world, pg)
     else:
         res = run_ours_moe(args, rank, world, pg)
     if rank != 0:
@@ -658,8 +782,9 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "dtype": res["dtype"],
             "config": res["config"], "e2e": res["e2e"], "roofline": res["roofline"], "clocks": res["clocks"],
             "gpu_launches": res["gpu_launches"]}
-    if "step_roofline" in res:
-        line["step_roofline"] = res["step_roofline"]
+    for k in ("step_roofline", "batch1"):
+        if k in res:
+            line[k] = res[k]
     line.update(common)
     if "scaling" in res:
         line["scaling"] = res["scaling"]
@@ -668,6 +793,9 @@ def main():
             if args.workload == "decode":
                 v, n = ref_decode_time(model, ks, vs, T, args.cpu_budget, max_steps=64)
                 sample = f"{n} greedy ds_decoder_forward steps from position 663"
+            elif args.workload == "lm_head":
+                v, n = ref_lmhead_time(T, args.cpu_budget)
+                sample = f"{n} ds_argmax_matvec_bf16 calls (one per input)"
             elif args.workload == "prefill":
                 v, n = ref_prefill_time(model, T, args.cpu_budget)
                 sample = f"{n} of 11 MoE layers of the prefill block at 3328 tokens"

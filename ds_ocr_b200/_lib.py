@@ -56,6 +56,7 @@ SIGNATURES = {
     "ds_cuda_prefill_moe": (c_int, [P, P, P, P, c_int, P, P, P]),
     "ds_cuda_prefill_moe_dev": (c_int, [P, P, P, P, c_int, P, P, P, P]),
     "ds_cuda_prefill_check": (c_int, [P]),
+    "ds_cuda_skinny_matmul_dev": (c_int, [P, P, c_int, c_int, P, c_int, P, P, P]),
     "ds_cuda_prefill_route_dev": (c_int, [P, P, P, P, c_int, P, P, P, P, P, P]),
     "ds_cuda_prefill_experts_dev": (c_int, [P, P, P, P, P, c_int, c_int, P, P, c_int, P, P, P, c_int, P, P]),
     "ds_cuda_prefill_combine_dev": (c_int, [P, P, P, c_int, P, P, P, P, P, P]),

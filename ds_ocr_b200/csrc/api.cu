@@ -171,7 +171,7 @@ extern "C" void ds_cuda_free(ds_cuda_ctx_t *c) {
         if (e) cudaEventDestroy(e);
     for (auto &kv : c->regs) cudaFree(kv.second.dev);
     void *bufs[] = {c->d_tickets, c->d_slots, c->d_tok, c->d_val, c->d_scores, c->d_idx, c->d_wt,
-                    c->d_x, c->d_out, c->d_h, c->d_tmp, c->d_lt_planes, c->d_lt_err};
+                    c->d_x, c->d_out, c->d_h, c->d_tmp, c->d_lt_planes, c->d_lt_err, c->d_sk_scratch};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (c->pin) cudaFreeHost(c->pin);

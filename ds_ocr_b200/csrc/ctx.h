@@ -40,6 +40,9 @@ struct ds_cuda_ctx {
     void *d_lt_planes = nullptr;
     size_t lt_planes_cap = 0;
     void *d_lt_err = nullptr;
+    // multi-stream GEMM standalone entry: planes + tile list
+    void *d_sk_scratch = nullptr;
+    size_t sk_scratch_cap = 0;
     // pinned staging
     void *pin = nullptr;
     size_t pin_cap = 0;

@@ -350,6 +350,12 @@ int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *ctx, int n_tokens, int top_k, int n_r
 int ds_cuda_ep_pairs_dev(ds_cuda_ctx_t *ctx, int n_rows, int top_k, int n_ranks, const int *recv_counts,
                          const uint16_t *d_payload, int hidden, int *d_pair_row, int *d_pair_expert, int *d_counts,
                          void *stream);
+/* The multi-stream decode GEMM on its own (no counterpart in the
+ * reference): d_y [n x N] = d_x [n x K] . d_W^T (+ d_resid), n <= 64 token
+ * rows, K % 64 == 0, on the tensor cores with the inputs split into two
+ * BF16 planes. d_W is the device copy of a registered weight. */
+int ds_cuda_skinny_matmul_dev(ds_cuda_ctx_t *ctx, const float *d_x, int n, int K, const uint16_t *d_W, int N,
+                              const float *d_resid, float *d_y, void *stream);
 /* Synchronises the context's stream and reports DS_CUDA_ETIMEOUT if a
  * prefill kernel's bounded wait gave up since the last check. */
 int ds_cuda_prefill_check(ds_cuda_ctx_t *ctx);

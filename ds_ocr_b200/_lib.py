@@ -53,6 +53,13 @@ SIGNATURES = {
     "ds_cuda_decoder_generate": (c_int, [P, c_int, P, c_int, P]),
     "ds_cuda_decoder_generate_dev": (c_int, [P, c_int, c_int, P]),
     "ds_cuda_decoder_launches_per_step": (c_int, [P, c_int]),
+    "ds_cuda_batch_decoder_create": (c_int, [P, P, P, P, P, c_int]),
+    "ds_cuda_batch_decoder_destroy": (c_int, [P, c_int]),
+    "ds_cuda_batch_decoder_load_kv": (c_int, [P, c_int, c_int, c_int, c_int, c_int, P, P]),
+    "ds_cuda_batch_decoder_set_len": (c_int, [P, c_int, c_int, c_int]),
+    "ds_cuda_batch_decoder_forward": (c_int, [P, c_int, P, P, P]),
+    "ds_cuda_batch_decoder_generate": (c_int, [P, c_int, P, c_int, P]),
+    "ds_cuda_batch_decoder_generate_dev": (c_int, [P, c_int, c_int, P]),
     "ds_cuda_prefill_moe": (c_int, [P, P, P, P, c_int, P, P, P]),
     "ds_cuda_prefill_moe_dev": (c_int, [P, P, P, P, c_int, P, P, P, P]),
     "ds_cuda_prefill_check": (c_int, [P]),

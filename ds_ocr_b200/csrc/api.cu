@@ -166,6 +166,7 @@ extern "C" void ds_cuda_free(ds_cuda_ctx_t *c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     ctx_release_models(c);
+    ctx_release_batch_models(c);
     prefill_release(c);
     for (auto &e : c->prefill_ev)
         if (e) cudaEventDestroy(e);

@@ -63,6 +63,7 @@ int ctx_register(ds_cuda_ctx *c, const void *p, size_t bytes);
 const void *ctx_lookup(ds_cuda_ctx *c, const void *p, size_t bytes, bool auto_register);
 void ctx_release_models(ds_cuda_ctx *c);
 void prefill_release(ds_cuda_ctx *c);
+void ctx_release_batch_models(ds_cuda_ctx *c);
 int moe_layer_enqueue(ds_cuda_ctx *c, ds::MoeArgs &a, const uint16_t *d_router, int n_experts, int *d_idx,
                       float *d_wt, cudaStream_t st, bool pdl);
 int lmhead_tc_enqueue(ds_cuda_ctx *c, const float *d_x, const uint16_t *d_W, int in_dim, int out_dim, int batch,

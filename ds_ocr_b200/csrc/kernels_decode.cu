@@ -216,19 +216,23 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
 
     pdl_wait();
     pdl_launch();
-    const int n = *a.d_pos + 1;
+    const int sidx = blockIdx.y;
+    const int n = a.d_pos[sidx] + 1;
+    const int lo_start = a.lo_starts ? a.lo_starts[sidx] : a.lo_start;
     const int per = (n + ATT_CL - 1) / ATT_CL;
     const int j0 = min(n, crank * per), j1 = min(n, j0 + per);
-    const size_t hoff = (size_t)h * a.kv_max * ATT_HD;
+    const size_t hoff = (size_t)h * a.kv_max * ATT_HD + (size_t)sidx * a.kv_stream_stride;
+    const float *qsrc = a.q + (size_t)sidx * a.q_stride;
+    float *out = a.out + (size_t)sidx * a.q_stride;
     const uint16_t *khi = a.k_hi + hoff, *klo = a.k_lo + hoff, *vhi = a.v_hi + hoff, *vlo = a.v_lo + hoff;
     if (tid == 0 && j1 > j0) {
         prefetch_range(vhi + (size_t)j0 * ATT_HD, (size_t)(j1 - j0) * ATT_HD * 2);
-        int ls = max(j0, a.lo_start);
+        int ls = max(j0, lo_start);
         if (ls < j1) prefetch_range(vlo + (size_t)ls * ATT_HD, (size_t)(j1 - ls) * ATT_HD * 2);
     }
     float qf[16];
     {
-        const float4 *qp = reinterpret_cast<const float4 *>(a.q + h * ATT_HD + li * 16);
+        const float4 *qp = reinterpret_cast<const float4 *>(qsrc + h * ATT_HD + li * 16);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             float4 v = qp[i];
@@ -245,7 +249,7 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
         for (int r = 0; r < ATT_KPG; r++) {
             int j = jb + g + 32 * r;
             kraw[r] = j < j1 ? load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16,
-                                          j >= a.lo_start)
+                                          j >= lo_start)
                              : Row16{};
         }
         if (blk == 0) {
@@ -253,7 +257,7 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
             for (int r = 0; r < ATT_KPG; r++) {
                 int j = jb + g + 32 * r;
                 vraw[r] = j < j1 ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
-                                              j >= a.lo_start)
+                                              j >= lo_start)
                                  : Row16{};
             }
         }
@@ -320,7 +324,7 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
             int j = jb + g + 32 * r;
             if (blk == 0) vr[r] = vraw[r];
             else vr[r] = j < j1 ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
-                                             j >= a.lo_start)
+                                             j >= lo_start)
                                 : Row16{};
         }
 #pragma unroll
@@ -349,7 +353,7 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
         float o = 0.f;
         for (int r = 0; r < ATT_CL; r++) o = __fadd_rn(o, cluster.map_shared_rank(opart, r)[tid]);
         float S = s_sum;
-        a.out[h * ATT_HD + tid] = S > 0.f ? __fmul_rn(o, __fdiv_rn(1.0f, S)) : o;
+        out[h * ATT_HD + tid] = S > 0.f ? __fmul_rn(o, __fdiv_rn(1.0f, S)) : o;
     }
     cluster.sync();
 }
@@ -496,12 +500,12 @@ cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl) {
     DS_CPL_SWITCH2(a.hidden, 8, return launch_ex((const void *)qkv_rope_kernel<CPL>, grid, 256, 0, st, pdl, args));
 }
 
-cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl) {
+cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int n_streams) {
     if (a.kv_max > ATT_MAXK) return cudaErrorInvalidValue;
     AttnArgs aa = a;
     void *args[] = {&aa};
     // cluster dims are compiled into the kernel (__cluster_dims__)
-    return launch_ex((const void *)attn_decode_kernel, a.n_heads * ATT_CL, 256, 0, st, pdl, args);
+    return launch_ex((const void *)attn_decode_kernel, dim3(a.n_heads * ATT_CL, n_streams), 256, 0, st, pdl, args);
 }
 
 cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl) {

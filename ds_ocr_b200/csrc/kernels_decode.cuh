@@ -26,6 +26,12 @@ struct AttnArgs {
     int lo_start;      // rows below lo_start are exact BF16 (lo plane is zero)
     float scale;
     float *out;        // [n_heads * 128]
+    // several independent streams (grid.y = stream): per-stream offsets of
+    // q/out (elements), of the KV planes (elements) and d_pos[stream];
+    // lo_starts (optional) per stream. Zero strides: one stream.
+    long long kv_stream_stride;
+    int q_stride;
+    const int *lo_starts;
 };
 
 struct MvArgs {
@@ -38,7 +44,7 @@ struct MvArgs {
 };
 
 cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl);
-cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int n_streams = 1);
 cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int n, float eps, cudaStream_t st, bool pdl);
 cudaError_t launch_decode_advance(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,

@@ -36,6 +36,7 @@
 #include "ctx.h"
 #include "umma.cuh"
 #include "tmap.h"
+#include "route.cuh"
 
 namespace ds {
 
@@ -300,58 +301,7 @@ __global__ void __launch_bounds__(256) pf_norm_route_kernel(const float *__restr
         __syncwarp();
         lg = out;
     }
-    // softmax + top-k: lane holds experts lane, lane+32, ...
-    const int per = (E + 31) / 32;
-    float p[8];
-    float mx = -1e30f;
-    for (int j = 0; j < per; j++) {
-        const int e = lane + 32 * j;
-        p[j] = e < E ? lg[e] : -1e30f;
-        mx = fmaxf(mx, p[j]);
-    }
-    mx = warp_max(mx);
-    float part = 0.f;
-    for (int j = 0; j < per; j++) {
-        const int e = lane + 32 * j;
-        p[j] = e < E ? fast_expf(__fsub_rn(p[j], mx)) : 0.f;
-        part = __fadd_rn(part, p[j]);
-    }
-    const float sinv = __fdiv_rn(1.0f, warp_sum(part));
-    for (int j = 0; j < per; j++) p[j] = __fmul_rn(p[j], sinv);
-    unsigned taken = 0;  // bit j: expert lane + 32j chosen
-    float wk[8];
-    int ik[8];
-    float wsum = 0.f;
-    for (int k = 0; k < K; k++) {
-        float bv = -1e30f;
-        int bi = 0x7fffffff;
-        for (int j = 0; j < per; j++) {
-            const int e = lane + 32 * j;
-            if (e < E && !((taken >> j) & 1u) && p[j] > bv) {
-                bv = p[j];
-                bi = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        wk[k] = bv;
-        ik[k] = bi;
-        wsum = __fadd_rn(wsum, bv);
-    }
-    if (lane == 0) {
-        for (int k = 0; k < K; k++) {
-            idx[(size_t)s * K + k] = ik[k];
-            wt[(size_t)s * K + k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
-        }
-    }
+    route_topk_warp(lg, E, K, renorm, idx + (size_t)s * K, wt + (size_t)s * K);
 }
 
 // Segment starts of the expert-sorted rows, cursors, and the tile lists of
@@ -422,11 +372,12 @@ __global__ void __launch_bounds__(256) pf_count_kernel(int P, const int *__restr
 
 // Copies the split row of each (row, expert) pair to the next free slot of
 // the expert's segment; slot_of[slot] = pair. pair_row == null: row = p / K.
-// Source rows are ld elements apart (ld % 8 == 0).
+// Source rows are ld elements apart (ld % 8 == 0). inv (optional): inv[p] =
+// the slot of pair p.
 __global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int ld, int K, const int *pair_row,
                                                          const int *pair_expert, int E, const int *seg, int *cursor,
                                                          const uint16_t *rows_hi, const uint16_t *rows_lo,
-                                                         uint16_t *xg_hi, uint16_t *xg_lo, int *slot_of) {
+                                                         uint16_t *xg_hi, uint16_t *xg_lo, int *slot_of, int *inv) {
     const int lane = threadIdx.x & 31;
     const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (p >= P) return;
@@ -437,6 +388,7 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int ld, i
     if (lane == 0) {
         pos = seg[e] + atomicAdd(&cursor[e], 1);
         slot_of[pos] = p;
+        if (inv) inv[p] = pos;
     }
     pos = __shfl_sync(0xffffffffu, pos, 0);
     const uint4 *sh = reinterpret_cast<const uint4 *>(rows_hi + (size_t)r * ld);
@@ -623,7 +575,7 @@ static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block,
     mark(c, 2, st);
     if (P > 0)
         pf_scatter_kernel<<<(P + 7) / 8, 256, 0, st>>>(P, H, rows_ld, g.K, pair_row, pair_expert, E, w->seg, w->cursor,
-                                                       rows_hi, rows_lo, w->xg_hi, w->xg_lo, w->slot_of);
+                                                       rows_hi, rows_lo, w->xg_hi, w->xg_lo, w->slot_of, nullptr);
     // gate/up (+SwiGLU): routed A = expert-sorted rows, shared A = sh planes;
     // B = the expert block [E*2I + 2S rows x H] for both
     PfGemm gu;
@@ -878,4 +830,26 @@ extern "C" int ds_cuda_prefill_stage_ms(ds_cuda_ctx_t *c, float *ms6) {
     for (int i = 0; i < 6 && e == cudaSuccess; i++) e = cudaEventElapsedTime(&ms6[i], c->prefill_ev[i], c->prefill_ev[i + 1]);
     if (e != cudaSuccess) return ctx_cuda(c, e, "prefill_stage_ms");
     return DS_CUDA_OK;
+}
+
+// Launchers of the grouping and combine kernels for other engines (the
+// multi-stream decoder groups its token rows by expert the same way).
+cudaError_t pf_count_launch(int P, const int *pair_expert, int E, int *counts, int grid, cudaStream_t st) {
+    if (P > 0) pf_count_kernel<<<min((P + 255) / 256, grid), 256, 0, st>>>(P, pair_expert, E, counts);
+    return cudaGetLastError();
+}
+
+cudaError_t pf_scatter_launch(int P, int H, int ld, int K, const int *pair_row, const int *pair_expert, int E,
+                              const int *seg, int *cursor, const uint16_t *rows_hi, const uint16_t *rows_lo,
+                              uint16_t *xg_hi, uint16_t *xg_lo, int *slot_of, int *inv, cudaStream_t st) {
+    if (P > 0)
+        pf_scatter_kernel<<<(P + 7) / 8, 256, 0, st>>>(P, H, ld, K, pair_row, pair_expert, E, seg, cursor, rows_hi,
+                                                       rows_lo, xg_hi, xg_lo, slot_of, inv);
+    return cudaGetLastError();
+}
+
+cudaError_t pf_combine_launch(float *x, int M, int H, int K, const int *idx, const float *wt, const float *y,
+                              const int *yrow, const float *ys, cudaStream_t st) {
+    if (M > 0) pf_combine_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, M, H, K, idx, wt, y, yrow, ys);
+    return cudaGetLastError();
 }

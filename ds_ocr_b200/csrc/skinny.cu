@@ -66,6 +66,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) sk_gemm_kernel(const __grid_con
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 const SkTile tl = p.tiles[t];
                 const CUtensorMap *am = &p.a[tl.amap];
+                const CUtensorMap *am2 = &p.a[MODE == 1 ? tl.amap2 : tl.amap];
                 const CUtensorMap *bm = &p.b[tl.kind];
                 const int r2 = MODE == 1 ? tl.a_row2 : tl.a_row + 64;
                 for (int kb = 0; kb < tl.kb; kb++, it++) {
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) sk_gemm_kernel(const __grid_con
                     uint8_t *st = smem + s * SK_STAGE_BYTES;
                     mbar_expect_tx(&full[s], SK_STAGE_BYTES);
                     tma_load_2d(st, am, kb * 64, tl.a_row, &full[s]);
-                    tma_load_2d(st + SK_A_BYTES / 2, am, kb * 64, r2, &full[s]);
+                    tma_load_2d(st + SK_A_BYTES / 2, am2, kb * 64, r2, &full[s]);
                     tma_load_2d(st + SK_A_BYTES, bm, kb * 64, tl.b_row, &full[s]);
                     tma_load_2d(st + SK_A_BYTES + SK_A_BYTES / 2, bm, kb * 64, p.lo_off[tl.kind] + tl.b_row,
                                 &full[s]);
@@ -283,7 +284,7 @@ extern "C" int ds_cuda_skinny_matmul_dev(ds_cuda_ctx_t *c, const float *d_x, int
     cudaError_t e = sk_split_launch(d_x, n, K, K, nullptr, 0.f, planes, SK_TOK, nullptr, st);
     if (e != cudaSuccess) return ctx_cuda(c, e, "skinny split");
     std::vector<SkTile> ht(ntiles);
-    for (int t = 0; t < ntiles; t++) ht[t] = SkTile{0, t * 128, 0, 0, 0, n, t * 128, K / 64};
+    for (int t = 0; t < ntiles; t++) ht[t] = SkTile{0, t * 128, 0, 0, 0, 0, n, t * 128, K / 64};
     // pageable sources: the copies are staged before the calls return
     cudaMemcpyAsync(tiles, ht.data(), ntiles * sizeof(SkTile), cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(nt, &ntiles, sizeof(int), cudaMemcpyHostToDevice, st);

@@ -19,7 +19,8 @@ constexpr int SK_TOK = 64;  // token rows per tile (B = 2 x 64 rows)
 struct SkTile {
     int amap;    // weight map (and output slot) index, 0..3
     int a_row;   // first weight row (SwiGLU: first gate row)
-    int a_row2;  // SwiGLU: first up row
+    int a_row2;  // SwiGLU: first up row (in map amap2)
+    int amap2;   // SwiGLU: weight map of the up rows
     int kind;    // activation plane map 0/1 (and SwiGLU output slot)
     int b_row;   // first token row in the plane
     int n_tok;   // valid token rows (<= 64)

@@ -143,3 +143,65 @@ class Decoder:
         if self.id and self.ctx.h:
             self.lib.ds_cuda_decoder_destroy(self.ctx.h, self.id)
             self.id = 0
+
+
+class BatchDecoder:
+    """Greedy decode of n_streams independent streams at once (the
+    multi-stream decode of config 3): forward(embeds) advances every stream
+    by one token. Streams have their own KV caches and positions."""
+
+    def __init__(self, model, n_streams, ctx=None, kv_max=1024):
+        self.ctx = ctx or Context(0)
+        self.lib = self.ctx.lib
+        self.model = model
+        self.S = n_streams
+        d = model.d
+        self.cfg = DecoderConfig(d.hidden, d.n_layers, d.n_heads, d.head_dim, d.dense_inter, d.moe_inter,
+                                 d.n_experts, d.n_shared, d.top_k, d.vocab, d.first_dense, synth.RMS_EPS,
+                                 synth.ROPE_THETA, kv_max, 0, 0)
+        self._layers = (LayerWeightsC * d.n_layers)(*[layer_struct(lw) for lw in model.layers])
+        for lw in model.layers:
+            self.ctx._pin(lw.wq, lw.wk, lw.wv, lw.wo, lw.input_norm, lw.post_norm, lw.dense_gate, lw.dense_up,
+                          lw.dense_down)
+            if lw.moe is not None:
+                self.ctx._pin(lw.moe.router, lw.moe.block, lw.moe.down, lw.moe.shared_down)
+        self.ctx._pin(model.final_norm, model.lm_head)
+        self.id = self.ctx.check(self.lib.ds_cuda_batch_decoder_create(
+            self.ctx.h, ctypes.byref(self.cfg), self._layers, _a(model.final_norm), _a(model.lm_head), n_streams),
+            "batch_decoder_create")
+
+    def load_kv(self, stream, ks, vs, pos0=0):
+        for l, (k, v) in enumerate(zip(ks, vs)):
+            k = np.ascontiguousarray(k, np.float32)
+            v = np.ascontiguousarray(v, np.float32)
+            if k.shape[0]:
+                self.ctx.check(self.lib.ds_cuda_batch_decoder_load_kv(self.ctx.h, self.id, stream, l, pos0,
+                                                                      k.shape[0], _a(k), _a(v)), "batch_load_kv")
+        self.set_len(stream, pos0 + ks[0].shape[0])
+
+    def set_len(self, stream, n):
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_set_len(self.ctx.h, self.id, stream, n), "batch_set_len")
+
+    def forward(self, embeds=None, want_x=False):
+        toks = np.empty(self.S, np.int32)
+        fx = np.empty((self.S, self.model.d.hidden), np.float32) if want_x else None
+        e = None if embeds is None else np.ascontiguousarray(embeds, np.float32)
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_forward(self.ctx.h, self.id, _a(e), _a(toks), _a(fx)),
+                       "batch_forward")
+        return (toks, fx) if want_x else toks
+
+    def generate(self, n_steps, first_embeds=None):
+        toks = np.empty((n_steps, self.S), np.int32)
+        e = None if first_embeds is None else np.ascontiguousarray(first_embeds, np.float32)
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_generate(self.ctx.h, self.id, _a(e), n_steps, _a(toks)),
+                       "batch_generate")
+        return toks
+
+    def generate_dev(self, n_steps, stream=None):
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_generate_dev(self.ctx.h, self.id, n_steps, stream),
+                       "batch_generate_dev")
+
+    def close(self):
+        if self.id:
+            self.lib.ds_cuda_batch_decoder_destroy(self.ctx.h, self.id)
+            self.id = 0

@@ -278,6 +278,34 @@ int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *ctx, int model, int n_steps, voi
 int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *ctx, int model);
 
 /* ---------------------------------------------------------------------
+ * Multi-stream decoder — ds_decoder_forward for up to 64 independent
+ * streams at once (each with its own KV cache and position; the reference
+ * runs streams one at a time). One step advances every stream by one token;
+ * the linear layers run on the tensor cores with the weights read once per
+ * step for all streams. Same configuration and layer structs as the
+ * single-stream decoder (BF16 experts; use_int8 and engine are ignored).
+ * --------------------------------------------------------------------- */
+int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
+                                 const ds_cuda_layer_weights_t *layers, const float *final_norm,
+                                 const uint16_t *lm_head, int n_streams);
+int ds_cuda_batch_decoder_destroy(ds_cuda_ctx_t *ctx, int model);
+/* KV rows [pos0, pos0+n) of one layer of one stream (F32 [n x heads*head_dim]). */
+int ds_cuda_batch_decoder_load_kv(ds_cuda_ctx_t *ctx, int model, int stream, int layer, int pos0, int n,
+                                  const float *k, const float *v);
+int ds_cuda_batch_decoder_set_len(ds_cuda_ctx_t *ctx, int model, int stream, int kv_len);
+/* One step: embeds [n_streams x hidden] (NULL: the embeddings of the
+ * previous step's tokens); tokens [n_streams]; final_x [n_streams x hidden]
+ * (optional) receives the final RMS-normed hidden states. */
+int ds_cuda_batch_decoder_forward(ds_cuda_ctx_t *ctx, int model, const float *embeds, int *tokens,
+                                  float *final_x);
+/* n_steps steps; tokens [n_steps x n_streams]. */
+int ds_cuda_batch_decoder_generate(ds_cuda_ctx_t *ctx, int model, const float *first_embeds, int n_steps,
+                                   int *tokens);
+/* n_steps steps enqueued on `stream` from the device state (a CUDA graph
+ * per step; no host copies). */
+int ds_cuda_batch_decoder_generate_dev(ds_cuda_ctx_t *ctx, int model, int n_steps, void *stream);
+
+/* ---------------------------------------------------------------------
  * Batched MoE prefill — the MoE block of ds_decoder_prefill for n tokens
  * (ds_moe_decoder.c:630-809): per token RMSNorm(post_attn_norm), router
  * softmax/top-k (fast exp, strict '>', weights = probabilities unless the

@@ -15,6 +15,8 @@ Workloads (synthetic random-init weights):
   prefill   config 4: batched MoE prefill, 3328 tokens through the 11 MoE
             layers (router logits overridden, skewed routing)
   lm_head   config 1: argmax LM head 129280 x 1280 at batch 64 (and batch 1)
+  decode64  config 3 at 64 independent streams, sharded by stream over the
+            GPUs (one tensor-core step for all of a GPU's streams)
 --impl reference times the reference's own CPU code (compiled unmodified
 into oracle/_ref/libdsref.so) on the same workload, on this host's cores.
 """
@@ -388,6 +390,86 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
     return res
 
 
+MS_STREAMS = 64
+MS_ATTN_BYTES = 157286400 + 52592640    # attention (12 layers) + dense layer 0 weights
+MS_MOE_LAYER_BYTES = 64 * 6881280 + 13762560 + 163840   # every expert touched (64 streams x top-6)
+
+
+def run_ours_decode_streams(args, rank, world, pg, model, prefixes):
+    """Config 3 at 64 streams, sharded by stream: this rank decodes streams
+    [rank*64/G, (rank+1)*64/G) in lockstep (one tensor-core step for all of
+    them), weights replicated per GPU, no collective."""
+    import torch
+    from ds_ocr_b200 import cuda
+    from ds_ocr_b200.decoder import BatchDecoder
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = cuda.Context(local if world > 1 else 0)
+    a, b = MS_STREAMS * rank // world, MS_STREAMS * (rank + 1) // world
+    S = b - a
+    kv_max = 1024
+    bd = BatchDecoder(model, S, ctx, kv_max=kv_max)
+    for i in range(S):
+        ks, vs = prefixes[a + i]
+        bd.load_kv(i, ks, vs)
+    st = torch.cuda.Stream()
+    sp = st.cuda_stream
+    E = np.stack([model.embed((1 + 7 * (a + i)) % model.d.vocab) for i in range(S)])
+    bd.forward(E)  # first step from the given embeddings (and scratch set-up)
+    bd.generate_dev(max(1, args.warmup - 1), sp)
+    st.synchronize()
+    barrier(pg)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(st)
+        bd.generate_dev(args.steps, sp)
+        ev1.record(st)
+        ev1.synchronize()
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), pg)
+    value = MS_STREAMS * args.steps / (ms_max / 1e3)
+    # e2e: the host API, one call per step (previous tokens' embeddings on
+    # the device, the S tokens copied back every step)
+    n_e2e = max(3, args.steps // 4)
+    for i in range(S):
+        bd.set_len(i, PREFIX)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    bd.forward(E)
+    for _ in range(n_e2e - 1):
+        bd.forward()
+    t1.record(st)
+    t1.synchronize()
+    e2e = MS_STREAMS * n_e2e / (max_over_ranks(t0.elapsed_time(t1), pg) / 1e3)
+    first = PREFIX + args.warmup
+    keys = sum(first + s + 1 for s in range(args.steps))
+    step_bytes = MS_ATTN_BYTES + 11 * MS_MOE_LAYER_BYTES + LM_BYTES + 128000 + KV_BYTES_PER_KEY * S * keys / args.steps
+    pk = peaks()
+    ach = step_bytes / (ms_max / args.steps / 1e3) / 1e9
+    res = {
+        "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
+        "metric": "decode tokens/s (greedy, 64 independent streams, 12-layer DeepSeek3B-MoE, 662-token KV prefixes)",
+        "unit": "tokens/s", "dtype": "bf16 weights + bf16 KV, f32 activations as two bf16 planes, f32 accumulate",
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": S * 4},
+        # per step: 7 per layer (norms, QKV, RoPE/KV, attention, O-proj), 2 per
+        # dense FFN, 8 per MoE layer (router, top-k, count, plan, scatter,
+        # gate/up, down, combine), 4 for the final norm, LM head and advance
+        "gpu_launches": (7 * model.d.n_layers + 2 * model.d.first_dense
+                         + 8 * (model.d.n_layers - model.d.first_dense) + 4) * args.steps,
+        "config": dict(decode_config(kv_max), workload="config3_decode_64_streams", global_batch=MS_STREAMS,
+                       streams_per_gpu=S, parallelism=f"sharded by stream over {world} GPU(s)"),
+        "roofline": {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": ach / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "whole step: weights once per step (all 64 experts of each MoE layer assumed "
+                               "touched) + every stream's KV",
+                     "peak_source": pk["source"]},
+        "scaling": "strong" if world > 1 else "weak",
+    }
+    bd.close()
+    del st
+    torch.cuda.synchronize()
+    ctx.close()
+    return res
+
+
 def ref_decode_time(model, ks, vs, threads, budget_s, max_steps):
     """The reference's own ds_decoder_forward (compiled unmodified) on the
     same weights and KV prefix, `threads` host threads."""
@@ -722,7 +804,8 @@ def main():
     ap.add_argument("--steps", type=int, default=224)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe_layer", "prefill", "lm_head"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "decode64", "moe_layer", "prefill", "lm_head"])
     ap.add_argument("--engine", type=int, default=0, choices=[0, 1],
                     help="decode engine: 0 CUDA graph of per-phase kernels, 1 persistent kernel")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
@@ -774,6 +857,12 @@ def main():
         res = run_ours_prefill(args, rank, world, pg, model)
     elif args.workload == "lm_head":
         res = run_ours_lmhead(args, rank, world, pg)
+    elif args.workload == "decode64":
+        from ds_ocr_b200 import synth
+        model = synth.Model()
+        prefixes = [synth.kv_prefix(model.d, PREFIX, stream=s) for s in range(MS_STREAMS)]
+        ks, vs = prefixes[0]
+        res = run_ours_decode_streams(args, rank, world, pg, model, prefixes)
     else:
         res = run_ours_moe(args, rank, world, pg)
     if rank != 0:
@@ -790,9 +879,10 @@ def main():
         line["scaling"] = res["scaling"]
     if not args.no_cpu_baseline and world == 1:
         try:
-            if args.workload == "decode":
+            if args.workload in ("decode", "decode64"):
                 v, n = ref_decode_time(model, ks, vs, T, args.cpu_budget, max_steps=64)
-                sample = f"{n} greedy ds_decoder_forward steps from position 663"
+                sample = f"{n} greedy ds_decoder_forward steps from position 663 (one stream; the reference " \
+                         "decodes streams one at a time)"
             elif args.workload == "lm_head":
                 v, n = ref_lmhead_time(T, args.cpu_budget)
                 sample = f"{n} ds_argmax_matvec_bf16 calls (one per input)"

@@ -27,7 +27,8 @@ using namespace ds;
 
 cudaError_t sk_gemm_launch(int mode, const SkGemm &g, int grid, cudaStream_t st);
 cudaError_t sk_split_launch(const float *x, int n, int K, int x_ld, const float *w, float eps, uint16_t *planes,
-                            int lo_off, float *normed, cudaStream_t st);
+                            int lo_off, float *normed, cudaStream_t st, const float *ws, int max_split, int nsplit,
+                            const float *resid, float *x_out);
 cudaError_t pf_count_launch(int P, const int *pair_expert, int E, int *counts, int grid, cudaStream_t st);
 cudaError_t pf_scatter_launch(int P, int H, int ld, int K, const int *pair_row, const int *pair_expert, int E,
                               const int *seg, int *cursor, const uint16_t *rows_hi, const uint16_t *rows_lo,
@@ -38,11 +39,11 @@ cudaError_t pf_combine_launch(float *x, int M, int H, int K, const int *idx, con
 namespace ds {
 
 // RoPE of q and k and the KV append for every stream at its own position
-// (the element math of qkv_rope_kernel). One thread per (stream, matrix,
-// head, rotary pair).
-__global__ void bd_rope_kv_kernel(const float *__restrict__ qkv, int S, int NH, int HD, const int *pos,
-                                  const float *cos_t, const float *sin_t, float *q_out, uint16_t *k_hi,
-                                  uint16_t *k_lo, uint16_t *v_hi, uint16_t *v_lo, int kv_max,
+// (the element math of qkv_rope_kernel), reading the QKV GEMM's split-K
+// parts. One thread per (stream, matrix, head, rotary pair).
+__global__ void bd_rope_kv_kernel(const float *__restrict__ ws, int max_split, int nsplit, int S, int NH, int HD,
+                                  const int *pos, const float *cos_t, const float *sin_t, float *q_out,
+                                  uint16_t *k_hi, uint16_t *k_lo, uint16_t *v_hi, uint16_t *v_lo, int kv_max,
                                   long long kv_stream_stride) {
     const int half = HD / 2, QD = NH * HD;
     const int per_s = 3 * NH * half;
@@ -51,8 +52,9 @@ __global__ void bd_rope_kv_kernel(const float *__restrict__ qkv, int S, int NH, 
     const int s = t / per_s, r = t - s * per_s;
     const int m = r / (NH * half), r2 = r - m * NH * half, h = r2 / half, d = r2 - h * half;
     const int row0 = h * HD + d;
-    const float *src = qkv + (size_t)s * 3 * QD + (size_t)m * QD;
-    const float s0 = src[row0], s1 = src[row0 + half];
+    // the QKV GEMM's split-K parts, feature m*QD + row
+    const float s0 = sk_part_sum(ws, max_split, nsplit, s, m * QD + row0);
+    const float s1 = sk_part_sum(ws, max_split, nsplit, s, m * QD + row0 + half);
     const int p = pos[s];
     float o0 = s0, o1 = s1;
     if (m < 2) {
@@ -78,10 +80,15 @@ __global__ void bd_rope_kv_kernel(const float *__restrict__ qkv, int S, int NH, 
     }
 }
 
-// Router softmax + top-k of every stream's token (one warp each).
-__global__ void bd_route_kernel(const float *logits, int S, int E, int K, int renorm, int *idx, float *wt) {
+// Router logits from the router GEMM's split-K parts, then softmax + top-k
+// of every stream's token (one warp each).
+__global__ void bd_route_kernel(const float *ws, int max_split, int nsplit, float *logits, int S, int E, int K,
+                                int renorm, int *idx, float *wt) {
     const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
     if (s >= S) return;
+    for (int e = lane; e < E; e += 32) logits[(size_t)s * E + e] = sk_part_sum(ws, max_split, nsplit, s, e);
+    __syncwarp();
     route_topk_warp(logits + (size_t)s * E, E, K, renorm, idx + (size_t)s * K, wt + (size_t)s * K);
 }
 
@@ -155,6 +162,10 @@ struct BdLayer {
     const float *in_norm, *post_norm;
     SkGemm qkv, oproj, router, gu, dn;  // dense: gu = dense gate/up, dn = dense down
     float *x_in, *x_mid, *x_out;        // residual buffers of this layer
+    // the input row is still split-K parts of the previous layer's dense
+    // down projection: x_in = in_resid + parts
+    bool in_parts;
+    const float *in_resid;
 };
 
 struct BatchModel {
@@ -172,6 +183,10 @@ struct BatchModel {
     int *idx = nullptr, *counts = nullptr, *seg = nullptr, *cursor = nullptr, *slot_of = nullptr, *inv = nullptr;
     int *nt = nullptr, *tok = nullptr, *pos = nullptr, *tok_log = nullptr, *lo_starts = nullptr;
     SkTile *tiles = nullptr;  // static lists, then the MoE gate/up and down lists
+    float *ws = nullptr;      // split-K partial sums
+    int sp_qkv = 1, sp_o = 1, sp_r = 1, sp_dd = 1;
+    bool out_parts = false;   // the last layer's output is split-K parts
+    const float *out_resid = nullptr;
     SkTile *moe_gu = nullptr, *moe_dn = nullptr;
     uint16_t *kv = nullptr;
     float *cos_t = nullptr, *sin_t = nullptr;
@@ -234,10 +249,13 @@ static int enqueue_step(ds_cuda_ctx *c, BatchModel *m, cudaStream_t st) {
     const int grid = c->sm_count;
     for (int l = 0; l < g.n_layers; l++) {
         BdLayer &L = m->layers[l];
-        BKL(sk_split_launch(L.x_in, S, H, H, L.in_norm, g.rms_eps, m->p0, 64, nullptr, st), "bd norm");
+        BKL(sk_split_launch(L.x_in, S, H, H, L.in_norm, g.rms_eps, m->p0, 64, nullptr, st,
+                            L.in_parts ? m->ws : nullptr, SK_MAX_SPLIT, m->sp_dd, L.in_resid, L.x_in),
+            "bd norm");
         BKL(sk_gemm_launch(0, L.qkv, grid, st), "bd qkv");
         const int nthr = S * 3 * NH * (HD / 2);
-        bd_rope_kv_kernel<<<(nthr + 255) / 256, 256, 0, st>>>(m->qkv, S, NH, HD, m->pos, m->cos_t, m->sin_t, m->q,
+        bd_rope_kv_kernel<<<(nthr + 255) / 256, 256, 0, st>>>(m->ws, SK_MAX_SPLIT, m->sp_qkv, S, NH, HD, m->pos,
+                                                              m->cos_t, m->sin_t, m->q,
                                                               m->plane(0, l), m->plane(1, l), m->plane(2, l),
                                                               m->plane(3, l), g.kv_max, m->stream_stride());
         AttnArgs aa = {};
@@ -255,16 +273,21 @@ static int enqueue_step(ds_cuda_ctx *c, BatchModel *m, cudaStream_t st) {
         aa.q_stride = QD;
         aa.lo_starts = m->lo_starts + (size_t)l * S;
         BKL(launch_attn_decode(aa, st, false, S), "bd attention");
-        BKL(sk_split_launch(m->att, S, QD, QD, nullptr, 0.f, m->p1, 64, nullptr, st), "bd split attn");
+        BKL(sk_split_launch(m->att, S, QD, QD, nullptr, 0.f, m->p1, 64, nullptr, st, nullptr, 0, 0, nullptr, nullptr),
+            "bd split attn");
         BKL(sk_gemm_launch(0, L.oproj, grid, st), "bd o-proj");
-        BKL(sk_split_launch(L.x_mid, S, H, H, L.post_norm, g.rms_eps, m->p2, 64, nullptr, st), "bd post norm");
+        // x_mid = x_in + O-proj (its split-K parts), then the post-norm planes
+        BKL(sk_split_launch(L.x_mid, S, H, H, L.post_norm, g.rms_eps, m->p2, 64, nullptr, st, m->ws, SK_MAX_SPLIT,
+                            m->sp_o, L.x_in, L.x_mid),
+            "bd post norm");
         if (L.dense) {
             BKL(sk_gemm_launch(1, L.gu, grid, st), "bd dense gate/up");
             BKL(sk_gemm_launch(0, L.dn, grid, st), "bd dense down");
         } else {
             const int P = S * K;
             BKL(sk_gemm_launch(0, L.router, grid, st), "bd router");
-            bd_route_kernel<<<(S + 7) / 8, 256, 0, st>>>(m->logits, S, E, K, c->renorm, m->idx, m->wt);
+            bd_route_kernel<<<(S + 7) / 8, 256, 0, st>>>(m->ws, SK_MAX_SPLIT, m->sp_r, m->logits, S, E, K, c->renorm,
+                                                         m->idx, m->wt);
             BKL(pf_count_launch(P, m->idx, E, m->counts, grid, st), "bd count");
             bd_plan_kernel<<<1, 256, 0, st>>>(m->counts, E, S, I, Sh, H, m->seg, m->cursor, m->moe_gu, m->moe_dn,
                                               m->nt);
@@ -277,7 +300,9 @@ static int enqueue_step(ds_cuda_ctx *c, BatchModel *m, cudaStream_t st) {
         }
     }
     float *x_last = m->layers.back().x_out;
-    BKL(sk_split_launch(x_last, S, H, H, m->final_norm, g.rms_eps, m->p0, 64, m->xfinal, st), "bd final norm");
+    BKL(sk_split_launch(x_last, S, H, H, m->final_norm, g.rms_eps, m->p0, 64, m->xfinal, st,
+                        m->out_parts ? m->ws : nullptr, SK_MAX_SPLIT, m->sp_dd, m->out_resid, x_last),
+        "bd final norm");
     int rc = lmhead_tc_enqueue(c, m->xfinal, m->lm_head, H, g.vocab, S, m->tok, m->val, st);
     if (rc < 0) return rc;
     bd_advance_kernel<<<S, 256, 0, st>>>(m->lm_head, H, m->tok, g.vocab, m->pos, m->tok_log, g.kv_max,
@@ -343,10 +368,19 @@ extern "C" int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_deco
     BA(m->cos_t, (size_t)g.kv_max * HD);
     BA(m->sin_t, (size_t)g.kv_max * HD);
     // static tile lists (per layer shape, shared by all layers) + MoE lists
-    const int n_qkv = 3 * QD / 128, n_o = H / 128, n_r = (E + 127) / 128, n_dgu = D / 64, n_ddn = H / 128;
+    // split K where a layer has too few 128-row output tiles to fill the
+    // SMs (QKV, O-proj, router, dense down); the parts meet in `ws`
+    const int sp_qkv = 5, sp_o = 10, sp_r = 20, sp_dd = 15;
+    m->sp_qkv = sp_qkv;
+    m->sp_o = sp_o;
+    m->sp_r = sp_r;
+    m->sp_dd = sp_dd;
+    const int n_qkv = (3 * QD / 128) * sp_qkv, n_o = (H / 128) * sp_o, n_r = ((E + 127) / 128) * sp_r;
+    const int n_dgu = D / 64, n_ddn = (H / 128) * sp_dd;
     const int n_moe_gu = E * (I / 64) + Sh / 64, n_moe_dn = E * (H / 128) + H / 128;
     const int n_static = n_qkv + n_o + n_r + n_dgu + n_ddn;
     BA(m->tiles, (size_t)n_static + n_moe_gu + n_moe_dn);
+    BA(m->ws, (size_t)std::max(3 * QD / 128, H / 128) * SK_MAX_SPLIT * 128 * SK_TOK);
 #undef BA
     if (rc < 0) {
         bm_free(m);
@@ -358,19 +392,22 @@ extern "C" int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_deco
     // counts of the static lists live in nt[2..6]
     std::vector<SkTile> v;
     for (int mtx = 0; mtx < 3; mtx++)
-        for (int t = 0; t < QD / 128; t++) v.push_back(SkTile{mtx, t * 128, 0, 0, 0, 0, S, mtx * QD + t * 128, H / 64});
+        for (int t = 0; t < QD / 128; t++)
+            sk_push_split(v, SkTile{mtx, t * 128, 0, 0, 0, 0, S, mtx * QD + t * 128, H / 64}, sp_qkv,
+                          mtx * (QD / 128) + t);
     rc = bm_tiles(c, t_qkv, v);
     v.clear();
-    for (int t = 0; t < n_o; t++) v.push_back(SkTile{0, t * 128, 0, 0, 0, 0, S, t * 128, QD / 64});
+    for (int t = 0; t < H / 128; t++) sk_push_split(v, SkTile{0, t * 128, 0, 0, 0, 0, S, t * 128, QD / 64}, sp_o, t);
     if (rc == DS_CUDA_OK) rc = bm_tiles(c, t_o, v);
     v.clear();
-    for (int t = 0; t < n_r; t++) v.push_back(SkTile{0, t * 128, 0, 0, 0, 0, S, t * 128, H / 64});
+    for (int t = 0; t < (E + 127) / 128; t++)
+        sk_push_split(v, SkTile{0, t * 128, 0, 0, 0, 0, S, t * 128, H / 64}, sp_r, t);
     if (rc == DS_CUDA_OK) rc = bm_tiles(c, t_r, v);
     v.clear();
     for (int t = 0; t < n_dgu; t++) v.push_back(SkTile{0, t * 64, t * 64, 1, 0, 0, S, t * 64, H / 64});
     if (rc == DS_CUDA_OK) rc = bm_tiles(c, t_dgu, v);
     v.clear();
-    for (int t = 0; t < n_ddn; t++) v.push_back(SkTile{0, t * 128, 0, 0, 0, 0, S, t * 128, D / 64});
+    for (int t = 0; t < H / 128; t++) sk_push_split(v, SkTile{0, t * 128, 0, 0, 0, 0, S, t * 128, D / 64}, sp_dd, t);
     if (rc == DS_CUDA_OK) rc = bm_tiles(c, t_ddn, v);
     int counts_h[7] = {0, 0, n_qkv, n_o, n_r, n_dgu, n_ddn};
     if (rc == DS_CUDA_OK && cudaMemcpy(m->nt, counts_h, sizeof counts_h, cudaMemcpyHostToDevice) != cudaSuccess)
@@ -400,6 +437,8 @@ extern "C" int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_deco
     }
     // per layer: weights, tensor maps and the residual buffers
     float *cur = m->xa;
+    bool pending = false;            // cur is (pending_resid + split-K parts)
+    const float *pending_resid = nullptr;
     for (int l = 0; l < g.n_layers && rc == DS_CUDA_OK; l++) {
         const ds_cuda_layer_weights_t &w = lw[l];
         BdLayer L;
@@ -415,6 +454,9 @@ extern "C" int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_deco
         float *other = cur == m->xa ? m->xb : m->xa;
         L.x_in = cur;
         L.x_mid = other;
+        L.in_parts = pending;
+        L.in_resid = pending_resid;
+        pending = false;
         // QKV: three weight maps into one [S x 3QD] output
         ok = ok && tmap_bf16(&L.qkv.a[0], wq, H, QD, 64) && tmap_bf16(&L.qkv.a[1], wk, H, QD, 64) &&
              tmap_bf16(&L.qkv.a[2], wv, H, QD, 64) && tmap_bf16(&L.qkv.b[0], m->p0, H, 128, 64);
@@ -454,12 +496,14 @@ extern "C" int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_deco
             L.dn.lo_off[0] = 64;
             L.dn.tiles = t_ddn;
             L.dn.n_tiles = m->nt + 6;
-            L.dn.out[0] = cur;  // x_out = x_mid + down(...), written over x_in
-            L.dn.resid[0] = other;
+            // x_out = x_mid + down(...): the down GEMM leaves split-K parts,
+            // the next reader assembles them into cur
             L.dn.out_ld[0] = H;
             L.dn.out_n[0] = H;
             L.dn.err = m->err;
             L.x_out = cur;
+            pending = true;
+            pending_resid = other;
         } else {
             const uint16_t *rt = (const uint16_t *)LOOKB(w.router, (size_t)E * H * 2);
             const uint16_t *blk = (const uint16_t *)LOOKB(w.expert_block, ((size_t)E * 2 * I + 2 * (size_t)Sh) * H * 2);
@@ -503,9 +547,15 @@ extern "C" int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_deco
             L.x_out = other;  // the combine adds into x_mid in place
             cur = other;
         }
+        for (SkGemm *gp : {&L.qkv, &L.oproj, &L.router, &L.gu, &L.dn}) {
+            gp->ws = m->ws;
+            gp->max_split = SK_MAX_SPLIT;
+        }
         if (!ok) rc = ctx_fail(c, DS_CUDA_ENOTREG, "batch_decoder_create: layer %d weights or tensor maps", l);
         m->layers.push_back(L);
     }
+    m->out_parts = pending;
+    m->out_resid = pending_resid;
     if (rc < 0) {
         bm_free(m);
         return rc;

@@ -199,9 +199,9 @@ __device__ __forceinline__ float block_sum256(float v, float *buf) {
     return r;
 }
 
-__global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
-    cg::cluster_group cluster = cg::this_cluster();
-    __shared__ float sc_own[ATT_MAXK / ATT_CL];
+template <int CL>
+__device__ __forceinline__ void attn_body(const AttnArgs &a) {
+    __shared__ float sc_own[CL > 1 ? ATT_MAXK / CL : 1];
     __shared__ float wts[ATT_MAXK];
     __shared__ __align__(16) float corr[ATT_MAXK];  // reused as the [32][128] PV reduction buffer
     __shared__ float opart[ATT_HD];
@@ -209,8 +209,8 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
     __shared__ float s_sum;
     float(*red)[ATT_HD] = reinterpret_cast<float(*)[ATT_HD]>(corr);
 
-    const int crank = (int)cluster.block_rank();
-    const int h = blockIdx.x / ATT_CL;
+    const int crank = CL > 1 ? (int)cg::this_cluster().block_rank() : 0;
+    const int h = blockIdx.x / CL;
     const int tid = threadIdx.x;
     const int g = tid >> 3, li = tid & 7;
 
@@ -219,7 +219,7 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
     const int sidx = blockIdx.y;
     const int n = a.d_pos[sidx] + 1;
     const int lo_start = a.lo_starts ? a.lo_starts[sidx] : a.lo_start;
-    const int per = (n + ATT_CL - 1) / ATT_CL;
+    const int per = (n + CL - 1) / CL;
     const int j0 = min(n, crank * per), j1 = min(n, j0 + per);
     const size_t hoff = (size_t)h * a.kv_max * ATT_HD + (size_t)sidx * a.kv_stream_stride;
     const float *qsrc = a.q + (size_t)sidx * a.q_stride;
@@ -272,15 +272,21 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
             s += __shfl_xor_sync(DS_FULL, s, 1);
             s += __shfl_xor_sync(DS_FULL, s, 2);
             s += __shfl_xor_sync(DS_FULL, s, 4);
-            if (li == 0 && j < j1) sc_own[j - j0] = __fmul_rn(s, a.scale);
+            if (li == 0 && j < j1) {
+                if (CL > 1) sc_own[j - j0] = __fmul_rn(s, a.scale);
+                else wts[j] = __fmul_rn(s, a.scale);
+            }
         }
     }
-    cluster.sync();
-    // 2. gather every key's score of this head
-    for (int j = tid; j < n; j += blockDim.x) {
-        int owner = j / per;
-        const float *src = cluster.map_shared_rank(sc_own, owner);
-        wts[j] = src[j - owner * per];
+    // 2. gather every key's score of this head (one CTA: already in place)
+    if constexpr (CL > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        for (int j = tid; j < n; j += blockDim.x) {
+            int owner = j / per;
+            const float *src = cluster.map_shared_rank(sc_own, owner);
+            wts[j] = src[j - owner * per];
+        }
     }
     __syncthreads();
     // 3. exclusive prefix max -> per-key factor a_j and correction c_j
@@ -347,16 +353,28 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
         for (int k = 0; k < 32; k++) o = __fadd_rn(o, red[k][tid]);
         opart[tid] = o;
     }
-    cluster.sync();
+    if constexpr (CL > 1) cg::this_cluster().sync();
+    else __syncthreads();
     // 6. rank 0 combines the cluster's partial outputs
     if (crank == 0 && tid < ATT_HD) {
         float o = 0.f;
-        for (int r = 0; r < ATT_CL; r++) o = __fadd_rn(o, cluster.map_shared_rank(opart, r)[tid]);
+        if constexpr (CL > 1) {
+            for (int r = 0; r < CL; r++) o = __fadd_rn(o, cg::this_cluster().map_shared_rank(opart, r)[tid]);
+        } else {
+            o = opart[tid];
+        }
         float S = s_sum;
         out[h * ATT_HD + tid] = S > 0.f ? __fmul_rn(o, __fdiv_rn(1.0f, S)) : o;
     }
-    cluster.sync();
+    if constexpr (CL > 1) cg::this_cluster().sync();
 }
+
+// batch 1: a cluster of ATT_CL CTAs per head splits the keys
+__global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
+    attn_body<ATT_CL>(a);
+}
+// many streams: one CTA per (head, stream) over all of the stream's keys
+__global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn_body<1>(a); }
 
 // ---------------------------------------------------------------------------
 // Generic row matvec with optional input RMSNorm, bias and residual:
@@ -505,7 +523,9 @@ cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int
     AttnArgs aa = a;
     void *args[] = {&aa};
     // cluster dims are compiled into the kernel (__cluster_dims__)
-    return launch_ex((const void *)attn_decode_kernel, dim3(a.n_heads * ATT_CL, n_streams), 256, 0, st, pdl, args);
+    if (n_streams == 1)
+        return launch_ex((const void *)attn_decode_kernel, a.n_heads * ATT_CL, 256, 0, st, pdl, args);
+    return launch_ex((const void *)attn_streams_kernel, dim3(a.n_heads, n_streams), 256, 0, st, pdl, args);
 }
 
 cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl) {

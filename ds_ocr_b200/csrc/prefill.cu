@@ -404,32 +404,37 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int ld, i
 // x[s] += (sum over the token's experts in ascending order of w_k * y_k) +
 // shared[s]  (ds_moe_decoder.c:785-800). y_k is row s*K + k of yr, or row
 // yrow[s*K + k] when given.
-__global__ void __launch_bounds__(256) pf_combine_kernel(float *x, int M, int H, int K, const int *idx, const float *wt,
+// One block of 128 threads per token; threads over float4 columns.
+__global__ void __launch_bounds__(128) pf_combine_kernel(float *x, int M, int H, int K, const int *idx, const float *wt,
                                                          const float *yr, const int *yrow, const float *ys) {
-    const int lane = threadIdx.x & 31;
-    const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int s = blockIdx.x;
     if (s >= M) return;
-    int ord[8];
-    for (int k = 0; k < K; k++) ord[k] = k;
+    int ord[8], e[8];
+    float w[8];
+    size_t rows[8];
+    for (int k = 0; k < K; k++) {
+        ord[k] = k;
+        e[k] = idx[(size_t)s * K + k];
+    }
     for (int a = 1; a < K; a++)  // insertion sort of the slots by expert
-        for (int b = a; b > 0 && idx[(size_t)s * K + ord[b]] < idx[(size_t)s * K + ord[b - 1]]; b--) {
+        for (int b = a; b > 0 && e[ord[b]] < e[ord[b - 1]]; b--) {
             int tmp = ord[b];
             ord[b] = ord[b - 1];
             ord[b - 1] = tmp;
         }
-    const int nv = H / 128;
-    for (int i = 0; i < nv; i++) {
-        const int c = 4 * (lane + 32 * i);
+    for (int j = 0; j < K; j++) {
+        const int k = ord[j];
+        w[j] = wt[(size_t)s * K + k];
+        rows[j] = yrow ? (size_t)yrow[(size_t)s * K + k] : (size_t)s * K + k;
+    }
+    for (int c = 4 * threadIdx.x; c < H; c += 4 * blockDim.x) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < K; j++) {
-            const int k = ord[j];
-            const float w = wt[(size_t)s * K + k];
-            const size_t row = yrow ? (size_t)yrow[(size_t)s * K + k] : (size_t)s * K + k;
-            const float4 y = *reinterpret_cast<const float4 *>(yr + row * H + c);
-            acc.x = __fmaf_rn(w, y.x, acc.x);
-            acc.y = __fmaf_rn(w, y.y, acc.y);
-            acc.z = __fmaf_rn(w, y.z, acc.z);
-            acc.w = __fmaf_rn(w, y.w, acc.w);
+            const float4 y = *reinterpret_cast<const float4 *>(yr + rows[j] * H + c);
+            acc.x = __fmaf_rn(w[j], y.x, acc.x);
+            acc.y = __fmaf_rn(w[j], y.y, acc.y);
+            acc.z = __fmaf_rn(w[j], y.z, acc.z);
+            acc.w = __fmaf_rn(w[j], y.w, acc.w);
         }
         const float4 sh = *reinterpret_cast<const float4 *>(ys + (size_t)s * H + c);
         float4 *xp = reinterpret_cast<float4 *>(x + (size_t)s * H + c);
@@ -630,7 +635,7 @@ static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block,
 static int pf_combine(ds_cuda_ctx *c, const PfShape &g, float *d_x, int M, const int *idx, const float *wt,
                       const float *y, const int *yrow, const float *ys, cudaStream_t st) {
     if (M <= 0) return DS_CUDA_OK;
-    pf_combine_kernel<<<(M + 7) / 8, 256, 0, st>>>(d_x, M, g.H, g.K, idx, wt, y, yrow, ys);
+    pf_combine_kernel<<<M, 128, 0, st>>>(d_x, M, g.H, g.K, idx, wt, y, yrow, ys);
     mark(c, 6, st);
     return DS_CUDA_OK;
 }
@@ -850,6 +855,6 @@ cudaError_t pf_scatter_launch(int P, int H, int ld, int K, const int *pair_row, 
 
 cudaError_t pf_combine_launch(float *x, int M, int H, int K, const int *idx, const float *wt, const float *y,
                               const int *yrow, const float *ys, cudaStream_t st) {
-    if (M > 0) pf_combine_kernel<<<(M + 7) / 8, 256, 0, st>>>(x, M, H, K, idx, wt, y, yrow, ys);
+    if (M > 0) pf_combine_kernel<<<M, 128, 0, st>>>(x, M, H, K, idx, wt, y, yrow, ys);
     return cudaGetLastError();
 }

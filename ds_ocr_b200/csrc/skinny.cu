@@ -76,12 +76,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1) sk_gemm_kernel(const __grid_con
                         break;
                     }
                     uint8_t *st = smem + s * SK_STAGE_BYTES;
+                    const int kx = (tl.k0 + kb) * 64;
                     mbar_expect_tx(&full[s], SK_STAGE_BYTES);
-                    tma_load_2d(st, am, kb * 64, tl.a_row, &full[s]);
-                    tma_load_2d(st + SK_A_BYTES / 2, am2, kb * 64, r2, &full[s]);
-                    tma_load_2d(st + SK_A_BYTES, bm, kb * 64, tl.b_row, &full[s]);
-                    tma_load_2d(st + SK_A_BYTES + SK_A_BYTES / 2, bm, kb * 64, p.lo_off[tl.kind] + tl.b_row,
-                                &full[s]);
+                    tma_load_2d(st, am, kx, tl.a_row, &full[s]);
+                    tma_load_2d(st + SK_A_BYTES / 2, am2, kx, r2, &full[s]);
+                    tma_load_2d(st + SK_A_BYTES, bm, kx, tl.b_row, &full[s]);
+                    tma_load_2d(st + SK_A_BYTES + SK_A_BYTES / 2, bm, kx, p.lo_off[tl.kind] + tl.b_row, &full[s]);
                 }
             }
             for (int i = max(0, it - SK_STAGES); i < it; i++)
@@ -123,8 +123,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1) sk_gemm_kernel(const __grid_con
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ti++) {
             const int b = ti & 1, u = ti >> 1;
             bool bad = !mbar_wait(&acc_full[b], u & 1, p.err);
-            // SwiGLU: the exchange buffer is free once all four warps are here
-            if (MODE == 1) bad = epi_bar_or(bad);
+            // the four warps leave together (SwiGLU exchange buffer, split-K
+            // hand-over)
+            bad = epi_bar_or(bad);
             if (bad) break;
             tc_fence_after();
             const SkTile tl = p.tiles[t];
@@ -135,20 +136,34 @@ __global__ void __launch_bounds__(SK_THREADS, 1) sk_gemm_kernel(const __grid_con
                 float *out = p.out[tl.amap];
                 const float *res = p.resid[tl.amap];
                 const int ld = p.out_ld[tl.amap];
+                if (tl.nsplit <= 1) {
 #pragma unroll 1
-                for (int c0 = 0; c0 < SK_TOK; c0 += 16) {
-                    float h[16], l[16];
-                    tmem_ld16(tb + c0, h);
-                    tmem_ld16(tb + SK_TOK + c0, l);
+                    for (int c0 = 0; c0 < SK_TOK; c0 += 16) {
+                        float h[16], l[16];
+                        tmem_ld16(tb + c0, h);
+                        tmem_ld16(tb + SK_TOK + c0, l);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int tok = c0 + j;
-                        if (cv && tok < tl.n_tok) {
-                            const size_t o = (size_t)(tl.b_row + tok) * ld + col;
-                            float v = __fadd_rn(h[j], l[j]);
-                            if (res) v = __fadd_rn(res[o], v);
-                            out[o] = v;
+                        for (int j = 0; j < 16; j++) {
+                            const int tok = c0 + j;
+                            if (cv && tok < tl.n_tok) {
+                                const size_t o = (size_t)(tl.b_row + tok) * ld + col;
+                                float v = __fadd_rn(h[j], l[j]);
+                                if (res) v = __fadd_rn(res[o], v);
+                                out[o] = v;
+                            }
                         }
+                    }
+                } else {
+                    // split K: this part to the part buffer ([tok][row]: a
+                    // warp's stores are contiguous); the reader sums the parts
+                    float *mine = p.ws + ((size_t)tl.otile * p.max_split + tl.split) * SK_TOK * 128 + row;
+#pragma unroll 1
+                    for (int c0 = 0; c0 < SK_TOK; c0 += 16) {
+                        float h[16], l[16];
+                        tmem_ld16(tb + c0, h);
+                        tmem_ld16(tb + SK_TOK + c0, l);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) mine[(size_t)(c0 + j) * 128] = __fadd_rn(h[j], l[j]);
                     }
                 }
             } else {
@@ -195,19 +210,47 @@ __global__ void __launch_bounds__(SK_THREADS, 1) sk_gemm_kernel(const __grid_con
 }
 
 // x [n x K] F32 (optionally RMS-normalised with w: (x * w) * inv) -> planes
-// [2*lo_off x K]: hi rows 0..n-1, lo rows lo_off..lo_off+n-1. One warp per
-// row; K % 4 == 0.
-__global__ void __launch_bounds__(256) sk_split_kernel(const float *__restrict__ x, int n, int K, int x_ld,
+// [2*lo_off x K]: hi rows 0..n-1, lo rows lo_off..lo_off+n-1. One block of
+// 128 threads per row; K % 4 == 0. With `parts` the row is first assembled
+// from a split-K GEMM's parts (+ resid) and written to x_out.
+struct SkParts {
+    const float *ws;
+    int max_split, nsplit;
+    const float *resid;
+    float *x_out;
+};
+
+__global__ void __launch_bounds__(128) sk_split_kernel(const float *__restrict__ x, int n, int K, int x_ld,
                                                        const float *__restrict__ w, float eps, uint16_t *planes,
-                                                       int lo_off, float *normed) {
-    const int lane = threadIdx.x & 31;
-    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                                                       int lo_off, float *normed, SkParts parts) {
+    __shared__ float part[4];
+    const int r = blockIdx.x;
     if (r >= n) return;
     const float *xr = x + (size_t)r * x_ld;
+    if (parts.ws) {
+        // assemble the row, then read it back like a plain input
+        for (int c = threadIdx.x * 4; c < K; c += 512) {
+            float4 v;
+            v.x = sk_part_sum(parts.ws, parts.max_split, parts.nsplit, r, c);
+            v.y = sk_part_sum(parts.ws, parts.max_split, parts.nsplit, r, c + 1);
+            v.z = sk_part_sum(parts.ws, parts.max_split, parts.nsplit, r, c + 2);
+            v.w = sk_part_sum(parts.ws, parts.max_split, parts.nsplit, r, c + 3);
+            if (parts.resid) {
+                const float4 q = *reinterpret_cast<const float4 *>(parts.resid + (size_t)r * K + c);
+                v.x = __fadd_rn(q.x, v.x);
+                v.y = __fadd_rn(q.y, v.y);
+                v.z = __fadd_rn(q.z, v.z);
+                v.w = __fadd_rn(q.w, v.w);
+            }
+            *reinterpret_cast<float4 *>(parts.x_out + (size_t)r * K + c) = v;
+        }
+        __syncthreads();
+        xr = parts.x_out + (size_t)r * K;
+    }
     float inv = 1.f;
     if (w) {
         float ss = 0.f;
-        for (int c = lane * 4; c < K; c += 128) {
+        for (int c = threadIdx.x * 4; c < K; c += 512) {
             const float4 v = *reinterpret_cast<const float4 *>(xr + c);
             ss = __fmaf_rn(v.x, v.x, ss);
             ss = __fmaf_rn(v.y, v.y, ss);
@@ -215,9 +258,12 @@ __global__ void __launch_bounds__(256) sk_split_kernel(const float *__restrict__
             ss = __fmaf_rn(v.w, v.w, ss);
         }
         ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        ss = __fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3]));
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
     }
-    for (int c = lane * 4; c < K; c += 128) {
+    for (int c = threadIdx.x * 4; c < K; c += 512) {
         float4 v = *reinterpret_cast<const float4 *>(xr + c);
         if (w) {
             const float4 g = *reinterpret_cast<const float4 *>(w + c);
@@ -259,10 +305,22 @@ cudaError_t sk_gemm_launch(int mode, const SkGemm &g, int grid, cudaStream_t st)
 }
 
 cudaError_t sk_split_launch(const float *x, int n, int K, int x_ld, const float *w, float eps, uint16_t *planes,
-                            int lo_off, float *normed, cudaStream_t st) {
+                            int lo_off, float *normed, cudaStream_t st, const float *ws, int max_split, int nsplit,
+                            const float *resid, float *x_out) {
     if (n <= 0) return cudaSuccess;
-    sk_split_kernel<<<(n + 7) / 8, 256, 0, st>>>(x, n, K, x_ld, w, eps, planes, lo_off, normed);
+    SkParts parts = {ws, max_split, nsplit, resid, x_out};
+    sk_split_kernel<<<n, 128, 0, st>>>(x, n, K, x_ld, w, eps, planes, lo_off, normed, parts);
     return cudaGetLastError();
+}
+
+// out [n x N] = resid + the split-K parts (the standalone GEMM entry's reader).
+__global__ void sk_reduce_kernel(const float *ws, int max_split, int nsplit, int n, int N, const float *resid,
+                                 float *out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * N) return;
+    const int tok = i / N, f = i - tok * N;
+    const float v = sk_part_sum(ws, max_split, nsplit, tok, f);
+    out[i] = resid ? __fadd_rn(resid[i], v) : v;
 }
 
 // Y [n x N] = x [n x K] . W^T on the tensor cores (n <= 64, K % 128 == 0),
@@ -273,18 +331,33 @@ extern "C" int ds_cuda_skinny_matmul_dev(ds_cuda_ctx_t *c, const float *d_x, int
         return DS_CUDA_EINVAL;
     cudaSetDevice(c->device);
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
-    const size_t plane_bytes = (size_t)2 * SK_TOK * K * 2;
-    const int ntiles = (N + 127) / 128;
-    const size_t tile_bytes = (size_t)ntiles * sizeof(SkTile) + 16;
-    if (ctx_grow(c, &c->d_sk_scratch, &c->sk_scratch_cap, plane_bytes + tile_bytes + 256) < 0) return DS_CUDA_ENOMEM;
-    uint16_t *planes = (uint16_t *)c->d_sk_scratch;
-    SkTile *tiles = (SkTile *)((uint8_t *)c->d_sk_scratch + ((plane_bytes + 255) & ~size_t(255)));
-    int *nt = (int *)(tiles + ntiles);
-    cudaMemsetAsync(planes, 0, plane_bytes, st);
-    cudaError_t e = sk_split_launch(d_x, n, K, K, nullptr, 0.f, planes, SK_TOK, nullptr, st);
+    const size_t plane_bytes = ((size_t)2 * SK_TOK * K * 2 + 255) & ~size_t(255);
+    const int otiles = (N + 127) / 128;
+    // split K so that the parts cover the SMs
+    int nsplit = c->sm_count / otiles;
+    nsplit = nsplit < 1 ? 1 : (nsplit > SK_MAX_SPLIT ? SK_MAX_SPLIT : nsplit);
+    const int ntiles_max = otiles * nsplit;
+    const size_t tile_bytes = ((size_t)ntiles_max * sizeof(SkTile) + 16 + 255) & ~size_t(255);
+    const size_t ws_bytes = nsplit > 1 ? (size_t)otiles * SK_MAX_SPLIT * 128 * SK_TOK * 4 : 0;
+    if (otiles > 1000) return ctx_fail(c, DS_CUDA_EINVAL, "skinny_matmul: N too large");
+    // [0, 4 KB): the tile count; then planes, tiles, split-K parts
+    const size_t head = 4096;
+    const size_t need = head + plane_bytes + tile_bytes + ws_bytes;
+    const bool fresh = need > c->sk_scratch_cap;
+    if (ctx_grow(c, &c->d_sk_scratch, &c->sk_scratch_cap, need) < 0) return DS_CUDA_ENOMEM;
+    uint8_t *base = (uint8_t *)c->d_sk_scratch;
+    int *nt = (int *)(base + head - 16);
+    uint16_t *planes = (uint16_t *)(base + head);
+    SkTile *tiles = (SkTile *)(base + head + plane_bytes);
+    float *ws = (float *)(base + head + plane_bytes + tile_bytes);
+    if (fresh) cudaMemsetAsync(base, 0, c->sk_scratch_cap, st);
+    else cudaMemsetAsync(planes, 0, plane_bytes, st);
+    cudaError_t e = sk_split_launch(d_x, n, K, K, nullptr, 0.f, planes, SK_TOK, nullptr, st, nullptr, 0, 0, nullptr,
+                                    nullptr);
     if (e != cudaSuccess) return ctx_cuda(c, e, "skinny split");
-    std::vector<SkTile> ht(ntiles);
-    for (int t = 0; t < ntiles; t++) ht[t] = SkTile{0, t * 128, 0, 0, 0, 0, n, t * 128, K / 64};
+    std::vector<SkTile> ht;
+    for (int t = 0; t < otiles; t++) sk_push_split(ht, SkTile{0, t * 128, 0, 0, 0, 0, n, t * 128, K / 64}, nsplit, t);
+    const int ntiles = (int)ht.size();
     // pageable sources: the copies are staged before the calls return
     cudaMemcpyAsync(tiles, ht.data(), ntiles * sizeof(SkTile), cudaMemcpyHostToDevice, st);
     cudaMemcpyAsync(nt, &ntiles, sizeof(int), cudaMemcpyHostToDevice, st);
@@ -299,6 +372,8 @@ extern "C" int ds_cuda_skinny_matmul_dev(ds_cuda_ctx_t *c, const float *d_x, int
     g.resid[0] = d_resid;
     g.out_ld[0] = N;
     g.out_n[0] = N;
+    g.ws = ws;
+    g.max_split = SK_MAX_SPLIT;
     g.err = (unsigned *)c->d_lt_err;
     if (!g.err) {
         if (cudaMalloc(&c->d_lt_err, 4) != cudaSuccess) return ctx_fail(c, DS_CUDA_ENOMEM, "skinny error flag");
@@ -306,5 +381,8 @@ extern "C" int ds_cuda_skinny_matmul_dev(ds_cuda_ctx_t *c, const float *d_x, int
         g.err = (unsigned *)c->d_lt_err;
     }
     e = sk_gemm_launch(0, g, ntiles < c->sm_count ? ntiles : c->sm_count, st);
+    if (e == cudaSuccess && nsplit > 1)
+        sk_reduce_kernel<<<(n * N + 255) / 256, 256, 0, st>>>(ws, SK_MAX_SPLIT, nsplit, n, N, d_resid, d_y);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? DS_CUDA_OK : ctx_cuda(c, e, "skinny gemm launch");
 }

@@ -8,6 +8,7 @@
 // accumulator column j holds x_hi[j].W and column 64 + j holds x_lo[j].W.
 #pragma once
 #include <cstdint>
+#include <vector>
 #include <cuda.h>
 
 namespace ds {
@@ -25,7 +26,11 @@ struct SkTile {
     int b_row;   // first token row in the plane
     int n_tok;   // valid token rows (<= 64)
     int out_col; // first output feature (PLAIN) / intermediate index (SwiGLU)
-    int kb;      // K blocks of 64
+    int kb;      // K blocks of 64 in this tile
+    // split K (PLAIN only): this tile covers K blocks k0 .. k0+kb-1 and
+    // writes part `split` of nsplit of output tile `otile` to the part
+    // buffer; the kernel that reads the output sums the parts in order
+    int k0, split, nsplit, otile;
 };
 
 struct SkGemm {
@@ -41,7 +46,40 @@ struct SkGemm {
     // SwiGLU: h planes [kind] rows b_row + j, columns out_col + i (hi, lo)
     uint16_t *h_hi[2], *h_lo[2];
     int h_ld[2];
+    // split K: parts [otile][split][64 tokens][128 rows]
+    float *ws;
+    int max_split;
     unsigned *err;
 };
+
+constexpr int SK_MAX_SPLIT = 20;
+
+// Output (token, feature) of a split-K GEMM: the sum of its parts in split
+// order (feature = output tile * 128 + row).
+__device__ __forceinline__ float sk_part_sum(const float *ws, int max_split, int nsplit, int tok, int f) {
+    const float *p = ws + ((size_t)(f >> 7) * max_split * 64 + tok) * 128 + (f & 127);
+    float v = p[0];
+    for (int s = 1; s < nsplit; s++) v = __fadd_rn(v, p[(size_t)s * 64 * 128]);
+    return v;
+}
+
+// Appends tile t split into nsplit K ranges (output tile id otile).
+inline void sk_push_split(std::vector<SkTile> &v, SkTile t, int nsplit, int otile) {
+    if (nsplit > t.kb) nsplit = t.kb;
+    if (nsplit <= 1) {
+        v.push_back(t);
+        return;
+    }
+    const int kb = t.kb;
+    for (int s = 0; s < nsplit; s++) {
+        SkTile u = t;
+        u.k0 = kb * s / nsplit;
+        u.kb = kb * (s + 1) / nsplit - u.k0;
+        u.split = s;
+        u.nsplit = nsplit;
+        u.otile = otile;
+        v.push_back(u);
+    }
+}
 
 }  // namespace ds

@@ -29,6 +29,7 @@ struct DecoderModel {
     // device state
     float *xa = nullptr, *xb = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *xfinal = nullptr;
     float *scores = nullptr, *wt = nullptr, *val = nullptr;
+    float *rpart = nullptr;  // router terms of the O-proj CTAs (router folded into the O-proj)
     int *idx = nullptr, *pos = nullptr, *tok = nullptr, *tok_log = nullptr;
     unsigned *tickets = nullptr;
     unsigned long long *slot = nullptr;
@@ -154,6 +155,22 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
         oa.y = m->xb;
         oa.rows = H;
         oa.n = NH * HD;
+        // MoE layers: the router rides in the O-proj (its logits are linear in
+        // the O-proj output; the last CTA applies the RMS scale and the top-k)
+        const bool fold = !L.dense && g.use_int8 == 0 && H % 16 == 0 && g.n_experts <= 255;
+        if (fold) {
+            oa.rf.Wr = L.router;
+            oa.rf.g = L.post_norm;
+            oa.rf.eps = g.rms_eps;
+            oa.rf.E = g.n_experts;
+            oa.rf.top_k = g.top_k;
+            oa.rf.renorm = c->renorm;
+            oa.rf.part = m->rpart;
+            oa.rf.ticket = m->tickets + 1;
+            oa.rf.scores = m->scores;
+            oa.rf.d_idx = m->idx;
+            oa.rf.d_wt = m->wt;
+        }
         CKL(launch_matvec_res(oa, st, pdl), "o-proj launch");
         launches += 3;
         if (L.dense) {
@@ -208,14 +225,17 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             a.out = m->xa;
             a.resid = m->xb;
             a.out_mode = 2;
-            CKL(launch_router(L.router, m->xb, g.n_experts, H, m->scores, m->tickets + 1, g.top_k, c->renorm, m->idx,
-                              m->wt, st, pdl, L.post_norm, g.rms_eps),
-                "router launch");
+            if (!fold) {
+                CKL(launch_router(L.router, m->xb, g.n_experts, H, m->scores, m->tickets + 1, g.top_k, c->renorm,
+                                  m->idx, m->wt, st, pdl, L.post_norm, g.rms_eps),
+                    "router launch");
+                launches += 1;
+            }
             a.d_idx = m->idx;
             a.d_wt = m->wt;
             CKL(launch_moe_gate_up(a, st, pdl), "moe gate_up launch");
             CKL(launch_moe_down(a, st, pdl), "moe down launch");
-            launches += 3;
+            launches += 2;
         }
     }
     if (with_final) {
@@ -455,6 +475,7 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->attn, QD);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->h, hcap);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->scores, 256);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->rpart, (size_t)(H / 16 + 1) * (g.n_experts + 1));
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->wt, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->val, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->idx, 16);

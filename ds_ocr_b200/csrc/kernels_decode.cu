@@ -383,6 +383,52 @@ __global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn
 // (ds_moe_decoder.c:447-453).
 // ---------------------------------------------------------------------------
 
+// The router terms of this CTA's 16 output rows (one pass: 2 rows per warp,
+// grid x 16 == rows), then, in the last CTA, logits, softmax and top-k.
+__device__ void router_fold(const MvArgs &a, float *yv) {
+    const RouterFold &f = a.rf;
+    __shared__ bool last;
+    __shared__ float lg[256];
+    __syncthreads();
+    const int row0 = blockIdx.x * 16;
+    const int nrow = min(16, a.rows - row0);
+    float *mine = f.part + (size_t)blockIdx.x * (f.E + 1);
+    // thread e: sum over the 16 rows of Wr[e][r] * g[r] * y[r], rows in order
+    for (int e = threadIdx.x; e <= f.E; e += blockDim.x) {
+        float acc = 0.f;
+        if (e < f.E) {
+            const uint16_t *wr = f.Wr + (size_t)e * a.rows + row0;
+            for (int i = 0; i < nrow; i++)
+                acc = __fmaf_rn(__uint_as_float((uint32_t)wr[i] << 16), __fmul_rn(f.g[row0 + i], yv[i]), acc);
+        } else {
+            for (int i = 0; i < nrow; i++) acc = __fmaf_rn(yv[i], yv[i], acc);
+        }
+        mine[e] = acc;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(f.ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int e = threadIdx.x; e <= f.E; e += blockDim.x) {
+        float acc = 0.f;
+        for (int b = 0; b < (int)gridDim.x; b++) acc = __fadd_rn(acc, __ldcg(f.part + (size_t)b * (f.E + 1) + e));
+        lg[e] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(lg[f.E], (float)a.rows), f.eps)));
+        for (int e = threadIdx.x; e < f.E; e += 32) {
+            lg[e] = __fmul_rn(lg[e], inv);
+            f.scores[e] = lg[e];
+        }
+        __syncwarp();
+        router_select(lg, f.E, f.top_k, f.renorm, f.d_idx, f.d_wt);
+        if (threadIdx.x == 0) *f.ticket = 0u;
+    }
+}
+
 template <int CPL>
 __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
     const int lane = threadIdx.x & 31;
@@ -398,6 +444,7 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
     const float inv = a.norm_w ? block_rms_inv(a.x, a.n, a.eps) : 1.f;
     XRegBF16<CPL> xr;
     xr.load_norm(a.x, a.norm_w, inv, a.n, lane);
+    __shared__ float yv[16];
     for (int r = r0; r < a.rows; r += 2 * nw) {
         if (r != r0)
             w.load(a.W + (size_t)r * a.n, r + 1 < a.rows ? a.W + (size_t)(r + 1) * a.n : nullptr, a.n, lane);
@@ -414,9 +461,11 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
                 if (a.bias) v = __fadd_rn(v, a.bias[rr]);
                 if (a.resid) v = __fadd_rn(a.resid[rr], v);
                 a.y[rr] = v;
+                if (r == r0) yv[2 * (threadIdx.x >> 5) + k] = v;
             }
         }
     }
+    if (a.rf.Wr) router_fold(a, yv);
 }
 
 // Long-K matvec (n up to 8192, x staged in shared memory): the dense FFN down
@@ -534,6 +583,8 @@ cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl) {
     if (a.n % 8) return cudaErrorInvalidValue;
     if (a.n <= 2048) {
         int grid = min(((a.rows + 1) / 2 + 7) / 8, sms() * 8);
+        // the router fold needs one pass: 16 output rows per CTA
+        if (a.rf.Wr && (grid * 16 < a.rows || a.rf.E > 255)) return cudaErrorInvalidValue;
         DS_CPL_SWITCH2(a.n, 8, return launch_ex((const void *)matvec_res_kernel<CPL>, grid, 256, 0, st, pdl, args));
     }
     if (a.n > 8192 || a.norm_w) return cudaErrorInvalidValue;  // x stays within the 48 KB default smem

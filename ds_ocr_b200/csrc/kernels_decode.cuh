@@ -34,6 +34,23 @@ struct AttnArgs {
     const int *lo_starts;
 };
 
+// Router folded into the O-projection (optional): logits_e =
+// (sum_r Wr[e][r] g[r] y[r]) * inv(y), y = the O-proj + residual output. Each
+// CTA adds the terms of its 16 output rows (and their squares) into `part`;
+// the last CTA sums the parts in CTA order, scales by the RMS of y and runs
+// softmax/top-k (ds_moe_decoder.c:140-183 on the post-attention RMSNorm).
+struct RouterFold {
+    const uint16_t *Wr;    // [E x rows] BF16, null = no router
+    const float *g;        // post-attention norm weight [rows]
+    float eps;
+    int E, top_k, renorm;
+    float *part;           // [gridDim.x x (E + 1)]
+    unsigned *ticket;      // zero between launches
+    float *scores;         // [E] (for inspection)
+    int *d_idx;
+    float *d_wt;
+};
+
 struct MvArgs {
     const uint16_t *W;
     const float *x, *norm_w;
@@ -41,6 +58,7 @@ struct MvArgs {
     const float *bias, *resid;
     float *y;
     int rows, n;
+    RouterFold rf;
 };
 
 cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl);

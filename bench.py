@@ -149,6 +149,12 @@ def cpu_threads():
 # Workloads
 # ---------------------------------------------------------------------------
 MOE_BYTES_PER_TOKEN = 163840 + 6 * 6881280 + 13762560   # config 0 algorithmic bytes
+# DRAM bytes (read + write) per launch of the dominant kernels, from one ncu
+# capture each (profiles/lmhead_b1_tma_ncu_full.md, lmhead_b64_ncu_full.md,
+# prefill_gemm_ncu_full.md)
+TRAFFIC_ARGMAX_TMA = 331042048 + 4175872
+TRAFFIC_LT_ARGMAX = 331387648 + 6157568
+TRAFFIC_PF_GATE_UP = 423503616 + 78080000
 LM_BYTES = 129280 * 1280 * 2                                 # config 1 per call
 
 
@@ -378,8 +384,8 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
         "gpu_launches": launches * args.steps if launches else 1,
         "config": dict(decode_config(kv_max), engine=["kernel graph", "persistent kernel"][args.engine]),
         "roofline": {"bound": "hbm", "achieved": lm_ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": lm_ach / pk["hbm_gbs"], "traffic": None,
-                     "kernel": "argmax_bf16_kernel (LM head 129280x1280, 330,956,800 B/launch)",
+                     "frac": lm_ach / pk["hbm_gbs"], "traffic": TRAFFIC_ARGMAX_TMA,
+                     "kernel": "argmax_tma_kernel (LM head 129280x1280, 330,956,800 B/launch)",
                      "kernel_us": lm_us, "peak_source": pk["source"]},
         "step_roofline": {"bound": "hbm", "achieved": step_ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                           "frac": step_ach / pk["hbm_gbs"], "frac_of_8tbs": step_ach / 8000.0,
@@ -574,7 +580,7 @@ def run_ours_lmhead(args, rank, world, pg):
                 "d2h_bytes_per_step": LM_BATCH * 8},
         "gpu_launches": 2 * args.steps, "config": lm_config(),
         "roofline": {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": ach / pk["hbm_gbs"], "traffic": None,
+                     "frac": ach / pk["hbm_gbs"], "traffic": TRAFFIC_LT_ARGMAX,
                      "kernel": "lt_argmax_kernel (330,956,800 B per call)", "kernel_us": us,
                      "peak_source": pk["source"]},
         "batch1": {"us_per_call": ms1 / args.steps * 1e3, "tokens_per_s": args.steps / (ms1 / 1e3),
@@ -760,7 +766,7 @@ def run_ours_prefill(args, rank, world, pg, model):
                        tokens_per_rank=b - a),
         "scaling": "strong" if world > 1 else "weak",
         "roofline": {"bound": "tensor", "achieved": gu_ach, "peak": peak_t, "unit": "TFLOP/s",
-                     "frac": gu_ach / peak_t, "traffic": None,
+                     "frac": gu_ach / peak_t, "traffic": TRAFFIC_PF_GATE_UP if world == 1 else None,
                      "kernel": "pf_gemm_kernel<0> (gate/up + SwiGLU), 122.1 GFLOP algorithmic per layer; "
                                "the split-BF16 A operand doubles the tensor work (not counted)",
                      "kernel_us": stages[3] * 1e3, "peak_source": pk["source"] + " (sustained bf16)"},

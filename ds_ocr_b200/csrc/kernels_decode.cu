@@ -574,6 +574,7 @@ cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int
     // cluster dims are compiled into the kernel (__cluster_dims__)
     if (n_streams == 1)
         return launch_ex((const void *)attn_decode_kernel, a.n_heads * ATT_CL, 256, 0, st, pdl, args);
+    // (clusters of 2 or 4 CTAs per (head, stream) measured slower at 64 streams)
     return launch_ex((const void *)attn_streams_kernel, dim3(a.n_heads, n_streams), 256, 0, st, pdl, args);
 }
 

@@ -149,9 +149,9 @@ def cpu_threads():
 # Workloads
 # ---------------------------------------------------------------------------
 MOE_BYTES_PER_TOKEN = 163840 + 6 * 6881280 + 13762560   # config 0 algorithmic bytes
-# DRAM bytes (read + write) per launch of the dominant kernels, from one ncu
-# capture each (profiles/lmhead_b1_tma_ncu_full.md, lmhead_b64_ncu_full.md,
-# prefill_gemm_ncu_full.md)
+# DRAM bytes per launch of the dominant kernels (dram__bytes_read.sum +
+# dram__bytes_write.sum of one ncu capture of each: the batch-1 and batch-64
+# LM heads and the prefill gate/up GEMM at 3328 tokens)
 TRAFFIC_ARGMAX_TMA = 331042048 + 4175872
 TRAFFIC_LT_ARGMAX = 331387648 + 6157568
 TRAFFIC_PF_GATE_UP = 423503616 + 78080000

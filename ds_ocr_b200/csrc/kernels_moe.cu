@@ -135,35 +135,47 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
             w += (size_t)i * n;
             wu += (size_t)i * n;
         };
-        Rows2<CPL> wr;
+        // item q's two rows (and the h index it writes)
+        auto item_rows = [&](int q, const uint16_t *&w, const uint16_t *&wu) {
+            if (q < ns) {
+                shared_rows(q, w, wu);
+            } else {
+                const int pr = q - ns, k = pr / a.inter, i = pr - k * a.inter;
+                const uint16_t *base = (const uint16_t *)expert_mat(a, k, true).w;
+                w = base + (size_t)i * n;
+                wu = base + (size_t)(a.inter + i) * n;
+            }
+        };
+        // each warp walks items gw, gw + nw, ...; the next item's rows load
+        // while the current item's dots run (two row buffers; the grid is one
+        // wave, so no CTA waits for a slot)
+        Rows2<CPL> cur, nxt;
         if (gw < ns) {
             const uint16_t *w, *wu;
             shared_rows(gw, w, wu);
-            wr.load(w, wu, n, lane);
+            cur.load(w, wu, n, lane);
         }
         pdl_wait();
         pdl_launch();
         const float inv = a.norm_w ? block_rms_inv(a.x, n, a.eps) : 1.f;
         XRegBF16<CPL> xr;
         xr.load_norm(a.x, a.norm_w, inv, n, lane);
+        if (gw >= ns && gw < total) {
+            const uint16_t *w, *wu;
+            item_rows(gw, w, wu);
+            cur.load(w, wu, n, lane);
+        }
         for (int q = gw; q < total; q += nw) {
-            int p;
-            if (q < ns) {
-                p = nr + q;
-                if (q != gw) {
-                    const uint16_t *w, *wu;
-                    shared_rows(q, w, wu);
-                    wr.load(w, wu, n, lane);
-                }
-            } else {
-                p = q - ns;
-                int k = p / a.inter;
-                int i = p - k * a.inter;
-                const uint16_t *w = (const uint16_t *)expert_mat(a, k, true).w;
-                wr.load(w + (size_t)i * n, w + (size_t)(a.inter + i) * n, n, lane);
+            const int p = q < ns ? nr + q : q - ns;
+            const int qn = q + nw;
+            if (qn < total) {
+                const uint16_t *w, *wu;
+                item_rows(qn, w, wu);
+                nxt.load(w, wu, n, lane);
             }
             float g, u;
-            wr.dot(xr, g, u);
+            cur.dot(xr, g, u);
+            cur = nxt;
             g = warp_sum(g);
             u = warp_sum(u);
             if (lane == 0) {
@@ -222,7 +234,7 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
 //   out = sum_k w_k * y_k (k = 0..K-1, FMA), then + shared.
 // ---------------------------------------------------------------------------
 template <int CPL, bool I8, int RB>
-__global__ void __launch_bounds__(256) moe_down_kernel(MoeArgs a) {
+__global__ void __launch_bounds__(256, 3) moe_down_kernel(MoeArgs a) {
     __shared__ float y[RB][8];
     const int lane = threadIdx.x & 31;
     const int slot = threadIdx.x >> 5;
@@ -474,7 +486,16 @@ cudaError_t launch_moe_gate_up(const MoeArgs &a, cudaStream_t st, bool pdl) {
     if (a.int8) {
         DS_CPL_SWITCH(a.hidden, 16, return launch_ex((const void *)moe_gate_up_kernel<CPL, true>, grid, 256, 0, st, pdl, args));
     } else {
-        DS_CPL_SWITCH(a.hidden, 8, return launch_ex((const void *)moe_gate_up_kernel<CPL, false>, grid, 256, 0, st, pdl, args));
+        // BF16: one wave of CTAs (as many as fit at once), items pipelined per warp
+        DS_CPL_SWITCH(a.hidden, 8, {
+            static int per_sm[9] = {0};
+            if (!per_sm[CPL]) {
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[CPL], moe_gate_up_kernel<CPL, false>, 256, 0);
+                if (per_sm[CPL] < 1) per_sm[CPL] = 1;
+            }
+            grid = min((total + 7) / 8, sm_count() * per_sm[CPL]);
+            return launch_ex((const void *)moe_gate_up_kernel<CPL, false>, grid, 256, 0, st, pdl, args);
+        });
     }
 }
 

@@ -199,7 +199,9 @@ __device__ __forceinline__ float block_sum256(float v, float *buf) {
     return r;
 }
 
-template <int CL>
+// PRE: load the first block of KV rows before the dependency wait (for
+// launches chained with programmatic dependent launch).
+template <int CL, bool PRE>
 __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     __shared__ float sc_own[CL > 1 ? ATT_MAXK / CL : 1];
     __shared__ float wts[ATT_MAXK];
@@ -214,8 +216,10 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     const int tid = threadIdx.x;
     const int g = tid >> 3, li = tid & 7;
 
-    pdl_wait();
-    pdl_launch();
+    // The position was advanced by a kernel that completed before the
+    // predecessor started its dependent part, so it (and every KV row but
+    // the newest, which the predecessor writes) is readable before the
+    // dependency wait: the first block of K and V rows loads here.
     const int sidx = blockIdx.y;
     const int n = a.d_pos[sidx] + 1;
     const int lo_start = a.lo_starts ? a.lo_starts[sidx] : a.lo_start;
@@ -230,6 +234,32 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
         int ls = max(j0, lo_start);
         if (ls < j1) prefetch_range(vlo + (size_t)ls * ATT_HD, (size_t)(j1 - ls) * ATT_HD * 2);
     }
+    Row16 kraw0[ATT_KPG], vraw[ATT_KPG];
+    if constexpr (PRE) {
+#pragma unroll
+        for (int r = 0; r < ATT_KPG; r++) {
+            const int j = j0 + g + 32 * r;
+            const bool old = j < j1 && j < n - 1;
+            kraw0[r] = old ? load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16,
+                                        j >= lo_start)
+                           : Row16{};
+            vraw[r] = old ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
+                                       j >= lo_start)
+                          : Row16{};
+        }
+    }
+    pdl_wait();
+    pdl_launch();
+    if constexpr (PRE) {
+#pragma unroll
+        for (int r = 0; r < ATT_KPG; r++) {
+            const int j = j0 + g + 32 * r;
+            if (j == n - 1 && j < j1) {  // the newest row, written by the predecessor
+                kraw0[r] = load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16, true);
+                vraw[r] = load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16, true);
+            }
+        }
+    }
     float qf[16];
     {
         const float4 *qp = reinterpret_cast<const float4 *>(qsrc + h * ATT_HD + li * 16);
@@ -241,18 +271,19 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     }
     // 1. scores of this CTA's keys: 8 lanes per key, ATT_KPG keys per lane
     //    group per block (all their K loads in flight together); the first
-    //    block's V rows are loaded alongside and kept in registers for step 5
-    Row16 vraw[ATT_KPG];
+    //    block's K and V rows were loaded above (V kept for step 5)
     for (int jb = j0, blk = 0; jb < j1; jb += 32 * ATT_KPG, blk++) {
         Row16 kraw[ATT_KPG];
 #pragma unroll
         for (int r = 0; r < ATT_KPG; r++) {
             int j = jb + g + 32 * r;
-            kraw[r] = j < j1 ? load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16,
-                                          j >= lo_start)
-                             : Row16{};
+            if (PRE && blk == 0) kraw[r] = kraw0[r];
+            else
+                kraw[r] = j < j1 ? load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16,
+                                              j >= lo_start)
+                                 : Row16{};
         }
-        if (blk == 0) {
+        if (!PRE && blk == 0) {
 #pragma unroll
             for (int r = 0; r < ATT_KPG; r++) {
                 int j = jb + g + 32 * r;
@@ -371,10 +402,10 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
 
 // batch 1: a cluster of ATT_CL CTAs per head splits the keys
 __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
-    attn_body<ATT_CL>(a);
+    attn_body<ATT_CL, true>(a);
 }
 // many streams: one CTA per (head, stream) over all of the stream's keys
-__global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn_body<1>(a); }
+__global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn_body<1, false>(a); }
 
 // ---------------------------------------------------------------------------
 // Generic row matvec with optional input RMSNorm, bias and residual:

@@ -484,3 +484,93 @@ void orc_prefill_moe(const orc_layer_t *ly, const orc_dims_t *d, float *x, int s
     for (size_t i = 0; i < (size_t)seq_len * H; i++) x[i] += routed[i] + sh[i];
     free(xn); free(lg); free(idx); free(w); free(sg); free(su); free(sh); free(routed);
 }
+
+/* LM-head token selection of ds_decoder_forward with the sampling settings
+ * (ds_moe_decoder.c:1021-1263), on the final RMS-normed hidden state xn.
+ * hist = the generated tokens so far (ds_ocr.c:2245-2248), in order.
+ * temperature <= 0, fast path (:1033-1099): argmax; best value recomputed
+ *   by a row dot; repetition penalty rp > 1 applied once to the winner if it
+ *   is in the history, then every history token other than the current
+ *   winner is scored, penalised and taken on a strict '>' (:1044-1066);
+ *   n-gram blocking (:1071-1094): if the winner would complete an n-gram
+ *   already in the history, fall through to the full path.
+ * full path (:1101-1263): all logits; the penalty once per history
+ *   OCCURRENCE (:1186-1198); tokens that complete a seen n-gram set to -1e30
+ *   (:1205-1230); strict '>' argmax; temperature > 0: softmax with expf and
+ *   a double sum, sampled with the uniform r by a sequential F32 cumulative
+ *   sum (:1241-1260).
+ * Returns the token; *val = the selected value (penalised logit, before
+ * temperature); *full = 1 when the full path ran. */
+static float orc_penalise(float v, float rp) { return v > 0 ? v / rp : v * rp; }
+
+static int orc_banned(const int *hist, int len, int ngram, int tok) {
+    if (ngram <= 0 || len < ngram - 1) return 0;
+    int p = ngram - 1;
+    for (int i = 0; i <= len - p - 1; i++) {
+        int m = 1;
+        for (int j = 0; j < p; j++)
+            if (hist[i + j] != hist[len - p + j]) { m = 0; break; }
+        if (m && hist[i + p] == tok) return 1;
+    }
+    return 0;
+}
+
+int orc_lm_select(const float *xn, const uint16_t *W, int H, int V, const int *hist, int len, float rp,
+                  int ngram, float temperature, float r, float *val, int *full) {
+    if (full) *full = 0;
+    if (temperature <= 0.0f) {
+        int best = orc_argmax_bf16(xn, W, H, V, NULL);
+        float bv = orc_dot_bf16_row(xn, W, H, best);
+        if (rp > 1.0f && len > 0) {
+            for (int i = 0; i < len; i++)
+                if (hist[i] == best) { bv = orc_penalise(bv, rp); break; }
+            for (int i = 0; i < len; i++) {
+                int t = hist[i];
+                if (t >= 0 && t < V && t != best) {
+                    float v = orc_penalise(orc_dot_bf16_row(xn, W, H, t), rp);
+                    if (v > bv) { bv = v; best = t; }
+                }
+            }
+        }
+        if (!orc_banned(hist, len, ngram, best)) {
+            if (val) *val = bv;
+            return best;
+        }
+    }
+    if (full) *full = 1;
+    float *lg = (float *)malloc((size_t)V * sizeof(float));
+    orc_matvec_bf16(lg, xn, W, H, V);
+    if (rp > 1.0f)
+        for (int i = 0; i < len; i++)
+            if (hist[i] >= 0 && hist[i] < V) lg[hist[i]] = orc_penalise(lg[hist[i]], rp);
+    if (ngram > 0 && len >= ngram - 1) {
+        int p = ngram - 1;
+        for (int i = 0; i <= len - p - 1; i++) {
+            int m = 1;
+            for (int j = 0; j < p; j++)
+                if (hist[i + j] != hist[len - p + j]) { m = 0; break; }
+            if (m && hist[i + p] >= 0 && hist[i + p] < V) lg[hist[i + p]] = -1e30f;
+        }
+    }
+    int tok = 0;
+    float best = lg[0];
+    for (int i = 1; i < V; i++)
+        if (lg[i] > best) { best = lg[i]; tok = i; }
+    if (val) *val = best;
+    if (temperature > 0.0f) {
+        double sum = 0.0;
+        for (int i = 0; i < V; i++) {
+            lg[i] = expf((lg[i] - best) / temperature);
+            sum += lg[i];
+        }
+        float inv = (float)(1.0 / sum);
+        float cum = 0.0f;
+        tok = V - 1;
+        for (int i = 0; i < V; i++) {
+            cum += lg[i] * inv;
+            if (cum >= r) { tok = i; break; }
+        }
+    }
+    free(lg);
+    return tok;
+}

@@ -80,6 +80,8 @@ int orc_decoder_step(const orc_layer_t *layers, const orc_dims_t *d,
                      float *kv_k, float *kv_v, int kv_max, int pos,
                      const float *cos_t, const float *sin_t, int use_int8,
                      const float *embed, float *final_x, float *logit);
+int orc_lm_select(const float *xn, const uint16_t *W, int H, int V, const int *hist, int len, float rp,
+                  int ngram, float temperature, float r, float *val, int *full);
 void orc_prefill_moe(const orc_layer_t *ly, const orc_dims_t *d, float *x, int seq_len,
                      const float *logits, int *idx_out, float *w_out);
 

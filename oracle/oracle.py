@@ -100,6 +100,7 @@ def oracle():
             "orc_attention_decode": (None, [P, P, P, P, c_int, c_int, c_int, c_int, c_float]),
             "orc_decoder_step": (c_int, [P, P, P, P, P, P, c_int, c_int, P, P, c_int, P, P, P]),
             "orc_prefill_moe": (None, [P, P, P, c_int, P, P, P]),
+            "orc_lm_select": (c_int, [P, P, c_int, c_int, P, c_int, c_float, c_int, c_float, c_float, P, P]),
         }
         for k, (r, a) in sig.items():
             f = getattr(o, k)
@@ -145,6 +146,11 @@ def ref():
             "ref_fast_expf": (c_float, [c_float]),
             "ref_prefill_moe": (None, [P, c_int, P, c_int, P, P, P]),
             "ref_ctx_free": (None, [P]),
+            "ref_ctx_set_sampling": (None, [P, c_float, c_int, c_float]),
+            "ref_ctx_set_history": (c_int, [P, P, c_int]),
+            "ref_ctx_get_history": (c_int, [P, P, c_int]),
+            "ref_decoder_step_gen": (c_int, [P, P]),
+            "ref_srand": (None, [ctypes.c_uint]),
         }
         for k, (res, a) in sig.items():
             f = getattr(r, k)
@@ -192,6 +198,22 @@ class RefDecoder:
         lg = np.empty(1, np.float32)
         tok = self.r.ref_decoder_step(self.ctx, addr(embed), addr(fx), addr(lg))
         return tok, fx, float(lg[0])
+
+    def set_sampling(self, repeat_penalty=1.0, no_repeat_ngram_size=0, temperature=0.0):
+        self.r.ref_ctx_set_sampling(self.ctx, repeat_penalty, no_repeat_ngram_size, temperature)
+
+    def set_history(self, tokens):
+        t = np.ascontiguousarray(tokens, np.int32)
+        assert self.r.ref_ctx_set_history(self.ctx, addr(t) if t.size else None, t.size) == 0
+
+    def history(self):
+        out = np.empty(self.r.ref_ctx_get_history(self.ctx, None, 0), np.int32)
+        self.r.ref_ctx_get_history(self.ctx, addr(out), out.size)
+        return out
+
+    def step_gen(self, embed):
+        """A generation-loop step: decode, then append the token to the history."""
+        return self.r.ref_decoder_step_gen(self.ctx, addr(embed))
 
     def moe_forward(self, layer, x):
         out = np.empty(self.model.d.hidden, np.float32)
@@ -278,6 +300,18 @@ class OracleDecoder:
                                       addr(self.cos), addr(self.sin), int(use_int8), addr(embed), addr(fx), addr(lg))
         self.pos += 1
         return tok, fx, float(lg[0])
+
+    def select(self, final_x, history, repeat_penalty=1.0, no_repeat_ngram_size=0, temperature=0.0, r=0.0):
+        """LM-head selection with the sampling settings on a final hidden state:
+        (token, value, full_path)."""
+        d = self.model.d
+        h = np.ascontiguousarray(history, np.int32)
+        val = np.empty(1, np.float32)
+        full = np.empty(1, np.int32)
+        tok = self.o.orc_lm_select(addr(final_x), addr(self.model.lm_head), d.hidden, d.vocab,
+                                   addr(h) if h.size else None, h.size, repeat_penalty, no_repeat_ngram_size,
+                                   temperature, r, addr(val), addr(full))
+        return tok, float(val[0]), bool(full[0])
 
     def moe_forward(self, layer, x, use_int8=False):
         d = self.model.d

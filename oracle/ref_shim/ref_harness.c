@@ -243,6 +243,44 @@ int ref_decoder_step(void *vctx, const float *embed, float *final_x, float *logi
     return tok;
 }
 
+/* Sampling settings read by ds_decoder_forward's LM head
+ * (ds_moe_decoder.c:1021-1263); the CLI sets them from its flags
+ * (main.c:132-134). */
+void ref_ctx_set_sampling(void *vctx, float repeat_penalty, int no_repeat_ngram_size, float temperature) {
+    ds_ctx_t *ctx = (ds_ctx_t *)vctx;
+    ctx->repeat_penalty = repeat_penalty;
+    ctx->no_repeat_ngram_size = no_repeat_ngram_size;
+    ctx->temperature = temperature;
+}
+
+/* Replace the generated-token history (ds_ctx_t.token_history). */
+int ref_ctx_set_history(void *vctx, const int *tokens, int n) {
+    ds_ctx_t *ctx = (ds_ctx_t *)vctx;
+    if (n < 0 || n > ctx->token_history_cap) return -1;
+    if (n) memcpy(ctx->token_history, tokens, (size_t)n * sizeof(int));
+    ctx->token_history_len = n;
+    return 0;
+}
+
+int ref_ctx_get_history(void *vctx, int *out, int cap) {
+    ds_ctx_t *ctx = (ds_ctx_t *)vctx;
+    int n = ctx->token_history_len < cap ? ctx->token_history_len : cap;
+    if (n > 0) memcpy(out, ctx->token_history, (size_t)n * sizeof(int));
+    return ctx->token_history_len;
+}
+
+/* One step of the generation loop: ds_decoder_forward, then the produced
+ * token appended to the history as ds_ocr.c:2245-2248 does. */
+int ref_decoder_step_gen(void *vctx, const float *embed) {
+    ds_ctx_t *ctx = (ds_ctx_t *)vctx;
+    int tok = ds_decoder_forward(ctx, embed);
+    if (ctx->token_history_len < ctx->token_history_cap) ctx->token_history[ctx->token_history_len++] = tok;
+    return tok;
+}
+
+/* Seeds the C library generator that the temperature path draws from. */
+void ref_srand(unsigned seed) { srand(seed); }
+
 /* One decoder layer (decoder_layer_forward, ds_moe_decoder.c:339): writes the
  * K/V row at kv_cache_len, attends over kv_cache_len+1 keys. */
 void ref_layer_forward(void *vctx, int l, const float *x, float *out) {
@@ -427,7 +465,7 @@ void ref_ctx_free(void *vctx) {
     free(ctx->dec_x); free(ctx->dec_x_norm); free(ctx->dec_q); free(ctx->dec_k); free(ctx->dec_v);
     free(ctx->dec_attn_out); free(ctx->dec_proj_out); free(ctx->dec_expert_out);
     free(ctx->dec_shared_out); free(ctx->dec_layer_out); free(ctx->dec_gate_scores);
-    free(ctx->dec_logits); free(ctx->token_history);
+    free(ctx->dec_logits); free(ctx->token_history); free(ctx->lm_head_f32);
     free(ctx->dec_dense_gate); free(ctx->dec_dense_up); free(ctx->dec_dense_swiglu); free(ctx->dec_dense_out);
     free(ctx->moe_expert_gate_buf); free(ctx->moe_expert_up_buf); free(ctx->moe_expert_gate_up_buf);
     free(ctx->moe_expert_hidden_buf); free(ctx->moe_expert_outputs);

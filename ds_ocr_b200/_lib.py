@@ -53,6 +53,10 @@ SIGNATURES = {
     "ds_cuda_decoder_generate": (c_int, [P, c_int, P, c_int, P]),
     "ds_cuda_decoder_generate_dev": (c_int, [P, c_int, c_int, P]),
     "ds_cuda_decoder_launches_per_step": (c_int, [P, c_int]),
+    "ds_cuda_decoder_set_sampling": (c_int, [P, c_int, c_float, c_int, c_float]),
+    "ds_cuda_decoder_set_history": (c_int, [P, c_int, P, c_int]),
+    "ds_cuda_decoder_get_history": (c_int, [P, c_int, P, c_int]),
+    "ds_cuda_decoder_set_uniforms": (c_int, [P, c_int, P, c_int]),
     "ds_cuda_batch_decoder_create": (c_int, [P, P, P, P, P, c_int]),
     "ds_cuda_batch_decoder_destroy": (c_int, [P, c_int]),
     "ds_cuda_batch_decoder_load_kv": (c_int, [P, c_int, c_int, c_int, c_int, c_int, P, P]),

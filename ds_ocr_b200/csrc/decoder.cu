@@ -50,6 +50,16 @@ struct DecoderModel {
     long long *trace = nullptr;
     bool pdl = true;
     int launches = 0;
+    // LM-head selection with sampling settings (select.cu); history of the
+    // generated tokens, kept in every mode
+    float rp = 1.f, temperature = 0.f;
+    int ngram = 0;
+    int hist_cap = 0;
+    int *hist = nullptr, *hist_len = nullptr, *sel_full = nullptr, *unif_pos = nullptr;
+    float *hval = nullptr, *bval = nullptr, *logits = nullptr, *unif = nullptr;
+    int unif_n = 0;       // uniforms supplied
+    int unif_used = 0;    // uniforms consumed by launched steps (host count)
+    bool sampling() const { return rp > 1.f || ngram > 0 || temperature > 0.f; }
     std::vector<void *> allocs;
 
     size_t plane_elems() const {
@@ -244,11 +254,48 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
         CKL(launch_rmsnorm(m->xa, m->final_norm, m->xfinal, H, g.rms_eps, st, pdl), "final norm launch");
         launches += 1;
     }
-    CKL(launch_argmax_bf16(m->lm_head, m->xa, g.vocab, H, m->slot, m->tickets + 0, m->tok, m->val, st, pdl,
-                           m->final_norm, g.rms_eps),
-        "lm head launch");
-    CKL(launch_decode_advance(m->lm_head, H, m->tok, m->pos, m->tok_log, m->xa, st, pdl), "advance launch");
-    launches += 2;
+    if (m->sampling()) {
+        if (!with_final) {
+            CKL(launch_rmsnorm(m->xa, m->final_norm, m->xfinal, H, g.rms_eps, st, pdl), "final norm launch");
+            launches += 1;
+        }
+        if (m->temperature <= 0.f) {
+            CKL(launch_argmax_bf16(m->lm_head, m->xa, g.vocab, H, m->slot, m->tickets + 0, m->tok, m->val, st, pdl,
+                                   m->final_norm, g.rms_eps),
+                "lm head launch");
+            launches += 2;  // the argmax and the history dots
+        }
+        SelectArgs sa = {};
+        sa.W = m->lm_head;
+        sa.x = m->xfinal;
+        sa.H = H;
+        sa.V = g.vocab;
+        sa.hist = m->hist;
+        sa.hist_len = m->hist_len;
+        sa.cap = m->hist_cap;
+        sa.hval = m->hval;
+        sa.bval = m->bval;
+        sa.logits = m->logits;
+        sa.tok = m->tok;
+        sa.val = m->val;
+        sa.full = m->sel_full;
+        sa.rp = m->rp;
+        sa.ngram = m->ngram;
+        sa.temperature = m->temperature;
+        sa.unif = m->unif;
+        sa.unif_pos = m->unif_pos;
+        CKL(launch_select(sa, st), "token selection launch");
+        launches += 3;
+    } else {
+        CKL(launch_argmax_bf16(m->lm_head, m->xa, g.vocab, H, m->slot, m->tickets + 0, m->tok, m->val, st, pdl,
+                               m->final_norm, g.rms_eps),
+            "lm head launch");
+        launches += 1;
+    }
+    CKL(launch_decode_advance(m->lm_head, H, m->tok, m->pos, m->tok_log, m->xa, st, pdl, m->hist, m->hist_len,
+                              m->hist_cap),
+        "advance launch");
+    launches += 1;
     m->launches = launches;
     return DS_CUDA_OK;
 }
@@ -482,6 +529,17 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->pos, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tok, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tok_log, (size_t)g.kv_max + 16);
+    // the generated-token history holds as many tokens as the reference's
+    // (max_seq + 512, ds_ocr.c:894)
+    m->hist_cap = g.kv_max + 512;
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->hist, (size_t)m->hist_cap);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->hval, (size_t)m->hist_cap);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->unif, (size_t)m->hist_cap);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->hist_len, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->sel_full, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->unif_pos, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->bval, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->logits, (size_t)g.vocab);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tickets, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->slot, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->kv, 4 * m->plane_elems());
@@ -625,6 +683,8 @@ extern "C" int ds_cuda_decoder_forward(ds_cuda_ctx_t *c, int id, const float *em
     DecoderModel *m = c ? get_model(c, id) : nullptr;
     if (!m || !embed) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_forward: bad argument");
     if (m->host_len + 1 > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_forward: KV cache full");
+    if (m->temperature > 0.f && m->unif_used + 1 > m->unif_n)
+        return ctx_fail(c, DS_CUDA_ESTATE, "decoder_forward: no uniform left for temperature sampling");
     cudaSetDevice(c->device);
     const int H = m->cfg.hidden;
     if (!m->mega) CK(ensure_graph(c, m, final_x != nullptr));
@@ -647,6 +707,7 @@ extern "C" int ds_cuda_decoder_forward(ds_cuda_ctx_t *c, int id, const float *em
     if (logit) memcpy(logit, pb + 4, 4);
     if (final_x) memcpy(final_x, pb + 64, (size_t)H * 4);
     m->host_len++;
+    if (m->temperature > 0.f) m->unif_used++;
     return tok;
 }
 
@@ -654,6 +715,9 @@ extern "C" int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *c, int id, int n_step
     DecoderModel *m = c ? get_model(c, id) : nullptr;
     if (!m || n_steps < 0) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_generate_dev: bad argument");
     if (m->host_len + n_steps > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_generate: KV cache full");
+    if (m->temperature > 0.f && m->unif_used + n_steps > m->unif_n)
+        return ctx_fail(c, DS_CUDA_ESTATE, "decoder_generate: %d uniforms left for %d temperature-sampled steps",
+                        m->unif_n - m->unif_used, n_steps);
     cudaSetDevice(c->device);
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     if (n_steps == 0) return DS_CUDA_OK;
@@ -667,6 +731,7 @@ extern "C" int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *c, int id, int n_step
         for (int s = 0; s < n_steps; s++) CKL(cudaGraphLaunch(m->graph, st), "graph launch");
     }
     m->host_len += n_steps;
+    if (m->temperature > 0.f) m->unif_used += n_steps;
     return DS_CUDA_OK;
 }
 
@@ -697,4 +762,69 @@ extern "C" int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *c, int id) {
     if (m->mega) return 0;  // the persistent engine: one launch per generate call, whatever n_steps
     if (!m->launches) CK(ensure_graph(c, m, false));
     return m->launches;
+}
+
+// Sampling settings of the LM head (the reference's ctx->repeat_penalty,
+// no_repeat_ngram_size and temperature, ds_ocr.h; read by ds_decoder_forward,
+// ds_moe_decoder.c:1021-1263). Graph engine only.
+extern "C" int ds_cuda_decoder_set_sampling(ds_cuda_ctx_t *c, int id, float repeat_penalty, int no_repeat_ngram_size,
+                                            float temperature) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || !(repeat_penalty > 0.f) || no_repeat_ngram_size < 0 || !(temperature >= 0.f))
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_sampling: bad argument");
+    const bool on = repeat_penalty > 1.f || no_repeat_ngram_size > 0 || temperature > 0.f;
+    if (m->mega && on)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_sampling: the persistent engine decodes greedily only");
+    if (m->cfg.hidden % 256) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_sampling: hidden must be a multiple of 256");
+    cudaSetDevice(c->device);
+    CKL(cudaStreamSynchronize(c->stream), "set sampling");
+    m->rp = repeat_penalty;
+    m->ngram = no_repeat_ngram_size;
+    m->temperature = temperature;
+    drop_graphs(m);
+    return DS_CUDA_OK;
+}
+
+// Replaces the generated-token history (the reference's ctx->token_history;
+// its generation loop appends every produced token, ds_ocr.c:2245-2248, and
+// so does each decode step here).
+extern "C" int ds_cuda_decoder_set_history(ds_cuda_ctx_t *c, int id, const int *tokens, int n) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || n < 0 || n > m->hist_cap || (n > 0 && !tokens))
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_history: bad argument");
+    cudaSetDevice(c->device);
+    CKL(cudaStreamSynchronize(c->stream), "set history");
+    if (n) CKL(cudaMemcpy(m->hist, tokens, (size_t)n * 4, cudaMemcpyHostToDevice), "history copy");
+    CKL(cudaMemcpy(m->hist_len, &n, 4, cudaMemcpyHostToDevice), "history length");
+    return DS_CUDA_OK;
+}
+
+// Copies up to cap history tokens out; returns the history length.
+extern "C" int ds_cuda_decoder_get_history(ds_cuda_ctx_t *c, int id, int *tokens, int cap) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || cap < 0 || (cap > 0 && !tokens)) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_get_history: bad argument");
+    cudaSetDevice(c->device);
+    CKL(cudaStreamSynchronize(c->stream), "get history");
+    int n = 0;
+    CKL(cudaMemcpy(&n, m->hist_len, 4, cudaMemcpyDeviceToHost), "history length");
+    const int k = n < cap ? n : cap;
+    if (k > 0) CKL(cudaMemcpy(tokens, m->hist, (size_t)k * 4, cudaMemcpyDeviceToHost), "history copy");
+    return n;
+}
+
+// Uniforms in [0, 1] for temperature sampling, one consumed per sampled step
+// in order (the reference draws (float)rand() / RAND_MAX each step,
+// ds_moe_decoder.c:1251). Replaces any unconsumed ones.
+extern "C" int ds_cuda_decoder_set_uniforms(ds_cuda_ctx_t *c, int id, const float *u, int n) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || n < 0 || n > m->hist_cap || (n > 0 && !u))
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_uniforms: bad argument (at most %d)", m ? m->hist_cap : 0);
+    cudaSetDevice(c->device);
+    CKL(cudaStreamSynchronize(c->stream), "set uniforms");
+    if (n) CKL(cudaMemcpy(m->unif, u, (size_t)n * 4, cudaMemcpyHostToDevice), "uniform copy");
+    const int zero = 0;
+    CKL(cudaMemcpy(m->unif_pos, &zero, 4, cudaMemcpyHostToDevice), "uniform position");
+    m->unif_n = n;
+    m->unif_used = 0;
+    return DS_CUDA_OK;
 }

@@ -549,9 +549,10 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
 
 // Step advance for greedy decode: next input = BF16 embedding row of the
 // token just produced, widened to F32 (ds_ocr.c:2272-2279); token logged at
-// its position; position advanced (ds_moe_decoder.c:997).
+// its position; position advanced (ds_moe_decoder.c:997); token appended to
+// the generated-token history when one is kept (ds_ocr.c:2245-2248).
 __global__ void decode_advance_kernel(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,
-                                      float *x_out) {
+                                      float *x_out, int *hist, int *hist_len, int hist_cap) {
     pdl_wait();
     pdl_launch();
     int tok = *d_tok;
@@ -563,6 +564,10 @@ __global__ void decode_advance_kernel(const uint16_t *E, int hidden, const int *
     if (threadIdx.x == 0) {
         tok_log[pos] = tok;
         *d_pos = pos + 1;
+        if (hist && *hist_len < hist_cap) {
+            hist[*hist_len] = tok;
+            *hist_len = *hist_len + 1;
+        }
     }
 }
 
@@ -625,8 +630,8 @@ cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_decode_advance(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,
-                                  float *x_out, cudaStream_t st, bool pdl) {
-    void *args[] = {&E, &hidden, &d_tok, &d_pos, &tok_log, &x_out};
+                                  float *x_out, cudaStream_t st, bool pdl, int *hist, int *hist_len, int hist_cap) {
+    void *args[] = {&E, &hidden, &d_tok, &d_pos, &tok_log, &x_out, &hist, &hist_len, &hist_cap};
     return launch_ex((const void *)decode_advance_kernel, 1, 256, 0, st, pdl, args);
 }
 

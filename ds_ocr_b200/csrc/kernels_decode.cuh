@@ -66,6 +66,29 @@ cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int
 cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int n, float eps, cudaStream_t st, bool pdl);
 cudaError_t launch_decode_advance(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,
-                                  float *x_out, cudaStream_t st, bool pdl);
+                                  float *x_out, cudaStream_t st, bool pdl, int *hist = nullptr, int *hist_len = nullptr,
+                                  int hist_cap = 0);
+
+// LM-head token selection with the sampling settings (select.cu).
+struct SelectArgs {
+    const uint16_t *W;   // LM head [V x H]
+    const float *x;      // final RMS-normed hidden state [H]
+    int H, V;
+    const int *hist;     // generated tokens so far
+    const int *hist_len;
+    int cap;             // history capacity
+    float *hval;         // [cap] history tokens' logits
+    float *bval;         // the argmax winner's logit
+    float *logits;       // [V]
+    int *tok;            // in: the argmax winner; out: the selected token
+    float *val;          // out: the selected value
+    int *full;           // the full-logits path runs
+    float rp;            // repetition penalty (> 1 enables)
+    int ngram;           // no-repeat n-gram size (> 0 enables)
+    float temperature;   // > 0: sampling
+    const float *unif;   // caller-supplied uniforms, one per sampling step
+    int *unif_pos;
+};
+cudaError_t launch_select(const SelectArgs &a, cudaStream_t st);
 
 }  // namespace ds

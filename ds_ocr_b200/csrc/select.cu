@@ -1,0 +1,316 @@
+// select.cu — LM-head token selection with the sampling settings of
+// ds_decoder_forward (ds_moe_decoder.c:1021-1263): repetition penalty,
+// n-gram blocking and temperature sampling, on the device, as kernels of
+// the batch-1 decode step.
+//
+//   fast path (temperature <= 0, :1033-1099), after the streaming argmax:
+//     select_dots_kernel   one warp per history entry (and one for the
+//                          argmax winner): the row dots W[t] . x_final
+//     select_fast_kernel   one CTA: the winner's value penalised once if it
+//                          is in the history; every history token other than
+//                          the winner penalised and taken on a strict '>'
+//                          (the earliest occurrence of the maximum); then
+//                          whether the winner completes a seen n-gram, which
+//                          sends the step to the full path
+//   full path (:1101-1263), skipped by an early exit unless needed:
+//     select_logits_kernel every logit (HBM-bound matvec over the vocab)
+//     select_full_kernel   one CTA: the penalty once per history
+//                          OCCURRENCE, banned tokens set to -1e30, strict
+//                          '>' argmax; temperature > 0: softmax with expf
+//                          and a double sum, sampled with the next caller-
+//                          supplied uniform by a cumulative F32 sum
+// The fast path re-scores history tokens only, as the reference does: a
+// penalised winner keeps the token when a token outside the history would
+// now score higher.
+#include "kernels_decode.cuh"
+
+namespace ds {
+
+__device__ __forceinline__ float sel_penalise(float v, float rp) {
+    return v > 0.f ? __fdiv_rn(v, rp) : __fmul_rn(v, rp);
+}
+
+// W[row] . x for one warp (hidden a multiple of 256).
+__device__ __forceinline__ float sel_row_dot(const uint16_t *W, const float *x, int H, int row, int lane) {
+    const uint16_t *w = W + (size_t)row * H;
+    float s = 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+        const uint4 u = ldg_stream(w + c);
+        const float4 x0 = *reinterpret_cast<const float4 *>(x + c);
+        const float4 x1 = *reinterpret_cast<const float4 *>(x + c + 4);
+        s = __fmaf_rn(bf16_lo(u.x), x0.x, s);
+        s = __fmaf_rn(bf16_hi(u.x), x0.y, s);
+        s = __fmaf_rn(bf16_lo(u.y), x0.z, s);
+        s = __fmaf_rn(bf16_hi(u.y), x0.w, s);
+        s = __fmaf_rn(bf16_lo(u.z), x1.x, s);
+        s = __fmaf_rn(bf16_hi(u.z), x1.y, s);
+        s = __fmaf_rn(bf16_lo(u.w), x1.z, s);
+        s = __fmaf_rn(bf16_hi(u.w), x1.w, s);
+    }
+    return warp_sum(s);
+}
+
+// Warp i < len: hval[i] = W[hist[i]] . x (0 for an out-of-range token);
+// warp i == cap: bval = W[*tok] . x (the argmax winner's value recomputed,
+// as the reference does with ds_bf16_dot_row).
+__global__ void __launch_bounds__(256) select_dots_kernel(SelectArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int len = *a.hist_len;
+    if (i == a.cap) {
+        const int t = *a.tok;
+        const float v = (t >= 0 && t < a.V) ? sel_row_dot(a.W, a.x, a.H, t, lane) : -1e30f;
+        if (lane == 0) *a.bval = v;
+        return;
+    }
+    if (i >= len || i >= a.cap) return;
+    const int t = a.hist[i];
+    const float v = (t >= 0 && t < a.V) ? sel_row_dot(a.W, a.x, a.H, t, lane) : 0.f;
+    if (lane == 0) a.hval[i] = v;
+}
+
+// Block-wide arg-max of (value, -index): the largest value, the smallest
+// index among equals. 1024 threads.
+__device__ __forceinline__ void sel_block_argmax(float &v, int &i, float *sv, int *si) {
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(DS_FULL, v, o);
+        const int oi = __shfl_xor_sync(DS_FULL, i, o);
+        if (ov > v || (ov == v && oi < i)) {
+            v = ov;
+            i = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) {
+        sv[w] = v;
+        si[w] = i;
+    }
+    __syncthreads();
+    if (w == 0) {
+        v = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+        i = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(DS_FULL, v, o);
+            const int oi = __shfl_xor_sync(DS_FULL, i, o);
+            if (ov > v || (ov == v && oi < i)) {
+                v = ov;
+                i = oi;
+            }
+        }
+        if (lane == 0) {
+            sv[0] = v;
+            si[0] = i;
+        }
+    }
+    __syncthreads();
+    v = sv[0];
+    i = si[0];
+    __syncthreads();
+}
+
+// True when token tok would complete an n-gram of the history: some
+// earlier window hist[i .. i+p-1] equals the last p tokens and is followed
+// by tok (p = ngram - 1). Block-wide (every thread gets the answer).
+__device__ __forceinline__ bool sel_banned(const int *hist, int len, int ngram, int tok) {
+    bool hit = false;
+    if (ngram > 0 && len >= ngram - 1) {
+        const int p = ngram - 1;
+        for (int i = threadIdx.x; i <= len - p - 1; i += blockDim.x) {
+            if (hist[i + p] != tok) continue;
+            bool m = true;
+            for (int j = 0; j < p && m; j++) m = hist[i + j] == hist[len - p + j];
+            hit = hit || m;
+        }
+    }
+    return __syncthreads_or(hit) != 0;
+}
+
+__global__ void __launch_bounds__(1024) select_fast_kernel(SelectArgs a) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    if (a.temperature > 0.f) {  // temperature sampling always takes the full path
+        if (threadIdx.x == 0) *a.full = 1;
+        return;
+    }
+    const int len = *a.hist_len;
+    int best = *a.tok;
+    float bv = *a.bval;
+    if (a.rp > 1.f && len > 0) {
+        bool in = false;
+        for (int i = threadIdx.x; i < len; i += blockDim.x) in = in || a.hist[i] == best;
+        if (__syncthreads_or(in)) bv = sel_penalise(bv, a.rp);
+        float v = -INFINITY;
+        int at = 0x7fffffff;
+        for (int i = threadIdx.x; i < len; i += blockDim.x) {
+            const int t = a.hist[i];
+            if (t < 0 || t >= a.V || t == best) continue;
+            const float pv = sel_penalise(a.hval[i], a.rp);
+            if (pv > v) {  // ascending i per thread: the first of equals stays
+                v = pv;
+                at = i;
+            }
+        }
+        sel_block_argmax(v, at, sv, si);
+        if (at != 0x7fffffff && v > bv) {
+            bv = v;
+            best = a.hist[at];
+        }
+    }
+    const bool banned = sel_banned(a.hist, len, a.ngram, best);
+    if (threadIdx.x == 0) {
+        *a.tok = best;
+        *a.val = bv;
+        *a.full = banned ? 1 : 0;
+    }
+}
+
+// Every logit, when the full path runs. Grid-stride over rows, one warp
+// per row; every CTA returns at once when the flag is clear.
+__global__ void __launch_bounds__(256) select_logits_kernel(SelectArgs a) {
+    if (!*a.full) return;
+    const int lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < a.V; r += nw) {
+        const float v = sel_row_dot(a.W, a.x, a.H, r, lane);
+        if (lane == 0) a.logits[r] = v;
+    }
+}
+
+__global__ void __launch_bounds__(1024) select_full_kernel(SelectArgs a) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ double sd[32];
+    __shared__ float sf[1024];
+    if (!*a.full) return;
+    const int len = *a.hist_len;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    float *lg = a.logits;
+    // 1. the penalty once per history occurrence: the first occurrence of
+    //    each token applies all of that token's divisions in turn
+    if (a.rp > 1.f) {
+        for (int i = tid; i < len; i += nt) {
+            const int t = a.hist[i];
+            if (t < 0 || t >= a.V) continue;
+            bool first = true;
+            for (int j = 0; j < i && first; j++) first = a.hist[j] != t;
+            if (!first) continue;
+            int k = 1;
+            for (int j = i + 1; j < len; j++) k += a.hist[j] == t;
+            float v = lg[t];
+            for (int q = 0; q < k; q++) v = sel_penalise(v, a.rp);
+            lg[t] = v;
+        }
+    }
+    __syncthreads();
+    // 2. tokens that would complete a seen n-gram
+    if (a.ngram > 0 && len >= a.ngram - 1) {
+        const int p = a.ngram - 1;
+        for (int i = tid; i <= len - p - 1; i += nt) {
+            bool m = true;
+            for (int j = 0; j < p && m; j++) m = a.hist[i + j] == a.hist[len - p + j];
+            const int t = a.hist[i + p];
+            if (m && t >= 0 && t < a.V) lg[t] = -1e30f;
+        }
+    }
+    __syncthreads();
+    // 3. strict '>' argmax: the largest logit, the lowest index among equals
+    float v = -INFINITY;
+    int at = 0x7fffffff;
+    for (int i = tid; i < a.V; i += nt) {
+        const float x = lg[i];
+        if (x > v) {
+            v = x;
+            at = i;
+        }
+    }
+    sel_block_argmax(v, at, sv, si);
+    int tok = at == 0x7fffffff ? 0 : at;
+    const float best = v;
+    // 4. temperature sampling over contiguous per-thread segments
+    if (a.temperature > 0.f) {
+        const int seg = (a.V + nt - 1) / nt;
+        const int s0 = min(a.V, tid * seg), s1 = min(a.V, s0 + seg);
+        double ds = 0.0;
+        for (int i = s0; i < s1; i++) {
+            const float e = expf(__fdiv_rn(__fsub_rn(lg[i], best), a.temperature));
+            lg[i] = e;
+            ds += (double)e;
+        }
+        for (int o = 16; o > 0; o >>= 1) ds += __shfl_xor_sync(DS_FULL, ds, o);
+        if ((tid & 31) == 0) sd[tid >> 5] = ds;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < (nt >> 5); w++) tot += sd[w];
+        const float inv = (float)(1.0 / tot);
+        float fs = 0.f;
+        for (int i = s0; i < s1; i++) fs = __fadd_rn(fs, __fmul_rn(lg[i], inv));
+        // exclusive prefix of the segment sums, in thread order
+        sf[tid] = fs;
+        __syncthreads();
+        if (tid == 0) {
+            float acc = 0.f;
+            for (int t = 0; t < nt; t++) {
+                const float x = sf[t];
+                sf[t] = acc;
+                acc = __fadd_rn(acc, x);
+            }
+        }
+        __syncthreads();
+        const float r = a.unif[*a.unif_pos];
+        float cum = sf[tid];
+        int hit = 0x7fffffff;
+        for (int i = s0; i < s1; i++) {
+            cum = __fadd_rn(cum, __fmul_rn(lg[i], inv));
+            if (cum >= r) {
+                hit = i;
+                break;
+            }
+        }
+        int h = hit;
+        // the first segment that reaches r
+        for (int o = 16; o > 0; o >>= 1) h = min(h, __shfl_xor_sync(DS_FULL, h, o));
+        __syncthreads();
+        if ((tid & 31) == 0) si[tid >> 5] = h;
+        __syncthreads();
+        h = 0x7fffffff;
+        for (int w = 0; w < (nt >> 5); w++) h = min(h, si[w]);
+        tok = h == 0x7fffffff ? a.V - 1 : h;
+        __syncthreads();
+        if (tid == 0) *a.unif_pos = *a.unif_pos + 1;
+    }
+    if (tid == 0) {
+        *a.tok = tok;
+        *a.val = best;
+    }
+}
+
+static int sel_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    }
+    return n;
+}
+
+cudaError_t launch_select(const SelectArgs &a, cudaStream_t st) {
+    if (a.H % 256 || a.cap <= 0 || !a.hist || !a.hist_len || !a.tok || !a.val || !a.full || !a.logits)
+        return cudaErrorInvalidValue;
+    SelectArgs aa = a;
+    void *args[] = {&aa};
+    cudaError_t e = cudaSuccess;
+    if (a.temperature <= 0.f) {
+        const int warps = a.cap + 1;
+        e = launch_ex((const void *)select_dots_kernel, (warps + 7) / 8, 256, 0, st, false, args);
+        if (e != cudaSuccess) return e;
+    }
+    e = launch_ex((const void *)select_fast_kernel, 1, 1024, 0, st, false, args);
+    if (e != cudaSuccess) return e;
+    e = launch_ex((const void *)select_logits_kernel, sel_sms() * 8, 256, 0, st, false, args);
+    if (e != cudaSuccess) return e;
+    return launch_ex((const void *)select_full_kernel, 1, 1024, 0, st, false, args);
+}
+
+}  // namespace ds

@@ -139,6 +139,33 @@ class Decoder:
     def launches_per_step(self):
         return self.ctx.check(self.lib.ds_cuda_decoder_launches_per_step(self.ctx.h, self.id), "launches")
 
+    def set_sampling(self, repeat_penalty=1.0, no_repeat_ngram_size=0, temperature=0.0):
+        """The reference's ctx->repeat_penalty / no_repeat_ngram_size /
+        temperature (ds_moe_decoder.c:1021-1263); defaults: greedy argmax."""
+        self.ctx.check(self.lib.ds_cuda_decoder_set_sampling(self.ctx.h, self.id, repeat_penalty,
+                                                             no_repeat_ngram_size, temperature),
+                       "decoder_set_sampling")
+
+    def set_history(self, tokens):
+        """Replace the generated-token history (ctx->token_history)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        self.ctx.check(self.lib.ds_cuda_decoder_set_history(self.ctx.h, self.id, _a(t) if t.size else None, t.size),
+                       "decoder_set_history")
+
+    def history(self):
+        n = self.ctx.check(self.lib.ds_cuda_decoder_get_history(self.ctx.h, self.id, None, 0), "decoder_get_history")
+        out = np.empty(n, np.int32)
+        if n:
+            self.ctx.check(self.lib.ds_cuda_decoder_get_history(self.ctx.h, self.id, _a(out), n),
+                           "decoder_get_history")
+        return out
+
+    def set_uniforms(self, u):
+        """Uniforms for temperature sampling, one per sampled step."""
+        u = np.ascontiguousarray(u, np.float32)
+        self.ctx.check(self.lib.ds_cuda_decoder_set_uniforms(self.ctx.h, self.id, _a(u) if u.size else None, u.size),
+                       "decoder_set_uniforms")
+
     def close(self):
         if self.id and self.ctx.h:
             self.lib.ds_cuda_decoder_destroy(self.ctx.h, self.id)

@@ -277,6 +277,29 @@ int ds_cuda_decoder_generate_dev(ds_cuda_ctx_t *ctx, int model, int n_steps, voi
  * persistent engine (one launch per forward/generate call). */
 int ds_cuda_decoder_launches_per_step(ds_cuda_ctx_t *ctx, int model);
 
+/* LM-head selection settings, the reference's ctx->repeat_penalty,
+ * no_repeat_ngram_size and temperature (ds_ocr.h; set from main.c:132-134,
+ * read by ds_decoder_forward at ds_moe_decoder.c:1021-1263). Defaults 1, 0,
+ * 0 (greedy argmax). repeat_penalty > 1: the history tokens' logits are
+ * divided (positive) or multiplied (negative) by it; no_repeat_ngram_size
+ * n > 0: a token that would complete an n-gram already in the history is
+ * banned; temperature > 0: softmax sampling with the uniforms given by
+ * ds_cuda_decoder_set_uniforms. Engine 0 only (EINVAL with engine 1).
+ * Forward and generate then return the selected token (and its penalised
+ * logit). */
+int ds_cuda_decoder_set_sampling(ds_cuda_ctx_t *ctx, int model, float repeat_penalty, int no_repeat_ngram_size,
+                                 float temperature);
+/* The generated-token history (ctx->token_history, ds_ocr.h:433-435): every
+ * decode step appends its token, as the reference's generation loop does
+ * (ds_ocr.c:2245-2248). set replaces it (n <= kv_max + 512); get copies up
+ * to cap tokens and returns the length. */
+int ds_cuda_decoder_set_history(ds_cuda_ctx_t *ctx, int model, const int *tokens, int n);
+int ds_cuda_decoder_get_history(ds_cuda_ctx_t *ctx, int model, int *tokens, int cap);
+/* Uniforms for temperature sampling, consumed one per sampled step in order
+ * (the reference draws (float)rand() / RAND_MAX, ds_moe_decoder.c:1251).
+ * Forward/generate return DS_CUDA_ESTATE when too few are left. */
+int ds_cuda_decoder_set_uniforms(ds_cuda_ctx_t *ctx, int model, const float *u, int n);
+
 /* ---------------------------------------------------------------------
  * Multi-stream decoder — ds_decoder_forward for up to 64 independent
  * streams at once (each with its own KV cache and position; the reference

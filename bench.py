@@ -291,6 +291,21 @@ def decode_bytes(first_pos, n_steps):
     return DEC_WEIGHT_BYTES * n_steps + KV_BYTES_PER_KEY * keys
 
 
+def sampling_of(args):
+    """(repeat_penalty, no_repeat_ngram_size, temperature) of the decode
+    workloads; all defaults = greedy argmax (the reference's defaults,
+    ds_ocr.c:949-951)."""
+    return (getattr(args, "repeat_penalty", 1.0), getattr(args, "no_repeat_ngram", 0),
+            getattr(args, "temperature", 0.0))
+
+
+def decode_mode(args):
+    rp, ng, t = sampling_of(args)
+    if rp <= 1.0 and ng <= 0 and t <= 0.0:
+        return "greedy"
+    return f"repeat_penalty={rp:g}, no_repeat_ngram_size={ng}, temperature={t:g}"
+
+
 def decode_config(kv_max):
     return {"workload": "config3_decode_b1", "model": "DeepSeek3B-MoE decoder (12 layers, random init)",
             "global_batch": 1, "streams_per_gpu": 1, "kv_prefix": PREFIX, "kv_max": kv_max,
@@ -314,11 +329,26 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
     kv_max = 1024
     dec = Decoder(model, ctx, kv_max=kv_max, engine=args.engine)
     dec.load_kv(ks, vs)
+    rp, ng, temp = sampling_of(args)
+    sampled = decode_mode(args) != "greedy"
+    if sampled:
+        dec.set_sampling(rp, ng, temp)
+    unif = np.random.default_rng(17).random(max(args.steps, args.warmup) + 1).astype(np.float32)
+
+    def fresh_history():
+        # each phase starts a generation: empty history, its own uniforms
+        if sampled:
+            dec.set_history([])
+            if temp > 0:
+                dec.set_uniforms(unif)
+
     st = torch.cuda.ExternalStream(ctx.stream)
     e0 = model.embed(1)
     # warm-up (graph capture happens here), then reset to the prefix
+    fresh_history()
     dec.generate(args.warmup, first_embed=e0)
     dec.set_len(PREFIX)
+    fresh_history()
     dec.forward(e0)
     first = PREFIX + 1
     ctx.synchronize()
@@ -340,6 +370,7 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
     # embedding (the reference's decode loop, ds_ocr.c:2157-2282)
     n_e2e = args.steps
     dec.set_len(PREFIX)
+    fresh_history()
     e = e0
     ctx.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -377,12 +408,14 @@ def run_ours_decode(args, rank, world, pg, model, ks, vs):
     step_ach = step_bytes / (ms_max / 1e3) / 1e9
     res = {
         "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
-        "metric": "decode tokens/s (greedy, batch 1 per GPU, 12-layer DeepSeek3B-MoE, 662-token KV prefix)",
+        "metric": f"decode tokens/s ({decode_mode(args)}, batch 1 per GPU, 12-layer DeepSeek3B-MoE, "
+                  "662-token KV prefix)",
         "unit": "tokens/s", "dtype": "bf16 weights + bf16 KV, f32 math",
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 1280 * 4, "d2h_bytes_per_step": 8},
         # persistent engine: the timed region is ONE kernel launch for all steps
         "gpu_launches": launches * args.steps if launches else 1,
-        "config": dict(decode_config(kv_max), engine=["kernel graph", "persistent kernel"][args.engine]),
+        "config": dict(decode_config(kv_max), engine=["kernel graph", "persistent kernel"][args.engine],
+                       **({"sampling": decode_mode(args)} if sampled else {})),
         "roofline": {"bound": "hbm", "achieved": lm_ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": lm_ach / pk["hbm_gbs"], "traffic": TRAFFIC_ARGMAX_TMA,
                      "kernel": "argmax_tma_kernel (LM head 129280x1280, 330,956,800 B/launch)",
@@ -476,20 +509,23 @@ def run_ours_decode_streams(args, rank, world, pg, model, prefixes):
     return res
 
 
-def ref_decode_time(model, ks, vs, threads, budget_s, max_steps):
+def ref_decode_time(model, ks, vs, threads, budget_s, max_steps, sampling=(1.0, 0, 0.0)):
     """The reference's own ds_decoder_forward (compiled unmodified) on the
-    same weights and KV prefix, `threads` host threads."""
+    same weights and KV prefix, `threads` host threads, with the sampling
+    settings and the generation loop's history (ds_ocr.c:2245-2248)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     R = O.RefDecoder(model, kv_max=1024, threads=threads)
     R.load_kv(ks, vs)
+    R.set_sampling(*sampling)
+    R.set_history([])
     e = model.embed(1)
-    tok, _, _ = R.step(e)           # warm (page-in, thread pool)
+    tok = R.step_gen(e)             # warm (page-in, thread pool)
     e = model.embed(tok)
     n, t_total = 0, 0.0
     while t_total < budget_s and n < max_steps:
         t = time.perf_counter()
-        tok, _, _ = R.step(e)
+        tok = R.step_gen(e)
         t_total += time.perf_counter() - t
         e = model.embed(tok)
         n += 1
@@ -818,6 +854,12 @@ def main():
     ap.add_argument("--prefill-layers", type=int, default=PF_LAYERS,
                     help="prefill: MoE layers per step (11 = config 4; fewer only for small profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--repeat-penalty", type=float, default=1.0,
+                    help="decode: the reference's --repeat-penalty (> 1 enables)")
+    ap.add_argument("--no-repeat-ngram", type=int, default=0,
+                    help="decode: the reference's --no-repeat-ngram (V3 CLI default 35)")
+    ap.add_argument("--temperature", type=float, default=0.0,
+                    help="decode: sampling temperature (> 0 enables; uniforms supplied per step)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local, pg = dist_setup(args.gpus)
@@ -830,9 +872,13 @@ def main():
             return
         if args.workload == "decode":
             model, ks, vs = build_decode_model()
-            v, n = ref_decode_time(model, ks, vs, T, max(args.cpu_budget, 1.0), max_steps=args.steps)
-            metric = "decode tokens/s (greedy, batch 1 per GPU, 12-layer DeepSeek3B-MoE, 662-token KV prefix)"
-            cfg, sample = decode_config(1024), f"{n} greedy ds_decoder_forward steps from position 663"
+            v, n = ref_decode_time(model, ks, vs, T, max(args.cpu_budget, 1.0), max_steps=args.steps,
+                                   sampling=sampling_of(args))
+            metric = (f"decode tokens/s ({decode_mode(args)}, batch 1 per GPU, 12-layer DeepSeek3B-MoE, "
+                      "662-token KV prefix)")
+            cfg, sample = decode_config(1024), f"{n} {decode_mode(args)} ds_decoder_forward steps from position 663"
+            if decode_mode(args) != "greedy":
+                cfg["sampling"] = decode_mode(args)
         elif args.workload == "lm_head":
             v, n = ref_lmhead_time(T, max(args.cpu_budget, 1.0))
             metric = "argmax LM head tokens/s (batch 64, vocab 129280 x 1280 BF16)"
@@ -886,9 +932,9 @@ def main():
     if not args.no_cpu_baseline and world == 1:
         try:
             if args.workload in ("decode", "decode64"):
-                v, n = ref_decode_time(model, ks, vs, T, args.cpu_budget, max_steps=64)
-                sample = f"{n} greedy ds_decoder_forward steps from position 663 (one stream; the reference " \
-                         "decodes streams one at a time)"
+                v, n = ref_decode_time(model, ks, vs, T, args.cpu_budget, max_steps=64, sampling=sampling_of(args))
+                sample = f"{n} {decode_mode(args)} ds_decoder_forward steps from position 663 (one stream; " \
+                         "the reference decodes streams one at a time)"
             elif args.workload == "lm_head":
                 v, n = ref_lmhead_time(T, args.cpu_budget)
                 sample = f"{n} ds_argmax_matvec_bf16 calls (one per input)"

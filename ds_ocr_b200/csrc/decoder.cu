@@ -263,7 +263,7 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             CKL(launch_argmax_bf16(m->lm_head, m->xa, g.vocab, H, m->slot, m->tickets + 0, m->tok, m->val, st, pdl,
                                    m->final_norm, g.rms_eps),
                 "lm head launch");
-            launches += 2;  // the argmax and the history dots
+            launches += m->rp > 1.f ? 2 : 1;  // the argmax (and the history dots for the penalty)
         }
         SelectArgs sa = {};
         sa.W = m->lm_head;

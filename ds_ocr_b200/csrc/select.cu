@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(1024) select_fast_kernel(SelectArgs a) {
     }
     const int len = *a.hist_len;
     int best = *a.tok;
-    float bv = *a.bval;
+    // the recomputed row dot with a penalty; the argmax kernel's value without
+    float bv = a.rp > 1.f ? *a.bval : *a.val;
     if (a.rp > 1.f && len > 0) {
         bool in = false;
         for (int i = threadIdx.x; i < len; i += blockDim.x) in = in || a.hist[i] == best;
@@ -181,7 +182,7 @@ __global__ void __launch_bounds__(1024) select_full_kernel(SelectArgs a) {
     __shared__ float sv[32];
     __shared__ int si[32];
     __shared__ double sd[32];
-    __shared__ float sf[1024];
+    __shared__ float sf[32];
     if (!*a.full) return;
     const int len = *a.hist_len;
     const int tid = threadIdx.x, nt = blockDim.x;
@@ -227,54 +228,55 @@ __global__ void __launch_bounds__(1024) select_full_kernel(SelectArgs a) {
     sel_block_argmax(v, at, sv, si);
     int tok = at == 0x7fffffff ? 0 : at;
     const float best = v;
-    // 4. temperature sampling over contiguous per-thread segments
+    // 4. temperature sampling: exponentials and their double sum in a
+    //    coalesced pass; then the cumulative F32 sum over contiguous
+    //    per-warp segments, each walked 32 elements at a time with a warp
+    //    scan, to the first element where it reaches r
     if (a.temperature > 0.f) {
-        const int seg = (a.V + nt - 1) / nt;
-        const int s0 = min(a.V, tid * seg), s1 = min(a.V, s0 + seg);
         double ds = 0.0;
-        for (int i = s0; i < s1; i++) {
+        for (int i = tid; i < a.V; i += nt) {
             const float e = expf(__fdiv_rn(__fsub_rn(lg[i], best), a.temperature));
             lg[i] = e;
             ds += (double)e;
         }
         for (int o = 16; o > 0; o >>= 1) ds += __shfl_xor_sync(DS_FULL, ds, o);
-        if ((tid & 31) == 0) sd[tid >> 5] = ds;
+        const int w = tid >> 5, lane = tid & 31, nwarp = nt >> 5;
+        if (lane == 0) sd[w] = ds;
         __syncthreads();
         double tot = 0.0;
-        for (int w = 0; w < (nt >> 5); w++) tot += sd[w];
+        for (int q = 0; q < nwarp; q++) tot += sd[q];
         const float inv = (float)(1.0 / tot);
+        const int seg = ((a.V + nwarp - 1) / nwarp + 31) & ~31;
+        const int s0 = min(a.V, w * seg), s1 = min(a.V, s0 + seg);
         float fs = 0.f;
-        for (int i = s0; i < s1; i++) fs = __fadd_rn(fs, __fmul_rn(lg[i], inv));
-        // exclusive prefix of the segment sums, in thread order
-        sf[tid] = fs;
+        for (int i = s0 + lane; i < s1; i += 32) fs = __fadd_rn(fs, __fmul_rn(lg[i], inv));
+        for (int o = 16; o > 0; o >>= 1) fs = __fadd_rn(fs, __shfl_xor_sync(DS_FULL, fs, o));
+        if (lane == 0) sf[w] = fs;
         __syncthreads();
-        if (tid == 0) {
-            float acc = 0.f;
-            for (int t = 0; t < nt; t++) {
-                const float x = sf[t];
-                sf[t] = acc;
-                acc = __fadd_rn(acc, x);
-            }
-        }
-        __syncthreads();
+        float carry = 0.f;  // exclusive prefix of the segment sums, in warp order
+        for (int q = 0; q < w; q++) carry = __fadd_rn(carry, sf[q]);
         const float r = a.unif[*a.unif_pos];
-        float cum = sf[tid];
         int hit = 0x7fffffff;
-        for (int i = s0; i < s1; i++) {
-            cum = __fadd_rn(cum, __fmul_rn(lg[i], inv));
-            if (cum >= r) {
-                hit = i;
+        for (int base = s0; base < s1; base += 32) {
+            const int i = base + lane;
+            float x = i < s1 ? __fmul_rn(lg[i], inv) : 0.f;
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(DS_FULL, x, o);
+                if (lane >= o) x = __fadd_rn(x, y);
+            }
+            const float cum = __fadd_rn(carry, x);
+            const unsigned b = __ballot_sync(DS_FULL, i < s1 && cum >= r);
+            if (b) {
+                hit = base + __ffs(b) - 1;
                 break;
             }
+            carry = __fadd_rn(carry, __shfl_sync(DS_FULL, x, 31));
         }
-        int h = hit;
-        // the first segment that reaches r
-        for (int o = 16; o > 0; o >>= 1) h = min(h, __shfl_xor_sync(DS_FULL, h, o));
         __syncthreads();
-        if ((tid & 31) == 0) si[tid >> 5] = h;
+        if (lane == 0) si[w] = hit;
         __syncthreads();
-        h = 0x7fffffff;
-        for (int w = 0; w < (nt >> 5); w++) h = min(h, si[w]);
+        int h = 0x7fffffff;
+        for (int q = 0; q < nwarp; q++) h = min(h, si[q]);
         tok = h == 0x7fffffff ? a.V - 1 : h;
         __syncthreads();
         if (tid == 0) *a.unif_pos = *a.unif_pos + 1;
@@ -301,7 +303,7 @@ cudaError_t launch_select(const SelectArgs &a, cudaStream_t st) {
     SelectArgs aa = a;
     void *args[] = {&aa};
     cudaError_t e = cudaSuccess;
-    if (a.temperature <= 0.f) {
+    if (a.temperature <= 0.f && a.rp > 1.f) {  // the history dots feed the penalty only
         const int warps = a.cap + 1;
         e = launch_ex((const void *)select_dots_kernel, (warps + 7) / 8, 256, 0, st, false, args);
         if (e != cudaSuccess) return e;

@@ -369,11 +369,45 @@ static void dense_ffn(float *out, const float *x, const orc_layer_t *ly, const o
  * first_dense) or MoE, residual add; final RMSNorm; argmax LM head.
  * KV layout [layer][kv_max][H] F32. Returns the token; final_x receives
  * the normed hidden state, logit its LM-head logit. */
+/* Reference sliding-window attention of V3 decode (R-SWA,
+ * ds_moe_decoder.c:409-436 -> ds_rswa_attention_aligned,
+ * ds_kernels.c:2255-2314): with window W > 0 and the query at or past the
+ * prefill length P, the keys are [0, P) then [max(P, n - W), n), through the
+ * same sequential softmax; when the two ranges touch, plain causal. The
+ * rows are gathered into a compact copy and attended in that order. */
+static void attention_rswa(float *out, const float *q, const float *K, const float *V, int n, int nh, int hd,
+                           int stride, float scale, int window, int ref_len, int pos) {
+    int ws = ref_len > n - window ? ref_len : n - window;
+    if (window <= 0 || pos < ref_len || ws <= ref_len) {
+        orc_attention_decode(out, q, K, V, n, nh, hd, stride, scale);
+        return;
+    }
+    int m = ref_len + (n - ws);
+    float *Kc = (float *)malloc((size_t)m * stride * sizeof(float));
+    float *Vc = (float *)malloc((size_t)m * stride * sizeof(float));
+    memcpy(Kc, K, (size_t)ref_len * stride * sizeof(float));
+    memcpy(Vc, V, (size_t)ref_len * stride * sizeof(float));
+    memcpy(Kc + (size_t)ref_len * stride, K + (size_t)ws * stride, (size_t)(n - ws) * stride * sizeof(float));
+    memcpy(Vc + (size_t)ref_len * stride, V + (size_t)ws * stride, (size_t)(n - ws) * stride * sizeof(float));
+    orc_attention_decode(out, q, Kc, Vc, m, nh, hd, stride, scale);
+    free(Kc);
+    free(Vc);
+}
+
 int orc_decoder_step(const orc_layer_t *layers, const orc_dims_t *d,
                      const float *final_norm, const uint16_t *lm_head,
                      float *kv_k, float *kv_v, int kv_max, int pos,
                      const float *cos_t, const float *sin_t, int use_int8,
                      const float *embed, float *final_x, float *logit) {
+    return orc_decoder_step_swa(layers, d, final_norm, lm_head, kv_k, kv_v, kv_max, pos, cos_t, sin_t, use_int8,
+                                embed, final_x, logit, 0, 0);
+}
+
+int orc_decoder_step_swa(const orc_layer_t *layers, const orc_dims_t *d,
+                         const float *final_norm, const uint16_t *lm_head,
+                         float *kv_k, float *kv_v, int kv_max, int pos,
+                         const float *cos_t, const float *sin_t, int use_int8,
+                         const float *embed, float *final_x, float *logit, int window, int ref_len) {
     int H = d->hidden, hd = d->head_dim, nh = d->n_heads, qd = nh * hd;
     float *x = (float *)malloc((size_t)H * sizeof(float));
     float *xn = (float *)malloc((size_t)H * sizeof(float));
@@ -398,7 +432,7 @@ int orc_decoder_step(const orc_layer_t *layers, const orc_dims_t *d,
         float *Vl = kv_v + (size_t)l * kv_max * qd;
         memcpy(Kl + (size_t)pos * qd, k, (size_t)qd * sizeof(float));
         memcpy(Vl + (size_t)pos * qd, v, (size_t)qd * sizeof(float));
-        orc_attention_decode(att, q, Kl, Vl, pos + 1, nh, hd, qd, scale);
+        attention_rswa(att, q, Kl, Vl, pos + 1, nh, hd, qd, scale, window, ref_len, pos);
         orc_matvec_bf16(proj, att, ly->wo, qd, H);
         orc_residual_rms_norm(o, xn, x, proj, ly->post_norm, H, d->eps);
         if (l < d->first_dense) dense_ffn(mlp, xn, ly, d);

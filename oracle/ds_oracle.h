@@ -82,6 +82,13 @@ int orc_decoder_step(const orc_layer_t *layers, const orc_dims_t *d,
                      const float *embed, float *final_x, float *logit);
 int orc_lm_select(const float *xn, const uint16_t *W, int H, int V, const int *hist, int len, float rp,
                   int ngram, float temperature, float r, float *val, int *full);
+/* orc_decoder_step with V3's reference sliding-window attention: window
+ * W > 0 and prefill length ref_len (ds_moe_decoder.c:409-436). */
+int orc_decoder_step_swa(const orc_layer_t *layers, const orc_dims_t *d,
+                         const float *final_norm, const uint16_t *lm_head,
+                         float *kv_k, float *kv_v, int kv_max, int pos,
+                         const float *cos_t, const float *sin_t, int use_int8,
+                         const float *embed, float *final_x, float *logit, int window, int ref_len);
 void orc_prefill_moe(const orc_layer_t *ly, const orc_dims_t *d, float *x, int seq_len,
                      const float *logits, int *idx_out, float *w_out);
 

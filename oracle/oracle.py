@@ -100,6 +100,7 @@ def oracle():
             "orc_attention_decode": (None, [P, P, P, P, c_int, c_int, c_int, c_int, c_float]),
             "orc_decoder_step": (c_int, [P, P, P, P, P, P, c_int, c_int, P, P, c_int, P, P, P]),
             "orc_prefill_moe": (None, [P, P, P, c_int, P, P, P]),
+            "orc_decoder_step_swa": (c_int, [P, P, P, P, P, P, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int]),
             "orc_lm_select": (c_int, [P, P, c_int, c_int, P, c_int, c_float, c_int, c_float, c_float, P, P]),
         }
         for k, (r, a) in sig.items():
@@ -151,6 +152,7 @@ def ref():
             "ref_ctx_get_history": (c_int, [P, P, c_int]),
             "ref_decoder_step_gen": (c_int, [P, P]),
             "ref_srand": (None, [ctypes.c_uint]),
+            "ref_ctx_set_window": (None, [P, c_int, c_int]),
         }
         for k, (res, a) in sig.items():
             f = getattr(r, k)
@@ -210,6 +212,10 @@ class RefDecoder:
         out = np.empty(self.r.ref_ctx_get_history(self.ctx, None, 0), np.int32)
         self.r.ref_ctx_get_history(self.ctx, addr(out), out.size)
         return out
+
+    def set_window(self, sliding_window_size, prefill_token_count):
+        """V3's reference sliding-window attention (ds_moe_decoder.c:409-436)."""
+        self.r.ref_ctx_set_window(self.ctx, sliding_window_size, prefill_token_count)
 
     def step_gen(self, embed):
         """A generation-loop step: decode, then append the token to the history."""
@@ -289,15 +295,19 @@ class OracleDecoder:
             self.v[l, :n] = vs[l]
         self.pos = n
 
+    window = 0    # V3 sliding window (0: full causal attention)
+    ref_len = 0   # prefill length the window keeps
+
     def step(self, embed, use_int8=False):
         d = self.model.d
         if use_int8:
             self.refresh()
         fx = np.empty(d.hidden, np.float32)
         lg = np.empty(1, np.float32)
-        tok = self.o.orc_decoder_step(self.layers, ctypes.byref(self.dims), addr(self.model.final_norm),
-                                      addr(self.model.lm_head), addr(self.k), addr(self.v), self.kv_max, self.pos,
-                                      addr(self.cos), addr(self.sin), int(use_int8), addr(embed), addr(fx), addr(lg))
+        tok = self.o.orc_decoder_step_swa(self.layers, ctypes.byref(self.dims), addr(self.model.final_norm),
+                                          addr(self.model.lm_head), addr(self.k), addr(self.v), self.kv_max,
+                                          self.pos, addr(self.cos), addr(self.sin), int(use_int8), addr(embed),
+                                          addr(fx), addr(lg), self.window, self.ref_len)
         self.pos += 1
         return tok, fx, float(lg[0])
 

@@ -278,6 +278,15 @@ int ref_decoder_step_gen(void *vctx, const float *embed) {
     return tok;
 }
 
+/* V3's reference sliding-window attention: cfg->sliding_window_size and
+ * ctx->prefill_token_count, read by decoder_layer_forward
+ * (ds_moe_decoder.c:409-436). */
+void ref_ctx_set_window(void *vctx, int sliding_window_size, int prefill_token_count) {
+    ds_ctx_t *ctx = (ds_ctx_t *)vctx;
+    ctx->config.sliding_window_size = sliding_window_size;
+    ctx->prefill_token_count = prefill_token_count;
+}
+
 /* Seeds the C library generator that the temperature path draws from. */
 void ref_srand(unsigned seed) { srand(seed); }
 

@@ -57,6 +57,7 @@ SIGNATURES = {
     "ds_cuda_decoder_set_history": (c_int, [P, c_int, P, c_int]),
     "ds_cuda_decoder_get_history": (c_int, [P, c_int, P, c_int]),
     "ds_cuda_decoder_set_uniforms": (c_int, [P, c_int, P, c_int]),
+    "ds_cuda_decoder_set_window": (c_int, [P, c_int, c_int, c_int]),
     "ds_cuda_batch_decoder_create": (c_int, [P, P, P, P, P, c_int]),
     "ds_cuda_batch_decoder_destroy": (c_int, [P, c_int]),
     "ds_cuda_batch_decoder_load_kv": (c_int, [P, c_int, c_int, c_int, c_int, c_int, P, P]),

@@ -60,6 +60,8 @@ struct DecoderModel {
     int unif_n = 0;       // uniforms supplied
     int unif_used = 0;    // uniforms consumed by launched steps (host count)
     bool sampling() const { return rp > 1.f || ngram > 0 || temperature > 0.f; }
+    // V3's reference sliding-window attention: window, prefill length
+    int swa_window = 0, swa_ref = 0;
     std::vector<void *> allocs;
 
     size_t plane_elems() const {
@@ -157,6 +159,8 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
         aa.lo_start = m->lo_start[l];
         aa.scale = 1.0f / sqrtf((float)HD);
         aa.out = m->attn;
+        aa.swa_window = m->swa_window;
+        aa.swa_ref = m->swa_ref;
         CKL(launch_attn_decode(aa, st, pdl), "attention launch");
         MvArgs oa = {};
         oa.W = L.wo;
@@ -826,5 +830,24 @@ extern "C" int ds_cuda_decoder_set_uniforms(ds_cuda_ctx_t *c, int id, const floa
     CKL(cudaMemcpy(m->unif_pos, &zero, 4, cudaMemcpyHostToDevice), "uniform position");
     m->unif_n = n;
     m->unif_used = 0;
+    return DS_CUDA_OK;
+}
+
+// V3's reference sliding-window decode attention (R-SWA): the reference's
+// cfg->sliding_window_size and ctx->prefill_token_count (ds_ocr.h), read by
+// decoder_layer_forward (ds_moe_decoder.c:409-436). 0 disables. Graph
+// engine only.
+extern "C" int ds_cuda_decoder_set_window(ds_cuda_ctx_t *c, int id, int sliding_window_size,
+                                          int prefill_token_count) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || sliding_window_size < 0 || prefill_token_count < 0)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_window: bad argument");
+    if (m->mega && sliding_window_size > 0)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_window: the persistent engine attends causally only");
+    cudaSetDevice(c->device);
+    CKL(cudaStreamSynchronize(c->stream), "set window");
+    m->swa_window = sliding_window_size;
+    m->swa_ref = prefill_token_count;
+    drop_graphs(m);
     return DS_CUDA_OK;
 }

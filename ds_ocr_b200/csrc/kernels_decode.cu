@@ -201,7 +201,9 @@ __device__ __forceinline__ float block_sum256(float v, float *buf) {
 
 // PRE: load the first block of KV rows before the dependency wait (for
 // launches chained with programmatic dependent launch).
-template <int CL, bool PRE>
+// SWA: V3's reference sliding window (a separate instantiation, so the
+// full-causal kernels keep their registers).
+template <int CL, bool PRE, bool SWA = false>
 __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     __shared__ float sc_own[CL > 1 ? ATT_MAXK / CL : 1];
     __shared__ float wts[ATT_MAXK];
@@ -221,7 +223,15 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     // the newest, which the predecessor writes) is readable before the
     // dependency wait: the first block of K and V rows loads here.
     const int sidx = blockIdx.y;
-    const int n = a.d_pos[sidx] + 1;
+    const int n_all = a.d_pos[sidx] + 1;
+    // V3's reference sliding window (ds_moe_decoder.c:409-436): once the
+    // query is at or past the prefill length P, the keys are rows [0, P)
+    // then [max(P, n - W), n); key j (0 .. n-1 below) is row j < P ? j : j + gap
+    int gap = 0;
+    if (SWA && a.swa_window > 0 && n_all - 1 >= a.swa_ref) gap = max(0, n_all - a.swa_window - a.swa_ref);
+    const int n = n_all - gap;
+    const int swa_ref = a.swa_ref;
+    auto row = [&](int j) { return SWA ? (j < swa_ref ? j : j + gap) : j; };
     const int lo_start = a.lo_starts ? a.lo_starts[sidx] : a.lo_start;
     const int per = (n + CL - 1) / CL;
     const int j0 = min(n, crank * per), j1 = min(n, j0 + per);
@@ -230,9 +240,16 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     float *out = a.out + (size_t)sidx * a.q_stride;
     const uint16_t *khi = a.k_hi + hoff, *klo = a.k_lo + hoff, *vhi = a.v_hi + hoff, *vlo = a.v_lo + hoff;
     if (tid == 0 && j1 > j0) {
-        prefetch_range(vhi + (size_t)j0 * ATT_HD, (size_t)(j1 - j0) * ATT_HD * 2);
-        int ls = max(j0, lo_start);
-        if (ls < j1) prefetch_range(vlo + (size_t)ls * ATT_HD, (size_t)(j1 - ls) * ATT_HD * 2);
+        // this CTA's V rows: one range, or two around the window's gap
+        const int cut = SWA && gap ? min(max(j0, swa_ref), j1) : j1;
+        for (int piece = 0; piece < 2; piece++) {
+            const int a0 = piece ? cut : j0, a1 = piece ? j1 : cut;
+            if (a1 <= a0) continue;
+            const int r0 = row(a0), r1 = row(a1 - 1) + 1;
+            prefetch_range(vhi + (size_t)r0 * ATT_HD, (size_t)(r1 - r0) * ATT_HD * 2);
+            const int ls = max(r0, lo_start);
+            if (ls < r1) prefetch_range(vlo + (size_t)ls * ATT_HD, (size_t)(r1 - ls) * ATT_HD * 2);
+        }
     }
     Row16 kraw0[ATT_KPG], vraw[ATT_KPG];
     if constexpr (PRE) {
@@ -240,11 +257,11 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
         for (int r = 0; r < ATT_KPG; r++) {
             const int j = j0 + g + 32 * r;
             const bool old = j < j1 && j < n - 1;
-            kraw0[r] = old ? load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16,
-                                        j >= lo_start)
+            kraw0[r] = old ? load_raw16(khi + (size_t)row(j) * ATT_HD + li * 16, klo + (size_t)row(j) * ATT_HD + li * 16,
+                                        row(j) >= lo_start)
                            : Row16{};
-            vraw[r] = old ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
-                                       j >= lo_start)
+            vraw[r] = old ? load_raw16(vhi + (size_t)row(j) * ATT_HD + li * 16, vlo + (size_t)row(j) * ATT_HD + li * 16,
+                                       row(j) >= lo_start)
                           : Row16{};
         }
     }
@@ -255,8 +272,8 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
         for (int r = 0; r < ATT_KPG; r++) {
             const int j = j0 + g + 32 * r;
             if (j == n - 1 && j < j1) {  // the newest row, written by the predecessor
-                kraw0[r] = load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16, true);
-                vraw[r] = load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16, true);
+                kraw0[r] = load_raw16(khi + (size_t)row(j) * ATT_HD + li * 16, klo + (size_t)row(j) * ATT_HD + li * 16, true);
+                vraw[r] = load_raw16(vhi + (size_t)row(j) * ATT_HD + li * 16, vlo + (size_t)row(j) * ATT_HD + li * 16, true);
             }
         }
     }
@@ -279,16 +296,16 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
             int j = jb + g + 32 * r;
             if (PRE && blk == 0) kraw[r] = kraw0[r];
             else
-                kraw[r] = j < j1 ? load_raw16(khi + (size_t)j * ATT_HD + li * 16, klo + (size_t)j * ATT_HD + li * 16,
-                                              j >= lo_start)
+                kraw[r] = j < j1 ? load_raw16(khi + (size_t)row(j) * ATT_HD + li * 16, klo + (size_t)row(j) * ATT_HD + li * 16,
+                                              row(j) >= lo_start)
                                  : Row16{};
         }
         if (!PRE && blk == 0) {
 #pragma unroll
             for (int r = 0; r < ATT_KPG; r++) {
                 int j = jb + g + 32 * r;
-                vraw[r] = j < j1 ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
-                                              j >= lo_start)
+                vraw[r] = j < j1 ? load_raw16(vhi + (size_t)row(j) * ATT_HD + li * 16, vlo + (size_t)row(j) * ATT_HD + li * 16,
+                                              row(j) >= lo_start)
                                  : Row16{};
             }
         }
@@ -360,8 +377,8 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
         for (int r = 0; r < ATT_KPG; r++) {
             int j = jb + g + 32 * r;
             if (blk == 0) vr[r] = vraw[r];
-            else vr[r] = j < j1 ? load_raw16(vhi + (size_t)j * ATT_HD + li * 16, vlo + (size_t)j * ATT_HD + li * 16,
-                                             j >= lo_start)
+            else vr[r] = j < j1 ? load_raw16(vhi + (size_t)row(j) * ATT_HD + li * 16, vlo + (size_t)row(j) * ATT_HD + li * 16,
+                                             row(j) >= lo_start)
                                 : Row16{};
         }
 #pragma unroll
@@ -401,8 +418,9 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
 }
 
 // batch 1: a cluster of ATT_CL CTAs per head splits the keys
+template <bool SWA>
 __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
-    attn_body<ATT_CL, true>(a);
+    attn_body<ATT_CL, true, SWA>(a);
 }
 // many streams: one CTA per (head, stream) over all of the stream's keys
 __global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn_body<1, false>(a); }
@@ -604,12 +622,13 @@ cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int n_streams) {
-    if (a.kv_max > ATT_MAXK) return cudaErrorInvalidValue;
+    if (a.kv_max > ATT_MAXK || (n_streams > 1 && a.swa_window > 0)) return cudaErrorInvalidValue;
     AttnArgs aa = a;
     void *args[] = {&aa};
     // cluster dims are compiled into the kernel (__cluster_dims__)
     if (n_streams == 1)
-        return launch_ex((const void *)attn_decode_kernel, a.n_heads * ATT_CL, 256, 0, st, pdl, args);
+        return launch_ex(a.swa_window > 0 ? (const void *)attn_decode_kernel<true> : (const void *)attn_decode_kernel<false>,
+                         a.n_heads * ATT_CL, 256, 0, st, pdl, args);
     // (clusters of 2 or 4 CTAs per (head, stream) measured slower at 64 streams)
     return launch_ex((const void *)attn_streams_kernel, dim3(a.n_heads, n_streams), 256, 0, st, pdl, args);
 }

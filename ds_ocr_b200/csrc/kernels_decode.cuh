@@ -32,6 +32,9 @@ struct AttnArgs {
     long long kv_stream_stride;
     int q_stride;
     const int *lo_starts;
+    // V3 reference sliding-window attention (0: off): window W, prefill
+    // length P
+    int swa_window, swa_ref;
 };
 
 // Router folded into the O-projection (optional): logits_e =

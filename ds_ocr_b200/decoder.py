@@ -160,6 +160,11 @@ class Decoder:
                            "decoder_get_history")
         return out
 
+    def set_window(self, sliding_window_size, prefill_token_count):
+        """V3's reference sliding-window attention (0 disables)."""
+        self.ctx.check(self.lib.ds_cuda_decoder_set_window(self.ctx.h, self.id, sliding_window_size,
+                                                           prefill_token_count), "decoder_set_window")
+
     def set_uniforms(self, u):
         """Uniforms for temperature sampling, one per sampled step."""
         u = np.ascontiguousarray(u, np.float32)

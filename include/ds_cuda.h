@@ -299,6 +299,13 @@ int ds_cuda_decoder_get_history(ds_cuda_ctx_t *ctx, int model, int *tokens, int 
  * (the reference draws (float)rand() / RAND_MAX, ds_moe_decoder.c:1251).
  * Forward/generate return DS_CUDA_ESTATE when too few are left. */
 int ds_cuda_decoder_set_uniforms(ds_cuda_ctx_t *ctx, int model, const float *u, int n);
+/* V3's reference sliding-window decode attention (R-SWA): the reference's
+ * cfg->sliding_window_size and ctx->prefill_token_count (ds_ocr.h:438),
+ * read at ds_moe_decoder.c:409-436. With W > 0 and the query at or past
+ * prefill_token_count P, each step attends rows [0, P) and then
+ * [max(P, len - W), len) through the same sequential softmax. 0 disables
+ * (full causal attention). Engine 0 only. */
+int ds_cuda_decoder_set_window(ds_cuda_ctx_t *ctx, int model, int sliding_window_size, int prefill_token_count);
 
 /* ---------------------------------------------------------------------
  * Multi-stream decoder — ds_decoder_forward for up to 64 independent

@@ -1,6 +1,7 @@
 // api.cu — the C ABI declared in include/ds_cuda.h: context, weight
 // registration keyed by host pointer, and the host-pointer / device-pointer
 // entry points of the decode MoE layer, LM head, matvec and INT8 quantiser.
+#include <sys/mman.h>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -105,6 +106,17 @@ int ctx_register(ds_cuda_ctx *c, const void *p, size_t bytes) {
     return DS_CUDA_OK;
 }
 
+void *ctx_adopt(ds_cuda_ctx *c, void *dev, size_t bytes) {
+    if (!dev || !bytes) return nullptr;
+    void *key = mmap(nullptr, bytes, PROT_NONE, MAP_PRIVATE | MAP_ANONYMOUS | MAP_NORESERVE, -1, 0);
+    if (key == MAP_FAILED) return nullptr;
+    c->key_ranges.emplace_back(key, bytes);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(key);
+    c->regs[a] = Reg{a, bytes, dev};
+    c->reg_bytes += bytes;
+    return key;
+}
+
 static int h2d(ds_cuda_ctx *c, void *d, const void *h, size_t bytes) {
     return ctx_cuda(c, cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, c->stream), "copy to device");
 }
@@ -171,6 +183,7 @@ extern "C" void ds_cuda_free(ds_cuda_ctx_t *c) {
     for (auto &e : c->prefill_ev)
         if (e) cudaEventDestroy(e);
     for (auto &kv : c->regs) cudaFree(kv.second.dev);
+    for (auto &r : c->key_ranges) munmap(r.first, r.second);
     void *bufs[] = {c->d_tickets, c->d_slots, c->d_tok, c->d_val, c->d_scores, c->d_idx, c->d_wt,
                     c->d_x, c->d_out, c->d_h, c->d_tmp, c->d_lt_planes, c->d_lt_err, c->d_sk_scratch};
     for (void *b : bufs)

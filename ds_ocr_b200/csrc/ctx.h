@@ -2,6 +2,7 @@
 #pragma once
 #include <cstdint>
 #include <map>
+#include <vector>
 #include <string>
 #include <cuda_runtime.h>
 #include "ds_cuda.h"
@@ -53,6 +54,9 @@ struct ds_cuda_ctx {
     // decoder models owned by this context
     std::map<int, DecoderModel *> models;
     int next_model = 1;
+    // host address ranges reserved (no access, no memory) as the keys of
+    // weights built directly in HBM (ingest.cu); released with the context
+    std::vector<std::pair<void *, size_t>> key_ranges;
 };
 
 int ctx_fail(ds_cuda_ctx *c, int code, const char *fmt, ...);
@@ -60,6 +64,9 @@ int ctx_cuda(ds_cuda_ctx *c, cudaError_t e, const char *what);
 int ctx_grow(ds_cuda_ctx *c, void **p, size_t *cap, size_t need);
 int ctx_pinned(ds_cuda_ctx *c, size_t need);
 int ctx_register(ds_cuda_ctx *c, const void *p, size_t bytes);
+// Registers device memory the context takes ownership of under a fresh
+// reserved host key range of the same size; returns the key (or null).
+void *ctx_adopt(ds_cuda_ctx *c, void *dev, size_t bytes);
 const void *ctx_lookup(ds_cuda_ctx *c, const void *p, size_t bytes, bool auto_register);
 void ctx_release_models(ds_cuda_ctx *c);
 void prefill_release(ds_cuda_ctx *c);

@@ -26,6 +26,7 @@ struct DecoderModel {
     std::vector<DecLayer> layers;
     const float *final_norm = nullptr;
     const uint16_t *lm_head = nullptr;
+    const uint16_t *embed = nullptr;  // token embedding table (the LM head unless set)
     // device state
     float *xa = nullptr, *xb = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *xfinal = nullptr;
     float *scores = nullptr, *wt = nullptr, *val = nullptr;
@@ -296,7 +297,7 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             "lm head launch");
         launches += 1;
     }
-    CKL(launch_decode_advance(m->lm_head, H, m->tok, m->pos, m->tok_log, m->xa, st, pdl, m->hist, m->hist_len,
+    CKL(launch_decode_advance(m->embed, H, m->tok, m->pos, m->tok_log, m->xa, st, pdl, m->hist, m->hist_len,
                               m->hist_cap),
         "advance launch");
     launches += 1;
@@ -355,6 +356,7 @@ static MegaParams mega_params(ds_cuda_ctx *c, DecoderModel *m) {
     p.layers = m->mega_dl;
     p.final_norm = m->final_norm;
     p.lm_head = m->lm_head;
+    p.embed = m->embed;
     p.cos_t = m->cos_t;
     p.sin_t = m->sin_t;
     p.xa = m->xa;
@@ -517,6 +519,7 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
         m->final_norm = (const float *)LOOK(final_norm, H * 4);
         m->lm_head = (const uint16_t *)LOOK(lm_head, (size_t)g.vocab * H * 2);
         if (!m->final_norm || !m->lm_head) rc = ctx_fail(c, DS_CUDA_ENOTREG, "decoder_create: head weights");
+        m->embed = m->lm_head;
     }
     size_t hcap = std::max((size_t)g.top_k * I + S, (size_t)g.dense_inter);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->xa, H);
@@ -848,6 +851,21 @@ extern "C" int ds_cuda_decoder_set_window(ds_cuda_ctx_t *c, int id, int sliding_
     CKL(cudaStreamSynchronize(c->stream), "set window");
     m->swa_window = sliding_window_size;
     m->swa_ref = prefill_token_count;
+    drop_graphs(m);
+    return DS_CUDA_OK;
+}
+
+// The token embedding table the step advance reads the next input from
+// (the reference's tok_embeddings_bf16, ds_ocr.c:2272-2279); by default the
+// LM head (tied embeddings). Host pointer to [vocab x hidden] BF16.
+extern "C" int ds_cuda_decoder_set_embeddings(ds_cuda_ctx_t *c, int id, const uint16_t *embed_tokens) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || !embed_tokens) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_set_embeddings: bad argument");
+    cudaSetDevice(c->device);
+    const void *d = ctx_lookup(c, embed_tokens, (size_t)m->cfg.vocab * m->cfg.hidden * 2, true);
+    if (!d) return ctx_fail(c, DS_CUDA_ENOTREG, "decoder_set_embeddings: table not registrable");
+    CKL(cudaStreamSynchronize(c->stream), "set embeddings");
+    m->embed = (const uint16_t *)d;
     drop_graphs(m);
     return DS_CUDA_OK;
 }

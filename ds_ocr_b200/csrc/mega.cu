@@ -519,7 +519,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(const MegaPa
                     // xa, normalised once per phase (xs persists across its chunks)
                     if (sub == 0) {
                         if (cur.layer == 0 && (cur.step > 0 || p.first_from_token)) {
-                            const uint16_t *e = p.lm_head + (size_t)tok * p.H;
+                            const uint16_t *e = p.embed + (size_t)tok * p.H;
                             for (int i = tid; i < p.H; i += MK_THREADS) xs[i] = __uint_as_float((uint32_t)e[i] << 16);
                             __syncthreads();
                             int xa0, xa1;

@@ -21,7 +21,8 @@ struct MegaParams {
     int simulate, renorm;
     const MegaLayer *layers;  // device array [L]
     const float *final_norm;
-    const uint16_t *lm_head;  // [V x H], also the embedding table
+    const uint16_t *lm_head;  // [V x H]
+    const uint16_t *embed;    // [V x H] token embeddings (the LM head when tied)
     const float *cos_t, *sin_t;
     // activations and cross-CTA exchange buffers (device)
     float *xa, *xb, *q;

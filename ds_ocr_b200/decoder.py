@@ -98,6 +98,32 @@ class Decoder:
                                                                  _a(model.final_norm), _a(model.lm_head)),
                                  "decoder_create")
 
+    @classmethod
+    def from_safetensors(cls, path, dims, ctx=None, kv_max=1024, use_int8=False, engine=0):
+        """A decoder whose weights come from a safetensors checkpoint (a
+        directory of model.safetensors / model-*.safetensors, or one file) in
+        the reference's tensor naming; dims: a synth.Dims of its shapes."""
+        self = cls.__new__(cls)
+        self.ctx = ctx or Context(0)
+        self.lib = self.ctx.lib
+        self.model = type("Shapes", (), {"d": dims})()
+        d = dims
+        self.cfg = DecoderConfig(d.hidden, d.n_layers, d.n_heads, d.head_dim, d.dense_inter, d.moe_inter,
+                                 d.n_experts, d.n_shared, d.top_k, d.vocab, d.first_dense, synth.RMS_EPS,
+                                 synth.ROPE_THETA, kv_max, int(use_int8), int(engine))
+        self.id = 0
+        self.id = self.ctx.check(self.lib.ds_cuda_decoder_create_from_safetensors(self.ctx.h, str(path).encode(),
+                                                                                ctypes.byref(self.cfg)),
+                                 "decoder_create_from_safetensors")
+        return self
+
+    def set_embeddings(self, table):
+        """The token embedding table of the device decode loop (default: the
+        LM head); a [vocab x hidden] BF16 array kept alive by the caller."""
+        t = np.ascontiguousarray(table, np.uint16)
+        self.ctx._pin(t)
+        self.ctx.check(self.lib.ds_cuda_decoder_set_embeddings(self.ctx.h, self.id, _a(t)), "decoder_set_embeddings")
+
     def load_kv(self, ks, vs, pos0=0):
         if ks[0].shape[0] == 0:
             self.set_len(pos0)

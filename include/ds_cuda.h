@@ -306,6 +306,35 @@ int ds_cuda_decoder_set_uniforms(ds_cuda_ctx_t *ctx, int model, const float *u, 
  * [max(P, len - W), len) through the same sequential softmax. 0 disables
  * (full causal attention). Engine 0 only. */
 int ds_cuda_decoder_set_window(ds_cuda_ctx_t *ctx, int model, int sliding_window_size, int prefill_token_count);
+/* The token embedding table the decode loop takes the next input from (the
+ * reference's tok_embeddings_bf16, ds_ocr.c:2272-2279), [vocab x hidden]
+ * BF16 host pointer (registered on first use). Default: the LM head (tied). */
+int ds_cuda_decoder_set_embeddings(ds_cuda_ctx_t *ctx, int model, const uint16_t *embed_tokens);
+
+/* ---------------------------------------------------------------------
+ * Weight ingest from a safetensors checkpoint (the reference's
+ * ds_safetensors.c reader and ds_ocr.c:608-757 decoder loader).
+ * --------------------------------------------------------------------- */
+/* A decoder model from `path`: a directory holding model.safetensors or
+ * model-*.safetensors shards (read in name order), or one file. Tensors are
+ * looked up by the reference's names (model.layers.N.self_attn.q_proj.weight,
+ * ...mlp.experts.E.gate_proj.weight, model.embed_tokens.weight,
+ * lm_head.weight (absent: tied), model.norm.weight, ...), checked against cfg,
+ * copied into HBM once; the expert blocks are assembled on the device, the
+ * INT8 copies (cfg->use_int8) quantised there. Returns a model handle as
+ * ds_cuda_decoder_create; DS_CUDA_EINVAL names a missing or mis-shaped
+ * tensor. The files are unmapped before it returns. */
+int ds_cuda_decoder_create_from_safetensors(ds_cuda_ctx_t *ctx, const char *path,
+                                            const ds_cuda_decoder_config_t *cfg);
+/* Host-only probes of a checkpoint (no device): number of tensors over all
+ * shards (< 0 on a bad file); metadata of one tensor (1 found, 0 absent,
+ * < 0 bad file): dtype as the reference's safetensor_dtype_t (F32 0, F16 1,
+ * BF16 2, I32 3, I64 4, BOOL 5, other -1), dims, and the byte offset and
+ * size within its file's data section. The message of the last failure. */
+int ds_cuda_safetensors_count(const char *path);
+int ds_cuda_safetensors_find(const char *path, const char *name, int *dtype, int *ndim, int64_t *shape8,
+                             size_t *data_offset, size_t *data_size);
+const char *ds_cuda_safetensors_error(void);
 
 /* ---------------------------------------------------------------------
  * Multi-stream decoder — ds_decoder_forward for up to 64 independent

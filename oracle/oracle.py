@@ -153,6 +153,8 @@ def ref():
             "ref_decoder_step_gen": (c_int, [P, P]),
             "ref_srand": (None, [ctypes.c_uint]),
             "ref_ctx_set_window": (None, [P, c_int, c_int]),
+            "ref_st_count": (c_int, [ctypes.c_char_p]),
+            "ref_st_find": (c_int, [ctypes.c_char_p, ctypes.c_char_p, P, P, P, P, P]),
         }
         for k, (res, a) in sig.items():
             f = getattr(r, k)

@@ -13,6 +13,7 @@
  * the way alloc_decoder_buffers (ds_ocr.c:847-961) builds it, with the
  * expert layout of load_all_weights (ds_ocr.c:696-768).
  */
+#include "ds_safetensors.h"
 #include "ds_moe_decoder.c"
 #include "ds_quantize.h"
 #include <cblas.h>
@@ -285,6 +286,36 @@ void ref_ctx_set_window(void *vctx, int sliding_window_size, int prefill_token_c
     ds_ctx_t *ctx = (ds_ctx_t *)vctx;
     ctx->config.sliding_window_size = sliding_window_size;
     ctx->prefill_token_count = prefill_token_count;
+}
+
+/* The reference's safetensors reader (ds_safetensors.c) on a checkpoint
+ * directory: tensor count, and one tensor's metadata (1 found, 0 absent,
+ * -1 the directory did not open). */
+int ref_st_count(const char *dir) {
+    multi_safetensors_t *ms = multi_safetensors_open(dir);
+    if (!ms) return -1;
+    int n = 0;
+    for (int s = 0; s < ms->num_shards; s++) n += ms->shards[s]->num_tensors;
+    multi_safetensors_close(ms);
+    return n;
+}
+
+int ref_st_find(const char *dir, const char *name, int *dtype, int *ndim, int64_t *shape8, size_t *off,
+                size_t *size) {
+    multi_safetensors_t *ms = multi_safetensors_open(dir);
+    if (!ms) return -1;
+    safetensors_file_t *sf = NULL;
+    const safetensor_t *t = multi_safetensors_find(ms, name, &sf);
+    int found = t != NULL;
+    if (t) {
+        *dtype = t->dtype;
+        *ndim = t->ndim;
+        for (int i = 0; i < t->ndim && i < 8; i++) shape8[i] = t->shape[i];
+        *off = t->data_offset;
+        *size = t->data_size;
+    }
+    multi_safetensors_close(ms);
+    return found;
 }
 
 /* Seeds the C library generator that the temperature path draws from. */

@@ -362,13 +362,6 @@ static void dense_ffn(float *out, const float *x, const orc_layer_t *ly, const o
     free(g); free(u); free(h);
 }
 
-/* ds_decoder_forward (ds_moe_decoder.c:911-1264) greedy branch with
- * decoder_layer_forward (:339-474) per layer: input RMSNorm, QKV matvecs,
- * RoPE at `pos`, K/V stored (F32) at row `pos`, attention over pos+1 keys,
- * O-proj, residual + post-attention RMSNorm, dense FFN (layer <
- * first_dense) or MoE, residual add; final RMSNorm; argmax LM head.
- * KV layout [layer][kv_max][H] F32. Returns the token; final_x receives
- * the normed hidden state, logit its LM-head logit. */
 /* Reference sliding-window attention of V3 decode (R-SWA,
  * ds_moe_decoder.c:409-436 -> ds_rswa_attention_aligned,
  * ds_kernels.c:2255-2314): with window W > 0 and the query at or past the
@@ -394,6 +387,13 @@ static void attention_rswa(float *out, const float *q, const float *K, const flo
     free(Vc);
 }
 
+/* ds_decoder_forward (ds_moe_decoder.c:911-1264) greedy branch with
+ * decoder_layer_forward (:339-474) per layer: input RMSNorm, QKV matvecs,
+ * RoPE at `pos`, K/V stored (F32) at row `pos`, attention over pos+1 keys,
+ * O-proj, residual + post-attention RMSNorm, dense FFN (layer <
+ * first_dense) or MoE, residual add; final RMSNorm; argmax LM head.
+ * KV layout [layer][kv_max][H] F32. Returns the token; final_x receives
+ * the normed hidden state, logit its LM-head logit. */
 int orc_decoder_step(const orc_layer_t *layers, const orc_dims_t *d,
                      const float *final_norm, const uint16_t *lm_head,
                      float *kv_k, float *kv_v, int kv_max, int pos,
@@ -606,5 +606,75 @@ int orc_lm_select(const float *xn, const uint16_t *W, int H, int V, const int *h
         }
     }
     free(lg);
+    return tok;
+}
+
+/* ds_decoder_prefill (ds_moe_decoder.c:480-905) for T tokens at positions
+ * pos0 .. pos0+T-1 (no BF16 truncation): per layer input RMSNorm of every
+ * row, Q/K/V GEMMs, RoPE per position, K/V rows stored (F32), causal
+ * attention (ds_causal_attention_heads_aligned, ds_kernels.c:2061-2114: the
+ * decode rule per query over keys 0 .. pos0+t), O-proj GEMM and residual,
+ * then the dense FFN (layer < first_dense: post-attention RMSNorm, gate/up
+ * GEMMs, SwiGLU, down GEMM, residual) or the MoE block (orc_prefill_moe).
+ * The first generated token is the argmax of the LM head on the final
+ * RMSNorm of the last row (:877-891); *logit = its value, last_x = that
+ * normed row. Returns the token. */
+int orc_decoder_prefill(const orc_layer_t *layers, const orc_dims_t *d, const float *final_norm,
+                        const uint16_t *lm_head, float *kv_k, float *kv_v, int kv_max, int pos0,
+                        const float *cos_t, const float *sin_t, const float *embeds, int T, float *last_x,
+                        float *logit) {
+    int H = d->hidden, hd = d->head_dim, nh = d->n_heads, qd = nh * hd, D = d->inter_dense;
+    float *x = (float *)malloc((size_t)T * H * sizeof(float));
+    float *xn = (float *)malloc((size_t)T * H * sizeof(float));
+    float *Q = (float *)malloc((size_t)T * qd * sizeof(float));
+    float *K = (float *)malloc((size_t)T * qd * sizeof(float));
+    float *V = (float *)malloc((size_t)T * qd * sizeof(float));
+    float *att = (float *)malloc((size_t)T * qd * sizeof(float));
+    float *proj = (float *)malloc((size_t)T * H * sizeof(float));
+    memcpy(x, embeds, (size_t)T * H * sizeof(float));
+    float scale = 1.0f / sqrtf((float)hd);
+    for (int l = 0; l < d->n_layers; l++) {
+        const orc_layer_t *ly = &layers[l];
+        for (int t = 0; t < T; t++) orc_rms_norm(xn + (size_t)t * H, x + (size_t)t * H, ly->input_norm, H, d->eps);
+        gemm_bf16(Q, xn, ly->wq, T, H, qd);
+        gemm_bf16(K, xn, ly->wk, T, H, qd);
+        gemm_bf16(V, xn, ly->wv, T, H, qd);
+        float *Kl = kv_k + (size_t)l * kv_max * qd;
+        float *Vl = kv_v + (size_t)l * kv_max * qd;
+        for (int t = 0; t < T; t++) {
+            int p = pos0 + t;
+            orc_apply_rope(Q + (size_t)t * qd, cos_t + (size_t)p * hd, sin_t + (size_t)p * hd, nh, hd);
+            orc_apply_rope(K + (size_t)t * qd, cos_t + (size_t)p * hd, sin_t + (size_t)p * hd, nh, hd);
+            memcpy(Kl + (size_t)p * qd, K + (size_t)t * qd, (size_t)qd * sizeof(float));
+            memcpy(Vl + (size_t)p * qd, V + (size_t)t * qd, (size_t)qd * sizeof(float));
+        }
+#pragma omp parallel for schedule(dynamic, 4)
+        for (int t = 0; t < T; t++)
+            orc_attention_decode(att + (size_t)t * qd, Q + (size_t)t * qd, Kl, Vl, pos0 + t + 1, nh, hd, qd, scale);
+        gemm_bf16(proj, att, ly->wo, T, qd, H);
+        for (size_t i = 0; i < (size_t)T * H; i++) x[i] += proj[i];
+        if (l < d->first_dense) {
+            float *g = (float *)malloc((size_t)T * D * sizeof(float));
+            float *u = (float *)malloc((size_t)T * D * sizeof(float));
+            float *mo = (float *)malloc((size_t)T * H * sizeof(float));
+            for (int t = 0; t < T; t++)
+                orc_rms_norm(xn + (size_t)t * H, x + (size_t)t * H, ly->post_norm, H, d->eps);
+            gemm_bf16(g, xn, ly->dense_gate, T, H, D);
+            gemm_bf16(u, xn, ly->dense_up, T, H, D);
+            for (int t = 0; t < T; t++) orc_swiglu(g + (size_t)t * D, g + (size_t)t * D, u + (size_t)t * D, D);
+            gemm_bf16(mo, g, ly->dense_down, T, D, H);
+            for (size_t i = 0; i < (size_t)T * H; i++) x[i] += mo[i];
+            free(g); free(u); free(mo);
+        } else {
+            orc_prefill_moe(ly, d, x, T, NULL, NULL, NULL);
+        }
+    }
+    float *lx = (float *)malloc((size_t)H * sizeof(float));
+    orc_rms_norm(lx, x + (size_t)(T - 1) * H, final_norm, H, d->eps);
+    float val;
+    int tok = orc_argmax_bf16(lx, lm_head, H, d->vocab, &val);
+    if (last_x) memcpy(last_x, lx, (size_t)H * sizeof(float));
+    if (logit) *logit = val;
+    free(lx); free(x); free(xn); free(Q); free(K); free(V); free(att); free(proj);
     return tok;
 }

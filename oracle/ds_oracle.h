@@ -80,6 +80,10 @@ int orc_decoder_step(const orc_layer_t *layers, const orc_dims_t *d,
                      float *kv_k, float *kv_v, int kv_max, int pos,
                      const float *cos_t, const float *sin_t, int use_int8,
                      const float *embed, float *final_x, float *logit);
+int orc_decoder_prefill(const orc_layer_t *layers, const orc_dims_t *d, const float *final_norm,
+                        const uint16_t *lm_head, float *kv_k, float *kv_v, int kv_max, int pos0,
+                        const float *cos_t, const float *sin_t, const float *embeds, int T, float *last_x,
+                        float *logit);
 int orc_lm_select(const float *xn, const uint16_t *W, int H, int V, const int *hist, int len, float rp,
                   int ngram, float temperature, float r, float *val, int *full);
 /* orc_decoder_step with V3's reference sliding-window attention: window

@@ -101,6 +101,7 @@ def oracle():
             "orc_decoder_step": (c_int, [P, P, P, P, P, P, c_int, c_int, P, P, c_int, P, P, P]),
             "orc_prefill_moe": (None, [P, P, P, c_int, P, P, P]),
             "orc_decoder_step_swa": (c_int, [P, P, P, P, P, P, c_int, c_int, P, P, c_int, P, P, P, c_int, c_int]),
+            "orc_decoder_prefill": (c_int, [P, P, P, P, P, P, c_int, c_int, P, P, P, c_int, P, P]),
             "orc_lm_select": (c_int, [P, P, c_int, c_int, P, c_int, c_float, c_int, c_float, c_float, P, P]),
         }
         for k, (r, a) in sig.items():
@@ -153,6 +154,7 @@ def ref():
             "ref_decoder_step_gen": (c_int, [P, P]),
             "ref_srand": (None, [ctypes.c_uint]),
             "ref_ctx_set_window": (None, [P, c_int, c_int]),
+            "ref_decoder_prefill": (c_int, [P, P, c_int, P]),
             "ref_st_count": (c_int, [ctypes.c_char_p]),
             "ref_st_find": (c_int, [ctypes.c_char_p, ctypes.c_char_p, P, P, P, P, P]),
         }
@@ -214,6 +216,20 @@ class RefDecoder:
         out = np.empty(self.r.ref_ctx_get_history(self.ctx, None, 0), np.int32)
         self.r.ref_ctx_get_history(self.ctx, addr(out), out.size)
         return out
+
+    def prefill(self, embeds):
+        """ds_decoder_prefill on [T x hidden] embeddings: (first token, logit)."""
+        e = np.ascontiguousarray(embeds, np.float32)
+        lg = np.empty(1, np.float32)
+        tok = self.r.ref_decoder_prefill(self.ctx, addr(e), e.shape[0], addr(lg))
+        return tok, float(lg[0])
+
+    def kv(self, layer, pos0, n):
+        kd = self.model.d.n_heads * self.model.d.head_dim
+        k = np.empty((n, kd), np.float32)
+        v = np.empty((n, kd), np.float32)
+        self.r.ref_ctx_kv_get(self.ctx, layer, pos0, n, addr(k), addr(v))
+        return k, v
 
     def set_window(self, sliding_window_size, prefill_token_count):
         """V3's reference sliding-window attention (ds_moe_decoder.c:409-436)."""
@@ -312,6 +328,19 @@ class OracleDecoder:
                                           addr(fx), addr(lg), self.window, self.ref_len)
         self.pos += 1
         return tok, fx, float(lg[0])
+
+    def prefill(self, embeds):
+        """The oracle's ds_decoder_prefill on [T x hidden] embeddings at the
+        current position: (first token, last normed row, logit)."""
+        d = self.model.d
+        e = np.ascontiguousarray(embeds, np.float32)
+        lx = np.empty(d.hidden, np.float32)
+        lg = np.empty(1, np.float32)
+        tok = self.o.orc_decoder_prefill(self.layers, ctypes.byref(self.dims), addr(self.model.final_norm),
+                                         addr(self.model.lm_head), addr(self.k), addr(self.v), self.kv_max, self.pos,
+                                         addr(self.cos), addr(self.sin), addr(e), e.shape[0], addr(lx), addr(lg))
+        self.pos += e.shape[0]
+        return tok, lx, float(lg[0])
 
     def select(self, final_x, history, repeat_penalty=1.0, no_repeat_ngram_size=0, temperature=0.0, r=0.0):
         """LM-head selection with the sampling settings on a final hidden state:

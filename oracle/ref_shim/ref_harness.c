@@ -318,6 +318,22 @@ int ref_st_find(const char *dir, const char *name, int *dtype, int *ndim, int64_
     return found;
 }
 
+/* ds_decoder_prefill (ds_moe_decoder.c:480-905) on T input embeddings at
+ * the current cache length; returns the first generated token, the strict
+ * '>' argmax of the logits it leaves in ctx->dec_logits (the generation
+ * loop's pick, ds_ocr.c), and its logit. */
+int ref_decoder_prefill(void *vctx, const float *embeds, int T, float *logit) {
+    ds_ctx_t *ctx = (ds_ctx_t *)vctx;
+    ds_decoder_prefill(ctx, embeds, T);
+    const float *lg = ctx->dec_logits;
+    int tok = 0;
+    float best = lg[0];
+    for (int i = 1; i < ctx->config.vocab_size; i++)
+        if (lg[i] > best) { best = lg[i]; tok = i; }
+    if (logit) *logit = best;
+    return tok;
+}
+
 /* Seeds the C library generator that the temperature path draws from. */
 void ref_srand(unsigned seed) { srand(seed); }
 

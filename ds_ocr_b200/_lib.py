@@ -59,6 +59,9 @@ SIGNATURES = {
     "ds_cuda_decoder_set_uniforms": (c_int, [P, c_int, P, c_int]),
     "ds_cuda_decoder_set_window": (c_int, [P, c_int, c_int, c_int]),
     "ds_cuda_decoder_set_embeddings": (c_int, [P, c_int, P]),
+    "ds_cuda_decoder_prefill": (c_int, [P, c_int, P, c_int, P, P]),
+    "ds_cuda_decoder_prefill_dev": (c_int, [P, c_int, P, c_int, P]),
+    "ds_cuda_decoder_get_kv": (c_int, [P, c_int, c_int, c_int, c_int, P, P]),
     "ds_cuda_decoder_create_from_safetensors": (c_int, [P, ctypes.c_char_p, P]),
     "ds_cuda_safetensors_count": (c_int, [ctypes.c_char_p]),
     "ds_cuda_safetensors_find": (c_int, [ctypes.c_char_p, ctypes.c_char_p, P, P, P, P, P]),

@@ -9,6 +9,7 @@
 #include "ctx.h"
 #include "kernels_decode.cuh"
 #include "mega.h"
+#include "prefill.h"
 
 using namespace ds;
 
@@ -63,6 +64,15 @@ struct DecoderModel {
     bool sampling() const { return rp > 1.f || ngram > 0 || temperature > 0.f; }
     // V3's reference sliding-window attention: window, prefill length
     int swa_window = 0, swa_ref = 0;
+    // whole-decoder prefill: fused [wq; wk; wv] per layer and the dense
+    // layers' gate/up and down with the width padded to a multiple of 128
+    // (built on first use), and a workspace for pf_cap tokens
+    std::vector<uint16_t *> pf_wqkv, pf_dgu, pf_ddown;
+    int pf_dpad = 0;
+    int pf_cap = 0;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_y = nullptr;
+    uint16_t *pf_ahi = nullptr, *pf_alo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
+    int *pf_pos = nullptr, *pf_lo = nullptr;
     std::vector<void *> allocs;
 
     size_t plane_elems() const {
@@ -82,6 +92,11 @@ static void drop_graphs(DecoderModel *m) {
 
 static void free_model(DecoderModel *m) {
     drop_graphs(m);
+    for (auto *v : {&m->pf_wqkv, &m->pf_dgu, &m->pf_ddown})
+        for (uint16_t *p : *v) cudaFree(p);
+    void *ws[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo,
+                  m->pf_pos, m->pf_lo};
+    for (void *p : ws) cudaFree(p);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
 }
@@ -867,5 +882,222 @@ extern "C" int ds_cuda_decoder_set_embeddings(ds_cuda_ctx_t *c, int id, const ui
     CKL(cudaStreamSynchronize(c->stream), "set embeddings");
     m->embed = (const uint16_t *)d;
     drop_graphs(m);
+    return DS_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Whole-decoder prefill (ds_decoder_prefill, ds_moe_decoder.c:480-905): T
+// input embeddings at positions len .. len+T-1 through every layer, their
+// K/V rows written to this model's cache, and the first generated token
+// (LM-head argmax of the last row's final RMSNorm). Per layer: input
+// RMSNorm split into BF16 planes; the QKV projection as one tensor-core GEMM
+// against [wq; wk; wv]; RoPE and the cache writes; the exact decode
+// attention with one query per token over keys 0 .. len+t; the O-projection
+// GEMM and residual; then the MoE prefill block, or for a dense layer the
+// gate/up GEMM with SwiGLU in its epilogue and the down GEMM, and residual.
+// ---------------------------------------------------------------------------
+static int pf_weights(ds_cuda_ctx *c, DecoderModel *m) {
+    if (!m->pf_wqkv.empty()) return DS_CUDA_OK;
+    const auto &g = m->cfg;
+    const size_t H = g.hidden, QD = (size_t)g.n_heads * g.head_dim, D = g.dense_inter;
+    m->pf_dpad = (int)((D + 127) / 128 * 128);
+    const size_t Dp = m->pf_dpad;
+    cudaStream_t st = c->stream;
+    for (int l = 0; l < g.n_layers; l++) {
+        const DecLayer &L = m->layers[l];
+        uint16_t *w = nullptr;
+        CKL(cudaMalloc(&w, 3 * QD * H * 2), "prefill qkv weights");
+        m->pf_wqkv.push_back(w);
+        CKL(cudaMemcpyAsync(w, L.wq, QD * H * 2, cudaMemcpyDeviceToDevice, st), "qkv copy");
+        CKL(cudaMemcpyAsync(w + QD * H, L.wk, QD * H * 2, cudaMemcpyDeviceToDevice, st), "qkv copy");
+        CKL(cudaMemcpyAsync(w + 2 * QD * H, L.wv, QD * H * 2, cudaMemcpyDeviceToDevice, st), "qkv copy");
+        uint16_t *gu = nullptr, *dn = nullptr;
+        if (L.dense) {
+            CKL(cudaMalloc(&gu, 2 * Dp * H * 2), "prefill dense weights");
+            CKL(cudaMalloc(&dn, H * Dp * 2), "prefill dense weights");
+            CKL(cudaMemsetAsync(gu, 0, 2 * Dp * H * 2, st), "dense pad");
+            CKL(cudaMemsetAsync(dn, 0, H * Dp * 2, st), "dense pad");
+            CKL(cudaMemcpyAsync(gu, L.dgate, D * H * 2, cudaMemcpyDeviceToDevice, st), "dense copy");
+            CKL(cudaMemcpyAsync(gu + Dp * H, L.dup, D * H * 2, cudaMemcpyDeviceToDevice, st), "dense copy");
+            CKL(cudaMemcpy2DAsync(dn, Dp * 2, L.ddown, D * 2, D * 2, H, cudaMemcpyDeviceToDevice, st), "dense copy");
+        }
+        m->pf_dgu.push_back(gu);
+        m->pf_ddown.push_back(dn);
+    }
+    return DS_CUDA_OK;
+}
+
+static int pf_workspace(ds_cuda_ctx *c, DecoderModel *m, int T) {
+    if (T <= m->pf_cap) return DS_CUDA_OK;
+    void *old[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo,
+                   m->pf_pos, m->pf_lo};
+    CKL(cudaStreamSynchronize(c->stream), "prefill workspace");
+    for (void *p : old) cudaFree(p);
+    const auto &g = m->cfg;
+    const size_t n = (size_t)T, H = g.hidden, QD = (size_t)g.n_heads * g.head_dim, Dp = m->pf_dpad;
+    const size_t A = std::max(H, QD);
+    cudaError_t e = cudaMalloc(&m->pf_x, n * H * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_qkv, n * 3 * QD * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_q, n * QD * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_att, n * QD * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_y, n * H * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_ahi, n * A * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_alo, n * A * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_hhi, n * std::max<size_t>(Dp, 1) * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_hlo, n * std::max<size_t>(Dp, 1) * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_pos, n * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_lo, n * 4);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        m->pf_cap = 0;
+        return ctx_fail(c, DS_CUDA_ENOMEM, "decoder_prefill: workspace for %d tokens", T);
+    }
+    m->pf_cap = T;
+    return DS_CUDA_OK;
+}
+
+static int prefill_enqueue(ds_cuda_ctx *c, DecoderModel *m, const float *d_embeds, int T, cudaStream_t st) {
+    const auto &g = m->cfg;
+    const int H = g.hidden, NH = g.n_heads, HD = g.head_dim, QD = NH * HD;
+    if (c->simulate)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_prefill: the BF16-truncation numerics mode is decode-only");
+    if (H % 256 || QD % 256 || g.moe_inter % 128 || (g.n_shared * g.moe_inter) % 128)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_prefill: unsupported shape");
+    for (const DecLayer &L : m->layers)
+        if (!L.dense && (!L.block || !L.down || !L.router || (g.n_shared && !L.sdown)))
+            return ctx_fail(c, DS_CUDA_EINVAL, "decoder_prefill: needs the BF16 expert weights (INT8-only model)");
+    CK(pf_weights(c, m));
+    CK(pf_workspace(c, m, T));
+    const int p0 = m->host_len;
+    const PfShape shape{H, g.moe_inter, g.n_shared * g.moe_inter, g.n_experts, g.top_k, g.rms_eps};
+    CKL(cudaMemcpyAsync(m->pf_x, d_embeds, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st), "prefill input");
+    bool lo_changed = false;
+    for (int l = 0; l < g.n_layers; l++) {
+        const DecLayer &L = m->layers[l];
+        CKL(launch_pd_split(m->pf_x, T, H, L.in_norm, g.rms_eps, m->pf_ahi, m->pf_alo, st), "prefill norm");
+        CK(pf_dense_gemm(c, 1, m->pf_ahi, m->pf_alo, T, H, m->pf_wqkv[l], 3 * QD, m->pf_qkv, 3 * QD, nullptr, nullptr,
+                         st));
+        CKL(launch_pd_rope_kv(m->pf_qkv, T, NH, HD, p0, m->cos_t, m->sin_t, m->pf_q, m->plane(0, l), m->plane(1, l),
+                              m->plane(2, l), m->plane(3, l), g.kv_max, st),
+            "prefill rope");
+        // the new rows carry lo planes: lo starts at p0 at the latest
+        if (m->lo_start[l] > p0) {
+            m->lo_start[l] = p0;
+            lo_changed = true;
+        }
+        CKL(launch_pd_positions(m->pf_pos, m->pf_lo, T, p0, m->lo_start[l], st), "prefill positions");
+        AttnArgs aa = {};
+        aa.q = m->pf_q;
+        aa.k_hi = m->plane(0, l);
+        aa.k_lo = m->plane(1, l);
+        aa.v_hi = m->plane(2, l);
+        aa.v_lo = m->plane(3, l);
+        aa.kv_max = g.kv_max;
+        aa.n_heads = NH;
+        aa.d_pos = m->pf_pos;
+        aa.lo_start = m->lo_start[l];
+        aa.lo_starts = m->pf_lo;
+        aa.scale = 1.0f / sqrtf((float)HD);
+        aa.out = m->pf_att;
+        aa.kv_stream_stride = 0;  // every query reads the same cache
+        aa.q_stride = QD;
+        CKL(launch_attn_decode(aa, st, false, T), "prefill attention");
+        CKL(launch_pd_split(m->pf_att, T, QD, nullptr, 0.f, m->pf_ahi, m->pf_alo, st), "prefill split");
+        CK(pf_dense_gemm(c, 1, m->pf_ahi, m->pf_alo, T, QD, L.wo, H, m->pf_y, H, nullptr, nullptr, st));
+        CKL(launch_pd_add(m->pf_x, m->pf_y, (size_t)T * H, st), "prefill residual");
+        if (L.dense) {
+            const int Dp = m->pf_dpad;
+            CKL(launch_pd_split(m->pf_x, T, H, L.post_norm, g.rms_eps, m->pf_ahi, m->pf_alo, st), "prefill norm");
+            CK(pf_dense_gemm(c, 0, m->pf_ahi, m->pf_alo, T, H, m->pf_dgu[l], Dp, nullptr, 0, m->pf_hhi, m->pf_hlo,
+                             st));
+            CK(pf_dense_gemm(c, 1, m->pf_hhi, m->pf_hlo, T, Dp, m->pf_ddown[l], H, m->pf_y, H, nullptr, nullptr, st));
+            CKL(launch_pd_add(m->pf_x, m->pf_y, (size_t)T * H, st), "prefill residual");
+        } else {
+            CK(prefill_moe_enqueue(c, shape, L.post_norm, L.router, L.block, L.down, L.sdown, m->pf_x, T, nullptr,
+                                   nullptr, nullptr, st));
+        }
+    }
+    if (lo_changed) drop_graphs(m);  // the decode graph bakes lo_start in
+    const float *last = m->pf_x + (size_t)(T - 1) * H;
+    CKL(launch_argmax_bf16(m->lm_head, last, g.vocab, H, m->slot, m->tickets + 0, m->tok, m->val, st, false,
+                           m->final_norm, g.rms_eps),
+        "prefill lm head");
+    CKL(launch_rmsnorm(last, m->final_norm, m->xfinal, H, g.rms_eps, st, false), "prefill final norm");
+    CKL(launch_pd_finish(m->embed, H, m->tok, m->xa, m->pos, p0 + T, m->tok_log, m->hist, m->hist_len,
+                         m->hist_cap, st),
+        "prefill finish");
+    m->host_len = p0 + T;
+    m->xa_staged = true;
+    return DS_CUDA_OK;
+}
+
+// d_embeds [n_tokens x hidden] F32 in device memory; enqueued on `stream`
+// (NULL: the context's); the first token stays on the device (read it with
+// ds_cuda_decoder_generate or the next forward's history).
+extern "C" int ds_cuda_decoder_prefill_dev(ds_cuda_ctx_t *c, int id, const float *d_embeds, int n_tokens,
+                                           void *stream) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || !d_embeds || n_tokens <= 0) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_prefill: bad argument");
+    if (m->host_len + n_tokens > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_prefill: KV cache full");
+    cudaSetDevice(c->device);
+    return prefill_enqueue(c, m, d_embeds, n_tokens, stream ? (cudaStream_t)stream : c->stream);
+}
+
+// Host embeddings [n_tokens x hidden]; returns the first generated token;
+// final_x (optional) the last row's final RMS-normed state, logit its LM-head
+// logit. The next forward/generate continues from position len + n_tokens
+// with the first token's embedding already staged.
+extern "C" int ds_cuda_decoder_prefill(ds_cuda_ctx_t *c, int id, const float *embeds, int n_tokens, float *final_x,
+                                       float *logit) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || !embeds || n_tokens <= 0) return ctx_fail(c, DS_CUDA_EINVAL, "decoder_prefill: bad argument");
+    if (m->host_len + n_tokens > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_prefill: KV cache full");
+    cudaSetDevice(c->device);
+    const size_t H = m->cfg.hidden, bytes = (size_t)n_tokens * H * 4;
+    float *d = nullptr;
+    CKL(cudaMalloc(&d, bytes), "prefill input");
+    int rc = ctx_cuda(c, cudaMemcpyAsync(d, embeds, bytes, cudaMemcpyHostToDevice, c->stream), "prefill input");
+    if (rc == DS_CUDA_OK) rc = prefill_enqueue(c, m, d, n_tokens, c->stream);
+    int tok = 0;
+    float val = 0.f;
+    if (rc == DS_CUDA_OK) rc = ctx_cuda(c, cudaMemcpyAsync(&tok, m->tok, 4, cudaMemcpyDeviceToHost, c->stream), "token");
+    if (rc == DS_CUDA_OK) rc = ctx_cuda(c, cudaMemcpyAsync(&val, m->val, 4, cudaMemcpyDeviceToHost, c->stream), "logit");
+    if (rc == DS_CUDA_OK && final_x)
+        rc = ctx_cuda(c, cudaMemcpyAsync(final_x, m->xfinal, H * 4, cudaMemcpyDeviceToHost, c->stream), "final x");
+    if (rc == DS_CUDA_OK) rc = ctx_cuda(c, cudaStreamSynchronize(c->stream), "decoder_prefill");
+    if (rc == DS_CUDA_OK) rc = prefill_check_flag(c);
+    cudaFree(d);
+    if (rc < 0) return rc;
+    if (logit) *logit = val;
+    return tok;
+}
+
+// The cache rows [pos0, pos0+n) of one layer as F32 [n x heads*head_dim]
+// (hi + lo planes), the layout ds_cuda_decoder_load_kv takes.
+extern "C" int ds_cuda_decoder_get_kv(ds_cuda_ctx_t *c, int id, int layer, int pos0, int n, float *k, float *v) {
+    DecoderModel *m = c ? get_model(c, id) : nullptr;
+    if (!m || layer < 0 || layer >= m->cfg.n_layers || pos0 < 0 || n <= 0 || pos0 + n > m->cfg.kv_max || !k || !v)
+        return ctx_fail(c, DS_CUDA_EINVAL, "decoder_get_kv: bad argument");
+    cudaSetDevice(c->device);
+    CKL(cudaStreamSynchronize(c->stream), "get kv");
+    const int NH = m->cfg.n_heads, HD = m->cfg.head_dim, QD = NH * HD;
+    std::vector<uint16_t> hi((size_t)n * HD), lo((size_t)n * HD);
+    for (int which = 0; which < 2; which++) {
+        float *out = which ? v : k;
+        for (int h = 0; h < NH; h++) {
+            const size_t off = ((size_t)h * m->cfg.kv_max + pos0) * HD;
+            CKL(cudaMemcpy(hi.data(), m->plane(2 * which, layer) + off, hi.size() * 2, cudaMemcpyDeviceToHost), "kv");
+            CKL(cudaMemcpy(lo.data(), m->plane(2 * which + 1, layer) + off, lo.size() * 2, cudaMemcpyDeviceToHost),
+                "kv");
+            for (int i = 0; i < n; i++)
+                for (int d = 0; d < HD; d++) {
+                    const uint32_t a = (uint32_t)hi[(size_t)i * HD + d] << 16, b = (uint32_t)lo[(size_t)i * HD + d] << 16;
+                    float fa, fb;
+                    memcpy(&fa, &a, 4);
+                    memcpy(&fb, &b, 4);
+                    out[(size_t)i * QD + h * HD + d] = fa + fb;
+                }
+        }
+    }
     return DS_CUDA_OK;
 }

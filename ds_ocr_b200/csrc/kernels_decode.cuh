@@ -72,6 +72,17 @@ cudaError_t launch_decode_advance(const uint16_t *E, int hidden, const int *d_to
                                   float *x_out, cudaStream_t st, bool pdl, int *hist = nullptr, int *hist_len = nullptr,
                                   int hist_cap = 0);
 
+// Whole-decoder prefill kernels (prefill_full.cu).
+cudaError_t launch_pd_split(const float *x, int M, int H, const float *nw, float eps, uint16_t *hi, uint16_t *lo,
+                            cudaStream_t st);
+cudaError_t launch_pd_rope_kv(const float *qkv, int T, int NH, int HD, int p0, const float *cos_t, const float *sin_t,
+                              float *q, uint16_t *k_hi, uint16_t *k_lo, uint16_t *v_hi, uint16_t *v_lo, int kv_max,
+                              cudaStream_t st);
+cudaError_t launch_pd_add(float *x, const float *y, size_t n, cudaStream_t st);
+cudaError_t launch_pd_positions(int *pos, int *lo_starts, int T, int p0, int lo_start, cudaStream_t st);
+cudaError_t launch_pd_finish(const uint16_t *E, int H, const int *tok, float *x_out, int *pos, int p_next,
+                             int *tok_log, int *hist, int *hist_len, int hist_cap, cudaStream_t st);
+
 // LM-head token selection with the sampling settings (select.cu).
 struct SelectArgs {
     const uint16_t *W;   // LM head [V x H]

@@ -31,12 +31,14 @@
 //     accumulation order) and adds the shared expert and the residual.
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <vector>
 #include <cuda.h>
 #include "ctx.h"
 #include "umma.cuh"
 #include "tmap.h"
 #include "route.cuh"
+#include "prefill.h"
 
 namespace ds {
 
@@ -463,6 +465,10 @@ struct PfWork {
     PfTile *gu_tiles = nullptr, *dn_tiles = nullptr;
     size_t c_xn_hi = 0, c_xn_lo = 0, c_xg_hi = 0, c_xg_lo = 0, c_hg_hi = 0, c_hg_lo = 0, c_hs_hi = 0, c_hs_lo = 0;
     size_t c_yr = 0, c_ys = 0, c_logits = 0, c_wt = 0, c_idx = 0, c_slot = 0, c_gu = 0, c_dn = 0;
+    // dense GEMMs of the whole-decoder prefill (tile list and its count)
+    PfTile *dense_tiles = nullptr;
+    size_t c_dense = 0;
+    int *dense_nt = nullptr;
     // fixed
     int *counts = nullptr, *seg = nullptr, *cursor = nullptr, *nt = nullptr;
     unsigned *err = nullptr;  // set by a device-side wait that gave up
@@ -473,7 +479,7 @@ void prefill_release(ds_cuda_ctx *c) {
     if (!w) return;
     void *ptrs[] = {w->xn_hi, w->xn_lo, w->xg_hi, w->xg_lo, w->hg_hi, w->hg_lo, w->hs_hi, w->hs_lo, w->yr,
                     w->ys, w->logits, w->wt, w->idx, w->slot_of, w->gu_tiles, w->dn_tiles, w->counts, w->seg,
-                    w->cursor, w->nt, w->err};
+                    w->cursor, w->nt, w->err, w->dense_tiles, w->dense_nt};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     delete w;
@@ -490,6 +496,7 @@ static int pf_work(ds_cuda_ctx *c, cudaStream_t st, PfWork **out) {
         if (e == cudaSuccess) e = cudaMalloc(&w->cursor, PF_MAXE * 4);
         if (e == cudaSuccess) e = cudaMalloc(&w->nt, 2 * 4);
         if (e == cudaSuccess) e = cudaMalloc(&w->err, 4);
+        if (e == cudaSuccess) e = cudaMalloc(&w->dense_nt, 4);
         // stream-ordered with the kernels (the context's stream does not
         // synchronise with the legacy default stream)
         if (e == cudaSuccess) e = cudaMemsetAsync(w->counts, 0, PF_MAXE * 4, st);
@@ -508,11 +515,6 @@ static int pf_work(ds_cuda_ctx *c, cudaStream_t st, PfWork **out) {
         int _rc = ctx_grow(c, (void **)&(ptr), &(cap), (bytes));                          \
         if (_rc < 0) return _rc;                                                          \
     } while (0)
-
-struct PfShape {
-    int H, I, S, E, K;
-    float eps;
-};
 
 static int pf_shape_ok(ds_cuda_ctx *c, const PfShape &g) {
     if (g.H % 256 || g.H > 2048 || g.I % 128 || g.I <= 0 || g.S % 128 || g.E <= 0 || g.E > PF_MAXE || g.K <= 0 ||
@@ -670,6 +672,66 @@ int prefill_moe_enqueue(ds_cuda_ctx *c, const PfShape &g, const float *d_norm, c
     return DS_CUDA_OK;
 }
 
+// A dense split-BF16 GEMM on the same kernel, for the whole-decoder prefill:
+// every tile is a "shared" (kind 1) tile over all M rows.
+//   mode 1: y [M x N] (row stride y_ld) = A [M x K] . B [N x K]^T, N % 256 == 0
+//   mode 0: B = [gate rows (N); up rows (N)] (N % 128 == 0); writes
+//           SwiGLU(A.gate^T, A.up^T) as BF16 planes h_hi/h_lo [M x N]
+// A = planes a_hi/a_lo [M x K], K % 64 == 0.
+int pf_dense_gemm(ds_cuda_ctx *c, int mode, const uint16_t *a_hi, const uint16_t *a_lo, int M, int K,
+                  const uint16_t *B, int N, float *y, int y_ld, uint16_t *h_hi, uint16_t *h_lo, cudaStream_t st) {
+    if (M <= 0) return DS_CUDA_OK;
+    if (K % PF_BK || (mode == 1 && N % PF_BN) || (mode == 0 && N % 128))
+        return ctx_fail(c, DS_CUDA_EINVAL, "prefill: dense GEMM shape not tileable");
+    PfWork *w;
+    int rc = pf_work(c, st, &w);
+    if (rc < 0) return rc;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(pf_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+        cudaFuncSetAttribute(pf_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+        attr = true;
+    }
+    const int mt = (M + PF_BM - 1) / PF_BM, bn = mode == 1 ? PF_BN : 128, nt = N / bn;
+    std::vector<PfTile> tiles;
+    tiles.reserve((size_t)mt * nt);
+    // n-major within a row block: consecutive CTAs share the A tile in L2
+    for (int m = 0; m < mt; m++)
+        for (int n = 0; n < nt; n++) tiles.push_back(PfTile{1, 0, m * PF_BM, std::min(PF_BM, M - m * PF_BM), n * bn});
+    PF_GROW(w->dense_tiles, w->c_dense, tiles.size() * sizeof(PfTile));
+    const int ntiles = (int)tiles.size();
+    // pageable sources: staged before the calls return; stream-ordered
+    // after any earlier GEMM that read the same list
+    cudaError_t e = cudaMemcpyAsync(w->dense_tiles, tiles.data(), tiles.size() * sizeof(PfTile),
+                                    cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w->dense_nt, &ntiles, 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return ctx_cuda(c, e, "prefill: tile list");
+    PfGemm g;
+    memset(&g, 0, sizeof g);
+    bool ok = tmap_bf16(&g.a_hi[1], a_hi, K, M, PF_BM) && tmap_bf16(&g.a_lo[1], a_lo, K, M, PF_BM) &&
+              tmap_bf16(&g.b[1], B, K, mode == 1 ? (uint64_t)N : 2 * (uint64_t)N, mode == 1 ? PF_BN : 128);
+    // kind 0 is unused: point its maps at the same tensors
+    g.a_hi[0] = g.a_hi[1];
+    g.a_lo[0] = g.a_lo[1];
+    g.b[0] = g.b[1];
+    if (!ok) return ctx_fail(c, DS_CUDA_ECUDA, "prefill: tensor map encoding failed");
+    g.tiles = w->dense_tiles;
+    g.n_tiles = w->dense_nt;
+    g.k_blocks[0] = g.k_blocks[1] = K / PF_BK;
+    g.b_half[1] = N;
+    g.h_hi[1] = h_hi;
+    g.h_lo[1] = h_lo;
+    g.h_ld[1] = N;
+    g.y[1] = y;
+    g.y_ld = y_ld;
+    g.err = w->err;
+    const int grid = std::min(c->sm_count, ntiles);
+    if (mode == 0) pf_gemm_kernel<0><<<grid, PF_THREADS, PF_SMEM, st>>>(g);
+    else pf_gemm_kernel<1><<<grid, PF_THREADS, PF_SMEM, st>>>(g);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? DS_CUDA_OK : ctx_cuda(c, e, "prefill: dense GEMM launch");
+}
+
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
@@ -705,6 +767,8 @@ static int pf_check(ds_cuda_ctx *c) {
     }
     return DS_CUDA_OK;
 }
+
+int prefill_check_flag(ds_cuda_ctx *c) { return pf_check(c); }
 
 static cudaStream_t pf_stream(ds_cuda_ctx *c, void *s) { return s ? (cudaStream_t)s : c->stream; }
 

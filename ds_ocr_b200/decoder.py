@@ -138,6 +138,29 @@ class Decoder:
     def set_len(self, n):
         self.ctx.check(self.lib.ds_cuda_decoder_set_len(self.ctx.h, self.id, n), "decoder_set_len")
 
+    def prefill(self, embeds, want_x=False):
+        """ds_decoder_prefill on [T x hidden] embeddings at the current
+        position: the first generated token (and the last row's final
+        normed state and logit with want_x)."""
+        e = np.ascontiguousarray(embeds, np.float32)
+        fx = np.empty(self.model.d.hidden, np.float32) if want_x else None
+        lg = np.empty(1, np.float32)
+        tok = self.ctx.check(self.lib.ds_cuda_decoder_prefill(self.ctx.h, self.id, _a(e), e.shape[0], _a(fx), _a(lg)),
+                             "decoder_prefill")
+        return (tok, fx, float(lg[0])) if want_x else tok
+
+    def prefill_dev(self, d_embeds, n_tokens, stream=None):
+        self.ctx.check(self.lib.ds_cuda_decoder_prefill_dev(self.ctx.h, self.id, d_embeds, n_tokens, stream),
+                       "decoder_prefill_dev")
+
+    def kv(self, layer, pos0, n):
+        kd = self.model.d.n_heads * self.model.d.head_dim
+        k = np.empty((n, kd), np.float32)
+        v = np.empty((n, kd), np.float32)
+        self.ctx.check(self.lib.ds_cuda_decoder_get_kv(self.ctx.h, self.id, layer, pos0, n, _a(k), _a(v)),
+                       "decoder_get_kv")
+        return k, v
+
     @property
     def length(self):
         return self.ctx.check(self.lib.ds_cuda_decoder_get_len(self.ctx.h, self.id), "decoder_get_len")

@@ -311,6 +311,24 @@ int ds_cuda_decoder_set_window(ds_cuda_ctx_t *ctx, int model, int sliding_window
  * BF16 host pointer (registered on first use). Default: the LM head (tied). */
 int ds_cuda_decoder_set_embeddings(ds_cuda_ctx_t *ctx, int model, const uint16_t *embed_tokens);
 
+/* Whole-decoder prefill, ds_decoder_prefill (ds_moe_decoder.c:480-905):
+ * n_tokens input embeddings (F32 [n_tokens x hidden]) at positions len ..
+ * len + n_tokens - 1 through every layer on the tensor cores (QKV, O-proj,
+ * dense FFN and MoE as split-BF16 GEMMs, the exact sequential-softmax
+ * attention per query), their K/V rows written to the cache. Returns the
+ * first generated token (LM-head argmax of the last row's final RMSNorm);
+ * final_x / logit (optional) receive that row and its logit. Decoding then
+ * continues at len + n_tokens with the token's embedding staged (forward
+ * takes an explicit embedding; generate with first_embed NULL uses it), and
+ * the token is appended to the history. BF16 expert weights required. */
+int ds_cuda_decoder_prefill(ds_cuda_ctx_t *ctx, int model, const float *embeds, int n_tokens, float *final_x,
+                            float *logit);
+/* The same on device embeddings, enqueued on `stream` (NULL: the context's)
+ * without host copies. */
+int ds_cuda_decoder_prefill_dev(ds_cuda_ctx_t *ctx, int model, const float *d_embeds, int n_tokens, void *stream);
+/* Cache rows [pos0, pos0 + n) of one layer as F32 [n x heads*head_dim]. */
+int ds_cuda_decoder_get_kv(ds_cuda_ctx_t *ctx, int model, int layer, int pos0, int n, float *k, float *v);
+
 /* ---------------------------------------------------------------------
  * Weight ingest from a safetensors checkpoint (the reference's
  * ds_safetensors.c reader and ds_ocr.c:608-757 decoder loader).

@@ -72,7 +72,6 @@ struct DecoderModel {
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_y = nullptr;
     uint16_t *pf_ahi = nullptr, *pf_alo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
-    int *pf_pos = nullptr, *pf_lo = nullptr;
     std::vector<void *> allocs;
 
     size_t plane_elems() const {
@@ -94,8 +93,7 @@ static void free_model(DecoderModel *m) {
     drop_graphs(m);
     for (auto *v : {&m->pf_wqkv, &m->pf_dgu, &m->pf_ddown})
         for (uint16_t *p : *v) cudaFree(p);
-    void *ws[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo,
-                  m->pf_pos, m->pf_lo};
+    void *ws[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo};
     for (void *p : ws) cudaFree(p);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
@@ -892,7 +890,8 @@ extern "C" int ds_cuda_decoder_set_embeddings(ds_cuda_ctx_t *c, int id, const ui
 // (LM-head argmax of the last row's final RMSNorm). Per layer: input
 // RMSNorm split into BF16 planes; the QKV projection as one tensor-core GEMM
 // against [wq; wk; wv]; RoPE and the cache writes; the exact decode
-// attention with one query per token over keys 0 .. len+t; the O-projection
+// attention over keys 0 .. len+t for every query (blocks of queries per
+// CTA); the O-projection
 // GEMM and residual; then the MoE prefill block, or for a dense layer the
 // gate/up GEMM with SwiGLU in its epilogue and the down GEMM, and residual.
 // ---------------------------------------------------------------------------
@@ -929,8 +928,7 @@ static int pf_weights(ds_cuda_ctx *c, DecoderModel *m) {
 
 static int pf_workspace(ds_cuda_ctx *c, DecoderModel *m, int T) {
     if (T <= m->pf_cap) return DS_CUDA_OK;
-    void *old[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo,
-                   m->pf_pos, m->pf_lo};
+    void *old[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo};
     CKL(cudaStreamSynchronize(c->stream), "prefill workspace");
     for (void *p : old) cudaFree(p);
     const auto &g = m->cfg;
@@ -945,8 +943,6 @@ static int pf_workspace(ds_cuda_ctx *c, DecoderModel *m, int T) {
     if (e == cudaSuccess) e = cudaMalloc(&m->pf_alo, n * A * 2);
     if (e == cudaSuccess) e = cudaMalloc(&m->pf_hhi, n * std::max<size_t>(Dp, 1) * 2);
     if (e == cudaSuccess) e = cudaMalloc(&m->pf_hlo, n * std::max<size_t>(Dp, 1) * 2);
-    if (e == cudaSuccess) e = cudaMalloc(&m->pf_pos, n * 4);
-    if (e == cudaSuccess) e = cudaMalloc(&m->pf_lo, n * 4);
     if (e != cudaSuccess) {
         cudaGetLastError();
         m->pf_cap = 0;
@@ -985,23 +981,9 @@ static int prefill_enqueue(ds_cuda_ctx *c, DecoderModel *m, const float *d_embed
             m->lo_start[l] = p0;
             lo_changed = true;
         }
-        CKL(launch_pd_positions(m->pf_pos, m->pf_lo, T, p0, m->lo_start[l], st), "prefill positions");
-        AttnArgs aa = {};
-        aa.q = m->pf_q;
-        aa.k_hi = m->plane(0, l);
-        aa.k_lo = m->plane(1, l);
-        aa.v_hi = m->plane(2, l);
-        aa.v_lo = m->plane(3, l);
-        aa.kv_max = g.kv_max;
-        aa.n_heads = NH;
-        aa.d_pos = m->pf_pos;
-        aa.lo_start = m->lo_start[l];
-        aa.lo_starts = m->pf_lo;
-        aa.scale = 1.0f / sqrtf((float)HD);
-        aa.out = m->pf_att;
-        aa.kv_stream_stride = 0;  // every query reads the same cache
-        aa.q_stride = QD;
-        CKL(launch_attn_decode(aa, st, false, T), "prefill attention");
+        CKL(launch_attn_prefill(m->pf_q, m->plane(0, l), m->plane(1, l), m->plane(2, l), m->plane(3, l), g.kv_max,
+                                NH, p0, T, m->lo_start[l], QD, 1.0f / sqrtf((float)HD), m->pf_att, st),
+            "prefill attention");
         CKL(launch_pd_split(m->pf_att, T, QD, nullptr, 0.f, m->pf_ahi, m->pf_alo, st), "prefill split");
         CK(pf_dense_gemm(c, 1, m->pf_ahi, m->pf_alo, T, QD, L.wo, H, m->pf_y, H, nullptr, nullptr, st));
         CKL(launch_pd_add(m->pf_x, m->pf_y, (size_t)T * H, st), "prefill residual");

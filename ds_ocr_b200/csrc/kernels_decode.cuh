@@ -79,7 +79,9 @@ cudaError_t launch_pd_rope_kv(const float *qkv, int T, int NH, int HD, int p0, c
                               float *q, uint16_t *k_hi, uint16_t *k_lo, uint16_t *v_hi, uint16_t *v_lo, int kv_max,
                               cudaStream_t st);
 cudaError_t launch_pd_add(float *x, const float *y, size_t n, cudaStream_t st);
-cudaError_t launch_pd_positions(int *pos, int *lo_starts, int T, int p0, int lo_start, cudaStream_t st);
+cudaError_t launch_attn_prefill(const float *q, const uint16_t *k_hi, const uint16_t *k_lo, const uint16_t *v_hi,
+                                const uint16_t *v_lo, int kv_max, int n_heads, int p0, int T, int lo_start,
+                                int q_stride, float scale, float *out, cudaStream_t st);
 cudaError_t launch_pd_finish(const uint16_t *E, int H, const int *tok, float *x_out, int *pos, int p_next,
                              int *tok_log, int *hist, int *hist_len, int hist_cap, cudaStream_t st);
 

@@ -1,8 +1,7 @@
 // prefill_full.cu — the per-token kernels of the whole-decoder prefill
 // (ds_decoder_prefill, ds_moe_decoder.c:480-905); the GEMMs run on the
-// tensor-core prefill kernel (prefill.cu), the attention on the exact
-// decode attention with one query per token (kernels_decode.cu), the MoE
-// block on the MoE prefill; decoder.cu strings them together.
+// tensor-core prefill kernel (prefill.cu), the MoE block on the MoE prefill;
+// decoder.cu strings them together.
 #include "kernels_decode.cuh"
 
 namespace ds {
@@ -106,14 +105,6 @@ __global__ void pd_add_kernel(float *x, const float *__restrict__ y, size_t n4) 
     reinterpret_cast<float4 *>(x)[i] = a;
 }
 
-// Per-query positions p0 + t and lo-plane starts for the attention.
-__global__ void pd_positions_kernel(int *pos, int *lo_starts, int T, int p0, int lo_start) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= T) return;
-    pos[t] = p0 + t;
-    lo_starts[t] = lo_start;
-}
-
 // After the prefill: the first token's embedding becomes the next decode
 // input, the token is logged against the last prefill position (as a decode
 // step logs its token against its input position) and appended to the
@@ -156,14 +147,261 @@ cudaError_t launch_pd_add(float *x, const float *y, size_t n, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_pd_positions(int *pos, int *lo_starts, int T, int p0, int lo_start, cudaStream_t st) {
-    pd_positions_kernel<<<(T + 255) / 256, 256, 0, st>>>(pos, lo_starts, T, p0, lo_start);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_pd_finish(const uint16_t *E, int H, const int *tok, float *x_out, int *pos, int p_next,
                              int *tok_log, int *hist, int *hist_len, int hist_cap, cudaStream_t st) {
     pd_finish_kernel<<<1, 256, 0, st>>>(E, H, tok, x_out, pos, p_next, tok_log, hist, hist_len, hist_cap);
+    return cudaGetLastError();
+}
+
+}  // namespace ds
+
+namespace ds {
+
+// ---------------------------------------------------------------------------
+// Prefill attention (ds_causal_attention_heads_aligned, ds_kernels.c:
+// 2061-2114): query t attends keys 0 .. p0 + t with the decode rule (the
+// sequential softmax with fast exp). Unrolled, key j contributes
+// w_j v_j with w_j = a_j * prod_{t > j} c_t (a_j = fexp(s_j - m) or 1 at a new
+// maximum, c_t = fexp(m - s_t) at a new maximum t, else 1, m the running
+// maximum before the key). A CTA takes PA_QB queries of one head and walks
+// the keys in blocks of PA_KC, in order, keeping per query the running
+// maximum m, the running sum L and the output O; per block:
+//   1. the block's K and V rows, widened to F32, are staged in shared memory
+//      (rows padded to 132 floats: conflict-free float4 reads) and the
+//      scores S [queries x keys] computed in register tiles;
+//   2. 8 threads per query scan the block's scores against m: a_j and c_j
+//      exactly as the sequential loop evaluates them, the block's
+//      correction product C and local weights w_j = a_j * prod_{t>j in
+//      block} c_t (an 8-lane suffix scan);
+//   3. O = O * C + sum_j w_j v_j, L = L * C + sum_j w_j (register tiles).
+// That is the sequential recurrence applied a block at a time: the same
+// factors, only the order of the F32 products differs.
+// ---------------------------------------------------------------------------
+constexpr int PA_QB = 32;     // queries per CTA
+constexpr int PA_KC = 64;     // keys per block
+constexpr int PA_LD = 132;    // padded F32 row
+constexpr int PA_HD = 128;
+constexpr int PA_SLD = 68;    // score row stride
+constexpr int PA_SMEM = (2 * PA_KC * PA_LD + PA_QB * PA_LD + PA_QB * PA_SLD + 3 * PA_QB) * 4;
+
+struct PrefillAttnArgs {
+    const float *q;  // [T x q_stride], head h at column h*128
+    const uint16_t *k_hi, *k_lo, *v_hi, *v_lo;  // layer planes [head][kv_max][128]
+    int kv_max, p0, T, lo_start, q_stride;
+    float scale;
+    float *out;  // [T x q_stride]
+};
+
+__device__ __forceinline__ void pa_stage(float *buf, const uint16_t *hi, const uint16_t *lo, int c0, int rows,
+                                         int lo_start) {
+    // rows x 128 elements: 16 uint4 of hi (and of lo) per row
+    for (int u = threadIdx.x; u < rows * 16; u += blockDim.x) {
+        const int r = u >> 4, c = (u & 15) * 8;
+        const int j = c0 + r;
+        const uint4 h = ldg_stream(hi + (size_t)j * PA_HD + c);
+        uint4 l = make_uint4(0, 0, 0, 0);
+        if (j >= lo_start) l = ldg_stream(lo + (size_t)j * PA_HD + c);
+        const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+        float f[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            f[2 * i] = __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i]));
+            f[2 * i + 1] = __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i]));
+        }
+        float4 *d = reinterpret_cast<float4 *>(buf + r * PA_LD + c);
+        d[0] = make_float4(f[0], f[1], f[2], f[3]);
+        d[1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+}
+
+__global__ void __launch_bounds__(256, 2) attn_prefill_kernel(PrefillAttnArgs a) {
+    extern __shared__ __align__(16) float pa_smem[];
+    float *kb = pa_smem;                  // [PA_KC][PA_LD]
+    float *vb = kb + PA_KC * PA_LD;       // [PA_KC][PA_LD]
+    float *qs = vb + PA_KC * PA_LD;       // [PA_QB][PA_LD]
+    float *sw = qs + PA_QB * PA_LD;       // [PA_QB][PA_SLD] scores, then weights
+    float *m_run = sw + PA_QB * PA_SLD;   // [PA_QB] running maximum
+    float *l_run = m_run + PA_QB;         // [PA_QB] running sum
+    float *cq = l_run + PA_QB;            // [PA_QB] this block's correction product
+    const int h = blockIdx.x, qb0 = blockIdx.y * PA_QB, tid = threadIdx.x;
+    const int nq = min(PA_QB, a.T - qb0);
+    const int n_end = a.p0 + qb0 + nq;  // keys of the block's last query
+    const size_t hoff = (size_t)h * a.kv_max * PA_HD;
+    const uint16_t *khi = a.k_hi + hoff, *klo = a.k_lo + hoff, *vhi = a.v_hi + hoff, *vlo = a.v_lo + hoff;
+    for (int u = tid; u < PA_QB * PA_HD; u += 256) {
+        const int i = u / PA_HD, d = u - i * PA_HD;
+        qs[i * PA_LD + d] = i < nq ? a.q[(size_t)(qb0 + i) * a.q_stride + h * PA_HD + d] : 0.f;
+    }
+    if (tid < PA_QB) {
+        m_run[tid] = -1e30f;  // the sequential loop's initial maximum
+        l_run[tid] = 0.f;
+    }
+    // score tile: 2 queries x 4 keys (key kg + 16 r); scan: 8 keys of one
+    // query; output tile: 4 queries x 4 dims
+    const int kg = tid & 15, qp = tid >> 4;
+    const int sq = tid >> 3, sg = tid & 7;
+    const int dq = tid & 31, qg = tid >> 5;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int d = 0; d < 4; d++) acc[i][d] = 0.f;
+    for (int c0 = 0; c0 < n_end; c0 += PA_KC) {
+        const int rows = min(PA_KC, n_end - c0);
+        __syncthreads();
+        pa_stage(kb, khi, klo, c0, rows, a.lo_start);
+        pa_stage(vb, vhi, vlo, c0, rows, a.lo_start);
+        __syncthreads();
+        // 1. scores
+        {
+            float s[2][4];
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+                for (int r = 0; r < 4; r++) s[i][r] = 0.f;
+            const float4 *q0 = reinterpret_cast<const float4 *>(qs + (2 * qp) * PA_LD);
+            const float4 *q1 = reinterpret_cast<const float4 *>(qs + (2 * qp + 1) * PA_LD);
+#pragma unroll 4
+            for (int c = 0; c < PA_HD / 4; c++) {
+                const float4 a0 = q0[c], a1 = q1[c];
+#pragma unroll
+                for (int r = 0; r < 4; r++) {
+                    const float4 k4 = reinterpret_cast<const float4 *>(kb + (kg + 16 * r) * PA_LD)[c];
+                    s[0][r] = __fmaf_rn(a0.x, k4.x, s[0][r]);
+                    s[0][r] = __fmaf_rn(a0.y, k4.y, s[0][r]);
+                    s[0][r] = __fmaf_rn(a0.z, k4.z, s[0][r]);
+                    s[0][r] = __fmaf_rn(a0.w, k4.w, s[0][r]);
+                    s[1][r] = __fmaf_rn(a1.x, k4.x, s[1][r]);
+                    s[1][r] = __fmaf_rn(a1.y, k4.y, s[1][r]);
+                    s[1][r] = __fmaf_rn(a1.z, k4.z, s[1][r]);
+                    s[1][r] = __fmaf_rn(a1.w, k4.w, s[1][r]);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+                for (int r = 0; r < 4; r++) sw[(2 * qp + i) * PA_SLD + kg + 16 * r] = __fmul_rn(s[i][r], a.scale);
+        }
+        __syncthreads();
+        // 2. the rule's factors for this block, 8 threads per query
+        {
+            const int n_q = a.p0 + qb0 + sq + 1;  // keys of query sq
+            float *row = sw + sq * PA_SLD;
+            const float m_in = m_run[sq];
+            const int j0 = sg * 8;
+            float sv[8];
+            float lm = -1e30f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const bool ok = c0 + j0 + k < n_q && j0 + k < rows;
+                sv[k] = ok ? row[j0 + k] : -INFINITY;
+                if (ok) lm = fmaxf(lm, sv[k]);
+            }
+            // exclusive prefix maximum over the 8 lanes of this query
+            float inc = lm;
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                const float y = __shfl_up_sync(DS_FULL, inc, o, 8);
+                if (sg >= o) inc = fmaxf(inc, y);
+            }
+            float m = __shfl_up_sync(DS_FULL, inc, 1, 8);
+            m = fmaxf(m_in, sg == 0 ? -1e30f : m);
+            float av[8], cv[8];
+            float lp = 1.f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (sv[k] == -INFINITY) {  // beyond the query's keys
+                    av[k] = 0.f;
+                    cv[k] = 1.f;
+                } else if (sv[k] > m) {
+                    cv[k] = fast_expf(__fsub_rn(m, sv[k]));
+                    av[k] = 1.f;
+                    m = sv[k];
+                } else {
+                    cv[k] = 1.f;
+                    av[k] = fast_expf(__fsub_rn(sv[k], m));
+                }
+                lp = __fmul_rn(lp, cv[k]);
+            }
+            // exclusive suffix product over the 8 lanes, then the weights
+            float sinc = lp;
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                const float y = __shfl_down_sync(DS_FULL, sinc, o, 8);
+                if (sg + o < 8) sinc = __fmul_rn(sinc, y);
+            }
+            float P = __shfl_down_sync(DS_FULL, sinc, 1, 8);
+            if (sg == 7) P = 1.f;
+            float lsum = 0.f;
+#pragma unroll
+            for (int k = 7; k >= 0; k--) {
+                const float w = __fmul_rn(av[k], P);
+                P = __fmul_rn(P, cv[k]);
+                row[j0 + k] = w;
+                lsum = __fadd_rn(lsum, w);
+            }
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) lsum = __fadd_rn(lsum, __shfl_xor_sync(DS_FULL, lsum, o, 8));
+            const float C = __shfl_sync(DS_FULL, sinc, 0, 8);  // product over the whole block
+            float mb = lm;
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(DS_FULL, mb, o, 8));
+            __syncwarp();
+            if (sg == 0) {
+                cq[sq] = C;
+                l_run[sq] = __fadd_rn(__fmul_rn(l_run[sq], C), lsum);
+                m_run[sq] = fmaxf(m_in, mb);
+            }
+        }
+        __syncthreads();
+        // 3. O = O * C + W V
+        {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float C = cq[4 * qg + i];
+#pragma unroll
+                for (int d = 0; d < 4; d++) acc[i][d] = __fmul_rn(acc[i][d], C);
+            }
+            for (int j = 0; j < rows; j++) {
+                const float4 v4 = reinterpret_cast<const float4 *>(vb + j * PA_LD)[dq];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float w = sw[(4 * qg + i) * PA_SLD + j];
+                    acc[i][0] = __fmaf_rn(w, v4.x, acc[i][0]);
+                    acc[i][1] = __fmaf_rn(w, v4.y, acc[i][1]);
+                    acc[i][2] = __fmaf_rn(w, v4.z, acc[i][2]);
+                    acc[i][3] = __fmaf_rn(w, v4.w, acc[i][3]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int qi = 4 * qg + i;
+        if (qi >= nq) continue;
+        const float L = l_run[qi];
+        const float inv = __fdiv_rn(1.0f, L);
+        float4 o;
+        o.x = L > 0.f ? __fmul_rn(acc[i][0], inv) : acc[i][0];
+        o.y = L > 0.f ? __fmul_rn(acc[i][1], inv) : acc[i][1];
+        o.z = L > 0.f ? __fmul_rn(acc[i][2], inv) : acc[i][2];
+        o.w = L > 0.f ? __fmul_rn(acc[i][3], inv) : acc[i][3];
+        *reinterpret_cast<float4 *>(a.out + (size_t)(qb0 + qi) * a.q_stride + h * PA_HD + 4 * dq) = o;
+    }
+}
+
+cudaError_t launch_attn_prefill(const float *q, const uint16_t *k_hi, const uint16_t *k_lo, const uint16_t *v_hi,
+                                const uint16_t *v_lo, int kv_max, int n_heads, int p0, int T, int lo_start,
+                                int q_stride, float scale, float *out, cudaStream_t st) {
+    PrefillAttnArgs a{q, k_hi, k_lo, v_hi, v_lo, kv_max, p0, T, lo_start, q_stride, scale, out};
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    attn_prefill_kernel<<<dim3(n_heads, (T + PA_QB - 1) / PA_QB), 256, PA_SMEM, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -820,6 +820,125 @@ def run_ours_prefill(args, rank, world, pg, model):
     return res
 
 
+# ---------------------------------------------------------------------------
+# Whole-decoder prefill (the widened config 4: ds_decoder_prefill)
+# ---------------------------------------------------------------------------
+PFF_REF_TOKENS = 128   # the reference's bounded CPU sample
+
+
+def prefill_full_flops(T, d):
+    """Algorithmic FLOPs of ds_decoder_prefill on T tokens from an empty
+    cache: QKV + O projections, causal attention (QK and PV), dense layer 0,
+    11 MoE layers (6 routed + shared experts + router), the first token's
+    LM-head row."""
+    H, QD = d.hidden, d.n_heads * d.head_dim
+    proj = 2 * T * (H * 3 * QD + QD * H)
+    attn = 4 * QD * T * (T + 1) // 2
+    dense = 2 * T * 3 * d.dense_inter * H
+    moe = 2 * T * (d.top_k * 3 * d.moe_inter * H + 3 * d.n_shared * d.moe_inter * H + d.n_experts * H)
+    n_moe = d.n_layers - d.first_dense
+    return d.n_layers * (proj + attn) + d.first_dense * dense + n_moe * moe + 2 * d.vocab * H
+
+
+def prefill_full_embeds(model, T):
+    """Input embeddings: the embedding rows of a seeded token sequence."""
+    ids = (np.arange(T, dtype=np.int64) * 7919 + 13) % model.d.vocab
+    return np.stack([model.embed(int(t)) for t in ids])
+
+
+def prefill_full_config(T):
+    return {"workload": "config4_full_prefill", "model": "DeepSeek3B-MoE decoder (12 layers, random init)",
+            "tokens": T, "layers": 12, "hidden": 1280, "experts": 64, "top_k": 6,
+            "routing": "the model's own router", "kv": "written to the decoder's cache (kv_max 4096)",
+            "gemm": "tcgen05 split-BF16 activations x BF16 weights, F32 accumulate; attention exact on CUDA cores",
+            "l2": "each step streams 5.9 GB of weights (> 126 MB L2)"}
+
+
+def run_ours_prefill_full(args, rank, world, pg, model):
+    """ds_decoder_prefill of 3328 tokens through all 12 layers on one GPU per
+    rank (replicas only: a prefill does not shard here; every rank runs its
+    own)."""
+    import torch
+    from ds_ocr_b200 import cuda
+    from ds_ocr_b200.decoder import Decoder
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = cuda.Context(local if world > 1 else 0)
+    d = model.d
+    T = PF_TOKENS
+    dec = Decoder(model, ctx, kv_max=4096)
+    emb = prefill_full_embeds(model, T).astype(np.float32)
+    st = torch.cuda.ExternalStream(ctx.stream)
+    d_emb = torch.from_numpy(emb).cuda()
+    torch.cuda.synchronize()
+
+    def step():
+        dec.set_len(0)
+        dec.prefill_dev(d_emb.data_ptr(), T)
+
+    for _ in range(args.warmup):
+        step()
+    ctx.synchronize()
+    barrier(pg)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(st)
+        for _ in range(args.steps):
+            step()
+        ev1.record(st)
+        ev1.synchronize()
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), pg)
+    value = world * T * args.steps / (ms_max / 1e3)
+    # e2e: the host-pointer API, embeddings in, first token out
+    n_e2e = max(1, min(args.steps, 3))
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.synchronize()
+    t0.record(st)
+    for _ in range(n_e2e):
+        dec.set_len(0)
+        dec.prefill(emb)
+    t1.record(st)
+    t1.synchronize()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1), pg)
+    pk = peaks()
+    peak_t = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    flops = prefill_full_flops(T, d)
+    ach = flops * args.steps / (ms_max / 1e3) / 1e12
+    res = {
+        "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
+        "metric": "whole-decoder prefill tokens/s (3328 tokens x 12 layers: attention, dense layer 0, 11 MoE layers)",
+        "unit": "tokens/s", "dtype": "bf16 weights, f32 activations as two bf16 planes, f32 accumulate",
+        "e2e": {"value": world * T * n_e2e / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * d.hidden * 4,
+                "d2h_bytes_per_step": 8},
+        "gpu_launches": (d.n_layers * 9 + 8 * (d.n_layers - d.first_dense) + 4) * args.steps,
+        "config": dict(prefill_full_config(T), parallelism=f"replicas on {world} GPU(s)"),
+        "roofline": {"bound": "tensor", "achieved": ach, "peak": peak_t, "unit": "TFLOP/s", "frac": ach / peak_t,
+                     "traffic": None, "kernel": "whole prefill step (algorithmic FLOPs of every GEMM and the "
+                                                "attention / step time)",
+                     "flops_per_step": flops, "peak_source": pk["source"]},
+    }
+    if world > 1:
+        res["scaling"] = "weak"
+    dec.close()
+    ctx.close()
+    return res
+
+
+def ref_prefill_full_time(model, threads, T=PFF_REF_TOKENS):
+    """The reference's own ds_decoder_prefill (compiled unmodified) on the
+    first T tokens of the same embeddings, from an empty cache."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    emb = prefill_full_embeds(model, T).astype(np.float32)
+    R = O.RefDecoder(model, kv_max=4096, threads=threads)
+    R.prefill(emb[:8])  # warm (weight conversion, thread pool)
+    R.r.ref_ctx_set_len(R.ctx, 0)
+    t = time.perf_counter()
+    R.prefill(emb)
+    dt = time.perf_counter() - t
+    R.close()
+    return T / dt, T
+
+
 def ref_prefill_time(model, threads, budget_s):
     """The reference's prefill MoE block (its own kernels and OpenBLAS sgemm,
     compiled unmodified) on the config-4 inputs, one layer per call, until
@@ -847,7 +966,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "decode64", "moe_layer", "prefill", "lm_head"])
+                    choices=["decode", "decode64", "moe_layer", "prefill", "prefill_full", "lm_head"])
     ap.add_argument("--engine", type=int, default=0, choices=[0, 1],
                     help="decode engine: 0 CUDA graph of per-phase kernels, 1 persistent kernel")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
@@ -888,6 +1007,13 @@ def main():
             v, n = ref_prefill_time(synth.Model(), T, max(args.cpu_budget, 1.0))
             metric = "MoE prefill tokens/s (3328 tokens x 11 MoE layers, 64 experts top-6 + 2 shared)"
             cfg, sample = prefill_config(), f"{n} of 11 MoE layers of the prefill block at 3328 tokens"
+        elif args.workload == "prefill_full":
+            from ds_ocr_b200 import synth
+            v, n = ref_prefill_full_time(synth.Model(), T)
+            metric = ("whole-decoder prefill tokens/s (3328 tokens x 12 layers: attention, dense layer 0, "
+                      "11 MoE layers)")
+            cfg = prefill_full_config(PF_TOKENS)
+            sample = f"one ds_decoder_prefill of the first {n} tokens (12 layers)"
         else:
             wl = MoeLayerWorkload()
             v, n = ref_moe_time(wl, T, max(args.cpu_budget, 1.0))
@@ -907,6 +1033,10 @@ def main():
         from ds_ocr_b200 import synth
         model = synth.Model()
         res = run_ours_prefill(args, rank, world, pg, model)
+    elif args.workload == "prefill_full":
+        from ds_ocr_b200 import synth
+        model = synth.Model()
+        res = run_ours_prefill_full(args, rank, world, pg, model)
     elif args.workload == "lm_head":
         res = run_ours_lmhead(args, rank, world, pg)
     elif args.workload == "decode64":
@@ -941,6 +1071,10 @@ def main():
             elif args.workload == "prefill":
                 v, n = ref_prefill_time(model, T, args.cpu_budget)
                 sample = f"{n} of 11 MoE layers of the prefill block at 3328 tokens"
+            elif args.workload == "prefill_full":
+                v, n = ref_prefill_full_time(model, T)
+                sample = f"one ds_decoder_prefill of the first {n} tokens (12 layers; the attention share grows " \
+                         "with the length, so 3328 tokens run slower per token)"
             else:
                 wl = MoeLayerWorkload()
                 v, n = ref_moe_time(wl, T, args.cpu_budget)

@@ -952,6 +952,8 @@ static int pf_workspace(ds_cuda_ctx *c, DecoderModel *m, int T) {
     return DS_CUDA_OK;
 }
 
+// d_embeds: the input rows in device memory, or null when the caller has
+// already placed them in the workspace's x (pf_workspace first).
 static int prefill_enqueue(ds_cuda_ctx *c, DecoderModel *m, const float *d_embeds, int T, cudaStream_t st) {
     const auto &g = m->cfg;
     const int H = g.hidden, NH = g.n_heads, HD = g.head_dim, QD = NH * HD;
@@ -966,7 +968,8 @@ static int prefill_enqueue(ds_cuda_ctx *c, DecoderModel *m, const float *d_embed
     CK(pf_workspace(c, m, T));
     const int p0 = m->host_len;
     const PfShape shape{H, g.moe_inter, g.n_shared * g.moe_inter, g.n_experts, g.top_k, g.rms_eps};
-    CKL(cudaMemcpyAsync(m->pf_x, d_embeds, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st), "prefill input");
+    if (d_embeds)
+        CKL(cudaMemcpyAsync(m->pf_x, d_embeds, (size_t)T * H * 4, cudaMemcpyDeviceToDevice, st), "prefill input");
     bool lo_changed = false;
     for (int l = 0; l < g.n_layers; l++) {
         const DecLayer &L = m->layers[l];
@@ -1036,10 +1039,15 @@ extern "C" int ds_cuda_decoder_prefill(ds_cuda_ctx_t *c, int id, const float *em
     if (m->host_len + n_tokens > m->cfg.kv_max) return ctx_fail(c, DS_CUDA_ESTATE, "decoder_prefill: KV cache full");
     cudaSetDevice(c->device);
     const size_t H = m->cfg.hidden, bytes = (size_t)n_tokens * H * 4;
-    float *d = nullptr;
-    CKL(cudaMalloc(&d, bytes), "prefill input");
-    int rc = ctx_cuda(c, cudaMemcpyAsync(d, embeds, bytes, cudaMemcpyHostToDevice, c->stream), "prefill input");
-    if (rc == DS_CUDA_OK) rc = prefill_enqueue(c, m, d, n_tokens, c->stream);
+    // the rows go through the context's pinned buffer straight into the
+    // workspace's x (one DMA, no device allocation per call)
+    CK(pf_weights(c, m));
+    CK(pf_workspace(c, m, n_tokens));
+    CK(ctx_pinned(c, bytes));
+    CKL(cudaStreamSynchronize(c->stream), "prefill staging");  // the pinned buffer is free
+    memcpy(c->pin, embeds, bytes);
+    int rc = ctx_cuda(c, cudaMemcpyAsync(m->pf_x, c->pin, bytes, cudaMemcpyHostToDevice, c->stream), "prefill input");
+    if (rc == DS_CUDA_OK) rc = prefill_enqueue(c, m, nullptr, n_tokens, c->stream);
     int tok = 0;
     float val = 0.f;
     if (rc == DS_CUDA_OK) rc = ctx_cuda(c, cudaMemcpyAsync(&tok, m->tok, 4, cudaMemcpyDeviceToHost, c->stream), "token");
@@ -1048,7 +1056,6 @@ extern "C" int ds_cuda_decoder_prefill(ds_cuda_ctx_t *c, int id, const float *em
         rc = ctx_cuda(c, cudaMemcpyAsync(final_x, m->xfinal, H * 4, cudaMemcpyDeviceToHost, c->stream), "final x");
     if (rc == DS_CUDA_OK) rc = ctx_cuda(c, cudaStreamSynchronize(c->stream), "decoder_prefill");
     if (rc == DS_CUDA_OK) rc = prefill_check_flag(c);
-    cudaFree(d);
     if (rc < 0) return rc;
     if (logit) *logit = val;
     return tok;

@@ -165,24 +165,27 @@ namespace ds {
 // maximum, c_t = fexp(m - s_t) at a new maximum t, else 1, m the running
 // maximum before the key). A CTA takes PA_QB queries of one head and walks
 // the keys in blocks of PA_KC, in order, keeping per query the running
-// maximum m, the running sum L and the output O; per block:
-//   1. the block's K and V rows, widened to F32, are staged in shared memory
-//      (rows padded to 132 floats: conflict-free float4 reads) and the
-//      scores S [queries x keys] computed in register tiles;
-//   2. 8 threads per query scan the block's scores against m: a_j and c_j
-//      exactly as the sequential loop evaluates them, the block's
+// maximum m, the running sum L and the output O (registers); per block:
+//   1. the block's K rows, widened to F32, are staged transposed (Kt[d][j])
+//      next to the transposed queries (Qt[d][q]), and the scores come from
+//      8 x 8 register tiles with float4 loads along both tile edges;
+//      they are stored key-major (St[j][q]);
+//   2. two threads per query scan the block's scores against m: a_j and
+//      c_j exactly as the sequential loop evaluates them, the block's
 //      correction product C and local weights w_j = a_j * prod_{t>j in
-//      block} c_t (an 8-lane suffix scan);
-//   3. O = O * C + sum_j w_j v_j, L = L * C + sum_j w_j (register tiles).
+//      block} c_t;
+//   3. the V rows are staged (V[j][d]) over the K tile and
+//      O = O * C + sum_j w_j v_j, L = L * C + sum_j w_j (8 x 8 tiles).
 // That is the sequential recurrence applied a block at a time: the same
-// factors, only the order of the F32 products differs.
+// factors, only the order of the F32 products differs. Query blocks are
+// launched longest first.
 // ---------------------------------------------------------------------------
-constexpr int PA_QB = 32;     // queries per CTA
-constexpr int PA_KC = 64;     // keys per block
-constexpr int PA_LD = 132;    // padded F32 row
+constexpr int PA_QB = 128;   // queries per CTA
+constexpr int PA_KC = 128;   // keys per block
 constexpr int PA_HD = 128;
-constexpr int PA_SLD = 68;    // score row stride
-constexpr int PA_SMEM = (2 * PA_KC * PA_LD + PA_QB * PA_LD + PA_QB * PA_SLD + 3 * PA_QB) * 4;
+constexpr int PA_LD = 132;   // padded F32 row of every shared tile
+constexpr int PA_TILE = PA_HD * PA_LD;  // floats per 128-row tile
+constexpr int PA_SMEM = (3 * PA_TILE + 9 * PA_QB) * 4;
 
 struct PrefillAttnArgs {
     const float *q;  // [T x q_stride], head h at column h*128
@@ -192,11 +195,16 @@ struct PrefillAttnArgs {
     float *out;  // [T x q_stride]
 };
 
+// Rows c0 .. c0+rows-1 of a plane pair widened to F32: row-major buf[j][d]
+// (transposed = false) or buf[d][j] (transposed = true).
+// Transposed: consecutive threads take consecutive rows (conflict-free
+// column writes); row-major: consecutive threads take one row's 16-byte
+// pieces (coalesced reads, conflict-free float4 writes).
+template <bool TRANSPOSED>
 __device__ __forceinline__ void pa_stage(float *buf, const uint16_t *hi, const uint16_t *lo, int c0, int rows,
                                          int lo_start) {
-    // rows x 128 elements: 16 uint4 of hi (and of lo) per row
     for (int u = threadIdx.x; u < rows * 16; u += blockDim.x) {
-        const int r = u >> 4, c = (u & 15) * 8;
+        const int r = TRANSPOSED ? u % rows : u >> 4, c = TRANSPOSED ? (u / rows) * 8 : (u & 15) * 8;
         const int j = c0 + r;
         const uint4 h = ldg_stream(hi + (size_t)j * PA_HD + c);
         uint4 l = make_uint4(0, 0, 0, 0);
@@ -208,31 +216,210 @@ __device__ __forceinline__ void pa_stage(float *buf, const uint16_t *hi, const u
             f[2 * i] = __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i]));
             f[2 * i + 1] = __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i]));
         }
-        float4 *d = reinterpret_cast<float4 *>(buf + r * PA_LD + c);
-        d[0] = make_float4(f[0], f[1], f[2], f[3]);
-        d[1] = make_float4(f[4], f[5], f[6], f[7]);
+        if (TRANSPOSED) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) buf[(c + i) * PA_LD + r] = f[i];
+        } else {
+            float4 *d = reinterpret_cast<float4 *>(buf + r * PA_LD + c);
+            d[0] = make_float4(f[0], f[1], f[2], f[3]);
+            d[1] = make_float4(f[4], f[5], f[6], f[7]);
+        }
     }
 }
 
-__global__ void __launch_bounds__(256, 2) attn_prefill_kernel(PrefillAttnArgs a) {
+// 8 floats: p[0..3] and p[gap..gap+3].
+__device__ __forceinline__ void pa_load8(const float *p, float v[8], int gap = 4) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0], b = *reinterpret_cast<const float4 *>(p + gap);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__global__ void __launch_bounds__(256, 1) attn_prefill_kernel(PrefillAttnArgs a) {
     extern __shared__ __align__(16) float pa_smem[];
-    float *kb = pa_smem;                  // [PA_KC][PA_LD]
-    float *vb = kb + PA_KC * PA_LD;       // [PA_KC][PA_LD]
-    float *qs = vb + PA_KC * PA_LD;       // [PA_QB][PA_LD]
-    float *sw = qs + PA_QB * PA_LD;       // [PA_QB][PA_SLD] scores, then weights
-    float *m_run = sw + PA_QB * PA_SLD;   // [PA_QB] running maximum
+    float *qt = pa_smem;                  // [128 d][PA_LD] queries, transposed
+    float *kv = qt + PA_TILE;             // [128 d][PA_LD] keys transposed, then [128 j][PA_LD] values
+    float *st = kv + PA_TILE;             // [128 j][PA_LD] scores, then weights
+    float *m_run = st + PA_TILE;          // [PA_QB] running maximum
     float *l_run = m_run + PA_QB;         // [PA_QB] running sum
     float *cq = l_run + PA_QB;            // [PA_QB] this block's correction product
-    const int h = blockIdx.x, qb0 = blockIdx.y * PA_QB, tid = threadIdx.x;
+    float *hm = cq + PA_QB;               // [2][PA_QB] half-block maxima
+    float *hp = hm + 2 * PA_QB;           // [2][PA_QB] half-block correction products
+    float *hs = hp + 2 * PA_QB;           // [2][PA_QB] half-block weight sums
+    const int h = blockIdx.x;
+    const int qb0 = (gridDim.y - 1 - blockIdx.y) * PA_QB;  // longest query blocks first
+    const int tid = threadIdx.x;
     const int nq = min(PA_QB, a.T - qb0);
     const int n_end = a.p0 + qb0 + nq;  // keys of the block's last query
     const size_t hoff = (size_t)h * a.kv_max * PA_HD;
     const uint16_t *khi = a.k_hi + hoff, *klo = a.k_lo + hoff, *vhi = a.v_hi + hoff, *vlo = a.v_lo + hoff;
     for (int u = tid; u < PA_QB * PA_HD; u += 256) {
         const int i = u / PA_HD, d = u - i * PA_HD;
-        qs[i * PA_LD + d] = i < nq ? a.q[(size_t)(qb0 + i) * a.q_stride + h * PA_HD + d] : 0.f;
+        qt[d * PA_LD + i] = i < nq ? a.q[(size_t)(qb0 + i) * a.q_stride + h * PA_HD + d] : 0.f;
     }
     if (tid < PA_QB) {
+        m_run[tid] = -1e30f;  // the sequential loop's initial maximum
+        l_run[tid] = 0.f;
+    }
+    // 8 x 8 tiles: queries 8tq .. 8tq+7; keys (phase 1) or dims (phase 3)
+    // 4tk .. 4tk+3 and 64+4tk .. 64+4tk+3, so a warp's float4 loads are contiguous
+    const int tq = tid >> 4, tk = tid & 15;
+    auto col = [&](int j) { return j < 4 ? 4 * tk + j : 60 + 4 * tk + j; };
+    const int sq = tid & 127, half = tid >> 7;  // scan: query sq, keys 64*half .. +63
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int d = 0; d < 8; d++) acc[i][d] = 0.f;
+    for (int c0 = 0; c0 < n_end; c0 += PA_KC) {
+        const int rows = min(PA_KC, n_end - c0);
+        __syncthreads();
+        pa_stage<true>(kv, khi, klo, c0, rows, a.lo_start);
+        __syncthreads();
+        // 1. scores S[q][j] = q . k_j * scale, stored St[j][q]
+        {
+            float s[8][8];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) s[i][j] = 0.f;
+#pragma unroll 2
+            for (int d = 0; d < PA_HD; d++) {
+                float qv[8], kv8[8];
+                pa_load8(qt + d * PA_LD + 8 * tq, qv);
+                pa_load8(kv + d * PA_LD + 4 * tk, kv8, 64);
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int j = 0; j < 8; j++) s[i][j] = __fmaf_rn(qv[i], kv8[j], s[i][j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                float4 *o = reinterpret_cast<float4 *>(st + col(j) * PA_LD + 8 * tq);
+                o[0] = make_float4(__fmul_rn(s[0][j], a.scale), __fmul_rn(s[1][j], a.scale),
+                                   __fmul_rn(s[2][j], a.scale), __fmul_rn(s[3][j], a.scale));
+                o[1] = make_float4(__fmul_rn(s[4][j], a.scale), __fmul_rn(s[5][j], a.scale),
+                                   __fmul_rn(s[6][j], a.scale), __fmul_rn(s[7][j], a.scale));
+            }
+        }
+        __syncthreads();
+        // the V rows replace the K tile (the scores are all in St)
+        pa_stage<false>(kv, vhi, vlo, c0, rows, a.lo_start);
+        // 2. the rule's factors: two threads per query, 64 keys each
+        const int n_q = a.p0 + qb0 + sq + 1;            // keys of query sq
+        const int kb0 = 64 * half;                      // this thread's first key of the block
+        const int kend = min(min(64, rows - kb0), n_q - c0 - kb0);  // its valid keys (may be <= 0)
+        float lm = -1e30f;
+        for (int k = 0; k < kend; k++) lm = fmaxf(lm, st[(kb0 + k) * PA_LD + sq]);
+        hm[half * PA_QB + sq] = lm;
+        __syncthreads();
+        const float m_in = m_run[sq];
+        float m = half == 0 ? m_in : fmaxf(m_in, hm[sq]);
+        float lp = 1.f;
+        for (int k = 0; k < 64; k++) {
+            float *p = st + (kb0 + k) * PA_LD + sq;
+            if (k >= kend) {
+                *p = 0.f;  // beyond the query's keys: a = 0, c = 1
+                continue;
+            }
+            const float s = *p;
+            if (s > m) {
+                const float cj = fast_expf(__fsub_rn(m, s));
+                *p = cj == 0.f ? -0.f : -cj;  // sign set: a new maximum (a_j = 1)
+                lp = __fmul_rn(lp, cj);
+                m = s;
+            } else {
+                *p = fast_expf(__fsub_rn(s, m));
+            }
+        }
+        hp[half * PA_QB + sq] = lp;
+        __syncthreads();
+        float P = half == 0 ? hp[PA_QB + sq] : 1.f;  // corrections of the later half
+        float lsum = 0.f;
+        for (int k = 63; k >= 0; k--) {
+            float *p = st + (kb0 + k) * PA_LD + sq;
+            const float v = *p;
+            const bool nm = signbit(v);
+            const float w = nm ? P : __fmul_rn(v, P);
+            if (nm) P = __fmul_rn(P, -v);
+            *p = w;
+            lsum = __fadd_rn(lsum, w);
+        }
+        hs[half * PA_QB + sq] = lsum;
+        __syncthreads();
+        if (half == 0) {
+            const float C = __fmul_rn(hp[sq], hp[PA_QB + sq]);
+            cq[sq] = C;
+            l_run[sq] = __fadd_rn(__fmul_rn(l_run[sq], C), __fadd_rn(hs[sq], hs[PA_QB + sq]));
+            m_run[sq] = fmaxf(m_in, fmaxf(hm[sq], hm[PA_QB + sq]));
+        }
+        __syncthreads();
+        // 3. O = O * C + W V over this block's keys (queries 8tq.., dims col(0..7))
+        {
+            float C8[8];
+            pa_load8(cq + 8 * tq, C8);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int d = 0; d < 8; d++) acc[i][d] = __fmul_rn(acc[i][d], C8[i]);
+#pragma unroll 2
+            for (int j = 0; j < rows; j++) {
+                float w8[8], v8[8];
+                pa_load8(st + j * PA_LD + 8 * tq, w8);
+                pa_load8(kv + j * PA_LD + 4 * tk, v8, 64);
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+#pragma unroll
+                    for (int d = 0; d < 8; d++) acc[i][d] = __fmaf_rn(w8[i], v8[d], acc[i][d]);
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int qi = 8 * tq + i;
+        if (qi >= nq) continue;
+        const float L = l_run[qi];
+        const float inv = __fdiv_rn(1.0f, L);
+        float o[8];
+#pragma unroll
+        for (int d = 0; d < 8; d++) o[d] = L > 0.f ? __fmul_rn(acc[i][d], inv) : acc[i][d];
+        float *dst = a.out + (size_t)(qb0 + qi) * a.q_stride + h * PA_HD + 4 * tk;
+        *reinterpret_cast<float4 *>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4 *>(dst + 64) = make_float4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+// The same attention with 32 queries per CTA (4 x 2 score tiles, 8 threads
+// per query in the scan), for prefills short enough that 128-query blocks
+// would leave SMs idle.
+constexpr int PS_QB = 32;     // queries per CTA
+constexpr int PS_KC = 64;     // keys per block
+constexpr int PS_LD = 132;    // padded F32 row
+constexpr int PS_HD = 128;
+constexpr int PS_SLD = 68;    // score row stride
+constexpr int PS_SMEM = (2 * PS_KC * PS_LD + PS_QB * PS_LD + PS_QB * PS_SLD + 3 * PS_QB) * 4;
+
+
+
+__global__ void __launch_bounds__(256, 2) attn_prefill_small_kernel(PrefillAttnArgs a) {
+    extern __shared__ __align__(16) float ps_smem[];
+    float *kb = ps_smem;                  // [PS_KC][PS_LD]
+    float *vb = kb + PS_KC * PS_LD;       // [PS_KC][PS_LD]
+    float *qs = vb + PS_KC * PS_LD;       // [PS_QB][PS_LD]
+    float *sw = qs + PS_QB * PS_LD;       // [PS_QB][PS_SLD] scores, then weights
+    float *m_run = sw + PS_QB * PS_SLD;   // [PS_QB] running maximum
+    float *l_run = m_run + PS_QB;         // [PS_QB] running sum
+    float *cq = l_run + PS_QB;            // [PS_QB] this block's correction product
+    const int h = blockIdx.x, qb0 = blockIdx.y * PS_QB, tid = threadIdx.x;
+    const int nq = min(PS_QB, a.T - qb0);
+    const int n_end = a.p0 + qb0 + nq;  // keys of the block's last query
+    const size_t hoff = (size_t)h * a.kv_max * PS_HD;
+    const uint16_t *khi = a.k_hi + hoff, *klo = a.k_lo + hoff, *vhi = a.v_hi + hoff, *vlo = a.v_lo + hoff;
+    for (int u = tid; u < PS_QB * PS_HD; u += 256) {
+        const int i = u / PS_HD, d = u - i * PS_HD;
+        qs[i * PS_LD + d] = i < nq ? a.q[(size_t)(qb0 + i) * a.q_stride + h * PS_HD + d] : 0.f;
+    }
+    if (tid < PS_QB) {
         m_run[tid] = -1e30f;  // the sequential loop's initial maximum
         l_run[tid] = 0.f;
     }
@@ -246,11 +433,11 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(PrefillAttnArgs a)
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int d = 0; d < 4; d++) acc[i][d] = 0.f;
-    for (int c0 = 0; c0 < n_end; c0 += PA_KC) {
-        const int rows = min(PA_KC, n_end - c0);
+    for (int c0 = 0; c0 < n_end; c0 += PS_KC) {
+        const int rows = min(PS_KC, n_end - c0);
         __syncthreads();
-        pa_stage(kb, khi, klo, c0, rows, a.lo_start);
-        pa_stage(vb, vhi, vlo, c0, rows, a.lo_start);
+        pa_stage<false>(kb, khi, klo, c0, rows, a.lo_start);
+        pa_stage<false>(vb, vhi, vlo, c0, rows, a.lo_start);
         __syncthreads();
         // 1. scores
         {
@@ -259,14 +446,14 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(PrefillAttnArgs a)
             for (int i = 0; i < 2; i++)
 #pragma unroll
                 for (int r = 0; r < 4; r++) s[i][r] = 0.f;
-            const float4 *q0 = reinterpret_cast<const float4 *>(qs + (2 * qp) * PA_LD);
-            const float4 *q1 = reinterpret_cast<const float4 *>(qs + (2 * qp + 1) * PA_LD);
+            const float4 *q0 = reinterpret_cast<const float4 *>(qs + (2 * qp) * PS_LD);
+            const float4 *q1 = reinterpret_cast<const float4 *>(qs + (2 * qp + 1) * PS_LD);
 #pragma unroll 4
-            for (int c = 0; c < PA_HD / 4; c++) {
+            for (int c = 0; c < PS_HD / 4; c++) {
                 const float4 a0 = q0[c], a1 = q1[c];
 #pragma unroll
                 for (int r = 0; r < 4; r++) {
-                    const float4 k4 = reinterpret_cast<const float4 *>(kb + (kg + 16 * r) * PA_LD)[c];
+                    const float4 k4 = reinterpret_cast<const float4 *>(kb + (kg + 16 * r) * PS_LD)[c];
                     s[0][r] = __fmaf_rn(a0.x, k4.x, s[0][r]);
                     s[0][r] = __fmaf_rn(a0.y, k4.y, s[0][r]);
                     s[0][r] = __fmaf_rn(a0.z, k4.z, s[0][r]);
@@ -280,13 +467,13 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(PrefillAttnArgs a)
 #pragma unroll
             for (int i = 0; i < 2; i++)
 #pragma unroll
-                for (int r = 0; r < 4; r++) sw[(2 * qp + i) * PA_SLD + kg + 16 * r] = __fmul_rn(s[i][r], a.scale);
+                for (int r = 0; r < 4; r++) sw[(2 * qp + i) * PS_SLD + kg + 16 * r] = __fmul_rn(s[i][r], a.scale);
         }
         __syncthreads();
         // 2. the rule's factors for this block, 8 threads per query
         {
             const int n_q = a.p0 + qb0 + sq + 1;  // keys of query sq
-            float *row = sw + sq * PA_SLD;
+            float *row = sw + sq * PS_SLD;
             const float m_in = m_run[sq];
             const int j0 = sg * 8;
             float sv[8];
@@ -363,10 +550,10 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(PrefillAttnArgs a)
                 for (int d = 0; d < 4; d++) acc[i][d] = __fmul_rn(acc[i][d], C);
             }
             for (int j = 0; j < rows; j++) {
-                const float4 v4 = reinterpret_cast<const float4 *>(vb + j * PA_LD)[dq];
+                const float4 v4 = reinterpret_cast<const float4 *>(vb + j * PS_LD)[dq];
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    const float w = sw[(4 * qg + i) * PA_SLD + j];
+                    const float w = sw[(4 * qg + i) * PS_SLD + j];
                     acc[i][0] = __fmaf_rn(w, v4.x, acc[i][0]);
                     acc[i][1] = __fmaf_rn(w, v4.y, acc[i][1]);
                     acc[i][2] = __fmaf_rn(w, v4.z, acc[i][2]);
@@ -387,7 +574,7 @@ __global__ void __launch_bounds__(256, 2) attn_prefill_kernel(PrefillAttnArgs a)
         o.y = L > 0.f ? __fmul_rn(acc[i][1], inv) : acc[i][1];
         o.z = L > 0.f ? __fmul_rn(acc[i][2], inv) : acc[i][2];
         o.w = L > 0.f ? __fmul_rn(acc[i][3], inv) : acc[i][3];
-        *reinterpret_cast<float4 *>(a.out + (size_t)(qb0 + qi) * a.q_stride + h * PA_HD + 4 * dq) = o;
+        *reinterpret_cast<float4 *>(a.out + (size_t)(qb0 + qi) * a.q_stride + h * PS_HD + 4 * dq) = o;
     }
 }
 
@@ -401,7 +588,19 @@ cudaError_t launch_attn_prefill(const float *q, const uint16_t *k_hi, const uint
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    attn_prefill_kernel<<<dim3(n_heads, (T + PA_QB - 1) / PA_QB), 256, PA_SMEM, st>>>(a);
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaError_t e = cudaFuncSetAttribute(attn_prefill_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             PS_SMEM);
+        if (e != cudaSuccess) return e;
+    }
+    if (n_heads * ((T + PA_QB - 1) / PA_QB) < sms)
+        attn_prefill_small_kernel<<<dim3(n_heads, (T + PS_QB - 1) / PS_QB), 256, PS_SMEM, st>>>(a);
+    else
+        attn_prefill_kernel<<<dim3(n_heads, (T + PA_QB - 1) / PA_QB), 256, PA_SMEM, st>>>(a);
     return cudaGetLastError();
 }
 

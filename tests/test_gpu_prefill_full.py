@@ -57,6 +57,26 @@ def test_prefill_matches_oracle(cuda_ctx, model, T, prefix):
         dec.close()
 
 
+def test_long_prefill_takes_the_large_query_blocks(cuda_ctx, model):
+    # 2000 tokens x 10 heads: enough 128-query blocks to fill the SMs, so the
+    # large-tile attention kernel runs (shorter prefills use 32-query blocks)
+    T = 2000
+    dec = Decoder(model, cuda_ctx, kv_max=2048)
+    ora = O.OracleDecoder(model, kv_max=2048)
+    try:
+        emb = np.stack([model.embed(t) for t in (np.arange(T) * 53 + 5) % model.d.vocab])
+        tok, fx, _ = dec.prefill(emb, want_x=True)
+        otok, ofx, _ = ora.prefill(emb)
+        assert rel_l2(fx, ofx) < 1e-3
+        for l in range(model.d.n_layers):
+            k, v = dec.kv(l, 0, T)
+            assert rel_l2(k, ora.k[l, :T]) < 1e-3 and rel_l2(v, ora.v[l, :T]) < 1e-3, l
+        if gap(model, ofx) > 1e-4:
+            assert tok == otok
+    finally:
+        dec.close()
+
+
 def test_prefill_dense_and_moe_layers_full_size(cuda_ctx):
     # the full 12-layer model (dense layer 0 + 11 MoE layers), 200 tokens
     m = synth.Model()

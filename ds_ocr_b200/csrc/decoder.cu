@@ -67,10 +67,11 @@ struct DecoderModel {
     // whole-decoder prefill: fused [wq; wk; wv] per layer and the dense
     // layers' gate/up and down with the width padded to a multiple of 128
     // (built on first use), and a workspace for pf_cap tokens
-    std::vector<uint16_t *> pf_wqkv, pf_dgu, pf_ddown;
+    std::vector<uint16_t *> pf_wqkv, pf_dgu, pf_ddown, pf_router;  // router: zero-padded to 256 rows
     int pf_dpad = 0;
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_y = nullptr;
+    float *pf_lg = nullptr;  // router logits [tokens x 256]
     uint16_t *pf_ahi = nullptr, *pf_alo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
     std::vector<void *> allocs;
 
@@ -91,9 +92,10 @@ static void drop_graphs(DecoderModel *m) {
 
 static void free_model(DecoderModel *m) {
     drop_graphs(m);
-    for (auto *v : {&m->pf_wqkv, &m->pf_dgu, &m->pf_ddown})
+    for (auto *v : {&m->pf_wqkv, &m->pf_dgu, &m->pf_ddown, &m->pf_router})
         for (uint16_t *p : *v) cudaFree(p);
-    void *ws[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo};
+    void *ws[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo,
+                  m->pf_lg};
     for (void *p : ws) cudaFree(p);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
@@ -922,13 +924,23 @@ static int pf_weights(ds_cuda_ctx *c, DecoderModel *m) {
         }
         m->pf_dgu.push_back(gu);
         m->pf_ddown.push_back(dn);
+        uint16_t *rt = nullptr;
+        if (!L.dense && g.n_experts <= 256) {
+            // the router as a GEMM B operand: E rows, zero rows up to 256
+            CKL(cudaMalloc(&rt, (size_t)256 * H * 2), "prefill router weights");
+            CKL(cudaMemsetAsync(rt, 0, (size_t)256 * H * 2, st), "router pad");
+            CKL(cudaMemcpyAsync(rt, L.router, (size_t)g.n_experts * H * 2, cudaMemcpyDeviceToDevice, st),
+                "router copy");
+        }
+        m->pf_router.push_back(rt);
     }
     return DS_CUDA_OK;
 }
 
 static int pf_workspace(ds_cuda_ctx *c, DecoderModel *m, int T) {
     if (T <= m->pf_cap) return DS_CUDA_OK;
-    void *old[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo};
+    void *old[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo,
+                   m->pf_lg};
     CKL(cudaStreamSynchronize(c->stream), "prefill workspace");
     for (void *p : old) cudaFree(p);
     const auto &g = m->cfg;
@@ -943,6 +955,7 @@ static int pf_workspace(ds_cuda_ctx *c, DecoderModel *m, int T) {
     if (e == cudaSuccess) e = cudaMalloc(&m->pf_alo, n * A * 2);
     if (e == cudaSuccess) e = cudaMalloc(&m->pf_hhi, n * std::max<size_t>(Dp, 1) * 2);
     if (e == cudaSuccess) e = cudaMalloc(&m->pf_hlo, n * std::max<size_t>(Dp, 1) * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&m->pf_lg, n * 256 * 4);
     if (e != cudaSuccess) {
         cudaGetLastError();
         m->pf_cap = 0;
@@ -998,8 +1011,19 @@ static int prefill_enqueue(ds_cuda_ctx *c, DecoderModel *m, const float *d_embed
             CK(pf_dense_gemm(c, 1, m->pf_hhi, m->pf_hlo, T, Dp, m->pf_ddown[l], H, m->pf_y, H, nullptr, nullptr, st));
             CKL(launch_pd_add(m->pf_x, m->pf_y, (size_t)T * H, st), "prefill residual");
         } else {
-            CK(prefill_moe_enqueue(c, shape, L.post_norm, L.router, L.block, L.down, L.sdown, m->pf_x, T, nullptr,
-                                   nullptr, nullptr, st));
+            // router logits for every token as one GEMM on the normed rows
+            // (the MoE block normalises again for its own planes)
+            const float *lg = nullptr;
+            PfShape sh = shape;
+            if (m->pf_router[l]) {
+                CKL(launch_pd_split(m->pf_x, T, H, L.post_norm, g.rms_eps, m->pf_ahi, m->pf_alo, st), "router norm");
+                CK(pf_dense_gemm(c, 1, m->pf_ahi, m->pf_alo, T, H, m->pf_router[l], 256, m->pf_lg, 256, nullptr,
+                                 nullptr, st));
+                lg = m->pf_lg;
+                sh.logits_ld = 256;
+            }
+            CK(prefill_moe_enqueue(c, sh, L.post_norm, L.router, L.block, L.down, L.sdown, m->pf_x, T, lg, nullptr,
+                                   nullptr, st));
         }
     }
     if (lo_changed) drop_graphs(m);  // the decode graph bakes lo_start in

@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_gemm_kernel(const __grid_con
 // token; H a multiple of 128, E <= 256.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) pf_norm_route_kernel(const float *__restrict__ x, const float *__restrict__ nw,
-                                                            float eps, int M, int H, const float *logits_in,
+                                                            float eps, int M, int H, const float *logits_in, int lg_ld,
                                                             const uint16_t *__restrict__ Wr, float *logits_buf, int E,
                                                             int K, int renorm, uint16_t *xn_hi, uint16_t *xn_lo,
                                                             int *idx, float *wt) {
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(256) pf_norm_route_kernel(const float *__restr
     }
     const float *lg;
     if (logits_in) {
-        lg = logits_in + (size_t)s * E;
+        lg = logits_in + (size_t)s * lg_ld;
     } else {
         // router scores in F32 from the normalised row (ds_linear_nobias_bf16)
         float *out = logits_buf + (size_t)s * E;
@@ -539,7 +539,8 @@ static int pf_route(ds_cuda_ctx *c, const PfShape &g, const float *d_norm, const
     if (rc < 0) return rc;
     if (!d_logits) PF_GROW(w->logits, w->c_logits, (size_t)M * g.E * 4);
     mark(c, 0, st);
-    pf_norm_route_kernel<<<(M + 7) / 8, 256, 0, st>>>(d_x, d_norm, g.eps, M, g.H, d_logits, d_router, w->logits,
+    pf_norm_route_kernel<<<(M + 7) / 8, 256, 0, st>>>(d_x, d_norm, g.eps, M, g.H, d_logits,
+                                                      g.logits_ld ? g.logits_ld : g.E, d_router, w->logits,
                                                       g.E, g.K, c->renorm, xn_hi, xn_lo, idx, wt);
     return DS_CUDA_OK;
 }

@@ -8,6 +8,7 @@
 struct PfShape {
     int H, I, S, E, K;
     float eps;
+    int logits_ld = 0;  // row stride of caller-supplied logits (0: E)
 };
 
 // One MoE prefill layer on device buffers: d_x [M x H] += MoE(RMSNorm(d_x)).

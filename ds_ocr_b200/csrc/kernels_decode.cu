@@ -203,7 +203,7 @@ __device__ __forceinline__ float block_sum256(float v, float *buf) {
 // launches chained with programmatic dependent launch).
 // SWA: V3's reference sliding window (a separate instantiation, so the
 // full-causal kernels keep their registers).
-template <int CL, bool PRE, bool SWA = false>
+template <int CL, bool PRE, bool SWA = false, int KPG = ATT_KPG>
 __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     __shared__ float sc_own[CL > 1 ? ATT_MAXK / CL : 1];
     __shared__ float wts[ATT_MAXK];
@@ -251,10 +251,10 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
             if (ls < r1) prefetch_range(vlo + (size_t)ls * ATT_HD, (size_t)(r1 - ls) * ATT_HD * 2);
         }
     }
-    Row16 kraw0[ATT_KPG], vraw[ATT_KPG];
+    Row16 kraw0[KPG], vraw[KPG];
     if constexpr (PRE) {
 #pragma unroll
-        for (int r = 0; r < ATT_KPG; r++) {
+        for (int r = 0; r < KPG; r++) {
             const int j = j0 + g + 32 * r;
             const bool old = j < j1 && j < n - 1;
             kraw0[r] = old ? load_raw16(khi + (size_t)row(j) * ATT_HD + li * 16, klo + (size_t)row(j) * ATT_HD + li * 16,
@@ -269,7 +269,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     pdl_launch();
     if constexpr (PRE) {
 #pragma unroll
-        for (int r = 0; r < ATT_KPG; r++) {
+        for (int r = 0; r < KPG; r++) {
             const int j = j0 + g + 32 * r;
             if (j == n - 1 && j < j1) {  // the newest row, written by the predecessor
                 kraw0[r] = load_raw16(khi + (size_t)row(j) * ATT_HD + li * 16, klo + (size_t)row(j) * ATT_HD + li * 16, true);
@@ -286,13 +286,13 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
             qf[4 * i] = v.x; qf[4 * i + 1] = v.y; qf[4 * i + 2] = v.z; qf[4 * i + 3] = v.w;
         }
     }
-    // 1. scores of this CTA's keys: 8 lanes per key, ATT_KPG keys per lane
+    // 1. scores of this CTA's keys: 8 lanes per key, KPG keys per lane
     //    group per block (all their K loads in flight together); the first
     //    block's K and V rows were loaded above (V kept for step 5)
-    for (int jb = j0, blk = 0; jb < j1; jb += 32 * ATT_KPG, blk++) {
-        Row16 kraw[ATT_KPG];
+    for (int jb = j0, blk = 0; jb < j1; jb += 32 * KPG, blk++) {
+        Row16 kraw[KPG];
 #pragma unroll
-        for (int r = 0; r < ATT_KPG; r++) {
+        for (int r = 0; r < KPG; r++) {
             int j = jb + g + 32 * r;
             if (PRE && blk == 0) kraw[r] = kraw0[r];
             else
@@ -302,7 +302,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
         }
         if (!PRE && blk == 0) {
 #pragma unroll
-            for (int r = 0; r < ATT_KPG; r++) {
+            for (int r = 0; r < KPG; r++) {
                 int j = jb + g + 32 * r;
                 vraw[r] = j < j1 ? load_raw16(vhi + (size_t)row(j) * ATT_HD + li * 16, vlo + (size_t)row(j) * ATT_HD + li * 16,
                                               row(j) >= lo_start)
@@ -310,7 +310,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
             }
         }
 #pragma unroll
-        for (int r = 0; r < ATT_KPG; r++) {
+        for (int r = 0; r < KPG; r++) {
             int j = jb + g + 32 * r;
             float kf[16];
             raw_to_f32(kraw[r], kf);
@@ -371,10 +371,10 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     float acc[16];
 #pragma unroll
     for (int i = 0; i < 16; i++) acc[i] = 0.f;
-    for (int jb = j0, blk = 0; jb < j1; jb += 32 * ATT_KPG, blk++) {
-        Row16 vr[ATT_KPG];
+    for (int jb = j0, blk = 0; jb < j1; jb += 32 * KPG, blk++) {
+        Row16 vr[KPG];
 #pragma unroll
-        for (int r = 0; r < ATT_KPG; r++) {
+        for (int r = 0; r < KPG; r++) {
             int j = jb + g + 32 * r;
             if (blk == 0) vr[r] = vraw[r];
             else vr[r] = j < j1 ? load_raw16(vhi + (size_t)row(j) * ATT_HD + li * 16, vlo + (size_t)row(j) * ATT_HD + li * 16,
@@ -382,7 +382,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
                                 : Row16{};
         }
 #pragma unroll
-        for (int r = 0; r < ATT_KPG; r++) {
+        for (int r = 0; r < KPG; r++) {
             int j = jb + g + 32 * r;
             if (j < j1) {
                 float vf[16];
@@ -423,7 +423,9 @@ __global__ void __cluster_dims__(ATT_CL, 1, 1) __launch_bounds__(256) attn_decod
     attn_body<ATT_CL, true, SWA>(a);
 }
 // many streams: one CTA per (head, stream) over all of the stream's keys
-__global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn_body<1, false>(a); }
+// (two keys in flight per lane group: the 2-CTA-per-SM register budget holds
+// without spills)
+__global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn_body<1, false, false, 2>(a); }
 
 // ---------------------------------------------------------------------------
 // Generic row matvec with optional input RMSNorm, bias and residual:

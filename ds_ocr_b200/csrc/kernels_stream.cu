@@ -4,17 +4,18 @@
 // of bytes in flight per SM. Register-held loads cap that at roughly
 // (warps x loads per lane x 16 B); here one producer thread per CTA keeps a
 // ring of shared-memory stages filled with cp.async.bulk copies (completion
-// tracked by mbarriers) while 8 consumer warps compute from shared memory,
-// so each SM keeps ~100-140 KB of weights in flight independent of
-// registers. The CTA owns a contiguous range of row tiles, so the DRAM
+// tracked by mbarriers) while 16 consumer warps compute from shared memory,
+// so each SM keeps ~100-200 KB of weights in flight independent of
+// registers (16 consumers: the per-row wait/dot/reduce chains of 8 were the
+// limit at 0.71 of the copy bandwidth). The CTA owns a contiguous range of row tiles, so the DRAM
 // stream of each SM is sequential.
 #include "kernels_moe.cuh"
 #include "launch.h"
 
 namespace ds {
 
-constexpr int ST_ROWS = 8;        // rows per tile (one per consumer warp)
-constexpr int ST_CONSUMERS = 8;   // consumer warps
+constexpr int ST_ROWS = 16;       // rows per tile (one per consumer warp)
+constexpr int ST_CONSUMERS = 16;  // consumer warps
 constexpr int ST_THREADS = 32 * (ST_CONSUMERS + 1);
 constexpr int ST_SMEM_BUDGET = 200 * 1024;
 

@@ -934,6 +934,8 @@ static int pf_weights(ds_cuda_ctx *c, DecoderModel *m) {
         }
         m->pf_router.push_back(rt);
     }
+    // the copies ran on the context's stream; a prefill may run on another
+    CKL(cudaStreamSynchronize(st), "prefill weights");
     return DS_CUDA_OK;
 }
 
@@ -941,7 +943,8 @@ static int pf_workspace(ds_cuda_ctx *c, DecoderModel *m, int T) {
     if (T <= m->pf_cap) return DS_CUDA_OK;
     void *old[] = {m->pf_x, m->pf_qkv, m->pf_q, m->pf_att, m->pf_y, m->pf_ahi, m->pf_alo, m->pf_hhi, m->pf_hlo,
                    m->pf_lg};
-    CKL(cudaStreamSynchronize(c->stream), "prefill workspace");
+    // an earlier prefill may still be using the old buffers, on any stream
+    CKL(cudaDeviceSynchronize(), "prefill workspace");
     for (void *p : old) cudaFree(p);
     const auto &g = m->cfg;
     const size_t n = (size_t)T, H = g.hidden, QD = (size_t)g.n_heads * g.head_dim, Dp = m->pf_dpad;

@@ -46,3 +46,21 @@ def test_synth_is_counter_based():
     e = np.empty(1000, np.float32)
     synth.fill_f32_bf16exact(e, 3)
     assert np.all((e.view(np.uint32) & 0xFFFF) == 0)
+
+
+def test_widened_entry_points_reject_a_missing_context():
+    # sampling, history, uniforms, window, embeddings, prefill, KV readback
+    # and checkpoint ingest: a NULL context is an error status, not a crash
+    lib = _lib.load()
+    x = np.zeros(1280, np.float32)
+    t = np.zeros(4, np.int32)
+    assert lib.ds_cuda_decoder_set_sampling(None, 1, 1.2, 3, 0.0) < 0
+    assert lib.ds_cuda_decoder_set_history(None, 1, t.ctypes.data, 4) < 0
+    assert lib.ds_cuda_decoder_get_history(None, 1, t.ctypes.data, 4) < 0
+    assert lib.ds_cuda_decoder_set_uniforms(None, 1, x.ctypes.data, 4) < 0
+    assert lib.ds_cuda_decoder_set_window(None, 1, 8, 16) < 0
+    assert lib.ds_cuda_decoder_set_embeddings(None, 1, x.ctypes.data) < 0
+    assert lib.ds_cuda_decoder_prefill(None, 1, x.ctypes.data, 1, None, None) < 0
+    assert lib.ds_cuda_decoder_prefill_dev(None, 1, x.ctypes.data, 1, None) < 0
+    assert lib.ds_cuda_decoder_get_kv(None, 1, 0, 0, 1, x.ctypes.data, x.ctypes.data) < 0
+    assert lib.ds_cuda_decoder_create_from_safetensors(None, b"/nonexistent", None) < 0

@@ -64,3 +64,34 @@ def test_widened_entry_points_reject_a_missing_context():
     assert lib.ds_cuda_decoder_prefill_dev(None, 1, x.ctypes.data, 1, None) < 0
     assert lib.ds_cuda_decoder_get_kv(None, 1, 0, 0, 1, x.ctypes.data, x.ctypes.data) < 0
     assert lib.ds_cuda_decoder_create_from_safetensors(None, b"/nonexistent", None) < 0
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    # the boundary is a C ABI: a C host includes the header, links the
+    # library and gets error statuses (not crashes) without a device
+    import os
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = tmp_path / "host.c"
+    src.write_text(
+        '#include <stdio.h>\n#include "ds_cuda.h"\n'
+        "int main(void) {\n"
+        "    ds_cuda_ctx_t *c = ds_cuda_init(0);\n"
+        "    ds_cuda_decoder_config_t cfg = {0};\n"
+        "    int rc = ds_cuda_decoder_create_from_safetensors(c, \"/nonexistent\", &cfg);\n"
+        "    printf(\"%d %d\\n\", c != 0, rc < 0);\n"
+        "    if (c) ds_cuda_free(c);\n"
+        "    return 0;\n"
+        "}\n")
+    lib_dir = os.path.dirname(_lib.LIB_PATH)
+    exe = tmp_path / "host"
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(root, "include"), str(src),
+                        "-o", str(exe), "-L", lib_dir, "-l:" + os.path.basename(_lib.LIB_PATH),
+                        "-Wl,-rpath," + lib_dir], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    has_ctx, failed = out.stdout.split()
+    assert failed == "1"
+    if not HAS_GPU:
+        assert has_ctx == "0"

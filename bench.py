@@ -734,6 +734,11 @@ def run_ours_prefill(args, rank, world, pg, model):
         ev1.synchronize()
     pf.check()
     ms_max = max_over_ranks(ev0.elapsed_time(ev1), pg)
+    # expert-parallel: (row, expert) pairs each rank computed, max / mean
+    ep_load = None
+    if ep is not None:
+        pairs, imbalance = ep.load()
+        ep_load = {"pairs_per_rank": pairs, "imbalance_max_over_mean": imbalance}
     # one GPU: 3328 tokens per step; expert-parallel: the same 3328 tokens
     # split over the ranks (strong scaling)
     value = PF_TOKENS * args.steps / (ms_max / 1e3)
@@ -811,6 +816,8 @@ def run_ours_prefill(args, rank, world, pg, model):
                           "stage_us": dict(zip(["norm_route", "plan", "scatter", "gemm_gate_up", "gemm_down",
                                                 "combine"], [round(float(s) * 1e3, 1) for s in stages]))},
     }
+    if ep_load is not None:
+        res["ep_load"] = ep_load
     # torch tensors used on the context's stream go before the stream does
     del dx, dx0, dlg, ep
     import gc
@@ -1053,7 +1060,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "dtype": res["dtype"],
             "config": res["config"], "e2e": res["e2e"], "roofline": res["roofline"], "clocks": res["clocks"],
             "gpu_launches": res["gpu_launches"]}
-    for k in ("step_roofline", "batch1"):
+    for k in ("step_roofline", "batch1", "ep_load"):
         if k in res:
             line[k] = res[k]
     line.update(common)

@@ -147,6 +147,7 @@ class ExpertParallelPrefill:
         if d.n_experts % world:
             raise ValueError(f"{d.n_experts} experts do not split over {world} ranks")
         self.e_per = d.n_experts // world
+        self.pairs_done = 0  # (row, expert) pairs this rank's experts computed
 
     def _a2a(self, send, send_counts, recv_counts):
         """all-to-all(v) along dim 0 (counts are host lists of rows)."""
@@ -161,6 +162,18 @@ class ExpertParallelPrefill:
         r = torch.empty_like(c)
         self.dist.all_to_all_single(r, c)
         return r.tolist()
+
+    def load(self):
+        """Expert work per rank since construction: the (row, expert) pairs
+        each rank computed, and the imbalance max / mean (1.0 = even).
+        Collective: every rank calls it."""
+        torch = self.torch
+        mine = torch.tensor([self.pairs_done], dtype=torch.int64, device=self.device)
+        every = [torch.empty_like(mine) for _ in range(self.world)]
+        self.dist.all_gather(every, mine)
+        pairs = [int(t.item()) for t in every]
+        mean = sum(pairs) / len(pairs)
+        return pairs, (max(pairs) / mean if mean > 0 else 1.0)
 
     def moe_layer(self, lw, x, logits):
         """x [n_local x H] F32 (this rank's tokens, updated in place);
@@ -186,6 +199,7 @@ class ExpertParallelPrefill:
         r_payload = r_payload.view(torch.int16).reshape(-1, 2 * width)
         # local experts over the received pairs; the shared expert on local rows
         pair_row, pair_expert, back_send = self.st.pairs(r_payload, recv_rows)
+        self.pairs_done += int(pair_row.shape[0])
         y, ys = self.st.experts(lw, r_payload, r_payload[:, H:], 2 * width, pair_row, pair_expert, hi, lo)
         # outputs return in request order; inv locates each (token, k)
         y_back = self._a2a(y, back_send, back_recv)

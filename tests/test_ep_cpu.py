@@ -118,7 +118,8 @@ def _rank(rank, world, port, n, q):
     ep = ExpertParallelPrefill(D, StandInStages(), dist, rank, world, torch.device("cpu"))
     xl = x[a:b].clone()
     idx, w = ep.moe_layer(None, xl, lg[a:b].contiguous())
-    q.put((rank, xl, idx))
+    pairs, imbalance = ep.load()
+    q.put((rank, xl, idx, pairs, imbalance))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -134,13 +135,20 @@ def test_two_ranks_match_one(n):
     procs = [ctx.Process(target=_rank, args=(r, 2, port, n, q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = dict()
+    got, loads = dict(), dict()
     for _ in range(2):
-        r, xl, idx = q.get(timeout=120)
+        r, xl, idx, pairs, imbalance = q.get(timeout=120)
         got[r] = xl
+        loads[r] = (pairs, imbalance)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
     out = torch.cat([got[0], got[1]])
     assert torch.equal(out, ref)
     assert not torch.equal(out, x)
+    # the load report: both ranks see the same counts, every (token, slot)
+    # pair computed exactly once, imbalance = max / mean
+    assert loads[0] == loads[1]
+    pairs, imbalance = loads[0]
+    assert sum(pairs) == n * K
+    assert imbalance == pytest.approx(max(pairs) / (sum(pairs) / 2))

@@ -1,4 +1,4 @@
-"""Generates tests/golden/golden.npz from the REFERENCE ITSELF (its own C
+"""Generates tests/golden/golden.npz and golden_widened.npz from the REFERENCE ITSELF (its own C
 sources compiled unmodified into oracle/_ref/libdsref.so; run `make -C
 oracle ref` first, which needs the reference tree).
 
@@ -19,6 +19,18 @@ import oracle as O  # noqa: E402
 from ds_ocr_b200 import synth  # noqa: E402
 
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden.npz")
+OUT_WIDENED = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_widened.npz")
+
+# selection cases of golden_widened.npz: (repeat_penalty, n-gram size,
+# temperature, history builder from the first step's top-4 tokens)
+SELECT_CASES = {
+    "penalty": (1.5, 0, 0.0, lambda t: [t[0], t[1], t[0], t[2], t[3]]),
+    "ngram_ban": (1.0, 3, 0.0, lambda t: [11, 12, t[0], 13, 14, 11, 12]),
+    "temperature": (1.2, 0, 0.8, lambda t: [t[0], t[2]]),
+}
+SWA = (8, 20, 20, 14)     # window, prefill length, KV prefix, steps
+PREFILL_T = 37
+PREFILL_ROWS = (0, 5, 36)  # K/V rows kept of every layer
 
 
 def main():
@@ -78,5 +90,70 @@ def main():
     print("wrote", OUT, os.path.getsize(OUT), "bytes")
 
 
+def _top4(model, fx):
+    lg = synth.bf16_to_f32(model.lm_head) @ fx
+    return [int(t) for t in np.argsort(-lg, kind="stable")[:4]]
+
+
+def widened():
+    """The rows added to the decode step: LM-head selection with sampling
+    settings (ds_moe_decoder.c:1021-1263), the V3 sliding window
+    (:409-436) and the whole prefill (:480-905), from the reference."""
+    import ctypes
+    r = O.ref()
+    g = {}
+    model = synth.Model(n_layers=2, vocab=4096)
+    ks, vs = synth.kv_prefix(model.d, 30)
+    probe = O.OracleDecoder(model, kv_max=64)
+    probe.load_kv(ks, vs)
+    _, fx0, _ = probe.step(model.embed(7))
+    top = _top4(model, fx0)
+    libc = ctypes.CDLL(None)
+    for name, (rp, ng, temp, hist_of) in SELECT_CASES.items():
+        R = O.RefDecoder(model, kv_max=64, threads=4)
+        R.load_kv(ks, vs)
+        R.set_sampling(rp, ng, temp)
+        R.set_history(hist_of(top))
+        libc.srand(4321)
+        us = np.array([libc.rand() / 2147483647.0 for _ in range(6)], np.float32)
+        r.ref_srand(4321)
+        e, toks = model.embed(7), []
+        for _ in range(6):
+            t = R.step_gen(e)
+            toks.append(t)
+            e = model.embed(t)
+        g[f"sel_{name}_tok"], g[f"sel_{name}_u"] = np.array(toks, np.int32), us
+        g[f"sel_{name}_hist0"] = np.array(hist_of(top), np.int32)
+        R.close()
+    W, P, prefix, steps = SWA
+    ks2, vs2 = synth.kv_prefix(model.d, prefix)
+    R = O.RefDecoder(model, kv_max=64, threads=4)
+    R.load_kv(ks2, vs2)
+    R.set_window(W, P)
+    e, toks, xs = model.embed(5), [], []
+    for _ in range(steps):
+        t, fx, _ = R.step(e)
+        toks.append(t)
+        xs.append(fx)
+        e = model.embed(t)
+    g["swa_tok"], g["swa_x_last"] = np.array(toks, np.int32), xs[-1]
+    R.close()
+    m3 = synth.Model(n_layers=3, vocab=4096)
+    R = O.RefDecoder(m3, kv_max=64, threads=4)
+    emb = np.stack([m3.embed(t) for t in (np.arange(PREFILL_T) * 37 + 11) % m3.d.vocab])
+    t, lg = R.prefill(emb)
+    g["pf_tok"], g["pf_logit"] = np.array(t, np.int32), np.array(lg, np.float32)
+    rows = list(PREFILL_ROWS)
+    g["pf_k"] = np.stack([R.kv(l, 0, PREFILL_T)[0][rows] for l in range(m3.d.n_layers)])
+    g["pf_v"] = np.stack([R.kv(l, 0, PREFILL_T)[1][rows] for l in range(m3.d.n_layers)])
+    R.close()
+    np.savez_compressed(OUT_WIDENED, **g)
+    print("wrote", OUT_WIDENED, os.path.getsize(OUT_WIDENED), "bytes")
+
+
 if __name__ == "__main__":
-    main()
+    if "--widened" in sys.argv:
+        widened()
+    else:
+        main()
+        widened()

@@ -39,6 +39,12 @@ CASES = {
     "penalty_and_ngram": (1.3, 3, 0.0, lambda t: [t[1], 12, t[0], 13, t[1], 12]),
     "temperature": (1.2, 0, 0.8, lambda t: [t[0], t[2]]),
     "temperature_ngram": (1.0, 2, 0.6, lambda t: [t[0], 5, t[0]]),
+    # n-gram size 1: every history token is banned (empty prefix matches all)
+    "ngram1": (1.0, 1, 0.0, lambda t: [t[0], t[1]]),
+    # size 2 with the winner right after the last token's earlier occurrence
+    "ngram2": (1.0, 2, 0.0, lambda t: [9, t[0], 4, 9]),
+    # a strong penalty on all top tokens: penalised positives and negatives
+    "penalty_strong": (4.0, 0, 0.0, lambda t: [t[0], t[1], t[2], t[3], 17, 18]),
 }
 
 

@@ -916,7 +916,12 @@ def run_ours_prefill_full(args, rank, world, pg, model):
         "unit": "tokens/s", "dtype": "bf16 weights, f32 activations as two bf16 planes, f32 accumulate",
         "e2e": {"value": world * T * n_e2e / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * d.hidden * 4,
                 "d2h_bytes_per_step": 8},
-        "gpu_launches": (d.n_layers * 9 + 8 * (d.n_layers - d.first_dense) + 4) * args.steps,
+        # per prefill: every layer norm/split, QKV GEMM, RoPE/KV, attention,
+        # split, O-proj GEMM, residual (7); a dense layer + norm/split, gate/up,
+        # down, residual (4); a MoE layer + router norm/split, router GEMM and
+        # route, count, plan, scatter, gate/up, down, combine (9); then the
+        # LM-head argmax, final norm, finish (3): 190 for 1 dense + 11 MoE
+        "gpu_launches": (7 * d.n_layers + 4 * d.first_dense + 9 * (d.n_layers - d.first_dense) + 3) * args.steps,
         "config": dict(prefill_full_config(T), parallelism=f"replicas on {world} GPU(s)"),
         "roofline": {"bound": "tensor", "achieved": ach, "peak": peak_t, "unit": "TFLOP/s", "frac": ach / peak_t,
                      "traffic": None, "kernel": "whole prefill step (algorithmic FLOPs of every GEMM and the "

@@ -488,11 +488,12 @@ def run_ours_decode_streams(args, rank, world, pg, model, prefixes):
         "metric": "decode tokens/s (greedy, 64 independent streams, 12-layer DeepSeek3B-MoE, 662-token KV prefixes)",
         "unit": "tokens/s", "dtype": "bf16 weights + bf16 KV, f32 activations as two bf16 planes, f32 accumulate",
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": S * 4},
-        # per step: 7 per layer (norms, QKV, RoPE/KV, attention, O-proj), 2 per
-        # dense FFN, 8 per MoE layer (router, top-k, count, plan, scatter,
-        # gate/up, down, combine), 4 for the final norm, LM head and advance
+        # per step: 7 per layer (3 norm/split passes, QKV, RoPE/KV, attention,
+        # O-proj), 2 per dense FFN, 8 per MoE layer (router, top-k, count,
+        # plan, scatter, gate/up, down, combine), 3 for the final norm, LM
+        # head and advance (177 per step, as in the ncu launch list)
         "gpu_launches": (7 * model.d.n_layers + 2 * model.d.first_dense
-                         + 8 * (model.d.n_layers - model.d.first_dense) + 4) * args.steps,
+                         + 8 * (model.d.n_layers - model.d.first_dense) + 3) * args.steps,
         "config": dict(decode_config(kv_max), workload="config3_decode_64_streams", global_batch=MS_STREAMS,
                        streams_per_gpu=S, parallelism=f"sharded by stream over {world} GPU(s)"),
         "roofline": {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -802,7 +803,10 @@ def run_ours_prefill(args, rank, world, pg, model):
         "metric": "MoE prefill tokens/s (3328 tokens x 11 MoE layers, 64 experts top-6 + 2 shared)",
         "unit": "tokens/s", "dtype": "bf16 weights, f32 activations as two bf16 planes, f32 accumulate",
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": 6 * n_layers * args.steps,
+        # per layer: norm/route, count, plan, scatter, gate/up, down, combine
+        # (7); expert-parallel adds the dispatch plan, row packing and pair
+        # compaction (10)
+        "gpu_launches": (7 if world == 1 else 10) * n_layers * args.steps,
         "config": dict(prefill_config(n_layers), parallelism=f"ep{world}" if world > 1 else "single GPU",
                        tokens_per_rank=b - a),
         "scaling": "strong" if world > 1 else "weak",

@@ -137,3 +137,22 @@ def test_int8_moe_and_prefill(small_model):
         i2, w2 = D.prefill_moe(1, xo, logits)
         assert np.array_equal(i1, i2)
         assert rel_l2(xo - xp, xr - xp) < 1e-5
+
+
+def test_full_size_decode_steps():
+    # the benchmark's shapes: 12 layers (dense layer 0 + 11 MoE), vocab
+    # 129280, 662-token BF16 KV prefix, three greedy steps
+    model = synth.Model()
+    R = O.RefDecoder(model, kv_max=700, threads=8)
+    D = O.OracleDecoder(model, kv_max=700)
+    ks, vs = synth.kv_prefix(model.d, 662)
+    R.load_kv(ks, vs)
+    D.load_kv(ks, vs)
+    e = model.embed(1)
+    for _ in range(3):
+        rt, rx, rl = R.step(e)
+        ot, ox, ol = D.step(e)
+        assert rel_l2(ox, rx) < 1e-4
+        assert rt == ot
+        e = model.embed(rt)
+    R.close()

@@ -534,6 +534,35 @@ def ref_decode_time(model, ks, vs, threads, budget_s, max_steps, sampling=(1.0, 
     return n / t_total, n
 
 
+_STREAM_MODEL = None  # shared with forked reference processes (copy-on-write)
+
+
+def _ref_stream(args):
+    threads, budget_s, max_steps, stream = args
+    from ds_ocr_b200 import synth
+    ks, vs = synth.kv_prefix(_STREAM_MODEL.d, PREFIX, stream=stream)
+    return ref_decode_time(_STREAM_MODEL, ks, vs, threads, budget_s, max_steps)
+
+
+def ref_decode_streams_time(model, threads, budget_s, max_steps):
+    """The reference decodes streams one at a time per context; its
+    multi-stream aggregate is floor(nproc / threads) concurrent processes,
+    one stream each (stream s's own KV prefix). Returns (aggregate tokens/s,
+    steps per process, processes). Forks: call only from a process without
+    a CUDA context."""
+    import multiprocessing as mp
+    global _STREAM_MODEL
+    n_proc = max(1, (os.cpu_count() or 1) // threads)
+    _STREAM_MODEL = model
+    jobs = [(threads, budget_s, max_steps, s) for s in range(n_proc)]
+    if n_proc == 1:
+        v, n = _ref_stream(jobs[0])
+        return v, n, 1
+    with mp.get_context("fork").Pool(n_proc) as pool:
+        res = pool.map(_ref_stream, jobs)
+    return sum(v for v, _ in res), min(n for _, n in res), n_proc
+
+
 # ---------------------------------------------------------------------------
 # Argmax LM head (config 1), batch 64 and batch 1
 # ---------------------------------------------------------------------------
@@ -1014,6 +1043,13 @@ def main():
             cfg, sample = decode_config(1024), f"{n} {decode_mode(args)} ds_decoder_forward steps from position 663"
             if decode_mode(args) != "greedy":
                 cfg["sampling"] = decode_mode(args)
+        elif args.workload == "decode64":
+            model, _, _ = build_decode_model()
+            v, n, n_proc = ref_decode_streams_time(model, T, max(args.cpu_budget, 1.0), args.steps)
+            metric = "decode tokens/s (greedy, 64 independent streams, 12-layer DeepSeek3B-MoE, 662-token KV prefixes)"
+            cfg = dict(decode_config(1024), workload="config3_decode_64_streams", global_batch=MS_STREAMS)
+            sample = (f"{n_proc} concurrent reference processes of {T} threads, one stream each "
+                      f"(the reference decodes one stream per context), {n} ds_decoder_forward steps each")
         elif args.workload == "lm_head":
             v, n = ref_lmhead_time(T, max(args.cpu_budget, 1.0))
             metric = "argmax LM head tokens/s (batch 64, vocab 129280 x 1280 BF16)"

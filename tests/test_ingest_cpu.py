@@ -103,3 +103,35 @@ def test_missing_directory_fails(tmp_path):
     lib = _lib.load()
     assert lib.ds_cuda_safetensors_count(str(tmp_path / "none").encode()) < 0
     assert b"cannot open" in lib.ds_cuda_safetensors_error()
+
+
+def test_parser_survives_mutated_files(tmp_path):
+    # truncated, bit-flipped and length-corrupted files: the parser returns
+    # a status (a count or < 0), never crashes or reads past the file
+    from hypothesis import given, settings, strategies as st
+
+    lib = _lib.load()
+    base = str(tmp_path / "base.safetensors")
+    write_safetensors(base, {"a": ("F32", np.arange(12, dtype=np.float32).reshape(3, 4)),
+                             "b.c": ("BF16", np.arange(8, dtype=np.uint16)),
+                             "z": ("I64", np.arange(2, dtype=np.int64))}, metadata={"k": "v"})
+    good = open(base, "rb").read()
+    p = str(tmp_path / "mut.safetensors")
+
+    @settings(max_examples=300, deadline=None)
+    @given(st.integers(0, len(good)), st.lists(st.tuples(st.integers(0, len(good) - 1), st.integers(0, 255)),
+                                               max_size=6), st.integers(0, 3))
+    def check(cut, flips, length_mode):
+        raw = bytearray(good[:max(cut, 0)] if cut < len(good) else good)
+        for pos, val in flips:
+            if pos < len(raw):
+                raw[pos] = val
+        if length_mode == 1 and len(raw) >= 8:
+            raw[:8] = np.uint64(2**63 - 1).tobytes()
+        elif length_mode == 2 and len(raw) >= 8:
+            raw[:8] = np.uint64(0).tobytes()
+        open(p, "wb").write(bytes(raw))
+        r = lib.ds_cuda_safetensors_count(p.encode())
+        assert r < 0 or 0 <= r <= 3 + 16
+
+    check()

@@ -1034,6 +1034,10 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
+        # the reference arm draws the same synthetic weights through the numpy
+        # restatement of the generator: this process maps no library of ours
+        from ds_ocr_b200 import synth
+        synth.use_numpy_backend(True)
         if args.workload == "decode":
             model, ks, vs = build_decode_model()
             v, n = ref_decode_time(model, ks, vs, T, max(args.cpu_budget, 1.0), max_steps=args.steps,

@@ -10,6 +10,7 @@
 // its one scratch buffer (the SwiGLU activations between the two kernels) in
 // the file-scope array below, which every GPU that loads this library holds
 // until the process exits.
+#include <atomic>
 #include <cstdio>
 
 #include "ds_cuda.h"
@@ -17,14 +18,18 @@
 
 using namespace ds;
 
-// Largest top_k * inter the scratch holds (8 experts of 2048 = 64 KB).
-constexpr int NOALLOC_MAX_H = 8 * 2048;
+// Largest top_k * inter the scratch holds: 12288 floats (48 KB), enough for
+// the decoder's 6 routed experts of up to 2048 rows each. The kernels alone
+// accept top_k <= 8 and inter <= 2048, so 8 experts of inter > 1536 are
+// refused by this bound.
+constexpr int NOALLOC_MAX_H = 12288;
 
 static __device__ __align__(256) float g_noalloc_h[NOALLOC_MAX_H];
 
 // Device address of g_noalloc_h per device, resolved on the first call made
-// with that device current (the host-side name is only a stand-in).
-static float *g_noalloc_ptr[64];
+// with that device current (the host-side name is only a stand-in). Atomic:
+// host threads making their first calls at once each store the same value.
+static std::atomic<float *> g_noalloc_ptr[64];
 
 static int noalloc_fail(int code, const char *msg) {
     fprintf(stderr, "ds_cuda_moe_experts_noalloc: %s\n", msg);
@@ -39,15 +44,17 @@ extern "C" int ds_cuda_moe_experts_noalloc(const float *d_x, const uint16_t *con
     if (top_k > 8 || inter <= 0 || inter % 8 || inter > 2048 || hidden <= 0 || hidden % 8 || hidden > 2048)
         return noalloc_fail(DS_CUDA_EINVAL, "unsupported shape (top_k <= 8, hidden and inter multiples of 8, <= 2048)");
     if (top_k * inter > NOALLOC_MAX_H)
-        return noalloc_fail(DS_CUDA_EINVAL, "top_k * inter exceeds the 16384-float static scratch");
+        return noalloc_fail(DS_CUDA_EINVAL, "top_k * inter exceeds the 12288-float static scratch");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return noalloc_fail(DS_CUDA_ECUDA, "no current CUDA device (or device index >= 64)");
-    if (!g_noalloc_ptr[dev]) {
+    float *scratch = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (!scratch) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_h);
         if (e != cudaSuccess || !p) return noalloc_fail(DS_CUDA_ECUDA, cudaGetErrorString(e));
-        g_noalloc_ptr[dev] = (float *)p;
+        scratch = (float *)p;
+        g_noalloc_ptr[dev].store(scratch, std::memory_order_release);
     }
     MoeArgs a = {};
     a.hidden = hidden;
@@ -60,7 +67,7 @@ extern "C" int ds_cuda_moe_experts_noalloc(const float *d_x, const uint16_t *con
         a.wt[k] = top_weights[k];
     }
     a.x = d_x;
-    a.h = g_noalloc_ptr[dev];  // fully written by gate_up before down reads it: nothing to clear
+    a.h = scratch;  // fully written by gate_up before down reads it: nothing to clear
     a.out = d_output;
     a.out_mode = 0;
     cudaStream_t st = (cudaStream_t)stream;

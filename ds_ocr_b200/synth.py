@@ -6,9 +6,15 @@ matrices, F32 RMSNorm weights of 1.0, F32 N(0, 1) activations, and (for the
 decode benchmark) a prefilled KV cache whose values are BF16-representable
 N(0, 1). Values come from the counter-based generator in csrc/synth.c, so a
 (seed, index) pair always yields the same number on any machine.
+
+The same generator is restated in numpy below (`use_numpy_backend`). The
+reference arm of the benchmark draws its weights with it, so that process
+maps no library of this package: it runs the reference and nothing else.
 """
 import ctypes
+import os
 import zlib
+from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
@@ -40,18 +46,83 @@ def _addr(a):
     return a.ctypes.data
 
 
+_NUMPY = False
+
+
+def use_numpy_backend(on=True):
+    """Draw every tensor with the numpy restatement of csrc/synth.c instead of
+    the compiled generator (same values; slower, and loads no library)."""
+    global _NUMPY
+    _NUMPY = bool(on)
+
+
+_U = np.uint64
+
+
+def _splitmix64(z):
+    z = z + _U(0x9E3779B97F4A7C15)
+    z = (z ^ (z >> _U(30))) * _U(0xBF58476D1CE4E5B9)
+    z = (z ^ (z >> _U(27))) * _U(0x94D049BB133111EB)
+    return z ^ (z >> _U(31))
+
+
+def _np_chunk(out, lo, hi, seed, mean, std, kind):
+    with np.errstate(over="ignore"):
+        k = _splitmix64(np.array([seed], _U) * _U(0xD1B54A32D192ED03) + _U(0x8CB92BA72F3D8DD7))[0]
+        i2 = np.arange(lo, hi, dtype=_U) * _U(2)
+        a = _splitmix64(k ^ i2)
+        b = _splitmix64(k ^ (i2 + _U(1)))
+    u1 = ((a >> _U(11)).astype(np.float64) + 0.5) * (1.0 / 9007199254740992.0)
+    u2 = ((b >> _U(11)).astype(np.float64) + 0.5) * (1.0 / 9007199254740992.0)
+    # mean and std are F32 in the C generator, widened to double
+    v = (float(np.float32(mean)) + float(np.float32(std))
+         * (np.sqrt(-2.0 * np.log(u1)) * np.cos(6.283185307179586 * u2))).astype(np.float32)
+    flat = out.reshape(-1)
+    if kind == 1:
+        flat[lo:hi] = v
+        return
+    u = v.view(np.uint32)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + (0x7FFF + ((u >> 16) & 1))) >> 16).astype(np.uint16)
+    r = np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+    if kind == 0:
+        flat[lo:hi] = r
+    else:
+        flat[lo:hi] = (r.astype(np.uint32) << 16).view(np.float32)
+
+
+def _np_fill(out, seed, mean, std, kind):
+    n = out.size
+    step = 1 << 22
+    if n <= step:
+        _np_chunk(out, 0, n, seed, mean, std, kind)
+        return
+    workers = max(1, min(32, os.cpu_count() or 1))
+    with ThreadPoolExecutor(workers) as ex:
+        list(ex.map(lambda lo: _np_chunk(out, lo, min(n, lo + step), seed, mean, std, kind), range(0, n, step)))
+
+
 def fill_bf16(out, seed, std=0.02, mean=0.0):
-    _lib.load().ds_synth_normal_bf16(_addr(out), out.size, seed, mean, std)
+    if _NUMPY:
+        _np_fill(out, seed, mean, std, 0)
+    else:
+        _lib.load().ds_synth_normal_bf16(_addr(out), out.size, seed, mean, std)
     return out
 
 
 def fill_f32(out, seed, std=1.0, mean=0.0):
-    _lib.load().ds_synth_normal_f32(_addr(out), out.size, seed, mean, std)
+    if _NUMPY:
+        _np_fill(out, seed, mean, std, 1)
+    else:
+        _lib.load().ds_synth_normal_f32(_addr(out), out.size, seed, mean, std)
     return out
 
 
 def fill_f32_bf16exact(out, seed, std=1.0, mean=0.0):
-    _lib.load().ds_synth_normal_f32_bf16exact(_addr(out), out.size, seed, mean, std)
+    if _NUMPY:
+        _np_fill(out, seed, mean, std, 2)
+    else:
+        _lib.load().ds_synth_normal_f32_bf16exact(_addr(out), out.size, seed, mean, std)
     return out
 
 

@@ -196,10 +196,10 @@ int ds_cuda_moe_layer_dev(ds_cuda_ctx_t *ctx, const float *d_x, float *d_out,
  * fixed after start-up. It creates no context and allocates nothing: x,
  * the weights and output are DEVICE pointers the caller owns (gate-up and
  * down are host arrays of top_k device pointers; top_weights is a host
- * array), and the SwiGLU activations live in a static 64 KB device array
+ * array), and the SwiGLU activations live in a static 48 KB device array
  * the library holds on every GPU that loads it until the process exits.
  * Limits: top_k <= 8, hidden and inter multiples of 8 and <= 2048,
- * top_k * inter <= 16384; larger sizes return DS_CUDA_EINVAL with a message
+ * top_k * inter <= 12288 (the scratch); larger sizes return DS_CUDA_EINVAL with a message
  * on stderr. Work is enqueued on `stream` (NULL = the legacy default stream)
  * of the current device. The first call on a device looks up the array's
  * device address; make that first call before any stream capture. All
@@ -215,8 +215,8 @@ int ds_cuda_moe_experts_noalloc(const float *d_x, const uint16_t *const *d_gate_
  * with the KV cache resident in HBM. One call = input RMSNorm, QKV, RoPE,
  * KV append, attention, O-proj + residual, post-attention RMSNorm, dense
  * FFN (layer < first_dense) or MoE, residual, for every layer; final
- * RMSNorm; argmax LM head. The step is one CUDA graph of ~85 kernels
- * chained with programmatic dependent launch.
+ * RMSNorm; argmax LM head. Engine 0 runs the step as one CUDA graph of
+ * per-phase kernels chained with programmatic dependent launch.
  * --------------------------------------------------------------------- */
 typedef struct {
     int hidden, n_layers, n_heads, head_dim; /* head_dim must be 128 */

@@ -22,9 +22,24 @@ def build_oracle():
     subprocess.check_call(["make", "-s", "-C", HERE, "liboracle.so"])
 
 
-def build_ref(ref_dir="/root/reference"):
+def reference_dir():
+    """Where the reference's source tree lies: $DS_REFERENCE_DIR, else the
+    `reference_path` that BASELINE.json at the repo root names, else None."""
+    d = os.environ.get("DS_REFERENCE_DIR")
+    if d:
+        return d
+    try:
+        import json
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+            return json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
+
+
+def build_ref(ref_dir=None):
     """Compile the reference from its own sources (needs the reference tree)."""
-    if not os.path.isdir(ref_dir):
+    ref_dir = ref_dir or reference_dir()
+    if not ref_dir or not os.path.isdir(ref_dir):
         return False
     subprocess.check_call(["make", "-s", "-C", HERE, "ref", f"REF={ref_dir}"])
     return True

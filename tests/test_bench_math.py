@@ -49,3 +49,20 @@ def test_prefill_flops():
     assert whole == D.n_layers * (proj + attn) + D.first_dense * dense + (D.n_layers - D.first_dense) * moe \
         + 2 * V * H
     assert 2.0e12 < whole < 3.5e12
+
+
+def test_synth_numpy_backend_matches_native():
+    """The numpy restatement of the generator (used by the reference arm so
+    that it maps no library of this package) gives the same bits."""
+    import numpy as np
+    from ds_ocr_b200 import synth
+    try:
+        for fn, dt, n in ((synth.fill_bf16, np.uint16, 5_000_011), (synth.fill_f32, np.float32, 4097),
+                          (synth.fill_f32_bf16exact, np.float32, 70_001)):
+            synth.use_numpy_backend(False)
+            a = fn(np.empty(n, dt), synth.seed_of("t", n), 0.3, 0.1)
+            synth.use_numpy_backend(True)
+            b = fn(np.empty(n, dt), synth.seed_of("t", n), 0.3, 0.1)
+            assert np.array_equal(a.view(np.uint8), b.view(np.uint8))
+    finally:
+        synth.use_numpy_backend(False)

@@ -77,7 +77,9 @@ def test_int8_matvec_bit_exact(orc):
     y1, y2 = np.empty(300, np.float32), np.empty(300, np.float32)
     orc.orc_int8_matvec(y1.ctypes.data, x.ctypes.data, q.ctypes.data, s.ctypes.data, o.ctypes.data, 300, 1280)
     r.ref_int8_matvec(y2.ctypes.data, x.ctypes.data, q.ctypes.data, s.ctypes.data, o.ctypes.data, 300, 1280)
-    assert rel_l2(y1, y2) < 1e-6
+    # the oracle follows the compiled reference's operation order (unfused
+    # product-add in the dot, fused tail), so every output bit agrees
+    assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
 
 
 @pytest.fixture(scope="module")
@@ -127,7 +129,9 @@ def test_int8_moe_and_prefill(small_model):
     ro = R.moe_forward(1, x)
     oo, _, _ = D.moe_forward(1, x, use_int8=True)
     assert rel_l2(oo, ro) < 1e-5
-    assert rel_l2(ro, bf) < 0.05  # INT8 vs BF16 (reference's own quantisation error)
+    # INT8 against BF16: the reference's own test bar for the INT8 matvec
+    # (test_int4.c:84, relative error < 0.02); measured ~0.013 on this layer
+    assert rel_l2(ro, bf) < 0.02
     small_model.layers[1].moe.int8 = None
     xp = synth.normal_f32((48, 1280), 78)
     lg = synth.normal_f32((48, 64), 79)

@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 H, I = 1280, 896
 
 
-def test_noalloc_matches_moe_experts():
+def test_noalloc_matches_moe_experts(orc):
     import torch
     ctx = cuda.Context(0)
     lib = ctx.lib
@@ -42,8 +42,22 @@ def test_noalloc_matches_moe_experts():
             assert rc == 0, f"call {call}"
             torch.cuda.synchronize()
             assert rel_l2(tout.cpu().numpy(), ref) < 1e-6, f"call {call}"
-        # sizes beyond the static scratch are refused
-        assert lib.ds_cuda_moe_experts_noalloc(tx.data_ptr(), dgu, ddn, w.ctypes.data, 8, H, 2056,
+            # and against the CPU oracle: sum_k w_k * ds_expert_forward_fused
+            # (ds_kernels.c:322-357, combine :359-371)
+            want = np.zeros(H, np.float32)
+            y = np.empty(H, np.float32)
+            for g, d, wk in zip(gus, dns, w):
+                orc.orc_expert_fused(y.ctypes.data, x.ctypes.data, g.ctypes.data, d.ctypes.data, H, I, 0)
+                want += np.float32(wk) * y
+            assert rel_l2(tout.cpu().numpy(), want) < 1e-5, f"call {call}"
+        # 8 experts of 1792 rows pass the per-argument limits but need 14336
+        # floats of scratch: refused by the 12288-float bound
+        assert lib.ds_cuda_moe_experts_noalloc(tx.data_ptr(), dgu, ddn, w.ctypes.data, 8, H, 1792,
+                                               tout.data_ptr(), None) < 0
+        # per-argument limits: inter beyond 2048, top_k beyond 8
+        assert lib.ds_cuda_moe_experts_noalloc(tx.data_ptr(), dgu, ddn, w.ctypes.data, 1, H, 2056,
+                                               tout.data_ptr(), None) < 0
+        assert lib.ds_cuda_moe_experts_noalloc(tx.data_ptr(), dgu, ddn, w.ctypes.data, 9, H, 8,
                                                tout.data_ptr(), None) < 0
     finally:
         ctx.close()

@@ -44,11 +44,21 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// 16-byte streaming load that bypasses L1 (weights are read once per step).
+// L2 policy for data read once per step (weights, KV rows): evicted first,
+// so the step's streams do not push the small, reused data (activations,
+// router terms, kernel code) out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// 16-byte streaming load that bypasses L1 and is evicted first from L2
+// (weights are read once per step).
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p), "l"(l2_evict_first()));
     return r;
 }
 __device__ __forceinline__ uint2 ldg_stream8(const void *p) {
@@ -77,6 +87,65 @@ __device__ __forceinline__ float ubyte_f(uint32_t w, int b) {
     uint32_t v = __byte_perm(w, 0x4B000000u, 0x7440 + b);  // bytes: [b,4,4,7]
     return __fsub_rn(__uint_as_float(v), 8388608.0f);
 }
+
+// Optional launch trace (a debugging aid, off unless a buffer is set): each
+// instrumented kernel's CTA appends one 12-word record: kind | block << 16 |
+// sm << 40, entry time, time past the dependency wait, exit time, and up to
+// eight intermediate marks (globaltimer ns; marks are kept in registers and
+// written with the record, so they add no memory traffic while the kernel
+// runs). The buffer pointer lives per translation unit; DS_TRACE_TU(tag)
+// exports ds_trace_set_<tag>(rec, counter, capacity) to set it (NULL: off).
+struct DsTrace {
+    unsigned long long *rec;
+    unsigned *cnt;
+    unsigned cap;
+};
+static __device__ DsTrace g_ds_trace;
+__device__ __forceinline__ unsigned long long ds_gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned ds_smid() {
+    unsigned s;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(s));
+    return s;
+}
+struct TraceScope {
+    unsigned long long t0 = 0, tw = 0, m[8];
+    __device__ __forceinline__ TraceScope() {
+        if (g_ds_trace.rec) t0 = ds_gtime();
+#pragma unroll
+        for (int i = 0; i < 8; i++) m[i] = 0;
+    }
+    __device__ __forceinline__ void waited() {
+        if (t0) tw = ds_gtime();
+    }
+    __device__ __forceinline__ void mark(int i) {
+        if (t0) m[i] = ds_gtime();
+    }
+    __device__ __forceinline__ void done(int kind) {
+        if (t0 && threadIdx.x == 0) {
+            const unsigned long long t1 = ds_gtime();
+            unsigned i = atomicAdd(g_ds_trace.cnt, 1u);
+            if (i < g_ds_trace.cap) {
+                unsigned long long *r = g_ds_trace.rec + 12ull * i;
+                r[0] = (unsigned long long)kind | ((unsigned long long)blockIdx.x << 16) |
+                       ((unsigned long long)ds_smid() << 40);
+                r[1] = t0;
+                r[2] = tw;
+                r[3] = t1;
+#pragma unroll
+                for (int k = 0; k < 8; k++) r[4 + k] = m[k];
+            }
+        }
+    }
+};
+#define DS_TRACE_TU(tag)                                                                          \
+    extern "C" int ds_trace_set_##tag(void *rec, unsigned *cnt, unsigned cap) {                   \
+        ds::DsTrace t = {(unsigned long long *)rec, cnt, cap};                                    \
+        return (int)cudaMemcpyToSymbol(ds::g_ds_trace, &t, sizeof(t));                            \
+    }
 
 // Programmatic dependent launch (PDL). wait: block until the predecessor
 // grid has completed and its memory is visible. launch_dependents: allow the
@@ -145,6 +214,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+// The same for data read once per step: evicted first from L2.
+__device__ __forceinline__ void bulk_g2s_stream(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(l2_evict_first()) : "memory");
 }
 
 // F32 -> BF16 with round-to-nearest-even, as raw bits.

@@ -9,6 +9,7 @@
 #include "ctx.h"
 #include "kernels_decode.cuh"
 #include "mega.h"
+#include "moe_step.h"
 #include "prefill.h"
 
 using namespace ds;
@@ -33,8 +34,10 @@ struct DecoderModel {
     float *scores = nullptr, *wt = nullptr, *val = nullptr;
     float *rpart = nullptr;  // router terms of the O-proj CTAs (router folded into the O-proj)
     int *idx = nullptr, *pos = nullptr, *tok = nullptr, *tok_log = nullptr;
-    unsigned *tickets = nullptr;
+    unsigned *tickets = nullptr;  // [0] LM head, [1] router, [8] LM-head wait error, [9] MoE-step wait error
     unsigned long long *slot = nullptr;
+    unsigned long long *step_bar = nullptr;  // grid-barrier counter of the MoE-step kernel
+    bool fused_moe = false;                  // MoE layers run as one kernel (moe_step.cu)
     uint16_t *kv = nullptr;  // 4 planes: k_hi, k_lo, v_hi, v_lo, each [L][heads][kv_max][hd]
     float *cos_t = nullptr, *sin_t = nullptr;
     std::vector<int> lo_start;  // per layer: rows below are exact BF16
@@ -177,7 +180,8 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
         aa.out = m->attn;
         aa.swa_window = m->swa_window;
         aa.swa_ref = m->swa_ref;
-        CKL(launch_attn_decode(aa, st, pdl), "attention launch");
+        if (m->fused_moe && aa.swa_window <= 0) CKL(launch_attn_step(aa, st, pdl), "attention launch");
+        else CKL(launch_attn_decode(aa, st, pdl), "attention launch");
         MvArgs oa = {};
         oa.W = L.wo;
         oa.x = m->attn;
@@ -188,6 +192,7 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
         // MoE layers: the router rides in the O-proj (its logits are linear in
         // the O-proj output; the last CTA applies the RMS scale and the top-k)
         const bool fold = !L.dense && g.use_int8 == 0 && H % 16 == 0 && g.n_experts <= 255;
+        const bool fused = fold && m->fused_moe;
         if (fold) {
             oa.rf.Wr = L.router;
             oa.rf.g = L.post_norm;
@@ -200,9 +205,38 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             oa.rf.scores = m->scores;
             oa.rf.d_idx = m->idx;
             oa.rf.d_wt = m->wt;
+            oa.rf.no_tail = fused ? 1 : 0;
         }
         CKL(launch_matvec_res(oa, st, pdl), "o-proj launch");
         launches += 3;
+        if (fused) {
+            MoeStepArgs ms = {};
+            ms.H = H;
+            ms.I = g.moe_inter;
+            ms.S = g.n_shared * g.moe_inter;
+            ms.E = g.n_experts;
+            ms.K = g.top_k;
+            ms.simulate = c->simulate;
+            ms.renorm = c->renorm;
+            ms.eps = g.rms_eps;
+            ms.x = m->xb;
+            ms.norm_w = L.post_norm;
+            ms.rpart = m->rpart;
+            ms.nparts = (H + 15) / 16;
+            ms.block = L.block;
+            ms.down = L.down;
+            ms.sdown = L.sdown;
+            ms.h = m->h;
+            ms.out = m->xa;
+            ms.d_idx = m->idx;
+            ms.d_wt = m->wt;
+            ms.scores = m->scores;
+            ms.bar = m->step_bar;
+            ms.err = m->tickets + 9;
+            CKL(launch_moe_step(ms, c->sm_count, st, pdl), "moe step launch");
+            launches += 1;
+            continue;
+        }
         if (L.dense) {
             MoeArgs da = {};
             da.hidden = H;
@@ -564,6 +598,15 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->logits, (size_t)g.vocab);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tickets, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->slot, 16);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->step_bar, 1);
+    if (rc == DS_CUDA_OK) {
+        // the MoE block as one kernel where its shapes allow (BF16 experts);
+        // DS_CUDA_DECODE_PER_PHASE=1 keeps the per-phase kernels (same numerics)
+        const char *pp = getenv("DS_CUDA_DECODE_PER_PHASE");
+        m->fused_moe = !(pp && pp[0] == '1') && !g.use_int8 && g.engine == 0 &&
+                       moe_step_supported(g.hidden, g.moe_inter, g.n_shared * g.moe_inter, g.n_experts, g.top_k,
+                                          c->sm_count);
+    }
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->kv, 4 * m->plane_elems());
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->cos_t, (size_t)g.kv_max * g.head_dim);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->sin_t, (size_t)g.kv_max * g.head_dim);
@@ -721,9 +764,13 @@ extern "C" int ds_cuda_decoder_forward(ds_cuda_ctx_t *c, int id, const float *em
     char *pb = (char *)c->pin;
     CKL(cudaMemcpyAsync(pb, m->tok, 4, cudaMemcpyDeviceToHost, c->stream), "token copy");
     CKL(cudaMemcpyAsync(pb + 4, m->val, 4, cudaMemcpyDeviceToHost, c->stream), "logit copy");
+    CKL(cudaMemcpyAsync(pb + 8, m->tickets + 8, 8, cudaMemcpyDeviceToHost, c->stream), "error flags copy");
     if (final_x) CKL(cudaMemcpyAsync(pb + 64, m->xfinal, (size_t)H * 4, cudaMemcpyDeviceToHost, c->stream), "x copy");
     CKL(cudaStreamSynchronize(c->stream), "decoder_forward");
     if (m->mega) CK(mega_check(c, m));
+    unsigned flags[2];
+    memcpy(flags, pb + 8, 8);
+    if (flags[0] | flags[1]) return ctx_fail(c, DS_CUDA_ETIMEOUT, "decoder_forward: a bounded device-side wait gave up");
     int tok;
     memcpy(&tok, pb, 4);
     if (logit) memcpy(logit, pb + 4, 4);
@@ -775,6 +822,9 @@ extern "C" int ds_cuda_decoder_generate(ds_cuda_ctx_t *c, int id, const float *f
         "token copy");
     CKL(cudaStreamSynchronize(c->stream), "decoder_generate");
     if (m->mega) CK(mega_check(c, m));
+    unsigned flags[2];
+    CKL(cudaMemcpy(flags, m->tickets + 8, 8, cudaMemcpyDeviceToHost), "error flags read");
+    if (flags[0] | flags[1]) return ctx_fail(c, DS_CUDA_ETIMEOUT, "decoder_generate: a bounded device-side wait gave up");
     return DS_CUDA_OK;
 }
 

@@ -4,7 +4,9 @@
 // for the dense FFN down projection, and the step advance (next embedding,
 // position, token log).
 #include <cooperative_groups.h>
+#include <cstdlib>
 
+#include "attn_rows.cuh"
 #include "kernels_decode.cuh"
 
 namespace cg = cooperative_groups;
@@ -31,6 +33,7 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
     const int n = a.hidden;
     const int half = a.head_dim >> 1;
     const int per_mat = a.n_heads * half;
+    TraceScope tr;
     // task t: the rotary row pair (row0, row0 + half) of Wq, Wk or Wv
     auto task_rows = [&](int t, const uint16_t *&p0, int &m, int &h, int &d) {
         m = t / per_mat;
@@ -50,6 +53,7 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
     }
     pdl_wait();
     pdl_launch();
+    tr.waited();
     const float inv = block_rms_inv(a.x, n, a.eps);
     XRegBF16<CPL> xr;
     xr.load_norm(a.x, a.norm_w, inv, n, lane);
@@ -89,6 +93,7 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
             }
         }
     }
+    tr.done(1);
 }
 
 // ---------------------------------------------------------------------------
@@ -110,42 +115,6 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
 // the CL partial outputs (DSMEM) and scales by 1/sum.
 // head_dim must be 128 (8 lanes x 16 elements per key row).
 // ---------------------------------------------------------------------------
-
-constexpr int ATT_CL = 8;
-constexpr int ATT_MAXK = 4096;
-constexpr int ATT_HD = 128;
-
-constexpr int ATT_KPG = 4;  // keys per 8-lane group per load batch
-
-// 16 consecutive head-dim elements of one KV row: hi plane and (optional) lo plane.
-struct Row16 {
-    uint4 h0, h1, l0, l1;
-};
-
-__device__ __forceinline__ Row16 load_raw16(const uint16_t *hi, const uint16_t *lo, bool use_lo) {
-    Row16 r;
-    r.h0 = ldg_stream(hi);
-    r.h1 = ldg_stream(hi + 8);
-    if (use_lo) {
-        r.l0 = ldg_stream(lo);
-        r.l1 = ldg_stream(lo + 8);
-    } else {
-        r.l0 = make_uint4(0, 0, 0, 0);
-        r.l1 = r.l0;
-    }
-    return r;
-}
-
-// hi + lo widened to F32 (lo is zero for exact-BF16 rows, and x + 0 == x).
-__device__ __forceinline__ void raw_to_f32(const Row16 &r, float f[16]) {
-    uint32_t hw[8] = {r.h0.x, r.h0.y, r.h0.z, r.h0.w, r.h1.x, r.h1.y, r.h1.z, r.h1.w};
-    uint32_t lw[8] = {r.l0.x, r.l0.y, r.l0.z, r.l0.w, r.l1.x, r.l1.y, r.l1.z, r.l1.w};
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        f[2 * i] = __fadd_rn(bf16_lo(hw[i]), bf16_lo(lw[i]));
-        f[2 * i + 1] = __fadd_rn(bf16_hi(hw[i]), bf16_hi(lw[i]));
-    }
-}
 
 // Block-wide exclusive scan of one value per thread (blockDim == 256) with an
 // associative op; reverse = scan from the last thread down. Warp 0 scans:
@@ -213,6 +182,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     __shared__ float s_sum;
     float(*red)[ATT_HD] = reinterpret_cast<float(*)[ATT_HD]>(corr);
 
+    TraceScope tr;
     const int crank = CL > 1 ? (int)cg::this_cluster().block_rank() : 0;
     const int h = blockIdx.x / CL;
     const int tid = threadIdx.x;
@@ -267,6 +237,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     }
     pdl_wait();
     pdl_launch();
+    tr.waited();
     if constexpr (PRE) {
 #pragma unroll
         for (int r = 0; r < KPG; r++) {
@@ -415,6 +386,7 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
         out[h * ATT_HD + tid] = S > 0.f ? __fmul_rn(o, __fdiv_rn(1.0f, S)) : o;
     }
     if constexpr (CL > 1) cg::this_cluster().sync();
+    tr.done(2);
 }
 
 // batch 1: a cluster of ATT_CL CTAs per head splits the keys
@@ -456,17 +428,26 @@ __device__ void router_fold(const MvArgs &a, float *yv) {
         }
         mine[e] = acc;
     }
+    if (f.no_tail) return;
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) last = atomicAdd(f.ticket, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!last) return;
+    TraceScope tr;
     __threadfence();
-    for (int e = threadIdx.x; e <= f.E; e += blockDim.x) {
+    // column e summed in three runs of consecutive CTAs, each in CTA order,
+    // then (r0 + r1) + r2 (the MoE-step kernel sums the same way)
+    __shared__ float ls[256][3];
+    for (int t = threadIdx.x; t < 3 * (f.E + 1); t += blockDim.x) {
+        const int e = t / 3, part = t - 3 * e;
+        const int b0 = (int)gridDim.x * part / 3, b1 = (int)gridDim.x * (part + 1) / 3;
         float acc = 0.f;
-        for (int b = 0; b < (int)gridDim.x; b++) acc = __fadd_rn(acc, __ldcg(f.part + (size_t)b * (f.E + 1) + e));
-        lg[e] = acc;
+        for (int b = b0; b < b1; b++) acc = __fadd_rn(acc, __ldcg(f.part + (size_t)b * (f.E + 1) + e));
+        ls[e][part] = acc;
     }
+    __syncthreads();
+    for (int e = threadIdx.x; e <= f.E; e += blockDim.x) lg[e] = __fadd_rn(__fadd_rn(ls[e][0], ls[e][1]), ls[e][2]);
     __syncthreads();
     if (threadIdx.x < 32) {
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(lg[f.E], (float)a.rows), f.eps)));
@@ -478,6 +459,7 @@ __device__ void router_fold(const MvArgs &a, float *yv) {
         router_select(lg, f.E, f.top_k, f.renorm, f.d_idx, f.d_wt);
         if (threadIdx.x == 0) *f.ticket = 0u;
     }
+    tr.done(4);
 }
 
 template <int CPL>
@@ -485,6 +467,7 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
+    TraceScope tr;
     // the first row pair's weights load before the dependency wait
     Rows2<CPL> w;
     const int r0 = 2 * gw;
@@ -492,6 +475,7 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
         w.load(a.W + (size_t)r0 * a.n, r0 + 1 < a.rows ? a.W + (size_t)(r0 + 1) * a.n : nullptr, a.n, lane);
     pdl_wait();
     pdl_launch();
+    tr.waited();
     const float inv = a.norm_w ? block_rms_inv(a.x, a.n, a.eps) : 1.f;
     XRegBF16<CPL> xr;
     xr.load_norm(a.x, a.norm_w, inv, a.n, lane);
@@ -516,6 +500,7 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
             }
         }
     }
+    tr.done(3);
     if (a.rf.Wr) router_fold(a, yv);
 }
 
@@ -523,8 +508,10 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
 // projection [1280 x 6848] with the residual add (ds_moe_decoder.c:101, :468).
 __global__ void __launch_bounds__(128) matvec_long_kernel(MvArgs a) {
     extern __shared__ float xs[];
+    TraceScope tr;
     pdl_wait();
     pdl_launch();
+    tr.waited();
     for (int i = threadIdx.x; i < a.n; i += blockDim.x) xs[i] = a.x[i];
     __syncthreads();
     const int lane = threadIdx.x & 31;
@@ -557,6 +544,7 @@ __global__ void __launch_bounds__(128) matvec_long_kernel(MvArgs a) {
         if (a.resid) v = __fadd_rn(a.resid[row], v);
         a.y[row] = v;
     }
+    tr.done(5);
 }
 
 // out = RMSNorm(x; w) for one vector (ds_rms_norm, ds_kernels.c:1387-1471).
@@ -573,8 +561,10 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
 // the generated-token history when one is kept (ds_ocr.c:2245-2248).
 __global__ void decode_advance_kernel(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,
                                       float *x_out, int *hist, int *hist_len, int hist_cap) {
+    TraceScope tr;
     pdl_wait();
     pdl_launch();
+    tr.waited();
     int tok = *d_tok;
     const int pos = *d_pos;
     // an all-NaN logit row leaves no winner (token -1): embed row 0, log -1
@@ -589,6 +579,7 @@ __global__ void decode_advance_kernel(const uint16_t *E, int hidden, const int *
             *hist_len = *hist_len + 1;
         }
     }
+    tr.done(9);
 }
 
 // ---------------------------------------------------------------------------
@@ -664,3 +655,5 @@ cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int n, fl
     return launch_ex((const void *)rmsnorm_kernel, 1, 256, 0, st, pdl, args);
 }
 }  // namespace ds
+
+DS_TRACE_TU(decode)

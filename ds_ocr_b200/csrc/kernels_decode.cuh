@@ -52,6 +52,7 @@ struct RouterFold {
     float *scores;         // [E] (for inspection)
     int *d_idx;
     float *d_wt;
+    int no_tail;           // 1: only write the parts (the MoE-step kernel reduces them)
 };
 
 struct MvArgs {
@@ -66,6 +67,8 @@ struct MvArgs {
 
 cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int n_streams = 1);
+// batch 1, causal: the cluster-exchange kernel (attn_step.cu)
+cudaError_t launch_attn_step(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int n, float eps, cudaStream_t st, bool pdl);
 cudaError_t launch_decode_advance(const uint16_t *E, int hidden, const int *d_tok, int *d_pos, int *tok_log,

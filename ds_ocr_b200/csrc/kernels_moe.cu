@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
     const int total = nr + ns;
     const int n = a.hidden;
     const bool sim = a.simulate && !a.dense;  // the dense FFN path never truncates (ds_moe_decoder.c:75-105)
+    TraceScope tr;
     if constexpr (!I8) {
         // work order: the shared expert's pairs first (their weights do not
         // depend on the routing, so they load before the dependency wait),
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
         }
         pdl_wait();
         pdl_launch();
+        tr.waited();
         const float inv = a.norm_w ? block_rms_inv(a.x, n, a.eps) : 1.f;
         XRegBF16<CPL> xr;
         xr.load_norm(a.x, a.norm_w, inv, n, lane);
@@ -223,6 +225,7 @@ __global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeArgs a) {
             }
         }
     }
+    tr.done(6);
 }
 
 // ---------------------------------------------------------------------------
@@ -241,6 +244,7 @@ __global__ void __launch_bounds__(256, 3) moe_down_kernel(MoeArgs a) {
     const int j0 = blockIdx.x * RB;
     const int nslots = a.top_k + (a.has_shared ? 2 : 0);
     const int nr = a.top_k * a.inter;
+    TraceScope tr;
     // the shared expert's down rows do not depend on the routing: its two
     // warps load them before the dependency wait
     Rows2<CPL> pre[(RB + 1) / 2];
@@ -260,6 +264,7 @@ __global__ void __launch_bounds__(256, 3) moe_down_kernel(MoeArgs a) {
     }
     pdl_wait();
     pdl_launch();
+    tr.waited();
     if (slot < nslots) {
         const float *hv;
         WMat m;
@@ -339,6 +344,7 @@ __global__ void __launch_bounds__(256, 3) moe_down_kernel(MoeArgs a) {
             else a.out[j] = __fadd_rn(a.resid[j], acc);
         }
     }
+    tr.done(7);
 }
 
 // ---------------------------------------------------------------------------
@@ -535,3 +541,5 @@ cudaError_t launch_quantize_int8(const uint16_t *W, int rows, int n, int8_t *q, 
 }
 
 }  // namespace ds
+
+DS_TRACE_TU(moe)

@@ -263,8 +263,8 @@ __device__ __forceinline__ float row_dot_i8(const int8_t *row, int n, const XReg
 // selection passes of ds_moe_decoder.c:157-183 (raw probabilities unless
 // renorm).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void router_select(const float *scores, int E, int top_k, int renorm, int *d_idx, float *d_wt) {
-    // called by warp 0 of one CTA
+__device__ __forceinline__ void router_select_generic(const float *scores, int E, int top_k, int renorm, int *d_idx, float *d_wt) {
+    // called by warp 0 of one CTA; any E <= 256
     __shared__ float p[256];
     const int lane = threadIdx.x & 31;
     float mx = -1e30f;
@@ -299,6 +299,63 @@ __device__ __forceinline__ void router_select(const float *scores, int E, int to
         taken[bidx >> 6] |= 1ull << (bidx & 63);
         wk[k] = bv;
         ik[k] = bidx;
+        wsum = __fadd_rn(wsum, bv);
+    }
+    if (lane == 0) {
+        for (int k = 0; k < top_k; k++) {
+            d_idx[k] = ik[k];
+            d_wt[k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
+        }
+    }
+}
+
+__device__ __forceinline__ void router_select(const float *scores, int E, int top_k, int renorm, int *d_idx, float *d_wt) {
+    if (E > 64) {
+        router_select_generic(scores, E, top_k, renorm, d_idx, d_wt);
+        return;
+    }
+    // called by warp 0 of one CTA; E <= 64: lane l holds experts l and l + 32
+    const int lane = threadIdx.x & 31;
+    const int e0 = lane, e1 = lane + 32;
+    const bool v0 = e0 < E, v1 = e1 < E;
+    const float sc0 = v0 ? scores[e0] : -1e30f, sc1 = v1 ? scores[e1] : -1e30f;
+    const float mx = warp_max(fmaxf(sc0, sc1));
+    float p0 = v0 ? fast_expf(__fsub_rn(sc0, mx)) : 0.f;
+    float p1 = v1 ? fast_expf(__fsub_rn(sc1, mx)) : 0.f;
+    // sum of exponentials: per-lane partials (expert l, then l + 32), then a
+    // fixed shuffle tree (the reference sums sequentially; the difference is
+    // a few ulp of the sum)
+    float part = 0.f;
+    if (v0) part = __fadd_rn(part, p0);
+    if (v1) part = __fadd_rn(part, p1);
+    const float inv = __fdiv_rn(1.0f, warp_sum(part));
+    p0 = __fmul_rn(p0, inv);
+    p1 = __fmul_rn(p1, inv);
+    // top_k selection passes with the reference's strict '>' scan in
+    // ascending expert order (ds_moe_decoder.c:167-183): the largest
+    // probability, the lowest index among equals. Probabilities are >= 0,
+    // so their bit patterns order like the values; key 0 = no candidate.
+    bool t0 = !v0, t1 = !v1;
+    float wsum = 0.f;
+    float wk[8];
+    int ik[8];
+    for (int k = 0; k < top_k; k++) {
+        uint32_t key = 0u, idx = 0xffffffffu;
+        if (!t0) {
+            key = __float_as_uint(p0) + 1u;
+            idx = (uint32_t)e0;
+        }
+        if (!t1 && __float_as_uint(p1) + 1u > key) {
+            key = __float_as_uint(p1) + 1u;
+            idx = (uint32_t)e1;
+        }
+        const uint32_t kmax = __reduce_max_sync(DS_FULL, key);
+        const uint32_t win = __reduce_min_sync(DS_FULL, key == kmax ? idx : 0xffffffffu);
+        if (win == (uint32_t)e0) t0 = true;
+        if (win == (uint32_t)e1) t1 = true;
+        const float bv = __uint_as_float(kmax - 1u);
+        wk[k] = bv;
+        ik[k] = (int)win;
         wsum = __fadd_rn(wsum, bv);
     }
     if (lane == 0) {

@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(ST_THREADS) argmax_tma_kernel(const uint16_t *
     __shared__ uint64_t full[8], empty[8];
     __shared__ unsigned long long cta_best;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    TraceScope tr;
     const int S = st_stages(n);
     const uint32_t row_b = (uint32_t)n * 2, stage_b = ST_ROWS * row_b;
     const int tiles = (rows + ST_ROWS - 1) / ST_ROWS;
@@ -59,13 +60,14 @@ __global__ void __launch_bounds__(ST_THREADS) argmax_tma_kernel(const uint16_t *
                 int r0 = t * ST_ROWS;
                 uint32_t bytes = (uint32_t)min(ST_ROWS, rows - r0) * row_b;
                 mbar_expect_tx(&full[s], bytes);
-                bulk_g2s(smem + (size_t)s * stage_b, W + (size_t)r0 * n, bytes, &full[s]);
+                bulk_g2s_stream(smem + (size_t)s * stage_b, W + (size_t)r0 * n, bytes, &full[s]);
             }
         }
         return;
     }
     pdl_wait();
     pdl_launch();
+    tr.waited();
     // block_rms_inv needs every thread of the block: consumers only here, so
     // compute the norm with the consumer warps through named barrier 1
     float inv = 1.f;
@@ -124,6 +126,7 @@ __global__ void __launch_bounds__(ST_THREADS) argmax_tma_kernel(const uint16_t *
             *ticket = 0u;
         }
     }
+    tr.done(8);
 }
 
 bool st_stages_ok(int n) { return n % 8 == 0 && n <= 2048 && st_stages(n) >= 2; }
@@ -157,3 +160,5 @@ cudaError_t launch_argmax_tma(const uint16_t *W, const float *x, int rows, int n
 }
 
 }  // namespace ds
+
+DS_TRACE_TU(stream)

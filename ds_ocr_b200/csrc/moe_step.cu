@@ -1,0 +1,379 @@
+// moe_step.cu — the MoE block of one batch-1 decode step as ONE kernel
+// (moe_forward, ds_moe_decoder.c:131-333, BF16 experts): routing from the
+// router terms the O-projection CTAs left behind, the shared expert's and
+// the six routed experts' gate/up + SwiGLU, a grid-wide barrier, then every
+// expert's down projection, the weighted combine and the residual add.
+//
+// Why one kernel: the step is a chain of dependent phases whose weights are
+// only a few MB each, so the time goes to latency (dependency waits, the
+// first bytes of each phase), not to bandwidth. Here every byte that does not
+// depend on the routing is in flight before the dependency wait, and every
+// byte that does is requested as soon as the routing is known:
+//   before the wait  this CTA's shared-expert gate/up rows and its rows of
+//                    the shared down projection, copied into shared memory
+//                    by the TMA engine;
+//   after routing    its rows of the six routed down projections (TMA, into
+//                    shared memory), while its warps stream the routed
+//                    gate/up rows through registers;
+//   after the grid barrier (all of h written) the down dot products read
+//                    only shared memory.
+// One CTA per SM; the barrier is safe because the grid never exceeds the SM
+// count and a CTA always fits on an SM (the kernels around it are small).
+//
+// Numerics match the per-phase kernels exactly (kernels_moe.cu: same
+// association of every dot product, RMS norm, router logits, SwiGLU,
+// truncation and combine), so the two paths give bit-identical results.
+#include <algorithm>
+#include <cstdlib>
+
+#include "kernels_moe.cuh"
+#include "launch.h"
+#include "moe_step.h"
+
+namespace ds {
+
+constexpr int MS_THREADS = 256;
+constexpr int MS_WARPS = MS_THREADS / 32;
+constexpr int MS_CPL = 5;      // hidden 1280 = 5 chunks of 8 columns per lane
+constexpr int MS_DCPL = 4;     // down rows of 896 columns: 112 chunks <= 4 per lane
+constexpr int MS_MAXROWS = 16; // output rows per CTA (hidden / grid, rounded up)
+constexpr int MS_NSLOT = 8;    // down dots per output row (one warp each): top_k (6) routed + the shared row's two halves
+constexpr int MS_MAXE = 84;    // experts: 3 (E + 1) threads sum the router terms
+constexpr int MS_MAXPART = 32; // router-term parts per summing thread (O-proj CTAs <= 96)
+
+struct MsLayout {
+    int i0, i1;   // shared items of this CTA
+    int q0, q1;   // routed items
+    int j0, j1;   // output rows
+    size_t a_bytes, d_bytes;
+};
+
+__device__ __forceinline__ MsLayout ms_layout(const MoeStepArgs &a) {
+    MsLayout L;
+    const int G = gridDim.x, b = blockIdx.x;
+    const int nr = a.K * a.I;
+    L.i0 = (int)((long long)a.S * b / G);
+    L.i1 = (int)((long long)a.S * (b + 1) / G);
+    L.q0 = (int)((long long)nr * b / G);
+    L.q1 = (int)((long long)nr * (b + 1) / G);
+    L.j0 = (int)((long long)a.H * b / G);
+    L.j1 = (int)((long long)a.H * (b + 1) / G);
+    return L;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier over co-resident CTAs on a counter that only grows: the
+// CTA's arrival number picks its generation, the barrier completes when the
+// counter reaches the end of that generation. Bounded: gives up after ~2^24
+// polls, sets *err and returns false.
+__device__ __forceinline__ bool ms_grid_sync(unsigned long long *ctr, unsigned *err) {
+    __shared__ int ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned long long old = atomicAdd(ctr, 1ull);
+        const unsigned long long target = (old / gridDim.x + 1ull) * gridDim.x;
+        int good = 0;
+        for (uint32_t it = 0; it < (1u << 24); it++) {
+            if (ld_acquire_u64(ctr) >= target) {
+                good = 1;
+                break;
+            }
+            if ((it & 1023u) == 1023u && *(volatile unsigned *)err) break;
+        }
+        if (!good) atomicExch(err, 1u);
+        __threadfence();
+        ok = good;
+    }
+    __syncthreads();
+    return ok != 0;
+}
+
+__global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bar_sh, bar_sd, bar_rd, bar_nw;
+    __shared__ float lg[MS_MAXE + 1];
+    __shared__ float lsum[MS_MAXE + 1][3];
+    __shared__ int s_idx[8];
+    __shared__ float s_wt[8];
+    __shared__ float ysm[MS_MAXROWS][10];
+    TraceScope tr;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int H = a.H, I = a.I, S = a.S, K = a.K, E = a.E;
+    const int nr = K * I;
+    const MsLayout L = ms_layout(a);
+    const int ns = L.i1 - L.i0, nrows = L.j1 - L.j0;
+    // shared memory: A = shared gate/up rows (later h), D = down rows, xs
+    uint16_t *regA = reinterpret_cast<uint16_t *>(smem);
+    uint16_t *regD = reinterpret_cast<uint16_t *>(smem + a.a_bytes);
+    float *xs = reinterpret_cast<float *>(smem + a.a_bytes + a.d_bytes);
+    float *nws = xs + H;  // post-attention norm weight
+    float *hs = reinterpret_cast<float *>(smem);
+    const uint16_t *sgu = a.block + (size_t)E * 2 * I * H;
+
+    if (tid == 0) {
+        mbar_init(&bar_sh, 1);
+        mbar_init(&bar_sd, 1);
+        mbar_init(&bar_rd, 1);
+        mbar_init(&bar_nw, 1);
+        mbar_fence_init();
+        mbar_expect_tx(&bar_nw, (uint32_t)H * 4);
+        bulk_g2s(nws, a.norm_w, (uint32_t)H * 4, &bar_nw);
+        // routing-independent weights: the shared expert's gate/up rows of
+        // this CTA's items and its down rows of this CTA's outputs
+        if (ns > 0) {
+            const uint32_t rb = (uint32_t)ns * H * 2;
+            mbar_expect_tx(&bar_sh, 2 * rb);
+            bulk_g2s_stream(regA, sgu + (size_t)L.i0 * H, rb, &bar_sh);
+            bulk_g2s_stream(regA + (size_t)ns * H, sgu + (size_t)(S + L.i0) * H, rb, &bar_sh);
+        }
+        if (nrows > 0) {
+            const uint32_t db = (uint32_t)nrows * S * 2;
+            mbar_expect_tx(&bar_sd, db);
+            bulk_g2s_stream(regD + (size_t)K * nrows * I, a.sdown + (size_t)L.j0 * S, db, &bar_sd);
+        }
+    }
+    __syncthreads();
+    pdl_wait();
+    if (a.launch_at == 0) pdl_launch();
+    tr.waited();
+    if (a.launch_at == 3) {  // debug: time of the routing-independent copies only
+        if (ns > 0) mbar_wait(&bar_sh, 0, a.err);
+        tr.mark(0);
+        if (nrows > 0) mbar_wait(&bar_sd, 0, a.err);
+        tr.mark(1);
+        mbar_wait(&bar_nw, 0, a.err);
+        tr.mark(2);
+        tr.done(10);
+        return;
+    }
+
+    // 1. router logits: column e of the O-proj CTAs' terms summed in three
+    //    runs of consecutive CTAs, each in CTA order, then (r0 + r1) + r2
+    //    (router_fold's last CTA sums the same way); the residual stream
+    //    into xs
+    if (tid < 3 * (E + 1)) {
+        const int e = tid / 3, part = tid - 3 * e;
+        const int b0 = a.nparts * part / 3, b1 = a.nparts * (part + 1) / 3;
+        const float *col = a.rpart + e;
+        float v[MS_MAXPART];
+#pragma unroll
+        for (int u = 0; u < MS_MAXPART; u++) v[u] = b0 + u < b1 ? __ldcg(col + (size_t)(b0 + u) * (E + 1)) : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int u = 0; u < MS_MAXPART; u++)
+            if (b0 + u < b1) acc = __fadd_rn(acc, v[u]);
+        lsum[e][part] = acc;
+    }
+    for (int i = tid * 4; i < H; i += MS_THREADS * 4)
+        *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
+    __syncthreads();
+    if (tid <= E) lg[tid] = __fadd_rn(__fadd_rn(lsum[tid][0], lsum[tid][1]), lsum[tid][2]);
+    tr.mark(0);
+    // 2. post-attention RMSNorm of x (block_rms_inv's order, the norm
+    //    weight from shared memory)
+    const float inv = block_rms_inv(xs, H, a.eps);
+    if (!mbar_wait(&bar_nw, 0, a.err)) return;
+    for (int i = tid * 4; i < H; i += MS_THREADS * 4) {
+        const float4 xv = *reinterpret_cast<const float4 *>(xs + i);
+        const float4 wv = *reinterpret_cast<const float4 *>(nws + i);
+        *reinterpret_cast<float4 *>(xs + i) = norm4(xv, wv, inv);
+    }
+    __syncthreads();
+    tr.mark(1);
+    const bool sim = a.simulate != 0;
+    auto swiglu_out = [&](float g, float u) {
+        if (sim) {
+            g = bf16_roundtrip(g);
+            u = bf16_roundtrip(u);
+        }
+        float hv = swiglu(g, u);
+        if (sim) hv = bf16_roundtrip(hv);
+        return hv;
+    };
+    // the normalised activation in registers (lane l: chunks l + 32c)
+    XRegBF16<MS_CPL> xr;
+    xr.load(xs, H, lane);
+    // 3. warp 0: routing; warps 1..7 meanwhile: the shared expert's items
+    //    (weights already in shared memory)
+    if (warp == 0) {
+        const float rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(lg[E], (float)H), a.eps)));
+        for (int e = lane; e < E; e += 32) {
+            lg[e] = __fmul_rn(lg[e], rinv);
+            if (blockIdx.x == 0) a.scores[e] = lg[e];
+        }
+        __syncwarp();
+        router_select(lg, E, K, a.renorm, s_idx, s_wt);
+        __syncwarp();
+        if (blockIdx.x == 0 && lane < K) {
+            a.d_idx[lane] = s_idx[lane];
+            a.d_wt[lane] = s_wt[lane];
+        }
+        tr.mark(2);
+    } else if (ns > 0) {
+        if (!mbar_wait(&bar_sh, 0, a.err)) return;
+        for (int it = warp - 1; it < ns; it += MS_WARPS - 1) {
+            const uint16_t *gr = regA + (size_t)it * H, *ur = regA + (size_t)(ns + it) * H;
+            float g = 0.f, u = 0.f;
+#pragma unroll
+            for (int c = 0; c < MS_CPL; c++) {
+                const int ch = lane + 32 * c;
+                g = dot8_bf16(*reinterpret_cast<const uint4 *>(gr + 8 * ch), xr.v[c][0], xr.v[c][1], g);
+                u = dot8_bf16(*reinterpret_cast<const uint4 *>(ur + 8 * ch), xr.v[c][0], xr.v[c][1], u);
+            }
+            g = warp_sum(g);
+            u = warp_sum(u);
+            if (lane == 0) a.h[nr + L.i0 + it] = swiglu_out(g, u);
+        }
+    }
+    __syncthreads();
+    tr.mark(3);
+    // 4. routed down rows into shared memory (TMA), routed gate/up rows into
+    //    registers
+    if (tid == 0 && nrows > 0) {
+        const uint32_t kb = (uint32_t)nrows * I * 2;
+        mbar_expect_tx(&bar_rd, (uint32_t)K * kb);
+        for (int k = 0; k < K; k++)
+            bulk_g2s_stream(regD + (size_t)k * nrows * I, a.down + ((size_t)s_idx[k] * H + L.j0) * I, kb, &bar_rd);
+    }
+    auto item_rows = [&](int q, const uint16_t *&g, const uint16_t *&u) {
+        const int k = q / I, i = q - k * I;
+        const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
+        g = base + (size_t)i * H;
+        u = base + (size_t)(I + i) * H;
+    };
+    Rows2<MS_CPL> cur, nxt;
+    int q = L.q0 + warp;
+    if (q < L.q1) {
+        const uint16_t *g, *u;
+        item_rows(q, g, u);
+        cur.load(g, u, H, lane);
+    }
+    tr.mark(4);
+    // 5. routed items, the next item's rows in flight during each dot
+    for (; q < L.q1; q += MS_WARPS) {
+        const int qn = q + MS_WARPS;
+        if (qn < L.q1) {
+            const uint16_t *g, *u;
+            item_rows(qn, g, u);
+            nxt.load(g, u, H, lane);
+        }
+        float g, u;
+        cur.dot(xr, g, u);
+        cur = nxt;
+        g = warp_sum(g);
+        u = warp_sum(u);
+        if (lane == 0) a.h[q] = swiglu_out(g, u);
+    }
+    tr.mark(6);
+    if (a.launch_at == 1) pdl_launch();
+    // 6. every h written (all CTAs), then h into shared memory
+    if (!ms_grid_sync(a.bar, a.err)) return;
+    const int hn = nr + S;
+    for (int i = tid * 4; i < hn; i += MS_THREADS * 4)
+        *reinterpret_cast<float4 *>(hs + i) = __ldcg(reinterpret_cast<const float4 *>(a.h + i));
+    if (nrows > 0) {
+        if (!mbar_wait(&bar_sd, 0, a.err)) return;
+        if (!mbar_wait(&bar_rd, 0, a.err)) return;
+    }
+    __syncthreads();
+    tr.mark(7);
+    // 7. down dot products: warp s owns slot s (s < K: routed expert s;
+    //    K, K + 1: the two halves of the shared expert's rows), its slice of
+    //    h in registers, and walks this CTA's output rows two at a time
+    const int half = S >> 1;
+    if (warp < K + 2) {
+        const int s = warp;
+        const float *hv = s < K ? hs + s * I : hs + nr + (s - K) * half;
+        XRegBF16<MS_DCPL> hr;
+        hr.load(hv, I, lane);
+        const int nch = I >> 3;
+        auto wrow = [&](int r) {
+            return s < K ? regD + ((size_t)s * nrows + r) * I
+                         : regD + (size_t)K * nrows * I + (size_t)r * S + (s - K) * half;
+        };
+        for (int r = 0; r < nrows; r += 2) {
+            const bool two = r + 1 < nrows;
+            const uint16_t *w0 = wrow(r), *w1 = wrow(two ? r + 1 : r);
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < MS_DCPL; c++) {
+                const int ch = lane + 32 * c;
+                if (ch < nch) {
+                    a0 = dot8_bf16(*reinterpret_cast<const uint4 *>(w0 + 8 * ch), hr.v[c][0], hr.v[c][1], a0);
+                    a1 = dot8_bf16(*reinterpret_cast<const uint4 *>(w1 + 8 * ch), hr.v[c][0], hr.v[c][1], a1);
+                }
+            }
+            a0 = warp_sum(a0);
+            a1 = warp_sum(a1);
+            if (lane == 0) {
+                ysm[r][s] = a0;
+                if (two) ysm[r + 1][s] = a1;
+            }
+        }
+    }
+    __syncthreads();
+    // 8. combine in the reference's order (ds_expert_combine, then + shared)
+    //    and the residual add
+    if (tid < nrows) {
+        const int j = L.j0 + tid;
+        float acc = 0.f;
+        for (int k = 0; k < K; k++) {
+            float yk = ysm[tid][k];
+            if (sim) yk = bf16_roundtrip(yk);
+            acc = __fmaf_rn(s_wt[k], yk, acc);
+        }
+        float sh = __fadd_rn(ysm[tid][K], ysm[tid][K + 1]);
+        if (sim) sh = bf16_roundtrip(sh);
+        acc = __fadd_rn(acc, sh);
+        a.out[j] = __fadd_rn(__ldcg(a.x + j), acc);
+    }
+    if (a.launch_at == 2) pdl_launch();
+    tr.done(10);
+}
+
+bool moe_step_supported(int H, int I, int S, int E, int K, int sms) {
+    if (H != 1280 || I % 8 || S % 16 || I > 8 * 32 * MS_DCPL || S / 2 > 8 * 32 * MS_DCPL) return false;
+    if (K != MS_NSLOT - 2 || E > MS_MAXE || E < K || sms < 1 || (H + 15) / 16 > 3 * MS_MAXPART) return false;
+    if (2 * S != 2 * I * (S / I) || S / 2 != I) return false;  // the shared row splits into two expert-width halves
+    if ((H + sms - 1) / sms > MS_MAXROWS) return false;
+    return moe_step_smem(H, I, S, K, sms) <= 210 * 1024;
+}
+
+size_t moe_step_smem(int H, int I, int S, int K, int G) {
+    const int ns_max = (S + G - 1) / G, rows_max = (H + G - 1) / G;
+    size_t a_bytes = std::max((size_t)ns_max * 2 * H * 2, (size_t)(K * I + S) * 4);
+    size_t d_bytes = (size_t)rows_max * (K * I + S) * 2;
+    a_bytes = (a_bytes + 127) & ~(size_t)127;
+    d_bytes = (d_bytes + 127) & ~(size_t)127;
+    return a_bytes + d_bytes + (size_t)H * 8;
+}
+
+cudaError_t launch_moe_step(MoeStepArgs a, int grid, cudaStream_t st, bool pdl) {
+    const int ns_max = (a.S + grid - 1) / grid, rows_max = (a.H + grid - 1) / grid;
+    a.a_bytes = std::max((size_t)ns_max * 2 * a.H * 2, (size_t)(a.K * a.I + a.S) * 4);
+    a.d_bytes = (size_t)rows_max * (a.K * a.I + a.S) * 2;
+    a.a_bytes = (a.a_bytes + 127) & ~(size_t)127;
+    a.d_bytes = (a.d_bytes + 127) & ~(size_t)127;
+    const size_t smem = a.a_bytes + a.d_bytes + (size_t)a.H * 8;
+    static size_t set = 0;
+    if (set < smem) {
+        cudaError_t e = cudaFuncSetAttribute((const void *)moe_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        set = smem;
+    }
+    static const char *la = getenv("DS_MS_LAUNCH_AT");
+    a.launch_at = la ? atoi(la) : 0;
+    void *args[] = {&a};
+    return launch_ex((const void *)moe_step_kernel, grid, MS_THREADS, smem, st, pdl, args);
+}
+
+}  // namespace ds
+
+DS_TRACE_TU(step)

@@ -165,6 +165,15 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
         qa.kv_max = g.kv_max;
         qa.n_heads = NH;
         qa.head_dim = HD;
+        qa.pos_ready = l > 0 ? 1 : 0;  // layer 0 follows the step-advance kernel that writes it
+        if (L.dense && m->fused_moe) {
+            // the dense FFN's weights into L2 while QKV, attention and the
+            // O-projection (latency-bound) leave the HBM idle
+            qa.pf[0] = L.dgate;
+            qa.pf[1] = L.dup;
+            qa.pf[2] = L.ddown;
+            qa.pf_bytes[0] = qa.pf_bytes[1] = qa.pf_bytes[2] = (size_t)g.dense_inter * H * 2;
+        }
         CKL(launch_qkv_rope(qa, st, pdl), "qkv launch");
         AttnArgs aa = {};
         aa.q = m->q;
@@ -205,7 +214,7 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             oa.rf.scores = m->scores;
             oa.rf.d_idx = m->idx;
             oa.rf.d_wt = m->wt;
-            oa.rf.no_tail = fused ? 1 : 0;
+            oa.rf.no_tail = fused ? 1 : 0;  // the MoE-step kernel reduces the parts itself
         }
         CKL(launch_matvec_res(oa, st, pdl), "o-proj launch");
         launches += 3;
@@ -233,11 +242,41 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             ms.scores = m->scores;
             ms.bar = m->step_bar;
             ms.err = m->tickets + 9;
+            if (l + 1 < g.n_layers) {
+                const DecLayer &N = m->layers[l + 1];
+                ms.pf[0] = N.wq;
+                ms.pf[1] = N.wk;
+                ms.pf[2] = N.wv;
+                ms.pf_bytes = (size_t)NH * HD * H * 2;
+            }
             CKL(launch_moe_step(ms, c->sm_count, st, pdl), "moe step launch");
             launches += 1;
             continue;
         }
-        if (L.dense) {
+        if (L.dense && m->fused_moe && dense_step_supported(H, g.dense_inter, c->sm_count)) {
+            DenseStepArgs ds = {};
+            ds.H = H;
+            ds.D = g.dense_inter;
+            ds.eps = g.rms_eps;
+            ds.x = m->xb;
+            ds.norm_w = L.post_norm;
+            ds.gate = L.dgate;
+            ds.up = L.dup;
+            ds.down = L.ddown;
+            ds.h = m->h;
+            ds.out = m->xa;
+            ds.bar = m->step_bar;
+            ds.err = m->tickets + 9;
+            if (l + 1 < g.n_layers) {
+                const DecLayer &N = m->layers[l + 1];
+                ds.pf[0] = N.wq;
+                ds.pf[1] = N.wk;
+                ds.pf[2] = N.wv;
+                ds.pf_bytes = (size_t)NH * HD * H * 2;
+            }
+            CKL(launch_dense_step(ds, c->sm_count, st, pdl), "dense step launch");
+            launches += 1;
+        } else if (L.dense) {
             MoeArgs da = {};
             da.hidden = H;
             da.sh_inter = g.dense_inter;

@@ -43,21 +43,48 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
         const uint16_t *W = m == 0 ? a.w[0] : (m == 1 ? a.w[1] : a.w[2]);
         p0 = W + (size_t)(h * a.head_dim + d) * n;
     };
-    // the first task's weights load before the dependency wait
+    // before the dependency wait: the first task's weights (registers), the
+    // norm weight (shared memory) and, once the position is readable (every
+    // layer but the first: an earlier step's advance kernel wrote it), the
+    // first task's RoPE factors
+    extern __shared__ float qs[];  // x [n], then the norm weight [n]
+    float *xs = qs, *nws = qs + n;
     Rows2<CPL> w;
+    int m0 = 0, h0 = 0, d0 = 0;
     if (gw < 3 * per_mat) {
         const uint16_t *p0;
-        int m, h, d;
-        task_rows(gw, p0, m, h, d);
+        task_rows(gw, p0, m0, h0, d0);
         w.load(p0, p0 + (size_t)half * n, n, lane);
+    }
+    if (threadIdx.x == 0) {
+        const size_t G = gridDim.x, b = blockIdx.x;
+        for (int k = 0; k < 3; k++) {
+            const size_t B = a.pf_bytes[k];
+            const size_t lo = (B * b / G) & ~(size_t)15, hi = b + 1 == G ? B : (B * (b + 1) / G) & ~(size_t)15;
+            if (a.pf[k] && hi > lo) prefetch_range(static_cast<const uint8_t *>(a.pf[k]) + lo, hi - lo);
+        }
+    }
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+        *reinterpret_cast<float4 *>(nws + i) = *reinterpret_cast<const float4 *>(a.norm_w + i);
+    int pos = a.pos_ready ? __ldcg(a.d_pos) : 0;
+    float rc0 = 0.f, rs0 = 0.f, rc1 = 0.f, rs1 = 0.f;
+    if (a.pos_ready && lane == 0 && gw < 3 * per_mat && m0 < 2) {
+        const float *cs = a.cos_t + (size_t)pos * a.head_dim, *sn = a.sin_t + (size_t)pos * a.head_dim;
+        rc0 = cs[d0];
+        rs0 = sn[d0];
+        rc1 = cs[d0 + half];
+        rs1 = sn[d0 + half];
     }
     pdl_wait();
     pdl_launch();
     tr.waited();
-    const float inv = block_rms_inv(a.x, n, a.eps);
+    if (!a.pos_ready) pos = __ldcg(a.d_pos);
+    for (int i = threadIdx.x * 4; i < n; i += blockDim.x * 4)
+        *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
+    __syncthreads();
+    const float inv = block_rms_inv(xs, n, a.eps);
     XRegBF16<CPL> xr;
-    xr.load_norm(a.x, a.norm_w, inv, n, lane);
-    const int pos = *a.d_pos;
+    xr.load_norm(xs, nws, inv, n, lane);
     for (int t = gw; t < 3 * per_mat; t += nw) {
         const uint16_t *p0;
         int m, h, d;
@@ -71,10 +98,17 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(QkvArgs a) {
         if (lane == 0) {
             float o0 = s0, o1 = s1;
             if (m < 2) {
-                const float *cs = a.cos_t + (size_t)pos * a.head_dim;
-                const float *sn = a.sin_t + (size_t)pos * a.head_dim;
-                o0 = __fsub_rn(__fmul_rn(s0, cs[d]), __fmul_rn(s1, sn[d]));
-                o1 = __fadd_rn(__fmul_rn(s0, sn[d + half]), __fmul_rn(s1, cs[d + half]));
+                float c0 = rc0, sn0 = rs0, c1 = rc1, sn1 = rs1;
+                if (!(a.pos_ready && t == gw)) {
+                    const float *cs = a.cos_t + (size_t)pos * a.head_dim;
+                    const float *sn = a.sin_t + (size_t)pos * a.head_dim;
+                    c0 = cs[d];
+                    sn0 = sn[d];
+                    c1 = cs[d + half];
+                    sn1 = sn[d + half];
+                }
+                o0 = __fsub_rn(__fmul_rn(s0, c0), __fmul_rn(s1, sn0));
+                o1 = __fadd_rn(__fmul_rn(s0, sn1), __fmul_rn(s1, c1));
             }
             if (m == 0) {
                 a.q_out[row0] = o0;
@@ -408,7 +442,9 @@ __global__ void __launch_bounds__(256, 2) attn_streams_kernel(AttnArgs a) { attn
 
 // The router terms of this CTA's 16 output rows (one pass: 2 rows per warp,
 // grid x 16 == rows), then, in the last CTA, logits, softmax and top-k.
-__device__ void router_fold(const MvArgs &a, float *yv) {
+// wr16: thread e's 16 router weights of this CTA's rows (loaded before the
+// dependency wait); gs: the post-attention norm weights of those rows.
+__device__ void router_fold(const MvArgs &a, const float *yv, const uint4 (&wr16)[2], const float *gs) {
     const RouterFold &f = a.rf;
     __shared__ bool last;
     __shared__ float lg[256];
@@ -420,9 +456,12 @@ __device__ void router_fold(const MvArgs &a, float *yv) {
     for (int e = threadIdx.x; e <= f.E; e += blockDim.x) {
         float acc = 0.f;
         if (e < f.E) {
-            const uint16_t *wr = f.Wr + (size_t)e * a.rows + row0;
-            for (int i = 0; i < nrow; i++)
-                acc = __fmaf_rn(__uint_as_float((uint32_t)wr[i] << 16), __fmul_rn(f.g[row0 + i], yv[i]), acc);
+            const uint32_t w[8] = {wr16[0].x, wr16[0].y, wr16[0].z, wr16[0].w,
+                                   wr16[1].x, wr16[1].y, wr16[1].z, wr16[1].w};
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                if (i < nrow)
+                    acc = __fmaf_rn((i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]), __fmul_rn(gs[i], yv[i]), acc);
         } else {
             for (int i = 0; i < nrow; i++) acc = __fmaf_rn(yv[i], yv[i], acc);
         }
@@ -437,13 +476,18 @@ __device__ void router_fold(const MvArgs &a, float *yv) {
     TraceScope tr;
     __threadfence();
     // column e summed in three runs of consecutive CTAs, each in CTA order,
-    // then (r0 + r1) + r2 (the MoE-step kernel sums the same way)
+    // then (r0 + r1) + r2; a run's loads are all in flight together
     __shared__ float ls[256][3];
     for (int t = threadIdx.x; t < 3 * (f.E + 1); t += blockDim.x) {
         const int e = t / 3, part = t - 3 * e;
         const int b0 = (int)gridDim.x * part / 3, b1 = (int)gridDim.x * (part + 1) / 3;
+        float v[32];
+#pragma unroll
+        for (int u = 0; u < 32; u++) v[u] = b0 + u < b1 ? __ldcg(f.part + (size_t)(b0 + u) * (f.E + 1) + e) : 0.f;
         float acc = 0.f;
-        for (int b = b0; b < b1; b++) acc = __fadd_rn(acc, __ldcg(f.part + (size_t)b * (f.E + 1) + e));
+#pragma unroll
+        for (int u = 0; u < 32; u++)
+            if (b0 + u < b1) acc = __fadd_rn(acc, v[u]);
         ls[e][part] = acc;
     }
     __syncthreads();
@@ -468,11 +512,30 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nw = (gridDim.x * blockDim.x) >> 5;
     TraceScope tr;
-    // the first row pair's weights load before the dependency wait
+    // the first row pair's weights load before the dependency wait, and the
+    // router's weights of this CTA's 16 rows (thread e: its 16 columns of
+    // expert e) with their norm weights
     Rows2<CPL> w;
     const int r0 = 2 * gw;
     if (r0 < a.rows)
         w.load(a.W + (size_t)r0 * a.n, r0 + 1 < a.rows ? a.W + (size_t)(r0 + 1) * a.n : nullptr, a.n, lane);
+    uint4 wr16[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    __shared__ float gs[16];
+    if (a.rf.Wr) {
+        const int rb = blockIdx.x * 16;
+        if ((int)threadIdx.x < a.rf.E && rb + 16 <= a.rows) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(a.rf.Wr + (size_t)threadIdx.x * a.rows + rb);
+            wr16[0] = ldg_stream(src);
+            wr16[1] = ldg_stream(src + 1);
+        } else if ((int)threadIdx.x < a.rf.E) {
+            uint32_t t[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int i = 0; i < 16 && rb + i < a.rows; i++)
+                t[i >> 1] |= (uint32_t)a.rf.Wr[(size_t)threadIdx.x * a.rows + rb + i] << ((i & 1) * 16);
+            wr16[0] = make_uint4(t[0], t[1], t[2], t[3]);
+            wr16[1] = make_uint4(t[4], t[5], t[6], t[7]);
+        }
+        if (threadIdx.x < 16) gs[threadIdx.x] = rb + threadIdx.x < a.rows ? a.rf.g[rb + threadIdx.x] : 0.f;
+    }
     pdl_wait();
     pdl_launch();
     tr.waited();
@@ -501,7 +564,7 @@ __global__ void __launch_bounds__(256) matvec_res_kernel(MvArgs a) {
         }
     }
     tr.done(3);
-    if (a.rf.Wr) router_fold(a, yv);
+    if (a.rf.Wr) router_fold(a, yv, wr16, gs);
 }
 
 // Long-K matvec (n up to 8192, x staged in shared memory): the dense FFN down
@@ -611,7 +674,8 @@ cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl) {
     int grid = min((tasks + 7) / 8, sms() * 8);
     QkvArgs aa = a;
     void *args[] = {&aa};
-    DS_CPL_SWITCH2(a.hidden, 8, return launch_ex((const void *)qkv_rope_kernel<CPL>, grid, 256, 0, st, pdl, args));
+    const size_t smem = (size_t)a.hidden * 8;
+    DS_CPL_SWITCH2(a.hidden, 8, return launch_ex((const void *)qkv_rope_kernel<CPL>, grid, 256, smem, st, pdl, args));
 }
 
 cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int n_streams) {

@@ -16,6 +16,9 @@ struct QkvArgs {
     float *q_out;
     uint16_t *k_hi, *k_lo, *v_hi, *v_lo;  // this layer's cache, [head][kv_max][head_dim]
     int kv_max, n_heads, head_dim;
+    int pos_ready;  // 1: *d_pos was written by a kernel that completed before the predecessor's dependent part
+    const void *pf[3];  // weights a later kernel of the step reads (e.g. the dense FFN), asked of L2 before the
+    size_t pf_bytes[3]; //   dependency wait, split over the CTAs (null / 0: none)
 };
 
 struct AttnArgs {

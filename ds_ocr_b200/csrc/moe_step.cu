@@ -36,10 +36,10 @@ constexpr int MS_THREADS = 256;
 constexpr int MS_WARPS = MS_THREADS / 32;
 constexpr int MS_CPL = 5;      // hidden 1280 = 5 chunks of 8 columns per lane
 constexpr int MS_DCPL = 4;     // down rows of 896 columns: 112 chunks <= 4 per lane
-constexpr int MS_MAXROWS = 16; // output rows per CTA (hidden / grid, rounded up)
-constexpr int MS_NSLOT = 8;    // down dots per output row (one warp each): top_k (6) routed + the shared row's two halves
+constexpr int MS_MAXROWS = 10; // output rows per CTA (hidden / grid, rounded up: 9 on 148 SMs)
 constexpr int MS_MAXE = 84;    // experts: 3 (E + 1) threads sum the router terms
 constexpr int MS_MAXPART = 32; // router-term parts per summing thread (O-proj CTAs <= 96)
+constexpr int MS_NSLOT = 8;    // down dots per output row (one warp each): top_k (6) routed + the shared row's two halves
 
 struct MsLayout {
     int i0, i1;   // shared items of this CTA
@@ -92,6 +92,16 @@ __device__ __forceinline__ bool ms_grid_sync(unsigned long long *ctr, unsigned *
     }
     __syncthreads();
     return ok != 0;
+}
+
+// This CTA's share of the next layer's Q, K and V weights, asked of L2: the
+// HBM is idle while the CTAs synchronise and run the down projection.
+__device__ __forceinline__ void prefetch_next(const void *const (&pf)[3], size_t bytes) {
+    if (threadIdx.x != 0 || bytes == 0) return;
+    const size_t G = gridDim.x, b = blockIdx.x;
+    const size_t lo = (bytes * b / G) & ~(size_t)15, hi = b + 1 == G ? bytes : (bytes * (b + 1) / G) & ~(size_t)15;
+    for (int m = 0; m < 3; m++)
+        if (pf[m] && hi > lo) prefetch_range(static_cast<const uint8_t *>(pf[m]) + lo, hi - lo);
 }
 
 __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) {
@@ -155,8 +165,8 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
 
     // 1. router logits: column e of the O-proj CTAs' terms summed in three
     //    runs of consecutive CTAs, each in CTA order, then (r0 + r1) + r2
-    //    (router_fold's last CTA sums the same way); the residual stream
-    //    into xs
+    //    (router_fold's last CTA sums the same way), every run's loads in
+    //    flight together; the residual stream into xs
     if (tid < 3 * (E + 1)) {
         const int e = tid / 3, part = tid - 3 * e;
         const int b0 = a.nparts * part / 3, b1 = a.nparts * (part + 1) / 3;
@@ -173,8 +183,46 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
     for (int i = tid * 4; i < H; i += MS_THREADS * 4)
         *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
     __syncthreads();
-    if (tid <= E) lg[tid] = __fadd_rn(__fadd_rn(lsum[tid][0], lsum[tid][1]), lsum[tid][2]);
     tr.mark(0);
+    // routing: softmax and top-k of the logits scaled by the RMS of x
+    if (warp == 0) {
+        for (int e = lane; e <= E; e += 32) lg[e] = __fadd_rn(__fadd_rn(lsum[e][0], lsum[e][1]), lsum[e][2]);
+        __syncwarp();
+        const float rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(lg[E], (float)H), a.eps)));
+        for (int e = lane; e < E; e += 32) {
+            lg[e] = __fmul_rn(lg[e], rinv);
+            if (blockIdx.x == 0) a.scores[e] = lg[e];
+        }
+        __syncwarp();
+        router_select(lg, E, K, a.renorm, s_idx, s_wt);
+        __syncwarp();
+        if (blockIdx.x == 0 && lane < K) {
+            a.d_idx[lane] = s_idx[lane];
+            a.d_wt[lane] = s_wt[lane];
+        }
+    }
+    __syncthreads();
+    // routed gate/up rows into registers and (the last warp's lane 0) the
+    // routed down rows into shared memory (TMA), as soon as the routing is known
+    auto item_rows = [&](int q, const uint16_t *&g, const uint16_t *&u) {
+        const int k = q / I, i = q - k * I;
+        const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
+        g = base + (size_t)i * H;
+        u = base + (size_t)(I + i) * H;
+    };
+    Rows2<MS_CPL> cur, nxt;
+    int q = L.q0 + warp;
+    if (q < L.q1) {
+        const uint16_t *g, *u;
+        item_rows(q, g, u);
+        cur.load(g, u, H, lane);
+    }
+    if (tid == MS_THREADS - 32 && nrows > 0) {
+        const uint32_t kb = (uint32_t)nrows * I * 2;
+        mbar_expect_tx(&bar_rd, (uint32_t)K * kb);
+        for (int k = 0; k < K; k++)
+            bulk_g2s_stream(regD + (size_t)k * nrows * I, a.down + ((size_t)s_idx[k] * H + L.j0) * I, kb, &bar_rd);
+    }
     // 2. post-attention RMSNorm of x (block_rms_inv's order, the norm
     //    weight from shared memory)
     const float inv = block_rms_inv(xs, H, a.eps);
@@ -199,25 +247,12 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
     // the normalised activation in registers (lane l: chunks l + 32c)
     XRegBF16<MS_CPL> xr;
     xr.load(xs, H, lane);
-    // 3. warp 0: routing; warps 1..7 meanwhile: the shared expert's items
-    //    (weights already in shared memory)
-    if (warp == 0) {
-        const float rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(lg[E], (float)H), a.eps)));
-        for (int e = lane; e < E; e += 32) {
-            lg[e] = __fmul_rn(lg[e], rinv);
-            if (blockIdx.x == 0) a.scores[e] = lg[e];
-        }
-        __syncwarp();
-        router_select(lg, E, K, a.renorm, s_idx, s_wt);
-        __syncwarp();
-        if (blockIdx.x == 0 && lane < K) {
-            a.d_idx[lane] = s_idx[lane];
-            a.d_wt[lane] = s_wt[lane];
-        }
-        tr.mark(2);
-    } else if (ns > 0) {
+    // 3. the shared expert's items (weights already in shared memory) while
+    //    the routed loads fly
+    tr.mark(2);
+    if (ns > 0) {
         if (!mbar_wait(&bar_sh, 0, a.err)) return;
-        for (int it = warp - 1; it < ns; it += MS_WARPS - 1) {
+        for (int it = warp; it < ns; it += MS_WARPS) {
             const uint16_t *gr = regA + (size_t)it * H, *ur = regA + (size_t)(ns + it) * H;
             float g = 0.f, u = 0.f;
 #pragma unroll
@@ -231,30 +266,7 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
             if (lane == 0) a.h[nr + L.i0 + it] = swiglu_out(g, u);
         }
     }
-    __syncthreads();
     tr.mark(3);
-    // 4. routed down rows into shared memory (TMA), routed gate/up rows into
-    //    registers
-    if (tid == 0 && nrows > 0) {
-        const uint32_t kb = (uint32_t)nrows * I * 2;
-        mbar_expect_tx(&bar_rd, (uint32_t)K * kb);
-        for (int k = 0; k < K; k++)
-            bulk_g2s_stream(regD + (size_t)k * nrows * I, a.down + ((size_t)s_idx[k] * H + L.j0) * I, kb, &bar_rd);
-    }
-    auto item_rows = [&](int q, const uint16_t *&g, const uint16_t *&u) {
-        const int k = q / I, i = q - k * I;
-        const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
-        g = base + (size_t)i * H;
-        u = base + (size_t)(I + i) * H;
-    };
-    Rows2<MS_CPL> cur, nxt;
-    int q = L.q0 + warp;
-    if (q < L.q1) {
-        const uint16_t *g, *u;
-        item_rows(q, g, u);
-        cur.load(g, u, H, lane);
-    }
-    tr.mark(4);
     // 5. routed items, the next item's rows in flight during each dot
     for (; q < L.q1; q += MS_WARPS) {
         const int qn = q + MS_WARPS;
@@ -271,6 +283,7 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
         if (lane == 0) a.h[q] = swiglu_out(g, u);
     }
     tr.mark(6);
+    prefetch_next(a.pf, a.pf_bytes);
     if (a.launch_at == 1) pdl_launch();
     // 6. every h written (all CTAs), then h into shared memory
     if (!ms_grid_sync(a.bar, a.err)) return;
@@ -335,6 +348,222 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
     }
     if (a.launch_at == 2) pdl_launch();
     tr.done(10);
+}
+
+// ---------------------------------------------------------------------------
+// The dense FFN layer (dense_ffn_forward, ds_moe_decoder.c:75-105: gate and
+// up [D x H], SwiGLU without truncation, down [H x D], residual add) as ONE
+// kernel. No weight depends on the data, so a producer warp streams this
+// CTA's gate/up rows (8 items of gate row + up row per stage) through a
+// ring of shared-memory stages with the TMA engine, starting before the
+// dependency wait; eight consumer warps compute from shared memory. A grid
+// barrier separates the SwiGLU outputs from the down projection: once the
+// ring has drained, the producer copies this CTA's down rows (one bulk copy;
+// an earlier kernel of the step asked L2 for them) into the ring's space
+// while the CTAs synchronise; warp w then reads column range w of every
+// output row and the eight partial sums of a row are added in warp order.
+// The gate/up dot products associate as the per-phase kernel's
+// (moe_gate_up_kernel).
+// ---------------------------------------------------------------------------
+constexpr int DS_CONSUMERS = 8;
+constexpr int DS_THREADS = 32 * (DS_CONSUMERS + 1);
+constexpr int DS_NST = 4;                         // ring stages
+constexpr int DS_ITEMS = DS_CONSUMERS;            // gate/up items per stage (one per consumer warp)
+
+// Consumer-only grid barrier (named barrier 1 over the consumer warps; the
+// producer warp keeps streaming): same counter protocol as ms_grid_sync.
+__device__ __forceinline__ bool ds_grid_sync_consumers(unsigned long long *ctr, unsigned *err) {
+    __shared__ int ok;
+    asm volatile("bar.sync 1, %0;" :: "r"(32 * DS_CONSUMERS) : "memory");
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned long long old = atomicAdd(ctr, 1ull);
+        const unsigned long long target = (old / gridDim.x + 1ull) * gridDim.x;
+        int good = 0;
+        for (uint32_t it = 0; it < (1u << 24); it++) {
+            if (ld_acquire_u64(ctr) >= target) {
+                good = 1;
+                break;
+            }
+            if ((it & 1023u) == 1023u && *(volatile unsigned *)err) break;
+        }
+        if (!good) atomicExch(err, 1u);
+        __threadfence();
+        ok = good;
+    }
+    asm volatile("bar.sync 1, %0;" :: "r"(32 * DS_CONSUMERS) : "memory");
+    return ok != 0;
+}
+
+__global__ void __launch_bounds__(DS_THREADS, 1) dense_step_kernel(DenseStepArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bar_nw, bar_dn, full[DS_NST], empty[DS_NST];
+    __shared__ float red[MS_MAXROWS][DS_CONSUMERS];
+    TraceScope tr;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int H = a.H, D = a.D, G = gridDim.x, b = blockIdx.x;
+    const int i0 = (int)((long long)D * b / G), i1 = (int)((long long)D * (b + 1) / G);
+    const int j0 = (int)((long long)H * b / G), j1 = (int)((long long)H * (b + 1) / G);
+    const int ngu = (i1 - i0 + DS_ITEMS - 1) / DS_ITEMS;  // gate/up stages
+    const size_t stage_b = (size_t)DS_ITEMS * 2 * H * 2;
+    uint8_t *ring = smem;
+    float *xs = reinterpret_cast<float *>(smem + DS_NST * stage_b);
+    float *nws = xs + H;
+    float *hs = nws + H;
+    if (tid == 0) {
+        mbar_init(&bar_nw, 1);
+        mbar_init(&bar_dn, 1);
+        for (int st = 0; st < DS_NST; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], DS_CONSUMERS);
+        }
+        mbar_fence_init();
+        mbar_expect_tx(&bar_nw, (uint32_t)H * 4);
+        bulk_g2s(nws, a.norm_w, (uint32_t)H * 4, &bar_nw);
+    }
+    __syncthreads();
+    if (warp == DS_CONSUMERS) {
+        // producer: every stage's rows, before and after the dependency wait
+        if (lane == 0) {
+            for (int q = 0; q < ngu; q++) {
+                const int st = q % DS_NST;
+                if (q >= DS_NST && !mbar_wait(&empty[st], ((q / DS_NST) - 1) & 1, a.err)) break;
+                uint8_t *dst = ring + (size_t)st * stage_b;
+                const int ia = i0 + q * DS_ITEMS, cnt = min(DS_ITEMS, i1 - ia);
+                const uint32_t rb = (uint32_t)cnt * H * 2;
+                mbar_expect_tx(&full[st], 2 * rb);
+                bulk_g2s_stream(dst, a.gate + (size_t)ia * H, rb, &full[st]);
+                bulk_g2s_stream(dst + (size_t)DS_ITEMS * H * 2, a.up + (size_t)ia * H, rb, &full[st]);
+            }
+            // the down rows, once every stage has been consumed
+            bool ok = true;
+            for (int q = max(0, ngu - DS_NST); q < ngu && ok; q++)
+                ok = mbar_wait(&empty[q % DS_NST], (q / DS_NST) & 1, a.err);
+            if (ok && j1 > j0) {
+                const uint32_t db = (uint32_t)(j1 - j0) * D * 2;
+                mbar_expect_tx(&bar_dn, db);
+                bulk_g2s_stream(ring, a.down + (size_t)j0 * D, db, &bar_dn);
+            }
+        }
+        return;
+    }
+    pdl_wait();
+    pdl_launch();
+    tr.waited();
+    const int ctid = tid;  // consumers are threads 0 .. 255
+    for (int i = ctid * 4; i < H; i += 32 * DS_CONSUMERS * 4)
+        *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
+    asm volatile("bar.sync 1, %0;" :: "r"(32 * DS_CONSUMERS) : "memory");
+    // block_rms_inv's order over the consumer threads
+    float inv;
+    {
+        __shared__ float rr[DS_CONSUMERS + 1];
+        float ss = 0.f;
+        for (int i = ctid; i < H; i += 32 * DS_CONSUMERS) ss = __fmaf_rn(xs[i], xs[i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) rr[warp] = ss;
+        asm volatile("bar.sync 1, %0;" :: "r"(32 * DS_CONSUMERS) : "memory");
+        if (ctid == 0) {
+            float t = 0.f;
+            for (int w = 0; w < DS_CONSUMERS; w++) t = __fadd_rn(t, rr[w]);
+            rr[DS_CONSUMERS] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), a.eps)));
+        }
+        asm volatile("bar.sync 1, %0;" :: "r"(32 * DS_CONSUMERS) : "memory");
+        inv = rr[DS_CONSUMERS];
+    }
+    if (!mbar_wait(&bar_nw, 0, a.err)) return;
+    XRegBF16<MS_CPL> xr;
+    xr.load_norm(xs, nws, inv, H, lane);
+    tr.mark(0);
+    // gate/up stages: warp w takes item w of the stage
+    for (int q = 0; q < ngu; q++) {
+        const int st = q % DS_NST;
+        if (!mbar_wait(&full[st], (q / DS_NST) & 1, a.err)) return;
+        const int it = i0 + q * DS_ITEMS + warp;
+        if (it < i1) {
+            const uint16_t *gr = reinterpret_cast<const uint16_t *>(ring + (size_t)st * stage_b) + (size_t)warp * H;
+            const uint16_t *ur = gr + (size_t)DS_ITEMS * H;
+            float g = 0.f, u = 0.f;
+#pragma unroll
+            for (int c = 0; c < MS_CPL; c++) {
+                const int ch = lane + 32 * c;
+                g = dot8_bf16(*reinterpret_cast<const uint4 *>(gr + 8 * ch), xr.v[c][0], xr.v[c][1], g);
+                u = dot8_bf16(*reinterpret_cast<const uint4 *>(ur + 8 * ch), xr.v[c][0], xr.v[c][1], u);
+            }
+            g = warp_sum(g);
+            u = warp_sum(u);
+            if (lane == 0) a.h[it] = swiglu(g, u);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    tr.mark(1);
+    if (!ds_grid_sync_consumers(a.bar, a.err)) return;
+    tr.mark(2);
+    for (int i = ctid * 4; i < D; i += 32 * DS_CONSUMERS * 4)
+        *reinterpret_cast<float4 *>(hs + i) = __ldcg(reinterpret_cast<const float4 *>(a.h + i));
+    asm volatile("bar.sync 1, %0;" :: "r"(32 * DS_CONSUMERS) : "memory");
+    tr.mark(3);
+    // down rows from shared memory: warp w owns chunk range w of every row
+    const int nch = D >> 3;
+    const int per = (nch + DS_CONSUMERS - 1) / DS_CONSUMERS;
+    const int c0 = warp * per, c1 = min(nch, c0 + per);
+    const int nrows = j1 - j0;
+    if (nrows > 0 && !mbar_wait(&bar_dn, 0, a.err)) return;
+    tr.mark(4);
+    // all rows at once (independent accumulators; each h chunk read once)
+    {
+        const uint16_t *w0 = reinterpret_cast<const uint16_t *>(ring);
+        float acc[MS_MAXROWS];
+#pragma unroll
+        for (int r = 0; r < MS_MAXROWS; r++) acc[r] = 0.f;
+        for (int ch = c0 + lane; ch < c1; ch += 32) {
+            const float4 *hp = reinterpret_cast<const float4 *>(hs + 8 * ch);
+            const float4 h0 = hp[0], h1 = hp[1];
+#pragma unroll
+            for (int r = 0; r < MS_MAXROWS; r++)
+                if (r < nrows) acc[r] = dot8_bf16(*reinterpret_cast<const uint4 *>(w0 + (size_t)r * D + 8 * ch), h0, h1, acc[r]);
+        }
+#pragma unroll
+        for (int r = 0; r < MS_MAXROWS; r++) {
+            if (r < nrows) {
+                const float v = warp_sum(acc[r]);
+                if (lane == 0) red[r][warp] = v;
+            }
+        }
+    }
+    tr.mark(5);
+    asm volatile("bar.sync 1, %0;" :: "r"(32 * DS_CONSUMERS) : "memory");
+    tr.mark(6);
+    if (ctid < nrows) {
+        float t = 0.f;
+        for (int k = 0; k < DS_CONSUMERS; k++) t = __fadd_rn(t, red[ctid][k]);
+        const int j = j0 + ctid;
+        a.out[j] = __fadd_rn(__ldcg(a.x + j), t);
+    }
+    tr.mark(7);
+    prefetch_next(a.pf, a.pf_bytes);
+    tr.done(11);
+}
+
+bool dense_step_supported(int H, int D, int sms) {
+    const size_t stage_b = (size_t)DS_ITEMS * 2 * H * 2;
+    return H == 1280 && D % 8 == 0 && sms >= 1 && (H + sms - 1) / sms <= MS_MAXROWS &&
+           (size_t)((H + sms - 1) / sms) * D * 2 <= DS_NST * stage_b &&
+           DS_NST * stage_b + (size_t)(2 * H + D) * 4 <= 210 * 1024;
+}
+
+cudaError_t launch_dense_step(DenseStepArgs a, int grid, cudaStream_t st, bool pdl) {
+    const size_t smem = DS_NST * (size_t)DS_ITEMS * 2 * a.H * 2 + (size_t)(2 * a.H + a.D) * 4;
+    static size_t set = 0;
+    if (set < smem) {
+        cudaError_t e = cudaFuncSetAttribute((const void *)dense_step_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        set = smem;
+    }
+    void *args[] = {&a};
+    return launch_ex((const void *)dense_step_kernel, grid, DS_THREADS, smem, st, pdl, args);
 }
 
 bool moe_step_supported(int H, int I, int S, int E, int K, int sms) {

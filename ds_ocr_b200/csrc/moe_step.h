@@ -19,14 +19,32 @@ struct MoeStepArgs {
     const uint16_t *sdown;   // shared down projection [H][S]
     float *h;                // SwiGLU outputs [K*I + S] (global: every CTA reads all of it)
     float *out;              // x + MoE(x) [H]
-    int *d_idx;              // routing, published by CTA 0
+    int *d_idx;              // routing, published by CTA 0 (for inspection)
     float *d_wt, *scores;
     unsigned long long *bar; // grid-barrier counter (only ever incremented)
     unsigned *err;           // set when a bounded wait gives up
+    const void *pf[3];       // the next layer's Q, K, V weights: asked of L2 once this CTA's stream is done
+    size_t pf_bytes;         // bytes of each (0: none)
     size_t a_bytes, d_bytes; // shared-memory regions (set by the launcher)
     int launch_at;
 };
 
+struct DenseStepArgs {
+    int H, D;                // hidden, dense intermediate
+    float eps;
+    const float *x;          // residual stream after attention [H]
+    const float *norm_w;     // post-attention RMSNorm weight [H]
+    const uint16_t *gate, *up, *down;  // [D x H], [D x H], [H x D]
+    float *h;                // SwiGLU outputs [D]
+    float *out;              // x + FFN(x) [H]
+    unsigned long long *bar; // grid-barrier counter (only ever incremented)
+    unsigned *err;
+    const void *pf[3];       // the next layer's Q, K, V weights (see MoeStepArgs)
+    size_t pf_bytes;
+};
+
+bool dense_step_supported(int H, int D, int sms);
+cudaError_t launch_dense_step(DenseStepArgs a, int grid, cudaStream_t st, bool pdl);
 bool moe_step_supported(int H, int I, int S, int E, int K, int sms);
 size_t moe_step_smem(int H, int I, int S, int K, int grid);
 cudaError_t launch_moe_step(MoeStepArgs a, int grid, cudaStream_t st, bool pdl);

@@ -166,7 +166,7 @@ def test_fused_step_matches_per_phase_kernels(cuda_ctx, small_model, simulate):
         os.environ.pop("DS_CUDA_DECODE_PER_PHASE", None)
         cuda_ctx.set_numerics(simulate_bf16=0)
     (a, la), (b, lb) = runs
-    assert lb == la - 2  # two MoE layers, one launch fewer each
+    assert lb == la - 3  # the dense layer and the two MoE layers: one launch fewer each
     y = synth.bf16_to_f32(small_model.lm_head)
     for s, ((t0, x0), (t1, x1)) in enumerate(zip(a, b)):
         # simulate=1 truncates to BF16 inside the MoE: a rounding-level

@@ -36,7 +36,8 @@ struct DecoderModel {
     int *idx = nullptr, *pos = nullptr, *tok = nullptr, *tok_log = nullptr;
     unsigned *tickets = nullptr;  // [0] LM head, [1] router, [8] LM-head wait error, [9] MoE-step wait error
     unsigned long long *slot = nullptr;
-    unsigned long long *step_bar = nullptr;  // grid-barrier counter of the MoE-step kernel
+    unsigned long long *step_bar = nullptr;  // grid-barrier counters of the MoE-step and dense-step kernels
+    unsigned long long *step_done = nullptr; // completion counters of the MoE-step kernel (top_k + 1)
     bool fused_moe = false;                  // MoE layers run as one kernel (moe_step.cu)
     uint16_t *kv = nullptr;  // 4 planes: k_hi, k_lo, v_hi, v_lo, each [L][heads][kv_max][hd]
     float *cos_t = nullptr, *sin_t = nullptr;
@@ -241,6 +242,7 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             ms.d_wt = m->wt;
             ms.scores = m->scores;
             ms.bar = m->step_bar;
+            ms.done = m->step_done;
             ms.err = m->tickets + 9;
             if (l + 1 < g.n_layers) {
                 const DecLayer &N = m->layers[l + 1];
@@ -265,7 +267,7 @@ static int enqueue_step(ds_cuda_ctx *c, DecoderModel *m, cudaStream_t st, bool w
             ds.down = L.ddown;
             ds.h = m->h;
             ds.out = m->xa;
-            ds.bar = m->step_bar;
+            ds.bar = m->step_bar + 1;
             ds.err = m->tickets + 9;
             if (l + 1 < g.n_layers) {
                 const DecLayer &N = m->layers[l + 1];
@@ -637,7 +639,8 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->logits, (size_t)g.vocab);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->tickets, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->slot, 16);
-    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->step_bar, 1);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->step_bar, 2);
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->step_done, 16);
     if (rc == DS_CUDA_OK) {
         // the MoE block as one kernel where its shapes allow (BF16 experts);
         // DS_CUDA_DECODE_PER_PHASE=1 keeps the per-phase kernels (same numerics)

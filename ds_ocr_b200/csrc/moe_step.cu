@@ -104,64 +104,76 @@ __device__ __forceinline__ void prefetch_next(const void *const (&pf)[3], size_t
         if (pf[m] && hi > lo) prefetch_range(static_cast<const uint8_t *>(pf[m]) + lo, hi - lo);
 }
 
-__global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) {
+// Named barrier over the consumer warps only (the producer warp never joins).
+__device__ __forceinline__ void ms_cbar() { asm volatile("bar.sync 1, %0;" :: "r"(MS_THREADS) : "memory"); }
+
+__global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bar_sh, bar_sd, bar_rd, bar_nw;
+    __shared__ uint64_t bar_sh, bar_sd, bar_rd, bar_nw, bar_route;
     __shared__ float lg[MS_MAXE + 1];
     __shared__ float lsum[MS_MAXE + 1][3];
+    __shared__ float rr[MS_WARPS + 1];
     __shared__ int s_idx[8];
     __shared__ float s_wt[8];
     __shared__ float ysm[MS_MAXROWS][10];
+    __shared__ unsigned long long s_epoch;
     TraceScope tr;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int H = a.H, I = a.I, S = a.S, K = a.K, E = a.E;
     const int nr = K * I;
     const MsLayout L = ms_layout(a);
     const int ns = L.i1 - L.i0, nrows = L.j1 - L.j0;
-    // shared memory: A = shared gate/up rows (later h), D = down rows, xs
+    // shared memory: A = shared gate/up rows, D = down rows, xs, norm weight
     uint16_t *regA = reinterpret_cast<uint16_t *>(smem);
     uint16_t *regD = reinterpret_cast<uint16_t *>(smem + a.a_bytes);
     float *xs = reinterpret_cast<float *>(smem + a.a_bytes + a.d_bytes);
-    float *nws = xs + H;  // post-attention norm weight
-    float *hs = reinterpret_cast<float *>(smem);
+    float *nws = xs + H;
     const uint16_t *sgu = a.block + (size_t)E * 2 * I * H;
 
     if (tid == 0) {
+        // this launch's number (every CTA of a launch adds one): the
+        // completion counters below only ever grow
+        s_epoch = atomicAdd(a.bar, 1ull) / gridDim.x;
         mbar_init(&bar_sh, 1);
         mbar_init(&bar_sd, 1);
         mbar_init(&bar_rd, 1);
         mbar_init(&bar_nw, 1);
+        mbar_init(&bar_route, 1);
         mbar_fence_init();
-        mbar_expect_tx(&bar_nw, (uint32_t)H * 4);
-        bulk_g2s(nws, a.norm_w, (uint32_t)H * 4, &bar_nw);
-        // routing-independent weights: the shared expert's gate/up rows of
-        // this CTA's items and its down rows of this CTA's outputs
-        if (ns > 0) {
-            const uint32_t rb = (uint32_t)ns * H * 2;
-            mbar_expect_tx(&bar_sh, 2 * rb);
-            bulk_g2s_stream(regA, sgu + (size_t)L.i0 * H, rb, &bar_sh);
-            bulk_g2s_stream(regA + (size_t)ns * H, sgu + (size_t)(S + L.i0) * H, rb, &bar_sh);
-        }
-        if (nrows > 0) {
-            const uint32_t db = (uint32_t)nrows * S * 2;
-            mbar_expect_tx(&bar_sd, db);
-            bulk_g2s_stream(regD + (size_t)K * nrows * I, a.sdown + (size_t)L.j0 * S, db, &bar_sd);
-        }
     }
     __syncthreads();
-    pdl_wait();
-    if (a.launch_at == 0) pdl_launch();
-    tr.waited();
-    if (a.launch_at == 3) {  // debug: time of the routing-independent copies only
-        if (ns > 0) mbar_wait(&bar_sh, 0, a.err);
-        tr.mark(0);
-        if (nrows > 0) mbar_wait(&bar_sd, 0, a.err);
-        tr.mark(1);
-        mbar_wait(&bar_nw, 0, a.err);
-        tr.mark(2);
-        tr.done(10);
+    if (warp == MS_WARPS) {
+        // producer warp: every TMA copy, so no consumer warp waits behind an
+        // issue. Before the dependency wait: the norm weight, the shared
+        // expert's gate/up rows of this CTA's items and its down rows of this
+        // CTA's outputs; once warp 0 has the routing: the routed down rows.
+        if (lane == 0) {
+            mbar_expect_tx(&bar_nw, (uint32_t)H * 4);
+            bulk_g2s(nws, a.norm_w, (uint32_t)H * 4, &bar_nw);
+            if (ns > 0) {
+                const uint32_t rb = (uint32_t)ns * H * 2;
+                mbar_expect_tx(&bar_sh, 2 * rb);
+                bulk_g2s_stream(regA, sgu + (size_t)L.i0 * H, rb, &bar_sh);
+                bulk_g2s_stream(regA + (size_t)ns * H, sgu + (size_t)(S + L.i0) * H, rb, &bar_sh);
+            }
+            if (nrows > 0) {
+                const uint32_t db = (uint32_t)nrows * S * 2;
+                mbar_expect_tx(&bar_sd, db);
+                bulk_g2s_stream(regD + (size_t)K * nrows * I, a.sdown + (size_t)L.j0 * S, db, &bar_sd);
+            }
+            if (mbar_wait(&bar_route, 0, a.err) && nrows > 0) {
+                const uint32_t kb = (uint32_t)nrows * I * 2;
+                mbar_expect_tx(&bar_rd, (uint32_t)K * kb);
+                for (int k = 0; k < K; k++)
+                    bulk_g2s_stream(regD + (size_t)k * nrows * I, a.down + ((size_t)s_idx[k] * H + L.j0) * I, kb,
+                                    &bar_rd);
+            }
+        }
         return;
     }
+    pdl_wait();
+    pdl_launch();
+    tr.waited();
 
     // 1. router logits: column e of the O-proj CTAs' terms summed in three
     //    runs of consecutive CTAs, each in CTA order, then (r0 + r1) + r2
@@ -182,9 +194,15 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
     }
     for (int i = tid * 4; i < H; i += MS_THREADS * 4)
         *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
-    __syncthreads();
+    ms_cbar();
     tr.mark(0);
-    // routing: softmax and top-k of the logits scaled by the RMS of x
+    // 2. warp 0: routing (softmax and top-k of the logits scaled by the RMS
+    //    of x), handed to the producer warp; the others meanwhile: the sum
+    //    of squares of x (block_rms_inv's order over 8 warps)
+    float ss = 0.f;
+    for (int i = tid; i < H; i += MS_THREADS) ss = __fmaf_rn(xs[i], xs[i], ss);
+    ss = warp_sum(ss);
+    if (lane == 0) rr[warp] = ss;
     if (warp == 0) {
         for (int e = lane; e <= E; e += 32) lg[e] = __fadd_rn(__fadd_rn(lsum[e][0], lsum[e][1]), lsum[e][2]);
         __syncwarp();
@@ -196,14 +214,15 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
         __syncwarp();
         router_select(lg, E, K, a.renorm, s_idx, s_wt);
         __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_route);
         if (blockIdx.x == 0 && lane < K) {
             a.d_idx[lane] = s_idx[lane];
             a.d_wt[lane] = s_wt[lane];
         }
     }
-    __syncthreads();
-    // routed gate/up rows into registers and (the last warp's lane 0) the
-    // routed down rows into shared memory (TMA), as soon as the routing is known
+    ms_cbar();
+    tr.mark(1);
+    // 3. routed gate/up rows into registers as soon as the routing is known
     auto item_rows = [&](int q, const uint16_t *&g, const uint16_t *&u) {
         const int k = q / I, i = q - k * I;
         const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
@@ -217,23 +236,15 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
         item_rows(q, g, u);
         cur.load(g, u, H, lane);
     }
-    if (tid == MS_THREADS - 32 && nrows > 0) {
-        const uint32_t kb = (uint32_t)nrows * I * 2;
-        mbar_expect_tx(&bar_rd, (uint32_t)K * kb);
-        for (int k = 0; k < K; k++)
-            bulk_g2s_stream(regD + (size_t)k * nrows * I, a.down + ((size_t)s_idx[k] * H + L.j0) * I, kb, &bar_rd);
+    // post-attention RMSNorm of x with the norm weight from shared memory
+    if (tid == 0) {
+        float t = 0.f;
+        for (int w = 0; w < MS_WARPS; w++) t = __fadd_rn(t, rr[w]);
+        rr[MS_WARPS] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), a.eps)));
     }
-    // 2. post-attention RMSNorm of x (block_rms_inv's order, the norm
-    //    weight from shared memory)
-    const float inv = block_rms_inv(xs, H, a.eps);
     if (!mbar_wait(&bar_nw, 0, a.err)) return;
-    for (int i = tid * 4; i < H; i += MS_THREADS * 4) {
-        const float4 xv = *reinterpret_cast<const float4 *>(xs + i);
-        const float4 wv = *reinterpret_cast<const float4 *>(nws + i);
-        *reinterpret_cast<float4 *>(xs + i) = norm4(xv, wv, inv);
-    }
-    __syncthreads();
-    tr.mark(1);
+    ms_cbar();
+    const float inv = rr[MS_WARPS];
     const bool sim = a.simulate != 0;
     auto swiglu_out = [&](float g, float u) {
         if (sim) {
@@ -244,12 +255,11 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
         if (sim) hv = bf16_roundtrip(hv);
         return hv;
     };
-    // the normalised activation in registers (lane l: chunks l + 32c)
     XRegBF16<MS_CPL> xr;
-    xr.load(xs, H, lane);
-    // 3. the shared expert's items (weights already in shared memory) while
-    //    the routed loads fly
+    xr.load_norm(xs, nws, inv, H, lane);
     tr.mark(2);
+    // 4. the shared expert's items (weights already in shared memory) while
+    //    the routed loads fly
     if (ns > 0) {
         if (!mbar_wait(&bar_sh, 0, a.err)) return;
         for (int it = warp; it < ns; it += MS_WARPS) {
@@ -265,6 +275,12 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
             u = warp_sum(u);
             if (lane == 0) a.h[nr + L.i0 + it] = swiglu_out(g, u);
         }
+    }
+    // this CTA's shared items are in h: count it (release)
+    ms_cbar();
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(a.done + K, 1ull);
     }
     tr.mark(3);
     // 5. routed items, the next item's rows in flight during each dot
@@ -282,30 +298,52 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
         u = warp_sum(u);
         if (lane == 0) a.h[q] = swiglu_out(g, u);
     }
-    tr.mark(6);
-    prefetch_next(a.pf, a.pf_bytes);
-    if (a.launch_at == 1) pdl_launch();
-    // 6. every h written (all CTAs), then h into shared memory
-    if (!ms_grid_sync(a.bar, a.err)) return;
-    const int hn = nr + S;
-    for (int i = tid * 4; i < hn; i += MS_THREADS * 4)
-        *reinterpret_cast<float4 *>(hs + i) = __ldcg(reinterpret_cast<const float4 *>(a.h + i));
-    if (nrows > 0) {
-        if (!mbar_wait(&bar_sd, 0, a.err)) return;
-        if (!mbar_wait(&bar_rd, 0, a.err)) return;
+    // count this CTA's routed slots as done (release)
+    ms_cbar();
+    if (tid == 0 && L.q1 > L.q0) {
+        __threadfence();
+        for (int k = L.q0 / I; k < K && k * I < L.q1; k++) atomicAdd(a.done + k, 1ull);
     }
-    __syncthreads();
-    tr.mark(7);
-    // 7. down dot products: warp s owns slot s (s < K: routed expert s;
-    //    K, K + 1: the two halves of the shared expert's rows), its slice of
-    //    h in registers, and walks this CTA's output rows two at a time
+    tr.mark(4);
+    prefetch_next(a.pf, a.pf_bytes);
+    // 6. down dot products: warp s owns slot s (s < K: routed expert s;
+    //    K, K + 1: the two halves of the shared expert's rows). It waits
+    //    until every CTA that computes part of its slice of h has counted it
+    //    done (no grid-wide barrier: the shared slots start at once, a
+    //    routed slot waits only for its own producer CTAs), loads that slice
+    //    into registers and walks this CTA's output rows two at a time.
     const int half = S >> 1;
     if (warp < K + 2) {
         const int s = warp;
-        const float *hv = s < K ? hs + s * I : hs + nr + (s - K) * half;
-        XRegBF16<MS_DCPL> hr;
-        hr.load(hv, I, lane);
+        const unsigned long long need =
+            (s_epoch + 1) * (s < K ? (unsigned long long)a.ncta[s] : (unsigned long long)gridDim.x);
+        const unsigned long long *ctr = a.done + (s < K ? s : K);
+        bool ok = false;
+        for (uint32_t it = 0; it < (1u << 24); it++) {
+            if (ld_acquire_u64(ctr) >= need) {
+                ok = true;
+                break;
+            }
+            if ((it & 1023u) == 1023u && *(volatile unsigned *)a.err) break;
+        }
+        if (!ok) {
+            if (lane == 0) atomicExch(a.err, 1u);
+            return;
+        }
+        const float *hv = s < K ? a.h + s * I : a.h + nr + (s - K) * half;
         const int nch = I >> 3;
+        XRegBF16<MS_DCPL> hr;
+#pragma unroll
+        for (int c = 0; c < MS_DCPL; c++) {
+            const int ch = lane + 32 * c;
+            if (ch < nch) {
+                hr.v[c][0] = __ldcg(reinterpret_cast<const float4 *>(hv + 8 * ch));
+                hr.v[c][1] = __ldcg(reinterpret_cast<const float4 *>(hv + 8 * ch + 4));
+            } else {
+                hr.v[c][0] = hr.v[c][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        if (nrows > 0 && !mbar_wait(s < K ? &bar_rd : &bar_sd, 0, a.err)) return;
         auto wrow = [&](int r) {
             return s < K ? regD + ((size_t)s * nrows + r) * I
                          : regD + (size_t)K * nrows * I + (size_t)r * S + (s - K) * half;
@@ -330,8 +368,9 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
             }
         }
     }
-    __syncthreads();
-    // 8. combine in the reference's order (ds_expert_combine, then + shared)
+    ms_cbar();
+    tr.mark(5);
+    // 7. combine in the reference's order (ds_expert_combine, then + shared)
     //    and the residual add
     if (tid < nrows) {
         const int j = L.j0 + tid;
@@ -346,7 +385,6 @@ __global__ void __launch_bounds__(MS_THREADS, 1) moe_step_kernel(MoeStepArgs a) 
         acc = __fadd_rn(acc, sh);
         a.out[j] = __fadd_rn(__ldcg(a.x + j), acc);
     }
-    if (a.launch_at == 2) pdl_launch();
     tr.done(10);
 }
 
@@ -597,10 +635,17 @@ cudaError_t launch_moe_step(MoeStepArgs a, int grid, cudaStream_t st, bool pdl) 
         if (e != cudaSuccess) return e;
         set = smem;
     }
-    static const char *la = getenv("DS_MS_LAUNCH_AT");
-    a.launch_at = la ? atoi(la) : 0;
+    // CTAs whose routed item range [nr b / G, nr (b + 1) / G) meets slot k's
+    // [k I, (k + 1) I): the count slot k's completion counter grows by
+    const long long nr = (long long)a.K * a.I;
+    for (int k = 0; k < 8; k++) a.ncta[k] = 0;
+    for (int b = 0; b < grid; b++) {
+        const long long q0 = nr * b / grid, q1 = nr * (b + 1) / grid;
+        if (q1 <= q0) continue;
+        for (int k = (int)(q0 / a.I); k < a.K && (long long)k * a.I < q1; k++) a.ncta[k]++;
+    }
     void *args[] = {&a};
-    return launch_ex((const void *)moe_step_kernel, grid, MS_THREADS, smem, st, pdl, args);
+    return launch_ex((const void *)moe_step_kernel, grid, MS_THREADS + 32, smem, st, pdl, args);
 }
 
 }  // namespace ds

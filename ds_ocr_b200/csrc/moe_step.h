@@ -21,12 +21,13 @@ struct MoeStepArgs {
     float *out;              // x + MoE(x) [H]
     int *d_idx;              // routing, published by CTA 0 (for inspection)
     float *d_wt, *scores;
-    unsigned long long *bar; // grid-barrier counter (only ever incremented)
+    unsigned long long *bar; // launch counter (every CTA adds 1 per launch; only ever incremented)
+    unsigned long long *done;// [K + 1] completion counters: routed slot k's h rows, then the shared rows
     unsigned *err;           // set when a bounded wait gives up
     const void *pf[3];       // the next layer's Q, K, V weights: asked of L2 once this CTA's stream is done
     size_t pf_bytes;         // bytes of each (0: none)
     size_t a_bytes, d_bytes; // shared-memory regions (set by the launcher)
-    int launch_at;
+    int ncta[8];             // CTAs contributing to each routed slot (set by the launcher)
 };
 
 struct DenseStepArgs {

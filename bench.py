@@ -178,18 +178,59 @@ class MoeLayerWorkload:
                 "l2": "weights rotate over 11 layers (5.0 GB) > L2"}
 
 
-def run_ours_moe(args, rank, world, pg):
+# Config 2: the INT8 (--int4) expert path. Per token: the BF16 router plus,
+# for each of the 6 routed experts, gate/up int8 [1792 x 1280] + 2 x 1792
+# F32 scale/offset and down int8 [1280 x 896] + 2 x 1280 F32, and the shared
+# expert's int8 gate/up [3584 x 1280] + 2 x 3584 F32 and down [1280 x 1792]
+# + 2 x 1280 F32.
+INT8_BYTES_PER_TOKEN = (163840 + 6 * (2293760 + 14336 + 1146880 + 10240)
+                        + (4587520 + 28672 + 2293760 + 10240))
+
+
+class MoeLayerInt8Workload(MoeLayerWorkload):
+    """Config 2: config 0's layers with per-row INT8 expert copies,
+    quantised by the GPU quantiser (bit-identical to ds_int4_quantize_bf16)."""
+
+    name = "moe_layer_int8"
+    metric = "INT8 MoE layer decode tokens/s (1 token, 64 experts top-6 + 2 shared, per-row INT8 experts)"
+
+    def __init__(self, ctx=None, n_layers=11, n_inputs=64):
+        super().__init__(n_layers, n_inputs)
+        if ctx is not None:
+            self.quantize(ctx)
+
+    def quantize(self, ctx):
+        from ds_ocr_b200 import synth
+        from ds_ocr_b200.decoder import quantize_int8
+        carrier = synth.Model.__new__(synth.Model)
+        carrier.d = self.d
+        carrier.layers = [type("L", (), {"moe": m})() for m in self.layers]
+        quantize_int8(carrier, ctx)
+
+    def config(self):
+        c = super().config()
+        c.update(workload="config2_moe_layer_int8", experts_dtype="int8 per-row asymmetric",
+                 l2="int8 weights rotate over 11 layers (2.5 GB) > L2")
+        return c
+
+
+def run_ours_moe(args, rank, world, pg, int8=False):
     import torch
     from ds_ocr_b200 import cuda
-    wl = MoeLayerWorkload()
-    d = wl.d
     ctx = cuda.Context(0 if world == 1 else int(os.environ.get("LOCAL_RANK", "0")))
+    wl = MoeLayerInt8Workload(ctx) if int8 else MoeLayerWorkload()
+    d = wl.d
     lib = ctx.lib
+    Q8 = ("gu_q", "gu_s", "gu_o", "dn_q", "dn_s", "dn_o", "sgu_q", "sgu_s", "sgu_o", "sdn_q", "sdn_s", "sdn_o")
     for mw in wl.layers:
         for a in (mw.router, mw.block, mw.down, mw.shared_down):
             ctx.register(a)
+        if int8:
+            for n in Q8:
+                ctx.register(getattr(mw.int8, n))
     dev = [(ctx.device_ptr(m.router), ctx.device_ptr(m.block), ctx.device_ptr(m.down), ctx.device_ptr(m.shared_down))
            for m in wl.layers]
+    dev8 = [[ctx.device_ptr(getattr(m.int8, n)) for n in Q8] for m in wl.layers] if int8 else None
     dX = torch.from_numpy(wl.X).cuda()
     dout = torch.empty((wl.X.shape[0], d.hidden), device="cuda")
     didx = torch.empty((wl.X.shape[0], 8), dtype=torch.int32, device="cuda")
@@ -201,9 +242,14 @@ def run_ours_moe(args, rank, world, pg):
     def step(s):
         r, b, dn, sd = dev[s % nL]
         i = s % nX
-        rc = lib.ds_cuda_moe_layer_dev(ctx.h, dX[i].data_ptr(), dout[i].data_ptr(), r, b, dn, sd, d.hidden,
-                                       d.moe_inter, d.shared_inter, d.n_experts, d.top_k, didx[i].data_ptr(),
-                                       dw[i].data_ptr(), None)
+        if int8:
+            rc = lib.ds_cuda_moe_layer_int8_dev(ctx.h, dX[i].data_ptr(), dout[i].data_ptr(), r, *dev8[s % nL],
+                                                d.hidden, d.moe_inter, d.shared_inter, d.n_experts, d.top_k,
+                                                didx[i].data_ptr(), dw[i].data_ptr(), None)
+        else:
+            rc = lib.ds_cuda_moe_layer_dev(ctx.h, dX[i].data_ptr(), dout[i].data_ptr(), r, b, dn, sd, d.hidden,
+                                           d.moe_inter, d.shared_inter, d.n_experts, d.top_k, didx[i].data_ptr(),
+                                           dw[i].data_ptr(), None)
         assert rc == 0, lib.ds_cuda_last_error(ctx.h)
 
     for s in range(args.warmup):
@@ -230,7 +276,10 @@ def run_ours_moe(args, rank, world, pg):
     t0.record(st)
     for s in range(e2e_steps):
         mw = wl.layers[s % nL]
-        ctx.moe_layer(wl.X[s % nX], mw)
+        if int8:
+            ctx.moe_layer_int8(wl.X[s % nX], mw)
+        else:
+            ctx.moe_layer(wl.X[s % nX], mw)
     t1.record(st)
     t1.synchronize()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1), pg)
@@ -242,36 +291,52 @@ def run_ours_moe(args, rank, world, pg):
         "gpu_launches": 3 * args.steps, "config": wl.config(), "metric": wl.metric, "unit": wl.unit,
         "dtype": "bf16 weights, f32 math",
     }
-    achieved = MOE_BYTES_PER_TOKEN / (ms_max / args.steps / 1e3) / 1e9
+    bpt = INT8_BYTES_PER_TOKEN if int8 else MOE_BYTES_PER_TOKEN
+    achieved = bpt / (ms_max / args.steps / 1e3) / 1e9
     pk = peaks()
     res["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                        "frac": achieved / pk["hbm_gbs"], "traffic": None,
-                       "kernel": "moe layer (router + gate_up + down), 55,214,080 B/token",
+                       "kernel": f"moe layer (router + gate_up + down{', INT8 experts' if int8 else ''}), "
+                                 f"{bpt:,} B/token",
                        "peak_source": pk["source"]}
+    if int8:
+        res["dtype"] = "int8 expert weights (per-row scale/offset), bf16 router, f32 math"
     ctx.close()
     return res
 
 
-def ref_moe_time(wl, threads, budget_s):
+def ref_moe_time(wl, threads, budget_s, int8=False):
     """Times the reference's own moe_forward (compiled unmodified into
     oracle/_ref/libdsref.so) on the same layers and inputs, `threads` host
-    threads, for about budget_s seconds of work. Returns (tokens/s, calls)."""
+    threads, for about budget_s seconds of work. Returns (tokens/s, calls).
+    int8: the reference's --int4 path (its own ds_int4_quantize_bf16, then
+    moe_forward's INT8 branch, ds_moe_decoder.c:237-243, 269-278) on the
+    first 3 layers (quantised outside the timed calls; 0.7 GB of INT8
+    weights, far above the host caches)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     from ds_ocr_b200 import synth
+    nl = 3 if int8 else 1
     carrier = synth.Model.__new__(synth.Model)
-    carrier.d = synth.Dims(n_layers=2, vocab=16)
+    carrier.d = synth.Dims(n_layers=1 + nl, vocab=16)
     carrier.layers = []
     carrier.final_norm = np.ones(1280, np.float32)
     carrier.lm_head = np.zeros((16, 1280), np.uint16)
     R = O.RefDecoder(carrier, kv_max=8, threads=threads)
+    if int8:
+        for l in range(nl):
+            R.set_layer(1 + l, wl.layers[l])
+        R.r.ref_ctx_quantize(R.ctx)
     n, t_total = 0, 0.0
     while t_total < budget_s:
-        mw = wl.layers[n % len(wl.layers)]
-        R.set_layer(1, mw)
+        if int8:
+            layer = 1 + n % nl
+        else:
+            layer = 1
+            R.set_layer(1, wl.layers[n % len(wl.layers)])
         x = wl.X[n % wl.X.shape[0]]
         t = time.perf_counter()
-        R.moe_forward(1, x)
+        R.moe_forward(layer, x)
         t_total += time.perf_counter() - t
         n += 1
     R.close()
@@ -1033,7 +1098,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "decode64", "moe_layer", "prefill", "prefill_full", "lm_head"])
+                    choices=["decode", "decode64", "moe_layer", "moe_layer_int8", "prefill", "prefill_full",
+                             "lm_head"])
     ap.add_argument("--engine", type=int, default=0, choices=[0, 1],
                     help="decode engine: 0 CUDA graph of per-phase kernels, 1 persistent kernel")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of reference CPU work to time")
@@ -1092,12 +1158,19 @@ def main():
                       "11 MoE layers)")
             cfg = prefill_full_config(PF_TOKENS)
             sample = f"one ds_decoder_prefill of the first {n} tokens (12 layers)"
+        elif args.workload == "moe_layer_int8":
+            wl = MoeLayerInt8Workload(n_layers=3)
+            v, n = ref_moe_time(wl, T, max(args.cpu_budget, 1.0), int8=True)
+            metric, cfg = wl.metric, dict(wl.config(), layers_rotated=11)
+            sample = f"{n} single-token INT8 moe_forward calls over 3 layers quantised by the reference"
         else:
             wl = MoeLayerWorkload()
             v, n = ref_moe_time(wl, T, max(args.cpu_budget, 1.0))
             metric, cfg, sample = wl.metric, wl.config(), f"{n} single-token moe_forward calls over 11 layers"
         line = {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": 0, "steps": n,
-                "warmup": 1, "ms_per_step": 1e3 / v, "dtype": "bf16 weights, f32 math", "config": cfg,
+                "warmup": 1, "ms_per_step": 1e3 / v,
+                "dtype": ("int8 expert weights (per-row scale/offset), bf16 router, f32 math"
+                          if args.workload == "moe_layer_int8" else "bf16 weights, f32 math"), "config": cfg,
                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": T, "kind": "reference", "sample": sample},
                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         line.update(common)
@@ -1123,6 +1196,8 @@ def main():
         prefixes = [synth.kv_prefix(model.d, PREFIX, stream=s) for s in range(MS_STREAMS)]
         ks, vs = prefixes[0]
         res = run_ours_decode_streams(args, rank, world, pg, model, prefixes)
+    elif args.workload == "moe_layer_int8":
+        res = run_ours_moe(args, rank, world, pg, int8=True)
     else:
         res = run_ours_moe(args, rank, world, pg)
     if rank != 0:
@@ -1153,6 +1228,10 @@ def main():
                 v, n = ref_prefill_full_time(model, T)
                 sample = f"one ds_decoder_prefill of the first {n} tokens (12 layers; the attention share grows " \
                          "with the length, so 3328 tokens run slower per token)"
+            elif args.workload == "moe_layer_int8":
+                wl = MoeLayerInt8Workload(n_layers=3)
+                v, n = ref_moe_time(wl, T, args.cpu_budget, int8=True)
+                sample = f"{n} single-token INT8 moe_forward calls over 3 layers quantised by the reference"
             else:
                 wl = MoeLayerWorkload()
                 v, n = ref_moe_time(wl, T, args.cpu_budget)

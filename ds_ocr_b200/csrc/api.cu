@@ -513,6 +513,45 @@ extern "C" int ds_cuda_moe_layer_int8(ds_cuda_ctx_t *c, const float *x, float *o
     return DS_CUDA_OK;
 }
 
+// Device-pointer form of ds_cuda_moe_layer_int8 (every pointer device
+// memory, enqueued on `stream`, nothing copied to or from the host).
+extern "C" int ds_cuda_moe_layer_int8_dev(ds_cuda_ctx_t *c, const float *d_x, float *d_out, const uint16_t *d_router,
+                                          const int8_t *gu_q, const float *gu_s, const float *gu_o,
+                                          const int8_t *dn_q, const float *dn_s, const float *dn_o,
+                                          const int8_t *sgu_q, const float *sgu_s, const float *sgu_o,
+                                          const int8_t *sdn_q, const float *sdn_s, const float *sdn_o, int hidden,
+                                          int inter, int shared_inter, int n_experts, int top_k, int *d_top_idx,
+                                          float *d_top_w, void *stream) {
+    if (!c || !d_x || !d_out || !d_router || !gu_q || !gu_s || !gu_o || !dn_q || !dn_s || !dn_o)
+        return ctx_fail(c, DS_CUDA_EINVAL, "moe_layer_int8_dev: null argument");
+    bool shared = shared_inter > 0 && sgu_q && sgu_s && sgu_o && sdn_q && sdn_s && sdn_o;
+    CK(layer_checks(c, hidden, inter, shared ? shared_inter : 0, n_experts, top_k, 16));
+    cudaSetDevice(c->device);
+    size_t H = hidden, I = inter;
+    MoeArgs a = {};
+    a.hidden = hidden;
+    a.inter = inter;
+    a.sh_inter = shared ? shared_inter : 0;
+    a.top_k = top_k;
+    a.int8 = 1;
+    a.simulate = c->simulate;
+    a.has_shared = shared;
+    a.gu_base = WMat{gu_q, gu_s, gu_o};
+    a.dn_base = WMat{dn_q, dn_s, dn_o};
+    a.gu_stride = (long long)(2 * I * H);
+    a.dn_stride = (long long)(H * I);
+    if (shared) {
+        a.sh_gu = WMat{sgu_q, sgu_s, sgu_o};
+        a.sh_dn = WMat{sdn_q, sdn_s, sdn_o};
+    }
+    a.x = d_x;
+    a.out = d_out;
+    CK(ensure_h(c, top_k * inter + a.sh_inter));
+    a.h = c->d_h;
+    return moe_layer_enqueue(c, a, d_router, n_experts, d_top_idx ? d_top_idx : c->d_idx,
+                             d_top_w ? d_top_w : c->d_wt, pick_stream(c, stream), false);
+}
+
 // ---------------------------------------------------------------------------
 // LM head argmax and matvec
 // ---------------------------------------------------------------------------

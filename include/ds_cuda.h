@@ -144,6 +144,18 @@ int ds_cuda_moe_layer_int8(ds_cuda_ctx_t *ctx, const float *x, float *out, const
                            const int8_t *sdn_q, const float *sdn_scale, const float *sdn_off,
                            int hidden, int inter, int shared_inter, int n_experts, int top_k,
                            int *top_idx, float *top_w);
+/* Device-pointer form of ds_cuda_moe_layer_int8 (the reference's int4
+ * branch of moe_forward, ds_moe_decoder.c:237-243, 269-278): every pointer
+ * is device memory, the work is enqueued on `stream` (NULL = the context's
+ * stream) and nothing is copied to or from the host; d_top_idx / d_top_w
+ * may be NULL. */
+int ds_cuda_moe_layer_int8_dev(ds_cuda_ctx_t *ctx, const float *d_x, float *d_out, const uint16_t *d_router,
+                               const int8_t *d_gu_q, const float *d_gu_scale, const float *d_gu_off,
+                               const int8_t *d_dn_q, const float *d_dn_scale, const float *d_dn_off,
+                               const int8_t *d_sgu_q, const float *d_sgu_scale, const float *d_sgu_off,
+                               const int8_t *d_sdn_q, const float *d_sdn_scale, const float *d_sdn_off,
+                               int hidden, int inter, int shared_inter, int n_experts, int top_k,
+                               int *d_top_idx, float *d_top_w, void *stream);
 
 /* ---------------------------------------------------------------------
  * LM head — ds_metal_lm_head_argmax (ds_metal.h:146-150) and

@@ -44,6 +44,10 @@ SIGNATURES = {
     "ds_cuda_argmax_matvec_bf16_batch_dev": (c_int, [P, P, P, c_int, c_int, c_int, P, P, P]),
     "ds_cuda_moe_layer_dev": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, P, P, P]),
     "ds_cuda_moe_layer_int8_dev": (c_int, [P] * 16 + [c_int] * 5 + [P, P, P]),
+    "ds_cuda_ep_unique_id": (c_int, [P, P]),
+    "ds_cuda_ep_init": (c_int, [P, c_int, c_int, P]),
+    "ds_cuda_ep_free": (c_int, [P]),
+    "ds_cuda_prefill_moe_ep": (c_int, [P, P, P, P, c_int, P, P, P, P]),
     "ds_cuda_moe_experts_noalloc": (c_int, [P, P, P, P, c_int, c_int, c_int, P, P]),
     "ds_cuda_decoder_create": (c_int, [P, P, P, P, P]),
     "ds_cuda_decoder_destroy": (c_int, [P, c_int]),

@@ -74,7 +74,7 @@ def build(verbose=False, force=False):
     objs.append(synth_o)
     if force or _stale(LIB, objs):
         cmd = [_nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB, *objs,
-               "-lcudart", "-lcuda", "-lpthread", "-lm"]
+               "-lcudart", "-lcuda", "-lpthread", "-ldl", "-lm"]
         if verbose:
             print(" ".join(cmd))
         subprocess.check_call(cmd)

@@ -180,6 +180,7 @@ extern "C" void ds_cuda_free(ds_cuda_ctx_t *c) {
     ctx_release_models(c);
     ctx_release_batch_models(c);
     prefill_release(c);
+    ep_release(c);
     for (auto &e : c->prefill_ev)
         if (e) cudaEventDestroy(e);
     for (auto &kv : c->regs) cudaFree(kv.second.dev);

@@ -50,6 +50,8 @@ struct ds_cuda_ctx {
     // batched-prefill workspace (prefill.cu) and optional per-stage timing
     void *prefill = nullptr;
     bool prefill_timing = false;
+    // expert-parallel state (ep_nccl.cu): communicator, stream, buffers
+    void *ep = nullptr;
     cudaEvent_t prefill_ev[7] = {};
     // decoder models owned by this context
     std::map<int, DecoderModel *> models;
@@ -70,6 +72,7 @@ void *ctx_adopt(ds_cuda_ctx *c, void *dev, size_t bytes);
 const void *ctx_lookup(ds_cuda_ctx *c, const void *p, size_t bytes, bool auto_register);
 void ctx_release_models(ds_cuda_ctx *c);
 void prefill_release(ds_cuda_ctx *c);
+void ep_release(ds_cuda_ctx *c);
 void ctx_release_batch_models(ds_cuda_ctx *c);
 int moe_layer_enqueue(ds_cuda_ctx *c, ds::MoeArgs &a, const uint16_t *d_router, int n_experts, int *d_idx,
                       float *d_wt, cudaStream_t st, bool pdl);

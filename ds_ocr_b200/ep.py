@@ -205,3 +205,48 @@ class ExpertParallelPrefill:
         y_back = self._a2a(y, back_send, back_recv)
         self.st.combine(x, idx, w, y_back, inv, ys)
         return idx, w
+
+
+class NativeExpertParallelPrefill:
+    """One rank of the expert-parallel prefill run inside the library
+    (ds_cuda_prefill_moe_ep: dispatch and return over NCCL from C, no
+    torch.distributed on the data path). `uid` is the 128-byte id from
+    unique_id() on rank 0, shared with the other ranks out of band."""
+
+    @staticmethod
+    def unique_id(ctx):
+        buf = ctypes.create_string_buffer(128)
+        ctx.check(ctx.lib.ds_cuda_ep_unique_id(ctx.h, buf), "ep_unique_id")
+        return buf.raw
+
+    def __init__(self, d, ctx, rank, world, uid):
+        self.d, self.ctx, self.rank, self.world = d, ctx, rank, world
+        self.cfg = DecoderConfig(d.hidden, d.n_layers, d.n_heads, d.head_dim, d.dense_inter, d.moe_inter,
+                                 d.n_experts, d.n_shared, d.top_k, d.vocab, d.first_dense, synth.RMS_EPS,
+                                 synth.ROPE_THETA, 0, 0, 0)
+        self._structs = {}
+        self._uid = ctypes.create_string_buffer(bytes(uid), 128)
+        ctx.check(ctx.lib.ds_cuda_ep_init(ctx.h, rank, world, self._uid), "ep_init")
+
+    def _layer(self, lw):
+        s = self._structs.get(id(lw))
+        if s is None:
+            m = lw.moe
+            self.ctx._pin(lw.post_norm, m.router, m.block, m.down, m.shared_down)
+            s = self._structs[id(lw)] = (lw, layer_struct(lw))
+        return ctypes.byref(s[1])
+
+    def moe_layer(self, lw, x, logits=None, stream=None):
+        """x: this rank's [n x H] F32 rows (torch CUDA tensor, updated in
+        place); logits [n x E] or None. Returns (idx, w) device tensors."""
+        import torch
+        n, K = x.shape[0], self.d.top_k
+        idx = torch.empty((n, K), dtype=torch.int32, device=x.device)
+        w = torch.empty((n, K), dtype=torch.float32, device=x.device)
+        self.ctx.check(self.ctx.lib.ds_cuda_prefill_moe_ep(
+            self.ctx.h, ctypes.byref(self.cfg), self._layer(lw), x.data_ptr(), n,
+            None if logits is None else logits.data_ptr(), idx.data_ptr(), w.data_ptr(), stream), "prefill_moe_ep")
+        return idx, w
+
+    def close(self):
+        self.ctx.lib.ds_cuda_ep_free(self.ctx.h)

@@ -467,6 +467,28 @@ int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *ctx, int n_tokens, int top_k, int n_r
 int ds_cuda_ep_pairs_dev(ds_cuda_ctx_t *ctx, int n_rows, int top_k, int n_ranks, const int *recv_counts,
                          const uint16_t *d_payload, int hidden, int *d_pair_row, int *d_pair_expert, int *d_counts,
                          void *stream);
+/* Expert-parallel prefill through the C ABI (no counterpart in the
+ * reference, which runs ds_decoder_prefill's MoE block, ds_moe_decoder.c:
+ * 630-809, on one host). One process per GPU; each context joins a group of
+ * `world` ranks (1..8) sharing a 128-byte id that rank 0 makes with
+ * ds_cuda_ep_unique_id and hands to the others out of band (as for NCCL).
+ * The library loads NCCL at run time (libnccl.so.2, or $DS_CUDA_NCCL_LIB).
+ * ds_cuda_prefill_moe_ep then runs one MoE layer on this rank's n_tokens
+ * rows of d_x (updated in place; the ranks' rows together are the batch,
+ * in rank order): routing, the token rows sent once to each rank owning one
+ * of their experts (experts in contiguous blocks of n_experts / world), the
+ * shared expert on local rows while the rows travel, the routed experts,
+ * the outputs sent back, and the combine — the same arithmetic as
+ * ds_cuda_prefill_moe_dev, so the result is bit-identical to one GPU. Every
+ * rank must call it for every layer (it synchronises its stream twice per
+ * call to size the transfers). d_logits / d_top_idx / d_top_w as in
+ * ds_cuda_prefill_moe_dev. */
+int ds_cuda_ep_unique_id(ds_cuda_ctx_t *ctx, void *id128);
+int ds_cuda_ep_init(ds_cuda_ctx_t *ctx, int rank, int world, const void *id128);
+int ds_cuda_ep_free(ds_cuda_ctx_t *ctx);
+int ds_cuda_prefill_moe_ep(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
+                           const ds_cuda_layer_weights_t *layer, float *d_x, int n_tokens, const float *d_logits,
+                           int *d_top_idx, float *d_top_w, void *stream);
 /* The multi-stream decode GEMM on its own (no counterpart in the
  * reference): d_y [n x N] = d_x [n x K] . d_W^T (+ d_resid), n <= 64 token
  * rows, K % 64 == 0, on the tensor cores with the inputs split into two

@@ -157,3 +157,94 @@ def test_dispatch_and_pairs_kernels(cuda_ctx):
     # the payload as if received from 4 ranks with these row counts
     pr, pe, per = st.pairs(payload[:rows], recv)
     assert torch.equal(pr.cpu(), rpr) and torch.equal(pe.cpu(), rpe) and per == rper
+
+
+def test_native_ep_one_rank_matches_prefill(cuda_ctx):
+    # the library's own expert-parallel layer (NCCL from C) at one rank:
+    # every transfer goes to itself; bit-identical to the fused single-GPU call
+    import torch
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from ds_ocr_b200 import synth
+    from ds_ocr_b200.ep import NativeExpertParallelPrefill
+    from ds_ocr_b200.prefill import Prefill
+    model = synth.Model(n_layers=3, vocab=256)
+    x, lg = _inputs(model.d)
+    ref = x.copy()
+    for l in (1, 2):
+        idx_ref, _ = Prefill(model.d, cuda_ctx).moe_layer(model.layers[l], ref, lg)
+    ep = NativeExpertParallelPrefill(model.d, cuda_ctx, 0, 1, NativeExpertParallelPrefill.unique_id(cuda_ctx))
+    try:
+        tx = torch.from_numpy(x).cuda()
+        tl = torch.from_numpy(lg).cuda()
+        torch.cuda.synchronize()
+        for l in (1, 2):
+            idx, _ = ep.moe_layer(model.layers[l], tx, tl)
+        cuda_ctx.synchronize()
+    finally:
+        ep.close()
+    assert np.array_equal(idx.cpu().numpy(), idx_ref)
+    assert np.array_equal(tx.cpu().numpy(), ref)
+
+
+def _native_rank(rank, world, q_uid, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    from ds_ocr_b200 import cuda, synth
+    from ds_ocr_b200.ep import NativeExpertParallelPrefill, token_range
+    torch.cuda.set_device(rank)
+    ctx = cuda.Context(rank)
+    try:
+        model = synth.Model(n_layers=3, vocab=256)
+        if rank == 0:
+            uid = NativeExpertParallelPrefill.unique_id(ctx)
+            for _ in range(world - 1):
+                q_uid.put(uid)
+        else:
+            uid = q_uid.get(timeout=120)
+        ep = NativeExpertParallelPrefill(model.d, ctx, rank, world, uid)
+        x, lg = _inputs(model.d)
+        a, b = token_range(N_TOKENS, rank, world)
+        xl = torch.from_numpy(x[a:b].copy()).cuda()
+        for l in (1, 2):
+            ll = torch.from_numpy(lg[a:b].copy()).cuda()
+            idx, _ = ep.moe_layer(model.layers[l], xl, ll)
+        ctx.synchronize()
+        q.put((rank, xl.cpu().numpy(), idx.cpu().numpy()))
+        ep.close()
+    except Exception as e:  # reported to the parent instead of a silent hang
+        q.put((rank, None, repr(e)))
+        raise
+    finally:
+        ctx.close()
+
+
+def test_native_ep_two_gpus_bit_identical_to_one():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from ds_ocr_b200 import cuda, synth
+    from ds_ocr_b200.prefill import Prefill
+    model = synth.Model(n_layers=3, vocab=256)
+    x, lg = _inputs(model.d)
+    ref = x.copy()
+    ctx = cuda.Context(0)
+    pf = Prefill(model.d, ctx)
+    for l in (1, 2):
+        idx_ref, _ = pf.moe_layer(model.layers[l], ref, lg)
+    ctx.close()
+    mpc = mp.get_context("spawn")
+    q, q_uid = mpc.Queue(), mpc.Queue()
+    procs = [mpc.Process(target=_native_rank, args=(r, 2, q_uid, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        r, xl, idx = q.get(timeout=240)
+        assert xl is not None, f"rank {r}: {idx}"
+        got[r] = (xl, idx)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert np.array_equal(np.concatenate([got[0][1], got[1][1]]), idx_ref)
+    assert np.array_equal(np.concatenate([got[0][0], got[1][0]]), ref)

@@ -807,14 +807,26 @@ def run_ours_prefill(args, rank, world, pg, model):
     layers = model.layers[1:1 + n_layers]
     logits = logits[:n_layers]
     ep = None
+    native = getattr(args, "ep_impl", "native") == "native"
     a, b = 0, PF_TOKENS
     if world > 1:
         # expert-parallel: this rank's token slice, experts [rank*E/G, ...)
-        from ds_ocr_b200.ep import CudaStages, ExpertParallelPrefill, token_range
-        stages = CudaStages(d, ctx)
-        ep = ExpertParallelPrefill(d, stages, pg, rank, world, stages.device)
+        from ds_ocr_b200.ep import CudaStages, ExpertParallelPrefill, NativeExpertParallelPrefill, token_range
         a, b = token_range(PF_TOKENS, rank, world)
-        st = stages.stream
+        if native:
+            # the library's own layer: NCCL from C, the id shared over the
+            # process group
+            uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(NativeExpertParallelPrefill.unique_id(ctx)),
+                                           dtype=torch.uint8))
+            torch.distributed.broadcast(uid, 0, group=pg)
+            ep = NativeExpertParallelPrefill(d, ctx, rank, world, bytes(uid.cpu().numpy().tobytes()))
+            st = torch.cuda.Stream()
+        else:
+            stages = CudaStages(d, ctx)
+            ep = ExpertParallelPrefill(d, stages, pg, rank, world, stages.device)
+            st = stages.stream
     else:
         st = torch.cuda.Stream()
     # every kernel, copy and collective of a step runs on stream st (the C
@@ -830,6 +842,8 @@ def run_ours_prefill(args, rank, world, pg, model):
         for lw, lg in zip(layers, lgs):
             if ep is None:
                 pf.moe_layer_dev(lw, xbuf.data_ptr(), PF_TOKENS, lg.data_ptr(), stream=sp)
+            elif native:
+                ep.moe_layer(lw, xbuf, lg, stream=sp)
             else:
                 ep.moe_layer(lw, xbuf, lg)
 
@@ -854,8 +868,21 @@ def run_ours_prefill(args, rank, world, pg, model):
     # expert-parallel: (row, expert) pairs each rank computed, max / mean
     ep_load = None
     if ep is not None:
-        pairs, imbalance = ep.load()
-        ep_load = {"pairs_per_rank": pairs, "imbalance_max_over_mean": imbalance}
+        if native:
+            # (token, expert) pairs each rank's experts take per step, from
+            # the routing the logits fix (top-6 of each row)
+            e_per = d.n_experts // world
+            pairs = [0] * world
+            for lg in logits:
+                top = np.argpartition(-lg, d.top_k - 1, axis=1)[:, :d.top_k]
+                cnt = np.bincount((top // e_per).ravel(), minlength=world)
+                pairs = [p + int(c) for p, c in zip(pairs, cnt)]
+        else:
+            pairs = ep.load()[0]
+        mean = sum(pairs) / len(pairs)
+        ep_load = {"pairs_per_rank_per_step": pairs, "imbalance_max_over_mean": max(pairs) / mean,
+                   "impl": "ds_cuda_prefill_moe_ep (NCCL from the library)" if native
+                           else "torch.distributed all_to_all_single between the stage kernels"}
     # one GPU: 3328 tokens per step; expert-parallel: the same 3328 tokens
     # split over the ranks (strong scaling)
     value = PF_TOKENS * args.steps / (ms_max / 1e3)
@@ -868,6 +895,8 @@ def run_ours_prefill(args, rank, world, pg, model):
     for lw, lg in zip(layers, dlg):
         if ep is None:
             pf.moe_layer_dev(lw, dx.data_ptr(), PF_TOKENS, lg.data_ptr(), stream=sp)
+        elif native:
+            ep.moe_layer(lw, dx, lg, stream=sp)
         else:
             ep.moe_layer(lw, dx, lg)
         stages += pf.stage_ms()
@@ -938,6 +967,9 @@ def run_ours_prefill(args, rank, world, pg, model):
     }
     if ep_load is not None:
         res["ep_load"] = ep_load
+    if native and ep is not None:
+        torch.cuda.synchronize()
+        ep.close()
     # torch tensors used on the context's stream go before the stream does
     del dx, dx0, dlg, ep
     import gc
@@ -1106,6 +1138,10 @@ def main():
     ap.add_argument("--prefill-layers", type=int, default=PF_LAYERS,
                     help="prefill: MoE layers per step (11 = config 4; fewer only for small profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-impl", default="native", choices=["native", "torch"],
+                    help="expert-parallel prefill: the library's NCCL layer or torch.distributed between stages")
+    ap.add_argument("--no-ep-prefill", action="store_true",
+                    help="decode: skip the expert-parallel prefill block reported beside the decode line")
     ap.add_argument("--repeat-penalty", type=float, default=1.0,
                     help="decode: the reference's --repeat-penalty (> 1 enables)")
     ap.add_argument("--no-repeat-ngram", type=int, default=0,
@@ -1180,6 +1216,20 @@ def main():
     if args.workload == "decode":
         model, ks, vs = build_decode_model()
         res = run_ours_decode(args, rank, world, pg, model, ks, vs)
+        if not args.no_ep_prefill:
+            # the path that shards with a collective, measured at every N
+            # beside the decode replicas: config 4's expert-parallel prefill
+            # (3328 tokens over the ranks, experts in blocks of 64 / N)
+            import copy
+            pa = copy.copy(args)
+            pa.steps, pa.warmup = min(args.steps, 10), 3
+            pr = run_ours_prefill(pa, rank, world, pg, model)
+            res["ep_prefill"] = {"metric": pr["metric"], "value": pr["value"], "unit": pr["unit"],
+                                 "ms_per_step": pr["ms_per_step"], "steps": pa.steps, "n_ranks": world,
+                                 "parallelism": pr["config"]["parallelism"], "scaling": "strong",
+                                 "ep_load": pr.get("ep_load"), "roofline": pr["roofline"],
+                                 "collective": "NCCL send/recv all-to-all(v) per direction per layer" if world > 1
+                                               else None}
     elif args.workload == "prefill":
         from ds_ocr_b200 import synth
         model = synth.Model()
@@ -1206,7 +1256,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "dtype": res["dtype"],
             "config": res["config"], "e2e": res["e2e"], "roofline": res["roofline"], "clocks": res["clocks"],
             "gpu_launches": res["gpu_launches"]}
-    for k in ("step_roofline", "dominant_kernel", "lm_head_roofline", "batch1", "ep_load"):
+    for k in ("step_roofline", "dominant_kernel", "lm_head_roofline", "batch1", "ep_load", "ep_prefill"):
         if k in res:
             line[k] = res[k]
     line.update(common)

@@ -820,7 +820,7 @@ def run_ours_prefill(args, rank, world, pg, model):
             if rank == 0:
                 uid.copy_(torch.frombuffer(bytearray(NativeExpertParallelPrefill.unique_id(ctx)),
                                            dtype=torch.uint8))
-            torch.distributed.broadcast(uid, 0, group=pg)
+            pg.broadcast(uid, 0)  # pg: the torch.distributed module (default group)
             ep = NativeExpertParallelPrefill(d, ctx, rank, world, bytes(uid.cpu().numpy().tobytes()))
             st = torch.cuda.Stream()
         else:

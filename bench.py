@@ -771,15 +771,16 @@ PF_FLOPS_LAYER = PF_TOKENS * (6 * 6881280 + 13762560)        # routed + shared, 
 PF_FLOPS_GU_LAYER = PF_TOKENS * (6 * 2 * 1792 * 1280 + 2 * 3584 * 1280)
 
 
-def prefill_inputs(d):
-    """x [3328 x 1280] N(0,1) (seed 5); per layer l = 1..11 the router logits
+def prefill_inputs(d, n=PF_TOKENS):
+    """x [n x 1280] N(0,1) (seed 5); per layer l = 1..11 the router logits
     N(0,1) (seed 600+l) plus a per-expert bias N(0,0.5) (seed 700+l), which
-    replace xn W_r^T and give the skewed routing of config 4."""
+    replace xn W_r^T and give the skewed routing of config 4. The generator
+    is counter-based, so the first 3328 rows are config 4's at any n."""
     from ds_ocr_b200 import synth
-    x = synth.normal_f32((PF_TOKENS, d.hidden), 5)
+    x = synth.normal_f32((n, d.hidden), 5)
     logits = []
     for l in range(1, PF_LAYERS + 1):
-        lg = synth.normal_f32((PF_TOKENS, d.n_experts), 600 + l)
+        lg = synth.normal_f32((n, d.n_experts), 600 + l)
         lg += 0.5 * synth.normal_f32(d.n_experts, 700 + l)[None, :]
         logits.append(lg)
     return x, logits
@@ -802,7 +803,11 @@ def run_ours_prefill(args, rank, world, pg, model):
     ctx = cuda.Context(local if world > 1 else 0)
     d = model.d
     pf = Prefill(d, ctx)
-    x, logits = prefill_inputs(d)
+    # strong scaling: config 4's 3328 tokens split over the ranks; weak:
+    # 3328 tokens per rank (a batch of 3328 x N)
+    weak = getattr(args, "ep_scaling", "strong") == "weak" and world > 1
+    ntot = PF_TOKENS * world if weak else PF_TOKENS
+    x, logits = prefill_inputs(d, ntot)
     n_layers = args.prefill_layers
     layers = model.layers[1:1 + n_layers]
     logits = logits[:n_layers]
@@ -812,7 +817,7 @@ def run_ours_prefill(args, rank, world, pg, model):
     if world > 1:
         # expert-parallel: this rank's token slice, experts [rank*E/G, ...)
         from ds_ocr_b200.ep import CudaStages, ExpertParallelPrefill, NativeExpertParallelPrefill, token_range
-        a, b = token_range(PF_TOKENS, rank, world)
+        a, b = token_range(ntot, rank, world)
         if native:
             # the library's own layer: NCCL from C, the id shared over the
             # process group
@@ -885,7 +890,7 @@ def run_ours_prefill(args, rank, world, pg, model):
                            else "torch.distributed all_to_all_single between the stage kernels"}
     # one GPU: 3328 tokens per step; expert-parallel: the same 3328 tokens
     # split over the ranks (strong scaling)
-    value = PF_TOKENS * args.steps / (ms_max / 1e3)
+    value = ntot * args.steps / (ms_max / 1e3)
 
     # per-stage device times (one extra, untimed pass): the gate/up GEMM is
     # the dominant kernel
@@ -937,12 +942,12 @@ def run_ours_prefill(args, rank, world, pg, model):
         d2h = (b - a) * d.hidden * 4
     t1.synchronize()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1), pg)
-    e2e = PF_TOKENS * n_e2e / (e2e_ms / 1e3)
+    e2e = ntot * n_e2e / (e2e_ms / 1e3)
     pk = peaks()
     peak_t = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
     # expert-parallel: rank 0's GEMM does about 1/G of the layer's work
-    gu_ach = PF_FLOPS_GU_LAYER / world / (stages[3] / 1e3) / 1e12
-    step_ach = PF_FLOPS_LAYER * n_layers * args.steps / (ms_max / 1e3) / 1e12 / world
+    gu_ach = PF_FLOPS_GU_LAYER * (ntot / PF_TOKENS) / world / (stages[3] / 1e3) / 1e12
+    step_ach = PF_FLOPS_LAYER * (ntot / PF_TOKENS) * n_layers * args.steps / (ms_max / 1e3) / 1e12 / world
     res = {
         "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
         "metric": "MoE prefill tokens/s (3328 tokens x 11 MoE layers, 64 experts top-6 + 2 shared)",
@@ -953,8 +958,8 @@ def run_ours_prefill(args, rank, world, pg, model):
         # compaction (10)
         "gpu_launches": (7 if world == 1 else 10) * n_layers * args.steps,
         "config": dict(prefill_config(n_layers), parallelism=f"ep{world}" if world > 1 else "single GPU",
-                       tokens_per_rank=b - a),
-        "scaling": "strong" if world > 1 else "weak",
+                       tokens_per_rank=b - a, global_batch=ntot),
+        "scaling": "strong" if world > 1 and not weak else "weak",
         "roofline": {"bound": "tensor", "achieved": gu_ach, "peak": peak_t, "unit": "TFLOP/s",
                      "frac": gu_ach / peak_t, "traffic": TRAFFIC_PF_GATE_UP if world == 1 else None,
                      "kernel": "pf_gemm_kernel<0> (gate/up + SwiGLU), 122.1 GFLOP algorithmic per layer; "
@@ -1140,6 +1145,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-impl", default="native", choices=["native", "torch"],
                     help="expert-parallel prefill: the library's NCCL layer or torch.distributed between stages")
+    ap.add_argument("--ep-scaling", default="strong", choices=["strong", "weak"],
+                    help="prefill on N GPUs: 3328 tokens split over the ranks (strong) or 3328 per rank (weak)")
     ap.add_argument("--no-ep-prefill", action="store_true",
                     help="decode: skip the expert-parallel prefill block reported beside the decode line")
     ap.add_argument("--repeat-penalty", type=float, default=1.0,
@@ -1223,10 +1230,13 @@ def main():
             import copy
             pa = copy.copy(args)
             pa.steps, pa.warmup = min(args.steps, 10), 3
+            pa.ep_scaling = "weak"
             pr = run_ours_prefill(pa, rank, world, pg, model)
-            res["ep_prefill"] = {"metric": pr["metric"], "value": pr["value"], "unit": pr["unit"],
+            res["ep_prefill"] = {"metric": pr["metric"].replace("3328 tokens", "3328 tokens per GPU"),
+                                 "value": pr["value"], "unit": pr["unit"],
                                  "ms_per_step": pr["ms_per_step"], "steps": pa.steps, "n_ranks": world,
-                                 "parallelism": pr["config"]["parallelism"], "scaling": "strong",
+                                 "parallelism": pr["config"]["parallelism"], "scaling": "weak",
+                                 "global_batch": pr["config"]["global_batch"],
                                  "ep_load": pr.get("ep_load"), "roofline": pr["roofline"],
                                  "collective": "NCCL send/recv all-to-all(v) per direction per layer" if world > 1
                                                else None}

@@ -109,67 +109,85 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(256) attn_step_kern
     }
     __syncthreads();
     tr.mark(1);
-    // 2. block maximum (warp 0: lane l owns a contiguous segment of keys)
-    const int seg = (cnt + 31) / 32;
-    const int s0 = min(cnt, lane * seg), s1 = min(cnt, s0 + seg);
+    // 2. the sequential rule over this block's keys, all 256 threads: thread
+    //    t owns a contiguous segment of keys; block scans (shuffles within a
+    //    warp, then the 8 warp totals) give each segment its entering
+    //    maximum and the product of the later segments' corrections
+    __shared__ float wtot[8];
+    const int seg = (cnt + 255) / 256;
+    const int s0 = min(cnt, tid * seg), s1 = min(cnt, s0 + seg);
     float lmax = -1e30f;
-    if (warp == 0) {
-        for (int j = s0; j < s1; j++) lmax = fmaxf(lmax, sc[j]);
-        const float bm = warp_max(lmax);
-        if (lane == 0) xch[0] = bm;
+    for (int j = s0; j < s1; j++) lmax = fmaxf(lmax, sc[j]);
+    // inclusive max scan within the warp, warp totals
+    float inc = lmax;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(DS_FULL, inc, o);
+        if (lane >= o) inc = fmaxf(inc, y);
+    }
+    if (lane == 31) wtot[warp] = inc;
+    __syncthreads();
+    if (tid == 0) {
+        float bm = -1e30f;
+        for (int w = 0; w < 8; w++) bm = fmaxf(bm, wtot[w]);
+        xch[0] = bm;
     }
     cluster.sync();
     tr.mark(2);
-    if (warp == 0) {
-        // running max entering the block, then entering the lane's segment
+    {
+        // running max entering the block, the earlier warps, the earlier lanes
         float m = -1e30f;
         for (int b = 0; b < crank; b++) m = fmaxf(m, cluster.map_shared_rank(xch, b)[0]);
-        float inc = lmax;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_up_sync(DS_FULL, inc, o);
-            if (lane >= o) inc = fmaxf(inc, y);
-        }
+        for (int w = 0; w < warp; w++) m = fmaxf(m, wtot[w]);
         const float ex = __shfl_up_sync(DS_FULL, inc, 1);
         if (lane > 0) m = fmaxf(m, ex);
-        // the sequential rule over the segment (exact arguments)
         for (int j = s0; j < s1; j++) {
-            const float s = sc[j];
-            if (s > m) {
-                cr[j] = fast_expf(__fsub_rn(m, s));
+            const float sj = sc[j];
+            if (sj > m) {
+                cr[j] = fast_expf(__fsub_rn(m, sj));
                 sc[j] = 1.0f;
-                m = s;
+                m = sj;
             } else {
                 cr[j] = 1.0f;
-                sc[j] = fast_expf(__fsub_rn(s, m));
+                sc[j] = fast_expf(__fsub_rn(sj, m));
             }
         }
-        // suffix products of the corrections: inside the segment, then over
-        // the later lanes (reverse scan)
-        float lp = 1.0f;
-        for (int j = s1 - 1; j >= s0; j--) lp = __fmul_rn(lp, cr[j]);
-        float incp = lp;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float y = __shfl_down_sync(DS_FULL, incp, o);
-            if (lane + o < 32) incp = __fmul_rn(incp, y);
-        }
-        float P = __shfl_down_sync(DS_FULL, incp, 1);
-        if (lane == 31) P = 1.0f;
-        for (int j = s1 - 1; j >= s0; j--) {
-            sc[j] = __fmul_rn(sc[j], P);
-            P = __fmul_rn(P, cr[j]);
-        }
-        float lsum = 0.f;
-        for (int j = s0; j < s1; j++) lsum = __fadd_rn(lsum, sc[j]);
-        lsum = warp_sum(lsum);
-        const float cb = __shfl_sync(DS_FULL, incp, 0);  // every correction of the block
-        if (lane == 0) {
-            xch[1] = cb;
-            xch[2] = lsum;
-        }
-        tr.mark(3);
     }
+    // suffix products of the corrections: the segment, the later lanes of the
+    // warp (reverse inclusive scan), the later warps
+    float lp = 1.0f;
+    for (int j = s1 - 1; j >= s0; j--) lp = __fmul_rn(lp, cr[j]);
+    float incp = lp;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(DS_FULL, incp, o);
+        if (lane + o < 32) incp = __fmul_rn(incp, y);
+    }
+    __syncthreads();  // wtot is reused
+    if (lane == 0) wtot[warp] = incp;
+    __syncthreads();
+    float P = __shfl_down_sync(DS_FULL, incp, 1);
+    if (lane == 31) P = 1.0f;
+    for (int w = 7; w > warp; w--) P = __fmul_rn(P, wtot[w]);
+    float lsum = 0.f;
+    for (int j = s1 - 1; j >= s0; j--) {
+        const float wj = __fmul_rn(sc[j], P);
+        sc[j] = wj;
+        P = __fmul_rn(P, cr[j]);
+    }
+    for (int j = s0; j < s1; j++) lsum = __fadd_rn(lsum, sc[j]);
+    lsum = warp_sum(lsum);
+    __shared__ float wsum[8];
+    if (lane == 0) wsum[warp] = lsum;
+    __syncthreads();
+    if (tid == 0) {
+        float cb = 1.0f, S = 0.f;
+        for (int w = 7; w >= 0; w--) cb = __fmul_rn(cb, wtot[w]);  // every correction of the block
+        for (int w = 0; w < 8; w++) S = __fadd_rn(S, wsum[w]);
+        xch[1] = cb;
+        xch[2] = S;
+    }
+    tr.mark(3);
     cluster.sync();
     tr.mark(4);
     // 3. the later blocks' factor; this block's sum_j w_j v_j

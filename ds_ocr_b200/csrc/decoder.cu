@@ -1092,9 +1092,19 @@ static int prefill_enqueue(ds_cuda_ctx *c, DecoderModel *m, const float *d_embed
             m->lo_start[l] = p0;
             lo_changed = true;
         }
-        CKL(launch_attn_prefill(m->pf_q, m->plane(0, l), m->plane(1, l), m->plane(2, l), m->plane(3, l), g.kv_max,
-                                NH, p0, T, m->lo_start[l], QD, 1.0f / sqrtf((float)HD), m->pf_att, st),
-            "prefill attention");
+        // tensor cores (split-BF16 Q K^T and W V, the sequential rule on each
+        // query's row of the score tile); DS_CUDA_PREFILL_ATTN_CUDA_CORES=1
+        // keeps the CUDA-core kernel (same block recurrence) for comparison
+        static const char *cc = getenv("DS_CUDA_PREFILL_ATTN_CUDA_CORES");
+        if (!(cc && cc[0] == '1') && attn_prefill_tc_ok(HD, g.kv_max, NH))
+            CKL(launch_attn_prefill_tc(m->pf_q, m->plane(0, l), m->plane(1, l), m->plane(2, l), m->plane(3, l),
+                                       g.kv_max, NH, p0, T, QD, 1.0f / sqrtf((float)HD), m->pf_att, m->tickets + 10,
+                                       st),
+                "prefill attention");
+        else
+            CKL(launch_attn_prefill(m->pf_q, m->plane(0, l), m->plane(1, l), m->plane(2, l), m->plane(3, l),
+                                    g.kv_max, NH, p0, T, m->lo_start[l], QD, 1.0f / sqrtf((float)HD), m->pf_att, st),
+                "prefill attention");
         CKL(launch_pd_split(m->pf_att, T, QD, nullptr, 0.f, m->pf_ahi, m->pf_alo, st), "prefill split");
         CK(pf_dense_gemm(c, 1, m->pf_ahi, m->pf_alo, T, QD, L.wo, H, m->pf_y, H, nullptr, nullptr, st));
         CKL(launch_pd_add(m->pf_x, m->pf_y, (size_t)T * H, st), "prefill residual");
@@ -1174,6 +1184,11 @@ extern "C" int ds_cuda_decoder_prefill(ds_cuda_ctx_t *c, int id, const float *em
     if (rc == DS_CUDA_OK && final_x)
         rc = ctx_cuda(c, cudaMemcpyAsync(final_x, m->xfinal, H * 4, cudaMemcpyDeviceToHost, c->stream), "final x");
     if (rc == DS_CUDA_OK) rc = ctx_cuda(c, cudaStreamSynchronize(c->stream), "decoder_prefill");
+    if (rc == DS_CUDA_OK) {
+        unsigned flag = 0;
+        cudaMemcpy(&flag, m->tickets + 10, sizeof flag, cudaMemcpyDeviceToHost);
+        if (flag) rc = ctx_fail(c, DS_CUDA_ETIMEOUT, "decoder_prefill: a bounded device-side wait gave up");
+    }
     if (rc == DS_CUDA_OK) rc = prefill_check_flag(c);
     if (rc < 0) return rc;
     if (logit) *logit = val;

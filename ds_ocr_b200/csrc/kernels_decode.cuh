@@ -85,6 +85,11 @@ cudaError_t launch_pd_rope_kv(const float *qkv, int T, int NH, int HD, int p0, c
                               float *q, uint16_t *k_hi, uint16_t *k_lo, uint16_t *v_hi, uint16_t *v_lo, int kv_max,
                               cudaStream_t st);
 cudaError_t launch_pd_add(float *x, const float *y, size_t n, cudaStream_t st);
+// The prefill attention on the tensor cores (attn_prefill_tc.cu); head_dim 128.
+bool attn_prefill_tc_ok(int head_dim, int kv_max, int n_heads);
+cudaError_t launch_attn_prefill_tc(const float *q, const uint16_t *k_hi, const uint16_t *k_lo,
+                                   const uint16_t *v_hi, const uint16_t *v_lo, int kv_max, int n_heads, int p0, int T,
+                                   int q_stride, float scale, float *out, unsigned *err, cudaStream_t st);
 cudaError_t launch_attn_prefill(const float *q, const uint16_t *k_hi, const uint16_t *k_lo, const uint16_t *v_hi,
                                 const uint16_t *v_lo, int kv_max, int n_heads, int p0, int T, int lo_start,
                                 int q_stride, float scale, float *out, cudaStream_t st);

@@ -1014,7 +1014,7 @@ def prefill_full_config(T):
     return {"workload": "config4_full_prefill", "model": "DeepSeek3B-MoE decoder (12 layers, random init)",
             "tokens": T, "layers": 12, "hidden": 1280, "experts": 64, "top_k": 6,
             "routing": "the model's own router", "kv": "written to the decoder's cache (kv_max 4096)",
-            "gemm": "tcgen05 split-BF16 activations x BF16 weights, F32 accumulate; attention exact on CUDA cores",
+            "gemm": "tcgen05 split-BF16 activations x BF16 weights, F32 accumulate; attention on tcgen05 (split-BF16 Q K^T and W V) with the reference's sequential fast-exp rule per query row",
             "l2": "each step streams 5.9 GB of weights (> 126 MB L2)"}
 
 

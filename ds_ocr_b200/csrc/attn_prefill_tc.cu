@@ -299,23 +299,24 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
         for (int j = 0; j < 32; j++)
             if (j < nvo) mo = fmaxf(mo, __fmul_rn(so[j], a.scale));
         if (hf) m = fmaxf(m, mo);
-        // the sequential rule: a_j in place; at a new maximum, c_j in place
-        // and the key's bit set
+        // The sequential rule: a_j in place; at a new maximum, c_j in place
+        // and the key's bit set. The running maximum before each key is a one-operation chain; the
+        // rest is independent per key. At a new maximum (d = s_j - m > 0) the
+        // reference's c_j = fexp(m - s_j) = fexp(-d), else a_j = fexp(d): the
+        // argument is -|d| either way (round-to-nearest is sign-symmetric).
         uint32_t nm = 0;
+        float pm[32];
 #pragma unroll
         for (int j = 0; j < 32; j++) {
-            if (j < nv) {
-                const float sj = __fmul_rn(sv[j], a.scale);
-                if (sj > m) {
-                    sv[j] = fast_expf(__fsub_rn(m, sj));
-                    nm |= 1u << j;
-                    m = sj;
-                } else {
-                    sv[j] = fast_expf(__fsub_rn(sj, m));
-                }
-            } else {
-                sv[j] = 0.f;
-            }
+            sv[j] = __fmul_rn(sv[j], a.scale);
+            pm[j] = m;
+            if (j < nv) m = fmaxf(m, sv[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const float d = __fsub_rn(sv[j], pm[j]);
+            if (j < nv) nm |= (d > 0.f ? 1u : 0u) << j;
+            sv[j] = j < nv ? fast_expf(-fabsf(d)) : 0.f;
         }
         if (!hf) m = fmaxf(m, mo);  // the running maximum at the block's end
         // w_j = a_j * prod_{t > j} c_t (a_j = 1 at a new maximum), from the

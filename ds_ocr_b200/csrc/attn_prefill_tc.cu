@@ -11,29 +11,33 @@
 //        memory). Q and K are split into BF16 planes (v = hi + lo; the cache
 //        already stores K that way) and S = Qh Kh + Qh Kl + Ql Kh: ~2^-16
 //        relative, in F32;
-//   the query's two threads (one per 32-key half) read its row of S and
-//        apply the sequential rule to their keys with exact arguments (the
-//        second half starts from max(m, max of the first half), which is
-//        exactly the reference's running maximum there): a_j, c_j, the
-//        block's weights w_j = a_j * prod_{t > j in the block} c_t and
-//        correction C_b = prod_t c_t (the product runs from the last key
-//        down, the first half continuing the second half's product);
+//   the query's four threads (one per 16-key quarter) read its row of S
+//        and apply the sequential rule to their keys with exact arguments
+//        (a quarter starts from max(m, maxima of the earlier quarters),
+//        which is exactly the reference's running maximum there): a_j, c_j,
+//        the quarter's weights w_j = a_j * prod_{t > j in the quarter} c_t
+//        and product P_q; the later quarters' products then scale each
+//        quarter's weights, and C_b = P_3 P_2 P_1 P_0;
 //   O <- O * C_b (in tensor memory; skipped when every C_b of a warp is 1)
 //        and O += W_b V_b on the tensor cores, W split into BF16 planes the
 //        same way (Wh Vh + Wh Vl + Wl Vh), sum <- sum * C_b + sum_j w_j.
 // The factors are the reference's; products and sums associate in blocks
 // (the CUDA-core kernel in prefill_full.cu does the same block recurrence).
 //
-// Roles: 256 row threads (8 warps; warps w and w + 4 share tensor-memory
-// lanes 32 (w % 4) .. +31, i.e. query rows, and take the two key halves)
-// and one issuing thread (TMA loads, MMAs). Shared memory: Q planes
-// (64 KB), two stages of K planes and V planes (32 KB + 32 KB each), the W
-// planes (32 KB). Tensor memory: two S buffers (64 columns each) so S_{b+1}
-// is computed while the rows work on S_b, and O (128 columns). K and W are
-// K-major operands; V is loaded as stored ([key][dim]) and taken by the MMA
-// as an MN-major B operand. All operand tiles use the 128-byte swizzle
-// (16-byte chunk c of a 128-byte row r at chunk c ^ (r % 8), 8-row atoms of
-// 1024 B), the layout TMA writes with SWIZZLE_128B.
+// Roles: 512 row threads (16 warps; warps w, w + 4, w + 8, w + 12 share
+// tensor-memory lanes 32 (w % 4) .. +31, i.e. query rows, and take the four
+// 16-key quarters of each block) and one issuing thread (TMA loads, MMAs).
+// The A operands of both products live in tensor memory, so the MMAs read
+// only their B operand from shared memory (which bounds them): tensor memory
+// holds two S buffers (64 columns each, so S_{b+1} is computed while the
+// rows work on S_b), O (128), the Q planes (2 x 64, written once) and the W
+// planes (2 x 32, written per block), BF16 pairs packed per 32-bit column.
+// Shared memory holds three stages each of the K and V planes (32 KB a
+// stage), refilled as soon as the block two behind is consumed. K is the
+// K-major B operand of S; V is loaded as stored ([key][dim]) and taken as an
+// MN-major B operand. Both use the 128-byte swizzle TMA writes with
+// SWIZZLE_128B (16-byte chunk c of a 128-byte row r at chunk c ^ (r % 8),
+// 8-row atoms of 1024 B).
 #include "kernels_decode.cuh"
 #include "tmap.h"
 #include "umma.cuh"
@@ -44,14 +48,25 @@ namespace ds {
 constexpr int PT_Q = 128;                   // queries per CTA
 constexpr int PT_K = 64;                    // keys per block
 constexpr int PT_HD = 128;                  // head dim
-constexpr int PT_QTILE = 128 * 128;         // swizzled 128-row x 64-column BF16 tile (16 KB)
 constexpr int PT_KTILE = 64 * 128;          // swizzled 64-row x 64-column BF16 tile (8 KB)
-constexpr int PT_QPLANES = 4 * PT_QTILE;    // Q hi, Q lo: two 64-column tiles each
 constexpr int PT_KV = 4 * PT_KTILE;         // one stage of K (or V) hi and lo planes
-constexpr int PT_WPLANES = 2 * PT_QTILE;    // W hi, W lo: 128 queries x 64 keys
-constexpr int PT_SMEM = PT_QPLANES + 4 * PT_KV + PT_WPLANES + 1024;
-constexpr int PT_ROWS = 256;                // 8 row warps
-constexpr int PT_THREADS = PT_ROWS + 32;    // + the issuing warp
+constexpr int PT_NS = 3;                    // stages of K and of V
+constexpr int PT_SMEM = 2 * PT_NS * PT_KV + 1024;
+constexpr int PT_ROWS = 512;                // 16 row warps: 4 threads per query
+constexpr int PT_THREADS = PT_ROWS + 64;    // + the two issuing warps
+// tensor-memory columns
+constexpr uint32_t PT_TS = 0;               // S buffers: 0..63, 64..127
+constexpr uint32_t PT_TO = 128;             // O: 128 columns
+constexpr uint32_t PT_TQ = 256;             // Q hi: 64 columns of BF16 pairs; Q lo: the next 64
+constexpr uint32_t PT_TW = 384;             // W hi: 32 columns; W lo: the next 32
+constexpr uint32_t PT_TCOLS = 512;
+
+#ifdef PT_TRACE
+__device__ unsigned long long pt_trace[12][64];
+#define PT_MARK(k, b) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (b) < 64) pt_trace[k][b] = ds_gtime(); } while (0)
+#else
+#define PT_MARK(k, b) do { } while (0)
+#endif
 
 struct AttnTcArgs {
     CUtensorMap k_hi, k_lo, v_hi, v_lo;     // the layer's planes as [heads * kv_max] x 128, 64-row boxes
@@ -62,16 +77,24 @@ struct AttnTcArgs {
     unsigned *err;
 };
 
-// Shared-memory descriptor of an MN-major BF16 operand in the 128-byte
-// swizzle: 64 MN-elements (128 B) per row, one row per K index, 8-row atoms
-// of 1024 B (stride byte offset) and 64-element MN blocks `lbo` bytes apart
-// (leading byte offset), version 1, layout type 2.
-__device__ __forceinline__ uint64_t sw128_mn_desc(const void *smem_tile, uint32_t lbo) {
-    const uint64_t start = (smem_u32(smem_tile) >> 4) & 0x3fffu;
-    return start | ((uint64_t)(lbo >> 4) << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+// 16 / 8 / 32 consecutive 32-bit columns of this thread's tensor-memory lane,
+// stored (then waited for).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n\t"
+        "tcgen05.wait::st.sync.aligned;"
+        :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+        : "memory");
 }
-
-// 32 consecutive F32 columns of this thread's tensor-memory lane, stored.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, "
+        "%9, %10, %11, %12, %13, %14, %15, %16};\n\t"
+        "tcgen05.wait::st.sync.aligned;"
+        :: "r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+           "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -92,17 +115,49 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         : "memory");
 }
 
-// Barrier of the two warps that share query rows (ids 1..4, 64 threads),
+// split_bf16 of two values at once (v ~= hi + lo, each a BF16 rounded to
+// nearest even), packed low value first: cvt.rn.bf16x2 rounds exactly as
+// bf16_rne_bits for finite inputs.
+__device__ __forceinline__ void split2_bf16(float v0, float v1, uint32_t &hi, uint32_t &lo) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(v1), "f"(v0));
+    const float r0 = __fsub_rn(v0, __uint_as_float(hi << 16));
+    const float r1 = __fsub_rn(v1, __uint_as_float(hi & 0xffff0000u));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(r1), "f"(r0));
+}
+
+// tcgen05.mma (kind::f16, one CTA) with A in tensor memory (128 lanes = M
+// rows, K = 16 BF16 as 8 columns of pairs) and B a shared-memory descriptor
+// given as its low word (start address and leading byte offset) and high
+// word; ACC = 0 overwrites D.
+template <int ACC>
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint32_t blo, uint32_t bhi, uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .b64 bd;\n\t.reg .pred p;\n\t"
+        "mov.b64 bd, {%2, %3};\n\tsetp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n\t}"
+        :: "r"(d), "r"(a_tmem), "r"(blo), "r"(bhi), "r"(idesc), "n"(ACC) : "memory");
+}
+// High word of both B descriptors: stride byte offset 1024 B (8-row atoms),
+// version 1, 128-byte swizzle.
+constexpr uint32_t PT_DHI = 64u | (1u << 14) | (2u << 29);
+// Low word of a K-major tile's descriptor (leading byte offset field 1), or
+// of an MN-major one with 64-element blocks `lbo` bytes apart.
+__device__ __forceinline__ uint32_t dlo_k(const void *p) { return ((smem_u32(p) >> 4) & 0x3fffu) | (1u << 16); }
+__device__ __forceinline__ uint32_t dlo_mn(const void *p, uint32_t lbo) {
+    return ((smem_u32(p) >> 4) & 0x3fffu) | ((lbo >> 4) << 16);
+}
+
+// Barrier of the four warps that share query rows (ids 1..4, 128 threads),
 // returning whether any of them passed `bad`.
-__device__ __forceinline__ bool pair_sync_or(int id, bool bad) {
+__device__ __forceinline__ bool group_sync_or(int id, bool bad) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        "bar.red.or.pred q, %2, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r) : "r"((uint32_t)bad), "r"(id) : "memory");
     return r != 0;
 }
-__device__ __forceinline__ void pair_sync(int id) { asm volatile("bar.sync %0, 64;" :: "r"(id) : "memory"); }
+__device__ __forceinline__ void group_sync(int id) { asm volatile("bar.sync %0, 128;" :: "r"(id) : "memory"); }
 
 __device__ __forceinline__ bool err_set(const unsigned *err) {
     return *reinterpret_cast<const volatile unsigned *>(err) != 0u;
@@ -111,304 +166,303 @@ __device__ __forceinline__ bool err_set(const unsigned *err) {
 __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __grid_constant__ AttnTcArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *qpl = smem;                                   // Q hi (2 tiles), Q lo (2 tiles)
-    uint8_t *kst = smem + PT_QPLANES;                      // K stages: hi (2 tiles), lo (2 tiles)
-    uint8_t *vst = kst + 2 * PT_KV;                        // V stages: hi (2 tiles), lo (2 tiles)
-    uint8_t *wpl = vst + 2 * PT_KV;                        // W hi, W lo
-    __shared__ uint64_t kfull[2], vfull[2], sfull[2], sfree[2], wfull, pvdone;
+    uint8_t *kst = smem;                                   // K stages: hi (2 tiles), lo (2 tiles)
+    uint8_t *vst = smem + PT_NS * PT_KV;                   // V stages: the same
+    __shared__ uint64_t kfull[PT_NS], vfull[PT_NS], sfull[2], sfree[2], qfull, wfull, pvdone;
     __shared__ uint32_t tmem_base;
-    __shared__ float2 xch[PT_Q];                           // per query: the two halves' exchange
+    __shared__ float xmax[4][PT_Q];                        // per key quarter and query: its maximum
+    __shared__ float2 xprod[4][PT_Q];                      // ... its product of c_j and sum of weights
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int h = blockIdx.x;
     const int q0 = (gridDim.y - 1 - blockIdx.y) * PT_Q;    // the longest query blocks launch first
     const int qend = min(a.T, q0 + PT_Q);                  // queries q0 .. qend-1 (relative to p0)
     const int nb = (a.p0 + qend - 1) / PT_K + 1;           // key blocks up to the last query's position
-    if (tid == 0) {
-        for (int s = 0; s < 2; s++) {
+    if (tid == PT_ROWS) {
+        for (int s = 0; s < PT_NS; s++) {
             mbar_init(&kfull[s], 1);
             mbar_init(&vfull[s], 1);
+        }
+        for (int s = 0; s < 2; s++) {
             mbar_init(&sfull[s], 1);
             mbar_init(&sfree[s], PT_ROWS / 32);
         }
+        mbar_init(&qfull, PT_ROWS / 32);
         mbar_init(&wfull, PT_ROWS / 32);
         mbar_init(&pvdone, 1);
         mbar_fence_init();
     }
-    if (warp == 8) tmem_alloc(&tmem_base, 256);
-    if (warp < 8) {
-        // Q: thread (row i, half hf) splits head dims 64 hf .. +63 of query
-        // q0 + i into tile hf of the two planes (zeros for rows past T)
-        const int i = tid & 127, hf = tid >> 7;
-        const bool qvalid = q0 + i < a.T;
-        const float *qr = a.q + (size_t)(q0 + i) * a.q_stride + h * PT_HD + hf * 64;
-#pragma unroll 4
+    if (warp == PT_ROWS / 32) tmem_alloc(&tmem_base, PT_TCOLS);
+    // row thread (query q0 + i, quarter qt): head dims 32 qt .. +31 of its
+    // query split into BF16 pairs (zeros for rows past T)
+    const int i = tid & 127, qt = (tid >> 7) & 3;
+    const bool qvalid = warp < PT_ROWS / 32 && q0 + i < a.T;
+    uint32_t qh[16], ql[16];
+    {
+        const float *qr = a.q + (size_t)(q0 + i) * a.q_stride + h * PT_HD + qt * 32;
+#pragma unroll
         for (int c = 0; c < 8; c++) {
-            float f[8];
-            if (qvalid) {
-                const float4 u0 = __ldcg(reinterpret_cast<const float4 *>(qr + 8 * c));
-                const float4 u1 = __ldcg(reinterpret_cast<const float4 *>(qr + 8 * c + 4));
-                f[0] = u0.x; f[1] = u0.y; f[2] = u0.z; f[3] = u0.w;
-                f[4] = u1.x; f[5] = u1.y; f[6] = u1.z; f[7] = u1.w;
-            } else {
-#pragma unroll
-                for (int k = 0; k < 8; k++) f[k] = 0.f;
-            }
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                uint16_t h0, l0, h1, l1;
-                split_bf16(f[2 * k], h0, l0);
-                split_bf16(f[2 * k + 1], h1, l1);
-                hw[k] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                lw[k] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-            }
-            const uint32_t o = hf * PT_QTILE + (i >> 3) * 1024 + (i & 7) * 128 + ((c ^ (i & 7)) << 4);
-            *reinterpret_cast<uint4 *>(qpl + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4 *>(qpl + 2 * PT_QTILE + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (qvalid) u = __ldcg(reinterpret_cast<const float4 *>(qr + 4 * c));
+            split2_bf16(u.x, u.y, qh[2 * c], ql[2 * c]);
+            split2_bf16(u.z, u.w, qh[2 * c + 1], ql[2 * c + 1]);
         }
-        fence_proxy_async();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = tmem_base;  // columns 0..63, 64..127: the S buffers; 128..255: O
+    const uint32_t tmem = tmem_base;
     constexpr uint32_t idesc_s = idesc_bf16_f32(PT_Q, PT_K);
     constexpr uint32_t idesc_pv = idesc_bf16_f32(PT_Q, PT_HD) | (1u << 16);  // B (V) MN-major
 
-    if (warp == 8) {
+    if (warp >= PT_ROWS / 32) {
+        // two issuing threads on different SM sub-partitions: warp 16 issues
+        // S and refills K, warp 17 issues W V and refills V
         if (lane == 0) {
+            const bool is_s = warp == PT_ROWS / 32;
             const int y0 = h * a.kv_max;
-            auto load_k = [&](int b) {
-                uint8_t *d = kst + (b & 1) * PT_KV;
-                mbar_expect_tx(&kfull[b & 1], PT_KV);
-                tma_load_2d(d, &a.k_hi, 0, y0 + b * PT_K, &kfull[b & 1]);
-                tma_load_2d(d + PT_KTILE, &a.k_hi, 64, y0 + b * PT_K, &kfull[b & 1]);
-                tma_load_2d(d + 2 * PT_KTILE, &a.k_lo, 0, y0 + b * PT_K, &kfull[b & 1]);
-                tma_load_2d(d + 3 * PT_KTILE, &a.k_lo, 64, y0 + b * PT_K, &kfull[b & 1]);
-            };
-            auto load_v = [&](int b) {
-                uint8_t *d = vst + (b & 1) * PT_KV;
-                mbar_expect_tx(&vfull[b & 1], PT_KV);
-                tma_load_2d(d, &a.v_hi, 0, y0 + b * PT_K, &vfull[b & 1]);
-                tma_load_2d(d + PT_KTILE, &a.v_hi, 64, y0 + b * PT_K, &vfull[b & 1]);
-                tma_load_2d(d + 2 * PT_KTILE, &a.v_lo, 0, y0 + b * PT_K, &vfull[b & 1]);
-                tma_load_2d(d + 3 * PT_KTILE, &a.v_lo, 64, y0 + b * PT_K, &vfull[b & 1]);
-            };
-            // O += W V for block c (W written by the rows, V in stage c & 1)
-            auto pv = [&](int c) {
-                const uint8_t *v = vst + (c & 1) * PT_KV;
-                const uint64_t dwh = sw128_desc(wpl), dwl = sw128_desc(wpl + PT_QTILE);
-                const uint64_t dvh = sw128_mn_desc(v, PT_KTILE), dvl = sw128_mn_desc(v + 2 * PT_KTILE, PT_KTILE);
-#pragma unroll
-                for (int j = 0; j < PT_K / 16; j++) {
-                    umma_bf16(tmem + 128, dwh + 2 * j, dvh + 128 * j, idesc_pv, (c | j) != 0);
-                    umma_bf16(tmem + 128, dwh + 2 * j, dvl + 128 * j, idesc_pv, 1u);
-                    umma_bf16(tmem + 128, dwl + 2 * j, dvh + 128 * j, idesc_pv, 1u);
-                }
-                umma_commit(&pvdone);
+            auto load = [&](uint8_t *dst, uint64_t *bar, const CUtensorMap *hi, const CUtensorMap *lo, int b) {
+                mbar_expect_tx(bar, PT_KV);
+                tma_load_2d(dst, hi, 0, y0 + b * PT_K, bar);
+                tma_load_2d(dst + PT_KTILE, hi, 64, y0 + b * PT_K, bar);
+                tma_load_2d(dst + 2 * PT_KTILE, lo, 0, y0 + b * PT_K, bar);
+                tma_load_2d(dst + 3 * PT_KTILE, lo, 64, y0 + b * PT_K, bar);
             };
             bool ok = !err_set(a.err);
-            if (ok) {
-                load_k(0);
-                load_v(0);
-                if (nb > 1) {
-                    load_k(1);
-                    load_v(1);
-                }
-            }
-            for (int b = 0; b < nb && ok; b++) {
-                const int s = b & 1;
-                ok = mbar_wait(&kfull[s], (b >> 1) & 1, a.err);
-                if (ok && b >= 2) ok = mbar_wait(&sfree[s], ((b - 2) >> 1) & 1, a.err);
-                if (!ok) break;
-                tc_fence_after();
-                const uint8_t *k = kst + s * PT_KV;
+            if (is_s) {
+                auto load_k = [&](int b) { load(kst + (b % PT_NS) * PT_KV, &kfull[b % PT_NS], &a.k_hi, &a.k_lo, b); };
+                const uint32_t k_lo = dlo_k(kst);
+                if (ok)
+                    for (int b = 0; b < PT_NS && b < nb; b++) load_k(b);
+                if (ok) ok = mbar_wait(&qfull, 0, a.err);  // the Q planes are in tensor memory
+                for (int b = 0; b < nb && ok; b++) {
+                    const int s = b & 1;
+                    ok = mbar_wait(&kfull[b % PT_NS], (b / PT_NS) & 1, a.err);
+                    if (ok && b >= 2) ok = mbar_wait(&sfree[s], ((b - 2) >> 1) & 1, a.err);
+                    if (!ok) break;
+                    PT_MARK(0, b);
+                    tc_fence_after();
+                    // S(b) = Q K_b^T (three split products) into S buffer s
+                    const uint32_t d = tmem + PT_TS + s * PT_K, kb = k_lo + (b % PT_NS) * (PT_KV >> 4);
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    const uint64_t dqh = sw128_desc(qpl + c * PT_QTILE), dql = sw128_desc(qpl + (2 + c) * PT_QTILE);
-                    const uint64_t dkh = sw128_desc(k + c * PT_KTILE), dkl = sw128_desc(k + (2 + c) * PT_KTILE);
+                    for (int c = 0; c < 2; c++) {
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        umma_bf16(tmem + s * PT_K, dqh + 2 * j, dkh + 2 * j, idesc_s, (c | j) != 0);
-                        umma_bf16(tmem + s * PT_K, dqh + 2 * j, dkl + 2 * j, idesc_s, 1u);
-                        umma_bf16(tmem + s * PT_K, dql + 2 * j, dkh + 2 * j, idesc_s, 1u);
+                        for (int j = 0; j < 4; j++) {
+                            const uint32_t qa = tmem + PT_TQ + 8 * (4 * c + j), qb = qa + 64;
+                            const uint32_t kh = kb + c * (PT_KTILE >> 4) + 2 * j, kl = kh + ((2 * PT_KTILE) >> 4);
+                            if (c == 0 && j == 0)
+                                umma_ts<0>(d, qa, kh, PT_DHI, idesc_s);
+                            else
+                                umma_ts<1>(d, qa, kh, PT_DHI, idesc_s);
+                            umma_ts<1>(d, qa, kl, PT_DHI, idesc_s);
+                            umma_ts<1>(d, qb, kh, PT_DHI, idesc_s);
+                        }
                     }
-                }
-                umma_commit(&sfull[s]);
-                if (b >= 1) {
-                    // K stage (b+1)&1 held block b-1, whose S is done: refill it now
-                    if (b + 1 < nb) {
+                    umma_commit(&sfull[s]);
+                    PT_MARK(1, b);
+                    // K stage of block b-1 is free once its S is done (its
+                    // barrier's next phase is S(b+1), not yet issued)
+                    if (b >= 1 && b + 2 < nb) {
                         ok = mbar_wait(&sfull[s ^ 1], ((b - 1) >> 1) & 1, a.err);
-                        if (ok) load_k(b + 1);
-                    }
-                    if (ok) ok = mbar_wait(&wfull, (b - 1) & 1, a.err);
-                    if (!ok) break;
-                    tc_fence_after();
-                    ok = mbar_wait(&vfull[s ^ 1], ((b - 1) >> 1) & 1, a.err);
-                    if (!ok) break;
-                    pv(b - 1);
-                    // V stage (b+1)&1 is free once that PV is done
-                    if (b + 1 < nb) {
-                        ok = mbar_wait(&pvdone, (b - 1) & 1, a.err);
-                        if (ok) load_v(b + 1);
+                        if (ok) load_k(b + 2);
                     }
                 }
-                if (ok && err_set(a.err)) ok = false;
-            }
-            if (ok) {
-                ok = mbar_wait(&wfull, (nb - 1) & 1, a.err);
-                if (ok) ok = mbar_wait(&vfull[(nb - 1) & 1], ((nb - 1) >> 1) & 1, a.err);
-                if (ok) {
+            } else {
+                auto load_v = [&](int b) { load(vst + (b % PT_NS) * PT_KV, &vfull[b % PT_NS], &a.v_hi, &a.v_lo, b); };
+                const uint32_t v_lo = dlo_mn(vst, PT_KTILE);
+                if (ok)
+                    for (int b = 0; b < PT_NS && b < nb; b++) load_v(b);
+                for (int c = 0; c < nb && ok; c++) {
+                    ok = mbar_wait(&wfull, c & 1, a.err);
+                    if (ok) ok = mbar_wait(&vfull[c % PT_NS], (c / PT_NS) & 1, a.err);
+                    // the previous W V done (before this commit, so the parity
+                    // is unambiguous): its V stage takes block c + 2
+                    if (ok && c >= 1) ok = mbar_wait(&pvdone, (c - 1) & 1, a.err);
+                    if (!ok) break;
+                    PT_MARK(2, c);
                     tc_fence_after();
-                    pv(nb - 1);
-                    mbar_wait(&pvdone, (nb - 1) & 1, a.err);
+                    // O += W V of block c: A = the W planes in tensor memory
+                    const uint32_t d = tmem + PT_TO, vb = v_lo + (c % PT_NS) * (PT_KV >> 4);
+#pragma unroll
+                    for (int j = 0; j < PT_K / 16; j++) {
+                        const uint32_t wh = tmem + PT_TW + 8 * j, wl = wh + 32;
+                        const uint32_t vh = vb + 128 * j, vl = vh + ((2 * PT_KTILE) >> 4);
+                        if (c == 0 && j == 0)
+                            umma_ts<0>(d, wh, vh, PT_DHI, idesc_pv);
+                        else
+                            umma_ts<1>(d, wh, vh, PT_DHI, idesc_pv);
+                        umma_ts<1>(d, wh, vl, PT_DHI, idesc_pv);
+                        umma_ts<1>(d, wl, vh, PT_DHI, idesc_pv);
+                    }
+                    umma_commit(&pvdone);
+                    PT_MARK(3, c);
+                    if (c >= 1 && c + 2 < nb) load_v(c + 2);
                 }
+                if (ok) mbar_wait(&pvdone, (nb - 1) & 1, a.err);
             }
         }
         __syncwarp();
         __syncthreads();  // the row threads have read O
         tc_fence_after();
-        tmem_dealloc(tmem, 256);
+        if (warp == PT_ROWS / 32) tmem_dealloc(tmem, PT_TCOLS);
         return;
     }
 
-    // ---- row threads: (query q0 + i, key half hf) ----
-    const int i = tid & 127, hf = tid >> 7, pid = 1 + (warp & 3);
-    const bool qvalid = q0 + i < a.T;
+    // ---- row threads: (query q0 + i, key quarter qt of each block) ----
+    const int gid = 1 + (warp & 3);
     const int qpos = a.p0 + q0 + i;
     const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's lanes
+    tmem_st16(tl + PT_TQ + 16 * qt, qh);
+    tmem_st16(tl + PT_TQ + 64 + 16 * qt, ql);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&qfull);
     float m = -1e30f, L = 0.f;
     bool bad = false;
     for (int b = 0; b < nb; b++) {
         const int s = b & 1;
         bad |= !mbar_wait(&sfull[s], (b >> 1) & 1, a.err);
+        if (tid == 0) PT_MARK(5, b);
         tc_fence_after();
-        float sv[32], so[32];
-        tmem_ld32(tl + s * PT_K + hf * 32, sv);
-        tmem_ld32(tl + s * PT_K + (hf ^ 1) * 32, so);
+        float sv[16];
+        tmem_ld16(tl + PT_TS + s * PT_K + qt * 16, sv);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sfree[s]);
-        const int kb = b * PT_K;
-        const int nv = qvalid ? max(0, min(32, qpos - (kb + hf * 32) + 1)) : 0;
-        const int nvo = qvalid ? max(0, min(32, qpos - (kb + (hf ^ 1) * 32) + 1)) : 0;
-        // the other half's maximum: the second half starts from the running
-        // maximum after the first
-        float mo = -1e30f;
+        const int nv = qvalid ? max(0, min(16, qpos - (b * PT_K + qt * 16) + 1)) : 0;
+        // blocks below the diagonal have every key valid in every row of the
+        // warp: no masking there
+        const bool full = __all_sync(0xffffffffu, nv == 16);
+        // this quarter's maximum, shared with the row's other three threads
+        float t[16];
 #pragma unroll
-        for (int j = 0; j < 32; j++)
-            if (j < nvo) mo = fmaxf(mo, __fmul_rn(so[j], a.scale));
-        if (hf) m = fmaxf(m, mo);
-        // The sequential rule: a_j in place; at a new maximum, c_j in place
-        // and the key's bit set. The running maximum before each key is a one-operation chain; the
-        // rest is independent per key. At a new maximum (d = s_j - m > 0) the
+        for (int j = 0; j < 16; j++) {
+            sv[j] = __fmul_rn(sv[j], a.scale);
+            t[j] = (full || j < nv) ? sv[j] : -1e30f;
+        }
+#pragma unroll
+        for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+            for (int j = 0; j < w; j++) t[j] = fmaxf(t[j], t[j + w]);
+        xmax[qt][i] = t[0];
+        if (group_sync_or(gid, bad)) {
+            bad = true;
+            break;
+        }
+        // the running maximum before this quarter (exactly the reference's
+        // there) and at the block's end
+        float mend = m;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float x = xmax[q][i];
+            if (q < qt) m = fmaxf(m, x);
+            mend = fmaxf(mend, x);
+        }
+        // The sequential rule: a_j in place, or c_j at a new maximum. The
+        // running maximum before each key is a one-operation chain; the rest
+        // is independent per key. At a new maximum (d = s_j - m > 0) the
         // reference's c_j = fexp(m - s_j) = fexp(-d), else a_j = fexp(d): the
         // argument is -|d| either way (round-to-nearest is sign-symmetric).
-        uint32_t nm = 0;
-        float pm[32];
+        // The quarter has a new maximum iff its running maximum moves.
+        const float m0 = m;
+        float pm[16], raw[16];
+        if (full) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            sv[j] = __fmul_rn(sv[j], a.scale);
-            pm[j] = m;
-            if (j < nv) m = fmaxf(m, sv[j]);
+            for (int j = 0; j < 16; j++) {
+                pm[j] = m;
+                m = fmaxf(m, sv[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                raw[j] = sv[j];
+                sv[j] = fast_expf_nonpos(-fabsf(__fsub_rn(sv[j], pm[j])));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                pm[j] = m;
+                if (j < nv) m = fmaxf(m, sv[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                raw[j] = j < nv ? sv[j] : -1e30f;  // masked keys are never a new maximum
+                sv[j] = j < nv ? fast_expf_nonpos(-fabsf(__fsub_rn(sv[j], pm[j]))) : 0.f;
+            }
         }
+        const bool anynew = __any_sync(0xffffffffu, m > m0);
+        m = mend;
+        // w_j = a_j * prod_{t > j in the quarter} c_t (a_j = 1 at a new
+        // maximum), from the quarter's last key down; P = the whole product
+        float P = 1.0f;
+        if (anynew) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-            const float d = __fsub_rn(sv[j], pm[j]);
-            if (j < nv) nm |= (d > 0.f ? 1u : 0u) << j;
-            sv[j] = j < nv ? fast_expf(-fabsf(d)) : 0.f;
-        }
-        if (!hf) m = fmaxf(m, mo);  // the running maximum at the block's end
-        // w_j = a_j * prod_{t > j} c_t (a_j = 1 at a new maximum), from the
-        // block's last key down: the second half first, the first half
-        // continuing its product; C = the whole product
-        auto backward = [&](float P) {
-#pragma unroll
-            for (int j = 31; j >= 0; j--) {
-                const bool isn = (nm >> j) & 1u;
+            for (int j = 15; j >= 0; j--) {
+                const bool isn = raw[j] > pm[j];
                 const float wj = isn ? P : __fmul_rn(sv[j], P);
                 if (isn) P = __fmul_rn(P, sv[j]);
                 sv[j] = wj;
             }
-            return P;
-        };
-        float ls = 0.f, C;
-        if (hf) {
-            const float P1 = backward(1.0f);
+        }
+        float ls = 0.f;
 #pragma unroll
-            for (int j = 0; j < 32; j++) ls = __fadd_rn(ls, sv[j]);
-            xch[i] = make_float2(P1, ls);
-        }
-        if (pair_sync_or(pid, bad)) {
-            bad = true;
-            break;
-        }
-        if (!hf) {
-            const float2 x = xch[i];
-            C = backward(x.x);
+        for (int j = 0; j < 16; j++) ls = __fadd_rn(ls, sv[j]);
+        xprod[qt][i] = make_float2(P, ls);
+        group_sync(gid);
+        // the product of the later quarters (this quarter's weights take
+        // it), the block's correction C and its weight sum, in the same
+        // order in all four threads
+        float Cr = 1.0f, lsb = 0.f, Sq = 1.0f;
 #pragma unroll
-            for (int j = 0; j < 32; j++) ls = __fadd_rn(ls, sv[j]);
-            L = __fadd_rn(__fmul_rn(L, C), __fadd_rn(ls, x.y));
-            xch[i].x = C;
+        for (int q = 3; q >= 0; q--) {
+            const float2 x = xprod[q][i];
+            if (q == qt) Sq = Cr;
+            lsb = __fadd_rn(lsb, __fmul_rn(x.y, Cr));
+            Cr = __fmul_rn(Cr, x.x);
         }
-        pair_sync(pid);
-        if (hf) C = xch[i].x;
+        const float C = Cr;
+        L = __fadd_rn(__fmul_rn(L, C), lsb);
+        if (__any_sync(0xffffffffu, Sq != 1.0f))
+#pragma unroll
+            for (int j = 0; j < 16; j++) sv[j] = __fmul_rn(sv[j], Sq);
+        uint32_t wh[8], wl[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) split2_bf16(sv[2 * k], sv[2 * k + 1], wh[k], wl[k]);
         // W and O are free once the previous block's W V is done
         if (b > 0) bad |= !mbar_wait(&pvdone, (b - 1) & 1, a.err);
+        if (tid == 0) PT_MARK(6, b);
         tc_fence_after();
-        // O <- O * C on this half's 64 columns (a warp whose rows all have
+        // O <- O * C on this quarter's 32 columns (a warp whose rows all have
         // C = 1 leaves O as it is)
         if (b > 0 && __any_sync(0xffffffffu, C != 1.0f)) {
-#pragma unroll 1
-            for (int c = 0; c < 2; c++) {
-                float t[32];
-                const uint32_t ta = tl + 128 + hf * 64 + 32 * c;
-                tmem_ld32(ta, t);
+            float o[32];
+            const uint32_t ta = tl + PT_TO + qt * 32;
+            tmem_ld32(ta, o);
 #pragma unroll
-                for (int k = 0; k < 32; k++) t[k] = __fmul_rn(t[k], C);
-                tmem_st32(ta, t);
-            }
+            for (int k = 0; k < 32; k++) o[k] = __fmul_rn(o[k], C);
+            tmem_st32(ta, o);
         }
-        // this half's 32 weights into the W planes (keys 32 hf .. +31 of row i)
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                uint16_t h0, l0, h1, l1;
-                split_bf16(sv[8 * c + 2 * k], h0, l0);
-                split_bf16(sv[8 * c + 2 * k + 1], h1, l1);
-                hw[k] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                lw[k] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-            }
-            const uint32_t o = (i >> 3) * 1024 + (i & 7) * 128 + ((((hf * 4 + c) ^ (i & 7))) << 4);
-            *reinterpret_cast<uint4 *>(wpl + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4 *>(wpl + PT_QTILE + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
-        fence_proxy_async();
+        // this quarter's 16 weights (keys 16 qt .. +15 of row i) into the W planes
+        tmem_st8(tl + PT_TW + 8 * qt, wh);
+        tmem_st8(tl + PT_TW + 32 + 8 * qt, wl);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&wfull);
+        if (tid == 0) PT_MARK(7, b);
     }
-    // O / sum into the output row (1 / sum from the first half's thread)
-    if (!hf) xch[i].y = L > 0.f ? __fdiv_rn(1.0f, L) : 0.f;
-    pair_sync(pid);
-    const float inv = xch[i].y;
+    // O / sum into this quarter's 32 output columns
+    const float inv = L > 0.f ? __fdiv_rn(1.0f, L) : 0.f;
     if (!bad) bad = !mbar_wait(&pvdone, (nb - 1) & 1, a.err);
     bad = __any_sync(0xffffffffu, bad);
     tc_fence_after();
     if (!bad) {
-        float *orow = a.out + (size_t)(q0 + i) * a.q_stride + h * PT_HD + hf * 64;
-#pragma unroll 1
-        for (int c = 0; c < 2; c++) {
-            float t[32];
-            tmem_ld32(tl + 128 + hf * 64 + 32 * c, t);
-            if (qvalid)
+        float o[32];
+        tmem_ld32(tl + PT_TO + qt * 32, o);
+        if (qvalid) {
+            float *orow = a.out + (size_t)(q0 + i) * a.q_stride + h * PT_HD + qt * 32;
 #pragma unroll
-                for (int k = 0; k < 32; k += 4)
-                    *reinterpret_cast<float4 *>(orow + 32 * c + k) =
-                        make_float4(__fmul_rn(t[k], inv), __fmul_rn(t[k + 1], inv), __fmul_rn(t[k + 2], inv),
-                                    __fmul_rn(t[k + 3], inv));
+            for (int k = 0; k < 32; k += 4)
+                *reinterpret_cast<float4 *>(orow + k) =
+                    make_float4(__fmul_rn(o[k], inv), __fmul_rn(o[k + 1], inv), __fmul_rn(o[k + 2], inv),
+                                __fmul_rn(o[k + 3], inv));
         }
     }
     tc_fence_before();

@@ -21,6 +21,10 @@ __device__ __forceinline__ float fast_expf(float x) {
     if (x > 88.0f) return 1e38f;
     return __uint_as_float(__float2uint_rz(__fmaf_rn(12102203.0f, x, 1064866805.0f)));
 }
+// The same for x <= 0, where the upper clamp cannot apply.
+__device__ __forceinline__ float fast_expf_nonpos(float x) {
+    return x < -88.0f ? 0.0f : __uint_as_float(__float2uint_rz(__fmaf_rn(12102203.0f, x, 1064866805.0f)));
+}
 
 // F32 -> BF16 -> F32 with the reference's round-half-up on the magnitude
 // (ds_kernels.c:2464-2492).

@@ -170,11 +170,14 @@ int orc_int8_quantize(const uint16_t *W, int out_dim, int in_dim,
 
 /* int8_matvec_generic (ds_quantize.c:154-169), the x86 path:
  * y[r] = scale[r] * sum_c (q+128) x[c] + off[r] * sum_c x[c], both sums
- * sequential. gcc 13 at -O3 -march=native (the flags oracle/Makefile builds
- * the reference with) leaves the inner product-add unfused (the int->float
- * conversion sits between the product and the add) and fuses the tail as
- * fma(scale, dot, off * x_sum); this restatement does the same, so the two
- * agree bit for bit. */
+ * sequential. The reference builds with -O3 -march=native and gcc's default
+ * contraction (its Makefile, as oracle/Makefile does), so what it computes
+ * depends on the host: where the target has FMA, gcc fuses the inner
+ * product-add into one FMA per element and the tail into
+ * fma(scale, dot, off * x_sum). This restatement, built with contraction
+ * off, spells out the same operations (fused dot under __FMA__, else the
+ * plain product-add), so the two agree bit for bit on the machine both are
+ * built on. */
 void orc_int8_matvec(float *y, const float *x, const int8_t *q, const float *scale,
                      const float *off, int out_dim, int in_dim) {
     float xs = 0.0f;
@@ -183,7 +186,11 @@ void orc_int8_matvec(float *y, const float *x, const int8_t *q, const float *sca
     for (int r = 0; r < out_dim; r++) {
         const int8_t *row = q + (size_t)r * in_dim;
         float d = 0.0f;
+#ifdef __FMA__
+        for (int c = 0; c < in_dim; c++) d = fmaf((float)((int)row[c] + 128), x[c], d);
+#else
         for (int c = 0; c < in_dim; c++) d += (float)((int)row[c] + 128) * x[c];
+#endif
         y[r] = fmaf(scale[r], d, off[r] * xs);
     }
 }

@@ -77,8 +77,9 @@ def test_int8_matvec_bit_exact(orc):
     y1, y2 = np.empty(300, np.float32), np.empty(300, np.float32)
     orc.orc_int8_matvec(y1.ctypes.data, x.ctypes.data, q.ctypes.data, s.ctypes.data, o.ctypes.data, 300, 1280)
     r.ref_int8_matvec(y2.ctypes.data, x.ctypes.data, q.ctypes.data, s.ctypes.data, o.ctypes.data, 300, 1280)
-    # the oracle follows the compiled reference's operation order (unfused
-    # product-add in the dot, fused tail), so every output bit agrees
+    # the oracle follows the operation order the reference's own build uses
+    # on this host (FMA-contracted dot and tail where the target has FMA),
+    # so every output bit agrees
     assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
 
 

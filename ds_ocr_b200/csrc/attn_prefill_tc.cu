@@ -58,7 +58,7 @@ constexpr int PT_THREADS = PT_ROWS + 64;    // + the two issuing warps
 constexpr uint32_t PT_TS = 0;               // S buffers: 0..63, 64..127
 constexpr uint32_t PT_TO = 128;             // O: 128 columns
 constexpr uint32_t PT_TQ = 256;             // Q hi: 64 columns of BF16 pairs; Q lo: the next 64
-constexpr uint32_t PT_TW = 384;             // W hi: 32 columns; W lo: the next 32
+constexpr uint32_t PT_TW = 384;             // two W buffers of 64: hi (32 columns of pairs), lo (32)
 constexpr uint32_t PT_TCOLS = 512;
 
 #ifdef PT_TRACE
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *kst = smem;                                   // K stages: hi (2 tiles), lo (2 tiles)
     uint8_t *vst = smem + PT_NS * PT_KV;                   // V stages: the same
-    __shared__ uint64_t kfull[PT_NS], vfull[PT_NS], sfull[2], sfree[2], qfull, wfull, pvdone;
+    __shared__ uint64_t kfull[PT_NS], vfull[PT_NS], sfull[2], sfree[2], qfull, wfull[2], pvdone[2];
     __shared__ uint32_t tmem_base;
     __shared__ float xmax[4][PT_Q];                        // per key quarter and query: its maximum
     __shared__ float2 xprod[4][PT_Q];                      // ... its product of c_j and sum of weights
@@ -187,8 +187,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
             mbar_init(&sfree[s], PT_ROWS / 32);
         }
         mbar_init(&qfull, PT_ROWS / 32);
-        mbar_init(&wfull, PT_ROWS / 32);
-        mbar_init(&pvdone, 1);
+        mbar_init(&wfull[0], PT_ROWS / 32);
+        mbar_init(&wfull[1], PT_ROWS / 32);
+        mbar_init(&pvdone[0], 1);
+        mbar_init(&pvdone[1], 1);
         mbar_fence_init();
     }
     if (warp == PT_ROWS / 32) tmem_alloc(&tmem_base, PT_TCOLS);
@@ -272,11 +274,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
                 if (ok)
                     for (int b = 0; b < PT_NS && b < nb; b++) load_v(b);
                 for (int c = 0; c < nb && ok; c++) {
-                    ok = mbar_wait(&wfull, c & 1, a.err);
-                    if (ok) ok = mbar_wait(&vfull[c % PT_NS], (c / PT_NS) & 1, a.err);
+                    ok = mbar_wait(&vfull[c % PT_NS], (c / PT_NS) & 1, a.err);
                     // the previous W V done (before this commit, so the parity
                     // is unambiguous): its V stage takes block c + 2
-                    if (ok && c >= 1) ok = mbar_wait(&pvdone, (c - 1) & 1, a.err);
+                    if (ok && c >= 1) ok = mbar_wait(&pvdone[(c - 1) & 1], ((c - 1) >> 1) & 1, a.err);
+                    if (ok) ok = mbar_wait(&wfull[c & 1], (c >> 1) & 1, a.err);
                     if (!ok) break;
                     PT_MARK(2, c);
                     tc_fence_after();
@@ -284,7 +286,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
                     const uint32_t d = tmem + PT_TO, vb = v_lo + (c % PT_NS) * (PT_KV >> 4);
 #pragma unroll
                     for (int j = 0; j < PT_K / 16; j++) {
-                        const uint32_t wh = tmem + PT_TW + 8 * j, wl = wh + 32;
+                        const uint32_t wh = tmem + PT_TW + (c & 1) * 64 + 8 * j, wl = wh + 32;
                         const uint32_t vh = vb + 128 * j, vl = vh + ((2 * PT_KTILE) >> 4);
                         if (c == 0 && j == 0)
                             umma_ts<0>(d, wh, vh, PT_DHI, idesc_pv);
@@ -293,11 +295,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
                         umma_ts<1>(d, wh, vl, PT_DHI, idesc_pv);
                         umma_ts<1>(d, wl, vh, PT_DHI, idesc_pv);
                     }
-                    umma_commit(&pvdone);
+                    umma_commit(&pvdone[c & 1]);
                     PT_MARK(3, c);
                     if (c >= 1 && c + 2 < nb) load_v(c + 2);
                 }
-                if (ok) mbar_wait(&pvdone, (nb - 1) & 1, a.err);
+                if (ok) mbar_wait(&pvdone[(nb - 1) & 1], ((nb - 1) >> 1) & 1, a.err);
             }
         }
         __syncwarp();
@@ -316,7 +318,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&qfull);
-    float m = -1e30f, L = 0.f;
+    // O is accumulated as O / R, R the product of the block corrections
+    // since the last renormalisation (so W_b / R_b is added and O needs no
+    // per-block rescale); R is folded back into O only when it gets small
+    float m = -1e30f, L = 0.f, R = 1.0f;
     bool bad = false;
     for (int b = 0; b < nb; b++) {
         const int s = b & 1;
@@ -423,34 +428,50 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
         if (__any_sync(0xffffffffu, Sq != 1.0f))
 #pragma unroll
             for (int j = 0; j < 16; j++) sv[j] = __fmul_rn(sv[j], Sq);
+        // W buffer b & 1 is free once the W V of block b-2 is done
+        if (b >= 2) bad |= !mbar_wait(&pvdone[(b - 2) & 1], ((b - 2) >> 1) & 1, a.err);
+        float Rn = __fmul_rn(R, C);
+        const bool renorm = Rn < 0x1p-60f;  // also C = 0: O * 0 as the reference
+        if (__any_sync(0xffffffffu, renorm)) {
+            // O (as O / R) <- O * C, i.e. times Rn, once the previous block's
+            // W V is in; then R = 1 for these rows
+            if (b >= 1) bad |= !mbar_wait(&pvdone[(b - 1) & 1], ((b - 1) >> 1) & 1, a.err);
+            tc_fence_after();
+            if (b >= 1) {
+                const float f = renorm ? Rn : 1.0f;
+                float o[32];
+                const uint32_t ta = tl + PT_TO + qt * 32;
+                tmem_ld32(ta, o);
+#pragma unroll
+                for (int k = 0; k < 32; k++) o[k] = __fmul_rn(o[k], f);
+                tmem_st32(ta, o);
+            }
+            if (renorm) Rn = 1.0f;
+        }
+        R = Rn;
+        if (__any_sync(0xffffffffu, Rn != 1.0f)) {
+            const float ir = __fdiv_rn(1.0f, Rn);
+#pragma unroll
+            for (int j = 0; j < 16; j++) sv[j] = __fmul_rn(sv[j], ir);
+        }
         uint32_t wh[8], wl[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) split2_bf16(sv[2 * k], sv[2 * k + 1], wh[k], wl[k]);
-        // W and O are free once the previous block's W V is done
-        if (b > 0) bad |= !mbar_wait(&pvdone, (b - 1) & 1, a.err);
         if (tid == 0) PT_MARK(6, b);
         tc_fence_after();
-        // O <- O * C on this quarter's 32 columns (a warp whose rows all have
-        // C = 1 leaves O as it is)
-        if (b > 0 && __any_sync(0xffffffffu, C != 1.0f)) {
-            float o[32];
-            const uint32_t ta = tl + PT_TO + qt * 32;
-            tmem_ld32(ta, o);
-#pragma unroll
-            for (int k = 0; k < 32; k++) o[k] = __fmul_rn(o[k], C);
-            tmem_st32(ta, o);
-        }
-        // this quarter's 16 weights (keys 16 qt .. +15 of row i) into the W planes
-        tmem_st8(tl + PT_TW + 8 * qt, wh);
-        tmem_st8(tl + PT_TW + 32 + 8 * qt, wl);
+        // this quarter's 16 weights (keys 16 qt .. +15 of row i) into W buffer b & 1
+        const uint32_t tw = tl + PT_TW + (b & 1) * 64 + 8 * qt;
+        tmem_st8(tw, wh);
+        tmem_st8(tw + 32, wl);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&wfull);
+        if (lane == 0) mbar_arrive(&wfull[b & 1]);
         if (tid == 0) PT_MARK(7, b);
     }
-    // O / sum into this quarter's 32 output columns
-    const float inv = L > 0.f ? __fdiv_rn(1.0f, L) : 0.f;
-    if (!bad) bad = !mbar_wait(&pvdone, (nb - 1) & 1, a.err);
+    // O = (O / R) * R / sum into this quarter's 32 output columns
+    const float f = L > 0.f ? __fdiv_rn(R, L) : 0.f;
+    if (!bad && nb >= 2) bad = !mbar_wait(&pvdone[(nb - 2) & 1], ((nb - 2) >> 1) & 1, a.err);
+    if (!bad) bad = !mbar_wait(&pvdone[(nb - 1) & 1], ((nb - 1) >> 1) & 1, a.err);
     bad = __any_sync(0xffffffffu, bad);
     tc_fence_after();
     if (!bad) {
@@ -461,8 +482,8 @@ __global__ void __launch_bounds__(PT_THREADS, 1) attn_prefill_tc_kernel(const __
 #pragma unroll
             for (int k = 0; k < 32; k += 4)
                 *reinterpret_cast<float4 *>(orow + k) =
-                    make_float4(__fmul_rn(o[k], inv), __fmul_rn(o[k + 1], inv), __fmul_rn(o[k + 2], inv),
-                                __fmul_rn(o[k + 3], inv));
+                    make_float4(__fmul_rn(o[k], f), __fmul_rn(o[k + 1], f), __fmul_rn(o[k + 2], f),
+                                __fmul_rn(o[k + 3], f));
         }
     }
     tc_fence_before();

@@ -92,6 +92,62 @@ __global__ void pd_rope_kv_kernel(const float *__restrict__ qkv, int T, int NH, 
     lp[idx + half] = b;
 }
 
+// The same with four consecutive rotary pairs per thread (hd/2 % 4 == 0):
+// float4 loads of the row and of the tables, 8-byte plane stores, the same
+// arithmetic per element.
+__device__ __forceinline__ uint2 pack4_bf16(uint16_t a, uint16_t b, uint16_t c, uint16_t d) {
+    return make_uint2((uint32_t)a | ((uint32_t)b << 16), (uint32_t)c | ((uint32_t)d << 16));
+}
+__global__ void pd_rope_kv4_kernel(const float *__restrict__ qkv, int T, int NH, int HD, int p0,
+                                   const float *__restrict__ cos_t, const float *__restrict__ sin_t, float *q,
+                                   uint16_t *k_hi, uint16_t *k_lo, uint16_t *v_hi, uint16_t *v_lo, int kv_max) {
+    const int half = HD / 2, QD = NH * HD, g4 = half / 4;
+    const unsigned per_tok = 3u * NH * g4;
+    const unsigned i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= per_tok * (unsigned)T) return;
+    const int t = (int)(i / per_tok);
+    int r = (int)(i - (unsigned)t * per_tok);
+    const int m = r / (NH * g4);
+    r -= m * NH * g4;
+    const int h = r / g4, d = 4 * (r - h * g4);
+    const float *row = qkv + (size_t)t * 3 * QD + (size_t)m * QD + h * HD;
+    const float4 x1 = *reinterpret_cast<const float4 *>(row + d), x2 = *reinterpret_cast<const float4 *>(row + d + half);
+    const int pos = p0 + t;
+    float a0[4] = {x1.x, x1.y, x1.z, x1.w}, a1[4] = {x2.x, x2.y, x2.z, x2.w};
+    if (m < 2) {
+        const float *cs = cos_t + (size_t)pos * HD, *sn = sin_t + (size_t)pos * HD;
+        const float4 c0 = *reinterpret_cast<const float4 *>(cs + d), s0 = *reinterpret_cast<const float4 *>(sn + d);
+        const float4 c1 = *reinterpret_cast<const float4 *>(cs + d + half);
+        const float4 s1 = *reinterpret_cast<const float4 *>(sn + d + half);
+        const float cc0[4] = {c0.x, c0.y, c0.z, c0.w}, ss0[4] = {s0.x, s0.y, s0.z, s0.w};
+        const float cc1[4] = {c1.x, c1.y, c1.z, c1.w}, ss1[4] = {s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const float u = a0[k], v = a1[k];
+            a0[k] = __fsub_rn(__fmul_rn(u, cc0[k]), __fmul_rn(v, ss0[k]));
+            a1[k] = __fadd_rn(__fmul_rn(u, ss1[k]), __fmul_rn(v, cc1[k]));
+        }
+    }
+    if (m == 0) {
+        float *qr = q + (size_t)t * QD + h * HD;
+        *reinterpret_cast<float4 *>(qr + d) = make_float4(a0[0], a0[1], a0[2], a0[3]);
+        *reinterpret_cast<float4 *>(qr + d + half) = make_float4(a1[0], a1[1], a1[2], a1[3]);
+        return;
+    }
+    const size_t idx = ((size_t)h * kv_max + pos) * HD + d;
+    uint16_t *hp = m == 1 ? k_hi : v_hi, *lp = m == 1 ? k_lo : v_lo;
+    uint16_t hh[8], ll[8];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        split_bf16(a0[k], hh[k], ll[k]);
+        split_bf16(a1[k], hh[4 + k], ll[4 + k]);
+    }
+    *reinterpret_cast<uint2 *>(hp + idx) = pack4_bf16(hh[0], hh[1], hh[2], hh[3]);
+    *reinterpret_cast<uint2 *>(lp + idx) = pack4_bf16(ll[0], ll[1], ll[2], ll[3]);
+    *reinterpret_cast<uint2 *>(hp + idx + half) = pack4_bf16(hh[4], hh[5], hh[6], hh[7]);
+    *reinterpret_cast<uint2 *>(lp + idx + half) = pack4_bf16(ll[4], ll[5], ll[6], ll[7]);
+}
+
 // x += y over n floats (n % 4 == 0): the residual adds (ds_vec_add).
 __global__ void pd_add_kernel(float *x, const float *__restrict__ y, size_t n4) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -135,6 +191,12 @@ cudaError_t launch_pd_split(const float *x, int M, int H, const float *nw, float
 cudaError_t launch_pd_rope_kv(const float *qkv, int T, int NH, int HD, int p0, const float *cos_t, const float *sin_t,
                               float *q, uint16_t *k_hi, uint16_t *k_lo, uint16_t *v_hi, uint16_t *v_lo, int kv_max,
                               cudaStream_t st) {
+    if ((HD / 2) % 4 == 0 && (long long)3 * NH * (HD / 8) * T < (1LL << 31)) {
+        const unsigned n4 = 3u * NH * (HD / 8) * (unsigned)T;
+        pd_rope_kv4_kernel<<<(n4 + 255) / 256, 256, 0, st>>>(qkv, T, NH, HD, p0, cos_t, sin_t, q, k_hi, k_lo, v_hi,
+                                                              v_lo, kv_max);
+        return cudaGetLastError();
+    }
     const long long n = 3LL * NH * (HD / 2) * T;
     pd_rope_kv_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(qkv, T, NH, HD, p0, cos_t, sin_t, q, k_hi, k_lo,
                                                                   v_hi, v_lo, kv_max);

@@ -8,15 +8,17 @@
 // only a few MB each, so the time goes to latency (dependency waits, the
 // first bytes of each phase), not to bandwidth. Here every byte that does not
 // depend on the routing is in flight before the dependency wait, and every
-// byte that does is requested as soon as the routing is known:
-//   before the wait  this CTA's shared-expert gate/up rows and its rows of
-//                    the shared down projection, copied into shared memory
-//                    by the TMA engine;
-//   after routing    its rows of the six routed down projections (TMA, into
-//                    shared memory), while its warps stream the routed
-//                    gate/up rows through registers;
-//   after the grid barrier (all of h written) the down dot products read
-//                    only shared memory.
+// byte that does is requested as soon as the routing is known. A producer
+// warp issues all of it as TMA bulk copies into shared memory (register loads
+// from eight warps cannot keep enough bytes in flight):
+//   before the wait  this CTA's rows of the shared down projection, and its
+//                    shared-expert gate/up items (a gate row and an up row)
+//                    into a ring of item slots;
+//   after routing    its rows of the six routed down projections, and its
+//                    routed gate/up items into the ring, each slot refilled
+//                    as soon as the consumer warp releases it;
+//   after the grid dependency (every CTA's part of h counted done) the down
+//                    dot products read only shared memory.
 // One CTA per SM; the barrier is safe because the grid never exceeds the SM
 // count and a CTA always fits on an SM (the kernels around it are small).
 //
@@ -40,6 +42,7 @@ constexpr int MS_MAXROWS = 10; // output rows per CTA (hidden / grid, rounded up
 constexpr int MS_MAXE = 84;    // experts: 3 (E + 1) threads sum the router terms
 constexpr int MS_MAXPART = 32; // router-term parts per summing thread (O-proj CTAs <= 96)
 constexpr int MS_NSLOT = 8;    // down dots per output row (one warp each): top_k (6) routed + the shared row's two halves
+constexpr int MS_RING = 32;    // gate/up items (a gate row and an up row) in flight in shared memory; one producer lane each
 
 struct MsLayout {
     int i0, i1;   // shared items of this CTA
@@ -109,7 +112,7 @@ __device__ __forceinline__ void ms_cbar() { asm volatile("bar.sync 1, %0;" :: "r
 
 __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t bar_sh, bar_sd, bar_rd, bar_nw, bar_route;
+    __shared__ uint64_t bar_sd, bar_rd, bar_nw, bar_route, ring_full[MS_RING], ring_empty[MS_RING], ring_drained;
     __shared__ float lg[MS_MAXE + 1];
     __shared__ float lsum[MS_MAXE + 1][3];
     __shared__ float rr[MS_WARPS + 1];
@@ -123,9 +126,10 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
     const int nr = K * I;
     const MsLayout L = ms_layout(a);
     const int ns = L.i1 - L.i0, nrows = L.j1 - L.j0;
-    // shared memory: A = shared gate/up rows, D = down rows, xs, norm weight
-    uint16_t *regA = reinterpret_cast<uint16_t *>(smem);
-    uint16_t *regD = reinterpret_cast<uint16_t *>(smem + a.a_bytes);
+    // shared memory: the gate/up item ring (then the routed down rows), the
+    // shared down rows, xs, norm weight
+    uint16_t *ring = reinterpret_cast<uint16_t *>(smem);
+    uint16_t *sdn = reinterpret_cast<uint16_t *>(smem + a.a_bytes);
     float *xs = reinterpret_cast<float *>(smem + a.a_bytes + a.d_bytes);
     float *nws = xs + H;
     const uint16_t *sgu = a.block + (size_t)E * 2 * I * H;
@@ -134,40 +138,75 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
         // this launch's number (every CTA of a launch adds one): the
         // completion counters below only ever grow
         s_epoch = atomicAdd(a.bar, 1ull) / gridDim.x;
-        mbar_init(&bar_sh, 1);
         mbar_init(&bar_sd, 1);
         mbar_init(&bar_rd, 1);
         mbar_init(&bar_nw, 1);
         mbar_init(&bar_route, 1);
+        for (int k = 0; k < MS_RING; k++) {
+            mbar_init(&ring_full[k], 1);
+            mbar_init(&ring_empty[k], 1);
+        }
+        mbar_init(&ring_drained, MS_RING);
         mbar_fence_init();
     }
     __syncthreads();
+    // this CTA's gate/up items: its shared-expert items first (i0 .. i1),
+    // then its routed items (q0 .. q1); item n sits in ring slot n % MS_RING
+    const int nitems = ns + (L.q1 - L.q0);
     if (warp == MS_WARPS) {
         // producer warp: every TMA copy, so no consumer warp waits behind an
-        // issue. Before the dependency wait: the norm weight, the shared
-        // expert's gate/up rows of this CTA's items and its down rows of this
-        // CTA's outputs; once warp 0 has the routing: the routed down rows.
+        // issue. At once: the norm weight, this CTA's rows of the shared
+        // down projection and its shared-expert items; once warp 0 has the
+        // routing: the routed down rows and the routed items. Each ring slot
+        // is refilled as soon as its consumer warp has released it.
+        // lane l < MS_RING owns ring slot l (items l, l + MS_RING, ...): a
+        // bulk copy costs its issuing thread a fixed time, so one thread
+        // alone could not keep the slots full
         if (lane == 0) {
             mbar_expect_tx(&bar_nw, (uint32_t)H * 4);
             bulk_g2s(nws, a.norm_w, (uint32_t)H * 4, &bar_nw);
-            if (ns > 0) {
-                const uint32_t rb = (uint32_t)ns * H * 2;
-                mbar_expect_tx(&bar_sh, 2 * rb);
-                bulk_g2s_stream(regA, sgu + (size_t)L.i0 * H, rb, &bar_sh);
-                bulk_g2s_stream(regA + (size_t)ns * H, sgu + (size_t)(S + L.i0) * H, rb, &bar_sh);
-            }
             if (nrows > 0) {
                 const uint32_t db = (uint32_t)nrows * S * 2;
                 mbar_expect_tx(&bar_sd, db);
-                bulk_g2s_stream(regD + (size_t)K * nrows * I, a.sdown + (size_t)L.j0 * S, db, &bar_sd);
+                bulk_g2s_stream(sdn, a.sdown + (size_t)L.j0 * S, db, &bar_sd);
             }
-            if (mbar_wait(&bar_route, 0, a.err) && nrows > 0) {
-                const uint32_t kb = (uint32_t)nrows * I * 2;
-                mbar_expect_tx(&bar_rd, (uint32_t)K * kb);
-                for (int k = 0; k < K; k++)
-                    bulk_g2s_stream(regD + (size_t)k * nrows * I, a.down + ((size_t)s_idx[k] * H + L.j0) * I, kb,
-                                    &bar_rd);
+        }
+        {
+            const uint32_t rb = (uint32_t)H * 2;
+            bool routed = false, ok = true;
+            int last = -1;
+            for (int n = lane; n < nitems; n += MS_RING) {
+                if (n >= MS_RING && !(ok = mbar_wait(&ring_empty[lane], ((n / MS_RING) - 1) & 1, a.err))) break;
+                const uint16_t *g, *u;
+                if (n < ns) {
+                    g = sgu + (size_t)(L.i0 + n) * H;
+                    u = sgu + (size_t)(S + L.i0 + n) * H;
+                } else {
+                    if (!routed && !(ok = mbar_wait(&bar_route, 0, a.err))) break;
+                    routed = true;
+                    const int q = L.q0 + n - ns, k = q / I, i = q - k * I;
+                    const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
+                    g = base + (size_t)i * H;
+                    u = base + (size_t)(I + i) * H;
+                }
+                uint16_t *d = ring + (size_t)lane * 2 * H;
+                mbar_expect_tx(&ring_full[lane], 2 * rb);
+                bulk_g2s_stream(d, g, rb, &ring_full[lane]);
+                bulk_g2s_stream(d + H, u, rb, &ring_full[lane]);
+                last = n;
             }
+            // this slot's last item consumed: the ring may take the routed
+            // down rows
+            if (ok && last >= 0) mbar_wait(&ring_empty[lane], (last / MS_RING) & 1, a.err);
+            mbar_arrive(&ring_drained);
+        }
+        // the routed down rows (the routing is known and the ring drained)
+        if (lane == 0 && nrows > 0 && mbar_wait(&bar_route, 0, a.err) && mbar_wait(&ring_drained, 0, a.err)) {
+            const uint32_t kb = (uint32_t)nrows * I * 2;
+            mbar_expect_tx(&bar_rd, (uint32_t)K * kb);
+            for (int k = 0; k < K; k++)
+                bulk_g2s_stream(ring + (size_t)k * nrows * I, a.down + ((size_t)s_idx[k] * H + L.j0) * I, kb,
+                                &bar_rd);
         }
         return;
     }
@@ -196,13 +235,16 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
         *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
     ms_cbar();
     tr.mark(0);
-    // 2. warp 0: routing (softmax and top-k of the logits scaled by the RMS
-    //    of x), handed to the producer warp; the others meanwhile: the sum
-    //    of squares of x (block_rms_inv's order over 8 warps)
+    // 2. the sum of squares of x (block_rms_inv's order over 8 warps), then
+    //    warp 0: routing (softmax and top-k of the logits scaled by the RMS
+    //    of x), handed to the producer warp; the others start on the
+    //    shared-expert items meanwhile
     float ss = 0.f;
     for (int i = tid; i < H; i += MS_THREADS) ss = __fmaf_rn(xs[i], xs[i], ss);
     ss = warp_sum(ss);
     if (lane == 0) rr[warp] = ss;
+    ms_cbar();
+    tr.mark(1);
     if (warp == 0) {
         for (int e = lane; e <= E; e += 32) lg[e] = __fadd_rn(__fadd_rn(lsum[e][0], lsum[e][1]), lsum[e][2]);
         __syncwarp();
@@ -215,36 +257,18 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
         router_select(lg, E, K, a.renorm, s_idx, s_wt);
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_route);
+        tr.mark(6);
         if (blockIdx.x == 0 && lane < K) {
             a.d_idx[lane] = s_idx[lane];
             a.d_wt[lane] = s_wt[lane];
         }
     }
-    ms_cbar();
-    tr.mark(1);
-    // 3. routed gate/up rows into registers as soon as the routing is known
-    auto item_rows = [&](int q, const uint16_t *&g, const uint16_t *&u) {
-        const int k = q / I, i = q - k * I;
-        const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
-        g = base + (size_t)i * H;
-        u = base + (size_t)(I + i) * H;
-    };
-    Rows2<MS_CPL> cur, nxt;
-    int q = L.q0 + warp;
-    if (q < L.q1) {
-        const uint16_t *g, *u;
-        item_rows(q, g, u);
-        cur.load(g, u, H, lane);
-    }
-    // post-attention RMSNorm of x with the norm weight from shared memory
-    if (tid == 0) {
-        float t = 0.f;
-        for (int w = 0; w < MS_WARPS; w++) t = __fadd_rn(t, rr[w]);
-        rr[MS_WARPS] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)H), a.eps)));
-    }
-    if (!mbar_wait(&bar_nw, 0, a.err)) return;
-    ms_cbar();
-    const float inv = rr[MS_WARPS];
+    // post-attention RMSNorm of x (every thread sums the warps' terms in
+    // warp order) with the norm weight from shared memory
+    float t2 = 0.f;
+    for (int w = 0; w < MS_WARPS; w++) t2 = __fadd_rn(t2, rr[w]);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t2, (float)H), a.eps)));
+    mbar_wait(&bar_nw, 0, a.err);  // a timeout is recorded in *err; every warp still reaches the barriers
     const bool sim = a.simulate != 0;
     auto swiglu_out = [&](float g, float u) {
         if (sim) {
@@ -258,51 +282,35 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
     XRegBF16<MS_CPL> xr;
     xr.load_norm(xs, nws, inv, H, lane);
     tr.mark(2);
-    // 4. the shared expert's items (weights already in shared memory) while
-    //    the routed loads fly
-    if (ns > 0) {
-        if (!mbar_wait(&bar_sh, 0, a.err)) return;
-        for (int it = warp; it < ns; it += MS_WARPS) {
-            const uint16_t *gr = regA + (size_t)it * H, *ur = regA + (size_t)(ns + it) * H;
-            float g = 0.f, u = 0.f;
+    // 3. the gate/up items from the ring: item n is warp n % 8's; its gate
+    //    and up dot products, SwiGLU, into h; the slot goes back to the
+    //    producer
+    for (int n = warp; n < nitems; n += MS_WARPS) {
+        const int sl = n % MS_RING;
+        if (!mbar_wait(&ring_full[sl], (n / MS_RING) & 1, a.err)) break;
+        if (n >= ns && n < ns + MS_WARPS) tr.mark(3);
+        tr.mark(7);
+        const uint16_t *gr = ring + (size_t)sl * 2 * H, *ur = gr + H;
+        float g = 0.f, u = 0.f;
 #pragma unroll
-            for (int c = 0; c < MS_CPL; c++) {
-                const int ch = lane + 32 * c;
-                g = dot8_bf16(*reinterpret_cast<const uint4 *>(gr + 8 * ch), xr.v[c][0], xr.v[c][1], g);
-                u = dot8_bf16(*reinterpret_cast<const uint4 *>(ur + 8 * ch), xr.v[c][0], xr.v[c][1], u);
-            }
-            g = warp_sum(g);
-            u = warp_sum(u);
-            if (lane == 0) a.h[nr + L.i0 + it] = swiglu_out(g, u);
+        for (int c = 0; c < MS_CPL; c++) {
+            const int ch = lane + 32 * c;
+            g = dot8_bf16(*reinterpret_cast<const uint4 *>(gr + 8 * ch), xr.v[c][0], xr.v[c][1], g);
+            u = dot8_bf16(*reinterpret_cast<const uint4 *>(ur + 8 * ch), xr.v[c][0], xr.v[c][1], u);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ring_empty[sl]);
+        g = warp_sum(g);
+        u = warp_sum(u);
+        if (lane == 0) a.h[n < ns ? nr + L.i0 + n : L.q0 + n - ns] = swiglu_out(g, u);
     }
-    // this CTA's shared items are in h: count it (release)
+    // this CTA's shared and routed items are in h: count them (release)
     ms_cbar();
     if (tid == 0) {
         __threadfence();
         atomicAdd(a.done + K, 1ull);
-    }
-    tr.mark(3);
-    // 5. routed items, the next item's rows in flight during each dot
-    for (; q < L.q1; q += MS_WARPS) {
-        const int qn = q + MS_WARPS;
-        if (qn < L.q1) {
-            const uint16_t *g, *u;
-            item_rows(qn, g, u);
-            nxt.load(g, u, H, lane);
-        }
-        float g, u;
-        cur.dot(xr, g, u);
-        cur = nxt;
-        g = warp_sum(g);
-        u = warp_sum(u);
-        if (lane == 0) a.h[q] = swiglu_out(g, u);
-    }
-    // count this CTA's routed slots as done (release)
-    ms_cbar();
-    if (tid == 0 && L.q1 > L.q0) {
-        __threadfence();
-        for (int k = L.q0 / I; k < K && k * I < L.q1; k++) atomicAdd(a.done + k, 1ull);
+        if (L.q1 > L.q0)
+            for (int k = L.q0 / I; k < K && k * I < L.q1; k++) atomicAdd(a.done + k, 1ull);
     }
     tr.mark(4);
     prefetch_next(a.pf, a.pf_bytes);
@@ -326,10 +334,7 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
             }
             if ((it & 1023u) == 1023u && *(volatile unsigned *)a.err) break;
         }
-        if (!ok) {
-            if (lane == 0) atomicExch(a.err, 1u);
-            return;
-        }
+        if (!ok && lane == 0) atomicExch(a.err, 1u);
         const float *hv = s < K ? a.h + s * I : a.h + nr + (s - K) * half;
         const int nch = I >> 3;
         XRegBF16<MS_DCPL> hr;
@@ -343,10 +348,9 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
                 hr.v[c][0] = hr.v[c][1] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
-        if (nrows > 0 && !mbar_wait(s < K ? &bar_rd : &bar_sd, 0, a.err)) return;
+        if (nrows > 0) mbar_wait(s < K ? &bar_rd : &bar_sd, 0, a.err);  // timeouts recorded in *err
         auto wrow = [&](int r) {
-            return s < K ? regD + ((size_t)s * nrows + r) * I
-                         : regD + (size_t)K * nrows * I + (size_t)r * S + (s - K) * half;
+            return s < K ? ring + ((size_t)s * nrows + r) * I : sdn + (size_t)r * S + (s - K) * half;
         };
         for (int r = 0; r < nrows; r += 2) {
             const bool two = r + 1 < nrows;
@@ -609,22 +613,24 @@ bool moe_step_supported(int H, int I, int S, int E, int K, int sms) {
     if (K != MS_NSLOT - 2 || E > MS_MAXE || E < K || sms < 1 || (H + 15) / 16 > 3 * MS_MAXPART) return false;
     if (2 * S != 2 * I * (S / I) || S / 2 != I) return false;  // the shared row splits into two expert-width halves
     if ((H + sms - 1) / sms > MS_MAXROWS) return false;
-    return moe_step_smem(H, I, S, K, sms) <= 210 * 1024;
+    // the routed down rows of a CTA's outputs fit in the drained ring
+    if ((size_t)((H + sms - 1) / sms) * K * I * 2 > (size_t)MS_RING * 2 * H * 2) return false;
+    return moe_step_smem(H, I, S, K, sms) <= 222 * 1024;  // + about 3 KB of static shared memory
 }
 
 size_t moe_step_smem(int H, int I, int S, int K, int G) {
-    const int ns_max = (S + G - 1) / G, rows_max = (H + G - 1) / G;
-    size_t a_bytes = std::max((size_t)ns_max * 2 * H * 2, (size_t)(K * I + S) * 4);
-    size_t d_bytes = (size_t)rows_max * (K * I + S) * 2;
+    const int rows_max = (H + G - 1) / G;
+    size_t a_bytes = (size_t)MS_RING * 2 * H * 2;  // the ring; later the routed down rows
+    size_t d_bytes = (size_t)rows_max * S * 2;      // the shared down rows
     a_bytes = (a_bytes + 127) & ~(size_t)127;
     d_bytes = (d_bytes + 127) & ~(size_t)127;
     return a_bytes + d_bytes + (size_t)H * 8;
 }
 
 cudaError_t launch_moe_step(MoeStepArgs a, int grid, cudaStream_t st, bool pdl) {
-    const int ns_max = (a.S + grid - 1) / grid, rows_max = (a.H + grid - 1) / grid;
-    a.a_bytes = std::max((size_t)ns_max * 2 * a.H * 2, (size_t)(a.K * a.I + a.S) * 4);
-    a.d_bytes = (size_t)rows_max * (a.K * a.I + a.S) * 2;
+    const int rows_max = (a.H + grid - 1) / grid;
+    a.a_bytes = (size_t)MS_RING * 2 * a.H * 2;
+    a.d_bytes = (size_t)rows_max * a.S * 2;
     a.a_bytes = (a.a_bytes + 127) & ~(size_t)127;
     a.d_bytes = (a.d_bytes + 127) & ~(size_t)127;
     const size_t smem = a.a_bytes + a.d_bytes + (size_t)a.H * 8;

@@ -172,28 +172,40 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
             }
         }
         {
+            // one warp-uniform polling loop: each pass, every lane whose slot
+            // is free (and, for a routed item, whose routing is known) issues
+            // its next item; no lane's wait holds up the others (a blocking
+            // wait per lane would reconverge the warp behind the slowest slot)
             const uint32_t rb = (uint32_t)H * 2;
             bool routed = false, ok = true;
-            int last = -1;
-            for (int n = lane; n < nitems; n += MS_RING) {
-                if (n >= MS_RING && !(ok = mbar_wait(&ring_empty[lane], ((n / MS_RING) - 1) & 1, a.err))) break;
-                const uint16_t *g, *u;
-                if (n < ns) {
-                    g = sgu + (size_t)(L.i0 + n) * H;
-                    u = sgu + (size_t)(S + L.i0 + n) * H;
-                } else {
-                    if (!routed && !(ok = mbar_wait(&bar_route, 0, a.err))) break;
-                    routed = true;
-                    const int q = L.q0 + n - ns, k = q / I, i = q - k * I;
-                    const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
-                    g = base + (size_t)i * H;
-                    u = base + (size_t)(I + i) * H;
+            int n = lane, last = -1;
+            for (uint32_t it = 0; __any_sync(0xffffffffu, n < nitems); it++) {
+                if (it >= (1u << 26)) {
+                    atomicExch(a.err, 1u);
+                    ok = false;
+                    break;
                 }
-                uint16_t *d = ring + (size_t)lane * 2 * H;
-                mbar_expect_tx(&ring_full[lane], 2 * rb);
-                bulk_g2s_stream(d, g, rb, &ring_full[lane]);
-                bulk_g2s_stream(d + H, u, rb, &ring_full[lane]);
-                last = n;
+                bool go = n < nitems;
+                if (go && n >= MS_RING) go = mbar_test(&ring_empty[lane], ((n / MS_RING) - 1) & 1);
+                if (go && n >= ns && !routed) go = routed = mbar_test(&bar_route, 0);
+                if (go) {
+                    const uint16_t *g, *u;
+                    if (n < ns) {
+                        g = sgu + (size_t)(L.i0 + n) * H;
+                        u = sgu + (size_t)(S + L.i0 + n) * H;
+                    } else {
+                        const int q = L.q0 + n - ns, k = q / I, i = q - k * I;
+                        const uint16_t *base = a.block + (size_t)s_idx[k] * 2 * I * H;
+                        g = base + (size_t)i * H;
+                        u = base + (size_t)(I + i) * H;
+                    }
+                    uint16_t *d = ring + (size_t)lane * 2 * H;
+                    mbar_expect_tx(&ring_full[lane], 2 * rb);
+                    bulk_g2s_stream(d, g, rb, &ring_full[lane]);
+                    bulk_g2s_stream(d + H, u, rb, &ring_full[lane]);
+                    last = n;
+                    n += MS_RING;
+                }
             }
             // this slot's last item consumed: the ring may take the routed
             // down rows

@@ -619,7 +619,7 @@ extern "C" int ds_cuda_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->attn, QD);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->h, hcap);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->scores, 256);
-    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->rpart, (size_t)(H / 16 + 1) * (g.n_experts + 1));
+    if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->rpart, (size_t)rf_pstride((H + 15) / 16) * (g.n_experts + 1));
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->wt, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->val, 16);
     if (rc == DS_CUDA_OK) rc = dalloc(c, m, &m->idx, 16);

@@ -451,7 +451,7 @@ __device__ void router_fold(const MvArgs &a, const float *yv, const uint4 (&wr16
     __syncthreads();
     const int row0 = blockIdx.x * 16;
     const int nrow = min(16, a.rows - row0);
-    float *mine = f.part + (size_t)blockIdx.x * (f.E + 1);
+    const int pst = rf_pstride((int)gridDim.x);
     // thread e: sum over the 16 rows of Wr[e][r] * g[r] * y[r], rows in order
     for (int e = threadIdx.x; e <= f.E; e += blockDim.x) {
         float acc = 0.f;
@@ -465,7 +465,7 @@ __device__ void router_fold(const MvArgs &a, const float *yv, const uint4 (&wr16
         } else {
             for (int i = 0; i < nrow; i++) acc = __fmaf_rn(yv[i], yv[i], acc);
         }
-        mine[e] = acc;
+        f.part[(size_t)e * pst + blockIdx.x] = acc;
     }
     if (f.no_tail) return;
     __threadfence();
@@ -475,20 +475,11 @@ __device__ void router_fold(const MvArgs &a, const float *yv, const uint4 (&wr16
     if (!last) return;
     TraceScope tr;
     __threadfence();
-    // column e summed in three runs of consecutive CTAs, each in CTA order,
-    // then (r0 + r1) + r2; a run's loads are all in flight together
+    // column e summed in three runs of consecutive CTAs (rf_run_sum)
     __shared__ float ls[256][3];
     for (int t = threadIdx.x; t < 3 * (f.E + 1); t += blockDim.x) {
         const int e = t / 3, part = t - 3 * e;
-        const int b0 = (int)gridDim.x * part / 3, b1 = (int)gridDim.x * (part + 1) / 3;
-        float v[32];
-#pragma unroll
-        for (int u = 0; u < 32; u++) v[u] = b0 + u < b1 ? __ldcg(f.part + (size_t)(b0 + u) * (f.E + 1) + e) : 0.f;
-        float acc = 0.f;
-#pragma unroll
-        for (int u = 0; u < 32; u++)
-            if (b0 + u < b1) acc = __fadd_rn(acc, v[u]);
-        ls[e][part] = acc;
+        ls[e][part] = rf_run_sum(f.part + (size_t)e * pst, (int)gridDim.x, part);
     }
     __syncthreads();
     for (int e = threadIdx.x; e <= f.E; e += blockDim.x) lg[e] = __fadd_rn(__fadd_rn(ls[e][0], ls[e][1]), ls[e][2]);
@@ -697,7 +688,8 @@ cudaError_t launch_matvec_res(const MvArgs &a, cudaStream_t st, bool pdl) {
     if (a.n <= 2048) {
         int grid = min(((a.rows + 1) / 2 + 7) / 8, sms() * 8);
         // the router fold needs one pass: 16 output rows per CTA
-        if (a.rf.Wr && (grid * 16 < a.rows || a.rf.E > 255)) return cudaErrorInvalidValue;
+        // (and its readers take the part count as (rows + 15) / 16)
+        if (a.rf.Wr && (grid != (a.rows + 15) / 16 || a.rf.E > 255)) return cudaErrorInvalidValue;
         DS_CPL_SWITCH2(a.n, 8, return launch_ex((const void *)matvec_res_kernel<CPL>, grid, 256, 0, st, pdl, args));
     }
     if (a.n > 8192 || a.norm_w) return cudaErrorInvalidValue;  // x stays within the 48 KB default smem

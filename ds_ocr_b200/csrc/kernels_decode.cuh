@@ -50,7 +50,7 @@ struct RouterFold {
     const float *g;        // post-attention norm weight [rows]
     float eps;
     int E, top_k, renorm;
-    float *part;           // [gridDim.x x (E + 1)]
+    float *part;           // [(E + 1) x rf_pstride(gridDim.x)]: column e's terms contiguous
     unsigned *ticket;      // zero between launches
     float *scores;         // [E] (for inspection)
     int *d_idx;

@@ -309,6 +309,34 @@ __device__ __forceinline__ void router_select_generic(const float *scores, int E
     }
 }
 
+// The router terms of the O-projection CTAs are stored per logit, each
+// logit's terms contiguous and padded to a multiple of 4 (float4 loads), and
+// summed in three runs of consecutive CTAs that start at multiples of 4 (each
+// run in CTA order, then (r0 + r1) + r2).
+__host__ __device__ __forceinline__ int rf_pstride(int nparts) { return (nparts + 3) & ~3; }
+__host__ __device__ __forceinline__ int rf_run(int nparts, int k) {
+    const int r = 4 * ((nparts + 11) / 12);
+    return r * k < nparts ? r * k : nparts;
+}
+// The sum of run `part` of logit column `col` (terms contiguous), every load
+// in flight together (a run holds at most 32 terms).
+__device__ __forceinline__ float rf_run_sum(const float *col, int nparts, int part) {
+    const int b0 = rf_run(nparts, part), b1 = rf_run(nparts, part + 1);
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+        v[u] = b0 + 4 * u < b1 ? __ldcg(reinterpret_cast<const float4 *>(col + b0 + 4 * u)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+        const float t[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (b0 + 4 * u + k < b1) acc = __fadd_rn(acc, t[k]);
+    }
+    return acc;
+}
+
 __device__ __forceinline__ void router_select(const float *scores, int E, int top_k, int renorm, int *d_idx, float *d_wt) {
     if (E > 64) {
         router_select_generic(scores, E, top_k, renorm, d_idx, d_wt);

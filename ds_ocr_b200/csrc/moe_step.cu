@@ -227,21 +227,11 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
     tr.waited();
 
     // 1. router logits: column e of the O-proj CTAs' terms summed in three
-    //    runs of consecutive CTAs, each in CTA order, then (r0 + r1) + r2
-    //    (router_fold's last CTA sums the same way), every run's loads in
-    //    flight together; the residual stream into xs
+    //    runs of consecutive CTAs (rf_run_sum, as router_fold's last CTA
+    //    sums them); the residual stream into xs
     if (tid < 3 * (E + 1)) {
         const int e = tid / 3, part = tid - 3 * e;
-        const int b0 = a.nparts * part / 3, b1 = a.nparts * (part + 1) / 3;
-        const float *col = a.rpart + e;
-        float v[MS_MAXPART];
-#pragma unroll
-        for (int u = 0; u < MS_MAXPART; u++) v[u] = b0 + u < b1 ? __ldcg(col + (size_t)(b0 + u) * (E + 1)) : 0.f;
-        float acc = 0.f;
-#pragma unroll
-        for (int u = 0; u < MS_MAXPART; u++)
-            if (b0 + u < b1) acc = __fadd_rn(acc, v[u]);
-        lsum[e][part] = acc;
+        lsum[e][part] = rf_run_sum(a.rpart + (size_t)e * rf_pstride(a.nparts), a.nparts, part);
     }
     for (int i = tid * 4; i < H; i += MS_THREADS * 4)
         *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));

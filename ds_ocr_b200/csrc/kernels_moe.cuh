@@ -301,12 +301,12 @@ __device__ __forceinline__ void router_select_generic(const float *scores, int E
         ik[k] = bidx;
         wsum = __fadd_rn(wsum, bv);
     }
-    if (lane == 0) {
-        for (int k = 0; k < top_k; k++) {
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+        if (k < top_k && lane == k) {
             d_idx[k] = ik[k];
             d_wt[k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
         }
-    }
 }
 
 // The router terms of the O-projection CTAs are stored per logit, each
@@ -367,7 +367,10 @@ __device__ __forceinline__ void router_select(const float *scores, int E, int to
     float wsum = 0.f;
     float wk[8];
     int ik[8];
-    for (int k = 0; k < top_k; k++) {
+    // (both loops unrolled to the bound 8 so wk and ik stay in registers)
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        if (k >= top_k) break;
         uint32_t key = 0u, idx = 0xffffffffu;
         if (!t0) {
             key = __float_as_uint(p0) + 1u;
@@ -386,12 +389,12 @@ __device__ __forceinline__ void router_select(const float *scores, int E, int to
         ik[k] = (int)win;
         wsum = __fadd_rn(wsum, bv);
     }
-    if (lane == 0) {
-        for (int k = 0; k < top_k; k++) {
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+        if (k < top_k && lane == k) {
             d_idx[k] = ik[k];
             d_wt[k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
         }
-    }
 }
 
 }  // namespace ds

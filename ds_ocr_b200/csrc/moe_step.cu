@@ -223,7 +223,6 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
         return;
     }
     pdl_wait();
-    pdl_launch();
     tr.waited();
 
     // 1. router logits: column e of the O-proj CTAs' terms summed in three
@@ -233,8 +232,20 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
         const int e = tid / 3, part = tid - 3 * e;
         lsum[e][part] = rf_run_sum(a.rpart + (size_t)e * rf_pstride(a.nparts), a.nparts, part);
     }
-    for (int i = tid * 4; i < H; i += MS_THREADS * 4)
-        *reinterpret_cast<float4 *>(xs + i) = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
+    {
+        // both of a thread's x loads in flight together (H <= 8 * MS_THREADS)
+        float4 xv[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int i = (tid + u * MS_THREADS) * 4;
+            if (i < H) xv[u] = __ldcg(reinterpret_cast<const float4 *>(a.x + i));
+        }
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int i = (tid + u * MS_THREADS) * 4;
+            if (i < H) *reinterpret_cast<float4 *>(xs + i) = xv[u];
+        }
+    }
     ms_cbar();
     tr.mark(0);
     // 2. the sum of squares of x (block_rms_inv's order over 8 warps), then
@@ -315,6 +326,9 @@ __global__ void __launch_bounds__(MS_THREADS + 32, 1) moe_step_kernel(MoeStepArg
             for (int k = L.q0 / I; k < K && k * I < L.q1; k++) atomicAdd(a.done + k, 1ull);
     }
     tr.mark(4);
+    // the next kernel may launch now: its prologue loads no longer compete
+    // with this kernel's routing and gate/up streams
+    pdl_launch();
     prefetch_next(a.pf, a.pf_bytes);
     // 6. down dot products: warp s owns slot s (s < K: routed expert s;
     //    K, K + 1: the two halves of the shared expert's rows). It waits
@@ -611,7 +625,7 @@ cudaError_t launch_dense_step(DenseStepArgs a, int grid, cudaStream_t st, bool p
 }
 
 bool moe_step_supported(int H, int I, int S, int E, int K, int sms) {
-    if (H != 1280 || I % 8 || S % 16 || I > 8 * 32 * MS_DCPL || S / 2 > 8 * 32 * MS_DCPL) return false;
+    if (H != 1280 || H > 8 * MS_THREADS || I % 8 || S % 16 || I > 8 * 32 * MS_DCPL || S / 2 > 8 * 32 * MS_DCPL) return false;
     if (K != MS_NSLOT - 2 || E > MS_MAXE || E < K || sms < 1 || (H + 15) / 16 > 3 * MS_MAXPART) return false;
     if (2 * S != 2 * I * (S / I) || S / 2 != I) return false;  // the shared row splits into two expert-width halves
     if ((H + sms - 1) / sms > MS_MAXROWS) return false;

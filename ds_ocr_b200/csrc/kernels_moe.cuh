@@ -359,42 +359,43 @@ __device__ __forceinline__ void router_select(const float *scores, int E, int to
     const float inv = __fdiv_rn(1.0f, warp_sum(part));
     p0 = __fmul_rn(p0, inv);
     p1 = __fmul_rn(p1, inv);
-    // top_k selection passes with the reference's strict '>' scan in
-    // ascending expert order (ds_moe_decoder.c:167-183): the largest
-    // probability, the lowest index among equals. Probabilities are >= 0,
-    // so their bit patterns order like the values; key 0 = no candidate.
-    bool t0 = !v0, t1 = !v1;
-    float wsum = 0.f;
-    float wk[8];
-    int ik[8];
-    // (both loops unrolled to the bound 8 so wk and ik stay in registers)
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        if (k >= top_k) break;
-        uint32_t key = 0u, idx = 0xffffffffu;
-        if (!t0) {
-            key = __float_as_uint(p0) + 1u;
-            idx = (uint32_t)e0;
-        }
-        if (!t1 && __float_as_uint(p1) + 1u > key) {
-            key = __float_as_uint(p1) + 1u;
-            idx = (uint32_t)e1;
-        }
-        const uint32_t kmax = __reduce_max_sync(DS_FULL, key);
-        const uint32_t win = __reduce_min_sync(DS_FULL, key == kmax ? idx : 0xffffffffu);
-        if (win == (uint32_t)e0) t0 = true;
-        if (win == (uint32_t)e1) t1 = true;
-        const float bv = __uint_as_float(kmax - 1u);
-        wk[k] = bv;
-        ik[k] = (int)win;
-        wsum = __fadd_rn(wsum, bv);
+    // top_k selection as the reference's strict '>' scan in ascending
+    // expert order picks (ds_moe_decoder.c:167-183): the largest probability
+    // first, the lowest index among equals. Expert e's position is its rank:
+    // the experts with a larger probability, plus those with an equal one and
+    // a lower index. Each lane counts the rank of its two experts against all
+    // of them (shared memory broadcasts; -1 marks a missing expert, below
+    // every probability), and the first top_k write their slot.
+    __shared__ float pp[64];
+    __shared__ float tw[8];
+    __shared__ int ti[8];
+    pp[e0] = v0 ? p0 : -1.0f;
+    pp[e1] = v1 ? p1 : -1.0f;
+    __syncwarp();
+    int r0 = 0, r1 = 0;
+#pragma unroll 16
+    for (int f = 0; f < 64; f++) {
+        const float q = pp[f];
+        r0 += (q > p0 || (q == p0 && f < e0)) ? 1 : 0;
+        r1 += (q > p1 || (q == p1 && f < e1)) ? 1 : 0;
     }
-#pragma unroll
-    for (int k = 0; k < 8; k++)
-        if (k < top_k && lane == k) {
-            d_idx[k] = ik[k];
-            d_wt[k] = renorm ? __fdiv_rn(wk[k], wsum) : wk[k];
-        }
+    if (v0 && r0 < top_k) {
+        tw[r0] = p0;
+        ti[r0] = e0;
+    }
+    if (v1 && r1 < top_k) {
+        tw[r1] = p1;
+        ti[r1] = e1;
+    }
+    __syncwarp();
+    // the selected weights' sum in selection order (for renormalisation)
+    float wsum = 0.f;
+    for (int k = 0; k < top_k; k++) wsum = __fadd_rn(wsum, tw[k]);
+    if (lane < top_k) {
+        d_idx[lane] = ti[lane];
+        d_wt[lane] = renorm ? __fdiv_rn(tw[lane], wsum) : tw[lane];
+    }
+    __syncwarp();
 }
 
 }  // namespace ds

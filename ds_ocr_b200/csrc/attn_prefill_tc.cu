@@ -61,6 +61,9 @@ constexpr uint32_t PT_TQ = 256;             // Q hi: 64 columns of BF16 pairs; Q
 constexpr uint32_t PT_TW = 384;             // two W buffers of 64: hi (32 columns of pairs), lo (32)
 constexpr uint32_t PT_TCOLS = 512;
 
+// Optional per-block timestamps of the longest CTA (head 0, last query
+// block), compiled in with -DPT_TRACE: the issuing threads' and a row
+// thread's progress through each key block, read back from pt_trace.
 #ifdef PT_TRACE
 __device__ unsigned long long pt_trace[12][64];
 #define PT_MARK(k, b) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (b) < 64) pt_trace[k][b] = ds_gtime(); } while (0)

@@ -12,6 +12,7 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#include <omp.h>
 
 /* ds_kernels.h:296-302 — Schraudolph (1999) exp; the reference's compiler
  * fuses 12102203*x + 1064866805 into one FMA (verified against the compiled
@@ -168,30 +169,21 @@ int orc_int8_quantize(const uint16_t *W, int out_dim, int in_dim,
     return 0;
 }
 
-/* int8_matvec_generic (ds_quantize.c:154-169), the x86 path:
- * y[r] = scale[r] * sum_c (q+128) x[c] + off[r] * sum_c x[c], both sums
- * sequential. The reference builds with -O3 -march=native and gcc's default
- * contraction (its Makefile, as oracle/Makefile does), so what it computes
- * depends on the host: where the target has FMA, gcc fuses the inner
- * product-add into one FMA per element and the tail into
- * fma(scale, dot, off * x_sum). This restatement, built with contraction
- * off, spells out the same operations (fused dot under __FMA__, else the
- * plain product-add), so the two agree bit for bit on the machine both are
- * built on. */
+/* int8_matvec_generic (ds_quantize.c:154-169): the rows are split over
+ * OpenMP threads; each row's dot and x-sum come from orc_int8_rows
+ * (int8_dot.c), compiled with the reference build's flags so its FMA
+ * contraction matches the reference's on the build host. */
+void orc_int8_rows(float *y, const float *x, const int8_t *q, const float *scale,
+                   const float *off, int row0, int row1, int in_dim);
+
 void orc_int8_matvec(float *y, const float *x, const int8_t *q, const float *scale,
                      const float *off, int out_dim, int in_dim) {
-    float xs = 0.0f;
-    for (int c = 0; c < in_dim; c++) xs += x[c];
-#pragma omp parallel for schedule(static)
-    for (int r = 0; r < out_dim; r++) {
-        const int8_t *row = q + (size_t)r * in_dim;
-        float d = 0.0f;
-#ifdef __FMA__
-        for (int c = 0; c < in_dim; c++) d = fmaf((float)((int)row[c] + 128), x[c], d);
-#else
-        for (int c = 0; c < in_dim; c++) d += (float)((int)row[c] + 128) * x[c];
-#endif
-        y[r] = fmaf(scale[r], d, off[r] * xs);
+#pragma omp parallel
+    {
+        int nt = omp_get_num_threads(), t = omp_get_thread_num();
+        int per = (out_dim + nt - 1) / nt;
+        int r0 = t * per, r1 = r0 + per < out_dim ? r0 + per : out_dim;
+        if (r0 < r1) orc_int8_rows(y, x, q, scale, off, r0, r1, in_dim);
     }
 }
 

@@ -78,6 +78,11 @@ SIGNATURES = {
     "ds_cuda_batch_decoder_forward": (c_int, [P, c_int, P, P, P]),
     "ds_cuda_batch_decoder_generate": (c_int, [P, c_int, P, c_int, P]),
     "ds_cuda_batch_decoder_generate_dev": (c_int, [P, c_int, c_int, P]),
+    "ds_cuda_batch_decoder_set_sampling": (c_int, [P, c_int, ctypes.c_float, c_int, ctypes.c_float]),
+    "ds_cuda_batch_decoder_set_history": (c_int, [P, c_int, c_int, P, c_int]),
+    "ds_cuda_batch_decoder_get_history": (c_int, [P, c_int, c_int, P, c_int]),
+    "ds_cuda_batch_decoder_set_uniforms": (c_int, [P, c_int, P, c_int]),
+    "ds_cuda_batch_decoder_set_window": (c_int, [P, c_int, c_int, P]),
     "ds_cuda_prefill_moe": (c_int, [P, P, P, P, c_int, P, P, P]),
     "ds_cuda_prefill_moe_dev": (c_int, [P, P, P, P, c_int, P, P, P, P]),
     "ds_cuda_prefill_check": (c_int, [P]),

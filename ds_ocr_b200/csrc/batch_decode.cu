@@ -14,6 +14,7 @@
 // the tensor-core batched argmax (csrc/lmhead_tc.cu). Activations enter each
 // GEMM as two BF16 planes (hi, lo), so the products are F32-class.
 #include <cmath>
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(256) bd_plan_kernel(int *counts, int E, int S,
 // Next step's input: the embedding row (tied LM head) of each stream's
 // token; the token is logged at the stream's position, which advances.
 __global__ void bd_advance_kernel(const uint16_t *E, int H, const int *tok, int V, int *pos, int *tok_log,
-                                  int kv_max, float *x) {
+                                  int kv_max, float *x, int *hist, int *hist_len, int hist_cap) {
     const int s = blockIdx.x;
     int t = tok[s];
     if (t < 0 || t >= V) t = 0;  // no winner (all-NaN logits): embed row 0
@@ -149,6 +150,13 @@ __global__ void bd_advance_kernel(const uint16_t *E, int H, const int *tok, int 
         const int p = pos[s];
         if (p < kv_max) tok_log[(size_t)s * kv_max + p] = t;
         pos[s] = p + 1;
+        // the stream's generated-token history takes the selected token
+        // (-1 when no logit won), as the batch-1 advance does
+        const int n = hist_len[s];
+        if (n < hist_cap) {
+            hist[(size_t)s * hist_cap + n] = tok[s];
+            hist_len[s] = n + 1;
+        }
     }
 }
 
@@ -191,6 +199,19 @@ struct BatchModel {
     uint16_t *kv = nullptr;
     float *cos_t = nullptr, *sin_t = nullptr;
     unsigned *err = nullptr;
+    // LM-head selection settings (select.cu), shared by the streams; each
+    // stream keeps its own history, uniforms and selection scratch
+    float rp = 1.f, temperature = 0.f;
+    int ngram = 0;
+    int hist_cap = 0;
+    int *hist = nullptr, *hist_len = nullptr, *sel_full = nullptr, *unif_pos = nullptr;
+    float *hval = nullptr, *bval = nullptr, *sel_logits = nullptr, *unif = nullptr;
+    int unif_n = 0;     // uniforms supplied per stream
+    int unif_used = 0;  // sampled steps launched since the uniforms were set
+    // V3's reference sliding window (0: off) and each stream's prefill length
+    int swa_window = 0;
+    int *swa_refs = nullptr;
+    bool sampling() const { return rp > 1.f || ngram > 0 || temperature > 0.f; }
     std::vector<int> host_lo;   // per layer and stream
     std::vector<int> host_pos;  // per stream: the position the next token is written at
     cudaGraphExec_t graph = nullptr;
@@ -272,6 +293,8 @@ static int enqueue_step(ds_cuda_ctx *c, BatchModel *m, cudaStream_t st) {
         aa.kv_stream_stride = m->stream_stride();
         aa.q_stride = QD;
         aa.lo_starts = m->lo_starts + (size_t)l * S;
+        aa.swa_window = m->swa_window;
+        aa.swa_refs = m->swa_refs;
         BKL(launch_attn_decode(aa, st, false, S), "bd attention");
         BKL(sk_split_launch(m->att, S, QD, QD, nullptr, 0.f, m->p1, 64, nullptr, st, nullptr, 0, 0, nullptr, nullptr),
             "bd split attn");
@@ -305,8 +328,36 @@ static int enqueue_step(ds_cuda_ctx *c, BatchModel *m, cudaStream_t st) {
         "bd final norm");
     int rc = lmhead_tc_enqueue(c, m->xfinal, m->lm_head, H, g.vocab, S, m->tok, m->val, st);
     if (rc < 0) return rc;
+    if (m->sampling()) {
+        // the reference's selection rules per stream on the argmax winner
+        // (ds_moe_decoder.c:1021-1263); the full-logits path runs for the
+        // streams that need it
+        SelectArgs sa = {};
+        sa.W = m->lm_head;
+        sa.x = m->xfinal;
+        sa.H = H;
+        sa.V = g.vocab;
+        sa.hist = m->hist;
+        sa.hist_len = m->hist_len;
+        sa.cap = m->hist_cap;
+        sa.hval = m->hval;
+        sa.bval = m->bval;
+        sa.logits = m->sel_logits;
+        sa.tok = m->tok;
+        sa.val = m->val;
+        sa.full = m->sel_full;
+        sa.rp = m->rp;
+        sa.ngram = m->ngram;
+        sa.temperature = m->temperature;
+        sa.unif = m->unif;
+        sa.unif_pos = m->unif_pos;
+        sa.n_streams = S;
+        sa.x_ld = H;
+        sa.unif_ld = m->hist_cap;
+        BKL(launch_select(sa, st), "bd token selection");
+    }
     bd_advance_kernel<<<S, 256, 0, st>>>(m->lm_head, H, m->tok, g.vocab, m->pos, m->tok_log, g.kv_max,
-                                         m->layers[0].x_in);
+                                         m->layers[0].x_in, m->hist, m->hist_len, m->hist_cap);
     BKL(cudaGetLastError(), "bd advance");
     return DS_CUDA_OK;
 }
@@ -334,6 +385,18 @@ extern "C" int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *c, const ds_cuda_deco
     do {                                                  \
         if (rc == DS_CUDA_OK) rc = bm_alloc(c, m, &(p), (n)); \
     } while (0)
+    // selection state: history and uniforms hold kv_max + 512 entries per
+    // stream (as the batch-1 decoder's); logits for the full path
+    m->hist_cap = g.kv_max + 512;
+    BA(m->hist, (size_t)S * m->hist_cap);
+    BA(m->hval, (size_t)S * m->hist_cap);
+    BA(m->unif, (size_t)S * m->hist_cap);
+    BA(m->hist_len, (size_t)S);
+    BA(m->unif_pos, (size_t)S);
+    BA(m->sel_full, (size_t)S);
+    BA(m->bval, (size_t)S);
+    BA(m->swa_refs, (size_t)S);
+    BA(m->sel_logits, (size_t)S * g.vocab);
     BA(m->xa, (size_t)S * H);
     BA(m->xb, (size_t)S * H);
     BA(m->qkv, (size_t)S * 3 * QD);
@@ -664,6 +727,106 @@ static int bm_check(ds_cuda_ctx *c, BatchModel *m) {
     return DS_CUDA_OK;
 }
 
+// Temperature sampling takes one uniform per stream per step.
+static int bm_uniforms(ds_cuda_ctx *c, BatchModel *m, int n) {
+    if (m->temperature <= 0.f) return DS_CUDA_OK;
+    if (m->unif_used + n > m->unif_n)
+        return ctx_fail(c, DS_CUDA_ESTATE, "batch decoder: %d uniforms left for %d temperature-sampled steps",
+                        m->unif_n - m->unif_used, n);
+    return DS_CUDA_OK;
+}
+static void bm_used(BatchModel *m, int n) {
+    if (m->temperature > 0.f) m->unif_used += n;
+}
+
+// The step graph bakes in the settings: drop it when they change.
+static void bm_drop_graph(ds_cuda_ctx *c, BatchModel *m) {
+    cudaStreamSynchronize(c->stream);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+}
+
+extern "C" int ds_cuda_batch_decoder_set_sampling(ds_cuda_ctx_t *c, int id, float repeat_penalty,
+                                                  int no_repeat_ngram_size, float temperature) {
+    BatchModel *m = bm_get(c, id);
+    if (!c || !m || !(repeat_penalty > 0.f) || no_repeat_ngram_size < 0 || !(temperature >= 0.f))
+        return ctx_fail(c, DS_CUDA_EINVAL, "batch_decoder_set_sampling: bad argument");
+    const bool on = repeat_penalty > 1.f || no_repeat_ngram_size > 0 || temperature > 0.f;
+    if (on && m->cfg.hidden % 256)
+        return ctx_fail(c, DS_CUDA_EINVAL, "batch_decoder_set_sampling: hidden must be a multiple of 256");
+    cudaSetDevice(c->device);
+    bm_drop_graph(c, m);
+    m->rp = repeat_penalty;
+    m->ngram = no_repeat_ngram_size;
+    m->temperature = temperature;
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_batch_decoder_set_history(ds_cuda_ctx_t *c, int id, int stream, const int *tokens, int n) {
+    BatchModel *m = bm_get(c, id);
+    if (!c || !m || stream < 0 || stream >= m->S || n < 0 || n > m->hist_cap || (n > 0 && !tokens))
+        return ctx_fail(c, DS_CUDA_EINVAL, "batch_decoder_set_history: bad argument");
+    cudaSetDevice(c->device);
+    BKL(cudaStreamSynchronize(c->stream), "batch set history");
+    if (n)
+        BKL(cudaMemcpy(m->hist + (size_t)stream * m->hist_cap, tokens, (size_t)n * 4, cudaMemcpyHostToDevice),
+            "batch history copy");
+    BKL(cudaMemcpy(m->hist_len + stream, &n, 4, cudaMemcpyHostToDevice), "batch history length");
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_batch_decoder_get_history(ds_cuda_ctx_t *c, int id, int stream, int *tokens, int cap) {
+    BatchModel *m = bm_get(c, id);
+    if (!c || !m || stream < 0 || stream >= m->S || cap < 0 || (cap > 0 && !tokens))
+        return ctx_fail(c, DS_CUDA_EINVAL, "batch_decoder_get_history: bad argument");
+    cudaSetDevice(c->device);
+    BKL(cudaStreamSynchronize(c->stream), "batch get history");
+    int n = 0;
+    BKL(cudaMemcpy(&n, m->hist_len + stream, 4, cudaMemcpyDeviceToHost), "batch history length");
+    const int k = std::min(n, cap);
+    if (k > 0)
+        BKL(cudaMemcpy(tokens, m->hist + (size_t)stream * m->hist_cap, (size_t)k * 4, cudaMemcpyDeviceToHost),
+            "batch history copy");
+    return n;
+}
+
+// Uniforms for temperature sampling: u is [S x n], row s the uniforms
+// stream s consumes in order, one per sampled step. Every stream restarts
+// from its first uniform.
+extern "C" int ds_cuda_batch_decoder_set_uniforms(ds_cuda_ctx_t *c, int id, const float *u, int n) {
+    BatchModel *m = bm_get(c, id);
+    if (!c || !m || n < 0 || n > m->hist_cap || (n > 0 && !u))
+        return ctx_fail(c, DS_CUDA_EINVAL, "batch_decoder_set_uniforms: bad argument (at most %d per stream)",
+                        m ? m->hist_cap : 0);
+    cudaSetDevice(c->device);
+    BKL(cudaStreamSynchronize(c->stream), "batch set uniforms");
+    if (n)
+        BKL(cudaMemcpy2D(m->unif, (size_t)m->hist_cap * 4, u, (size_t)n * 4, (size_t)n * 4, m->S,
+                         cudaMemcpyHostToDevice),
+            "batch uniform copy");
+    BKL(cudaMemset(m->unif_pos, 0, (size_t)m->S * 4), "batch uniform positions");
+    m->unif_n = n;
+    m->unif_used = 0;
+    return DS_CUDA_OK;
+}
+
+extern "C" int ds_cuda_batch_decoder_set_window(ds_cuda_ctx_t *c, int id, int sliding_window_size,
+                                                const int *prefill_token_counts) {
+    BatchModel *m = bm_get(c, id);
+    if (!c || !m || sliding_window_size < 0 || (sliding_window_size > 0 && !prefill_token_counts))
+        return ctx_fail(c, DS_CUDA_EINVAL, "batch_decoder_set_window: bad argument");
+    std::vector<int> refs(m->S, 0);
+    for (int s = 0; s < m->S && sliding_window_size > 0; s++) {
+        refs[s] = prefill_token_counts[s];
+        if (refs[s] < 0) return ctx_fail(c, DS_CUDA_EINVAL, "batch_decoder_set_window: negative prefill count");
+    }
+    cudaSetDevice(c->device);
+    bm_drop_graph(c, m);
+    BKL(cudaMemcpy(m->swa_refs, refs.data(), (size_t)m->S * 4, cudaMemcpyHostToDevice), "batch window");
+    m->swa_window = sliding_window_size;
+    return DS_CUDA_OK;
+}
+
 // One step for all streams: embeds [S x H] (NULL: the embeddings of the
 // previous tokens); tokens [S] out; final_x [S x H] optional.
 extern "C" int ds_cuda_batch_decoder_forward(ds_cuda_ctx_t *c, int id, const float *embeds, int *tokens,
@@ -674,12 +837,14 @@ extern "C" int ds_cuda_batch_decoder_forward(ds_cuda_ctx_t *c, int id, const flo
     cudaStream_t st = c->stream;
     const size_t SH = (size_t)m->S * m->cfg.hidden;
     BK(bm_room(c, m, 1));
+    BK(bm_uniforms(c, m, 1));
     if (embeds) BKL(cudaMemcpyAsync(m->layers[0].x_in, embeds, SH * 4, cudaMemcpyHostToDevice, st), "embeds");
     BK(enqueue_step(c, m, st));
     BKL(cudaMemcpyAsync(tokens, m->tok, (size_t)m->S * 4, cudaMemcpyDeviceToHost, st), "tokens");
     if (final_x) BKL(cudaMemcpyAsync(final_x, m->xfinal, SH * 4, cudaMemcpyDeviceToHost, st), "final x");
     BKL(cudaStreamSynchronize(st), "batch forward");
     bm_advance(m, 1);
+    bm_used(m, 1);
     return bm_check(c, m);
 }
 
@@ -692,7 +857,9 @@ extern "C" int ds_cuda_batch_decoder_generate_dev(ds_cuda_ctx_t *c, int id, int 
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     if (n_steps == 0) return DS_CUDA_OK;
     BK(bm_room(c, m, n_steps));
+    BK(bm_uniforms(c, m, n_steps));
     bm_advance(m, n_steps);
+    bm_used(m, n_steps);
     if (!m->graph) {
         // the first step runs uncaptured (scratch allocation), then capture
         BK(enqueue_step(c, m, st));

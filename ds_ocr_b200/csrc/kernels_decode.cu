@@ -232,9 +232,9 @@ __device__ __forceinline__ void attn_body(const AttnArgs &a) {
     // query is at or past the prefill length P, the keys are rows [0, P)
     // then [max(P, n - W), n); key j (0 .. n-1 below) is row j < P ? j : j + gap
     int gap = 0;
-    if (SWA && a.swa_window > 0 && n_all - 1 >= a.swa_ref) gap = max(0, n_all - a.swa_window - a.swa_ref);
+    const int swa_ref = SWA && a.swa_refs ? a.swa_refs[sidx] : a.swa_ref;
+    if (SWA && a.swa_window > 0 && n_all - 1 >= swa_ref) gap = max(0, n_all - a.swa_window - swa_ref);
     const int n = n_all - gap;
-    const int swa_ref = a.swa_ref;
     auto row = [&](int j) { return SWA ? (j < swa_ref ? j : j + gap) : j; };
     const int lo_start = a.lo_starts ? a.lo_starts[sidx] : a.lo_start;
     const int per = (n + CL - 1) / CL;
@@ -670,10 +670,15 @@ cudaError_t launch_qkv_rope(const QkvArgs &a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_attn_decode(const AttnArgs &a, cudaStream_t st, bool pdl, int n_streams) {
-    if (a.kv_max > ATT_MAXK || (n_streams > 1 && a.swa_window > 0)) return cudaErrorInvalidValue;
+    if (a.kv_max > ATT_MAXK) return cudaErrorInvalidValue;
     AttnArgs aa = a;
     void *args[] = {&aa};
-    // cluster dims are compiled into the kernel (__cluster_dims__)
+    // cluster dims are compiled into the kernel (__cluster_dims__); with the
+    // sliding window, several streams run the batch-1 kernel with grid.y =
+    // stream (each stream its own prefill length in swa_refs)
+    if (n_streams > 1 && a.swa_window > 0)
+        return launch_ex((const void *)attn_decode_kernel<true>, dim3(a.n_heads * ATT_CL, n_streams), 256, 0, st,
+                         pdl, args);
     if (n_streams == 1)
         return launch_ex(a.swa_window > 0 ? (const void *)attn_decode_kernel<true> : (const void *)attn_decode_kernel<false>,
                          a.n_heads * ATT_CL, 256, 0, st, pdl, args);

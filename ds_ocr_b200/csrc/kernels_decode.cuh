@@ -38,6 +38,7 @@ struct AttnArgs {
     // V3 reference sliding-window attention (0: off): window W, prefill
     // length P
     int swa_window, swa_ref;
+    const int *swa_refs;  // per stream P (several streams; null: swa_ref)
 };
 
 // Router folded into the O-projection (optional): logits_e =
@@ -115,6 +116,12 @@ struct SelectArgs {
     float temperature;   // > 0: sampling
     const float *unif;   // caller-supplied uniforms, one per sampling step
     int *unif_pos;
+    // several independent streams (grid.y = stream; 0 or 1: one stream).
+    // Stream s reads x + s * x_ld, hist + s * cap, unif + s * unif_ld,
+    // logits + s * V, hval + s * cap and entry s of hist_len, bval, tok,
+    // val, full and unif_pos.
+    int n_streams;
+    int x_ld, unif_ld;
 };
 cudaError_t launch_select(const SelectArgs &a, cudaStream_t st);
 

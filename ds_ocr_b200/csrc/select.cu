@@ -50,10 +50,31 @@ __device__ __forceinline__ float sel_row_dot(const uint16_t *W, const float *x, 
     return warp_sum(s);
 }
 
+// The arguments of stream blockIdx.y (the same pointers for one stream).
+__device__ __forceinline__ SelectArgs sel_stream(const SelectArgs &a0) {
+    SelectArgs a = a0;
+    const int s = blockIdx.y;
+    if (s) {
+        a.x += (size_t)s * a.x_ld;
+        a.hist += (size_t)s * a.cap;
+        a.hist_len += s;
+        a.hval += (size_t)s * a.cap;
+        a.bval += s;
+        a.logits += (size_t)s * a.V;
+        a.tok += s;
+        a.val += s;
+        a.full += s;
+        if (a.unif) a.unif += (size_t)s * a.unif_ld;
+        if (a.unif_pos) a.unif_pos += s;
+    }
+    return a;
+}
+
 // Warp i < len: hval[i] = W[hist[i]] . x (0 for an out-of-range token);
 // warp i == cap: bval = W[*tok] . x (the argmax winner's value recomputed,
 // as the reference does with ds_bf16_dot_row).
-__global__ void __launch_bounds__(256) select_dots_kernel(SelectArgs a) {
+__global__ void __launch_bounds__(256) select_dots_kernel(SelectArgs a0) {
+    const SelectArgs a = sel_stream(a0);
     const int lane = threadIdx.x & 31;
     const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int len = *a.hist_len;
@@ -126,7 +147,8 @@ __device__ __forceinline__ bool sel_banned(const int *hist, int len, int ngram, 
     return __syncthreads_or(hit) != 0;
 }
 
-__global__ void __launch_bounds__(1024) select_fast_kernel(SelectArgs a) {
+__global__ void __launch_bounds__(1024) select_fast_kernel(SelectArgs a0) {
+    const SelectArgs a = sel_stream(a0);
     __shared__ float sv[32];
     __shared__ int si[32];
     if (a.temperature > 0.f) {  // temperature sampling always takes the full path
@@ -178,7 +200,50 @@ __global__ void __launch_bounds__(256) select_logits_kernel(SelectArgs a) {
     }
 }
 
-__global__ void __launch_bounds__(1024) select_full_kernel(SelectArgs a) {
+// Every logit of every stream whose full path runs, several streams at
+// once: one warp per LM-head row keeps the row in registers (each lane the
+// same 8-element chunks that sel_row_dot gives it, so each logit is the same
+// sum in the same order) and dots it with each flagged stream's x, so the
+// head streams from HBM once per step instead of once per stream.
+template <int CH>
+__global__ void __launch_bounds__(256) select_logits_streams_kernel(SelectArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int S = a.n_streams;
+    bool any = false;
+    for (int s = 0; s < S; s++) any = any || a.full[s];
+    if (!any) return;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < a.V; r += nw) {
+        const uint16_t *w = a.W + (size_t)r * a.H;
+        uint4 u[CH];
+#pragma unroll
+        for (int k = 0; k < CH; k++) u[k] = ldg_stream(w + lane * 8 + k * 256);
+        for (int s = 0; s < S; s++) {
+            if (!a.full[s]) continue;
+            const float *x = a.x + (size_t)s * a.x_ld;
+            float acc = 0.f;
+#pragma unroll
+            for (int k = 0; k < CH; k++) {
+                const int c = lane * 8 + k * 256;
+                const float4 x0 = *reinterpret_cast<const float4 *>(x + c);
+                const float4 x1 = *reinterpret_cast<const float4 *>(x + c + 4);
+                acc = __fmaf_rn(bf16_lo(u[k].x), x0.x, acc);
+                acc = __fmaf_rn(bf16_hi(u[k].x), x0.y, acc);
+                acc = __fmaf_rn(bf16_lo(u[k].y), x0.z, acc);
+                acc = __fmaf_rn(bf16_hi(u[k].y), x0.w, acc);
+                acc = __fmaf_rn(bf16_lo(u[k].z), x1.x, acc);
+                acc = __fmaf_rn(bf16_hi(u[k].z), x1.y, acc);
+                acc = __fmaf_rn(bf16_lo(u[k].w), x1.z, acc);
+                acc = __fmaf_rn(bf16_hi(u[k].w), x1.w, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) a.logits[(size_t)s * a.V + r] = acc;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(1024) select_full_kernel(SelectArgs a0) {
+    const SelectArgs a = sel_stream(a0);
     __shared__ float sv[32];
     __shared__ int si[32];
     __shared__ double sd[32];
@@ -298,21 +363,38 @@ static int sel_sms() {
 }
 
 cudaError_t launch_select(const SelectArgs &a, cudaStream_t st) {
-    if (a.H % 256 || a.cap <= 0 || !a.hist || !a.hist_len || !a.tok || !a.val || !a.full || !a.logits)
+    const int S = a.n_streams > 1 ? a.n_streams : 1;
+    if (a.H % 256 || a.H > 2048 || a.cap <= 0 || !a.hist || !a.hist_len || !a.tok || !a.val || !a.full ||
+        !a.logits || (S > 1 && a.x_ld < a.H))
         return cudaErrorInvalidValue;
     SelectArgs aa = a;
     void *args[] = {&aa};
     cudaError_t e = cudaSuccess;
     if (a.temperature <= 0.f && a.rp > 1.f) {  // the history dots feed the penalty only
         const int warps = a.cap + 1;
-        e = launch_ex((const void *)select_dots_kernel, (warps + 7) / 8, 256, 0, st, false, args);
+        e = launch_ex((const void *)select_dots_kernel, dim3((warps + 7) / 8, S), 256, 0, st, false, args);
         if (e != cudaSuccess) return e;
     }
-    e = launch_ex((const void *)select_fast_kernel, 1, 1024, 0, st, false, args);
+    e = launch_ex((const void *)select_fast_kernel, dim3(1, S), 1024, 0, st, false, args);
     if (e != cudaSuccess) return e;
-    e = launch_ex((const void *)select_logits_kernel, sel_sms() * 8, 256, 0, st, false, args);
+    if (S == 1) {
+        e = launch_ex((const void *)select_logits_kernel, sel_sms() * 8, 256, 0, st, false, args);
+    } else {
+        const void *k = nullptr;
+        switch (a.H / 256) {
+            case 1: k = (const void *)select_logits_streams_kernel<1>; break;
+            case 2: k = (const void *)select_logits_streams_kernel<2>; break;
+            case 3: k = (const void *)select_logits_streams_kernel<3>; break;
+            case 4: k = (const void *)select_logits_streams_kernel<4>; break;
+            case 5: k = (const void *)select_logits_streams_kernel<5>; break;
+            case 6: k = (const void *)select_logits_streams_kernel<6>; break;
+            case 7: k = (const void *)select_logits_streams_kernel<7>; break;
+            default: k = (const void *)select_logits_streams_kernel<8>; break;
+        }
+        e = launch_ex(k, sel_sms() * 8, 256, 0, st, false, args);
+    }
     if (e != cudaSuccess) return e;
-    return launch_ex((const void *)select_full_kernel, 1, 1024, 0, st, false, args);
+    return launch_ex((const void *)select_full_kernel, dim3(1, S), 1024, 0, st, false, args);
 }
 
 }  // namespace ds

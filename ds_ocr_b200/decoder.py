@@ -282,6 +282,45 @@ class BatchDecoder:
         self.ctx.check(self.lib.ds_cuda_batch_decoder_generate_dev(self.ctx.h, self.id, n_steps, stream),
                        "batch_generate_dev")
 
+    def set_sampling(self, repeat_penalty=1.0, no_repeat_ngram_size=0, temperature=0.0):
+        """The reference's repeat_penalty / no_repeat_ngram_size /
+        temperature (ds_moe_decoder.c:1021-1263) for every stream."""
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_set_sampling(self.ctx.h, self.id, repeat_penalty,
+                                                                   no_repeat_ngram_size, temperature),
+                       "batch_set_sampling")
+
+    def set_history(self, stream, tokens):
+        """Replace one stream's generated-token history."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_set_history(self.ctx.h, self.id, stream,
+                                                                  _a(t) if t.size else None, t.size),
+                       "batch_set_history")
+
+    def history(self, stream):
+        n = self.ctx.check(self.lib.ds_cuda_batch_decoder_get_history(self.ctx.h, self.id, stream, None, 0),
+                           "batch_get_history")
+        out = np.empty(n, np.int32)
+        if n:
+            self.ctx.check(self.lib.ds_cuda_batch_decoder_get_history(self.ctx.h, self.id, stream, _a(out), n),
+                           "batch_get_history")
+        return out
+
+    def set_uniforms(self, u):
+        """Uniforms for temperature sampling: [n_streams x n], row s for
+        stream s, one per sampled step."""
+        u = np.ascontiguousarray(u, np.float32)
+        assert u.ndim == 2 and u.shape[0] == self.S
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_set_uniforms(self.ctx.h, self.id, _a(u) if u.size else None,
+                                                                   u.shape[1]), "batch_set_uniforms")
+
+    def set_window(self, sliding_window_size, prefill_token_counts):
+        """V3's reference sliding-window attention (0 disables), with each
+        stream's prefill length."""
+        p = np.ascontiguousarray(prefill_token_counts, np.int32)
+        assert p.size == self.S
+        self.ctx.check(self.lib.ds_cuda_batch_decoder_set_window(self.ctx.h, self.id, sliding_window_size, _a(p)),
+                       "batch_set_window")
+
     def close(self):
         if self.id:
             self.lib.ds_cuda_batch_decoder_destroy(self.ctx.h, self.id)

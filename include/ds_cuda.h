@@ -373,6 +373,8 @@ const char *ds_cuda_safetensors_error(void);
  * the linear layers run on the tensor cores with the weights read once per
  * step for all streams. Same configuration and layer structs as the
  * single-stream decoder (BF16 experts; use_int8 and engine are ignored).
+ * Greedy with causal attention unless set_sampling / set_window say
+ * otherwise.
  * --------------------------------------------------------------------- */
 int ds_cuda_batch_decoder_create(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config_t *cfg,
                                  const ds_cuda_layer_weights_t *layers, const float *final_norm,
@@ -393,6 +395,30 @@ int ds_cuda_batch_decoder_generate(ds_cuda_ctx_t *ctx, int model, const float *f
 /* n_steps steps enqueued on `stream` from the device state (a CUDA graph
  * per step; no host copies). */
 int ds_cuda_batch_decoder_generate_dev(ds_cuda_ctx_t *ctx, int model, int n_steps, void *stream);
+/* LM-head selection settings for every stream, as
+ * ds_cuda_decoder_set_sampling (ds_moe_decoder.c:1021-1263, the reference's
+ * per-context repeat_penalty, no_repeat_ngram_size and temperature, applied
+ * here to each stream against its own history). Needs hidden % 256 == 0
+ * when any setting is on. */
+int ds_cuda_batch_decoder_set_sampling(ds_cuda_ctx_t *ctx, int model, float repeat_penalty,
+                                       int no_repeat_ngram_size, float temperature);
+/* One stream's generated-token history (the reference's per-context
+ * ctx->token_history, ds_ocr.h:433-435); every step appends each stream's
+ * token (ds_ocr.c:2245-2248). set replaces it (n <= kv_max + 512); get
+ * copies up to cap tokens and returns the length. */
+int ds_cuda_batch_decoder_set_history(ds_cuda_ctx_t *ctx, int model, int stream, const int *tokens, int n);
+int ds_cuda_batch_decoder_get_history(ds_cuda_ctx_t *ctx, int model, int stream, int *tokens, int cap);
+/* Uniforms for temperature sampling (the reference's (float)rand() /
+ * RAND_MAX, ds_moe_decoder.c:1251): u [n_streams x n], row s consumed by
+ * stream s in order, one per sampled step; every stream restarts at its
+ * first. Steps return DS_CUDA_ESTATE when too few are left. */
+int ds_cuda_batch_decoder_set_uniforms(ds_cuda_ctx_t *ctx, int model, const float *u, int n);
+/* V3's reference sliding-window decode attention (ds_moe_decoder.c:409-436)
+ * for every stream: window W (0 disables) and each stream's prefill length
+ * prefill_token_counts[n_streams] (the reference's per-context
+ * ctx->prefill_token_count, ds_ocr.h:438). */
+int ds_cuda_batch_decoder_set_window(ds_cuda_ctx_t *ctx, int model, int sliding_window_size,
+                                     const int *prefill_token_counts);
 
 /* ---------------------------------------------------------------------
  * Batched MoE prefill — the MoE block of ds_decoder_prefill for n tokens

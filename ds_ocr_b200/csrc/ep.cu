@@ -5,7 +5,8 @@
 // Ranks own contiguous expert blocks of experts_per_rank experts. A token is
 // sent once to every rank owning one of its top-k experts, in the order
 // (destination rank ascending, token ascending); with the row go the k expert
-// ids served there (-1 for the others). Expert outputs come back one row per
+// ids served there (-1 for the others) and, in the last meta slot, the
+// offset of the row's first pair within its destination's pairs. Expert outputs come back one row per
 // (token, k) pair in the order (rank ascending, token ascending, k
 // ascending); inv[s*K + k] is that pair's row in the returned stream, so the
 // combine reads them without a scatter.
@@ -79,6 +80,9 @@ __global__ void __launch_bounds__(EP_THREADS) ep_dispatch_plan_kernel(int n, int
                     if (mine) inv[s * K + k] = pair_base + pairs_g + p_ex + j++;
                 }
                 for (int k = K; k < EP_META; k++) meta[k] = -1;
+                // the row's first pair within its destination's section: the
+                // receiver places its pairs without a scan
+                meta[EP_META - 1] = pairs_g + p_ex;
             }
             rows_g += r_tot;
             pairs_g += p_tot;
@@ -118,42 +122,51 @@ struct EpCounts {
 
 // Compact (row, expert) pairs of R received payload rows, row-major; out[g]
 // = pairs whose row came from rank g (rows arrive grouped by source rank,
-// recv.c[g] rows each), out[G] = total.
-__global__ void __launch_bounds__(EP_THREADS) ep_pairs_kernel(int R, int K, int G, EpCounts recv,
-                                                              const uint16_t *__restrict__ payload, int H, int ld,
-                                                              int *pair_row, int *pair_expert, int *out) {
-    int base = 0;
-    __shared__ int per_src[8];
-    if (threadIdx.x < 8) per_src[threadIdx.x] = 0;
-    __syncthreads();
-    for (int c0 = 0; c0 < R; c0 += EP_THREADS) {
-        const int r = c0 + threadIdx.x;
-        int cnt = 0;
-        const int *meta = nullptr;
-        if (r < R) {
-            meta = reinterpret_cast<const int *>(payload + (size_t)r * ld + 2 * H);
-            for (int k = 0; k < K; k++) cnt += meta[k] >= 0;
+// recv.c[g] rows each), out[G] = total. One thread per row over many CTAs:
+// each row carries the offset of its first pair within its source's section
+// (meta slot EP_META - 1, written by the dispatch), and a section's pair
+// count is its last row's offset plus that row's pairs.
+__device__ __forceinline__ int ep_row_pairs(const int *meta, int K) {
+    int c = 0;
+    for (int k = 0; k < K; k++) c += meta[k] >= 0;
+    return c;
+}
+
+__global__ void __launch_bounds__(256) ep_pairs_kernel(int R, int K, int G, EpCounts recv,
+                                                       const uint16_t *__restrict__ payload, int H, int ld,
+                                                       int *pair_row, int *pair_expert, int *out) {
+    __shared__ int base[9];
+    if (threadIdx.x == 0) {
+        int b = 0, r_end = 0;
+        for (int g = 0; g < G; g++) {
+            base[g] = b;
+            r_end += recv.c[g];
+            if (recv.c[g] > 0) {
+                const int *m = reinterpret_cast<const int *>(payload + (size_t)(r_end - 1) * ld + 2 * H);
+                b += m[EP_META - 1] + ep_row_pairs(m, K);
+            }
         }
-        int ex;
-        const int tot = ep_scan(cnt, ex);
-        if (r < R) {
-            int j = base + ex;
-            for (int k = 0; k < K; k++)
-                if (meta[k] >= 0) {
-                    pair_row[j] = r;
-                    pair_expert[j] = meta[k];
-                    j++;
-                }
-            // source rank of row r
-            int g = 0, acc = recv.c[0];
-            while (g + 1 < G && r >= acc) acc += recv.c[++g];
-            if (cnt) atomicAdd(&per_src[g], cnt);
+        base[G] = b;
+        if (blockIdx.x == 0) {
+            for (int g = 0; g < G; g++) out[g] = base[g + 1] - base[g];
+            out[G] = b;
         }
-        base += tot;
     }
     __syncthreads();
-    if (threadIdx.x < G) out[threadIdx.x] = per_src[threadIdx.x];
-    if (threadIdx.x == 0) out[G] = base;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    int g = 0, acc = recv.c[0];
+    while (g + 1 < G && r >= acc) acc += recv.c[++g];
+    const int *meta = reinterpret_cast<const int *>(payload + (size_t)r * ld + 2 * H);
+    int j = base[g] + meta[EP_META - 1];
+    for (int k = 0; k < K; k++) {
+        const int e = meta[k];
+        if (e >= 0) {
+            pair_row[j] = r;
+            pair_expert[j] = e;
+            j++;
+        }
+    }
 }
 
 }  // namespace ds
@@ -164,7 +177,7 @@ extern "C" int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *c, int n_tokens, int top_k
                                        int experts_per_rank, const int *d_top_idx, const uint16_t *d_xn_hi,
                                        const uint16_t *d_xn_lo, int hidden, uint16_t *d_payload, int *d_send_tok,
                                        int *d_counts, int *d_inv, void *stream) {
-    if (!c || !c->ok || n_tokens < 0 || top_k <= 0 || top_k > EP_META || n_ranks <= 0 || n_ranks > 8 ||
+    if (!c || !c->ok || n_tokens < 0 || top_k <= 0 || top_k > EP_META - 1 || n_ranks <= 0 || n_ranks > 8 ||
         experts_per_rank <= 0 || hidden % 8 ||
         (n_tokens > 0 && (!d_top_idx || !d_xn_hi || !d_xn_lo || !d_payload || !d_send_tok || !d_inv)) || !d_counts)
         return DS_CUDA_EINVAL;
@@ -185,7 +198,7 @@ extern "C" int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *c, int n_tokens, int top_k
 extern "C" int ds_cuda_ep_pairs_dev(ds_cuda_ctx_t *c, int n_rows, int top_k, int n_ranks, const int *recv_counts,
                                     const uint16_t *d_payload, int hidden, int *d_pair_row, int *d_pair_expert,
                                     int *d_counts, void *stream) {
-    if (!c || !c->ok || n_rows < 0 || top_k <= 0 || top_k > EP_META || n_ranks <= 0 || n_ranks > 8 ||
+    if (!c || !c->ok || n_rows < 0 || top_k <= 0 || top_k > EP_META - 1 || n_ranks <= 0 || n_ranks > 8 ||
         !recv_counts || !d_counts || (n_rows > 0 && (!d_payload || !d_pair_row || !d_pair_expert)))
         return DS_CUDA_EINVAL;
     cudaSetDevice(c->device);
@@ -197,8 +210,8 @@ extern "C" int ds_cuda_ep_pairs_dev(ds_cuda_ctx_t *c, int n_rows, int top_k, int
         sum += recv_counts[g];
     }
     if (sum != n_rows) return ctx_fail(c, DS_CUDA_EINVAL, "ep_pairs: receive counts do not add up to n_rows");
-    ep_pairs_kernel<<<1, EP_THREADS, 0, st>>>(n_rows, top_k, n_ranks, rc, d_payload, hidden, 2 * hidden + 2 * EP_META,
-                                              d_pair_row, d_pair_expert, d_counts);
+    ep_pairs_kernel<<<n_rows > 0 ? (n_rows + 255) / 256 : 1, 256, 0, st>>>(
+        n_rows, top_k, n_ranks, rc, d_payload, hidden, 2 * hidden + 2 * EP_META, d_pair_row, d_pair_expert, d_counts);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? DS_CUDA_OK : ctx_cuda(c, e, "ep_pairs");
 }

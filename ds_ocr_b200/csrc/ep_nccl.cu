@@ -17,9 +17,11 @@
 //   return    the outputs travel back in request order (all-to-all);
 //   combine   x += sum_k w_k y_k in ascending expert order, plus shared: the
 //             single-GPU arithmetic, so results are bit-identical to it.
-// The counts are needed on the host to size the transfers, so the layer
-// synchronises the compute stream twice (after dispatch, after the pair
-// compaction).
+// The counts are needed on the host to size the transfers: each rank
+// announces to every peer the rows it sends and the pairs it asks of it, so
+// the layer synchronises the compute stream once (after dispatch). Each
+// rank's own rows and outputs are device-to-device copies; NCCL carries only
+// what crosses to another GPU.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2, or $DS_CUDA_NCCL_LIB),
 // so the library itself has no link-time dependency on it; only the entry
@@ -34,6 +36,10 @@
 #include <vector>
 
 #include "ctx.h"
+
+cudaError_t pf_combine_split_launch(float *x, int M, int H, int K, const int *idx, const float *wt, const float *y,
+                                    const int *yrow, const float *ys, const float *y_alt, long long alt_lo,
+                                    long long alt_hi, cudaStream_t st);
 
 namespace {
 
@@ -104,14 +110,14 @@ struct EpState {
     NcclComm comm = nullptr;
     int rank = 0, world = 1;
     cudaStream_t cs = nullptr;                 // payload all-to-all
-    cudaEvent_t ev_packed = nullptr, ev_recv = nullptr;
+    cudaEvent_t ev_packed = nullptr, ev_recv = nullptr, ev_counts = nullptr;
     struct Buf {
         void *p = nullptr;
         size_t cap = 0;
     };
-    Buf hi, lo, idx, w, payload, send_tok, counts, inv, cnt_recv, rpayload, pair_row, pair_expert, pcounts, y, ys,
-        yback;
-    int *h_counts = nullptr;                   // pinned: [2G] dispatch counts, [G] received rows, [G + 1] pairs
+    Buf hi, lo, idx, w, payload, send_tok, counts, inv, cnt_pack, cnt_recv, rpayload, pair_row, pair_expert, pcounts,
+        y, ys, yback;
+    int *h_counts = nullptr;                   // pinned: [2G] dispatch counts, [2G] received (rows, pairs) per peer
 };
 
 }  // namespace
@@ -152,6 +158,7 @@ void ep_release(ds_cuda_ctx *c) {
     if (s->h_counts) cudaFreeHost(s->h_counts);
     if (s->ev_packed) cudaEventDestroy(s->ev_packed);
     if (s->ev_recv) cudaEventDestroy(s->ev_recv);
+    if (s->ev_counts) cudaEventDestroy(s->ev_counts);
     if (s->cs) cudaStreamDestroy(s->cs);
     delete s;
     c->ep = nullptr;
@@ -193,6 +200,7 @@ extern "C" int ds_cuda_ep_init(ds_cuda_ctx_t *c, int rank, int world, const void
     if (cudaStreamCreateWithFlags(&s->cs, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&s->ev_packed, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&s->ev_recv, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s->ev_counts, cudaEventDisableTiming) != cudaSuccess ||
         cudaMallocHost((void **)&s->h_counts, 64 * sizeof(int)) != cudaSuccess) {
         cudaGetLastError();
         ep_release(c);
@@ -209,17 +217,38 @@ extern "C" int ds_cuda_ep_free(ds_cuda_ctx_t *c) {
 }
 
 // all-to-all(v) of byte rows on `st`: row counts per peer (host), rows are
-// `row_b` bytes, laid out rank after rank on both sides.
+// `row_b` bytes, laid out rank after rank on both sides. This rank's own
+// section is a stream-ordered device-to-device copy; NCCL moves only the
+// sections of the other ranks (its point-to-point kernels copy to self at a
+// fraction of the HBM rate, and at one rank every row is a self row).
 static int ep_a2a(ds_cuda_ctx *c, EpState *s, const void *send, const int *send_rows, void *recv, const int *recv_rows,
-                  size_t row_b, cudaStream_t st, const char *what) {
+                  size_t row_b, cudaStream_t st, const char *what, bool copy_self = true) {
     const Nccl *nc = s->nc;
-    int r = nc->group_start();
     size_t so = 0, ro = 0;
+    for (int p = 0; p < s->world; p++) {
+        if (p == s->rank) {
+            if (send_rows[p] != recv_rows[p])
+                return ctx_fail(c, DS_CUDA_ESTATE, "%s: %d rows sent to self, %d expected", what, send_rows[p],
+                                recv_rows[p]);
+            if (send_rows[p] > 0 && copy_self) {
+                cudaError_t e = cudaMemcpyAsync(static_cast<char *>(recv) + ro * row_b,
+                                                static_cast<const char *>(send) + so * row_b,
+                                                (size_t)send_rows[p] * row_b, cudaMemcpyDeviceToDevice, st);
+                if (e != cudaSuccess) return ctx_cuda(c, e, what);
+            }
+        }
+        so += send_rows[p];
+        ro += recv_rows[p];
+    }
+    if (s->world == 1) return DS_CUDA_OK;
+    int r = nc->group_start();
+    so = 0;
+    ro = 0;
     for (int p = 0; p < s->world && r == 0; p++) {
-        if (send_rows[p] > 0)
+        if (p != s->rank && send_rows[p] > 0)
             r = nc->send(static_cast<const char *>(send) + so * row_b, (size_t)send_rows[p] * row_b, NCCL_INT8, p,
                          s->comm, st);
-        if (r == 0 && recv_rows[p] > 0)
+        if (r == 0 && p != s->rank && recv_rows[p] > 0)
             r = nc->recv(static_cast<char *>(recv) + ro * row_b, (size_t)recv_rows[p] * row_b, NCCL_INT8, p, s->comm,
                          st);
         so += send_rows[p];
@@ -260,7 +289,8 @@ extern "C" int ds_cuda_prefill_moe_ep(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
     EPK(ep_grow(c, s->payload, cap_rows * row_b));
     EPK(ep_grow(c, s->send_tok, cap_rows * 4));
     EPK(ep_grow(c, s->counts, 2 * G * 4));
-    EPK(ep_grow(c, s->cnt_recv, G * 4));
+    EPK(ep_grow(c, s->cnt_pack, 2 * G * 4));
+    EPK(ep_grow(c, s->cnt_recv, 2 * G * 4));
     EPK(ep_grow(c, s->inv, n * K * 4));
     EPK(ep_grow(c, s->ys, n * H * 4));
     uint16_t *hi = (uint16_t *)s->hi.p, *lo = (uint16_t *)s->lo.p;
@@ -270,53 +300,71 @@ extern "C" int ds_cuda_prefill_moe_ep(ds_cuda_ctx_t *c, const ds_cuda_decoder_co
     EPK(ds_cuda_prefill_route_dev(c, cfg, layer, d_x, n_tokens, d_logits, hi, lo, idx, w, st));
     EPK(ds_cuda_ep_dispatch_dev(c, n_tokens, K, G, E / G, idx, hi, lo, H, (uint16_t *)s->payload.p,
                                 (int *)s->send_tok.p, (int *)s->counts.p, (int *)s->inv.p, st));
-    // row counts to every peer (int32 as 4 bytes)
-    std::vector<int> ones(G, 1);
-    EPK(ep_a2a(c, s, s->counts.p, ones.data(), s->cnt_recv.p, ones.data(), 4, st, "prefill_moe_ep counts"));
-    int *hc = s->h_counts;
-    EPC(cudaMemcpyAsync(hc, s->counts.p, 2 * G * 4, cudaMemcpyDeviceToHost, st), "counts copy");
-    EPC(cudaMemcpyAsync(hc + 2 * G, s->cnt_recv.p, G * 4, cudaMemcpyDeviceToHost, st), "counts copy");
-    EPC(cudaStreamSynchronize(st), "prefill_moe_ep dispatch");
-    std::vector<int> send_rows(hc, hc + G), back_recv(hc + G, hc + 2 * G), recv_rows(hc + 2 * G, hc + 3 * G);
-    size_t R = 0;
-    for (int p = 0; p < G; p++) R += recv_rows[p];
-    EPK(ep_grow(c, s->rpayload, R * row_b));
-    // 3. payload all-to-all on the communication stream, the shared expert
-    //    on the compute stream meanwhile
     EPC(cudaEventRecord(s->ev_packed, st), "event");
+    // (rows, pairs) to every peer as one 8-byte record: the rows it will
+    // receive and the (row, expert) pairs it will compute for this rank, so
+    // one host synchronisation sizes every transfer of the layer
+    int *cnt = (int *)s->counts.p, *pack = (int *)s->cnt_pack.p;
+    EPC(cudaMemcpy2DAsync(pack, 8, cnt, 4, 4, G, cudaMemcpyDeviceToDevice, st), "counts pack");
+    EPC(cudaMemcpy2DAsync(pack + 1, 8, cnt + G, 4, 4, G, cudaMemcpyDeviceToDevice, st), "counts pack");
+    std::vector<int> ones(G, 1);
+    EPK(ep_a2a(c, s, pack, ones.data(), s->cnt_recv.p, ones.data(), 8, st, "prefill_moe_ep counts"));
+    int *hc = s->h_counts;
+    EPC(cudaMemcpyAsync(hc, cnt, 2 * G * 4, cudaMemcpyDeviceToHost, st), "counts copy");
+    EPC(cudaMemcpyAsync(hc + 2 * G, s->cnt_recv.p, 2 * G * 4, cudaMemcpyDeviceToHost, st), "counts copy");
+    EPC(cudaEventRecord(s->ev_counts, st), "event");
+    // 3a. the shared expert on the local rows, queued before the host waits
+    //     for the counts so the GPU has work meanwhile
+    if (n_tokens > 0)
+        EPK(ds_cuda_prefill_experts_dev(c, cfg, layer, nullptr, nullptr, H, 0, nullptr, nullptr, 0, nullptr, hi, lo,
+                                        n_tokens, (float *)s->ys.p, st));
+    EPC(cudaEventSynchronize(s->ev_counts), "prefill_moe_ep dispatch counts");
+    std::vector<int> send_rows(hc, hc + G), back_recv(hc + G, hc + 2 * G), recv_rows(G), back_send(G);
+    size_t R = 0, P = 0, Bk = 0, self_y0 = 0, self_b0 = 0;
+    for (int p = 0; p < G; p++) {
+        recv_rows[p] = hc[2 * G + 2 * p];
+        back_send[p] = hc[2 * G + 2 * p + 1];
+        if (p < s->rank) {
+            self_y0 += back_send[p];
+            self_b0 += back_recv[p];
+        }
+        R += recv_rows[p];
+        P += back_send[p];
+        Bk += back_recv[p];
+    }
+    EPK(ep_grow(c, s->rpayload, R * row_b));
+    EPK(ep_grow(c, s->pair_row, R * K * 4));
+    EPK(ep_grow(c, s->pair_expert, R * K * 4));
+    EPK(ep_grow(c, s->pcounts, (G + 1) * 4));
+    EPK(ep_grow(c, s->y, P * H * 4));
+    EPK(ep_grow(c, s->yback, Bk * H * 4));
+    // 3b. payload all-to-all on the communication stream (after the pack,
+    //     beside the shared expert)
     EPC(cudaStreamWaitEvent(s->cs, s->ev_packed, 0), "event wait");
     EPK(ep_a2a(c, s, s->payload.p, send_rows.data(), s->rpayload.p, recv_rows.data(), row_b, s->cs,
                "prefill_moe_ep dispatch all-to-all"));
     EPC(cudaEventRecord(s->ev_recv, s->cs), "event");
-    if (n_tokens > 0)
-        EPK(ds_cuda_prefill_experts_dev(c, cfg, layer, nullptr, nullptr, H, 0, nullptr, nullptr, 0, nullptr, hi, lo,
-                                        n_tokens, (float *)s->ys.p, st));
     EPC(cudaStreamWaitEvent(st, s->ev_recv, 0), "event wait");
-    // 4. the received (row, expert) pairs, the routed experts
-    EPK(ep_grow(c, s->pair_row, R * K * 4));
-    EPK(ep_grow(c, s->pair_expert, R * K * 4));
-    EPK(ep_grow(c, s->pcounts, (G + 1) * 4));
+    // 4. the received (row, expert) pairs (their count per source rank is
+    //    the back_send the peers announced), the routed experts
     EPK(ds_cuda_ep_pairs_dev(c, (int)R, K, G, recv_rows.data(), (const uint16_t *)s->rpayload.p, H,
                              (int *)s->pair_row.p, (int *)s->pair_expert.p, (int *)s->pcounts.p, st));
-    EPC(cudaMemcpyAsync(hc + 3 * G, s->pcounts.p, (G + 1) * 4, cudaMemcpyDeviceToHost, st), "pairs copy");
-    EPC(cudaStreamSynchronize(st), "prefill_moe_ep pairs");
-    std::vector<int> back_send(hc + 3 * G, hc + 4 * G);
-    const size_t P = (size_t)hc[4 * G];
-    size_t Bk = 0;
-    for (int p = 0; p < G; p++) Bk += back_recv[p];
-    EPK(ep_grow(c, s->y, P * H * 4));
-    EPK(ep_grow(c, s->yback, Bk * H * 4));
     const uint16_t *rp = (const uint16_t *)s->rpayload.p;
     if (P > 0)
         EPK(ds_cuda_prefill_experts_dev(c, cfg, layer, rp, rp + H, (int)ld, (int)R, (const int *)s->pair_row.p,
                                         (const int *)s->pair_expert.p, (int)P, (float *)s->y.p, nullptr, nullptr, 0,
                                         nullptr, st));
     // 5. outputs back in request order; 6. combine
+    //    (this rank's own outputs stay in y: the combine reads that
+    //    section of the returned stream from there)
     EPK(ep_a2a(c, s, s->y.p, back_send.data(), s->yback.p, back_recv.data(), (size_t)H * 4, st,
-               "prefill_moe_ep return all-to-all"));
+               "prefill_moe_ep return all-to-all", false));
     if (n_tokens > 0)
-        EPK(ds_cuda_prefill_combine_dev(c, cfg, d_x, n_tokens, idx, w, (const float *)s->yback.p,
-                                        (const int *)s->inv.p, (const float *)s->ys.p, st));
+        EPC(pf_combine_split_launch(d_x, n_tokens, H, K, idx, w, (const float *)s->yback.p, (const int *)s->inv.p,
+                                    (const float *)s->ys.p, (const float *)s->y.p + self_y0 * H, (long long)self_b0,
+                                    (long long)(self_b0 + back_recv[s->rank]), st),
+            "prefill_moe_ep combine");
+    if (c->prefill_timing) EPC(cudaEventRecord(c->prefill_ev[6], st), "stage event");  // the combine's stage end
     if (d_top_idx) EPC(cudaMemcpyAsync(d_top_idx, idx, n * K * 4, cudaMemcpyDeviceToDevice, st), "idx copy");
     if (d_top_w) EPC(cudaMemcpyAsync(d_top_w, w, n * K * 4, cudaMemcpyDeviceToDevice, st), "w copy");
     return DS_CUDA_OK;

@@ -407,13 +407,18 @@ __global__ void __launch_bounds__(256) pf_scatter_kernel(int P, int H, int ld, i
 // shared[s]  (ds_moe_decoder.c:785-800). y_k is row s*K + k of yr, or row
 // yrow[s*K + k] when given.
 // One block of 128 threads per token; threads over float4 columns.
+// y_alt (optional): rows [alt_lo, alt_hi) of the yrow index space are read
+// from y_alt instead (row r at y_alt + (r - alt_lo) * H), so an
+// expert-parallel rank reads its own experts' outputs where they were
+// written, without copying them into the returned stream.
 __global__ void __launch_bounds__(128) pf_combine_kernel(float *x, int M, int H, int K, const int *idx, const float *wt,
-                                                         const float *yr, const int *yrow, const float *ys) {
+                                                         const float *yr, const int *yrow, const float *ys,
+                                                         const float *y_alt, long long alt_lo, long long alt_hi) {
     const int s = blockIdx.x;
     if (s >= M) return;
     int ord[8], e[8];
     float w[8];
-    size_t rows[8];
+    const float *src[8];
     for (int k = 0; k < K; k++) {
         ord[k] = k;
         e[k] = idx[(size_t)s * K + k];
@@ -427,12 +432,13 @@ __global__ void __launch_bounds__(128) pf_combine_kernel(float *x, int M, int H,
     for (int j = 0; j < K; j++) {
         const int k = ord[j];
         w[j] = wt[(size_t)s * K + k];
-        rows[j] = yrow ? (size_t)yrow[(size_t)s * K + k] : (size_t)s * K + k;
+        const long long r = yrow ? (long long)yrow[(size_t)s * K + k] : (long long)s * K + k;
+        src[j] = y_alt && r >= alt_lo && r < alt_hi ? y_alt + (size_t)(r - alt_lo) * H : yr + (size_t)r * H;
     }
     for (int c = 4 * threadIdx.x; c < H; c += 4 * blockDim.x) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < K; j++) {
-            const float4 y = *reinterpret_cast<const float4 *>(yr + rows[j] * H + c);
+            const float4 y = *reinterpret_cast<const float4 *>(src[j] + c);
             acc.x = __fmaf_rn(w[j], y.x, acc.x);
             acc.y = __fmaf_rn(w[j], y.y, acc.y);
             acc.z = __fmaf_rn(w[j], y.z, acc.z);
@@ -638,7 +644,7 @@ static int pf_experts(ds_cuda_ctx *c, const PfShape &g, const uint16_t *d_block,
 static int pf_combine(ds_cuda_ctx *c, const PfShape &g, float *d_x, int M, const int *idx, const float *wt,
                       const float *y, const int *yrow, const float *ys, cudaStream_t st) {
     if (M <= 0) return DS_CUDA_OK;
-    pf_combine_kernel<<<M, 128, 0, st>>>(d_x, M, g.H, g.K, idx, wt, y, yrow, ys);
+    pf_combine_kernel<<<M, 128, 0, st>>>(d_x, M, g.H, g.K, idx, wt, y, yrow, ys, nullptr, 0, 0);
     mark(c, 6, st);
     return DS_CUDA_OK;
 }
@@ -920,6 +926,13 @@ cudaError_t pf_scatter_launch(int P, int H, int ld, int K, const int *pair_row, 
 
 cudaError_t pf_combine_launch(float *x, int M, int H, int K, const int *idx, const float *wt, const float *y,
                               const int *yrow, const float *ys, cudaStream_t st) {
-    if (M > 0) pf_combine_kernel<<<M, 128, 0, st>>>(x, M, H, K, idx, wt, y, yrow, ys);
+    if (M > 0) pf_combine_kernel<<<M, 128, 0, st>>>(x, M, H, K, idx, wt, y, yrow, ys, nullptr, 0, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t pf_combine_split_launch(float *x, int M, int H, int K, const int *idx, const float *wt, const float *y,
+                                    const int *yrow, const float *ys, const float *y_alt, long long alt_lo,
+                                    long long alt_hi, cudaStream_t st) {
+    if (M > 0) pf_combine_kernel<<<M, 128, 0, st>>>(x, M, H, K, idx, wt, y, yrow, ys, y_alt, alt_lo, alt_hi);
     return cudaGetLastError();
 }

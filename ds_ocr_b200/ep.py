@@ -88,6 +88,7 @@ class CudaStages:
                                                         self._p(lo), H, payload.data_ptr(), send_tok.data_ptr(),
                                                         counts.data_ptr(), inv.data_ptr(), self._st()),
                        "ep_dispatch")
+        self.stream.synchronize()  # the host read below, whatever the caller's current stream
         return payload, counts.tolist(), inv
 
     def pairs(self, payload, recv_counts):
@@ -102,6 +103,7 @@ class CudaStages:
         self.ctx.check(self.lib.ds_cuda_ep_pairs_dev(self.ctx.h, R, K, G, rc, self._p(payload), self.d.hidden,
                                                      pr.data_ptr(), pe.data_ptr(), out.data_ptr(), self._st()),
                        "ep_pairs")
+        self.stream.synchronize()
         o = out.tolist()
         return pr[:o[G]], pe[:o[G]], o[:G]
 

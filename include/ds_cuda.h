@@ -473,9 +473,11 @@ int ds_cuda_prefill_combine_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config
                                 int n_tokens, const int *d_top_idx, const float *d_top_w, const float *d_y,
                                 const int *d_y_row, const float *d_ys, void *stream);
 /* Expert-parallel bookkeeping (no counterpart in the reference). Ranks own
- * contiguous blocks of experts_per_rank experts (n_ranks <= 8, top_k <= 8).
- * A payload row is [hi plane H | lo plane H | 8 int32 expert ids] as
- * uint16_t, row pitch 2*H + 16.
+ * contiguous blocks of experts_per_rank experts (n_ranks <= 8, top_k <= 7).
+ * A payload row is [hi plane H | lo plane H | 8 int32 meta] as uint16_t, row
+ * pitch 2*H + 16; meta = the top_k expert ids served at the destination (-1
+ * for the others, -1 padding) and, in the last slot, the offset of the
+ * row's first (row, expert) pair within that destination's pairs.
  *  dispatch: plans sending each token once to every rank owning one of its
  *            experts (rank ascending, token ascending) and packs those rows
  *            into d_payload (capacity n_tokens * min(top_k, n_ranks) rows);
@@ -484,7 +486,8 @@ int ds_cuda_prefill_combine_dev(ds_cuda_ctx_t *ctx, const ds_cuda_decoder_config
  *            d_inv[s*top_k + k] = row of that pair's output in the stream
  *            that comes back (rank, token, k ascending).
  *  pairs:    for n_rows received payload rows (recv_counts [n_ranks], a HOST
- *            array, rows per source rank in rank order) the compact
+ *            array, rows per source rank in rank order, each source's rows
+ *            one destination section of its dispatch) the compact
  *            row-major (row, expert) pairs; d_counts[0..G) pairs per source
  *            rank, d_counts[G] all pairs. */
 int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *ctx, int n_tokens, int top_k, int n_ranks, int experts_per_rank,

@@ -45,7 +45,9 @@ class StandInStages:
                 if not ks:
                     continue
                 counts[g] += 1
-                m = [int(idx[s_, k]) if k in ks else -1 for k in range(K)] + [-1] * (8 - K)
+                # expert ids of this destination, then in the last slot the
+                # row's first pair within the destination's pairs
+                m = [int(idx[s_, k]) if k in ks else -1 for k in range(K)] + [-1] * (7 - K) + [pairs[g]]
                 rows.append(torch.cat([hi[s_], lo[s_], torch.tensor(m, dtype=torch.int32).view(torch.int16)]))
                 for k in ks:
                     inv[s_ * K + k] = base

@@ -119,16 +119,18 @@ def test_ep_one_rank_path_matches_prefill(cuda_ctx):
     assert np.array_equal(tx.cpu().numpy(), ref)
 
 
-def test_dispatch_and_pairs_kernels(cuda_ctx):
+@pytest.mark.parametrize("n", [300, 3000])
+def test_dispatch_and_pairs_kernels(cuda_ctx, n):
     # the bookkeeping kernels against the CPU stand-in's reading of the same
-    # contract, for 4 ranks of 16 experts
+    # contract, for 4 ranks of 16 experts (3000 tokens: several tokens and
+    # rows per thread)
     import torch
     from test_ep_cpu import StandInStages
     from ds_ocr_b200 import synth
     from ds_ocr_b200.ep import CudaStages
     model = synth.Model(n_layers=2, vocab=256)
     st = CudaStages(model.d, cuda_ctx)
-    n, K, H, G = 300, model.d.top_k, model.d.hidden, 4
+    K, H, G = model.d.top_k, model.d.hidden, 4
     rng = np.random.default_rng(3)
     idx = np.stack([rng.choice(64, K, replace=False) for _ in range(n)]).astype(np.int32)
     idx[:20] = np.arange(K)  # all on rank 0
@@ -144,9 +146,9 @@ def test_dispatch_and_pairs_kernels(cuda_ctx):
     try:
         r_payload, r_counts, r_inv = ref.dispatch(torch.from_numpy(idx), torch.from_numpy(hi), torch.from_numpy(lo),
                                                   G, 64 // G)
-        recv = [0, 0, 0, 0]
-        rows = sum(r_counts[:G])
-        recv = [rows // 4, rows // 4, rows // 4, rows - 3 * (rows // 4)]
+        # the payload as if each destination's section had come from a
+        # different rank (the offsets in a row are relative to its section)
+        recv = list(r_counts[:G])
         rpr, rpe, rper = ref.pairs(r_payload, recv)
     finally:
         T.K, T.H = saved
@@ -154,7 +156,6 @@ def test_dispatch_and_pairs_kernels(cuda_ctx):
     rows = sum(counts[:G])
     assert torch.equal(payload[:rows].cpu(), r_payload)
     assert torch.equal(inv[:n * K].cpu(), r_inv)
-    # the payload as if received from 4 ranks with these row counts
     pr, pe, per = st.pairs(payload[:rows], recv)
     assert torch.equal(pr.cpu(), rpr) and torch.equal(pe.cpu(), rpe) and per == rper
 
@@ -177,9 +178,14 @@ def test_native_ep_one_rank_matches_prefill(cuda_ctx):
         tx = torch.from_numpy(x).cuda()
         tl = torch.from_numpy(lg).cuda()
         torch.cuda.synchronize()
+        pf = Prefill(model.d, cuda_ctx)
+        pf.timing(True)  # the per-stage events cover the expert-parallel layer too
         for l in (1, 2):
             idx, _ = ep.moe_layer(model.layers[l], tx, tl)
         cuda_ctx.synchronize()
+        ms = pf.stage_ms()
+        assert all(np.isfinite(ms)) and min(ms) >= 0
+        pf.timing(False)
     finally:
         ep.close()
     assert np.array_equal(idx.cpu().numpy(), idx_ref)

@@ -11,88 +11,153 @@
 // ascending); inv[s*K + k] is that pair's row in the returned stream, so the
 // combine reads them without a scatter.
 //
-// These are planning kernels over a few thousand tokens: one CTA, block-wide
-// scans in chunks of 1024.
+// These are planning kernels over a few thousand tokens: the dispatch plan
+// gives each CTA 256 tokens (each CTA reads all top-k ids for its offsets),
+// the pair list one thread per received row.
 #include "ctx.h"
 
 namespace ds {
 
-constexpr int EP_THREADS = 1024;
 constexpr int EP_META = 8;  // int32 slots after the two BF16 planes of a payload row
 
-// exclusive block scan of one int per thread; returns the block total
-__device__ int ep_scan(int v, int &excl) {
-    __shared__ int warp_tot[32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int x = v;
+// Exclusive block scan of NV ints per thread at once (one pair of
+// barriers for all of them); tot[v] gets the block total of value v.
+template <int NV>
+__device__ __forceinline__ void ep_scan_multi(int (&v)[NV], int (&excl)[NV], int (&tot)[NV]) {
+    __shared__ int wt[NV][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    int inc[NV];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_tot[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-        int t = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+    for (int q = 0; q < NV; q++) {
+        int x = v[q];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            int y = __shfl_up_sync(0xffffffffu, t, o);
-            if (lane >= o) t += y;
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
         }
-        warp_tot[lane] = t;  // inclusive
+        inc[q] = x;
+        if (lane == 31) wt[q][warp] = x;
     }
     __syncthreads();
-    const int before = warp ? warp_tot[warp - 1] : 0;
-    excl = before + x - v;
-    const int total = warp_tot[(blockDim.x >> 5) - 1];
+    if (warp == 0) {
+#pragma unroll
+        for (int q = 0; q < NV; q++) {
+            int t = lane < nwarp ? wt[q][lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, t, o);
+                if (lane >= o) t += y;
+            }
+            wt[q][lane] = t;  // inclusive over warps
+        }
+    }
     __syncthreads();
-    return total;
+#pragma unroll
+    for (int q = 0; q < NV; q++) {
+        excl[q] = (warp ? wt[q][warp - 1] : 0) + inc[q] - v[q];
+        tot[q] = wt[q][nwarp - 1];
+    }
 }
 
-// Plans the dispatch of n tokens and writes each sent row's expert list into
-// the payload (row pitch `ld` int16 elements; the meta sits at int16 offset
+// Rows (a 0/1 flag) and pairs token s sends to each of the eight possible
+// destinations: v[q] and v[8 + q].
+__device__ __forceinline__ void ep_token_counts(const int *__restrict__ idx, int s, int K, int e_per, int (&v)[16]) {
+    unsigned mask = 0;
+#pragma unroll
+    for (int q = 0; q < 16; q++) v[q] = 0;
+    for (int k = 0; k < K; k++) {
+        const int g = idx[s * K + k] / e_per;
+        mask |= 1u << g;
+#pragma unroll
+        for (int q = 0; q < 8; q++) v[8 + q] += g == q;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; q++) v[q] = (mask >> q) & 1u;
+}
+
+constexpr int EP_PLAN_TOK = 256;  // tokens (threads) per CTA of the dispatch plan
+
+// Plans the dispatch of n tokens and writes each sent row's meta into the
+// payload (row pitch `ld` int16 elements; the meta sits at int16 offset
 // 2*H). counts[0..G) = rows per destination, counts[G..2G) = pairs per
-// destination. send_tok[i] = token of send row i.
-__global__ void __launch_bounds__(EP_THREADS) ep_dispatch_plan_kernel(int n, int K, int G, int e_per,
-                                                                      const int *__restrict__ idx, int H, int ld,
-                                                                      uint16_t *payload, int *send_tok, int *counts,
-                                                                      int *inv) {
-    int row_base = 0, pair_base = 0;
-    for (int g = 0; g < G; g++) {
-        int rows_g = 0, pairs_g = 0;
-        for (int c0 = 0; c0 < n; c0 += EP_THREADS) {
-            const int s = c0 + threadIdx.x;
-            int cnt = 0;
-            if (s < n)
-                for (int k = 0; k < K; k++) cnt += idx[s * K + k] / e_per == g;
-            int r_ex, p_ex;
-            const int r_tot = ep_scan(cnt > 0, r_ex);
-            const int p_tot = ep_scan(cnt, p_ex);
-            if (s < n && cnt > 0) {
-                const int row = row_base + rows_g + r_ex;
+// destination. send_tok[i] = token of send row i. Each CTA owns 256 tokens
+// (one per thread): it first reads every token's top-k ids (a few tens of
+// KB, from L2) for the per-destination totals and the counts of the tokens
+// before its own, then one block scan places its rows.
+__global__ void __launch_bounds__(EP_PLAN_TOK) ep_dispatch_plan_kernel(int n, int K, int G, int e_per,
+                                                                       const int *__restrict__ idx, int H, int ld,
+                                                                       uint16_t *payload, int *send_tok, int *counts,
+                                                                       int *inv) {
+    __shared__ int s_before[16], s_total[16];
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < 16) {
+        s_before[tid] = 0;
+        s_total[tid] = 0;
+    }
+    __syncthreads();
+    const int blk0 = blockIdx.x * EP_PLAN_TOK;
+    int before[16], total[16];
+#pragma unroll
+    for (int q = 0; q < 16; q++) before[q] = total[q] = 0;
+    for (int s = tid; s < n; s += EP_PLAN_TOK) {
+        int v[16];
+        ep_token_counts(idx, s, K, e_per, v);
+        const bool b = s < blk0;
+#pragma unroll
+        for (int q = 0; q < 16; q++) {
+            total[q] += v[q];
+            before[q] += b ? v[q] : 0;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 16; q++) {
+        int t = total[q], b = before[q];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            t += __shfl_xor_sync(0xffffffffu, t, o);
+            b += __shfl_xor_sync(0xffffffffu, b, o);
+        }
+        if (lane == 0) {
+            if (t) atomicAdd(&s_total[q], t);
+            if (b) atomicAdd(&s_before[q], b);
+        }
+    }
+    __syncthreads();
+    const int s = blk0 + tid;
+    int v[16], ex[16], bt[16];
+    if (s < n) ep_token_counts(idx, s, K, e_per, v);
+    else
+#pragma unroll
+        for (int q = 0; q < 16; q++) v[q] = 0;
+    ep_scan_multi<16>(v, ex, bt);
+    if (s < n) {
+        int row_base = 0, pair_base = 0;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            if (q < G && v[q]) {
+                const int row = row_base + s_before[q] + ex[q];
+                const int p_in = s_before[8 + q] + ex[8 + q];  // within the destination's pairs
                 send_tok[row] = s;
                 int *meta = reinterpret_cast<int *>(payload + (size_t)row * ld + 2 * H);
                 int j = 0;
                 for (int k = 0; k < K; k++) {
                     const int e = idx[s * K + k];
-                    const bool mine = e / e_per == g;
+                    const bool mine = e / e_per == q;
                     meta[k] = mine ? e : -1;
-                    if (mine) inv[s * K + k] = pair_base + pairs_g + p_ex + j++;
+                    if (mine) inv[s * K + k] = pair_base + p_in + j++;
                 }
-                for (int k = K; k < EP_META; k++) meta[k] = -1;
-                // the row's first pair within its destination's section: the
+                for (int k = K; k < EP_META - 1; k++) meta[k] = -1;
+                // the row's first pair within its destination's pairs: the
                 // receiver places its pairs without a scan
-                meta[EP_META - 1] = pairs_g + p_ex;
+                meta[EP_META - 1] = p_in;
             }
-            rows_g += r_tot;
-            pairs_g += p_tot;
+            row_base += q < G ? s_total[q] : 0;
+            pair_base += q < G ? s_total[8 + q] : 0;
         }
-        if (threadIdx.x == 0) {
-            counts[g] = rows_g;
-            counts[G + g] = pairs_g;
-        }
-        row_base += rows_g;
-        pair_base += pairs_g;
+    }
+    if (blockIdx.x == 0 && tid < G) {
+        counts[tid] = s_total[tid];
+        counts[G + tid] = s_total[8 + tid];
     }
 }
 
@@ -184,8 +249,8 @@ extern "C" int ds_cuda_ep_dispatch_dev(ds_cuda_ctx_t *c, int n_tokens, int top_k
     cudaSetDevice(c->device);
     cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
     const int ld = 2 * hidden + 2 * EP_META;
-    ep_dispatch_plan_kernel<<<1, EP_THREADS, 0, st>>>(n_tokens, top_k, n_ranks, experts_per_rank, d_top_idx, hidden,
-                                                      ld, d_payload, d_send_tok, d_counts, d_inv);
+    ep_dispatch_plan_kernel<<<n_tokens > 0 ? (n_tokens + EP_PLAN_TOK - 1) / EP_PLAN_TOK : 1, EP_PLAN_TOK, 0, st>>>(
+        n_tokens, top_k, n_ranks, experts_per_rank, d_top_idx, hidden, ld, d_payload, d_send_tok, d_counts, d_inv);
     // rows <= n * min(top_k, n_ranks)
     const int max_rows = n_tokens * (top_k < n_ranks ? top_k : n_ranks);
     if (max_rows > 0)

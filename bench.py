@@ -540,6 +540,16 @@ def run_ours_decode_streams(args, rank, world, pg, model, prefixes):
     st = torch.cuda.Stream()
     sp = st.cuda_stream
     E = np.stack([model.embed((1 + 7 * (a + i)) % model.d.vocab) for i in range(S)])
+    rp, ng, temp = sampling_of(args)
+    sampled = decode_mode(args) != "greedy"
+    n_e2e = max(3, args.steps // 4)
+    if sampled:
+        # the LM head's sampling settings for every stream (each with its own
+        # history); uniforms for every step the run takes
+        bd.set_sampling(rp, ng, temp)
+        if temp > 0:
+            bd.set_uniforms(np.random.default_rng(11).random((S, 1 + args.warmup + args.steps + n_e2e))
+                            .astype(np.float32))
     bd.forward(E)  # first step from the given embeddings (and scratch set-up)
     bd.generate_dev(max(1, args.warmup - 1), sp)
     st.synchronize()
@@ -554,7 +564,6 @@ def run_ours_decode_streams(args, rank, world, pg, model, prefixes):
     value = MS_STREAMS * args.steps / (ms_max / 1e3)
     # e2e: the host API, one call per step (previous tokens' embeddings on
     # the device, the S tokens copied back every step)
-    n_e2e = max(3, args.steps // 4)
     for i in range(S):
         bd.set_len(i, PREFIX)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -572,17 +581,22 @@ def run_ours_decode_streams(args, rank, world, pg, model, prefixes):
     ach = step_bytes / (ms_max / args.steps / 1e3) / 1e9
     res = {
         "value": value, "ms_per_step": ms_max / args.steps, "clocks": clk.summary(),
-        "metric": "decode tokens/s (greedy, 64 independent streams, 12-layer DeepSeek3B-MoE, 662-token KV prefixes)",
+        "metric": (f"decode tokens/s ({decode_mode(args)}, 64 independent streams, 12-layer DeepSeek3B-MoE, "
+                   "662-token KV prefixes)"),
         "unit": "tokens/s", "dtype": "bf16 weights + bf16 KV, f32 activations as two bf16 planes, f32 accumulate",
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": S * 4},
         # per step: 7 per layer (3 norm/split passes, QKV, RoPE/KV, attention,
         # O-proj), 2 per dense FFN, 8 per MoE layer (router, top-k, count,
         # plan, scatter, gate/up, down, combine), 3 for the final norm, LM
-        # head and advance (177 per step, as in the ncu launch list)
+        # head and advance (177 per step, as in the ncu launch list); with
+        # sampling settings the selection kernels (history dots with a
+        # penalty and no temperature, fast, full-logits, full selection)
         "gpu_launches": (7 * model.d.n_layers + 2 * model.d.first_dense
-                         + 8 * (model.d.n_layers - model.d.first_dense) + 3) * args.steps,
+                         + 8 * (model.d.n_layers - model.d.first_dense) + 3
+                         + ((4 if rp > 1.0 and temp <= 0.0 else 3) if sampled else 0)) * args.steps,
         "config": dict(decode_config(kv_max), workload="config3_decode_64_streams", global_batch=MS_STREAMS,
-                       streams_per_gpu=S, parallelism=f"sharded by stream over {world} GPU(s)"),
+                       streams_per_gpu=S, parallelism=f"sharded by stream over {world} GPU(s)",
+                       **({"sampling": decode_mode(args)} if sampled else {})),
         "roofline": {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": ach / pk["hbm_gbs"], "traffic": None,
                      "kernel": "whole step: weights once per step (all 64 experts of each MoE layer assumed "
@@ -625,13 +639,13 @@ _STREAM_MODEL = None  # shared with forked reference processes (copy-on-write)
 
 
 def _ref_stream(args):
-    threads, budget_s, max_steps, stream = args
+    threads, budget_s, max_steps, stream, sampling = args
     from ds_ocr_b200 import synth
     ks, vs = synth.kv_prefix(_STREAM_MODEL.d, PREFIX, stream=stream)
-    return ref_decode_time(_STREAM_MODEL, ks, vs, threads, budget_s, max_steps)
+    return ref_decode_time(_STREAM_MODEL, ks, vs, threads, budget_s, max_steps, sampling=sampling)
 
 
-def ref_decode_streams_time(model, threads, budget_s, max_steps):
+def ref_decode_streams_time(model, threads, budget_s, max_steps, sampling=(1.0, 0, 0.0)):
     """The reference decodes streams one at a time per context; its
     multi-stream aggregate is floor(nproc / threads) concurrent processes,
     one stream each (stream s's own KV prefix). Returns (aggregate tokens/s,
@@ -641,7 +655,7 @@ def ref_decode_streams_time(model, threads, budget_s, max_steps):
     global _STREAM_MODEL
     n_proc = max(1, (os.cpu_count() or 1) // threads)
     _STREAM_MODEL = model
-    jobs = [(threads, budget_s, max_steps, s) for s in range(n_proc)]
+    jobs = [(threads, budget_s, max_steps, s, sampling) for s in range(n_proc)]
     if n_proc == 1:
         v, n = _ref_stream(jobs[0])
         return v, n, 1
@@ -1180,9 +1194,13 @@ def main():
                 cfg["sampling"] = decode_mode(args)
         elif args.workload == "decode64":
             model, _, _ = build_decode_model()
-            v, n, n_proc = ref_decode_streams_time(model, T, max(args.cpu_budget, 1.0), args.steps)
-            metric = "decode tokens/s (greedy, 64 independent streams, 12-layer DeepSeek3B-MoE, 662-token KV prefixes)"
+            v, n, n_proc = ref_decode_streams_time(model, T, max(args.cpu_budget, 1.0), args.steps,
+                                                   sampling=sampling_of(args))
+            metric = (f"decode tokens/s ({decode_mode(args)}, 64 independent streams, 12-layer DeepSeek3B-MoE, "
+                      "662-token KV prefixes)")
             cfg = dict(decode_config(1024), workload="config3_decode_64_streams", global_batch=MS_STREAMS)
+            if decode_mode(args) != "greedy":
+                cfg["sampling"] = decode_mode(args)
             sample = (f"{n_proc} concurrent reference processes of {T} threads, one stream each "
                       f"(the reference decodes one stream per context), {n} ds_decoder_forward steps each")
         elif args.workload == "lm_head":

@@ -201,10 +201,13 @@ __global__ void __launch_bounds__(256) select_logits_kernel(SelectArgs a) {
 }
 
 // Every logit of every stream whose full path runs, several streams at
-// once: one warp per LM-head row keeps the row in registers (each lane the
-// same 8-element chunks that sel_row_dot gives it, so each logit is the same
-// sum in the same order) and dots it with each flagged stream's x, so the
-// head streams from HBM once per step instead of once per stream.
+// once: one warp per four LM-head rows keeps them in registers (each lane
+// the same 8-element chunks that sel_row_dot gives it, so each logit is the
+// same sum in the same order) and dots them with each flagged stream's x,
+// each x load serving the four rows; the head streams from HBM once per
+// step instead of once per stream.
+constexpr int SEL_RW = 4;  // LM-head rows per warp
+
 template <int CH>
 __global__ void __launch_bounds__(256) select_logits_streams_kernel(SelectArgs a) {
     const int lane = threadIdx.x & 31;
@@ -213,31 +216,45 @@ __global__ void __launch_bounds__(256) select_logits_streams_kernel(SelectArgs a
     for (int s = 0; s < S; s++) any = any || a.full[s];
     if (!any) return;
     const int nw = (gridDim.x * blockDim.x) >> 5;
-    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < a.V; r += nw) {
-        const uint16_t *w = a.W + (size_t)r * a.H;
-        uint4 u[CH];
+    const int n_grp = (a.V + SEL_RW - 1) / SEL_RW;
+    for (int grp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; grp < n_grp; grp += nw) {
+        const int r0 = grp * SEL_RW;
+        uint4 u[SEL_RW][CH];
 #pragma unroll
-        for (int k = 0; k < CH; k++) u[k] = ldg_stream(w + lane * 8 + k * 256);
+        for (int q = 0; q < SEL_RW; q++) {
+            const int r = min(r0 + q, a.V - 1);  // a short last group repeats the last row
+            const uint16_t *w = a.W + (size_t)r * a.H;
+#pragma unroll
+            for (int k = 0; k < CH; k++) u[q][k] = ldg_stream(w + lane * 8 + k * 256);
+        }
         for (int s = 0; s < S; s++) {
             if (!a.full[s]) continue;
             const float *x = a.x + (size_t)s * a.x_ld;
-            float acc = 0.f;
+            float acc[SEL_RW];
+#pragma unroll
+            for (int q = 0; q < SEL_RW; q++) acc[q] = 0.f;
 #pragma unroll
             for (int k = 0; k < CH; k++) {
                 const int c = lane * 8 + k * 256;
                 const float4 x0 = *reinterpret_cast<const float4 *>(x + c);
                 const float4 x1 = *reinterpret_cast<const float4 *>(x + c + 4);
-                acc = __fmaf_rn(bf16_lo(u[k].x), x0.x, acc);
-                acc = __fmaf_rn(bf16_hi(u[k].x), x0.y, acc);
-                acc = __fmaf_rn(bf16_lo(u[k].y), x0.z, acc);
-                acc = __fmaf_rn(bf16_hi(u[k].y), x0.w, acc);
-                acc = __fmaf_rn(bf16_lo(u[k].z), x1.x, acc);
-                acc = __fmaf_rn(bf16_hi(u[k].z), x1.y, acc);
-                acc = __fmaf_rn(bf16_lo(u[k].w), x1.z, acc);
-                acc = __fmaf_rn(bf16_hi(u[k].w), x1.w, acc);
+#pragma unroll
+                for (int q = 0; q < SEL_RW; q++) {
+                    acc[q] = __fmaf_rn(bf16_lo(u[q][k].x), x0.x, acc[q]);
+                    acc[q] = __fmaf_rn(bf16_hi(u[q][k].x), x0.y, acc[q]);
+                    acc[q] = __fmaf_rn(bf16_lo(u[q][k].y), x0.z, acc[q]);
+                    acc[q] = __fmaf_rn(bf16_hi(u[q][k].y), x0.w, acc[q]);
+                    acc[q] = __fmaf_rn(bf16_lo(u[q][k].z), x1.x, acc[q]);
+                    acc[q] = __fmaf_rn(bf16_hi(u[q][k].z), x1.y, acc[q]);
+                    acc[q] = __fmaf_rn(bf16_lo(u[q][k].w), x1.z, acc[q]);
+                    acc[q] = __fmaf_rn(bf16_hi(u[q][k].w), x1.w, acc[q]);
+                }
             }
-            acc = warp_sum(acc);
-            if (lane == 0) a.logits[(size_t)s * a.V + r] = acc;
+#pragma unroll
+            for (int q = 0; q < SEL_RW; q++) {
+                const float v = warp_sum(acc[q]);
+                if (lane == 0 && r0 + q < a.V) a.logits[(size_t)s * a.V + r0 + q] = v;
+            }
         }
     }
 }

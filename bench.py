@@ -182,7 +182,7 @@ class MoeLayerWorkload:
 # for each of the 6 routed experts, gate/up int8 [1792 x 1280] + 2 x 1792
 # F32 scale/offset and down int8 [1280 x 896] + 2 x 1280 F32, and the shared
 # expert's int8 gate/up [3584 x 1280] + 2 x 3584 F32 and down [1280 x 1792]
-# + 2 x 1280 F32.
+# + 2 x 1280 F32 = 27,875,328 B.
 INT8_BYTES_PER_TOKEN = (163840 + 6 * (2293760 + 14336 + 1146880 + 10240)
                         + (4587520 + 28672 + 2293760 + 10240))
 
